@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Decode throughput of libqwen_b200 on B200s (one process per GPU).
+
+Workload (a "step"): one greedy decode step of the seeded random-int8
+Qwen2.5-0.5B for 64 independent sequences per GPU, each at context 2048+
+(batched decode serving; the KV8 caches are filled with seeded synthetic codes
+so the long prefill is not part of the measurement). Request-sharded: every
+rank holds a full replica and its own 64 sequences, no data-path collective
+(weak scaling). value = all ranks' tokens / max-over-ranks device time.
+
+Also reported: e2e (the same step through the host-buffer C ABI call
+qwen_b200_decode_step, H2D ids and D2H tokens inside the timed region), bs1
+decode at short context (16-token prompt, the reference's CPU-runnable case),
+per-kernel-class device times from CUDA events, the roofline of the dominant
+kernel class and of the whole step, clocks sampled during the timed region,
+and the oracle (CPU port of the reference model) timed on the host cores.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+    python bench.py --impl reference ...   # the CPU reference path alone
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / 'fpga2026-40999-llm-accelerator-for-qwen2.5-0.5b-on-fpga_b200'
+for _p in (str(PKG), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+SEED = 2026
+HID, FFN, QKV, VOCAB, LAYERS = 896, 4864, 1152, 151936, 24
+KV_BYTES_PER_TOKEN_LAYER = 2 * 2 * (64 + 4)  # K and V, 2 heads, 64 codes + fp32 scale
+CLASSES = ['embedding', 'qkv_rope_kv8', 'attention', 'o_proj_residual', 'gate_up_swiglu', 'down_residual',
+           'lm_head_argmax', 'bookkeeping']
+KERNEL_NAMES = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_score_kernel + attn_pv_kernel',
+                'o_proj_residual': 'gemv_kernel<896,EPI_RESIDUAL>', 'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
+                'down_residual': 'gemv_kernel<4864,EPI_RESIDUAL>', 'lm_head_argmax': 'lm_head_kernel + argmax_reduce',
+                'embedding': 'embed_kernel', 'bookkeeping': 'decode prologue/epilogue'}
+
+
+def weight_bytes():
+    """Algorithmic bytes that one decode step reads once, whatever the batch."""
+    layer = (QKV * HID + HID * HID + 2 * FFN * HID + HID * FFN  # int8 codes
+             + 4 * (QKV + HID + 2 * FFN + HID)                   # fp32 scales
+             + 2 * QKV + 2 * 2 * HID)                            # bf16 bias, gains
+    return LAYERS * layer + VOCAB * HID + 4 * VOCAB + 2 * HID
+
+
+def class_bytes(n, contexts):
+    """Algorithmic bytes per launch of each kernel class for a step of n rows."""
+    kv = sum(contexts) * KV_BYTES_PER_TOKEN_LAYER
+    return {
+        'embedding': n * HID * 2 * 2,
+        'qkv_rope_kv8': QKV * HID + 4 * QKV + 2 * QKV + 2 * HID + n * HID * 2 * 2 + n * 2 * 2 * (64 + 4),
+        'attention': kv + n * HID * 2 * 2,
+        'o_proj_residual': HID * HID + 4 * HID + n * HID * 2 * 3,
+        'gate_up_swiglu': 2 * FFN * HID + 4 * 2 * FFN + 2 * HID + n * HID * 2 + n * FFN * 2,
+        'down_residual': HID * FFN + 4 * HID + n * FFN * 2 + n * HID * 2 * 2,
+        'lm_head_argmax': VOCAB * HID + 4 * VOCAB + 2 * HID + n * HID * 2 + n * 4,
+        'bookkeeping': n * 16,
+    }
+
+
+def step_bytes(contexts):
+    return weight_bytes() + sum(contexts) * KV_BYTES_PER_TOKEN_LAYER * LAYERS
+
+
+def peaks():
+    p = REPO / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d['hbm_gbs']), 'measured'
+    return 6650.0, 'fallback'
+
+
+class Clocks:
+    """nvidia-smi sampler started before and stopped after the timed region."""
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_id):
+        self.gpu_id, self.proc, self.path = gpu_id, None, None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix='.csv')
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.QUERY}', '--format=csv,noheader,nounits',
+                                          '-i', str(self.gpu_id), '-lms', '100'],
+                                         stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(',')]
+            if len(f) >= 9 and f[1].isdigit():
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [int(r[1]) for r in rows]
+        reasons = set()
+        for r in rows:
+            for name, col in [('hw_slowdown', 5), ('hw_thermal_slowdown', 6), ('sw_thermal_slowdown', 7),
+                              ('sw_power_cap', 8)]:
+                if r[col].lower() == 'active':
+                    reasons.add(name)
+        loaded = [s for s in sm if s > 0.5 * max(sm)]
+        return {'sm_mhz': int(statistics.median(loaded or sm)), 'sm_max_mhz': int(rows[0][2]),
+                'samples': len(rows), 'reasons': sorted(reasons)}
+
+
+def dist_setup():
+    import torch
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device('cuda', local))
+    return rank, world, local
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def cpu_decode_sample(min_seconds, max_seconds, context, threads):
+    """The oracle (plain-C port of the reference's behavioural model, KV8 mode)
+    decoding one sequence at `context` on the host cores. Returns tokens/s."""
+    from oracle import ref
+    import qwen_b200
+    with tempfile.TemporaryDirectory() as tmp:
+        assert qwen_b200.lib().qwen_b200_synth_write(tmp.encode(), SEED) == 0
+        m = ref.RefModel(tmp, capacity=context + 512, mode=ref.KV8, threads=threads)
+    m.fill_kv_synthetic(context, SEED)
+    tok, n, pos = 1, 0, context
+    m.forward([tok], pos)  # warm
+    pos += 1
+    t0 = time.perf_counter()
+    while True:
+        tok = m.forward([tok], pos)
+        pos, n = pos + 1, n + 1
+        el = time.perf_counter() - t0
+        if (el >= min_seconds and n >= 3) or el >= max_seconds or pos >= context + 500:
+            break
+    m.close()
+    return n / el, n
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return 0
+    from oracle import ref
+    import qwen_b200
+    threads = os.cpu_count() or 1
+    tokens_per_step = 4
+    with tempfile.TemporaryDirectory() as tmp:
+        assert qwen_b200.lib().qwen_b200_synth_write(tmp.encode(), SEED) == 0
+        m = ref.RefModel(tmp, capacity=args.context + tokens_per_step * (args.steps + args.warmup) + 8,
+                         mode=ref.KV8, threads=threads)
+    m.fill_kv_synthetic(args.context, SEED)
+    tok, pos = 1, args.context
+    for _ in range(args.warmup * tokens_per_step):
+        tok = m.forward([tok], pos)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps * tokens_per_step):
+        tok = m.forward([tok], pos)
+        pos += 1
+    el = time.perf_counter() - t0
+    value = args.steps * tokens_per_step / el
+    sample = (f'oracle/qwen_ref.c (KV8 mode) decoding {tokens_per_step} tokens per step of one sequence '
+              f'at context {args.context}+ (one request at a time, as src/software/main.c serves them), '
+              f'{threads} OpenMP threads')
+    line = {'metric': 'decode tokens/s', 'value': round(value, 3), 'unit': 'tokens/s', 'impl': 'reference',
+            'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': round(1000 * el / args.steps, 3), 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'int8 weights x bf16 activations, fp32 accumulate, int8 KV',
+            'data': 'synthetic (seeded random-init int8 weights, seeded KV8 fill)',
+            'config': workload_config(args),
+            'cpu_baseline': {'value': round(value, 3), 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+                             'sample': sample},
+            'e2e': {'value': round(value, 3), 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    m.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args):
+    return {'workload': f'batched greedy decode, {args.seqs} sequences per GPU at context {args.context}+, '
+                        'Qwen2.5-0.5B W8A16 with KV8 cache',
+            'model': 'Qwen2.5-0.5B (24 layers, hidden 896, seeded random int8 weights)',
+            'seqs_per_gpu': args.seqs, 'global_batch': args.seqs * args.gpus, 'context': args.context,
+            'parallelism': f'request-sharded replicas x{args.gpus} (no inter-GPU traffic)',
+            'l2': 'inputs larger than L2 (weights 496 MB + KV ~0.88 GB per step)'}
+
+
+def run_ours(args):
+    import torch
+    import qwen_b200
+    rank, world, local = dist_setup()
+    torch.cuda.set_device(local)
+    if args.steps + args.warmup > 120:
+        raise SystemExit('--steps + --warmup must stay within one 128-key context bucket (<= 120)')
+    S, C = args.seqs, args.context
+    cap = C + 2 * (args.steps + args.warmup) + 64
+    eng = qwen_b200.Engine(device=local, max_seqs=S, max_context=cap, max_rows=256).load_synthetic(SEED)
+    for s in range(S):
+        eng.fill_kv_synthetic(s, C, SEED + 17 * s + rank)
+    rng = np.random.default_rng(SEED + rank)
+    first = rng.integers(0, VOCAB, S).astype(np.int32)
+    bufs = [torch.tensor(first, device='cuda'), torch.zeros(S, dtype=torch.int32, device='cuda')]
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def step(i):
+        a, b = bufs[i % 2], bufs[(i + 1) % 2]
+        eng.decode_step_device(ctypes.c_void_p(a.data_ptr()), S, ctypes.c_void_p(b.data_ptr()), sp)
+
+    for i in range(args.warmup):
+        step(i)
+    contexts0 = [eng.position(s) + 1 for s in range(S)]
+    barrier(world)
+    clocks = Clocks(gpu_index(local))
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    t1.record(stream)
+    barrier(world)
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    ms_max = max_over_ranks(ms, world)
+    launches = qwen_b200.lib().qwen_b200_step_launches(eng.h) * args.steps
+    value = world * S * args.steps / (ms_max / 1000.0)
+    contexts = [c + args.steps // 2 for c in contexts0]  # mean context over the timed steps
+    sbytes = step_bytes(contexts)
+    hbm, peak_kind = peaks()
+
+    # e2e: the same step through the host-buffer C ABI call
+    toks = bufs[args.warmup % 2].cpu().numpy().astype(np.uint32)
+    slots = np.arange(S, dtype=np.uint32)
+    for _ in range(2):
+        toks = eng.decode_step(slots, toks)
+    barrier(world)
+    e0 = time.perf_counter()
+    for _ in range(args.steps):
+        toks = eng.decode_step(slots, toks)
+    e_s = max_over_ranks(time.perf_counter() - e0, world)
+    e2e = {'value': round(world * S * args.steps / e_s, 1), 'unit': 'tokens/s',
+           'h2d_bytes_per_step': 3 * 4 * S, 'd2h_bytes_per_step': 4 * S,
+           'api': 'qwen_b200_decode_step (host buffers)'}
+
+    # per-kernel-class device times of a real step (events on the launching stream)
+    ms_cls = np.zeros(8, np.float32)
+    n_cls = np.zeros(8, np.uint32)
+    out = np.empty(S, np.uint32)
+    for rep in range(2):
+        rc = qwen_b200.lib().qwen_b200_profile_decode(
+            eng.h, toks.ctypes.data_as(qwen_b200._lib._P32), S, out.ctypes.data_as(qwen_b200._lib._P32),
+            ms_cls.ctypes.data_as(qwen_b200._lib._PF), n_cls.ctypes.data_as(qwen_b200._lib._P32))
+        assert rc == 0, qwen_b200.lib().qwen_b200_last_error(eng.h)
+        toks = out.copy()
+    prof_ctx = [eng.position(s) for s in range(S)]
+    cb = class_bytes(S, prof_ctx)
+    kernels = {}
+    for i, name in enumerate(CLASSES):
+        if n_cls[i]:
+            per = float(ms_cls[i]) / int(n_cls[i])
+            kernels[name] = {'launches_per_step': int(n_cls[i]), 'ms_per_step': round(float(ms_cls[i]), 4),
+                             'us_per_launch': round(1000 * per, 2),
+                             'gbs': round(cb[name] / (per / 1000) / 1e9, 1)}
+    dom = max(kernels, key=lambda k: kernels[k]['ms_per_step'])
+    dom_us = kernels[dom]['us_per_launch']
+    achieved = cb[dom] / (dom_us / 1e6) / 1e9
+    roofline = {'kernel': KERNEL_NAMES[dom], 'class': dom, 'bound': 'hbm', 'achieved': round(achieved, 1),
+                'peak': hbm, 'peak_kind': peak_kind, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4),
+                'algorithmic_bytes_per_launch': cb[dom], 'traffic': committed_traffic(dom)}
+    step_ms = ms_max / args.steps
+    step_roof = {'bytes_per_step': sbytes, 'achieved': round(sbytes / (step_ms / 1000) / 1e9, 1), 'peak': hbm,
+                 'unit': 'GB/s', 'frac': round(sbytes / (step_ms / 1000) / 1e9 / hbm, 4)}
+
+    # bs1 decode at short context (16-token prompt), slot 0
+    bs1 = bs1_decode(eng, args, stream, sp, hbm)
+
+    result = None
+    if rank == 0:
+        result = {
+            'metric': 'decode tokens/s', 'value': round(value, 1), 'unit': 'tokens/s', 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(step_ms, 4),
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+            'dtype': 'int8 weights x bf16 activations, fp32 accumulate, int8 KV',
+            'data': 'synthetic (seeded random-init int8 weights, seeded KV8 fill, random token ids)',
+            'config': workload_config(args), 'roofline': roofline, 'step_roofline': step_roof,
+            'kernels': kernels, 'e2e': e2e, 'gpu_launches': int(launches), 'bs1': bs1, 'clocks': clk}
+    if world == 1 and not args.no_cpu_baseline:
+        tps, n = cpu_decode_sample(10.0, 30.0, C, os.cpu_count() or 1)
+        result['cpu_baseline'] = {'value': round(tps, 3), 'unit': 'tokens/s', 'cores': os.cpu_count() or 1,
+                                  'kind': 'port',
+                                  'sample': f'oracle/qwen_ref.c KV8 decode of {n} tokens of one sequence at '
+                                            f'context {C}+ (one request at a time)'}
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def bs1_decode(eng, args, stream, sp, hbm):
+    import torch
+    prompt = np.zeros(16, np.uint32)
+    import qwen_b200
+    qwen_b200.lib().qwen_b200_synth_prompt(SEED, 16, prompt.ctypes.data_as(qwen_b200._lib._P32))
+    eng.reset(0)
+    tok, _ = eng.forward(0, prompt, 0)
+    a = torch.tensor([tok], dtype=torch.int32, device='cuda')
+    b = torch.zeros(1, dtype=torch.int32, device='cuda')
+    bufs = [a, b]
+    for i in range(args.warmup):
+        eng.decode_step_device(ctypes.c_void_p(bufs[i % 2].data_ptr()), 1,
+                               ctypes.c_void_p(bufs[(i + 1) % 2].data_ptr()), sp)
+    ctx0 = eng.position(0) + 1
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        j = args.warmup + i
+        eng.decode_step_device(ctypes.c_void_p(bufs[j % 2].data_ptr()), 1,
+                               ctypes.c_void_p(bufs[(j + 1) % 2].data_ptr()), sp)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    sb = step_bytes([ctx0 + args.steps // 2])
+    ach = sb / (ms / 1000) / 1e9
+    return {'value': round(1000 / ms, 1), 'unit': 'tokens/s', 'ms_per_token': round(ms, 4),
+            'context': ctx0 + args.steps // 2, 'bytes_per_token': sb, 'achieved_gbs': round(ach, 1),
+            'frac_of_hbm_roofline': round(ach / hbm, 4)}
+
+
+def gpu_index(local):
+    vis = os.environ.get('CUDA_VISIBLE_DEVICES')
+    if vis:
+        ids = [v.strip() for v in vis.split(',') if v.strip()]
+        if local < len(ids):
+            return ids[local]
+    return local
+
+
+def committed_traffic(cls):
+    """DRAM bytes per launch from the committed ncu summary, if one exists for
+    this kernel class at this workload (profiles/traffic.json)."""
+    p = REPO / 'profiles' / 'traffic.json'
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(cls)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=30)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    ap.add_argument('--seqs', type=int, default=64)
+    ap.add_argument('--context', type=int, default=2048)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit('--warmup must be >= 3')
+    if args.impl == 'reference':
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

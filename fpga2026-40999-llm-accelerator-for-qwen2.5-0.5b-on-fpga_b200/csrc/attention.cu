@@ -1,0 +1,231 @@
+// GQA decode/prefill attention over the int8 (KV8) cache, split over context
+// chunks of 128 keys so that long contexts spread across all SMs.
+//
+// Arithmetic contract (legacy_100mhz_closed/src/PC/model_backend.py:97-102 with
+// the cache dequantised as code * scale in fp32):
+//   S[t]  = bf16(fma-chain_d(q[d] * (kcode[t][d] * kscale[t])) / 8)
+//   P[t]  = bf16(exp(S[t] - max S) * (1 / sum exp(S - max S)))
+//   ctx   = bf16(sum_t P[t] * (vcode[t][d] * vscale[t]))
+// Query head h reads KV head h / 7 (repeat_interleave(7), model_backend.py:97-98).
+// The exact bf16 rounding of P needs the global max and sum before P.V, so:
+//   pass 1 (score):  S for the chunk -> workspace, chunk max m_c and
+//                    l_c = sum exp(S - m_c)
+//   pass 2 (pv):     global max / sum from all chunk stats, P for the chunk,
+//                    partial P.V -> workspace; the last CTA of a (row, kv head)
+//                    adds the partials in chunk order and writes ctx.
+// Cache layout: codes [slot][kv head][capacity][64] int8, scales
+// [slot][kv head][capacity] fp32.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+constexpr int AT = 128;  // keys per chunk
+
+struct AttnArgs {
+    const uint16_t *q;
+    const uint32_t *slots, *positions;
+    const int8_t *kc, *vc;
+    const float *ks, *vs;
+    int cap;
+    uint16_t *ctx;
+    float *S;           // [rows][14][cap]
+    float2 *stats;      // [rows][14][nck]
+    float *part;        // [rows][14][nck][64]
+    unsigned *counters; // [rows][2]
+    int nck;            // chunk capacity = ceil(cap / AT)
+};
+
+struct AttnLayout {
+    size_t s_off, st_off, part_off, cnt_off, total;
+};
+
+static AttnLayout attn_layout(int rows, int cap) {
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t nck = (size_t)(cap + AT - 1) / AT;
+    AttnLayout L;
+    L.s_off = 0;
+    L.st_off = al((size_t)rows * QB_QH * cap * 4);
+    L.part_off = L.st_off + al((size_t)rows * QB_QH * nck * 8);
+    L.cnt_off = L.part_off + al((size_t)rows * QB_QH * nck * 64 * 4);
+    L.total = L.cnt_off + al((size_t)rows * 2 * 4);
+    return L;
+}
+
+size_t attention_workspace(int rows, int cap) { return attn_layout(rows, cap).total; }
+
+__global__ void __launch_bounds__(AT) attn_score_kernel(AttnArgs a) {
+    const int c = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+    const int L = (int)a.positions[r] + 1;
+    const int t0 = c * AT;
+    if (t0 >= L) return;
+    const int slot = (int)a.slots[r];
+    __shared__ float qs[7][QB_HD];
+    __shared__ float red[AT / 32][7];
+    for (int i = threadIdx.x; i < 7 * QB_HD; i += AT)
+        qs[i / QB_HD][i % QB_HD] = bf2f(a.q[(size_t)r * QB_HID + g * 7 * QB_HD + i]);
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    const bool valid = t < L;
+    float sc[7];
+#pragma unroll
+    for (int h = 0; h < 7; ++h) sc[h] = 0.f;
+    if (valid) {
+        const size_t base = ((size_t)slot * QB_KVH + g) * a.cap + t;
+        const float s = a.ks[base];
+        const uint4 *kp = reinterpret_cast<const uint4 *>(a.kc + base * QB_HD);
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+            const uint4 kw = kp[v4];
+            const uint32_t words[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                float f[4];
+                i8x4_to_f32(words[wi], f[0], f[1], f[2], f[3]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int d = v4 * 16 + wi * 4 + j;
+                    const float kd = __fmul_rn(f[j], s);
+#pragma unroll
+                    for (int h = 0; h < 7; ++h) sc[h] = fmaf(qs[h][d], kd, sc[h]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 7; ++h) {
+            sc[h] = rbf(sc[h] * 0.125f);
+            a.S[((size_t)r * QB_QH + g * 7 + h) * a.cap + t] = sc[h];
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 7; ++h) sc[h] = -INFINITY;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float mc[7];
+#pragma unroll
+    for (int h = 0; h < 7; ++h) {
+        const float m = warp_max(sc[h]);
+        if (lane == 0) red[warp][h] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 7; ++h) {
+        float m = red[0][h];
+        for (int w = 1; w < AT / 32; ++w) m = fmaxf(m, red[w][h]);
+        mc[h] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 7; ++h) {
+        const float e = valid ? expf(sc[h] - mc[h]) : 0.f;
+        const float l = warp_sum(e);
+        if (lane == 0) red[warp][h] = l;
+    }
+    __syncthreads();
+    if (threadIdx.x < 7) {
+        const int h = threadIdx.x;
+        float l = 0.f;
+        for (int w = 0; w < AT / 32; ++w) l += red[w][h];
+        a.stats[((size_t)r * QB_QH + g * 7 + h) * a.nck + c] = make_float2(mc[h], l);
+    }
+}
+
+__global__ void __launch_bounds__(7 * QB_HD) attn_pv_kernel(AttnArgs a) {
+    const int c = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+    const int L = (int)a.positions[r] + 1;
+    const int t0 = c * AT;
+    if (t0 >= L) return;
+    const int nch = (L + AT - 1) / AT;
+    const int slot = (int)a.slots[r];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float Ms[7], Is[7];
+    __shared__ float P[7][AT];
+    __shared__ float V[AT][QB_HD];
+    __shared__ unsigned ticket;
+    if (warp < 7) {
+        const float2 *st = a.stats + ((size_t)r * QB_QH + g * 7 + warp) * a.nck;
+        float mx = -INFINITY;
+        for (int i = lane; i < nch; i += 32) mx = fmaxf(mx, st[i].x);
+        mx = warp_max(mx);
+        float z = 0.f;
+        for (int i = lane; i < nch; i += 32) {
+            const float2 s = st[i];
+            z += s.y * expf(s.x - mx);
+        }
+        z = warp_sum(z);
+        if (lane == 0) {
+            Ms[warp] = mx;
+            Is[warp] = 1.0f / z;
+        }
+    }
+    // V chunk, dequantised to fp32: V[t][d] = code * scale.
+    for (int i = tid; i < AT * 16; i += 7 * QB_HD) {
+        const int tt = i >> 4, q4 = i & 15, t = t0 + tt;
+        float f[4] = {0.f, 0.f, 0.f, 0.f};
+        if (t < L) {
+            const size_t base = ((size_t)slot * QB_KVH + g) * a.cap + t;
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(a.vc + base * QB_HD + q4 * 4);
+            const float s = a.vs[base];
+            i8x4_to_f32(w, f[0], f[1], f[2], f[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) f[j] = __fmul_rn(f[j], s);
+        }
+        *reinterpret_cast<float4 *>(&V[tt][q4 * 4]) = make_float4(f[0], f[1], f[2], f[3]);
+    }
+    __syncthreads();
+    for (int i = tid; i < 7 * AT; i += 7 * QB_HD) {
+        const int h = i / AT, tt = i % AT, t = t0 + tt;
+        float p = 0.f;
+        if (t < L) p = rbf(expf(a.S[((size_t)r * QB_QH + g * 7 + h) * a.cap + t] - Ms[h]) * Is[h]);
+        P[h][tt] = p;
+    }
+    __syncthreads();
+    const int h = tid >> 6, d = tid & 63;
+    const int nt = min(AT, L - t0);
+    float acc = 0.f;
+    for (int tt = 0; tt < nt; ++tt) acc = fmaf(P[h][tt], V[tt][d], acc);
+    float *pp = a.part + ((size_t)r * QB_QH + g * 7 + h) * a.nck * QB_HD;
+    pp[(size_t)c * QB_HD + d] = acc;
+    // The last CTA of this (row, kv head) combines the partials in chunk order.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(&a.counters[r * 2 + g], 1u);
+    __syncthreads();
+    if (ticket != (unsigned)(nch - 1)) return;
+    __threadfence();
+    float sum = 0.f;
+    for (int cc = 0; cc < nch; ++cc) sum += __ldcg(pp + (size_t)cc * QB_HD + d);
+    a.ctx[(size_t)r * QB_HID + (g * 7 + h) * QB_HD + d] = f2bf(sum);
+    if (tid == 0) a.counters[r * 2 + g] = 0u;  // ready for the next launch
+}
+
+int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
+                     const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
+                     void *ws, size_t ws_bytes, bool clear_counters, cudaStream_t st) {
+    if (rows <= 0 || max_len <= 0 || max_len > cap) return -1;
+    const AttnLayout L = attn_layout(rows, cap);
+    if (ws_bytes < L.total) return -1;
+    char *base = reinterpret_cast<char *>(ws);
+    AttnArgs a;
+    a.q = q;
+    a.slots = slots;
+    a.positions = positions;
+    a.kc = kc;
+    a.vc = vc;
+    a.ks = ks;
+    a.vs = vs;
+    a.cap = cap;
+    a.ctx = ctx;
+    a.S = reinterpret_cast<float *>(base + L.s_off);
+    a.stats = reinterpret_cast<float2 *>(base + L.st_off);
+    a.part = reinterpret_cast<float *>(base + L.part_off);
+    a.counters = reinterpret_cast<unsigned *>(base + L.cnt_off);
+    a.nck = (cap + AT - 1) / AT;
+    if (clear_counters && cudaMemsetAsync(a.counters, 0, (size_t)rows * 2 * 4, st) != cudaSuccess) return -3;
+    dim3 grid((max_len + AT - 1) / AT, QB_KVH, rows);
+    attn_score_kernel<<<grid, AT, 0, st>>>(a);
+    attn_pv_kernel<<<grid, 7 * QB_HD, 0, st>>>(a);
+    return QB_LAUNCH_CHECK();
+}
+
+}  // namespace qb

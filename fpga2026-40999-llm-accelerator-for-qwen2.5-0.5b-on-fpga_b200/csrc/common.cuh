@@ -1,0 +1,68 @@
+// Device helpers shared by the sm_100a kernels: bf16 bit conversions (round to
+// nearest even, matching torch's .to(bfloat16) used by model_backend.py:45),
+// int8 -> fp32 unpacking, streaming loads and warp reductions.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define QB_HID 896
+#define QB_FFN 4864
+#define QB_QKV 1152
+#define QB_VOCAB 151936
+#define QB_QH 14
+#define QB_KVH 2
+#define QB_HD 64
+
+namespace qb {
+
+__device__ __forceinline__ float bf2f(uint32_t b16) { return __uint_as_float(b16 << 16); }
+__device__ __forceinline__ uint16_t f2bf(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+// Round an fp32 value to the nearest bf16 value (returned as fp32).
+__device__ __forceinline__ float rbf(float x) { return bf2f(f2bf(x)); }
+// Low / high bf16 of a packed pair as fp32.
+__device__ __forceinline__ float bflo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bfhi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Four signed bytes of w as exact fp32 values: byte j is placed into the low
+// mantissa byte of 2^23 (after a +128 bias by flipping its sign bit), and the
+// bias 2^23 + 128 is subtracted.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float &f0, float &f1, float &f2, float &f3) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float bias = 8388736.0f;  // 2^23 + 128
+    f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - bias;
+    f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - bias;
+    f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - bias;
+    f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - bias;
+}
+
+// 16-byte global load that bypasses L1 allocation (weights are streamed once).
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// (value, index) argmax with the reference's tie rule: the higher index wins
+// (model_backend.py:113-114, CONFIG.JSON "greedy latest-token-index on ties").
+__device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t bi) {
+    return v > bv || (v == bv && i > bi);
+}
+
+}  // namespace qb
+
+// Launch error helper used by the host-side launchers.
+#define QB_LAUNCH_CHECK() (cudaGetLastError() == cudaSuccess ? 0 : -3)

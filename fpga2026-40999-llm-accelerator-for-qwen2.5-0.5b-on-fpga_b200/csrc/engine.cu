@@ -1,0 +1,909 @@
+// libqwen_b200 host engine: owns the device copy of the model and the KV8
+// caches, sequences the per-layer kernels (the role of the PL's layer FSM,
+// src/rtl/storage/qwen25_qkv_controller.v:123-136), emulates the CSR protocol
+// of src/software/generation.c:5-39 and exports the C ABI of qwen_b200.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "assets.h"
+#include "kernels.h"
+#include "qwen_b200.h"
+
+using namespace qb;
+
+namespace {
+
+constexpr int NL = QWEN_B200_LAYERS;
+constexpr int HID = QWEN_B200_HIDDEN;
+constexpr int FFN = QWEN_B200_FFN;
+constexpr int VOC = QWEN_B200_VOCAB;
+constexpr int QKVN = QWEN_B200_QKV;
+constexpr int CSR_IDS = 256;  // ACT_IN rows addressable through the embedding callback
+
+struct LayerW {
+    int8_t *qkv, *o, *gu, *d;  // [1152][896], [896][896], [9728][896] gate/up interleaved, [896][4864]
+    float *s_qkv, *s_o, *s_gu, *s_d;
+    uint16_t *bias, *g_attn, *g_ffn;
+};
+
+enum CsrState { CSR_IDLE = 0, CSR_BUSY = 1, CSR_DONE = 2, CSR_ERROR = 3 };
+
+}  // namespace
+
+struct qwen_b200 {
+    qwen_b200_config cfg{};
+    std::string err;
+    bool loaded = false;
+    int R = 0;  // activation rows
+    cudaStream_t stream = nullptr, cap_stream = nullptr;
+    std::vector<void *> dev_allocs;
+    // model
+    LayerW L[NL];
+    uint16_t *g_final = nullptr, *embed = nullptr;
+    int8_t *lmw = nullptr;
+    float *s_lm = nullptr, *rope = nullptr;
+    // KV8 caches: codes [layer][slot][2][cap][64], scales [layer][slot][2][cap]
+    int8_t *kc = nullptr, *vc = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    // activations
+    uint16_t *x = nullptr, *q = nullptr, *ctx = nullptr, *mid = nullptr, *xl = nullptr, *logits = nullptr;
+    uint32_t *meta = nullptr;  // [4][R]: ids | slots | positions | logit rows
+    uint32_t *tokens = nullptr, *slot_pos = nullptr;
+    void *attn_ws = nullptr, *lm_ws = nullptr;
+    size_t attn_ws_bytes = 0, lm_ws_bytes = 0;
+    // pinned staging
+    uint32_t *h_meta = nullptr, *h_tokens = nullptr, *h_slot_pos = nullptr;
+    std::vector<uint32_t> pos;  // host mirror of every slot's position
+    // decode graphs keyed by (n, context chunks, tokens_in, tokens_out)
+    std::map<std::tuple<uint32_t, uint32_t, const void *, const void *>, cudaGraphExec_t> graphs;
+    // layer dump (tests): device buffers and host destinations
+    int dump_layer = -1;
+    uint16_t *dump_host[7] = {};
+    uint16_t *d_dump = nullptr;  // [R][896 q | 256 kv | 896 ctx | 896 h | 4864 mid | 896 y]
+    // per-kernel-class CUDA events (profiled steps) and the launch count of the
+    // last enqueued step
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_ev[QWEN_B200_KCLASSES];
+    size_t prof_used[QWEN_B200_KCLASSES] = {};
+    uint32_t nlaunch = 0;
+    // CSR protocol state (slot 0)
+    uint64_t regs[128] = {};
+    uint32_t csr_ids[CSR_IDS] = {};
+    int csr_state = CSR_IDLE;
+    uint64_t csr_error = 0;
+    uint32_t csr_token = 0;
+    cudaEvent_t csr_event = nullptr;
+};
+
+namespace {
+
+int fail(qwen_b200 *h, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    h->err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                       \
+    do {                                                                                               \
+        cudaError_t e_ = (call);                                                                       \
+        if (e_ != cudaSuccess) return fail(h, QWEN_B200_EDEVICE, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+#define RK(call)                                                                           \
+    do {                                                                                   \
+        int r_ = (call);                                                                   \
+        if (r_) return fail(h, r_, "%s failed (%d): %s", #call, r_, cudaGetErrorString(cudaGetLastError())); \
+    } while (0)
+
+int dalloc(qwen_b200 *h, void **p, size_t bytes) {
+    if (cudaMalloc(p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(h, QWEN_B200_ENOMEM, "cudaMalloc(%zu) failed", bytes);
+    }
+    h->dev_allocs.push_back(*p);
+    return 0;
+}
+
+// Brackets one kernel launch of class c with a pair of events on stream st
+// when a profiled step is running; counts launches either way.
+struct LaunchScope {
+    qwen_b200 *h;
+    int c;
+    cudaStream_t st;
+    LaunchScope(qwen_b200 *h_, int c_, cudaStream_t st_, uint32_t kernels) : h(h_), c(c_), st(st_) {
+        h->nlaunch += kernels;
+        if (h->prof) record();
+    }
+    ~LaunchScope() {
+        if (h->prof) record();
+    }
+    void record() {
+        auto &pool = h->prof_ev[c];
+        if (h->prof_used[c] == pool.size()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            pool.push_back(e);
+        }
+        cudaEventRecord(pool[h->prof_used[c]++], st);
+    }
+};
+
+constexpr size_t DUMP_COLS = 896 + 256 + 896 + 896 + 4864 + 896;
+
+size_t kv_layer_codes(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * h->cfg.max_context * 64; }
+size_t kv_layer_scales(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * h->cfg.max_context; }
+
+int allocate(qwen_b200 *h) {
+    const qwen_b200_config &c = h->cfg;
+    h->R = (int)std::max(c.max_rows, c.max_seqs);
+    const size_t R = (size_t)h->R;
+    CK(cudaSetDevice(c.device));
+    CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&h->cap_stream, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&h->csr_event, cudaEventDisableTiming));
+    void *p;
+    int rc;
+    // weights: one block per layer
+    const size_t lw = (size_t)QKVN * HID + (size_t)HID * HID + (size_t)2 * FFN * HID + (size_t)HID * FFN;
+    if ((rc = dalloc(h, &p, lw * NL))) return rc;
+    for (int l = 0; l < NL; ++l) {
+        int8_t *b = (int8_t *)p + lw * l;
+        h->L[l].qkv = b;
+        h->L[l].o = b + (size_t)QKVN * HID;
+        h->L[l].gu = h->L[l].o + (size_t)HID * HID;
+        h->L[l].d = h->L[l].gu + (size_t)2 * FFN * HID;
+    }
+    const size_t ls = QKVN + HID + 2 * FFN + HID;
+    if ((rc = dalloc(h, &p, ls * NL * sizeof(float)))) return rc;
+    for (int l = 0; l < NL; ++l) {
+        float *b = (float *)p + ls * l;
+        h->L[l].s_qkv = b;
+        h->L[l].s_o = b + QKVN;
+        h->L[l].s_gu = h->L[l].s_o + HID;
+        h->L[l].s_d = h->L[l].s_gu + 2 * FFN;
+    }
+    const size_t lb = QKVN + 2 * HID;
+    if ((rc = dalloc(h, &p, (lb * NL + HID) * 2))) return rc;
+    for (int l = 0; l < NL; ++l) {
+        uint16_t *b = (uint16_t *)p + lb * l;
+        h->L[l].bias = b;
+        h->L[l].g_attn = b + QKVN;
+        h->L[l].g_ffn = b + QKVN + HID;
+    }
+    h->g_final = (uint16_t *)p + lb * NL;
+    if ((rc = dalloc(h, (void **)&h->embed, (size_t)VOC * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->lmw, (size_t)VOC * HID))) return rc;
+    if ((rc = dalloc(h, (void **)&h->s_lm, (size_t)VOC * 4))) return rc;
+    if ((rc = dalloc(h, (void **)&h->rope, (size_t)c.max_context * 64 * 4))) return rc;
+    // KV8 caches
+    if ((rc = dalloc(h, (void **)&h->kc, kv_layer_codes(h) * NL))) return rc;
+    if ((rc = dalloc(h, (void **)&h->vc, kv_layer_codes(h) * NL))) return rc;
+    if ((rc = dalloc(h, (void **)&h->ks, kv_layer_scales(h) * NL * 4))) return rc;
+    if ((rc = dalloc(h, (void **)&h->vs, kv_layer_scales(h) * NL * 4))) return rc;
+    CK(cudaMemset(h->kc, 0, kv_layer_codes(h) * NL));
+    CK(cudaMemset(h->vc, 0, kv_layer_codes(h) * NL));
+    CK(cudaMemset(h->ks, 0, kv_layer_scales(h) * NL * 4));
+    CK(cudaMemset(h->vs, 0, kv_layer_scales(h) * NL * 4));
+    // activations
+    if ((rc = dalloc(h, (void **)&h->x, R * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->q, R * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->ctx, R * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->mid, R * FFN * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->xl, R * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->logits, (size_t)VOC * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->meta, R * 4 * 4))) return rc;
+    if ((rc = dalloc(h, (void **)&h->tokens, R * 4))) return rc;
+    if ((rc = dalloc(h, (void **)&h->slot_pos, (size_t)c.max_seqs * 4))) return rc;
+    CK(cudaMemset(h->slot_pos, 0, (size_t)c.max_seqs * 4));
+    h->attn_ws_bytes = attention_workspace(h->R, (int)c.max_context);
+    if ((rc = dalloc(h, &h->attn_ws, h->attn_ws_bytes))) return rc;
+    CK(cudaMemset(h->attn_ws, 0, h->attn_ws_bytes));  // completion counters start at zero
+    h->lm_ws_bytes = lm_head_workspace(h->R, VOC);
+    if ((rc = dalloc(h, &h->lm_ws, h->lm_ws_bytes))) return rc;
+    CK(cudaMallocHost((void **)&h->h_meta, R * 4 * 4));
+    CK(cudaMallocHost((void **)&h->h_tokens, R * 4));
+    CK(cudaMallocHost((void **)&h->h_slot_pos, (size_t)c.max_seqs * 4));
+    h->pos.assign(c.max_seqs, 0);
+    std::vector<float> table((size_t)c.max_context * 64);
+    qwen_b200_rope_table(c.max_context, table.data());
+    CK(cudaMemcpy(h->rope, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int upload(qwen_b200 *h, const qa_model &m) {
+    std::vector<int8_t> gu((size_t)2 * FFN * HID), qkv((size_t)QKVN * HID);
+    std::vector<float> s(QKVN + HID + 2 * FFN + HID);
+    std::vector<uint16_t> b(QKVN + 2 * HID);
+    for (int l = 0; l < NL; ++l) {
+        memcpy(qkv.data(), m.w[l][QA_Q], (size_t)896 * HID);
+        memcpy(qkv.data() + (size_t)896 * HID, m.w[l][QA_K], (size_t)128 * HID);
+        memcpy(qkv.data() + (size_t)1024 * HID, m.w[l][QA_V], (size_t)128 * HID);
+        for (int j = 0; j < FFN; ++j) {
+            memcpy(gu.data() + (size_t)(2 * j) * HID, m.w[l][QA_GATE] + (size_t)j * HID, HID);
+            memcpy(gu.data() + (size_t)(2 * j + 1) * HID, m.w[l][QA_UP] + (size_t)j * HID, HID);
+        }
+        const uint16_t *sc = m.scale + (size_t)l * QA_SCALE_LAYER;
+        for (int i = 0; i < QKVN; ++i) s[i] = qa_bf2f(sc[i]);  // q@0 k@896 v@1024
+        for (int i = 0; i < HID; ++i) s[QKVN + i] = qa_bf2f(sc[1152 + i]);
+        for (int j = 0; j < FFN; ++j) {
+            s[QKVN + HID + 2 * j] = qa_bf2f(sc[2048 + j]);
+            s[QKVN + HID + 2 * j + 1] = qa_bf2f(sc[6912 + j]);
+        }
+        for (int i = 0; i < HID; ++i) s[QKVN + HID + 2 * FFN + i] = qa_bf2f(sc[11776 + i]);
+        memcpy(b.data(), m.bias + (size_t)l * QA_BIAS_LAYER, QKVN * 2);
+        memcpy(b.data() + QKVN, m.gamma + (size_t)l * QA_GAMMA_LAYER, (size_t)2 * HID * 2);
+        const LayerW &W = h->L[l];
+        CK(cudaMemcpy(W.qkv, qkv.data(), qkv.size(), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(W.o, m.w[l][QA_O], (size_t)HID * HID, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(W.gu, gu.data(), gu.size(), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(W.d, m.w[l][QA_DOWN], (size_t)HID * FFN, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(W.s_qkv, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(W.bias, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
+    }
+    CK(cudaMemcpy(h->g_final, m.gamma + QA_GAMMA_FINAL, HID * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(h->embed, m.embed, (size_t)VOC * HID * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(h->lmw, m.lmw, (size_t)VOC * HID, cudaMemcpyHostToDevice));
+    std::vector<float> slm(VOC);
+    for (int i = 0; i < VOC; ++i) slm[i] = qa_bf2f(m.scale[QA_SCALE_LM + i]);
+    CK(cudaMemcpy(h->s_lm, slm.data(), (size_t)VOC * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int ensure_device(qwen_b200 *h) {
+    if (!h->loaded) return fail(h, QWEN_B200_EINVAL, "no assets loaded");
+    CK(cudaSetDevice(h->cfg.device));
+    return 0;
+}
+
+// One forward over R rows whose ids/slots/positions are at meta[0..3R) with
+// stride n (ids n | slots n | positions n | logit rows n). nlog rows get the
+// LM head: rows listed at meta+3n, or all rows when identity.
+int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool want_logits, uint32_t *tokens_dst,
+                cudaStream_t st) {
+    const uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n, *lrows = h->meta + 3 * n;
+    const int cap = (int)h->cfg.max_context;
+    const float eps = h->cfg.rms_eps;
+    const bool dump = h->dump_layer >= 0 && h->d_dump;
+    {
+        LaunchScope ls(h, 0, st, 1);
+        RK(launch_embed(h->embed, ids, n, h->x, st));
+    }
+    for (int l = 0; l < NL; ++l) {
+        const LayerW &W = h->L[l];
+        int8_t *kc = h->kc + kv_layer_codes(h) * l, *vc = h->vc + kv_layer_codes(h) * l;
+        float *ks = h->ks + kv_layer_scales(h) * l, *vs = h->vs + kv_layer_scales(h) * l;
+        uint16_t *dq = nullptr;
+        if (dump && l == h->dump_layer) dq = h->d_dump;
+        QkvArgs a;
+        a.x = h->x;
+        a.rows = n;
+        a.gamma = W.g_attn;
+        a.eps = eps;
+        a.w = W.qkv;
+        a.scale = W.s_qkv;
+        a.bias = W.bias;
+        a.slots = slots;
+        a.positions = positions;
+        a.table = h->rope;
+        a.q_out = h->q;
+        a.kc = kc;
+        a.vc = vc;
+        a.ks = ks;
+        a.vs = vs;
+        a.cap = cap;
+        a.kv_out = dq ? dq + (size_t)n * 896 : nullptr;
+        {
+            LaunchScope ls(h, 1, st, 1);
+            RK(launch_qkv(a, st));
+        }
+        {
+            LaunchScope ls(h, 2, st, 2);
+            RK(launch_attention(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx, h->attn_ws,
+                                h->attn_ws_bytes, false, st));
+        }
+        if (dq) {
+            CK(cudaMemcpyAsync(dq, h->q, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+            CK(cudaMemcpyAsync(dq + (size_t)n * 1152, h->ctx, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+        }
+        {
+            LaunchScope ls(h, 3, st, 1);
+            RK(launch_gemv(EPI_RESIDUAL, h->ctx, n, HID, nullptr, 0.f, W.o, W.s_o, nullptr, HID, h->x, st));
+        }
+        if (dq) CK(cudaMemcpyAsync(dq + (size_t)n * 2048, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+        {
+            LaunchScope ls(h, 4, st, 1);
+            RK(launch_gemv(EPI_SWIGLU, h->x, n, HID, W.g_ffn, eps, W.gu, W.s_gu, nullptr, 2 * FFN, h->mid, st));
+        }
+        {
+            LaunchScope ls(h, 5, st, 1);
+            RK(launch_gemv(EPI_RESIDUAL, h->mid, n, FFN, nullptr, 0.f, W.d, W.s_d, nullptr, HID, h->x, st));
+        }
+        if (dq) {
+            CK(cudaMemcpyAsync(dq + (size_t)n * 2944, h->mid, (size_t)n * FFN * 2, cudaMemcpyDeviceToDevice, st));
+            CK(cudaMemcpyAsync(dq + (size_t)n * 7808, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+        }
+    }
+    if (nlog > 0) {
+        const uint16_t *xin = h->x;
+        if (!identity) {
+            LaunchScope ls(h, 7, st, 1);
+            RK(launch_gather_rows(h->x, lrows, nlog, h->xl, st));
+            xin = h->xl;
+        }
+        LaunchScope ls(h, 6, st, 2);
+        RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw, h->s_lm, VOC, want_logits ? h->logits : nullptr,
+                          tokens_dst, h->lm_ws, h->lm_ws_bytes, st));
+    }
+    return 0;
+}
+
+int sync_slot_positions(qwen_b200 *h, cudaStream_t st) {
+    memcpy(h->h_slot_pos, h->pos.data(), h->pos.size() * 4);
+    CK(cudaMemcpyAsync(h->slot_pos, h->h_slot_pos, h->pos.size() * 4, cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
+// Copies dump buffers of one forward chunk (rows [r0, r0+n)) to the host.
+int copy_dump(qwen_b200 *h, int n, int r0) {
+    uint16_t *d = h->d_dump;
+    uint16_t **o = h->dump_host;
+    struct Part {
+        uint16_t *dst;
+        size_t off, cols, pitch_cols, col0;
+    } parts[7] = {
+        {o[0], 0, 896, 896, 0},          {o[1], (size_t)n * 896, 128, 256, 0},
+        {o[2], (size_t)n * 896, 128, 256, 128}, {o[3], (size_t)n * 1152, 896, 896, 0},
+        {o[4], (size_t)n * 2048, 896, 896, 0}, {o[5], (size_t)n * 2944, 4864, 4864, 0},
+        {o[6], (size_t)n * 7808, 896, 896, 0}};
+    for (const Part &p : parts) {
+        if (!p.dst) continue;
+        CK(cudaMemcpy2D(p.dst + (size_t)r0 * p.cols, p.cols * 2, d + p.off + p.col0, p.pitch_cols * 2, p.cols * 2,
+                        (size_t)n, cudaMemcpyDeviceToHost));
+    }
+    return 0;
+}
+
+void csr_start(qwen_b200 *h) {
+    auto error = [&](uint64_t code) {
+        h->csr_state = CSR_ERROR;
+        h->csr_error = code;
+    };
+    // Error codes at 0x30: 1 malformed request, 2 CUDA error, 3 no model
+    // loaded, 4 START while busy.
+    if (h->csr_state == CSR_BUSY) return error(4);
+    const uint64_t mode = h->regs[0x80 / 8] & 1, rows = h->regs[0x88 / 8], ctxlen = h->regs[0x90 / 8],
+                   position = h->regs[0x98 / 8];
+    const uint32_t cached = h->loaded ? h->pos[0] : 0;
+    if (rows == 0 || rows > CSR_IDS || rows > std::max(h->cfg.max_rows, h->cfg.max_seqs) ||
+        ctxlen != position + rows || position + rows > h->cfg.max_context)
+        return error(1);
+    if (mode == 0 ? position != 0 : position != cached) return error(1);
+    for (uint64_t i = 0; i < rows; ++i)
+        if (h->csr_ids[i] >= (uint32_t)VOC) return error(1);
+    if (!h->loaded || cudaSetDevice(h->cfg.device) != cudaSuccess) return error(3);
+    if (mode == 0) h->pos[0] = 0;
+    const int n = (int)rows;
+    for (int i = 0; i < n; ++i) {
+        h->h_meta[i] = h->csr_ids[i];
+        h->h_meta[n + i] = 0;
+        h->h_meta[2 * n + i] = (uint32_t)position + (uint32_t)i;
+    }
+    h->h_meta[3 * n] = (uint32_t)(n - 1);
+    cudaStream_t st = h->stream;
+    bool ok = cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * n + 1) * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    ok = ok && run_forward(h, n, (int)(position + rows), 1, false, false, h->tokens, st) == 0;
+    ok = ok && cudaMemcpyAsync(h->h_tokens, h->tokens, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    ok = ok && cudaEventRecord(h->csr_event, st) == cudaSuccess;
+    if (!ok) return error(2);
+    h->pos[0] = (uint32_t)(position + rows);
+    h->csr_state = CSR_BUSY;
+}
+
+}  // namespace
+
+// ============================================================== C ABI
+extern "C" {
+
+void qwen_b200_default_config(qwen_b200_config *cfg) {
+    if (!cfg) return;
+    cfg->device = 0;
+    cfg->max_seqs = 1;
+    cfg->max_context = 256;
+    cfg->max_rows = 256;
+    cfg->rms_eps = 1e-6f;
+    cfg->flags = 0;
+}
+
+int qwen_b200_open(const qwen_b200_config *cfg, qwen_b200 **out) {
+    if (!out) return QWEN_B200_EINVAL;
+    *out = nullptr;
+    qwen_b200_config c;
+    qwen_b200_default_config(&c);
+    if (cfg) c = *cfg;
+    if (c.max_seqs == 0 || c.max_context == 0 || c.max_rows == 0 || c.device < 0 || !(c.rms_eps > 0.f))
+        return QWEN_B200_EINVAL;
+    qwen_b200 *h = new (std::nothrow) qwen_b200();
+    if (!h) return QWEN_B200_ENOMEM;
+    h->cfg = c;
+    *out = h;
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_close(qwen_b200 *h) {
+    if (!h) return QWEN_B200_EINVAL;
+    if (h->loaded) {
+        cudaSetDevice(h->cfg.device);
+        cudaDeviceSynchronize();
+        for (auto &kv : h->graphs) cudaGraphExecDestroy(kv.second);
+        for (auto &pool : h->prof_ev)
+            for (cudaEvent_t e : pool) cudaEventDestroy(e);
+        for (void *p : h->dev_allocs) cudaFree(p);
+        if (h->d_dump) cudaFree(h->d_dump);
+        cudaFreeHost(h->h_meta);
+        cudaFreeHost(h->h_tokens);
+        cudaFreeHost(h->h_slot_pos);
+        if (h->csr_event) cudaEventDestroy(h->csr_event);
+        if (h->stream) cudaStreamDestroy(h->stream);
+        if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
+    }
+    delete h;
+    return QWEN_B200_OK;
+}
+
+const char *qwen_b200_last_error(const qwen_b200 *h) { return h ? h->err.c_str() : "null handle"; }
+
+static int load_model(qwen_b200 *h, qa_model &m) {
+    int rc = allocate(h);
+    if (!rc) rc = upload(h, m);
+    qa_free(&m);
+    if (!rc) {
+        CK(cudaDeviceSynchronize());
+        h->loaded = true;
+    }
+    return rc;
+}
+
+int qwen_b200_load_assets(qwen_b200 *h, const char *sd_root) {
+    if (!h || !sd_root) return QWEN_B200_EINVAL;
+    if (h->loaded) return fail(h, QWEN_B200_EINVAL, "assets already loaded");
+    qa_model m;
+    char err[512] = "";
+    int rc = qa_read(sd_root, &m, err, sizeof(err));
+    if (rc) return fail(h, rc, "%s", err);
+    return load_model(h, m);
+}
+
+int qwen_b200_load_synthetic(qwen_b200 *h, uint64_t seed) {
+    if (!h) return QWEN_B200_EINVAL;
+    if (h->loaded) return fail(h, QWEN_B200_EINVAL, "assets already loaded");
+    qa_model m;
+    if (qa_alloc(&m)) {
+        qa_free(&m);
+        return fail(h, QWEN_B200_ENOMEM, "host allocation failed");
+    }
+    qa_generate(seed, &m);
+    return load_model(h, m);
+}
+
+int qwen_b200_synth_write(const char *sd_root, uint64_t seed) {
+    if (!sd_root) return QWEN_B200_EINVAL;
+    qa_model m;
+    if (qa_alloc(&m)) {
+        qa_free(&m);
+        return QWEN_B200_ENOMEM;
+    }
+    qa_generate(seed, &m);
+    int rc = qa_write(&m, sd_root, seed);
+    qa_free(&m);
+    return rc;
+}
+
+void qwen_b200_synth_prompt(uint64_t seed, uint32_t n, uint32_t *ids) {
+    if (ids) qa_prompt(seed, n, ids);
+}
+
+void qwen_b200_rope_table(uint32_t positions, float *table) {
+    // 1 / 1e6^(2i/64) rounded to fp32, phase = pos * inv in fp32, cos/sin of
+    // that fp32 phase rounded to fp32 (model_backend.py:41,74-76).
+    float inv[32];
+    for (int i = 0; i < 32; ++i) inv[i] = 1.0f / (float)pow(1000000.0, (double)(2 * i) / 64.0);
+    for (uint32_t p = 0; p < positions; ++p)
+        for (int i = 0; i < 32; ++i) {
+            const float phase = (float)p * inv[i];
+            table[(size_t)p * 64 + i] = (float)cos((double)phase);
+            table[(size_t)p * 64 + 32 + i] = (float)sin((double)phase);
+        }
+}
+
+int qwen_b200_reset(qwen_b200 *h, uint32_t slot) {
+    if (!h || slot >= h->cfg.max_seqs) return QWEN_B200_EINVAL;
+    if (!h->loaded) return QWEN_B200_OK;
+    h->pos[slot] = 0;
+    CK(cudaSetDevice(h->cfg.device));
+    return sync_slot_positions(h, h->stream) ? QWEN_B200_EDEVICE : QWEN_B200_OK;
+}
+
+int qwen_b200_position(const qwen_b200 *h, uint32_t slot, uint32_t *position) {
+    if (!h || !position || slot >= h->cfg.max_seqs) return QWEN_B200_EINVAL;
+    *position = h->loaded ? h->pos[slot] : 0;
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t rows, uint32_t position,
+                      uint32_t *token, uint16_t *logits) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (!ids || slot >= h->cfg.max_seqs) return fail(h, QWEN_B200_EINVAL, "bad slot or ids");
+    for (uint32_t i = 0; i < rows; ++i)
+        if (ids[i] >= (uint32_t)VOC) return fail(h, QWEN_B200_EINVAL, "token id %u >= vocab", ids[i]);
+    if (position != h->pos[slot] || rows == 0 || (uint64_t)position + rows > h->cfg.max_context)
+        return fail(h, QWEN_B200_ESTATE, "KV position mismatch pos=%u cached=%u ids=%u", position, h->pos[slot],
+                    rows);
+    cudaStream_t st = h->stream;
+    for (uint32_t c0 = 0; c0 < rows; c0 += (uint32_t)h->cfg.max_rows) {
+        const int n = (int)std::min<uint32_t>(h->cfg.max_rows, rows - c0);
+        const bool last = c0 + (uint32_t)n == rows;
+        for (int i = 0; i < n; ++i) {
+            h->h_meta[i] = ids[c0 + i];
+            h->h_meta[n + i] = slot;
+            h->h_meta[2 * n + i] = position + c0 + (uint32_t)i;
+        }
+        h->h_meta[3 * n] = (uint32_t)(n - 1);
+        CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * n + 1) * 4, cudaMemcpyHostToDevice, st));
+        rc = run_forward(h, n, (int)(position + c0 + (uint32_t)n), last ? 1 : 0, n == 1, last && logits, h->tokens,
+                         st);
+        if (rc) return rc;
+        if (h->dump_layer >= 0 && h->d_dump) {
+            CK(cudaStreamSynchronize(st));
+            if ((rc = copy_dump(h, n, (int)c0))) return rc;
+        }
+    }
+    CK(cudaMemcpyAsync(h->h_tokens, h->tokens, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (logits) CK(cudaMemcpy(logits, h->logits, (size_t)VOC * 2, cudaMemcpyDeviceToHost));
+    h->pos[slot] = position + rows;
+    if ((rc = sync_slot_positions(h, st))) return rc;
+    if (h->h_tokens[0] >= (uint32_t)VOC) return fail(h, QWEN_B200_ETOKEN, "token %u", h->h_tokens[0]);
+    if (token) *token = h->h_tokens[0];
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
+                          uint32_t *tokens_out) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (!slots || !tokens_in || !tokens_out || n == 0 || n > h->cfg.max_seqs || (int)n > h->R)
+        return fail(h, QWEN_B200_EINVAL, "bad decode batch");
+    std::vector<char> seen(h->cfg.max_seqs, 0);
+    uint32_t max_len = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (slots[i] >= h->cfg.max_seqs || seen[slots[i]]) return fail(h, QWEN_B200_EINVAL, "bad or repeated slot");
+        seen[slots[i]] = 1;
+        if (tokens_in[i] >= (uint32_t)VOC) return fail(h, QWEN_B200_EINVAL, "token id %u >= vocab", tokens_in[i]);
+        if (h->pos[slots[i]] >= h->cfg.max_context) return fail(h, QWEN_B200_ESTATE, "slot %u is full", slots[i]);
+        max_len = std::max(max_len, h->pos[slots[i]] + 1);
+    }
+    cudaStream_t st = h->stream;
+    for (uint32_t i = 0; i < n; ++i) {
+        h->h_meta[i] = tokens_in[i];
+        h->h_meta[n + i] = slots[i];
+        h->h_meta[2 * n + i] = h->pos[slots[i]];
+    }
+    CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)3 * n * 4, cudaMemcpyHostToDevice, st));
+    h->nlaunch = 0;
+    if ((rc = run_forward(h, (int)n, (int)max_len, (int)n, true, false, h->tokens, st))) return rc;
+    CK(cudaMemcpyAsync(h->h_tokens, h->tokens, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    for (uint32_t i = 0; i < n; ++i) {
+        h->pos[slots[i]] += 1;
+        tokens_out[i] = h->h_tokens[i];
+    }
+    if ((rc = sync_slot_positions(h, st))) return rc;
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens_out[i] >= (uint32_t)VOC) return fail(h, QWEN_B200_ETOKEN, "token %u", tokens_out[i]);
+    return QWEN_B200_OK;
+}
+
+static int enqueue_device_step(qwen_b200 *h, const uint32_t *d_in, int n, int max_len, uint32_t *d_out,
+                               cudaStream_t st) {
+    uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n;
+    h->nlaunch = 0;
+    {
+        LaunchScope ls(h, 7, st, 1);
+        RK(launch_decode_prologue(d_in, n, h->slot_pos, ids, slots, positions, st));
+    }
+    int rc = run_forward(h, n, max_len, n, true, false, d_out, st);
+    if (rc) return rc;
+    LaunchScope ls(h, 7, st, 1);
+    RK(launch_decode_epilogue(n, h->slot_pos, st));
+    return 0;
+}
+
+int qwen_b200_decode_step_device(qwen_b200 *h, const uint32_t *d_tokens_in, uint32_t n, uint32_t *d_tokens_out,
+                                 void *stream) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (!d_tokens_in || !d_tokens_out || n == 0 || n > h->cfg.max_seqs || (int)n > h->R)
+        return fail(h, QWEN_B200_EINVAL, "bad decode batch");
+    uint32_t max_len = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (h->pos[i] >= h->cfg.max_context) return fail(h, QWEN_B200_ESTATE, "slot %u is full", i);
+        max_len = std::max(max_len, h->pos[i] + 1);
+    }
+    const uint32_t chunks = (max_len + 127) / 128;
+    const int bucket_len = (int)std::min<uint32_t>(chunks * 128, h->cfg.max_context);
+    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    const auto key = std::make_tuple(n, chunks, (const void *)d_tokens_in, (const void *)d_tokens_out);
+    auto it = h->graphs.find(key);
+    if (it != h->graphs.end()) {
+        CK(cudaGraphLaunch(it->second, st));
+    } else {
+        if ((rc = enqueue_device_step(h, d_tokens_in, (int)n, bucket_len, d_tokens_out, st))) return rc;
+        cudaGraph_t graph;
+        CK(cudaStreamBeginCapture(h->cap_stream, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_device_step(h, d_tokens_in, (int)n, bucket_len, d_tokens_out, h->cap_stream);
+        cudaError_t e = cudaStreamEndCapture(h->cap_stream, &graph);
+        if (rc) return rc;
+        if (e != cudaSuccess) return fail(h, QWEN_B200_EDEVICE, "graph capture: %s", cudaGetErrorString(e));
+        cudaGraphExec_t exec;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail(h, QWEN_B200_EDEVICE, "graph instantiate: %s", cudaGetErrorString(e));
+        h->graphs[key] = exec;
+    }
+    for (uint32_t i = 0; i < n; ++i) h->pos[i] += 1;
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_fill_kv_synthetic(qwen_b200 *h, uint32_t slot, uint32_t length, uint64_t seed) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (slot >= h->cfg.max_seqs || length == 0 || length > h->cfg.max_context)
+        return fail(h, QWEN_B200_EINVAL, "bad slot or length");
+    RK(launch_fill_kv(h->kc, h->ks, h->vc, h->vs, NL, (int)h->cfg.max_seqs, (int)slot, (int)h->cfg.max_context,
+                      (int)length, seed, h->stream));
+    h->pos[slot] = length;
+    if ((rc = sync_slot_positions(h, h->stream))) return rc;
+    CK(cudaStreamSynchronize(h->stream));
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_read_kv(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, int8_t *kcodes, float *kscales,
+                      int8_t *vcodes, float *vscales) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (slot >= h->cfg.max_seqs || layer >= (uint32_t)NL || n > h->cfg.max_context)
+        return fail(h, QWEN_B200_EINVAL, "bad slot/layer/length");
+    CK(cudaStreamSynchronize(h->stream));
+    const size_t cap = h->cfg.max_context;
+    for (int g = 0; g < 2; ++g) {
+        const size_t row = ((size_t)slot * 2 + g) * cap;
+        if (kcodes)
+            CK(cudaMemcpy(kcodes + (size_t)g * n * 64, h->kc + kv_layer_codes(h) * layer + row * 64, (size_t)n * 64,
+                          cudaMemcpyDeviceToHost));
+        if (vcodes)
+            CK(cudaMemcpy(vcodes + (size_t)g * n * 64, h->vc + kv_layer_codes(h) * layer + row * 64, (size_t)n * 64,
+                          cudaMemcpyDeviceToHost));
+        if (kscales)
+            CK(cudaMemcpy(kscales + (size_t)g * n, h->ks + kv_layer_scales(h) * layer + row, (size_t)n * 4,
+                          cudaMemcpyDeviceToHost));
+        if (vscales)
+            CK(cudaMemcpy(vscales + (size_t)g * n, h->vs + kv_layer_scales(h) * layer + row, (size_t)n * 4,
+                          cudaMemcpyDeviceToHost));
+    }
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_set_dump(qwen_b200 *h, int layer, uint16_t *q, uint16_t *k, uint16_t *v, uint16_t *ctx,
+                       uint16_t *hbuf, uint16_t *mid, uint16_t *y) {
+    if (!h || layer >= NL) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    h->dump_layer = layer;
+    uint16_t *ptrs[7] = {q, k, v, ctx, hbuf, mid, y};
+    memcpy(h->dump_host, ptrs, sizeof(ptrs));
+    if (layer >= 0 && !h->d_dump) CK(cudaMalloc((void **)&h->d_dump, (size_t)h->R * DUMP_COLS * 2));
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_profile_decode(qwen_b200 *h, const uint32_t *tokens_in, uint32_t n, uint32_t *tokens_out,
+                             float *ms, uint32_t *launches) {
+    if (!h || !ms || !launches) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    std::vector<uint32_t> slots(n);
+    for (uint32_t i = 0; i < n; ++i) slots[i] = i;
+    for (int c = 0; c < QWEN_B200_KCLASSES; ++c) h->prof_used[c] = 0;
+    h->prof = true;
+    rc = qwen_b200_decode_step(h, slots.data(), tokens_in, n, tokens_out);
+    h->prof = false;
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(h->stream));
+    for (int c = 0; c < QWEN_B200_KCLASSES; ++c) {
+        float total = 0.f;
+        for (size_t i = 0; i + 1 < h->prof_used[c]; i += 2) {
+            float t = 0.f;
+            CK(cudaEventElapsedTime(&t, h->prof_ev[c][i], h->prof_ev[c][i + 1]));
+            total += t;
+        }
+        ms[c] = total;
+        launches[c] = (uint32_t)(h->prof_used[c] / 2);
+    }
+    return QWEN_B200_OK;
+}
+
+uint32_t qwen_b200_step_launches(const qwen_b200 *h) { return h ? h->nlaunch : 0; }
+
+// ----------------------------------------------------------------- CSR protocol
+void qwen_b200_csr_write(void *ctx, unsigned offset, uint64_t value) {
+    qwen_b200 *h = (qwen_b200 *)ctx;
+    if (!h || offset % 8 || offset / 8 >= 128) return;
+    h->regs[offset / 8] = value;
+    if (offset != QWEN_B200_CSR_CONTROL) return;
+    if (value & 8u) {  // CLEAR: drop a latched error / finished result
+        if (h->csr_state != CSR_BUSY) h->csr_state = CSR_IDLE;
+        h->csr_error = 0;
+    }
+    if (value & 1u) csr_start(h);
+    h->regs[offset / 8] = 0;  // the control register reads back 0 (no IRQ)
+}
+
+uint64_t qwen_b200_csr_read(void *ctx, unsigned offset) {
+    qwen_b200 *h = (qwen_b200 *)ctx;
+    if (!h) return 0;
+    switch (offset) {
+        case QWEN_B200_CSR_ID: return QWEN_B200_ID_VALUE;
+        case QWEN_B200_CSR_VERSION: return QWEN_B200_VERSION_VALUE;
+        case QWEN_B200_CSR_STATUS:
+            if (h->csr_state == CSR_BUSY) {
+                cudaSetDevice(h->cfg.device);
+                cudaError_t e = cudaEventQuery(h->csr_event);
+                if (e == cudaErrorNotReady) return 0x2;
+                if (e != cudaSuccess) {
+                    h->csr_state = CSR_ERROR;
+                    h->csr_error = 2;
+                } else {
+                    h->csr_token = h->h_tokens[0];
+                    h->csr_state = CSR_DONE;
+                }
+            }
+            if (h->csr_state == CSR_ERROR) return 0x8;
+            if (h->csr_state == CSR_DONE) return 0x44;
+            return 0x0;
+        case QWEN_B200_CSR_ERROR: return h->csr_error;
+        case QWEN_B200_CSR_BEST_TOKEN: return h->csr_token & 0x3ffffu;
+        default: return (offset % 8 || offset / 8 >= 128) ? 0 : h->regs[offset / 8];
+    }
+}
+
+void qwen_b200_embedding(void *ctx, unsigned token, unsigned row) {
+    qwen_b200 *h = (qwen_b200 *)ctx;
+    if (h && row < CSR_IDS) h->csr_ids[row] = token;
+}
+
+void qwen_b200_clear(void *ctx) {
+    qwen_b200 *h = (qwen_b200 *)ctx;
+    if (!h) return;
+    if (h->csr_state == CSR_BUSY && h->loaded) {
+        cudaSetDevice(h->cfg.device);
+        cudaEventSynchronize(h->csr_event);
+    }
+    h->csr_state = CSR_IDLE;
+    h->csr_error = 0;
+    qwen_b200_reset(h, 0);
+}
+
+// ------------------------------------------------------------ operator level
+int qwen_b200_op_embed(const uint16_t *embed, const uint32_t *ids, uint32_t rows, uint16_t *x, void *stream) {
+    if (!embed || !ids || !x) return QWEN_B200_EINVAL;
+    return launch_embed(embed, ids, (int)rows, x, (cudaStream_t)stream);
+}
+
+int qwen_b200_op_rmsnorm(const uint16_t *x, const uint16_t *gamma, uint32_t rows, float eps, uint16_t *out,
+                         void *stream) {
+    if (!x || !gamma || !out) return QWEN_B200_EINVAL;
+    return launch_rmsnorm(x, gamma, (int)rows, eps, out, (cudaStream_t)stream);
+}
+
+int qwen_b200_op_gemm_w8a16(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w, const float *scale,
+                            uint32_t n, const uint16_t *bias, uint16_t *y, void *stream) {
+    if (!x || !w || !scale || !y) return QWEN_B200_EINVAL;
+    return launch_gemv(bias ? EPI_BIAS : EPI_PLAIN, x, (int)rows, (int)k, nullptr, 0.f, w, scale, bias, (int)n, y,
+                       (cudaStream_t)stream);
+}
+
+int qwen_b200_op_gemm_w8a16_residual(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
+                                     const float *scale, uint32_t n, uint16_t *y, void *stream) {
+    if (!x || !w || !scale || !y) return QWEN_B200_EINVAL;
+    return launch_gemv(EPI_RESIDUAL, x, (int)rows, (int)k, nullptr, 0.f, w, scale, nullptr, (int)n, y,
+                       (cudaStream_t)stream);
+}
+
+int qwen_b200_op_rope(uint16_t *x, uint32_t rows, uint32_t heads, const uint32_t *positions, const float *table,
+                      void *stream) {
+    if (!x || !positions || !table) return QWEN_B200_EINVAL;
+    return launch_rope(x, (int)rows, (int)heads, positions, table, (cudaStream_t)stream);
+}
+
+int qwen_b200_op_kv8_append(const uint16_t *kv, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                            int8_t *codes, float *scales, uint32_t capacity, void *stream) {
+    if (!kv || !slots || !positions || !codes || !scales) return QWEN_B200_EINVAL;
+    return launch_kv8_append(kv, (int)rows, slots, positions, codes, scales, (int)capacity, (cudaStream_t)stream);
+}
+
+int qwen_b200_op_qkv(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w,
+                     const float *scale, const uint16_t *bias, const uint32_t *slots, const uint32_t *positions,
+                     const float *table, uint16_t *q_out, int8_t *kcodes, float *kscales, int8_t *vcodes,
+                     float *vscales, uint32_t capacity, void *stream) {
+    if (!x || !gamma || !w || !scale || !bias || !slots || !positions || !table || !q_out || !kcodes || !kscales ||
+        !vcodes || !vscales)
+        return QWEN_B200_EINVAL;
+    QkvArgs a;
+    a.x = x;
+    a.rows = (int)rows;
+    a.gamma = gamma;
+    a.eps = eps;
+    a.w = w;
+    a.scale = scale;
+    a.bias = bias;
+    a.slots = slots;
+    a.positions = positions;
+    a.table = table;
+    a.q_out = q_out;
+    a.kc = kcodes;
+    a.vc = vcodes;
+    a.ks = kscales;
+    a.vs = vscales;
+    a.cap = (int)capacity;
+    a.kv_out = nullptr;
+    return launch_qkv(a, (cudaStream_t)stream);
+}
+
+size_t qwen_b200_attention_workspace(uint32_t rows, uint32_t capacity) {
+    return attention_workspace((int)rows, (int)capacity);
+}
+
+int qwen_b200_op_attention(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                           uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
+                           const float *vscales, uint32_t capacity, uint16_t *ctx, void *workspace,
+                           size_t workspace_bytes, void *stream) {
+    if (!q || !slots || !positions || !kcodes || !kscales || !vcodes || !vscales || !ctx || !workspace)
+        return QWEN_B200_EINVAL;
+    return launch_attention(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
+                            (int)capacity, ctx, workspace, workspace_bytes, true, (cudaStream_t)stream);
+}
+
+int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w_gu,
+                        const float *s_gu, uint16_t *mid, void *stream) {
+    if (!x || !w_gu || !s_gu || !mid) return QWEN_B200_EINVAL;
+    return launch_gemv(EPI_SWIGLU, x, (int)rows, HID, gamma, eps, w_gu, s_gu, nullptr, 2 * FFN, mid,
+                       (cudaStream_t)stream);
+}
+
+size_t qwen_b200_lm_head_workspace(uint32_t rows, uint32_t vocab) { return lm_head_workspace((int)rows, (int)vocab); }
+
+int qwen_b200_op_lm_head_argmax(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps,
+                                const int8_t *w, const float *scale, uint32_t vocab, uint16_t *logits,
+                                uint32_t *tokens, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!x || !w || !scale || !tokens || !workspace) return QWEN_B200_EINVAL;
+    return launch_lm_head(x, (int)rows, gamma, eps, w, scale, (int)vocab, logits, tokens, workspace,
+                          workspace_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+// Host-side launchers of the sm_100a kernels. Every launcher enqueues on the
+// given stream and returns 0 or a QWEN_B200_* status (-1 bad shape, -3 CUDA).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace qb {
+
+enum Epi { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3 };
+
+// y = epi(bf16(bf16(norm?(x) W^T) * scale)); W int8 row-major [n][k].
+// EPI_SWIGLU: W holds interleaved gate/up rows, y is [rows][n/2].
+// gamma != nullptr fuses the RMSNorm prologue (k must be 896).
+int launch_gemv(int epi, const uint16_t *x, int rows, int k, const uint16_t *gamma, float eps, const int8_t *w,
+                const float *scale, const uint16_t *bias, int n, uint16_t *y, cudaStream_t st);
+
+// RMSNorm + QKV + bias + RoPE + KV8 append (one CTA per 64-row head block).
+struct QkvArgs {
+    const uint16_t *x;
+    int rows;
+    const uint16_t *gamma;
+    float eps;
+    const int8_t *w;       // [1152][896]
+    const float *scale;    // [1152]
+    const uint16_t *bias;  // [1152]
+    const uint32_t *slots, *positions;
+    const float *table;    // [capacity][64]
+    uint16_t *q_out;       // [rows][896]
+    int8_t *kc, *vc;       // [slots][2][cap][64]
+    float *ks, *vs;        // [slots][2][cap]
+    int cap;
+    uint16_t *kv_out;      // nullable [rows][256]: post-RoPE k (128) | v (128), bf16
+};
+int launch_qkv(const QkvArgs &a, cudaStream_t st);
+
+// Final RMSNorm + LM head + argmax. part: [rows][nblocks] (value, index).
+size_t lm_head_workspace(int rows, int vocab);
+int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
+                   const float *scale, int vocab, uint16_t *logits, uint32_t *tokens, void *ws, size_t ws_bytes,
+                   cudaStream_t st);
+
+// Attention over a KV8 cache (two passes + last-block combine).
+size_t attention_workspace(int rows, int cap);
+int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
+                     const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
+                     void *ws, size_t ws_bytes, bool clear_counters, cudaStream_t st);
+
+int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t *x, cudaStream_t st);
+int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st);
+int launch_rope(uint16_t *x, int rows, int heads, const uint32_t *positions, const float *table, cudaStream_t st);
+int launch_kv8_append(const uint16_t *kv, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *codes,
+                      float *scales, int cap, cudaStream_t st);
+int launch_gather_rows(const uint16_t *x, const uint32_t *rows_idx, int n, uint16_t *out, cudaStream_t st);
+// Decode-step bookkeeping for slots 0..n-1: ids/slots/positions from the
+// device position table, and the table's advance after the step.
+int launch_decode_prologue(const uint32_t *tokens_in, int n, const uint32_t *slot_pos, uint32_t *ids,
+                           uint32_t *slots, uint32_t *positions, cudaStream_t st);
+int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
+// Seeded synthetic KV8 contents for positions [0, length) of one slot, all layers.
+int launch_fill_kv(int8_t *kc, float *ks, int8_t *vc, float *vs, int layers, int nslots, int slot, int cap,
+                   int length, uint64_t seed, cudaStream_t st);
+
+}  // namespace qb

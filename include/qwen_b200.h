@@ -1,0 +1,211 @@
+/* libqwen_b200 — B200 (sm_100a) engine for the Qwen2.5-0.5B W8A16 / KV8 decode
+ * path that the reference runs in KV260 programmable logic.
+ *
+ * The boundary keeps the reference's host call surface:
+ *   - the qgen_ops CSR protocol (src/software/generation.h:5-18): write / read /
+ *     embedding callbacks, START at 0x10, status at 0x18, token at 0x1f8;
+ *   - the behavioural model's Model.forward(ids, position) / clear()
+ *     (legacy_100mhz_closed/src/PC/model_backend.py:57-115);
+ *   - one operator-level entry per PL stage (embedding, RMSNorm, W8A16 GEMM,
+ *     RoPE, KV8 quantise-append, GQA attention, SwiGLU FFN, LM head + argmax).
+ * Plain C types only: bf16 tensors are uint16_t bit patterns, device pointers
+ * are CUDA global-memory addresses, streams are cudaStream_t passed as void*.
+ * One handle per GPU; a handle is not thread-safe; one host thread per handle.
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Model geometry (legacy_100mhz_closed/board/deployment/QWEN25/CONFIG.JSON). */
+#define QWEN_B200_LAYERS 24
+#define QWEN_B200_HIDDEN 896
+#define QWEN_B200_FFN 4864
+#define QWEN_B200_Q_HEADS 14
+#define QWEN_B200_KV_HEADS 2
+#define QWEN_B200_HEAD_DIM 64
+#define QWEN_B200_QKV 1152
+#define QWEN_B200_VOCAB 151936
+
+/* Status codes. -1..-5 keep the meanings of src/software/generation.h:16. */
+#define QWEN_B200_OK 0
+#define QWEN_B200_EINVAL (-1)   /* bad input */
+#define QWEN_B200_ETIMEOUT (-2) /* a bounded device wait expired */
+#define QWEN_B200_EDEVICE (-3)  /* CUDA error (the reference's "PL error") */
+#define QWEN_B200_ETOKEN (-4)   /* produced token id >= vocab */
+#define QWEN_B200_EOUTPUT (-5)  /* output buffer error */
+#define QWEN_B200_ENOMEM (-6)   /* device or host allocation failed */
+#define QWEN_B200_EIO (-7)      /* asset file missing or of the wrong size */
+#define QWEN_B200_ESTATE (-8)   /* KV position mismatch (model_backend.py:82-83) */
+
+/* CSR map emulated by qwen_b200_csr_read/write (src/software/README.md CSR
+ * table; src/rtl/qwen25_compute_cfg.v, qwen25_result_regs.v). */
+#define QWEN_B200_CSR_ID 0x0000
+#define QWEN_B200_CSR_VERSION 0x0008
+#define QWEN_B200_CSR_CONTROL 0x0010 /* bit0 START, bit3 CLEAR */
+#define QWEN_B200_CSR_STATUS 0x0018  /* done <=> (s & 0x46) == 0x44; bit3 error */
+#define QWEN_B200_CSR_ERROR 0x0030
+#define QWEN_B200_CSR_RUN_MODE 0x0080 /* 0 prefill (clears the context), 1 decode */
+#define QWEN_B200_CSR_SEQ_LEN 0x0088
+#define QWEN_B200_CSR_CONTEXT_LEN 0x0090
+#define QWEN_B200_CSR_TOKEN_POS 0x0098
+#define QWEN_B200_CSR_BEST_TOKEN 0x01f8
+#define QWEN_B200_ID_VALUE 0x515732354b563236ULL
+#define QWEN_B200_VERSION_VALUE 0x10000ULL
+
+typedef struct qwen_b200 qwen_b200;
+
+typedef struct qwen_b200_config {
+    int device;           /* CUDA device ordinal */
+    uint32_t max_seqs;    /* sequence slots (KV caches) */
+    uint32_t max_context; /* KV capacity per slot, tokens (reference firmware: 256) */
+    uint32_t max_rows;    /* rows per forward chunk; longer prompts are chunked */
+    float rms_eps;        /* RMSNorm epsilon, 1e-6 (model_backend.py:71) */
+    uint32_t flags;       /* reserved, 0 */
+} qwen_b200_config;
+
+/* ---- handle lifecycle ------------------------------------------------------ */
+/* Fills defaults: device 0, 1 slot, 256-token context, 256 rows, eps 1e-6. */
+void qwen_b200_default_config(qwen_b200_config *cfg);
+/* Allocates nothing on the device until assets are loaded. */
+int qwen_b200_open(const qwen_b200_config *cfg, qwen_b200 **out);
+int qwen_b200_close(qwen_b200 *h);
+/* Loads <sd_root>/QWEN25/{DESC,SCALE,BIAS,GAMMA,WEIGHTS,LMW,EMBED}.BIN (the
+ * reference's SD package, main.c:88-104 / board_parameters.h:18-26). */
+int qwen_b200_load_assets(qwen_b200 *h, const char *sd_root);
+/* Same model as qwen_b200_synth_write(seed) would write, generated in memory. */
+int qwen_b200_load_synthetic(qwen_b200 *h, uint64_t seed);
+const char *qwen_b200_last_error(const qwen_b200 *h);
+
+/* ---- seeded synthetic assets (no checkpoint is available offline) ---------- */
+/* Writes <sd_root>/QWEN25/* in the reference format from a seed: fp32
+ * N(0,0.02) weights quantised per output channel with the rule of
+ * legacy_.../tests/validate_model_weights.py:38-39, gains 1.0, bf16 biases. */
+int qwen_b200_synth_write(const char *sd_root, uint64_t seed);
+/* n uniform prompt ids in [0, 151936) from the seed. */
+void qwen_b200_synth_prompt(uint64_t seed, uint32_t n, uint32_t *ids);
+
+/* ---- sequence level (model_backend.py:57-115) ------------------------------ */
+/* Model.clear(): the slot's position returns to 0. */
+int qwen_b200_reset(qwen_b200 *h, uint32_t slot);
+int qwen_b200_position(const qwen_b200 *h, uint32_t slot, uint32_t *position);
+/* Model.forward(ids, position): rows tokens at position..position+rows-1 of one
+ * slot; returns the greedy token of the last row (highest index on ties) and,
+ * if logits != NULL, its 151936 bf16 logits. ESTATE when position differs from
+ * the slot's position or the capacity would overflow. Host buffers. */
+int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t rows, uint32_t position,
+                      uint32_t *token, uint16_t *logits);
+/* One decode step for n slots (one token each, each at its own position).
+ * Host buffers; the host->device and device->host copies are inside the call. */
+int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
+                          uint32_t *tokens_out);
+/* The same step for slots 0..n-1 with device-resident token arrays, enqueued
+ * on `stream` (NULL = the handle's stream); d_tokens_out is written on the
+ * device and ids are not range-checked on the host. The first call for a given
+ * (n, context bucket of 128, buffers) runs eagerly and captures a CUDA graph
+ * that later calls replay. */
+int qwen_b200_decode_step_device(qwen_b200 *h, const uint32_t *d_tokens_in, uint32_t n, uint32_t *d_tokens_out,
+                                 void *stream);
+/* Fills the first `length` KV entries of every layer of a slot with seeded
+ * synthetic KV8 codes/scales and sets its position to `length` (bench set-up
+ * for long contexts whose prefill is not under test). */
+int qwen_b200_fill_kv_synthetic(qwen_b200 *h, uint32_t slot, uint32_t length, uint64_t seed);
+/* Copies one layer's KV8 cache of a slot to host: codes [2][n][64], scales [2][n]. */
+int qwen_b200_read_kv(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, int8_t *kcodes, float *kscales,
+                      int8_t *vcodes, float *vscales);
+/* Records the bf16 tensors of one layer (q k v context h m y, rows x dims) at
+ * the next forward into host buffers (the reference's RTL_DUMP_LAYERS names,
+ * src/verification/rtl_bridge.cpp:109-171). layer < 0 disables. */
+int qwen_b200_set_dump(qwen_b200 *h, int layer, uint16_t *q, uint16_t *k, uint16_t *v, uint16_t *ctx,
+                       uint16_t *hbuf, uint16_t *mid, uint16_t *y);
+
+/* Kernel classes reported by qwen_b200_profile_decode. */
+#define QWEN_B200_KCLASSES 8 /* 0 embedding, 1 RMSNorm+QKV+RoPE+KV8 append, 2 attention,
+                                3 O proj+residual, 4 RMSNorm+gate/up+SiLU*mul, 5 down+residual,
+                                6 LM head+argmax, 7 bookkeeping (row gathers, position updates) */
+/* One decode step of slots 0..n-1 (host buffers, like qwen_b200_decode_step)
+ * with CUDA events around every kernel launch on the launching stream: ms[c]
+ * is the summed device time of class c, launches[c] its launch count. */
+int qwen_b200_profile_decode(qwen_b200 *h, const uint32_t *tokens_in, uint32_t n, uint32_t *tokens_out, float *ms,
+                             uint32_t *launches);
+/* Kernels enqueued by the last forward / decode step (a replayed graph
+ * launches the same number). */
+uint32_t qwen_b200_step_launches(const qwen_b200 *h);
+
+/* ---- CSR protocol: drop-in for struct qgen_ops (generation.h:5-14) ---------- */
+/* ops.context = handle; ops.write = qwen_b200_csr_write; ops.read =
+ * qwen_b200_csr_read; ops.embedding = qwen_b200_embedding. Slot 0 is used.
+ * START (0x10 bit0) enqueues the forward and returns at once; 0x18 reads 2
+ * while it runs, 0x44 when the token is ready, 8 on error. */
+void qwen_b200_csr_write(void *h, unsigned offset, uint64_t value);
+uint64_t qwen_b200_csr_read(void *h, unsigned offset);
+/* main.c:114-125 copy_embedding: records token id for ACT_IN row `row`. */
+void qwen_b200_embedding(void *h, unsigned token, unsigned row);
+/* main.c:162-170 reset_context. */
+void qwen_b200_clear(void *h);
+
+/* ---- operator level: device pointers, enqueued on `stream` ----------------- */
+/* x[r] = embed[ids[r]] (main.c:114-125). */
+int qwen_b200_op_embed(const uint16_t *embed, const uint32_t *ids, uint32_t rows, uint16_t *x, void *stream);
+/* out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * gamma), x [rows][896]
+ * (model_backend.py:69-71; AFU src/rtl/afu/qwen25_afu.v:75-125). */
+int qwen_b200_op_rmsnorm(const uint16_t *x, const uint16_t *gamma, uint32_t rows, float eps, uint16_t *out,
+                         void *stream);
+/* y = bf16(bf16(x W^T) * scale) [+ bias: bf16(. + bias)], W int8 row-major [n][k]
+ * (model_backend.py:62-67; GEMM src/rtl/qwen25_gemm_i.sv). k is 896 or 4864;
+ * n a multiple of 4. */
+int qwen_b200_op_gemm_w8a16(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w, const float *scale,
+                            uint32_t n, const uint16_t *bias, uint16_t *y, void *stream);
+/* y = bf16(y + bf16(bf16(x W^T) * scale)): O / down projection + residual
+ * (model_backend.py:103,107). */
+int qwen_b200_op_gemm_w8a16_residual(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
+                                     const float *scale, uint32_t n, uint16_t *y, void *stream);
+/* Host-side cos/sin table [positions][64] (cos 0..31, sin 32..63) for
+ * theta_i = 1e6^(-2i/64) (model_backend.py:41). */
+void qwen_b200_rope_table(uint32_t positions, float *table);
+/* In-place split-half RoPE on x [rows][heads][64] (model_backend.py:73-78;
+ * src/rtl/rope/qwen25_rope.v). table: device copy of qwen_b200_rope_table. */
+int qwen_b200_op_rope(uint16_t *x, uint32_t rows, uint32_t heads, const uint32_t *positions, const float *table,
+                      void *stream);
+/* KV8 quantise-append: kv [rows][2][64] bf16 -> codes[slot][2][capacity][64],
+ * scales[slot][2][capacity] at positions[r] (scale = amax/127, code =
+ * clamp(rne(x/scale), +-127)). */
+int qwen_b200_op_kv8_append(const uint16_t *kv, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                            int8_t *codes, float *scales, uint32_t capacity, void *stream);
+/* Fused attention block input: RMSNorm + QKV GEMM + bias + RoPE + KV8 append.
+ * x [rows][896]; w [1152][896] (q|k|v rows); q_out [rows][896] post-RoPE. */
+int qwen_b200_op_qkv(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w,
+                     const float *scale, const uint16_t *bias, const uint32_t *slots, const uint32_t *positions,
+                     const float *table, uint16_t *q_out, int8_t *kcodes, float *kscales, int8_t *vcodes,
+                     float *vscales, uint32_t capacity, void *stream);
+/* GQA attention over a KV8 cache (model_backend.py:97-102; src/rtl/attention/
+ * qwen25_attention.v): q [rows][14][64]; row r of slot slots[r] sees keys
+ * 0..positions[r]; ctx [rows][896]. Workspace from qwen_b200_attention_workspace. */
+size_t qwen_b200_attention_workspace(uint32_t rows, uint32_t capacity);
+/* max_len: an upper bound of positions[r] + 1 over all rows (capacity is
+ * always valid; a tight bound launches fewer context chunks). */
+int qwen_b200_op_attention(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                           uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
+                           const float *vscales, uint32_t capacity, uint16_t *ctx, void *workspace,
+                           size_t workspace_bytes, void *stream);
+/* SwiGLU FFN input half: mid = bf16(bf16(silu(g)) * u) with g, u from
+ * RMSNorm(x) (gamma NULL: no norm) times the interleaved gate/up weight
+ * w_gu [2*4864][896] (row 2j gate j, row 2j+1 up j) and scales s_gu [2*4864]
+ * (model_backend.py:104-106; AFU op 13, qwen25_afu.v:81,172-180). */
+int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w_gu,
+                        const float *s_gu, uint16_t *mid, void *stream);
+/* Final RMSNorm (gamma NULL: none) + LM head + greedy argmax, highest index on
+ * ties (model_backend.py:108-114; qwen25_bf16_argmax.v). logits (nullable)
+ * [rows][vocab] bf16. Workspace from qwen_b200_lm_head_workspace. */
+size_t qwen_b200_lm_head_workspace(uint32_t rows, uint32_t vocab);
+int qwen_b200_op_lm_head_argmax(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps,
+                                const int8_t *w, const float *scale, uint32_t vocab, uint16_t *logits,
+                                uint32_t *tokens, void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

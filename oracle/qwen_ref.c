@@ -1,0 +1,659 @@
+/* ORACLE — test infrastructure only (tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference legs of bench.py). The product never links it.
+ *
+ * A plain-C restatement of the reference's behavioural model
+ *   legacy_100mhz_closed/src/PC/model_backend.py:14-115
+ * with the rounding variants of
+ *   legacy_100mhz_closed/src/software/interactive/tests/rtl_numeric_reference.py:6-32
+ * and the per-token-per-head KV8 rule (amax/127 fp32 scale, round-half-even
+ * codes clamped to +-127) used by the B200 engine's KV cache.
+ *
+ * Fixed evaluation order (so that results do not depend on thread count):
+ *   linear:  per output, fp32 sum over k in increasing order (every product
+ *            bf16 x int8 is exact in fp32, so FMA or not gives the same sum)
+ *   scores:  per (row, head, key), fmaf over d in increasing order
+ *   softmax: max, e = expf(s - max), Z = sequential sum, P = bf16(e * (1/Z))
+ *   context: per (row, head, d), fmaf over keys in increasing order
+ * Build with -ffp-contract=off (oracle/Makefile).
+ */
+#include "qwen_ref.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define NL 24
+#define HID 896
+#define FFN 4864
+#define VOC 151936
+#define QH 14
+#define KVH 2
+#define HD 64
+#define QKV 1152
+
+/* Projection table: out, in, SCALE.BIN offset, DESC.BIN byte offset
+ * (model_backend.py:29-32). */
+static const unsigned P_OUT[7] = {896, 128, 128, 896, 4864, 4864, 896};
+static const unsigned P_IN[7] = {896, 896, 896, 896, 896, 896, 4864};
+static const unsigned P_SCALE[7] = {0, 896, 1024, 1152, 2048, 6912, 11776};
+static const unsigned P_FIELD[7] = {40, 48, 56, 80, 96, 104, 120};
+enum { PQ, PK, PV, PO, PG, PU, PD };
+
+struct ref_model {
+    int8_t *w[NL][7];  /* logical [out][in] */
+    int8_t *wt[NL][7]; /* transposed [in][out] */
+    int8_t *lm, *lmt;
+    float *scale, *bias, *gamma;
+    uint16_t *embed;
+    unsigned mode, capacity, position;
+    float *rope; /* [capacity][64] */
+    float *kf[NL], *vf[NL];         /* bf16 KV: [cap][2][64] */
+    int8_t *kc[NL], *vc[NL];        /* KV8: [2][cap][64] */
+    float *ks[NL], *vs[NL];         /* KV8: [2][cap] */
+    int dump_layer;
+    float *dq, *dk, *dv, *dctx, *dh, *dm, *dy;
+};
+
+/* ---------------------------------------------------------------- rounding */
+static inline uint32_t f2u(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    return u;
+}
+static inline float u2f(uint32_t u) {
+    float x;
+    memcpy(&x, &u, 4);
+    return x;
+}
+/* torch .to(bfloat16): round to nearest even (model_backend.py:45). */
+static inline float bf_rne(float x) {
+    uint32_t u = f2u(x);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return u2f(0x7fc00000u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return u2f(u & 0xffff0000u);
+}
+/* rtl_numeric_reference.py:6-12: half away from zero, FTZ, canonical NaN. */
+static inline float bf_rnd8(float x) {
+    uint32_t b = f2u(x);
+    uint32_t upper = ((b >> 16) + ((b >> 15) & 1u)) & 0xffffu;
+    uint32_t e = (b >> 23) & 0xffu;
+    if (e == 0) upper = (b >> 16) & 0x8000u;
+    if (e == 255 && (b & 0x7fffffu)) upper = 0x7fc0u;
+    return u2f(upper << 16);
+}
+float ref_bf(float x, unsigned mode) { return (mode & REF_RND8) ? bf_rnd8(x) : bf_rne(x); }
+static inline float bfm(float x, unsigned mode) { return (mode & REF_RND8) ? bf_rnd8(x) : bf_rne(x); }
+static inline float bf2f(uint16_t b) { return u2f((uint32_t)b << 16); }
+
+void ref_set_threads(int threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+}
+
+/* ------------------------------------------------------------------- loader */
+static void *slurp(const char *root, const char *name, size_t expect, char *err, size_t errlen) {
+    char path[4096];
+    snprintf(path, sizeof(path), "%s/QWEN25/%s", root, name);
+    FILE *f = fopen(path, "rb");
+    if (!f) {
+        snprintf(err, errlen, "cannot open %s", path);
+        return NULL;
+    }
+    fseek(f, 0, SEEK_END);
+    long n = ftell(f);
+    rewind(f);
+    void *p = NULL;
+    if (expect == 0 || (long)expect == n) {
+        p = malloc((size_t)n + 1);
+        if (p && fread(p, 1, (size_t)n, f) != (size_t)n) {
+            free(p);
+            p = NULL;
+        }
+        if (p) ((char *)p)[n] = 0;
+    } else {
+        snprintf(err, errlen, "wrong size %s", path);
+    }
+    fclose(f);
+    return p;
+}
+
+/* model_backend.py:51-55: physical [C/128][I/128][4][128][2][16] -> logical [C][I]. */
+static void unpack_tiles(const int8_t *raw, unsigned columns, unsigned inner, int8_t *out) {
+#pragma omp parallel for schedule(static)
+    for (long c = 0; c < (long)columns; ++c) {
+        unsigned cb = (unsigned)c / 128, ci = (unsigned)c % 128, a = ci / 64, b = (ci % 64) / 16, d = ci % 16;
+        for (unsigned i = 0; i < inner; ++i) {
+            unsigned ib = i / 128, e = i % 128;
+            size_t off = (((((size_t)cb * (inner / 128) + ib) * 4 + b) * 128 + e) * 2 + a) * 16 + d;
+            out[(size_t)c * inner + i] = raw[off];
+        }
+    }
+}
+
+static int8_t *transpose_i8(const int8_t *w, unsigned out, unsigned in) {
+    int8_t *t = (int8_t *)malloc((size_t)out * in);
+    if (!t) return NULL;
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < (long)in; ++i)
+        for (unsigned o = 0; o < out; ++o) t[(size_t)i * out + o] = w[(size_t)o * in + i];
+    return t;
+}
+
+static float *bf16_file(const char *root, const char *name, size_t count, char *err, size_t errlen) {
+    uint16_t *raw = (uint16_t *)slurp(root, name, count * 2, err, errlen);
+    if (!raw) return NULL;
+    float *f = (float *)malloc(count * sizeof(float));
+    for (size_t i = 0; f && i < count; ++i) f[i] = bf2f(raw[i]);
+    free(raw);
+    return f;
+}
+
+void ref_rope_table(unsigned positions, float *table) {
+    /* model_backend.py:41: 1 / 1e6^(2i/64) in fp32; phase = pos * inv (fp32). */
+    float inv[32];
+    for (int i = 0; i < 32; ++i) inv[i] = 1.0f / (float)pow(1000000.0, (double)(2 * i) / 64.0);
+    for (unsigned p = 0; p < positions; ++p)
+        for (int i = 0; i < 32; ++i) {
+            float phase = (float)p * inv[i];
+            table[(size_t)p * 64 + i] = (float)cos((double)phase);
+            table[(size_t)p * 64 + 32 + i] = (float)sin((double)phase);
+        }
+}
+
+ref_model *ref_open(const char *root, unsigned capacity, char *err, size_t errlen) {
+    ref_model *m = (ref_model *)calloc(1, sizeof(ref_model));
+    if (!m) return NULL;
+    m->capacity = capacity ? capacity : 256;
+    m->dump_layer = -1;
+    char *cfg = (char *)slurp(root, "CONFIG.JSON", 0, err, errlen);
+    if (!cfg) goto fail;
+    /* model_backend.py:19 asserts hidden/layers/vocab. */
+    if (!strstr(cfg, "\"hidden\": 896") || !strstr(cfg, "\"layers\": 24") || !strstr(cfg, "\"vocab\": 151936")) {
+        snprintf(err, errlen, "CONFIG.JSON is not Qwen2.5-0.5B (hidden 896, 24 layers, vocab 151936)");
+        free(cfg);
+        goto fail;
+    }
+    free(cfg);
+    m->scale = bf16_file(root, "SCALE.BIN", 304128 + VOC, err, errlen);
+    m->bias = bf16_file(root, "BIAS.BIN", NL * QKV, err, errlen);
+    m->gamma = bf16_file(root, "GAMMA.BIN", NL * 1792 + HID, err, errlen);
+    m->embed = (uint16_t *)slurp(root, "EMBED.BIN", (size_t)VOC * HID * 2, err, errlen);
+    if (!m->scale || !m->bias || !m->gamma || !m->embed) goto fail;
+    {
+        uint8_t *desc = (uint8_t *)slurp(root, "DESC.BIN", 0, err, errlen);
+        int8_t *packed = (int8_t *)slurp(root, "WEIGHTS.BIN", 0, err, errlen);
+        if (!desc || !packed) {
+            free(desc);
+            free(packed);
+            goto fail;
+        }
+        size_t packed_size = (size_t)24 * 14909440ULL;
+        for (int l = 0; l < NL; ++l)
+            for (int p = 0; p < 7; ++p) {
+                uint64_t address;
+                memcpy(&address, desc + l * 256 + P_FIELD[p], 8);
+                uint64_t off = address - 0x41000000ULL;
+                size_t bytes = (size_t)P_OUT[p] * P_IN[p];
+                if (address < 0x41000000ULL || off + bytes > packed_size) {
+                    snprintf(err, errlen, "descriptor %d/%u outside WEIGHTS.BIN", l, P_FIELD[p]);
+                    free(desc);
+                    free(packed);
+                    goto fail;
+                }
+                m->w[l][p] = (int8_t *)malloc(bytes);
+                unpack_tiles(packed + off, P_OUT[p], P_IN[p], m->w[l][p]);
+                m->wt[l][p] = transpose_i8(m->w[l][p], P_OUT[p], P_IN[p]);
+            }
+        free(desc);
+        free(packed);
+        int8_t *lm = (int8_t *)slurp(root, "LMW.BIN", (size_t)VOC * HID, err, errlen);
+        if (!lm) goto fail;
+        m->lm = (int8_t *)malloc((size_t)VOC * HID);
+        unpack_tiles(lm, VOC, HID, m->lm);
+        free(lm);
+        m->lmt = transpose_i8(m->lm, VOC, HID);
+    }
+    m->rope = (float *)malloc((size_t)m->capacity * 64 * sizeof(float));
+    ref_rope_table(m->capacity, m->rope);
+    for (int l = 0; l < NL; ++l) {
+        m->kf[l] = (float *)calloc((size_t)m->capacity * KVH * HD, sizeof(float));
+        m->vf[l] = (float *)calloc((size_t)m->capacity * KVH * HD, sizeof(float));
+        m->kc[l] = (int8_t *)calloc((size_t)m->capacity * KVH * HD, 1);
+        m->vc[l] = (int8_t *)calloc((size_t)m->capacity * KVH * HD, 1);
+        m->ks[l] = (float *)calloc((size_t)m->capacity * KVH, sizeof(float));
+        m->vs[l] = (float *)calloc((size_t)m->capacity * KVH, sizeof(float));
+    }
+    return m;
+fail:
+    ref_close(m);
+    return NULL;
+}
+
+void ref_close(ref_model *m) {
+    if (!m) return;
+    for (int l = 0; l < NL; ++l) {
+        for (int p = 0; p < 7; ++p) {
+            free(m->w[l][p]);
+            free(m->wt[l][p]);
+        }
+        free(m->kf[l]);
+        free(m->vf[l]);
+        free(m->kc[l]);
+        free(m->vc[l]);
+        free(m->ks[l]);
+        free(m->vs[l]);
+    }
+    free(m->lm);
+    free(m->lmt);
+    free(m->scale);
+    free(m->bias);
+    free(m->gamma);
+    free(m->embed);
+    free(m->rope);
+    free(m);
+}
+
+void ref_set_mode(ref_model *m, unsigned mode) { m->mode = mode; }
+void ref_clear(ref_model *m) { m->position = 0; } /* model_backend.py:57-60 */
+unsigned ref_position(const ref_model *m) { return m->position; }
+const int8_t *ref_weight(const ref_model *m, int layer, int proj) { return m->w[layer][proj]; }
+const float *ref_scale(const ref_model *m) { return m->scale; }
+const float *ref_bias(const ref_model *m) { return m->bias; }
+const float *ref_gamma(const ref_model *m) { return m->gamma; }
+const int8_t *ref_lm_weight(const ref_model *m) { return m->lm; }
+const uint16_t *ref_embedding(const ref_model *m) { return m->embed; }
+
+void ref_set_dump(ref_model *m, int layer, float *q, float *k, float *v, float *ctx, float *h, float *mid,
+                  float *y) {
+    m->dump_layer = layer;
+    m->dq = q;
+    m->dk = k;
+    m->dv = v;
+    m->dctx = ctx;
+    m->dh = h;
+    m->dm = mid;
+    m->dy = y;
+}
+
+/* -------------------------------------------------------------- operators */
+static float eps_of(unsigned mode) {
+    return (mode & REF_CSR_EPS) ? u2f(0x35860000u) : 1e-6f; /* rtl_numeric_reference.py:18 */
+}
+
+/* model_backend.py:69-71 */
+void ref_rmsnorm(const float *x, unsigned rows, const float *gamma, float eps, unsigned mode, float *out) {
+    for (unsigned r = 0; r < rows; ++r) {
+        const float *xr = x + (size_t)r * HID;
+        float ss = 0.0f;
+        for (unsigned i = 0; i < HID; ++i) ss += xr[i] * xr[i];
+        float mean = ss / (float)HID;
+        float rs = 1.0f / sqrtf(mean + eps);
+        for (unsigned i = 0; i < HID; ++i) out[(size_t)r * HID + i] = bfm(bfm(xr[i] * rs, mode) * gamma[i], mode);
+    }
+}
+
+/* Raw fp32 accumulation acc[r][n] = sum_k x[r][k] * w[n][k], k ascending, from
+ * the transposed weight wt[k][n]. */
+static void accum_t(const float *x, unsigned rows, unsigned K, const int8_t *wt, unsigned N, float *acc) {
+    const unsigned NB = 256, RB = 16;
+    long nblocks = (N + NB - 1) / NB;
+#pragma omp parallel for schedule(static)
+    for (long nb = 0; nb < nblocks; ++nb) {
+        unsigned n0 = (unsigned)nb * NB, nn = N - n0 < NB ? N - n0 : NB;
+        float wf[256];
+        float a[16][256];
+        for (unsigned r0 = 0; r0 < rows; r0 += RB) {
+            unsigned rb = rows - r0 < RB ? rows - r0 : RB;
+            for (unsigned r = 0; r < rb; ++r)
+                for (unsigned j = 0; j < nn; ++j) a[r][j] = 0.0f;
+            for (unsigned k = 0; k < K; ++k) {
+                const int8_t *wr = wt + (size_t)k * N + n0;
+                for (unsigned j = 0; j < nn; ++j) wf[j] = (float)wr[j];
+                for (unsigned r = 0; r < rb; ++r) {
+                    float xk = x[(size_t)(r0 + r) * K + k];
+                    for (unsigned j = 0; j < nn; ++j) a[r][j] += xk * wf[j];
+                }
+            }
+            for (unsigned r = 0; r < rb; ++r)
+                memcpy(acc + (size_t)(r0 + r) * N + n0, a[r], nn * sizeof(float));
+        }
+    }
+}
+
+/* Same sums from a row-major weight w[n][k] (operator-level entry). */
+static void accum_rowmajor(const float *x, unsigned rows, unsigned K, const int8_t *w, unsigned N, float *acc) {
+#pragma omp parallel for schedule(static)
+    for (long n = 0; n < (long)N; ++n)
+        for (unsigned r = 0; r < rows; ++r) {
+            float s = 0.0f;
+            const int8_t *wr = w + (size_t)n * K;
+            const float *xr = x + (size_t)r * K;
+            for (unsigned k = 0; k < K; ++k) s += xr[k] * (float)wr[k];
+            acc[(size_t)r * N + n] = s;
+        }
+}
+
+/* model_backend.py:62-64: bf16(bf16(x W^T) * scale). */
+static void epi_linear(float *acc, unsigned rows, unsigned N, const float *scale, unsigned mode) {
+    for (size_t i = 0; i < (size_t)rows * N; ++i) acc[i] = bfm(bfm(acc[i], mode) * scale[i % N], mode);
+}
+/* model_backend.py:66-67 (two roundings) or rtl_numeric_reference.py:27-32 (one). */
+static void epi_bias(float *acc, unsigned rows, unsigned N, const float *scale, const float *bias, unsigned mode) {
+    for (size_t i = 0; i < (size_t)rows * N; ++i) {
+        unsigned n = (unsigned)(i % N);
+        if (mode & REF_FUSED_BIAS)
+            acc[i] = bfm(bfm(acc[i], mode) * scale[n] + bias[n], mode);
+        else
+            acc[i] = bfm(bfm(bfm(acc[i], mode) * scale[n], mode) + bias[n], mode);
+    }
+}
+
+void ref_linear(const float *x, unsigned rows, unsigned k, const int8_t *w, const float *scale, unsigned n,
+                unsigned mode, float *out) {
+    accum_rowmajor(x, rows, k, w, n, out);
+    epi_linear(out, rows, n, scale, mode);
+}
+
+void ref_linear_bias(const float *x, unsigned rows, unsigned k, const int8_t *w, const float *scale,
+                     const float *bias, unsigned n, unsigned mode, float *out) {
+    accum_rowmajor(x, rows, k, w, n, out);
+    epi_bias(out, rows, n, scale, bias, mode);
+}
+
+/* model_backend.py:73-78 with the fp32 cos/sin table. */
+static void rope_rows(float *x, unsigned rows, unsigned heads, const uint32_t *positions, const float *table,
+                      unsigned mode, float *out) {
+    for (unsigned r = 0; r < rows; ++r) {
+        const float *cs = table + (size_t)positions[r] * 64;
+        for (unsigned h = 0; h < heads; ++h) {
+            const float *xi = x + ((size_t)r * heads + h) * HD;
+            float *yo = out + ((size_t)r * heads + h) * HD;
+            float tmp[HD];
+            for (int i = 0; i < HD; ++i) {
+                float c = cs[i & 31], s = cs[32 + (i & 31)];
+                float rot = i < 32 ? -xi[i + 32] : xi[i - 32];
+                float a = xi[i] * c;
+                float b = rot * s;
+                tmp[i] = bfm(a + b, mode);
+            }
+            memcpy(yo, tmp, sizeof(tmp));
+        }
+    }
+}
+
+void ref_rope(const float *x, unsigned rows, unsigned heads, const uint32_t *positions, unsigned mode, float *out) {
+    unsigned maxp = 0;
+    for (unsigned r = 0; r < rows; ++r)
+        if (positions[r] > maxp) maxp = positions[r];
+    float *table = (float *)malloc((size_t)(maxp + 1) * 64 * sizeof(float));
+    ref_rope_table(maxp + 1, table);
+    float *tmp = (float *)malloc((size_t)rows * heads * HD * sizeof(float));
+    memcpy(tmp, x, (size_t)rows * heads * HD * sizeof(float));
+    rope_rows(tmp, rows, heads, positions, table, mode, out);
+    free(tmp);
+    free(table);
+}
+
+/* KV8 rule per (token, kv head): s = amax/127 (fp32), code = clamp(rne(x/s), +-127);
+ * an all-zero vector gets s = 0 and zero codes. */
+void ref_kv8_quant(const float *x, unsigned rows, int8_t *codes, float *scales) {
+    for (unsigned r = 0; r < rows; ++r) {
+        const float *xr = x + (size_t)r * HD;
+        float amax = 0.0f;
+        for (int d = 0; d < HD; ++d) {
+            float a = fabsf(xr[d]);
+            if (a > amax) amax = a;
+        }
+        float s = amax / 127.0f;
+        scales[r] = s;
+        for (int d = 0; d < HD; ++d) {
+            float q = s > 0.0f ? nearbyintf(xr[d] / s) : 0.0f;
+            if (q > 127.0f) q = 127.0f;
+            if (q < -127.0f) q = -127.0f;
+            codes[(size_t)r * HD + d] = (int8_t)q;
+        }
+    }
+}
+
+/* model_backend.py:97-102 for one (row, head): S = bf(q.k/8), causal mask
+ * (keys 0..visible-1), P = bf(softmax(S)), ctx = bf(P.v). key/val read the
+ * (dequantised) cache through their own views. */
+typedef float (*kv_at)(const void *view, unsigned t, unsigned d);
+static void attend(const float *q, unsigned visible, kv_at key, const void *kview, kv_at val, const void *vview,
+                   unsigned mode, float *out) {
+    float *scratch = (float *)malloc(visible * sizeof(float));
+    float mx = -INFINITY;
+    for (unsigned t = 0; t < visible; ++t) {
+        float acc = 0.0f;
+        for (unsigned d = 0; d < HD; ++d) acc = fmaf(q[d], key(kview, t, d), acc);
+        float s = bfm(acc / 8.0f, mode);
+        scratch[t] = s;
+        if (s > mx) mx = s;
+    }
+    float z = 0.0f;
+    for (unsigned t = 0; t < visible; ++t) {
+        scratch[t] = expf(scratch[t] - mx);
+        z += scratch[t];
+    }
+    float inv = 1.0f / z;
+    float acc[HD];
+    for (unsigned d = 0; d < HD; ++d) acc[d] = 0.0f;
+    for (unsigned t = 0; t < visible; ++t) {
+        float p = bfm(scratch[t] * inv, mode);
+        for (unsigned d = 0; d < HD; ++d) acc[d] = fmaf(p, val(vview, t, d), acc[d]);
+    }
+    for (unsigned d = 0; d < HD; ++d) out[d] = bfm(acc[d], mode);
+    free(scratch);
+}
+
+/* KV8 view: codes [t][64], scales [t]; dequantised value = code * scale (fp32). */
+typedef struct kv8_view { const int8_t *codes; const float *scales; } kv8_view;
+static float kv8_at(const void *c, unsigned t, unsigned d) {
+    const kv8_view *v = (const kv8_view *)c;
+    return (float)v->codes[(size_t)t * HD + d] * v->scales[t];
+}
+/* bf16 view: data [t][2][64], pre-offset to one KV head. */
+typedef struct bf_view { const float *data; } bf_view;
+static float bf_at(const void *c, unsigned t, unsigned d) {
+    const bf_view *v = (const bf_view *)c;
+    return v->data[(size_t)t * KVH * HD + d];
+}
+
+void ref_attention_kv8(const float *q, unsigned rows, const uint32_t *positions, const int8_t *kcodes,
+                       const float *kscales, const int8_t *vcodes, const float *vscales, unsigned capacity,
+                       unsigned mode, float *ctx) {
+#pragma omp parallel for schedule(dynamic)
+    for (long rh = 0; rh < (long)rows * QH; ++rh) {
+        unsigned r = (unsigned)rh / QH, h = (unsigned)rh % QH, g = h / 7; /* repeat_interleave(7), :97-98 */
+        kv8_view kv = {kcodes + (size_t)g * capacity * HD, kscales + (size_t)g * capacity};
+        kv8_view vv = {vcodes + (size_t)g * capacity * HD, vscales + (size_t)g * capacity};
+        attend(q + ((size_t)r * QH + h) * HD, positions[r] + 1, kv8_at, &kv, kv8_at, &vv, mode,
+               ctx + (size_t)r * HID + (size_t)h * HD);
+    }
+}
+
+void ref_attention_bf16(const float *q, unsigned rows, const uint32_t *positions, const float *k, const float *v,
+                        unsigned mode, float *ctx) {
+#pragma omp parallel for schedule(dynamic)
+    for (long rh = 0; rh < (long)rows * QH; ++rh) {
+        unsigned r = (unsigned)rh / QH, h = (unsigned)rh % QH, g = h / 7;
+        bf_view kv = {k + (size_t)g * HD}, vv = {v + (size_t)g * HD};
+        attend(q + ((size_t)r * QH + h) * HD, positions[r] + 1, bf_at, &kv, bf_at, &vv, mode,
+               ctx + (size_t)r * HID + (size_t)h * HD);
+    }
+}
+
+/* model_backend.py:106: bf16(bf16(silu(gate)) * up), silu(g) = g / (1 + exp(-g)). */
+void ref_swiglu(const float *gate, const float *up, unsigned count, unsigned mode, float *out) {
+    for (unsigned i = 0; i < count; ++i) {
+        float g = gate[i];
+        float s = g / (1.0f + expf(-g));
+        out[i] = bfm(bfm(s, mode) * up[i], mode);
+    }
+}
+
+/* Greedy token, highest index on ties (model_backend.py:113-114). */
+static uint32_t argmax_last(const float *v, unsigned n) {
+    uint32_t best = 0;
+    for (unsigned i = 1; i < n; ++i)
+        if (v[i] >= v[best]) best = i;
+    return best;
+}
+
+uint32_t ref_lm_head(const ref_model *m, const float *x, unsigned mode, float *logits) {
+    float h[HID];
+    ref_rmsnorm(x, 1, m->gamma + 43008, eps_of(mode), mode, h);
+    float *acc = (float *)malloc((size_t)VOC * sizeof(float));
+    accum_t(h, 1, HID, m->lmt, VOC, acc);
+    const float *s = m->scale + 304128;
+    float *pre = (float *)malloc((size_t)VOC * sizeof(float));
+    for (unsigned n = 0; n < VOC; ++n) {
+        pre[n] = bfm(acc[n], mode) * s[n];
+        acc[n] = bfm(pre[n], mode);
+    }
+    uint32_t tok = (mode & REF_ARGMAX_F32) ? argmax_last(pre, VOC) : argmax_last(acc, VOC);
+    if (logits) memcpy(logits, acc, (size_t)VOC * sizeof(float));
+    free(acc);
+    free(pre);
+    return tok;
+}
+
+int ref_kv8_state(const ref_model *m, int layer, int8_t *kcodes, float *kscales, int8_t *vcodes, float *vscales) {
+    unsigned n = m->position;
+    for (int g = 0; g < KVH; ++g) {
+        memcpy(kcodes + (size_t)g * n * HD, m->kc[layer] + (size_t)g * m->capacity * HD, (size_t)n * HD);
+        memcpy(vcodes + (size_t)g * n * HD, m->vc[layer] + (size_t)g * m->capacity * HD, (size_t)n * HD);
+        memcpy(kscales + (size_t)g * n, m->ks[layer] + (size_t)g * m->capacity, n * sizeof(float));
+        memcpy(vscales + (size_t)g * n, m->vs[layer] + (size_t)g * m->capacity, n * sizeof(float));
+    }
+    return (int)n;
+}
+
+int ref_fill_kv_synthetic(ref_model *m, unsigned length, uint64_t seed) {
+    if (length > m->capacity) return -1;
+    for (int l = 0; l < NL; ++l)
+        for (int g = 0; g < KVH; ++g)
+            for (unsigned t = 0; t < length; ++t) {
+                uint64_t z = seed * 0x9E3779B97F4A7C15ULL + ((uint64_t)l * 2 + g) * 0x100000001B3ULL + t;
+                for (int d = 0; d < HD; ++d) {
+                    z ^= z >> 33;
+                    z *= 0xff51afd7ed558ccdULL;
+                    z ^= z >> 29;
+                    m->kc[l][((size_t)g * m->capacity + t) * HD + d] = (int8_t)((int)(z % 255u) - 127);
+                    m->vc[l][((size_t)g * m->capacity + t) * HD + d] = (int8_t)((int)((z >> 16) % 255u) - 127);
+                }
+                m->ks[l][(size_t)g * m->capacity + t] = 0.01f + 0.02f * (float)((z >> 40) & 0xffff) / 65536.0f;
+                m->vs[l][(size_t)g * m->capacity + t] = 0.01f + 0.02f * (float)((z >> 24) & 0xffff) / 65536.0f;
+            }
+    m->position = length;
+    return 0;
+}
+
+/* ------------------------------------------------------------------ forward */
+int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned position, uint32_t *token,
+                float *logits) {
+    if (position != m->position || rows == 0 || position + rows > m->capacity) return -8;
+    for (unsigned r = 0; r < rows; ++r)
+        if (ids[r] >= VOC) return -1;
+    const unsigned mode = m->mode;
+    const float eps = eps_of(mode);
+    float *x = (float *)malloc((size_t)rows * HID * sizeof(float));
+    float *h = (float *)malloc((size_t)rows * HID * sizeof(float));
+    float *qkv = (float *)malloc((size_t)rows * QKV * sizeof(float));
+    float *q = (float *)malloc((size_t)rows * HID * sizeof(float));
+    float *k = (float *)malloc((size_t)rows * KVH * HD * sizeof(float));
+    float *v = (float *)malloc((size_t)rows * KVH * HD * sizeof(float));
+    float *ctx = (float *)malloc((size_t)rows * HID * sizeof(float));
+    float *gu = (float *)malloc((size_t)rows * FFN * 2 * sizeof(float));
+    float *mid = (float *)malloc((size_t)rows * FFN * sizeof(float));
+    float *tmp = (float *)malloc((size_t)rows * FFN * sizeof(float));
+    uint32_t *pos = (uint32_t *)malloc(rows * sizeof(uint32_t));
+    for (unsigned r = 0; r < rows; ++r) {
+        pos[r] = position + r;
+        for (unsigned i = 0; i < HID; ++i) x[(size_t)r * HID + i] = bf2f(m->embed[(size_t)ids[r] * HID + i]);
+    }
+    for (int l = 0; l < NL; ++l) {
+        const float *sc = m->scale + (size_t)l * 12672;
+        const float *bias = m->bias + (size_t)l * QKV;
+        ref_rmsnorm(x, rows, m->gamma + (size_t)l * 1792, eps, mode, h);
+        /* q, k, v projections with bias (model_backend.py:91-93) */
+        accum_t(h, rows, HID, m->wt[l][PQ], 896, q);
+        epi_bias(q, rows, 896, sc + P_SCALE[PQ], bias, mode);
+        accum_t(h, rows, HID, m->wt[l][PK], 128, k);
+        epi_bias(k, rows, 128, sc + P_SCALE[PK], bias + 896, mode);
+        accum_t(h, rows, HID, m->wt[l][PV], 128, v);
+        epi_bias(v, rows, 128, sc + P_SCALE[PV], bias + 1024, mode);
+        rope_rows(q, rows, QH, pos, m->rope, mode, q);
+        rope_rows(k, rows, KVH, pos, m->rope, mode, k);
+        /* append to the cache (model_backend.py:95-96) */
+        for (unsigned r = 0; r < rows; ++r)
+            for (int g = 0; g < KVH; ++g) {
+                const float *kr = k + ((size_t)r * KVH + g) * HD, *vr = v + ((size_t)r * KVH + g) * HD;
+                size_t t = pos[r];
+                memcpy(m->kf[l] + (t * KVH + g) * HD, kr, HD * sizeof(float));
+                memcpy(m->vf[l] + (t * KVH + g) * HD, vr, HD * sizeof(float));
+                ref_kv8_quant(kr, 1, m->kc[l] + ((size_t)g * m->capacity + t) * HD, m->ks[l] + (size_t)g * m->capacity + t);
+                ref_kv8_quant(vr, 1, m->vc[l] + ((size_t)g * m->capacity + t) * HD, m->vs[l] + (size_t)g * m->capacity + t);
+            }
+        if (mode & REF_KV8) {
+            ref_attention_kv8(q, rows, pos, m->kc[l], m->ks[l], m->vc[l], m->vs[l], m->capacity, mode, ctx);
+        } else {
+#pragma omp parallel for schedule(dynamic)
+            for (long rh = 0; rh < (long)rows * QH; ++rh) {
+                unsigned r = (unsigned)rh / QH, hh = (unsigned)rh % QH, g = hh / 7;
+                bf_view kv = {m->kf[l] + (size_t)g * HD}, vv = {m->vf[l] + (size_t)g * HD};
+                attend(q + ((size_t)r * QH + hh) * HD, pos[r] + 1, bf_at, &kv, bf_at, &vv, mode,
+                       ctx + (size_t)r * HID + (size_t)hh * HD);
+            }
+        }
+        if (l == m->dump_layer) {
+            if (m->dq) memcpy(m->dq, q, (size_t)rows * HID * sizeof(float));
+            if (m->dk) memcpy(m->dk, k, (size_t)rows * 128 * sizeof(float));
+            if (m->dv) memcpy(m->dv, v, (size_t)rows * 128 * sizeof(float));
+            if (m->dctx) memcpy(m->dctx, ctx, (size_t)rows * HID * sizeof(float));
+        }
+        /* O projection + residual (model_backend.py:103) */
+        accum_t(ctx, rows, HID, m->wt[l][PO], HID, tmp);
+        epi_linear(tmp, rows, HID, sc + P_SCALE[PO], mode);
+        for (size_t i = 0; i < (size_t)rows * HID; ++i) x[i] = bfm(x[i] + tmp[i], mode);
+        if (l == m->dump_layer && m->dh) memcpy(m->dh, x, (size_t)rows * HID * sizeof(float));
+        /* FFN (model_backend.py:104-107) */
+        ref_rmsnorm(x, rows, m->gamma + (size_t)l * 1792 + 896, eps, mode, h);
+        float *gate = gu, *up = gu + (size_t)rows * FFN;
+        accum_t(h, rows, HID, m->wt[l][PG], FFN, gate);
+        epi_linear(gate, rows, FFN, sc + P_SCALE[PG], mode);
+        accum_t(h, rows, HID, m->wt[l][PU], FFN, up);
+        epi_linear(up, rows, FFN, sc + P_SCALE[PU], mode);
+        ref_swiglu(gate, up, rows * FFN, mode, mid);
+        accum_t(mid, rows, FFN, m->wt[l][PD], HID, tmp);
+        epi_linear(tmp, rows, HID, sc + P_SCALE[PD], mode);
+        for (size_t i = 0; i < (size_t)rows * HID; ++i) x[i] = bfm(x[i] + tmp[i], mode);
+        if (l == m->dump_layer) {
+            if (m->dm) memcpy(m->dm, mid, (size_t)rows * FFN * sizeof(float));
+            if (m->dy) memcpy(m->dy, x, (size_t)rows * HID * sizeof(float));
+        }
+    }
+    /* final norm on the last row + LM head + argmax (model_backend.py:108-114) */
+    uint32_t tok = ref_lm_head(m, x + (size_t)(rows - 1) * HID, mode, logits);
+    m->position = position + rows;
+    if (token) *token = tok;
+    free(x);
+    free(h);
+    free(qkv);
+    free(q);
+    free(k);
+    free(v);
+    free(ctx);
+    free(gu);
+    free(mid);
+    free(tmp);
+    free(pos);
+    return 0;
+}

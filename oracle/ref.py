@@ -1,0 +1,258 @@
+"""ORACLE — test infrastructure only (tests/, __graft_entry__.smoke() and the
+cpu_baseline / reference legs of bench.py). ctypes wrapper of oracle/qwen_ref.c,
+the plain-C restatement of legacy_100mhz_closed/src/PC/model_backend.py.
+"""
+import ctypes
+import subprocess
+from ctypes import POINTER, c_char_p, c_float, c_int, c_uint32, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / '_build' / 'libqwen_ref.so'
+
+KV8, RND8, FUSED_BIAS, CSR_EPS, ARGMAX_F32 = 1, 2, 4, 8, 16
+VOCAB = 151936
+
+_P8 = POINTER(ctypes.c_int8)
+_PF = POINTER(c_float)
+_P32 = POINTER(c_uint32)
+_lib = None
+
+
+def build():
+    subprocess.run(['make', '-s', '-C', str(HERE)], check=True)
+    return LIB
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        L = ctypes.CDLL(str(LIB))
+        sig = {
+            'ref_open': (c_void_p, [c_char_p, ctypes.c_uint, c_char_p, ctypes.c_size_t]),
+            'ref_close': (None, [c_void_p]),
+            'ref_set_mode': (None, [c_void_p, ctypes.c_uint]),
+            'ref_set_threads': (None, [c_int]),
+            'ref_clear': (None, [c_void_p]),
+            'ref_position': (ctypes.c_uint, [c_void_p]),
+            'ref_forward': (c_int, [c_void_p, _P32, ctypes.c_uint, ctypes.c_uint, _P32, _PF]),
+            'ref_set_dump': (None, [c_void_p, c_int] + [_PF] * 7),
+            'ref_weight': (_P8, [c_void_p, c_int, c_int]),
+            'ref_scale': (_PF, [c_void_p]),
+            'ref_bias': (_PF, [c_void_p]),
+            'ref_gamma': (_PF, [c_void_p]),
+            'ref_lm_weight': (_P8, [c_void_p]),
+            'ref_embedding': (POINTER(ctypes.c_uint16), [c_void_p]),
+            'ref_kv8_state': (c_int, [c_void_p, c_int, _P8, _PF, _P8, _PF]),
+            'ref_bf': (c_float, [c_float, ctypes.c_uint]),
+            'ref_rmsnorm': (None, [_PF, ctypes.c_uint, _PF, c_float, ctypes.c_uint, _PF]),
+            'ref_linear': (None, [_PF, ctypes.c_uint, ctypes.c_uint, _P8, _PF, ctypes.c_uint, ctypes.c_uint, _PF]),
+            'ref_linear_bias': (None, [_PF, ctypes.c_uint, ctypes.c_uint, _P8, _PF, _PF, ctypes.c_uint,
+                                       ctypes.c_uint, _PF]),
+            'ref_rope_table': (None, [ctypes.c_uint, _PF]),
+            'ref_rope': (None, [_PF, ctypes.c_uint, ctypes.c_uint, _P32, ctypes.c_uint, _PF]),
+            'ref_kv8_quant': (None, [_PF, ctypes.c_uint, _P8, _PF]),
+            'ref_attention_kv8': (None, [_PF, ctypes.c_uint, _P32, _P8, _PF, _P8, _PF, ctypes.c_uint,
+                                         ctypes.c_uint, _PF]),
+            'ref_attention_bf16': (None, [_PF, ctypes.c_uint, _P32, _PF, _PF, ctypes.c_uint, _PF]),
+            'ref_swiglu': (None, [_PF, _PF, ctypes.c_uint, ctypes.c_uint, _PF]),
+            'ref_lm_head': (c_uint32, [c_void_p, _PF, ctypes.c_uint, _PF]),
+            'ref_fill_kv_synthetic': (c_int, [c_void_p, ctypes.c_uint, ctypes.c_uint64]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def pf(a):
+    return a.ctypes.data_as(_PF)
+
+
+def p8(a):
+    return a.ctypes.data_as(_P8)
+
+
+def p32(a):
+    return a.ctypes.data_as(_P32)
+
+
+def bf16_to_f32(bits):
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    bits = a.view(np.uint32)
+    assert not (bits & 0xffff).any(), 'array is not bf16-valued'
+    return (bits >> 16).astype(np.uint16)
+
+
+class RefModel:
+    """The oracle model over an SD-card asset folder; mirrors model_backend.Model."""
+
+    def __init__(self, sd, capacity=256, mode=0, threads=0):
+        err = ctypes.create_string_buffer(512)
+        L = lib()
+        if threads:
+            L.ref_set_threads(threads)
+        self.h = L.ref_open(str(sd).encode(), capacity, err, len(err))
+        if not self.h:
+            raise RuntimeError(f'oracle could not load {sd}: {err.value.decode()}')
+        self.capacity = capacity
+        self.set_mode(mode)
+        self.last_logits = None
+
+    def set_mode(self, mode):
+        self.mode = mode
+        lib().ref_set_mode(self.h, mode)
+
+    def clear(self):
+        lib().ref_clear(self.h)
+
+    @property
+    def position(self):
+        return lib().ref_position(self.h)
+
+    def forward(self, ids, position):
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        tok = c_uint32()
+        logits = np.empty(VOCAB, dtype=np.float32)
+        rc = lib().ref_forward(self.h, p32(ids), len(ids), position, ctypes.byref(tok), pf(logits))
+        if rc == -8:
+            raise ValueError(f'KV position mismatch pos={position} cached={self.position} ids={len(ids)}')
+        if rc:
+            raise ValueError(f'oracle forward failed ({rc})')
+        self.last_logits = logits
+        return tok.value
+
+    def dump(self, layer, rows):
+        bufs = {k: np.zeros((rows, c), dtype=np.float32)
+                for k, c in dict(q=896, k=128, v=128, context=896, h=896, m=4864, y=896).items()}
+        lib().ref_set_dump(self.h, layer, *[pf(bufs[k]) for k in ['q', 'k', 'v', 'context', 'h', 'm', 'y']])
+        self._dump = bufs
+        return bufs
+
+    def fill_kv_synthetic(self, length, seed):
+        if lib().ref_fill_kv_synthetic(self.h, length, seed):
+            raise ValueError('length exceeds capacity')
+
+    def kv8_state(self, layer):
+        n = self.position
+        kc = np.empty((2, n, 64), dtype=np.int8)
+        vc = np.empty((2, n, 64), dtype=np.int8)
+        ks = np.empty((2, n), dtype=np.float32)
+        vs = np.empty((2, n), dtype=np.float32)
+        lib().ref_kv8_state(self.h, layer, p8(kc), pf(ks), p8(vc), pf(vs))
+        return kc, ks, vc, vs
+
+    def weight(self, layer, proj, shape):
+        p = lib().ref_weight(self.h, layer, proj)
+        return np.ctypeslib.as_array(p, shape=shape)
+
+    def scale(self):
+        return np.ctypeslib.as_array(lib().ref_scale(self.h), shape=(304128 + VOCAB,))
+
+    def bias(self):
+        return np.ctypeslib.as_array(lib().ref_bias(self.h), shape=(24 * 1152,))
+
+    def gamma(self):
+        return np.ctypeslib.as_array(lib().ref_gamma(self.h), shape=(24 * 1792 + 896,))
+
+    def lm_weight(self):
+        return np.ctypeslib.as_array(lib().ref_lm_weight(self.h), shape=(VOCAB, 896))
+
+    def embedding(self):
+        return np.ctypeslib.as_array(lib().ref_embedding(self.h), shape=(VOCAB, 896))
+
+    def close(self):
+        if self.h:
+            lib().ref_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------ operator level
+def rmsnorm(x, gamma, eps=1e-6, mode=0):
+    x = f32(x)
+    out = np.empty_like(x)
+    lib().ref_rmsnorm(pf(x), x.shape[0], pf(f32(gamma)), eps, mode, pf(out))
+    return out
+
+
+def linear(x, w, scale, bias=None, mode=0):
+    x = f32(x)
+    w = np.ascontiguousarray(w, dtype=np.int8)
+    n, k = w.shape
+    out = np.empty((x.shape[0], n), dtype=np.float32)
+    if bias is None:
+        lib().ref_linear(pf(x), x.shape[0], k, p8(w), pf(f32(scale)), n, mode, pf(out))
+    else:
+        lib().ref_linear_bias(pf(x), x.shape[0], k, p8(w), pf(f32(scale)), pf(f32(bias)), n, mode, pf(out))
+    return out
+
+
+def rope_table(positions):
+    t = np.empty((positions, 64), dtype=np.float32)
+    lib().ref_rope_table(positions, pf(t))
+    return t
+
+
+def rope(x, positions, mode=0):
+    x = f32(x)
+    rows, heads = x.shape[0], x.shape[1]
+    out = np.empty_like(x)
+    pos = np.ascontiguousarray(positions, dtype=np.uint32)
+    lib().ref_rope(pf(x), rows, heads, p32(pos), mode, pf(out))
+    return out
+
+
+def kv8_quant(x):
+    x = f32(x).reshape(-1, 64)
+    codes = np.empty(x.shape, dtype=np.int8)
+    scales = np.empty(x.shape[0], dtype=np.float32)
+    lib().ref_kv8_quant(pf(x), x.shape[0], p8(codes), pf(scales))
+    return codes, scales
+
+
+def attention_kv8(q, positions, kcodes, kscales, vcodes, vscales, mode=0):
+    """q [rows][14][64]; caches [2][cap][64] / [2][cap] of one sequence."""
+    q = f32(q)
+    cap = kcodes.shape[1]
+    ctx = np.empty((q.shape[0], 896), dtype=np.float32)
+    pos = np.ascontiguousarray(positions, dtype=np.uint32)
+    lib().ref_attention_kv8(pf(q), q.shape[0], p32(pos), p8(np.ascontiguousarray(kcodes)),
+                            pf(f32(kscales)), p8(np.ascontiguousarray(vcodes)), pf(f32(vscales)), cap, mode,
+                            pf(ctx))
+    return ctx
+
+
+def attention_bf16(q, positions, k, v, mode=0):
+    """q [rows][14][64]; k, v [t][2][64] bf16-valued (one sequence)."""
+    q = f32(q)
+    ctx = np.empty((q.shape[0], 896), dtype=np.float32)
+    pos = np.ascontiguousarray(positions, dtype=np.uint32)
+    lib().ref_attention_bf16(pf(q), q.shape[0], p32(pos), pf(f32(k)), pf(f32(v)), mode, pf(ctx))
+    return ctx
+
+
+def swiglu(gate, up, mode=0):
+    g, u = f32(gate), f32(up)
+    out = np.empty_like(g)
+    lib().ref_swiglu(pf(g), pf(u), g.size, mode, pf(out))
+    return out

@@ -1,0 +1,118 @@
+"""C ABI (include/qwen_b200.h) on CPU: every declared entry point is exported
+by the in-tree libqwen_b200.so, and the host logic that needs no GPU behaves
+like the reference's boundary (status codes of generation.h:16, CSR map of
+src/software/README.md, request checks of generation.c:8-9)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import qwen_b200
+from qwen_b200 import _lib
+
+from qgen import EngineOps, qgen_run
+
+HEADER = Path(__file__).resolve().parents[1] / 'include' / 'qwen_b200.h'
+
+
+def declared():
+    text = re.sub(r'/\*.*?\*/', '', HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r'\b(qwen_b200_\w+)\s*\(', text)))
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared()
+    assert len(names) >= 30
+    so = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in names if not hasattr(so, n)]
+    assert not missing, missing
+
+
+def test_every_declared_symbol_has_a_binding():
+    assert set(declared()) <= set(_lib._SIGNATURES), set(declared()) - set(_lib._SIGNATURES)
+
+
+@pytest.fixture
+def handle():
+    L = qwen_b200.lib()
+    cfg = _lib.Config()
+    L.qwen_b200_default_config(ctypes.byref(cfg))
+    h = ctypes.c_void_p()
+    assert L.qwen_b200_open(ctypes.byref(cfg), ctypes.byref(h)) == 0
+    yield L, h
+    assert L.qwen_b200_close(h) == 0
+
+
+def test_default_config_and_bad_config():
+    L = qwen_b200.lib()
+    cfg = _lib.Config()
+    L.qwen_b200_default_config(ctypes.byref(cfg))
+    assert (cfg.device, cfg.max_seqs, cfg.max_context, cfg.max_rows) == (0, 1, 256, 256)
+    assert abs(cfg.rms_eps - 1e-6) < 1e-12
+    cfg.max_context = 0
+    h = ctypes.c_void_p()
+    assert L.qwen_b200_open(ctypes.byref(cfg), ctypes.byref(h)) == _lib.EINVAL
+    assert L.qwen_b200_open(None, None) == _lib.EINVAL
+
+
+def test_csr_identity_registers(handle):
+    L, h = handle
+    assert L.qwen_b200_csr_read(h, 0x00) == 0x515732354b563236
+    assert L.qwen_b200_csr_read(h, 0x08) == 0x10000
+    assert L.qwen_b200_csr_read(h, 0x18) == 0  # idle
+    L.qwen_b200_csr_write(h, 0x0140, 255)      # address/config CSRs are accepted (main.c:149-161)
+    assert L.qwen_b200_csr_read(h, 0x0140) == 255
+
+
+def test_csr_rejects_malformed_requests(handle):
+    L, h = handle
+    L.qwen_b200_embedding(h, 5, 0)
+    for mode, seq, ctx, pos in [(0, 0, 0, 0), (0, 1, 2, 0), (0, 1, 3, 2), (1, 1, 2, 1), (0, 300, 300, 0)]:
+        L.qwen_b200_csr_write(h, 0x10, 8)  # CLEAR
+        for off, v in [(0x80, mode), (0x88, seq), (0x90, ctx), (0x98, pos)]:
+            L.qwen_b200_csr_write(h, off, v)
+        L.qwen_b200_csr_write(h, 0x10, 1)
+        assert L.qwen_b200_csr_read(h, 0x18) == 8, (mode, seq, ctx, pos)
+        assert L.qwen_b200_csr_read(h, 0x30) == 1
+    L.qwen_b200_embedding(h, 151936, 0)  # out-of-vocab id recorded in ACT_IN row 0
+    L.qwen_b200_csr_write(h, 0x10, 8)
+    for off, v in [(0x80, 0), (0x88, 1), (0x90, 1), (0x98, 0)]:
+        L.qwen_b200_csr_write(h, off, v)
+    L.qwen_b200_csr_write(h, 0x10, 1)
+    assert L.qwen_b200_csr_read(h, 0x30) == 1
+
+
+def test_generation_loop_without_model_reports_device_error(handle):
+    L, h = handle
+    status, res, tokens = qgen_run(EngineOps(L, h), [1, 2, 3], 4)
+    assert status == -3 and res.produced == 0 and not tokens
+    assert L.qwen_b200_csr_read(h, 0x30) == 3  # no model loaded
+
+
+def test_sequence_calls_without_model(handle):
+    L, h = handle
+    tok = ctypes.c_uint32()
+    ids = (ctypes.c_uint32 * 2)(1, 2)
+    assert L.qwen_b200_forward(h, 0, ids, 2, 0, ctypes.byref(tok), None) == _lib.EINVAL
+    assert b'no assets' in L.qwen_b200_last_error(h)
+    assert L.qwen_b200_reset(h, 0) == 0
+    assert L.qwen_b200_reset(h, 7) == _lib.EINVAL
+    assert L.qwen_b200_load_assets(h, b'/nonexistent/sd') == _lib.EIO
+
+
+def test_op_entry_points_reject_null_pointers():
+    L = qwen_b200.lib()
+    assert L.qwen_b200_op_embed(None, None, 1, None, None) == _lib.EINVAL
+    assert L.qwen_b200_op_attention(None, 1, None, None, 1, None, None, None, None, 16, None, None, 0, None) \
+        == _lib.EINVAL
+    assert L.qwen_b200_attention_workspace(64, 2048) > 64 * 14 * 2048 * 4
+    assert L.qwen_b200_lm_head_workspace(1, 151936) >= 4748 * 8
+
+
+def test_rope_table_matches_oracle():
+    import numpy as np
+    from oracle import ref
+    t = np.empty((300, 64), np.float32)
+    qwen_b200.lib().qwen_b200_rope_table(300, t.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    assert np.array_equal(t, ref.rope_table(300))

@@ -1,0 +1,212 @@
+"""Whole-model parity on the B200: the engine (through the C ABI) against the
+oracle in KV8 mode on the seeded synthetic Qwen2.5-0.5B, following the
+reference's own sign-off (legacy_.../tests/compare_rtl_math.py:38 token
+equality on identical histories; compare_all_layers.py given-operand stages).
+
+Bars: greedy token ids identical; KV8 codes/scales bit-exact given the same
+bf16 K/V; logits within max|d| <= 2e-2 x logit range; per-stage given-operand
+outputs >= 97 % bit-equal (rel-L2 < 1e-3).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import qwen_b200
+from gpu_util import assert_bf16_close, from_bits
+from oracle import ref
+from qgen import EngineOps, qgen_run
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def engine(sd_root):
+    e = qwen_b200.Engine(device=0, max_seqs=4, max_context=512, max_rows=256).load_assets(sd_root)
+    yield e
+    e.close()
+
+
+@pytest.fixture(scope='module')
+def oracle_kv8(oracle_model):
+    oracle_model.set_mode(ref.KV8)
+    yield oracle_model
+    oracle_model.set_mode(0)
+
+
+def rel_l2(a, b):
+    a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def generate_gpu(engine, prompt, steps, slot=0):
+    engine.reset(slot)
+    ids, pos, toks, logits = list(prompt), 0, [], []
+    for _ in range(steps):
+        tok, lg = engine.forward(slot, ids, pos, want_logits=True)
+        toks.append(tok)
+        logits.append(from_bits(lg))
+        pos += len(ids)
+        ids = [tok]
+    return toks, logits
+
+
+def generate_oracle(m, prompt, steps):
+    m.clear()
+    ids, pos, toks, logits = list(prompt), 0, [], []
+    for _ in range(steps):
+        tok = m.forward(ids, pos)
+        toks.append(tok)
+        logits.append(m.last_logits.copy())
+        pos += len(ids)
+        ids = [tok]
+    return toks, logits
+
+
+def test_generation_matches_oracle(engine, oracle_kv8, golden):
+    g_toks, g_logits = generate_gpu(engine, golden['prompt'], 6)
+    o_toks, o_logits = generate_oracle(oracle_kv8, golden['prompt'], 6)
+    assert g_toks == o_toks
+    for g, o in zip(g_logits, o_logits):
+        assert np.abs(g - o).max() <= 2e-2 * float(o.max() - o.min())
+
+
+def test_teacher_forced_matches_oracle(engine, oracle_kv8, golden):
+    engine.reset(0)
+    oracle_kv8.clear()
+    for i, tok in enumerate(golden['prompt']):
+        g, lg = engine.forward(0, [tok], i, want_logits=True)
+        o = oracle_kv8.forward([tok], i)
+        assert g == o, f'position {i}'
+        ol = oracle_kv8.last_logits
+        assert np.abs(from_bits(lg) - ol).max() <= 2e-2 * float(ol.max() - ol.min())
+
+
+def test_kv8_tokens_against_reference_bf16_kv(engine, golden):
+    """The reference keeps a bf16 KV cache; the engine's KV8 cache is the
+    north-star change. Record agreement with the reference's own tokens."""
+    g_toks, _ = generate_gpu(engine, golden['prompt'], 6)
+    ref_toks = [s['token'] for s in golden['generate']]
+    # the oracle in KV8 mode reproduces all six reference tokens on this seed
+    assert g_toks == ref_toks
+
+
+@pytest.mark.parametrize('layer', [0, 23])
+def test_given_operand_stages_and_kv_codes(engine, oracle_kv8, golden, layer):
+    rows = len(golden['prompt'])
+    engine.reset(0)
+    dump = engine.set_dump(layer, rows)
+    engine.forward(0, golden['prompt'], 0)
+    engine.disarm_dump()
+    d = {k: from_bits(v) for k, v in dump.items()}
+    m = oracle_kv8
+    sc = m.scale()[layer * 12672:(layer + 1) * 12672]
+    gamma = m.gamma()[layer * 1792:(layer + 1) * 1792]
+    pos = np.arange(rows, dtype=np.uint32)
+    # KV8 codes: bit-exact given the engine's own bf16 k / v
+    kc, ks, vc, vs = engine.read_kv(0, layer, rows)
+    for codes, scales, src in [(kc, ks, d['k']), (vc, vs, d['v'])]:
+        ec, es = ref.kv8_quant(src.reshape(rows, 2, 64))
+        assert np.array_equal(codes.transpose(1, 0, 2).reshape(-1, 64), ec)
+        assert np.array_equal(scales.T.reshape(-1), es)
+    # attention given the engine's q and its KV8 cache
+    cap = rows
+    ctx = ref.attention_kv8(d['q'].reshape(rows, 14, 64), pos, kc, ks, vc, vs)
+    assert_bf16_close(d['context'], ctx, min_equal=0.97, max_ulps=2, what='attention')
+    # O projection + residual is checked through h = x_in + o; x_in is not
+    # dumped, so check the FFN and down stages, which have all operands
+    z = ref.rmsnorm(d['h'], gamma[896:])
+    gate = ref.linear(z, m.weight(layer, 4, (4864, 896)), sc[2048:6912])
+    up = ref.linear(z, m.weight(layer, 5, (4864, 896)), sc[6912:11776])
+    assert_bf16_close(d['m'], ref.swiglu(gate, up), min_equal=0.97, what='ffn')
+    dn = ref.linear(d['m'], m.weight(layer, 6, (896, 4864)), sc[11776:12672])
+    y = np.vectorize(lambda a: ref.lib().ref_bf(a, 0))(d['h'] + dn).astype(np.float32)
+    assert_bf16_close(d['y'], y, min_equal=0.97, what='down')
+    del cap
+
+
+def test_batched_decode_equals_single_sequences(engine, golden):
+    prompts = [golden['prompt'], golden['prompt'][::-1], golden['prompt'][3:11]]
+    singles = [generate_gpu(engine, p, 4, slot=0)[0] for p in prompts]
+    firsts = []
+    for s, p in enumerate(prompts):
+        engine.reset(s)
+        firsts.append(engine.forward(s, p, 0)[0])
+    toks = np.array(firsts, np.uint32)
+    out = [toks.tolist()]
+    for _ in range(3):
+        toks = engine.decode_step([0, 1, 2], toks)
+        out.append(toks.tolist())
+    batched = [[step[i] for step in out] for i in range(3)]
+    assert batched == singles
+
+
+def test_chunked_prefill_equals_single_chunk(sd_root, golden):
+    e = qwen_b200.Engine(device=0, max_seqs=1, max_context=64, max_rows=5).load_assets(sd_root)
+    try:
+        tok, logits = e.forward(0, golden['prompt'], 0, want_logits=True)
+    finally:
+        e.close()
+    e2 = qwen_b200.Engine(device=0, max_seqs=1, max_context=64, max_rows=64).load_assets(sd_root)
+    try:
+        tok2, logits2 = e2.forward(0, golden['prompt'], 0, want_logits=True)
+    finally:
+        e2.close()
+    assert tok == tok2
+    assert np.array_equal(logits, logits2)
+
+
+def test_device_decode_graph_equals_host_decode(engine, golden):
+    import torch
+    prompts = [golden['prompt'], golden['prompt'][::-1]]
+    firsts = []
+    for s, p in enumerate(prompts):
+        engine.reset(s)
+        firsts.append(engine.forward(s, p, 0)[0])
+    host_toks = [np.array(firsts, np.uint32)]
+    for _ in range(4):
+        host_toks.append(engine.decode_step([0, 1], host_toks[-1]))
+    for s, p in enumerate(prompts):
+        engine.reset(s)
+        engine.forward(s, p, 0)
+    a = torch.tensor(firsts, dtype=torch.int32, device='cuda')
+    b = torch.zeros(2, dtype=torch.int32, device='cuda')
+    dev_toks = []
+    for _ in range(4):  # first call runs eagerly and captures, the rest replay the graph
+        engine.decode_step_device(ctypes.c_void_p(a.data_ptr()), 2, ctypes.c_void_p(b.data_ptr()),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        dev_toks.append(b.cpu().numpy().astype(np.uint32))
+        a.copy_(b)
+    assert [t.tolist() for t in dev_toks] == [t.tolist() for t in host_toks[1:]]
+    assert engine.position(0) == len(prompts[0]) + 4
+
+
+def test_csr_protocol_drives_generation(engine, golden):
+    L = qwen_b200.lib()
+    expect, _ = generate_gpu(engine, golden['prompt'], 5)
+    L.qwen_b200_clear(engine.h)
+    status, res, toks = qgen_run(EngineOps(L, engine.h), golden['prompt'], 5)
+    assert status == 0 and res.produced == 5 and toks == expect
+    # a decode START at a stale position is rejected like a PL error
+    L.qwen_b200_csr_write(engine.h, 0x80, 1)
+    L.qwen_b200_csr_write(engine.h, 0x88, 1)
+    L.qwen_b200_csr_write(engine.h, 0x90, 4)
+    L.qwen_b200_csr_write(engine.h, 0x98, 3)
+    L.qwen_b200_csr_write(engine.h, 0x10, 1)
+    assert L.qwen_b200_csr_read(engine.h, 0x18) == 8
+
+
+def test_model_mirror_interface(sd_root, golden):
+    m = qwen_b200.Model(sd_root)
+    try:
+        tok = m.forward(golden['prompt'], 0)
+        assert m.position == 16 and m.last_logits.shape == (151936,)
+        with pytest.raises(ValueError):
+            m.forward([tok], 3)
+        with pytest.raises(ValueError):
+            m.forward([], 16)
+        m.clear()
+        assert m.forward(golden['prompt'], 0) == tok
+    finally:
+        m.close()
