@@ -135,7 +135,9 @@ __global__ void __launch_bounds__(7 * QB_HD) attn_pv_kernel(AttnArgs a) {
     const int L = (int)a.positions[r] + 1;
     const int t0 = c * AT;
     if (t0 >= L) return;
-    const int nch = (L + AT - 1) / AT;
+    // Chunks actually launched for this row: a caller bound below positions+1
+    // truncates the context instead of leaving the combine waiting for chunks.
+    const int nch = min((L + AT - 1) / AT, (int)gridDim.x);
     const int slot = (int)a.slots[r];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ float Ms[7], Is[7];
