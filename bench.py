@@ -374,9 +374,21 @@ def bs1_decode(eng, args, stream, sp, hbm):
     ms = t0.elapsed_time(t1) / args.steps
     sb = step_bytes([ctx0 + args.steps // 2])
     ach = sb / (ms / 1000) / 1e9
+    # device time per kernel class of one bs1 step (events around each launch)
+    ms_cls = np.zeros(8, np.float32)
+    n_cls = np.zeros(8, np.uint32)
+    tok_in = np.array([int(bufs[(args.warmup + args.steps) % 2][0].item())], np.uint32)
+    out = np.empty(1, np.uint32)
+    qwen_b200.lib().qwen_b200_profile_decode(eng.h, tok_in.ctypes.data_as(qwen_b200._lib._P32), 1,
+                                             out.ctypes.data_as(qwen_b200._lib._P32),
+                                             ms_cls.ctypes.data_as(qwen_b200._lib._PF),
+                                             n_cls.ctypes.data_as(qwen_b200._lib._P32))
+    kernels = {name: {'launches': int(n_cls[i]), 'us_per_step': round(1000 * float(ms_cls[i]), 1)}
+               for i, name in enumerate(CLASSES) if n_cls[i]}
     return {'value': round(1000 / ms, 1), 'unit': 'tokens/s', 'ms_per_token': round(ms, 4),
             'context': ctx0 + args.steps // 2, 'bytes_per_token': sb, 'achieved_gbs': round(ach, 1),
-            'frac_of_hbm_roofline': round(ach / hbm, 4)}
+            'frac_of_hbm_roofline': round(ach / hbm, 4), 'kernels': kernels,
+            'kernel_sum_us': round(1000 * float(ms_cls.sum()), 1)}
 
 
 def gpu_index(local):

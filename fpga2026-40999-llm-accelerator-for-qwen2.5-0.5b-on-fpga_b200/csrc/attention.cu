@@ -37,18 +37,21 @@ struct AttnArgs {
 };
 
 struct AttnLayout {
-    size_t s_off, st_off, part_off, cnt_off, total;
+    size_t cnt_off, s_off, st_off, part_off, total;
 };
 
+// Workspace regions for up to `rows` rows. The layout depends only on the
+// workspace's row capacity, never on the rows of one launch, so the completion
+// counters (first region) are never overwritten by another launch's scores.
 static AttnLayout attn_layout(int rows, int cap) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
     const size_t nck = (size_t)(cap + AT - 1) / AT;
     AttnLayout L;
-    L.s_off = 0;
-    L.st_off = al((size_t)rows * QB_QH * cap * 4);
+    L.cnt_off = 0;
+    L.s_off = al((size_t)rows * 2 * 4);
+    L.st_off = L.s_off + al((size_t)rows * QB_QH * cap * 4);
     L.part_off = L.st_off + al((size_t)rows * QB_QH * nck * 8);
-    L.cnt_off = L.part_off + al((size_t)rows * QB_QH * nck * 64 * 4);
-    L.total = L.cnt_off + al((size_t)rows * 2 * 4);
+    L.total = L.part_off + al((size_t)rows * QB_QH * nck * 64 * 4);
     return L;
 }
 
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(7 * QB_HD) attn_pv_kernel(AttnArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ float Ms[7], Is[7];
     __shared__ float P[7][AT];
-    __shared__ float V[AT][QB_HD];
+    __shared__ __align__(16) float V[AT][QB_HD];  // written with float4 stores
     __shared__ unsigned ticket;
     if (warp < 7) {
         const float2 *st = a.stats + ((size_t)r * QB_QH + g * 7 + warp) * a.nck;
@@ -203,9 +206,9 @@ __global__ void __launch_bounds__(7 * QB_HD) attn_pv_kernel(AttnArgs a) {
 
 int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
                      const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
-                     void *ws, size_t ws_bytes, bool clear_counters, cudaStream_t st) {
-    if (rows <= 0 || max_len <= 0 || max_len > cap) return -1;
-    const AttnLayout L = attn_layout(rows, cap);
+                     void *ws, size_t ws_bytes, int ws_rows, bool clear_counters, cudaStream_t st) {
+    if (rows <= 0 || rows > ws_rows || max_len <= 0 || max_len > cap) return -1;
+    const AttnLayout L = attn_layout(ws_rows, cap);
     if (ws_bytes < L.total) return -1;
     char *base = reinterpret_cast<char *>(ws);
     AttnArgs a;

@@ -81,6 +81,7 @@ struct qwen_b200 {
     uint64_t csr_error = 0;
     uint32_t csr_token = 0;
     cudaEvent_t csr_event = nullptr;
+    cudaEvent_t staged = nullptr;  // the last host->device copy out of h_meta has been read
 };
 
 namespace {
@@ -152,6 +153,7 @@ int allocate(qwen_b200 *h) {
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&h->cap_stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&h->csr_event, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&h->staged, cudaEventDisableTiming));
     void *p;
     int rc;
     // weights: one block per layer
@@ -310,7 +312,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         {
             LaunchScope ls(h, 2, st, 2);
             RK(launch_attention(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx, h->attn_ws,
-                                h->attn_ws_bytes, false, st));
+                                h->attn_ws_bytes, h->R, false, st));
         }
         if (dq) {
             CK(cudaMemcpyAsync(dq, h->q, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
@@ -454,6 +456,7 @@ int qwen_b200_close(qwen_b200 *h) {
         cudaFreeHost(h->h_tokens);
         cudaFreeHost(h->h_slot_pos);
         if (h->csr_event) cudaEventDestroy(h->csr_event);
+        if (h->staged) cudaEventDestroy(h->staged);
         if (h->stream) cudaStreamDestroy(h->stream);
         if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
     }
@@ -555,6 +558,9 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
     for (uint32_t c0 = 0; c0 < rows; c0 += (uint32_t)h->cfg.max_rows) {
         const int n = (int)std::min<uint32_t>(h->cfg.max_rows, rows - c0);
         const bool last = c0 + (uint32_t)n == rows;
+        // the previous chunk's copy out of the pinned staging buffer must have
+        // happened before the buffer is rewritten
+        if (c0) CK(cudaEventSynchronize(h->staged));
         for (int i = 0; i < n; ++i) {
             h->h_meta[i] = ids[c0 + i];
             h->h_meta[n + i] = slot;
@@ -562,6 +568,7 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
         }
         h->h_meta[3 * n] = (uint32_t)(n - 1);
         CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * n + 1) * 4, cudaMemcpyHostToDevice, st));
+        CK(cudaEventRecord(h->staged, st));
         rc = run_forward(h, n, (int)(position + c0 + (uint32_t)n), last ? 1 : 0, n == 1, last && logits, h->tokens,
                          st);
         if (rc) return rc;
@@ -646,7 +653,7 @@ int qwen_b200_decode_step_device(qwen_b200 *h, const uint32_t *d_tokens_in, uint
     }
     const uint32_t chunks = (max_len + 127) / 128;
     const int bucket_len = (int)std::min<uint32_t>(chunks * 128, h->cfg.max_context);
-    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
     const auto key = std::make_tuple(n, chunks, (const void *)d_tokens_in, (const void *)d_tokens_out);
     auto it = h->graphs.find(key);
     if (it != h->graphs.end()) {
@@ -886,7 +893,7 @@ int qwen_b200_op_attention(const uint16_t *q, uint32_t rows, const uint32_t *slo
     if (!q || !slots || !positions || !kcodes || !kscales || !vcodes || !vscales || !ctx || !workspace)
         return QWEN_B200_EINVAL;
     return launch_attention(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
-                            (int)capacity, ctx, workspace, workspace_bytes, true, (cudaStream_t)stream);
+                            (int)capacity, ctx, workspace, workspace_bytes, (int)rows, true, (cudaStream_t)stream);
 }
 
 int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w_gu,

@@ -40,11 +40,14 @@ int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps
                    const float *scale, int vocab, uint16_t *logits, uint32_t *tokens, void *ws, size_t ws_bytes,
                    cudaStream_t st);
 
-// Attention over a KV8 cache (two passes + last-block combine).
+// Attention over a KV8 cache (two passes + last-block combine). The
+// workspace is laid out for ws_rows rows (>= rows); its completion counters
+// must be zero before the first launch and are left zero by every launch
+// (clear_counters zeroes them first).
 size_t attention_workspace(int rows, int cap);
 int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
                      const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
-                     void *ws, size_t ws_bytes, bool clear_counters, cudaStream_t st);
+                     void *ws, size_t ws_bytes, int ws_rows, bool clear_counters, cudaStream_t st);
 
 int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t *x, cudaStream_t st);
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st);

@@ -103,7 +103,7 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
 int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
                           uint32_t *tokens_out);
 /* The same step for slots 0..n-1 with device-resident token arrays, enqueued
- * on `stream` (NULL = the handle's stream); d_tokens_out is written on the
+ * on `stream` (a cudaStream_t; NULL is the CUDA default stream); d_tokens_out is written on the
  * device and ids are not range-checked on the host. The first call for a given
  * (n, context bucket of 128, buffers) runs eagerly and captures a CUDA graph
  * that later calls replay. */

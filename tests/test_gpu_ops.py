@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import qwen_b200
-from gpu_util import assert_bf16_close, bf16_round, dev, from_bits, host, stream, sync, to_bits, vp
+from gpu_util import Keep, assert_bf16_close, bf16_round, dev, from_bits, host, stream, sync, to_bits, vp
 from oracle import ref
 
 pytestmark = pytest.mark.gpu
@@ -48,31 +48,34 @@ def test_embed_bit_exact():
 
 @pytest.mark.parametrize('rows', [1, 7, 64])
 def test_rmsnorm(rows):
+    keep = Keep()
     r = rng(rows)
     x = rand_bf16(r, (rows, 896), 3.0)
     g = bf16_round(r.uniform(0.5, 1.5, 896).astype(np.float32))
     out = dev(np.zeros((rows, 896), np.int16))
-    assert L().qwen_b200_op_rmsnorm(vp(dev(to_bits(x).view(np.int16))), vp(dev(to_bits(g).view(np.int16))), rows,
+    assert L().qwen_b200_op_rmsnorm(keep((to_bits(x).view(np.int16))), keep((to_bits(g).view(np.int16))), rows,
                                     ctypes.c_float(1e-6), vp(out), stream()) == 0
     sync()
-    assert_bf16_close(from_bits(host(out).view(np.uint16)), ref.rmsnorm(x, g), what='rmsnorm')
+    # two bf16 roundings (x * r, then * gamma): an ulp flip in the first can move the second by two
+    assert_bf16_close(from_bits(host(out).view(np.uint16)), ref.rmsnorm(x, g), max_ulps=2, what='rmsnorm')
 
 
 @pytest.mark.parametrize('k,n', [(896, 1152), (896, 896), (4864, 896)])
 @pytest.mark.parametrize('rows', [1, 3, 8, 13, 64])
 @pytest.mark.parametrize('epi', ['plain', 'bias', 'residual'])
 def test_gemm_w8a16(k, n, rows, epi):
+    keep = Keep()
     r = rng(k + n + rows)
     x = rand_bf16(r, (rows, k))
     w, s = rand_weights(r, n, k)
     b = rand_bf16(r, n, 0.02)
     y0 = rand_bf16(r, (rows, n))
     yd = dev(to_bits(y0).view(np.int16))
-    args = (vp(dev(to_bits(x).view(np.int16))), rows, k, vp(dev(w)), vp(dev(s)), n)
+    args = (keep((to_bits(x).view(np.int16))), rows, k, keep((w)), keep((s)), n)
     if epi == 'residual':
         assert L().qwen_b200_op_gemm_w8a16_residual(*args, vp(yd), stream()) == 0
     else:
-        bias = vp(dev(to_bits(b).view(np.int16))) if epi == 'bias' else None
+        bias = keep((to_bits(b).view(np.int16))) if epi == 'bias' else None
         assert L().qwen_b200_op_gemm_w8a16(*args, bias, vp(yd), stream()) == 0
     sync()
     got = from_bits(host(yd).view(np.uint16))
@@ -80,11 +83,13 @@ def test_gemm_w8a16(k, n, rows, epi):
         exp = ref.f32(np.vectorize(lambda a: ref.lib().ref_bf(a, 0))(y0 + ref.linear(x, w, s)))
     else:
         exp = ref.linear(x, w, s, bias=b if epi == 'bias' else None)
-    assert_bf16_close(got, exp, what=f'gemm {k}x{n} rows {rows} {epi}')
+    # bias / residual add a second bf16 rounding after the scaled product
+    assert_bf16_close(got, exp, max_ulps=1 if epi == 'plain' else 2, what=f'gemm {k}x{n} rows {rows} {epi}')
 
 
 @pytest.mark.parametrize('rows', [1, 5, 16])
 def test_swiglu(rows):
+    keep = Keep()
     r = rng(100 + rows)
     x = rand_bf16(r, (rows, 896), 2.0)
     g = bf16_round(r.uniform(0.5, 1.5, 896).astype(np.float32))
@@ -95,33 +100,35 @@ def test_swiglu(rows):
     sgu = np.empty(9728, np.float32)
     sgu[0::2], sgu[1::2] = sg, su
     mid = dev(np.zeros((rows, 4864), np.int16))
-    assert L().qwen_b200_op_swiglu(vp(dev(to_bits(x).view(np.int16))), rows, vp(dev(to_bits(g).view(np.int16))),
-                                   ctypes.c_float(1e-6), vp(dev(wgu)), vp(dev(sgu)), vp(mid), stream()) == 0
+    assert L().qwen_b200_op_swiglu(keep((to_bits(x).view(np.int16))), rows, keep((to_bits(g).view(np.int16))),
+                                   ctypes.c_float(1e-6), keep((wgu)), keep((sgu)), vp(mid), stream()) == 0
     sync()
     z = ref.rmsnorm(x, g)
     exp = ref.swiglu(ref.linear(z, wg, sg), ref.linear(z, wu, su))
     assert_bf16_close(from_bits(host(mid).view(np.uint16)), exp, what='swiglu')
 
 
-def rope_table_dev(positions):
+def rope_table(positions):
     t = np.empty((positions, 64), np.float32)
     L().qwen_b200_rope_table(positions, t.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
-    return dev(t)
+    return t
 
 
 def test_rope_bit_exact():
+    keep = Keep()
     r = rng(7)
     rows, heads = 23, 14
     x = rand_bf16(r, (rows, heads, 64), 2.0)
     pos = r.integers(0, 4096, rows).astype(np.uint32)
     xd = dev(to_bits(x).view(np.int16))
-    assert L().qwen_b200_op_rope(vp(xd), rows, heads, vp(dev(pos.view(np.int32))), vp(rope_table_dev(4096)),
+    assert L().qwen_b200_op_rope(vp(xd), rows, heads, keep((pos.view(np.int32))), keep(rope_table(4096)),
                                  stream()) == 0
     sync()
     assert np.array_equal(from_bits(host(xd).view(np.uint16)), ref.rope(x, pos))
 
 
 def test_kv8_append_bit_exact():
+    keep = Keep()
     r = rng(8)
     rows, nslots, cap = 40, 3, 64
     x = rand_bf16(r, (rows, 2, 64), 3.0)
@@ -134,8 +141,8 @@ def test_kv8_append_bit_exact():
         positions[idx] = r.permutation(cap)[:len(idx)]
     codes = dev(np.zeros((nslots, 2, cap, 64), np.int8))
     scales = dev(np.full((nslots, 2, cap), -1.0, np.float32))
-    assert L().qwen_b200_op_kv8_append(vp(dev(to_bits(x).view(np.int16))), rows, vp(dev(slots.view(np.int32))),
-                                       vp(dev(positions.view(np.int32))), vp(codes), vp(scales), cap,
+    assert L().qwen_b200_op_kv8_append(keep((to_bits(x).view(np.int16))), rows, keep((slots.view(np.int32))),
+                                       keep((positions.view(np.int32))), vp(codes), vp(scales), cap,
                                        stream()) == 0
     sync()
     c, s = host(codes), host(scales)
@@ -156,14 +163,15 @@ def random_cache(r, nslots, cap):
 
 
 def run_attention(q, slots, positions, cache, cap, max_len=None):
+    keep = Keep()
     kc, ks, vc, vs = (dev(a) for a in cache)
     rows = q.shape[0]
     ws_bytes = L().qwen_b200_attention_workspace(rows, cap)
     ws = dev(np.zeros(ws_bytes, np.uint8))
     ctx = dev(np.zeros((rows, 896), np.int16))
     max_len = max_len or int(positions.max()) + 1
-    rc = L().qwen_b200_op_attention(vp(dev(to_bits(q).view(np.int16))), rows, vp(dev(slots.view(np.int32))),
-                                    vp(dev(positions.view(np.int32))), max_len, vp(kc), vp(ks), vp(vc), vp(vs), cap,
+    rc = L().qwen_b200_op_attention(keep((to_bits(q).view(np.int16))), rows, keep((slots.view(np.int32))),
+                                    keep((positions.view(np.int32))), max_len, vp(kc), vp(ks), vp(vc), vp(vs), cap,
                                     vp(ctx), vp(ws), ws_bytes, stream())
     assert rc == 0
     sync()
@@ -203,6 +211,7 @@ def test_attention_prefill_rows_and_loose_bound():
 
 
 def test_qkv_fused_against_oracle_chain():
+    keep = Keep()
     r = rng(21)
     rows, cap = 9, 64
     x = rand_bf16(r, (rows, 896), 2.0)
@@ -214,10 +223,10 @@ def test_qkv_fused_against_oracle_chain():
     q = dev(np.zeros((rows, 896), np.int16))
     kc, vc = dev(np.zeros((1, 2, cap, 64), np.int8)), dev(np.zeros((1, 2, cap, 64), np.int8))
     ks, vs = dev(np.zeros((1, 2, cap), np.float32)), dev(np.zeros((1, 2, cap), np.float32))
-    assert L().qwen_b200_op_qkv(vp(dev(to_bits(x).view(np.int16))), rows, vp(dev(to_bits(g).view(np.int16))),
-                                ctypes.c_float(1e-6), vp(dev(w)), vp(dev(s)), vp(dev(to_bits(b).view(np.int16))),
-                                vp(dev(slots.view(np.int32))), vp(dev(positions.view(np.int32))),
-                                vp(rope_table_dev(cap)), vp(q), vp(kc), vp(ks), vp(vc), vp(vs), cap, stream()) == 0
+    assert L().qwen_b200_op_qkv(keep((to_bits(x).view(np.int16))), rows, keep((to_bits(g).view(np.int16))),
+                                ctypes.c_float(1e-6), keep((w)), keep((s)), keep((to_bits(b).view(np.int16))),
+                                keep((slots.view(np.int32))), keep((positions.view(np.int32))),
+                                keep(rope_table(cap)), vp(q), vp(kc), vp(ks), vp(vc), vp(vs), cap, stream()) == 0
     sync()
     h = ref.rmsnorm(x, g)
     y = ref.linear(h, w, s, bias=b)
@@ -244,6 +253,7 @@ def lm_oracle(x, g, w, s):
 
 @pytest.mark.parametrize('rows', [1, 5])
 def test_lm_head_argmax_with_planted_ties(rows):
+    keep = Keep()
     r = rng(30 + rows)
     vocab = 8192
     x = rand_bf16(r, (rows, 896), 2.0)
@@ -258,9 +268,9 @@ def test_lm_head_argmax_with_planted_ties(rows):
     toks_d = dev(np.zeros(rows, np.int32))
     ws_bytes = L().qwen_b200_lm_head_workspace(rows, vocab)
     ws = dev(np.zeros(ws_bytes, np.uint8))
-    assert L().qwen_b200_op_lm_head_argmax(vp(dev(to_bits(x).view(np.int16))), rows,
-                                           vp(dev(to_bits(g).view(np.int16))), ctypes.c_float(1e-6), vp(dev(w)),
-                                           vp(dev(s)), vocab, vp(logits_d), vp(toks_d), vp(ws), ws_bytes,
+    assert L().qwen_b200_op_lm_head_argmax(keep((to_bits(x).view(np.int16))), rows,
+                                           keep((to_bits(g).view(np.int16))), ctypes.c_float(1e-6), keep((w)),
+                                           keep((s)), vocab, vp(logits_d), vp(toks_d), vp(ws), ws_bytes,
                                            stream()) == 0
     sync()
     exp_logits, exp_toks = lm_oracle(x, g, w, s)
