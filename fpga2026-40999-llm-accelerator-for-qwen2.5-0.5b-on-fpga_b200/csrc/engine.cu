@@ -30,9 +30,13 @@ constexpr int CSR_IDS = 256;  // ACT_IN rows addressable through the embedding c
 
 struct LayerW {
     int8_t *qkv, *o, *gu, *d;  // [1152][896], [896][896], [9728][896] gate/up interleaved, [896][4864]
+    int8_t *tqkv, *to, *tgu, *td;  // the same weights tiled [n/128][k/64][128][64] for the tensor-core GEMM
     float *s_qkv, *s_o, *s_gu, *s_d;
     uint16_t *bias, *g_attn, *g_ffn;
 };
+
+// Rows at or above which a step uses the tcgen05 GEMMs instead of the GEMVs.
+constexpr int TC_MIN_ROWS = 9;
 
 enum CsrState { CSR_IDLE = 0, CSR_BUSY = 1, CSR_DONE = 2, CSR_ERROR = 3 };
 
@@ -48,13 +52,17 @@ struct qwen_b200 {
     // model
     LayerW L[NL];
     uint16_t *g_final = nullptr, *embed = nullptr;
-    int8_t *lmw = nullptr;
+    int8_t *lmw = nullptr, *tlmw = nullptr;
     float *s_lm = nullptr, *rope = nullptr;
     // KV8 caches: codes [layer][slot][2][cap][64], scales [layer][slot][2][cap]
     int8_t *kc = nullptr, *vc = nullptr;
     float *ks = nullptr, *vs = nullptr;
     // activations
     uint16_t *x = nullptr, *q = nullptr, *ctx = nullptr, *mid = nullptr, *xl = nullptr, *logits = nullptr;
+    uint16_t *hn = nullptr, *qkvb = nullptr;  // normalised rows / q|k|v rows of the tensor-core path
+    void *tc_ws = nullptr;                    // error flag | tile counters | split-K partials
+    size_t tc_ws_bytes = 0;
+    std::map<std::tuple<const void *, int, int>, CUtensorMap> maps;  // (buffer, rows, k)
     uint32_t *meta = nullptr;  // [4][R]: ids | slots | positions | logit rows
     uint32_t *tokens = nullptr, *slot_pos = nullptr;
     void *attn_ws = nullptr, *lm_ws = nullptr;
@@ -166,6 +174,14 @@ int allocate(qwen_b200 *h) {
         h->L[l].gu = h->L[l].o + (size_t)HID * HID;
         h->L[l].d = h->L[l].gu + (size_t)2 * FFN * HID;
     }
+    if ((rc = dalloc(h, &p, lw * NL))) return rc;
+    for (int l = 0; l < NL; ++l) {
+        int8_t *b = (int8_t *)p + lw * l;
+        h->L[l].tqkv = b;
+        h->L[l].to = b + (size_t)QKVN * HID;
+        h->L[l].tgu = h->L[l].to + (size_t)HID * HID;
+        h->L[l].td = h->L[l].tgu + (size_t)2 * FFN * HID;
+    }
     const size_t ls = QKVN + HID + 2 * FFN + HID;
     if ((rc = dalloc(h, &p, ls * NL * sizeof(float)))) return rc;
     for (int l = 0; l < NL; ++l) {
@@ -186,6 +202,7 @@ int allocate(qwen_b200 *h) {
     h->g_final = (uint16_t *)p + lb * NL;
     if ((rc = dalloc(h, (void **)&h->embed, (size_t)VOC * HID * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->lmw, (size_t)VOC * HID))) return rc;
+    if ((rc = dalloc(h, (void **)&h->tlmw, (size_t)VOC * HID))) return rc;
     if ((rc = dalloc(h, (void **)&h->s_lm, (size_t)VOC * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->rope, (size_t)c.max_context * 64 * 4))) return rc;
     // KV8 caches
@@ -203,6 +220,12 @@ int allocate(qwen_b200 *h) {
     if ((rc = dalloc(h, (void **)&h->ctx, R * HID * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->mid, R * FFN * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->xl, R * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->hn, R * HID * 2))) return rc;
+    if ((rc = dalloc(h, (void **)&h->qkvb, R * QKVN * 2))) return rc;
+    // worst case over the layer GEMMs: 8 splits of the widest (gate/up) output
+    h->tc_ws_bytes = tc_gemm_workspace(h->R, 2 * FFN, 8);
+    if ((rc = dalloc(h, &h->tc_ws, h->tc_ws_bytes))) return rc;
+    CK(cudaMemset(h->tc_ws, 0, h->tc_ws_bytes));
     if ((rc = dalloc(h, (void **)&h->logits, (size_t)VOC * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->meta, R * 4 * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->tokens, R * 4))) return rc;
@@ -223,7 +246,35 @@ int allocate(qwen_b200 *h) {
     return 0;
 }
 
+// Row-major [n][k] int8 -> [n/128][k/64][128][64] (tensor-core GEMM layout),
+// each group of four codes stored as (k0, k2, k1, k3) so that the dequant
+// produces the bf16 pairs (k0, k1), (k2, k3) without byte shuffles.
+void tile_weights(const int8_t *w, int n, int k, int8_t *t) {
+    const int kc = k / 64;
+    for (int nb = 0; nb < n / 128; ++nb)
+        for (int c = 0; c < kc; ++c)
+            for (int r = 0; r < 128; ++r) {
+                int8_t *dst = t + (((size_t)nb * kc + c) * 128 + r) * 64;
+                const int8_t *src = w + (size_t)(nb * 128 + r) * k + c * 64;
+                for (int g = 0; g < 64; g += 4) {
+                    dst[g] = src[g];
+                    dst[g + 1] = src[g + 2];
+                    dst[g + 2] = src[g + 1];
+                    dst[g + 3] = src[g + 3];
+                }
+            }
+}
+
+int upload_tiled(qwen_b200 *h, int8_t *dst, const int8_t *w, int n, int k, std::vector<int8_t> &tmp) {
+    tmp.resize((size_t)n * k);
+    tile_weights(w, n, k, tmp.data());
+    CK(cudaMemcpy(dst, tmp.data(), tmp.size(), cudaMemcpyHostToDevice));
+    return 0;
+}
+
 int upload(qwen_b200 *h, const qa_model &m) {
+    std::vector<int8_t> tiled;
+    int rc;
     std::vector<int8_t> gu((size_t)2 * FFN * HID), qkv((size_t)QKVN * HID);
     std::vector<float> s(QKVN + HID + 2 * FFN + HID);
     std::vector<uint16_t> b(QKVN + 2 * HID);
@@ -250,12 +301,17 @@ int upload(qwen_b200 *h, const qa_model &m) {
         CK(cudaMemcpy(W.o, m.w[l][QA_O], (size_t)HID * HID, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.gu, gu.data(), gu.size(), cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.d, m.w[l][QA_DOWN], (size_t)HID * FFN, cudaMemcpyHostToDevice));
+        if ((rc = upload_tiled(h, W.tqkv, qkv.data(), QKVN, HID, tiled))) return rc;
+        if ((rc = upload_tiled(h, W.to, m.w[l][QA_O], HID, HID, tiled))) return rc;
+        if ((rc = upload_tiled(h, W.tgu, gu.data(), 2 * FFN, HID, tiled))) return rc;
+        if ((rc = upload_tiled(h, W.td, m.w[l][QA_DOWN], HID, FFN, tiled))) return rc;
         CK(cudaMemcpy(W.s_qkv, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.bias, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
     }
     CK(cudaMemcpy(h->g_final, m.gamma + QA_GAMMA_FINAL, HID * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->embed, m.embed, (size_t)VOC * HID * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->lmw, m.lmw, (size_t)VOC * HID, cudaMemcpyHostToDevice));
+    if ((rc = upload_tiled(h, h->tlmw, m.lmw, VOC, HID, tiled))) return rc;
     std::vector<float> slm(VOC);
     for (int i = 0; i < VOC; ++i) slm[i] = qa_bf2f(m.scale[QA_SCALE_LM + i]);
     CK(cudaMemcpy(h->s_lm, slm.data(), (size_t)VOC * 4, cudaMemcpyHostToDevice));
@@ -265,6 +321,36 @@ int upload(qwen_b200 *h, const qa_model &m) {
 int ensure_device(qwen_b200 *h) {
     if (!h->loaded) return fail(h, QWEN_B200_EINVAL, "no assets loaded");
     CK(cudaSetDevice(h->cfg.device));
+    return 0;
+}
+
+const CUtensorMap *act_map(qwen_b200 *h, const uint16_t *buf, int rows, int k) {
+    const auto key = std::make_tuple((const void *)buf, rows, k);
+    auto it = h->maps.find(key);
+    if (it != h->maps.end()) return &it->second;
+    CUtensorMap m;
+    if (make_act_map(&m, buf, rows, k, tc_bn_for_rows(rows))) return nullptr;
+    return &(h->maps[key] = m);
+}
+
+// Tensor-core GEMM y = epi(x W^T) for n rows of buffer x [R][k].
+int tc_gemm(qwen_b200 *h, int epi, const uint16_t *x, int n, int k, const int8_t *wt, const float *scale,
+            const uint16_t *bias, int nout, uint16_t *y, const TcArgmax *am, cudaStream_t st) {
+    const CUtensorMap *map = act_map(h, x, n, k);
+    if (!map) return fail(h, QWEN_B200_EDEVICE, "cannot encode the activation tensor map");
+    const int splits = am ? 1 : tc_pick_splits(n, nout, k);
+    RK(launch_gemm_tc(epi, *map, n, k, wt, scale, bias, nout, y, splits, h->tc_ws, h->tc_ws_bytes, false, am, st));
+    return 0;
+}
+
+// Reads the error flag that tcgen05 kernels set when a bounded wait expires.
+int check_device_flags(qwen_b200 *h) {
+    unsigned flag = 0;
+    CK(cudaMemcpy(&flag, h->tc_ws, 4, cudaMemcpyDeviceToHost));
+    if (flag) {
+        cudaMemset(h->tc_ws, 0, 4);
+        return fail(h, QWEN_B200_ETIMEOUT, "a tensor-core pipeline wait timed out (code %u)", flag);
+    }
     return 0;
 }
 
@@ -305,7 +391,13 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         a.vs = vs;
         a.cap = cap;
         a.kv_out = dq ? dq + (size_t)n * 896 : nullptr;
-        {
+        if (n >= TC_MIN_ROWS) {
+            LaunchScope ls(h, 1, st, 3);
+            RK(launch_rmsnorm(h->x, W.g_attn, n, eps, h->hn, st));
+            int rc = tc_gemm(h, EPI_BIAS, h->hn, n, HID, W.tqkv, W.s_qkv, W.bias, QKVN, h->qkvb, nullptr, st);
+            if (rc) return rc;
+            RK(launch_rope_kv8(h->qkvb, n, slots, positions, h->rope, h->q, kc, ks, vc, vs, cap, a.kv_out, st));
+        } else {
             LaunchScope ls(h, 1, st, 1);
             RK(launch_qkv(a, st));
         }
@@ -320,14 +412,29 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         }
         {
             LaunchScope ls(h, 3, st, 1);
-            RK(launch_gemv(EPI_RESIDUAL, h->ctx, n, HID, nullptr, 0.f, W.o, W.s_o, nullptr, HID, h->x, st));
+            if (n >= TC_MIN_ROWS) {
+                int rc = tc_gemm(h, EPI_RESIDUAL, h->ctx, n, HID, W.to, W.s_o, nullptr, HID, h->x, nullptr, st);
+                if (rc) return rc;
+            } else {
+                RK(launch_gemv(EPI_RESIDUAL, h->ctx, n, HID, nullptr, 0.f, W.o, W.s_o, nullptr, HID, h->x, st));
+            }
         }
         if (dq) CK(cudaMemcpyAsync(dq + (size_t)n * 2048, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
-        {
-            LaunchScope ls(h, 4, st, 1);
-            RK(launch_gemv(EPI_SWIGLU, h->x, n, HID, W.g_ffn, eps, W.gu, W.s_gu, nullptr, 2 * FFN, h->mid, st));
-        }
-        {
+        if (n >= TC_MIN_ROWS) {
+            {
+                LaunchScope ls(h, 4, st, 2);
+                RK(launch_rmsnorm(h->x, W.g_ffn, n, eps, h->hn, st));
+                int rc = tc_gemm(h, EPI_SWIGLU, h->hn, n, HID, W.tgu, W.s_gu, nullptr, 2 * FFN, h->mid, nullptr, st);
+                if (rc) return rc;
+            }
+            LaunchScope ls(h, 5, st, 1);
+            int rc = tc_gemm(h, EPI_RESIDUAL, h->mid, n, FFN, W.td, W.s_d, nullptr, HID, h->x, nullptr, st);
+            if (rc) return rc;
+        } else {
+            {
+                LaunchScope ls(h, 4, st, 1);
+                RK(launch_gemv(EPI_SWIGLU, h->x, n, HID, W.g_ffn, eps, W.gu, W.s_gu, nullptr, 2 * FFN, h->mid, st));
+            }
             LaunchScope ls(h, 5, st, 1);
             RK(launch_gemv(EPI_RESIDUAL, h->mid, n, FFN, nullptr, 0.f, W.d, W.s_d, nullptr, HID, h->x, st));
         }
@@ -343,9 +450,23 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
             RK(launch_gather_rows(h->x, lrows, nlog, h->xl, st));
             xin = h->xl;
         }
-        LaunchScope ls(h, 6, st, 2);
-        RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw, h->s_lm, VOC, want_logits ? h->logits : nullptr,
-                          tokens_dst, h->lm_ws, h->lm_ws_bytes, st));
+        if (nlog >= TC_MIN_ROWS) {
+            LaunchScope ls(h, 6, st, 3);
+            RK(launch_rmsnorm(xin, h->g_final, nlog, eps, h->hn, st));
+            const int nblk = VOC / 128;
+            TcArgmax am;
+            am.pv = reinterpret_cast<float *>(h->lm_ws);
+            am.pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(h->lm_ws) + (size_t)nlog * nblk * 4);
+            am.nblk = nblk;
+            am.logits = want_logits ? h->logits : nullptr;
+            int rc = tc_gemm(h, EPI_ARGMAX, h->hn, nlog, HID, h->tlmw, h->s_lm, nullptr, VOC, nullptr, &am, st);
+            if (rc) return rc;
+            RK(launch_argmax_reduce(am.pv, am.pi, nlog, nblk, tokens_dst, st));
+        } else {
+            LaunchScope ls(h, 6, st, 2);
+            RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw, h->s_lm, VOC, want_logits ? h->logits : nullptr,
+                              tokens_dst, h->lm_ws, h->lm_ws_bytes, st));
+        }
     }
     return 0;
 }
@@ -579,6 +700,7 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
     }
     CK(cudaMemcpyAsync(h->h_tokens, h->tokens, 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+    if ((rc = check_device_flags(h))) return rc;
     if (logits) CK(cudaMemcpy(logits, h->logits, (size_t)VOC * 2, cudaMemcpyDeviceToHost));
     h->pos[slot] = position + rows;
     if ((rc = sync_slot_positions(h, st))) return rc;
@@ -614,6 +736,7 @@ int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *t
     if ((rc = run_forward(h, (int)n, (int)max_len, (int)n, true, false, h->tokens, st))) return rc;
     CK(cudaMemcpyAsync(h->h_tokens, h->tokens, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+    if ((rc = check_device_flags(h))) return rc;
     for (uint32_t i = 0; i < n; ++i) {
         h->pos[slots[i]] += 1;
         tokens_out[i] = h->h_tokens[i];
@@ -901,6 +1024,29 @@ int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma,
     if (!x || !w_gu || !s_gu || !mid) return QWEN_B200_EINVAL;
     return launch_gemv(EPI_SWIGLU, x, (int)rows, HID, gamma, eps, w_gu, s_gu, nullptr, 2 * FFN, mid,
                        (cudaStream_t)stream);
+}
+
+int qwen_b200_tile_weights(const int8_t *w, uint32_t n, uint32_t k, int8_t *tiled) {
+    if (!w || !tiled || n % 128 || k % 64 || !n || !k) return QWEN_B200_EINVAL;
+    tile_weights(w, (int)n, (int)k, tiled);
+    return QWEN_B200_OK;
+}
+
+size_t qwen_b200_gemm_tc_workspace(uint32_t rows, uint32_t n, uint32_t k) {
+    return tc_gemm_workspace((int)rows, (int)n, tc_pick_splits((int)rows, (int)n, (int)k));
+}
+
+int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w_tiled,
+                               const float *scale, uint32_t n, const uint16_t *bias, int epi, uint16_t *y,
+                               void *workspace, size_t workspace_bytes, void *stream) {
+    if (!x || !w_tiled || !scale || !y || !workspace || epi < EPI_PLAIN || epi > EPI_SWIGLU) return QWEN_B200_EINVAL;
+    if (epi == EPI_BIAS && !bias) return QWEN_B200_EINVAL;
+    CUtensorMap map;
+    if (make_act_map(&map, x, (int)rows, (int)k, tc_bn_for_rows((int)rows))) return QWEN_B200_EINVAL;
+    const int splits = tc_pick_splits((int)rows, (int)n, (int)k);
+    int rc = launch_gemm_tc(epi, map, (int)rows, (int)k, w_tiled, scale, bias, (int)n, y, splits, workspace,
+                            workspace_bytes, true, nullptr, (cudaStream_t)stream);
+    return rc;
 }
 
 size_t qwen_b200_lm_head_workspace(uint32_t rows, uint32_t vocab) { return lm_head_workspace((int)rows, (int)vocab); }

@@ -9,6 +9,7 @@
 // from a sequential sum (per lane in k order, then a fixed butterfly).
 #include "common.cuh"
 #include "kernels.h"
+#include "qkv_epi.cuh"
 
 namespace qb {
 
@@ -237,43 +238,8 @@ __global__ void __launch_bounds__(256) qkv_kernel(QkvArgs a) {
     __syncthreads();
     if (warp >= mrows) return;
     const int row = m0 + warp;
-    const uint32_t pos = a.positions[row];
-    float lo = outs[warp][lane], hi = outs[warp][lane + 32];
-    if (hb < QB_QH + QB_KVH) {
-        // model_backend.py:73-78: y = x*cos + cat(-x[32:], x[:32])*sin, no FMA.
-        const float *cs = a.table + (size_t)pos * 64;
-        const float c = cs[lane], s = cs[32 + lane];
-        const float nlo = rbf(__fadd_rn(__fmul_rn(lo, c), __fmul_rn(-hi, s)));
-        const float nhi = rbf(__fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, s)));
-        lo = nlo;
-        hi = nhi;
-    }
-    if (hb < QB_QH) {
-        uint16_t *q = a.q_out + (size_t)row * QB_HID + hb * 64;
-        q[lane] = f2bf(lo);
-        q[lane + 32] = f2bf(hi);
-        return;
-    }
-    const bool isv = hb >= QB_QH + QB_KVH;
-    const int g = (hb - QB_QH) & 1;
-    if (a.kv_out) {
-        uint16_t *o = a.kv_out + (size_t)row * 256 + (isv ? 128 : 0) + g * 64;
-        o[lane] = f2bf(lo);
-        o[lane + 32] = f2bf(hi);
-    }
-    // KV8: scale = amax/127, code = clamp(rne(x / scale), +-127); zero vector -> 0.
-    const float amax = warp_max(fmaxf(fabsf(lo), fabsf(hi)));
-    const float s = __fdiv_rn(amax, 127.0f);
-    int clo = 0, chi = 0;
-    if (s > 0.f) {
-        clo = (int)fminf(fmaxf(rintf(__fdiv_rn(lo, s)), -127.f), 127.f);
-        chi = (int)fminf(fmaxf(rintf(__fdiv_rn(hi, s)), -127.f), 127.f);
-    }
-    const size_t base = ((size_t)a.slots[row] * 2 + g) * a.cap + pos;
-    int8_t *codes = (isv ? a.vc : a.kc) + base * 64;
-    codes[lane] = (int8_t)clo;
-    codes[lane + 32] = (int8_t)chi;
-    if (lane == 0) (isv ? a.vs : a.ks)[base] = s;
+    qkv_head_epilogue(outs[warp][lane], outs[warp][lane + 32], row, hb, a.slots[row], a.positions[row], a.table,
+                      a.q_out, a.kc, a.ks, a.vc, a.vs, a.cap, a.kv_out);
 }
 
 template <int MT>
@@ -381,6 +347,11 @@ __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float *pv, con
         __syncthreads();
     }
     if (threadIdx.x == 0) tokens[row] = si[0];
+}
+
+int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st) {
+    argmax_reduce_kernel<<<rows, 256, 0, st>>>(pv, pi, nblk, tokens);
+    return QB_LAUNCH_CHECK();
 }
 
 size_t lm_head_workspace(int rows, int vocab) {

@@ -1,13 +1,14 @@
 // Host-side launchers of the sm_100a kernels. Every launcher enqueues on the
 // given stream and returns 0 or a QWEN_B200_* status (-1 bad shape, -3 CUDA).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
 namespace qb {
 
-enum Epi { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3 };
+enum Epi { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
 
 // y = epi(bf16(bf16(norm?(x) W^T) * scale)); W int8 row-major [n][k].
 // EPI_SWIGLU: W holds interleaved gate/up rows, y is [rows][n/2].
@@ -63,5 +64,45 @@ int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
 // Seeded synthetic KV8 contents for positions [0, length) of one slot, all layers.
 int launch_fill_kv(int8_t *kc, float *ks, int8_t *vc, float *vs, int layers, int nslots, int slot, int cap,
                    int length, uint64_t seed, cudaStream_t st);
+
+// ---- tcgen05 W8A16 GEMM (rows > 8). Weights in the tiled layout
+// [n/128][k/64][128][64] int8 (16-byte coalesced loads per dequant thread).
+struct TcArgs {
+    const int8_t *w;
+    const float *scale;
+    const uint16_t *bias;
+    uint16_t *y;
+    int M, N, K, Mpad, kc_per_split, splits;
+    float *part;
+    unsigned *counters;
+    unsigned *err;
+    float *pv;
+    uint32_t *pi;
+    int nblk;
+    uint16_t *logits;
+};
+struct TcArgmax {
+    float *pv;
+    uint32_t *pi;
+    int nblk;         // = n / 128 partial candidates per row
+    uint16_t *logits; // nullable [rows][n]
+};
+// Tensor map of an activation matrix [rows][K] bf16 for the GEMM's B operand.
+int make_act_map(CUtensorMap *map, const uint16_t *x, int rows, int K, int BN);
+int tc_bn_for_rows(int rows);
+int tc_pick_splits(int rows, int n, int k);
+// Workspace: [256 B error flag][tile counters][split partials]; the flag and
+// counters must be zero before the first launch and are left zero (clear
+// zeroes them first).
+size_t tc_gemm_workspace(int rows, int n, int splits);
+int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8_t *w_tiled, const float *scale,
+                   const uint16_t *bias, int n, uint16_t *y, int splits, void *ws, size_t ws_bytes, bool clear,
+                   const TcArgmax *am, cudaStream_t st);
+int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st);
+// RoPE + KV8 append for the q|k|v rows produced by the tensor-core QKV GEMM
+// (qkv [rows][1152], bias already added).
+int launch_rope_kv8(const uint16_t *qkv, int rows, const uint32_t *slots, const uint32_t *positions,
+                    const float *table, uint16_t *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs, int cap,
+                    uint16_t *kv_out, cudaStream_t st);
 
 }  // namespace qb

@@ -3,6 +3,7 @@
 // bookkeeping and the seeded synthetic KV fill used to set up long contexts.
 #include "common.cuh"
 #include "kernels.h"
+#include "qkv_epi.cuh"
 
 namespace qb {
 
@@ -103,6 +104,30 @@ int launch_kv8_append(const uint16_t *kv, int rows, const uint32_t *slots, const
     if (rows <= 0 || cap <= 0) return -1;
     const int items = rows * QB_KVH;
     kv8_append_kernel<<<(items + 7) / 8, 256, 0, st>>>(kv, rows, slots, positions, codes, scales, cap);
+    return QB_LAUNCH_CHECK();
+}
+
+// q|k|v rows after the tensor-core projection: one warp per (row, head block).
+__global__ void rope_kv8_kernel(const uint16_t *__restrict__ qkv, int rows, const uint32_t *__restrict__ slots,
+                                const uint32_t *__restrict__ positions, const float *__restrict__ table,
+                                uint16_t *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs, int cap,
+                                uint16_t *kv_out) {
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    constexpr int HB = QB_QH + 2 * QB_KVH;
+    if (item >= rows * HB) return;
+    const int row = item / HB, hb = item % HB;
+    const uint16_t *src = qkv + (size_t)row * QB_QKV + hb * 64;
+    qkv_head_epilogue(bf2f(src[lane]), bf2f(src[lane + 32]), row, hb, slots[row], positions[row], table, q_out, kc,
+                      ks, vc, vs, cap, kv_out);
+}
+
+int launch_rope_kv8(const uint16_t *qkv, int rows, const uint32_t *slots, const uint32_t *positions,
+                    const float *table, uint16_t *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs, int cap,
+                    uint16_t *kv_out, cudaStream_t st) {
+    if (rows <= 0) return -1;
+    const int items = rows * (QB_QH + 2 * QB_KVH);
+    rope_kv8_kernel<<<(items + 7) / 8, 256, 0, st>>>(qkv, rows, slots, positions, table, q_out, kc, ks, vc, vs, cap,
+                                                     kv_out);
     return QB_LAUNCH_CHECK();
 }
 

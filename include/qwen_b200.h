@@ -163,6 +163,18 @@ int qwen_b200_op_gemm_w8a16(const uint16_t *x, uint32_t rows, uint32_t k, const 
  * (model_backend.py:103,107). */
 int qwen_b200_op_gemm_w8a16_residual(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
                                      const float *scale, uint32_t n, uint16_t *y, void *stream);
+/* Tensor-core (tcgen05) form of the same GEMM for rows > 8: host helper that
+ * re-tiles a row-major int8 weight [n][k] into [n/128][k/64][128][64] with
+ * each group of four codes stored as (k0, k2, k1, k3) (n % 128 == 0,
+ * k % 64 == 0), the workspace size, and the launch. epi: 0
+ * plain, 1 + bias, 2 residual (y in/out), 3 SiLU(gate)*up over interleaved
+ * gate/up rows (y [rows][n/2]). The first 4 workspace bytes become non-zero if
+ * a bounded pipeline wait expired. */
+int qwen_b200_tile_weights(const int8_t *w, uint32_t n, uint32_t k, int8_t *tiled);
+size_t qwen_b200_gemm_tc_workspace(uint32_t rows, uint32_t n, uint32_t k);
+int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w_tiled,
+                               const float *scale, uint32_t n, const uint16_t *bias, int epi, uint16_t *y,
+                               void *workspace, size_t workspace_bytes, void *stream);
 /* Host-side cos/sin table [positions][64] (cos 0..31, sin 32..63) for
  * theta_i = 1e6^(-2i/64) (model_backend.py:41). */
 void qwen_b200_rope_table(uint32_t positions, float *table);

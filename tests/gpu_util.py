@@ -72,9 +72,11 @@ def ulp_bf16(x):
     return np.exp2(e - 7)
 
 
-def assert_bf16_close(got, exp, min_equal=0.99, max_ulps=1.0, what=''):
+def assert_bf16_close(got, exp, min_equal=0.99, max_ulps=1.0, what='', mag=None):
     """Bound for bf16 outputs whose fp32 pre-rounding values differ only by
-    summation order: nearly all equal, the rest within max_ulps bf16 ulps."""
+    summation order: nearly all equal, the rest within max_ulps bf16 ulps.
+    `mag` (optional, same shape) is an intermediate whose ulp also counts, e.g.
+    the linear term of a residual sum that can cancel against the residual."""
     got = np.asarray(got, np.float32).ravel()
     exp = np.asarray(exp, np.float32).ravel()
     assert got.shape == exp.shape, what
@@ -83,7 +85,10 @@ def assert_bf16_close(got, exp, min_equal=0.99, max_ulps=1.0, what=''):
     diff = np.abs(got.astype(np.float64) - exp)
     # plus a floor at 2^-12 of the tensor's scale for outputs that are sums
     # with cancellation (tiny results whose own ulp is below fp32 noise)
-    bound = max_ulps * ulp_bf16(np.maximum(np.abs(got), np.abs(exp))) + 2.0 ** -12 * float(np.abs(exp).max()) + 1e-30
+    ref_mag = np.maximum(np.abs(got), np.abs(exp))
+    if mag is not None:
+        ref_mag = np.maximum(ref_mag, np.abs(np.asarray(mag, np.float32).ravel()))
+    bound = max_ulps * ulp_bf16(ref_mag) + 2.0 ** -12 * float(np.abs(exp).max()) + 1e-30
     worst = float((diff / bound).max())
     assert eq >= min_equal, f'{what}: only {eq:.4f} bit-equal'
     assert worst <= 1.0, f'{what}: max difference {worst:.2f} x {max_ulps} ulp'

@@ -116,3 +116,15 @@ def test_rope_table_matches_oracle():
     t = np.empty((300, 64), np.float32)
     qwen_b200.lib().qwen_b200_rope_table(300, t.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
     assert np.array_equal(t, ref.rope_table(300))
+
+
+def test_weight_tiling_layout():
+    import numpy as np
+    w = np.arange(256 * 128, dtype=np.int64).astype(np.int8).reshape(256, 128)
+    t = np.empty_like(w)
+    L = qwen_b200.lib()
+    assert L.qwen_b200_tile_weights(w.ctypes.data_as(ctypes.c_void_p), 256, 128, t.ctypes.data_as(ctypes.c_void_p)) == 0
+    exp = w.reshape(2, 128, 2, 16, 4).transpose(0, 2, 1, 3, 4)[..., [0, 2, 1, 3]]
+    assert np.array_equal(t.reshape(2, 2, 128, 16, 4), exp)
+    assert L.qwen_b200_tile_weights(w.ctypes.data_as(ctypes.c_void_p), 200, 128, t.ctypes.data_as(ctypes.c_void_p)) \
+        == _lib.EINVAL

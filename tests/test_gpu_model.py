@@ -160,7 +160,10 @@ def test_small_capacity_engine_matches_oracle(sd_root, oracle_kv8, golden):
     assert g_toks == o_toks
 
 
-def test_chunked_prefill_equals_single_chunk(sd_root, golden):
+def test_chunked_prefill_matches_single_chunk(sd_root, golden):
+    """A 16-token prompt as chunks of 5 rows (GEMV path, rows <= 8) against one
+    chunk of 16 rows (tensor-core path): the two paths sum in different orders,
+    so the bar is the token and the logits tolerance, not bit equality."""
     e = qwen_b200.Engine(device=0, max_seqs=1, max_context=64, max_rows=5).load_assets(sd_root)
     try:
         tok, logits = e.forward(0, golden['prompt'], 0, want_logits=True)
@@ -172,7 +175,9 @@ def test_chunked_prefill_equals_single_chunk(sd_root, golden):
     finally:
         e2.close()
     assert tok == tok2
-    assert np.array_equal(logits, logits2)
+    a, b = from_bits(logits), from_bits(logits2)
+    assert np.abs(a - b).max() <= 2e-2 * float(b.max() - b.min())
+    assert (a == b).mean() > 0.9
 
 
 def test_device_decode_graph_equals_host_decode(engine, golden):

@@ -4,8 +4,9 @@ given-operand checks (legacy_.../tests/compare_all_layers.py:31-57).
 
 Bars: integer / index work (KV8 codes and scales, embedding rows, RoPE with
 the shared table, greedy token ids) bit-exact; bf16 outputs of fp32
-reductions >= 99 % bit-equal and otherwise within one bf16 ulp (two for
-attention, whose softmax exp/sum and P.V orders differ).
+reductions >= 99 % bit-equal and otherwise within two bf16 ulps (the
+epilogues round twice, e.g. bf16(bf16(acc) * scale), so a one-ulp flip of the
+inner value can move the output by two).
 """
 import ctypes
 
@@ -79,12 +80,16 @@ def test_gemm_w8a16(k, n, rows, epi):
         assert L().qwen_b200_op_gemm_w8a16(*args, bias, vp(yd), stream()) == 0
     sync()
     got = from_bits(host(yd).view(np.uint16))
+    lin = None
     if epi == 'residual':
-        exp = ref.f32(np.vectorize(lambda a: ref.lib().ref_bf(a, 0))(y0 + ref.linear(x, w, s)))
+        lin = ref.linear(x, w, s)
+        exp = ref.f32(np.vectorize(lambda a: ref.lib().ref_bf(a, 0))(y0 + lin))
     else:
         exp = ref.linear(x, w, s, bias=b if epi == 'bias' else None)
-    # bias / residual add a second bf16 rounding after the scaled product
-    assert_bf16_close(got, exp, max_ulps=1 if epi == 'plain' else 2, what=f'gemm {k}x{n} rows {rows} {epi}')
+    # residual: a third rounding after a sum that may cancel -> 3 ulps of the
+    # larger of the output and the added linear term
+    assert_bf16_close(got, exp, max_ulps=3 if epi == 'residual' else 2, mag=lin,
+                      what=f'gemm {k}x{n} rows {rows} {epi}')
 
 
 @pytest.mark.parametrize('rows', [1, 5, 16])
@@ -105,7 +110,7 @@ def test_swiglu(rows):
     sync()
     z = ref.rmsnorm(x, g)
     exp = ref.swiglu(ref.linear(z, wg, sg), ref.linear(z, wu, su))
-    assert_bf16_close(from_bits(host(mid).view(np.uint16)), exp, what='swiglu')
+    assert_bf16_close(from_bits(host(mid).view(np.uint16)), exp, max_ulps=2, what='swiglu')
 
 
 def rope_table(positions):
