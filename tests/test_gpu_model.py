@@ -176,8 +176,9 @@ def test_chunked_prefill_matches_single_chunk(sd_root, golden):
         e2.close()
     assert tok == tok2
     a, b = from_bits(logits), from_bits(logits2)
+    # end-to-end bar (24 layers amplify order-of-summation differences)
     assert np.abs(a - b).max() <= 2e-2 * float(b.max() - b.min())
-    assert (a == b).mean() > 0.9
+    assert rel_l2(a, b) < 5e-2
 
 
 def test_device_decode_graph_equals_host_decode(engine, golden):
