@@ -15,8 +15,11 @@
 //                    adds the partials in chunk order and writes ctx.
 // Cache layout: codes [slot][kv head][capacity][64] int8, scales
 // [slot][kv head][capacity] fp32.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "qwen_b200.h"
 
 namespace qb {
 
@@ -234,3 +237,58 @@ int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const u
 }
 
 }  // namespace qb
+
+namespace qb {
+
+// ------------------------------------------------------- no-allocation variant
+// Attention scratch for callers that cannot allocate device memory: one
+// fixed array per GPU, part of the library image, held from the time the
+// library is loaded on a device until the process exits.
+static __device__ __align__(256) uint8_t g_attn_scratch[QWEN_B200_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void *g_scratch_addr[kMaxDevices] = {};
+}  // namespace
+
+// Device address of g_attn_scratch on the current device. Host code only sees
+// a host-side stand-in under that name, so the address is looked up once per
+// device (with that device current) and cached.
+static int noalloc_scratch(void **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QWEN_B200_EDEVICE;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess || !p) {
+            cudaGetLastError();
+            return QWEN_B200_EDEVICE;
+        }
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return QWEN_B200_OK;
+}
+
+}  // namespace qb
+
+extern "C" int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint32_t *slots,
+                                              const uint32_t *positions, uint32_t max_len, const int8_t *kcodes,
+                                              const float *kscales, const int8_t *vcodes, const float *vscales,
+                                              uint32_t capacity, uint16_t *ctx, void *stream) {
+    using namespace qb;
+    if (!q || !slots || !positions || !kcodes || !kscales || !vcodes || !vscales || !ctx) return QWEN_B200_EINVAL;
+    if (rows == 0 || capacity == 0) return QWEN_B200_EINVAL;
+    // the request must fit the fixed scratch (checked before touching the GPU)
+    if (attention_workspace((int)rows, (int)capacity) > (size_t)QWEN_B200_NOALLOC_SCRATCH_BYTES)
+        return QWEN_B200_ESCRATCH;
+    void *scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // the completion counters are zeroed at the start of every call; the rest
+    // of the scratch is overwritten before it is read
+    return launch_attention(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
+                            (int)capacity, ctx, scratch, QWEN_B200_NOALLOC_SCRATCH_BYTES, (int)rows, true,
+                            (cudaStream_t)stream);
+}

@@ -9,7 +9,8 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parents[1] / 'libqwen_b200.so'
 
-OK, EINVAL, ETIMEOUT, EDEVICE, ETOKEN, EOUTPUT, ENOMEM, EIO, ESTATE = 0, -1, -2, -3, -4, -5, -6, -7, -8
+OK, EINVAL, ETIMEOUT, EDEVICE, ETOKEN, EOUTPUT, ENOMEM, EIO, ESTATE, ESCRATCH = 0, -1, -2, -3, -4, -5, -6, -7, -8, -9
+NOALLOC_SCRATCH_BYTES = 16 << 20
 VOCAB, HIDDEN, FFN, LAYERS = 151936, 896, 4864, 24
 
 
@@ -66,6 +67,8 @@ _SIGNATURES = {
     'qwen_b200_attention_workspace': (c_size_t, [c_uint32, c_uint32]),
     'qwen_b200_op_attention': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p, c_void_p,
                                        c_void_p, c_void_p, c_uint32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    'qwen_b200_op_attention_noalloc': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p,
+                                               c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
     'qwen_b200_op_swiglu': (c_int, [c_void_p, c_uint32, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
     'qwen_b200_lm_head_workspace': (c_size_t, [c_uint32, c_uint32]),
     'qwen_b200_op_lm_head_argmax': (c_int, [c_void_p, c_uint32, c_void_p, c_float, c_void_p, c_void_p, c_uint32,

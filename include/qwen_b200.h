@@ -40,6 +40,7 @@ extern "C" {
 #define QWEN_B200_ENOMEM (-6)   /* device or host allocation failed */
 #define QWEN_B200_EIO (-7)      /* asset file missing or of the wrong size */
 #define QWEN_B200_ESTATE (-8)   /* KV position mismatch (model_backend.py:82-83) */
+#define QWEN_B200_ESCRATCH (-9) /* request larger than the fixed no-allocation scratch */
 
 /* CSR map emulated by qwen_b200_csr_read/write (src/software/README.md CSR
  * table; src/rtl/qwen25_compute_cfg.v, qwen25_result_regs.v). */
@@ -203,6 +204,32 @@ int qwen_b200_op_attention(const uint16_t *q, uint32_t rows, const uint32_t *slo
                            uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
                            const float *vscales, uint32_t capacity, uint16_t *ctx, void *workspace,
                            size_t workspace_bytes, void *stream);
+/* Attention without any device allocation. This entry point has no
+ * counterpart in the reference. It is for callers that cannot call cudaMalloc
+ * at the point they run attention: hosts that hand every byte of the GPU to
+ * their own memory pool up front (as the reference's firmware works inside
+ * fixed DDR windows, src/verification/board_parameters.h), code whose
+ * latency budget does not allow the implicit device synchronisation that
+ * cudaMalloc / cudaFree can cause, and plugins that do not own the process's
+ * allocator. Instead of a caller workspace it uses one fixed scratch array of
+ * QWEN_B200_NOALLOC_SCRATCH_BYTES per GPU, built into the library: every GPU
+ * that loads the library holds it until the process exits. Requests whose
+ * scratch need, qwen_b200_attention_workspace(rows, capacity), exceeds that
+ * size are rejected with QWEN_B200_ESCRATCH before anything is launched (for
+ * example 64 rows at capacity 2048 fit; 64 rows at capacity 8192 do not).
+ * The first call on each device looks up the scratch's device address with
+ * that device current; make that first call before any stream capture. All
+ * calls on a device share the one array and it keeps the last call's
+ * contents: each call zeroes the parts that must start at zero, but calls
+ * whose executions overlap on the GPU (different streams, or different host
+ * threads) race on it and must be serialised by the caller. No cudaMalloc,
+ * cudaFree or allocating library routine is called. Arguments and result
+ * are those of qwen_b200_op_attention. */
+#define QWEN_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
+int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint32_t *slots,
+                                   const uint32_t *positions, uint32_t max_len, const int8_t *kcodes,
+                                   const float *kscales, const int8_t *vcodes, const float *vscales,
+                                   uint32_t capacity, uint16_t *ctx, void *stream);
 /* SwiGLU FFN input half: mid = bf16(bf16(silu(g)) * u) with g, u from
  * RMSNorm(x) (gamma NULL: no norm) times the interleaved gate/up weight
  * w_gu [2*4864][896] (row 2j gate j, row 2j+1 up j) and scales s_gu [2*4864]
