@@ -14,9 +14,11 @@
 //               (tcgen05.ld of the accumulator, per-channel scale, bf16
 //               rounding points of model_backend.py:62-67, bias / residual /
 //               SiLU*mul / LM-head argmax)
-// Split-K: CTAs of one output tile write fp32 partials; the last one to
-// finish (atomic ticket) adds them in split order and runs the epilogue, so
-// results do not depend on scheduling.
+// Split-K: the CTAs of one output tile form a thread-block cluster. Each
+// writes its fp32 partial tile to its own shared memory; after a cluster
+// barrier every CTA reduces its share of the tile (32x32 units) by reading the
+// partials of all CTAs over distributed shared memory in rank order and runs
+// the epilogue on it. No global scratch, no atomics, deterministic.
 // Every mbarrier wait is bounded: on timeout the kernel records an error code
 // in a device flag, skips its remaining work and still frees its TMEM.
 #include "common.cuh"
@@ -32,7 +34,6 @@ constexpr int TC_WSTAGES = 8;  // int8 weight tiles in flight
 constexpr int TC_CONV = 256;                 // dequant / epilogue threads (warps 2..9)
 constexpr int TC_THREADS = 64 + TC_CONV;
 constexpr int TC_MAX_SPLITS = 8;
-constexpr size_t TC_COUNTERS = 16384;  // tile counters (fixed region: layouts never overlap)
 
 template <int BN>
 struct TcSmem {
@@ -79,6 +80,80 @@ __device__ __forceinline__ void codes4_to_bf16(uint32_t w, uint32_t &k01, uint32
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// Epilogue of 32 accumulators of output channel n: columns c0..c0+31 of the
+// tile (batch rows m0 + c0 + j). Residual rows are read before any write.
+template <int BN, int EPI>
+__device__ __forceinline__ void tc_epilogue32(const TcArgs &a, const float (&v)[32], int n, int m0, int c0, int q,
+                                              int lane, uint8_t *red) {
+    const float sc = a.scale[n];
+    float res[32];
+    if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c0 + j;
+            res[j] = m < a.M ? bf2f(a.y[(size_t)m * a.N + n]) : 0.f;
+        }
+    }
+    float bias = 0.f;
+    if constexpr (EPI == EPI_BIAS) bias = bf2f(a.bias[n]);
+    float *red_v = reinterpret_cast<float *>(red);
+    uint32_t *red_i = reinterpret_cast<uint32_t *>(red + 4 * BN * 4);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int cj = c0 + j, m = m0 + cj;
+        const bool valid = m < a.M;
+        float val = rbf(rbf(v[j]) * sc);
+        if constexpr (EPI == EPI_SWIGLU) {
+            // rows 2j (gate) and 2j+1 (up) sit in adjacent lanes
+            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+            if (valid && !(lane & 1)) {
+                const float sl = val / (1.0f + expf(-val));
+                a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = f2bf(rbf(sl) * other);
+            }
+        } else if constexpr (EPI == EPI_ARGMAX) {
+            if (valid && a.logits) a.logits[(size_t)m * a.N + n] = f2bf(val);
+            float bv = valid ? val : -INFINITY;
+            uint32_t bi = (uint32_t)n;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (better(ov, oi, bv, bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (lane == 0) {
+                red_v[q * BN + cj] = bv;
+                red_i[q * BN + cj] = bi;
+            }
+        } else if (valid) {
+            if (EPI == EPI_BIAS) val = rbf(val + bias);
+            if (EPI == EPI_RESIDUAL) val = rbf(res[j] + val);
+            a.y[(size_t)m * a.N + n] = f2bf(val);
+        }
+    }
+}
+
+// Best (value, index) per batch row over the tile's four lane quarters.
+template <int BN>
+__device__ __forceinline__ void tc_argmax_flush(const TcArgs &a, const uint8_t *red, int m0, int n_tile, int ct) {
+    const float *red_v = reinterpret_cast<const float *>(red);
+    const uint32_t *red_i = reinterpret_cast<const uint32_t *>(red + 4 * BN * 4);
+    for (int m = ct; m < BN; m += TC_CONV) {
+        if (m0 + m >= a.M) continue;
+        float bv = red_v[m];
+        uint32_t bi = red_i[m];
+        for (int qq = 1; qq < 4; ++qq)
+            if (better(red_v[qq * BN + m], red_i[qq * BN + m], bv, bi)) {
+                bv = red_v[qq * BN + m];
+                bi = red_i[qq * BN + m];
+            }
+        a.pv[(size_t)(m0 + m) * a.nblk + n_tile] = bv;
+        a.pi[(size_t)(m0 + m) * a.nblk + n_tile] = bi;
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
     using L = TcSmem<BN>;
@@ -90,7 +165,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     uint64_t *accum = w_empty + TC_WSTAGES, *done = accum + 1;
     uint32_t *slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_tile = blockIdx.x, split = blockIdx.y, m_tile = blockIdx.z;
+    const int split = a.splits > 1 ? (int)tc::cluster_rank() : 0;
+    const int n_tile = blockIdx.x / a.splits, m_tile = blockIdx.z;
     const int n0 = n_tile * TC_BM, m0 = m_tile * BN;
     const int KC = a.K / TC_BK;
     const int kc0 = split * a.kc_per_split;
@@ -215,18 +291,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         // ---------------- epilogue: this thread owns output channel n and
         // half of the tile's columns (two warps per TMEM lane quarter)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const int n = n0 + q * 32 + lane;
         constexpr int HALF = BN / 2;
         const int cbeg = ((warp - 2) >> 2) * HALF;
         ok = ok && tc::mbar_wait(accum, 0, a.err, 6);
         tc::tc_fence_after();
-        float *red_v = reinterpret_cast<float *>(smem + L::RED_OFF);
-        uint32_t *red_i = reinterpret_cast<uint32_t *>(smem + L::RED_OFF + 4 * BN * 4);
-        __shared__ unsigned ticket;
-        bool last = true;
-        // partials [split][n][Mpad] fp32: each thread's columns are contiguous
-        float *mypart = a.part + ((size_t)split * a.N + n) * a.Mpad + m0;
         if (a.splits > 1) {
+            // this warp's 32 x HALF block of the fp32 partial tile -> own shared
+            // memory (the A stages are free once the accumulator is complete),
+            // 16-byte groups rotated by lane to spread shared-memory banks
+            float *part = reinterpret_cast<float *>(smem + L::A_OFF);
+            const int unit = ((warp - 2) >> 2) * 4 + q;  // half * 4 + lane quarter
+#pragma unroll 1
+            for (int c = 0; c < HALF; c += 32) {
+                float v[32];
+                if (ok) {
+                    tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cbeg + c), v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+                }
+                float *row = part + ((size_t)(unit * 32 + lane) * HALF + c);
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    *reinterpret_cast<float4 *>(row + 4 * ((g + lane) & 7)) =
+                        make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+            }
+        } else {
+            const int n = n0 + q * 32 + lane;
 #pragma unroll 1
             for (int c = cbeg; c < cbeg + HALF; c += 32) {
                 float v[32];
@@ -236,114 +327,54 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = 0.f;
                 }
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4 *>(mypart + c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            }
-            __threadfence();
-            epi_bar();
-            if (ct == 0) ticket = atomicAdd(&a.counters[m_tile * gridDim.x + n_tile], 1u);
-            epi_bar();
-            last = ticket == (unsigned)(a.splits - 1);
-            if (last) __threadfence();
-        }
-        if (last) {
-            const float sc = a.scale[n];
-            // epilogue of one accumulator: column cj of the tile (batch row m0 + cj)
-            auto emit = [&](float accv, int cj) {
-                const int m = m0 + cj;
-                const bool valid = m < a.M;
-                float val = rbf(rbf(accv) * sc);
-                if constexpr (EPI == EPI_SWIGLU) {
-                    // rows 2j (gate) and 2j+1 (up) sit in adjacent lanes
-                    const float other = __shfl_xor_sync(0xffffffffu, val, 1);
-                    if (valid && !(lane & 1)) {
-                        const float sl = val / (1.0f + expf(-val));
-                        a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = f2bf(rbf(sl) * other);
-                    }
-                } else if constexpr (EPI == EPI_ARGMAX) {
-                    if (valid && a.logits) a.logits[(size_t)m * a.N + n] = f2bf(val);
-                    float bv = valid ? val : -INFINITY;
-                    uint32_t bi = (uint32_t)n;
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                        if (better(ov, oi, bv, bi)) {
-                            bv = ov;
-                            bi = oi;
-                        }
-                    }
-                    if (lane == 0) {
-                        red_v[q * BN + cj] = bv;
-                        red_i[q * BN + cj] = bi;
-                    }
-                } else {
-                    if (valid) {
-                        uint16_t *yp = a.y + (size_t)m * a.N + n;
-                        if (EPI == EPI_BIAS) val = rbf(val + bf2f(a.bias[n]));
-                        if (EPI == EPI_RESIDUAL) val = rbf(bf2f(*yp) + val);
-                        *yp = f2bf(val);
-                    }
-                }
-            };
-            if (a.splits > 1) {
-                // every partial of four columns is requested before the
-                // additions, which then run in split order
-                const float *p0 = a.part + (size_t)n * a.Mpad + m0;
-                const size_t sstride = (size_t)a.N * a.Mpad;
-#pragma unroll 2
-                for (int cj = cbeg; cj < cbeg + HALF; cj += 4) {
-                    float4 pv8[TC_MAX_SPLITS];
-#pragma unroll
-                    for (int sp = 0; sp < TC_MAX_SPLITS; ++sp)
-                        pv8[sp] = sp < a.splits ? __ldcg(reinterpret_cast<const float4 *>(p0 + sp * sstride + cj))
-                                                : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                    for (int sp = 0; sp < TC_MAX_SPLITS; ++sp)
-                        if (sp < a.splits) {
-                            acc.x += pv8[sp].x;
-                            acc.y += pv8[sp].y;
-                            acc.z += pv8[sp].z;
-                            acc.w += pv8[sp].w;
-                        }
-                    emit(acc.x, cj);
-                    emit(acc.y, cj + 1);
-                    emit(acc.z, cj + 2);
-                    emit(acc.w, cj + 3);
-                }
-            } else {
-#pragma unroll 1
-                for (int c = cbeg; c < cbeg + HALF; c += 32) {
-                    float v[32];
-                    if (ok) {
-                        tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) emit(v[j], c + j);
-                }
+                tc_epilogue32<BN, EPI>(a, v, n, m0, c, q, lane, smem + L::RED_OFF);
             }
             if constexpr (EPI == EPI_ARGMAX) {
                 epi_bar();
-                for (int m = ct; m < BN; m += TC_CONV) {
-                    if (m0 + m >= a.M) continue;
-                    float bv = red_v[m];
-                    uint32_t bi = red_i[m];
-                    for (int qq = 1; qq < 4; ++qq)
-                        if (better(red_v[qq * BN + m], red_i[qq * BN + m], bv, bi)) {
-                            bv = red_v[qq * BN + m];
-                            bi = red_i[qq * BN + m];
+                tc_argmax_flush<BN>(a, smem + L::RED_OFF, m0, n_tile, ct);
+            }
+        }
+    }
+    if (EPI != EPI_ARGMAX && a.splits > 1) {  // the LM head (argmax) never splits K
+        tc::cluster_sync();  // every partial tile of the cluster is in shared memory
+        if (warp >= 2) {
+            // unit u = (half, quarter) of the tile is reduced by CTA u % splits,
+            // warp 2 + u / splits; sources are added in rank order
+            const int j = warp - 2;
+            const int u = j * a.splits + split;
+            if (u < 8) {
+                const int uq = u & 3, uhalf = u >> 2;
+                const int n = n0 + uq * 32 + lane;
+                constexpr int HALF = BN / 2;
+                const float *part = reinterpret_cast<const float *>(smem + L::A_OFF);
+#pragma unroll 1
+                for (int c = 0; c < HALF; c += 32) {
+                    const uint32_t row =
+                        tc::smem_u32(part + ((size_t)(u * 32 + lane) * HALF + c));
+                    float v[32];
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) v[k] = 0.f;
+                    for (int sr = 0; sr < a.splits; ++sr) {
+#pragma unroll
+                        for (int h = 0; h < 8; h += 4) {
+                            float4 g4[4];
+#pragma unroll
+                            for (int g = 0; g < 4; ++g)
+                                g4[g] = tc::ld_dsmem_f4(row + 16u * ((h + g + lane) & 7), sr);
+#pragma unroll
+                            for (int g = 0; g < 4; ++g) {
+                                v[4 * (h + g)] += g4[g].x;
+                                v[4 * (h + g) + 1] += g4[g].y;
+                                v[4 * (h + g) + 2] += g4[g].z;
+                                v[4 * (h + g) + 3] += g4[g].w;
+                            }
                         }
-                    a.pv[(size_t)(m0 + m) * a.nblk + n_tile] = bv;
-                    a.pi[(size_t)(m0 + m) * a.nblk + n_tile] = bi;
+                    }
+                    tc_epilogue32<BN, EPI>(a, v, n, m0, uhalf * HALF + c, uq, lane, smem + L::RED_OFF);
                 }
             }
-            if (a.splits > 1 && ct == 0) a.counters[m_tile * gridDim.x + n_tile] = 0u;
         }
+        tc::cluster_sync();  // no CTA leaves while another may still read its shared memory
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -387,20 +418,13 @@ int make_act_map(CUtensorMap *map, const uint16_t *x, int rows, int K, int BN) {
 
 int tc_bn_for_rows(int rows) { return rows <= 64 ? 64 : 128; }
 
-struct TcWs {
-    size_t cnt_off, part_off, total;
-};
-static TcWs tc_ws_layout(int rows, int n, int splits) {
-    const int bn = tc_bn_for_rows(rows);
-    const size_t mpad = (size_t)((rows + bn - 1) / bn) * bn;
-    TcWs w;
-    w.cnt_off = 256;  // bytes 0..255: error flag
-    w.part_off = w.cnt_off + TC_COUNTERS * 4;
-    w.total = w.part_off + (splits > 1 ? (size_t)splits * mpad * n * 4 : 0);
-    return w;
+// Workspace: the 4-byte error flag of the bounded waits (256 bytes reserved).
+size_t tc_gemm_workspace(int rows, int n, int splits) {
+    (void)rows;
+    (void)n;
+    (void)splits;
+    return 256;
 }
-
-size_t tc_gemm_workspace(int rows, int n, int splits) { return tc_ws_layout(rows, n, splits).total; }
 
 int tc_pick_splits(int rows, int n, int k) {
     const int bn = tc_bn_for_rows(rows);
@@ -410,7 +434,9 @@ int tc_pick_splits(int rows, int n, int k) {
     s = s < 1 ? 1 : s;
     s = s > TC_MAX_SPLITS ? TC_MAX_SPLITS : s;
     s = s > kc / 2 ? kc / 2 : s;  // at least two k chunks per split
-    return s < 1 ? 1 : s;
+    if (s < 1) s = 1;
+    while (s > 1 && (s - 1) * ((kc + s - 1) / s) >= kc) --s;  // no empty split
+    return s;
 }
 
 template <int BN, int EPI>
@@ -425,8 +451,19 @@ static int run_tc(const CUtensorMap &map, TcArgs &a, int splits, cudaStream_t st
             return -3;
         configured |= 1u << (dev & 31);
     }
-    dim3 grid(a.N / TC_BM, splits, (a.M + BN - 1) / BN);
-    tc_gemm_kernel<BN, EPI><<<grid, TC_THREADS, L::ALLOC, st>>>(map, a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.N / TC_BM) * splits, 1, (a.M + BN - 1) / BN);
+    cfg.blockDim = dim3(TC_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = L::ALLOC;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)splits;  // the split CTAs of a tile share one cluster
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI>, map, a) != cudaSuccess) return -3;
     return QB_LAUNCH_CHECK();
 }
 
@@ -446,14 +483,12 @@ int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8
                    const uint16_t *bias, int n, uint16_t *y, int splits, void *ws, size_t ws_bytes, bool clear,
                    const TcArgmax *am, cudaStream_t st) {
     if (rows <= 0 || n % TC_BM || k % TC_BK || splits < 1 || splits > k / TC_BK || splits > TC_MAX_SPLITS) return -1;
-    if (epi == EPI_ARGMAX && !am) return -1;
+    if (epi == EPI_ARGMAX && (!am || splits != 1)) return -1;
+    if (ws_bytes < tc_gemm_workspace(rows, n, splits)) return -1;
     const int bn = tc_bn_for_rows(rows);
     const int kc = k / TC_BK;
     const int kcps = (kc + splits - 1) / splits;
-    splits = (kc + kcps - 1) / kcps;  // no empty splits
-    const TcWs L = tc_ws_layout(rows, n, splits);
-    if (ws_bytes < L.total) return -1;
-    if ((size_t)((rows + bn - 1) / bn) * (n / TC_BM) > TC_COUNTERS) return -1;
+    if ((splits - 1) * kcps >= kc) return -1;  // every split owns at least one k chunk
     TcArgs a;
     a.w = w_tiled;
     a.scale = scale;
@@ -466,13 +501,13 @@ int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8
     a.kc_per_split = kcps;
     a.splits = splits;
     a.err = reinterpret_cast<unsigned *>(ws);
-    a.counters = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(ws) + L.cnt_off);
-    a.part = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + L.part_off);
+    a.counters = nullptr;
+    a.part = nullptr;
     a.pv = am ? am->pv : nullptr;
     a.pi = am ? am->pi : nullptr;
     a.nblk = am ? am->nblk : 0;
     a.logits = am ? am->logits : nullptr;
-    if (clear && cudaMemsetAsync(ws, 0, L.part_off, st) != cudaSuccess) return -3;
+    if (clear && cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return -3;
     return bn == 64 ? dispatch_epi<64>(epi, xmap, a, splits, st) : dispatch_epi<128>(epi, xmap, a, splits, st);
 }
 
