@@ -65,8 +65,8 @@ struct qwen_b200 {
     std::map<std::tuple<const void *, int, int>, CUtensorMap> maps;  // (buffer, rows, k)
     uint32_t *meta = nullptr;  // [4][R]: ids | slots | positions | logit rows
     uint32_t *tokens = nullptr, *slot_pos = nullptr;
-    void *attn_ws = nullptr, *lm_ws = nullptr;
-    size_t attn_ws_bytes = 0, lm_ws_bytes = 0;
+    void *lm_ws = nullptr;
+    size_t lm_ws_bytes = 0;
     // pinned staging
     uint32_t *h_meta = nullptr, *h_tokens = nullptr, *h_slot_pos = nullptr;
     std::vector<uint32_t> pos;  // host mirror of every slot's position
@@ -231,9 +231,6 @@ int allocate(qwen_b200 *h) {
     if ((rc = dalloc(h, (void **)&h->tokens, R * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->slot_pos, (size_t)c.max_seqs * 4))) return rc;
     CK(cudaMemset(h->slot_pos, 0, (size_t)c.max_seqs * 4));
-    h->attn_ws_bytes = attention_workspace(h->R, (int)c.max_context);
-    if ((rc = dalloc(h, &h->attn_ws, h->attn_ws_bytes))) return rc;
-    CK(cudaMemset(h->attn_ws, 0, h->attn_ws_bytes));  // completion counters start at zero
     h->lm_ws_bytes = lm_head_workspace(h->R, VOC);
     if ((rc = dalloc(h, &h->lm_ws, h->lm_ws_bytes))) return rc;
     CK(cudaMallocHost((void **)&h->h_meta, R * 4 * 4));
@@ -402,9 +399,8 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
             RK(launch_qkv(a, st));
         }
         {
-            LaunchScope ls(h, 2, st, 2);
-            RK(launch_attention(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx, h->attn_ws,
-                                h->attn_ws_bytes, h->R, false, st));
+            LaunchScope ls(h, 2, st, 1);
+            RK(launch_attention_cluster(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx, st));
         }
         if (dq) {
             CK(cudaMemcpyAsync(dq, h->q, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
@@ -1017,6 +1013,14 @@ int qwen_b200_op_attention(const uint16_t *q, uint32_t rows, const uint32_t *slo
         return QWEN_B200_EINVAL;
     return launch_attention(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
                             (int)capacity, ctx, workspace, workspace_bytes, (int)rows, true, (cudaStream_t)stream);
+}
+
+int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                                   uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
+                                   const float *vscales, uint32_t capacity, uint16_t *ctx, void *stream) {
+    if (!q || !slots || !positions || !kcodes || !kscales || !vcodes || !vscales || !ctx) return QWEN_B200_EINVAL;
+    return launch_attention_cluster(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
+                                    (int)capacity, ctx, (cudaStream_t)stream);
 }
 
 int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w_gu,

@@ -230,6 +230,14 @@ int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint3
                                    const uint32_t *positions, uint32_t max_len, const int8_t *kcodes,
                                    const float *kscales, const int8_t *vcodes, const float *vscales,
                                    uint32_t capacity, uint16_t *ctx, void *stream);
+/* The same attention in one launch with no workspace (the form the engine
+ * uses): a thread-block cluster per (row, KV head) splits the context (up to
+ * 8 CTAs), keeps the scores in shared memory, and exchanges the softmax
+ * statistics and partial contexts over distributed shared memory; results are
+ * independent of scheduling. max_len <= 65536. */
+int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                                   uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
+                                   const float *vscales, uint32_t capacity, uint16_t *ctx, void *stream);
 /* SwiGLU FFN input half: mid = bf16(bf16(silu(g)) * u) with g, u from
  * RMSNorm(x) (gamma NULL: no norm) times the interleaved gate/up weight
  * w_gu [2*4864][896] (row 2j gate j, row 2j+1 up j) and scales s_gu [2*4864]

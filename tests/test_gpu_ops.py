@@ -167,17 +167,20 @@ def random_cache(r, nslots, cap):
     return kc, ks, vc, vs
 
 
-def run_attention(q, slots, positions, cache, cap, max_len=None):
+def run_attention(q, slots, positions, cache, cap, max_len=None, cluster=False):
     keep = Keep()
     kc, ks, vc, vs = (dev(a) for a in cache)
     rows = q.shape[0]
-    ws_bytes = L().qwen_b200_attention_workspace(rows, cap)
-    ws = dev(np.zeros(ws_bytes, np.uint8))
     ctx = dev(np.zeros((rows, 896), np.int16))
     max_len = max_len or int(positions.max()) + 1
-    rc = L().qwen_b200_op_attention(keep((to_bits(q).view(np.int16))), rows, keep((slots.view(np.int32))),
-                                    keep((positions.view(np.int32))), max_len, vp(kc), vp(ks), vp(vc), vp(vs), cap,
-                                    vp(ctx), vp(ws), ws_bytes, stream())
+    args = (keep((to_bits(q).view(np.int16))), rows, keep((slots.view(np.int32))), keep((positions.view(np.int32))),
+            max_len, vp(kc), vp(ks), vp(vc), vp(vs), cap, vp(ctx))
+    if cluster:
+        rc = L().qwen_b200_op_attention_cluster(*args, stream())
+    else:
+        ws_bytes = L().qwen_b200_attention_workspace(rows, cap)
+        ws = dev(np.zeros(ws_bytes, np.uint8))
+        rc = L().qwen_b200_op_attention(*args, vp(ws), ws_bytes, stream())
     assert rc == 0
     sync()
     return from_bits(host(ctx).view(np.uint16))
@@ -192,27 +195,46 @@ def oracle_attention(q, slots, positions, cache):
     return out
 
 
-@pytest.mark.parametrize('positions', [[0], [16], [127], [128], [300, 5, 2047, 129]])
-def test_attention_decode(positions):
+@pytest.mark.parametrize('cluster', [False, True])
+@pytest.mark.parametrize('positions', [[0], [16], [127], [128], [255], [256], [300, 5, 2047, 129]])
+def test_attention_decode(positions, cluster):
     r = rng(sum(positions) + 11)
     cap = 2048
     positions = np.array(positions, np.uint32)
     slots = np.arange(len(positions), dtype=np.uint32)
     cache = random_cache(r, len(positions), cap)
     q = rand_bf16(r, (len(positions), 14, 64))
-    got = run_attention(q, slots, positions, cache, cap)
+    got = run_attention(q, slots, positions, cache, cap, cluster=cluster)
     assert_bf16_close(got, oracle_attention(q, slots, positions, cache), max_ulps=2, what='attention decode')
 
 
-def test_attention_prefill_rows_and_loose_bound():
+@pytest.mark.parametrize('cluster', [False, True])
+def test_attention_prefill_rows_and_loose_bound(cluster):
     r = rng(12)
     cap = 512
     slots = np.array([1] * 40 + [0] * 3, np.uint32)  # ragged: 40 causal rows of slot 1, 3 of slot 0
     positions = np.array(list(range(200, 240)) + [0, 1, 2], np.uint32)
     cache = random_cache(r, 2, cap)
     q = rand_bf16(r, (43, 14, 64))
-    got = run_attention(q, slots, positions, cache, cap, max_len=cap)  # capacity as the bound
+    got = run_attention(q, slots, positions, cache, cap, max_len=cap, cluster=cluster)  # capacity as the bound
     assert_bf16_close(got, oracle_attention(q, slots, positions, cache), max_ulps=2, what='attention prefill')
+
+
+@pytest.mark.parametrize('length', [8192, 32768])
+def test_attention_cluster_long_context(length):
+    """Long contexts (the attention config's 8192 / 32768): the cluster splits
+    the row over up to 8 CTAs."""
+    r = rng(length)
+    cap = length
+    positions = np.array([length - 1, length // 3], np.uint32)
+    slots = np.arange(2, dtype=np.uint32)
+    cache = random_cache(r, 2, cap)
+    q = rand_bf16(r, (2, 14, 64))
+    got = run_attention(q, slots, positions, cache, cap, cluster=True)
+    # 32768 fp32 terms summed in another order than the oracle's sequential
+    # sum move more results across a bf16 rounding boundary
+    assert_bf16_close(got, oracle_attention(q, slots, positions, cache), max_ulps=2,
+                      min_equal=0.99 if length <= 8192 else 0.97, what=f'attention L={length}')
 
 
 def test_qkv_fused_against_oracle_chain():
