@@ -42,10 +42,24 @@ HID, FFN, QKV, VOCAB, LAYERS = 896, 4864, 1152, 151936, 24
 KV_BYTES_PER_TOKEN_LAYER = 2 * 2 * (64 + 4)  # K and V, 2 heads, 64 codes + fp32 scale
 CLASSES = ['embedding', 'qkv_rope_kv8', 'attention', 'o_proj_residual', 'gate_up_swiglu', 'down_residual',
            'lm_head_argmax', 'bookkeeping']
-KERNEL_NAMES = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_score_kernel + attn_pv_kernel',
-                'o_proj_residual': 'gemv_kernel<896,EPI_RESIDUAL>', 'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
-                'down_residual': 'gemv_kernel<4864,EPI_RESIDUAL>', 'lm_head_argmax': 'lm_head_kernel + argmax_reduce',
-                'embedding': 'embed_kernel', 'bookkeeping': 'decode prologue/epilogue'}
+# kernels behind each class: rows <= 8 run the GEMV family, more rows the
+# tcgen05 GEMM (qkv/o/gate_up/down/LM head), attention is one cluster launch
+KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_cluster_kernel',
+                     'o_proj_residual': 'gemv_kernel<896,EPI_RESIDUAL>',
+                     'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
+                     'down_residual': 'gemv_kernel<4864,EPI_RESIDUAL>',
+                     'lm_head_argmax': 'lm_head_kernel + argmax_reduce_kernel',
+                     'embedding': 'embed_kernel', 'bookkeeping': 'decode_prologue/epilogue_kernel'}
+KERNEL_NAMES_TC = dict(KERNEL_NAMES_GEMV,
+                       qkv_rope_kv8='rmsnorm_kernel + tc_gemm_kernel<EPI_BIAS> + rope_kv8_kernel',
+                       o_proj_residual='tc_gemm_kernel<EPI_RESIDUAL>',
+                       gate_up_swiglu='rmsnorm_kernel + tc_gemm_kernel<EPI_SWIGLU>',
+                       down_residual='tc_gemm_kernel<EPI_RESIDUAL>',
+                       lm_head_argmax='rmsnorm_kernel + tc_gemm_kernel<EPI_ARGMAX> + argmax_reduce_kernel')
+
+
+def kernel_names(rows):
+    return KERNEL_NAMES_TC if rows > 8 else KERNEL_NAMES_GEMV
 
 
 def weight_bytes():
@@ -312,7 +326,7 @@ def run_ours(args):
     dom = max(kernels, key=lambda k: kernels[k]['ms_per_step'])
     dom_us = kernels[dom]['us_per_launch']
     achieved = cb[dom] / (dom_us / 1e6) / 1e9
-    roofline = {'kernel': KERNEL_NAMES[dom], 'class': dom, 'bound': 'hbm', 'achieved': round(achieved, 1),
+    roofline = {'kernel': kernel_names(S)[dom], 'class': dom, 'bound': 'hbm', 'achieved': round(achieved, 1),
                 'peak': hbm, 'peak_kind': peak_kind, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4),
                 'algorithmic_bytes_per_launch': cb[dom], 'traffic': committed_traffic(dom)}
     step_ms = ms_max / args.steps

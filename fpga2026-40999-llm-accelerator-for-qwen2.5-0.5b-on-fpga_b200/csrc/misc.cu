@@ -23,32 +23,43 @@ int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t 
     return QB_LAUNCH_CHECK();
 }
 
-// model_backend.py:69-71, one warp per row.
-__global__ void rmsnorm_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ gamma, int rows,
-                               float eps, uint16_t *__restrict__ out) {
+// model_backend.py:69-71, one warp per row. The row and gamma are loaded into
+// registers up front (14 words per lane, all requests in flight at once); the
+// sum of squares runs in the order lane, lane + 32, ... as before.
+constexpr int RMS_WORDS = QB_HID / 2 / 32;
+__global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict__ x,
+                                                     const uint16_t *__restrict__ gamma, int rows, float eps,
+                                                     uint16_t *__restrict__ out) {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const uint32_t *xr = reinterpret_cast<const uint32_t *>(x + (size_t)row * QB_HID);
     const uint32_t *gr = reinterpret_cast<const uint32_t *>(gamma);
     uint32_t *orow = reinterpret_cast<uint32_t *>(out + (size_t)row * QB_HID);
+    uint32_t xv[RMS_WORDS], gv[RMS_WORDS];
+#pragma unroll
+    for (int j = 0; j < RMS_WORDS; ++j) xv[j] = xr[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < RMS_WORDS; ++j) gv[j] = __ldg(gr + lane + 32 * j);
     float ss = 0.f;
-    for (int i = lane; i < QB_HID / 2; i += 32) {
-        const float a = bflo(xr[i]), b = bfhi(xr[i]);
+#pragma unroll
+    for (int j = 0; j < RMS_WORDS; ++j) {
+        const float a = bflo(xv[j]), b = bfhi(xv[j]);
         ss += a * a;
         ss += b * b;
     }
     ss = warp_sum(ss);
     const float rs = 1.0f / sqrtf(ss / (float)QB_HID + eps);
-    for (int i = lane; i < QB_HID / 2; i += 32) {
-        const float a = rbf(rbf(bflo(xr[i]) * rs) * bflo(gr[i]));
-        const float b = rbf(rbf(bfhi(xr[i]) * rs) * bfhi(gr[i]));
-        orow[i] = (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
+#pragma unroll
+    for (int j = 0; j < RMS_WORDS; ++j) {
+        const float a = rbf(rbf(bflo(xv[j]) * rs) * bflo(gv[j]));
+        const float b = rbf(rbf(bfhi(xv[j]) * rs) * bfhi(gv[j]));
+        orow[lane + 32 * j] = (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
     }
 }
 
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st) {
     if (rows <= 0) return -1;
-    rmsnorm_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, gamma, rows, eps, out);
+    rmsnorm_kernel<<<(rows + 1) / 2, 64, 0, st>>>(x, gamma, rows, eps, out);
     return QB_LAUNCH_CHECK();
 }
 
