@@ -1,9 +1,12 @@
 // GQA decode/prefill attention over the int8 (KV8) cache, split over context
 // chunks of 128 keys so that long contexts spread across all SMs.
 //
-// Arithmetic contract (legacy_100mhz_closed/src/PC/model_backend.py:97-102 with
-// the cache dequantised as code * scale in fp32):
-//   S[t]  = bf16(fma-chain_d(q[d] * (kcode[t][d] * kscale[t])) / 8)
+// Arithmetic contract (legacy_100mhz_closed/src/PC/model_backend.py:97-102
+// over the KV8 cache in the accelerator's order, oracle ref_kv8_scores):
+//   S[t]  = bf16(RN32(RN32(Q . kcode[t]) * 2^(E-26) * kscale[t]) / 8), q
+//           aligned to its largest exponent E as 28-bit integers
+//           Q[d] = rint(q[d] * 2^(26-E)), the dot product exact (four int8
+//           limbs of Q against the codes with dp4a, combined in int64)
 //   P[t]  = bf16(exp(S[t] - max S) * (1 / sum exp(S - max S)))
 //   ctx   = bf16(sum_t P[t] * (vcode[t][d] * vscale[t]))
 // Query head h reads KV head h / 7 (repeat_interleave(7), model_backend.py:97-98).
@@ -66,10 +69,37 @@ __global__ void __launch_bounds__(AT) attn_score_kernel(AttnArgs a) {
     const int t0 = c * AT;
     if (t0 >= L) return;
     const int slot = (int)a.slots[r];
-    __shared__ float qs[7][QB_HD];
+    // q of the group's heads as int8 limbs: ql[h][word][limb] holds dims
+    // 4*word .. 4*word+3 of limb l of Q = rint(q * 2^(26-E_h))
+    __shared__ __align__(16) uint32_t ql[7][16][4];
+    __shared__ int qe[7];
     __shared__ float red[AT / 32][7];
-    for (int i = threadIdx.x; i < 7 * QB_HD; i += AT)
-        qs[i / QB_HD][i % QB_HD] = bf2f(a.q[(size_t)r * QB_HID + g * 7 * QB_HD + i]);
+    {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int h = warp; h < 7; h += AT / 32) {
+            const uint16_t *qh = a.q + (size_t)r * QB_HID + (g * 7 + h) * QB_HD;
+            const float q0 = bf2f(qh[lane]), q1 = bf2f(qh[lane + 32]);
+            const float amax = warp_max(fmaxf(fabsf(q0), fabsf(q1)));
+            const int e = amax > 0.f ? ilogbf(amax) : 0;
+            const float qv[2] = {q0, q1};
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int d = lane + 32 * k;
+                const int qi = __float2int_rn(ldexpf(qv[k], 26 - e));
+                const int l0 = ((qi + 64) & 127) - 64;
+                const int r1 = (qi - l0) >> 7;
+                const int l1 = ((r1 + 64) & 127) - 64;
+                const int r2 = (r1 - l1) >> 7;
+                const int l2 = ((r2 + 64) & 127) - 64;
+                const int l3 = (r2 - l2) >> 7;
+                const int limb[4] = {l0, l1, l2, l3};
+#pragma unroll
+                for (int l = 0; l < 4; ++l)
+                    reinterpret_cast<int8_t *>(&ql[h][d >> 2][l])[d & 3] = (int8_t)limb[l];
+            }
+            if (lane == 0) qe[h] = e;
+        }
+    }
     __syncthreads();
     const int t = t0 + threadIdx.x;
     const bool valid = t < L;
@@ -80,26 +110,31 @@ __global__ void __launch_bounds__(AT) attn_score_kernel(AttnArgs a) {
         const size_t base = ((size_t)slot * QB_KVH + g) * a.cap + t;
         const float s = a.ks[base];
         const uint4 *kp = reinterpret_cast<const uint4 *>(a.kc + base * QB_HD);
+        int acc[7][4];
+#pragma unroll
+        for (int h = 0; h < 7; ++h)
+#pragma unroll
+            for (int l = 0; l < 4; ++l) acc[h][l] = 0;
 #pragma unroll
         for (int v4 = 0; v4 < 4; ++v4) {
             const uint4 kw = kp[v4];
-            const uint32_t words[4] = {kw.x, kw.y, kw.z, kw.w};
+            const int words[4] = {(int)kw.x, (int)kw.y, (int)kw.z, (int)kw.w};
 #pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-                float f[4];
-                i8x4_to_f32(words[wi], f[0], f[1], f[2], f[3]);
+            for (int wi = 0; wi < 4; ++wi)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int d = v4 * 16 + wi * 4 + j;
-                    const float kd = __fmul_rn(f[j], s);
-#pragma unroll
-                    for (int h = 0; h < 7; ++h) sc[h] = fmaf(qs[h][d], kd, sc[h]);
+                for (int h = 0; h < 7; ++h) {
+                    const uint4 lq = *reinterpret_cast<const uint4 *>(&ql[h][v4 * 4 + wi][0]);
+                    acc[h][0] = __dp4a(words[wi], (int)lq.x, acc[h][0]);
+                    acc[h][1] = __dp4a(words[wi], (int)lq.y, acc[h][1]);
+                    acc[h][2] = __dp4a(words[wi], (int)lq.z, acc[h][2]);
+                    acc[h][3] = __dp4a(words[wi], (int)lq.w, acc[h][3]);
                 }
-            }
         }
 #pragma unroll
         for (int h = 0; h < 7; ++h) {
-            sc[h] = rbf(sc[h] * 0.125f);
+            const long long dot = (long long)acc[h][0] + ((long long)acc[h][1] << 7) + ((long long)acc[h][2] << 14) +
+                                  ((long long)acc[h][3] << 21);
+            sc[h] = rbf(__fmul_rn(ldexpf(__ll2float_rn(dot), qe[h] - 26), s) * 0.125f);
             a.S[((size_t)r * QB_QH + g * 7 + h) * a.cap + t] = sc[h];
         }
     } else {

@@ -1,32 +1,48 @@
-// GQA attention over the KV8 cache in one launch: one thread-block cluster
-// per (query row, KV head), its CTAs splitting the row's context. Same
-// arithmetic as attention.cu (legacy_100mhz_closed/src/PC/model_backend.py:
-// 97-102 with the cache dequantised as code * scale in fp32):
-//   S[t] = bf16(fma-chain_d(q[d] * (kcode[t][d] * kscale[t])) / 8)   (d ascending)
-//   P[t] = bf16(exp(S[t] - max S) * (1 / sum exp(S - max S)))
-//   ctx  = bf16(sum_t P[t] * (vcode[t][d] * vscale[t]))
-// The seven query heads of a KV head are processed together with packed
-// f32x2 FMAs (each lane an IEEE fma, so S keeps the oracle's bits).
-//   phase 1  S for this CTA's keys -> shared memory (bf16), per-head max
-//   phase 2  per-head exp-sums; the cluster exchanges (max, sum) over
-//            distributed shared memory and every CTA forms the same global
-//            max and 1/sum (rank order)
-//   phase 3  P for each 256-key chunk, partial P.V per CTA
-//   phase 4  CTA rank 0 adds the partial contexts of all ranks in rank order
-//            and writes ctx (bf16)
-// No global scratch, no atomics; cluster barriers only (the hardware
-// co-schedules a cluster's CTAs).
+// GQA decode/prefill attention over the KV8 cache in one launch: one
+// thread-block cluster per (query row, KV head), its CTAs splitting the row's
+// context. Arithmetic of legacy_100mhz_closed/src/PC/model_backend.py:97-102
+// over the KV8 cache in the accelerator's order (oracle ref_kv8_scores):
+//   S[h][t] = bf16(RN32(RN32(Q_h . kcode[t]) * 2^(E_h-26) * kscale[t]) / 8)
+//             with q_h aligned to its largest exponent E_h as 28-bit integers
+//             Q_h[d] = rint(q_h[d] * 2^(26-E_h)) and an exact integer dot
+//   P[h][t] = bf16(exp(S[h][t] - max_t S[h]) * (1 / sum_t exp(S[h][t] - max S[h])))
+//   ctx[h]  = bf16(sum_t P[h][t] * vscale[t] * vcode[t])
+//
+// The seven query heads of a KV head make the score product a small matrix
+// product on the tensor cores (mma.sync, register fragments):
+//   scores   D[16 keys][8 heads] = Kcode[16][64] . Q^T[64][8] with int8 x int8
+//            -> int32 products (m16n8k32): Q is split into four signed 7-bit
+//            limbs, the raw codes are the A operand as they sit in shared
+//            memory, and the four exact limb sums combine in int64; the
+//            scores are therefore bit-identical to the oracle's
+//   context  on the CUDA cores with the oracle's products P * (vcode * vscale)
+//            (packed f32x2 fmas), keys in 16 slices, slices then ranks added
+//            in order
+// K and then V stream through one 8-slot shared-memory ring in 128-key chunks
+// (8 KB of codes) by bulk copy, completing on mbarriers (bounded waits); the
+// per-key scales are staged in shared memory once.
+//   phase 1  scores of this CTA's keys -> shared memory (fp32 holding bf16
+//            values), per-head CTA max; the cluster forms the global max
+//   phase 2  E = exp(S - max) in place, per-head sums; the cluster adds the
+//            sums in rank order
+//   phase 3  P = bf16(E / sum) per chunk, partial P.V per key slice
+//   phase 4  slice partials added in slice order, CTA rank 0 adds the ranks'
+//            partials in rank order and writes ctx (bf16)
+// No global scratch, no atomics; results do not depend on scheduling.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc05.cuh"
 
 namespace qb {
 
-constexpr int AC_THREADS = 256;
-constexpr int AC_CHUNK = 256;  // keys per phase-1 pass (one per thread)
-constexpr int AC_SLICES = 16;  // phase 3: 16 four-dim words x 16 key slices
-constexpr int AC_MAX_SPLITS = 8;
-constexpr int AC_MAX_KPC = 8192;  // keys per CTA (shared-memory S budget)
+constexpr int AM_THREADS = 256;
+constexpr int AM_WARPS = AM_THREADS / 32;
+constexpr int AM_CHUNK = 16 * AM_WARPS;  // keys per ring stage: a 16-key block per warp
+constexpr int AM_STAGE_BYTES = AM_CHUNK * QB_HD;
+constexpr int AM_SLOTS_RING = 8;  // ring slots (K chunks, then V chunks)
+constexpr int AM_MAX_SPLITS = 8;
+constexpr int AM_MAX_KPC = 4096;  // keys per CTA (shared-memory score budget)
+constexpr int AM_SLOTS = 2 * 148;  // resident CTAs the split plan aims at (2 per SM)
 
 struct AcArgs {
     const uint16_t *q;
@@ -35,26 +51,40 @@ struct AcArgs {
     const float *ks, *vs;
     int cap;
     uint16_t *ctx;
-    int kpc;  // keys per CTA (multiple of AC_CHUNK)
+    int kpc;  // keys per CTA (multiple of AM_CHUNK)
+    unsigned *err;
 };
 
 struct AcSmem {
-    int s_off, p_off, q_off, part_off, stat_off, ctxp_off, red_off, v_off, vs_off, total;
+    int ring, s, sld, kss, vss, p, stat, red, bars, total;
 };
 
+// ring [8][128][64] int8 | S [7][kpc + 4] fp32 | K scales [kpc] | V scales
+// [kpc] | P of one chunk [128][8] | stat (max[8], sum[8], ctx partial
+// [7][64]) | per-warp reductions [2][8][8] | mbarriers [8]. The per-slice
+// context partials [16][8][64] reuse the ring once the last chunk is consumed.
 __host__ __device__ inline AcSmem ac_smem(int kpc) {
     AcSmem L;
-    L.s_off = 0;                                  // bf16 S [7][kpc]
-    L.p_off = L.s_off + 7 * kpc * 2;              // float P [AC_CHUNK][8]
-    L.q_off = L.p_off + AC_CHUNK * 8 * 4;         // float q [64][8]
-    L.part_off = L.q_off + 64 * 8 * 4;            // float [AC_SLICES][8][64]
-    L.stat_off = L.part_off + AC_SLICES * 8 * 64 * 4;  // float m[8], l[8]
-    L.ctxp_off = L.stat_off + 16 * 4;             // float CTA partial [7][64]
-    L.red_off = L.ctxp_off + 7 * 64 * 4;          // float [8 warps][8]
-    L.v_off = L.red_off + 8 * 8 * 4 * 2;          // int8 V chunk [AC_CHUNK][64]
-    L.vs_off = L.v_off + AC_CHUNK * 64;           // float V scales [AC_CHUNK]
-    L.total = L.vs_off + AC_CHUNK * 4;
+    L.ring = 0;
+    L.s = L.ring + AM_SLOTS_RING * AM_STAGE_BYTES;
+    L.sld = kpc + 4;  // row stride: the 4 head rows a warp writes fall in distinct banks
+    L.kss = L.s + 7 * L.sld * 4;
+    L.vss = L.kss + kpc * 4;
+    L.p = L.vss + kpc * 4;
+    L.stat = L.p + AM_CHUNK * 8 * 4;
+    L.red = L.stat + (16 + 7 * QB_HD) * 4;
+    L.bars = L.red + 2 * AM_WARPS * 8 * 4;
+    L.total = L.bars + AM_SLOTS_RING * 8;
     return L;
+}
+
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
@@ -67,242 +97,316 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
 template <bool CLUSTER>
-__global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(AcArgs a) {
-    extern __shared__ __align__(16) uint8_t sm[];
+__global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
     const int kpc = a.kpc;
     const AcSmem L = ac_smem(kpc);
-    uint16_t *S = reinterpret_cast<uint16_t *>(sm + L.s_off);
-    float *P = reinterpret_cast<float *>(sm + L.p_off);
-    float *qs = reinterpret_cast<float *>(sm + L.q_off);
-    float *part = reinterpret_cast<float *>(sm + L.part_off);
-    float *stat = reinterpret_cast<float *>(sm + L.stat_off);
-    float *ctxp = reinterpret_cast<float *>(sm + L.ctxp_off);
-    float *red = reinterpret_cast<float *>(sm + L.red_off);
-    uint8_t *Vc = sm + L.v_off;
-    float *Vsc = reinterpret_cast<float *>(sm + L.vs_off);
+    const int8_t *ring = reinterpret_cast<const int8_t *>(sm + L.ring);
+    float *S = reinterpret_cast<float *>(sm + L.s);
+    float *kss = reinterpret_cast<float *>(sm + L.kss);
+    float *vss = reinterpret_cast<float *>(sm + L.vss);
+    float *part = reinterpret_cast<float *>(sm + L.ring);  // phase 4, after the last chunk
+    float *P = reinterpret_cast<float *>(sm + L.p);
+    float *stat = reinterpret_cast<float *>(sm + L.stat);
+    float *ctxp = stat + 16;
+    float *red = reinterpret_cast<float *>(sm + L.red);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + L.bars);
+    const int sld = L.sld;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.y, r = blockIdx.z;
+    const int gid = lane >> 2, tig = lane & 3;  // fragment row group / thread in group
+    const int kvh = blockIdx.y, r = blockIdx.z;
     const int rank = CLUSTER ? (int)tc::cluster_rank() : 0;
     const int nranks = CLUSTER ? (int)gridDim.x : 1;
     const int L_row = (int)a.positions[r] + 1;
     const int slot = (int)a.slots[r];
     const int t_begin = rank * kpc;
-    const int t_end = min(L_row, t_begin + kpc);
-    const int nkeys = max(0, t_end - t_begin);
-    const size_t kvbase = ((size_t)slot * QB_KVH + g) * a.cap;
+    const int nkeys = max(0, min(L_row, t_begin + kpc) - t_begin);
+    const int nchunks = (nkeys + AM_CHUNK - 1) / AM_CHUNK;
+    const size_t kvbase = ((size_t)slot * QB_KVH + kvh) * a.cap + t_begin;  // first key of this CTA
+    const int8_t *kg = a.kc + kvbase * QB_HD;
+    const int8_t *vg = a.vc + kvbase * QB_HD;
 
-    // q of the group's seven heads, [d][h] with a zero eighth head
-    for (int i = tid; i < 64 * 8; i += AC_THREADS) {
-        const int d = i >> 3, h = i & 7;
-        qs[i] = h < 7 ? bf2f(a.q[(size_t)r * QB_HID + (g * 7 + h) * QB_HD + d]) : 0.f;
+    // ring item i: K chunk i (i < nchunks), then V chunk i - nchunks; slot i % 8
+    const int items = 2 * nchunks;
+    auto issue = [&](int i) {
+        const bool isv = i >= nchunks;
+        const int c = isv ? i - nchunks : i;
+        const int n = min(AM_CHUNK, nkeys - c * AM_CHUNK);
+        const int sl = i % AM_SLOTS_RING;
+        tc::mbar_arrive_expect_tx(&full[sl], (uint32_t)(n * QB_HD));
+        tc::bulk_load(sm + L.ring + sl * AM_STAGE_BYTES, (isv ? vg : kg) + (size_t)c * AM_STAGE_BYTES,
+                      (uint32_t)(n * QB_HD), &full[sl]);
+    };
+    if (tid == 0) {
+        for (int sl = 0; sl < AM_SLOTS_RING; ++sl) tc::mbar_init(&full[sl], 1);
+        tc::mbar_fence_init();
+        for (int i = 0; i < min(items, AM_SLOTS_RING); ++i) issue(i);
     }
-    __syncthreads();
+    for (int t = tid; t < nkeys; t += AM_THREADS) {
+        kss[t] = __ldg(a.ks + kvbase + t);
+        vss[t] = __ldg(a.vs + kvbase + t);
+    }
+    bool ok = true;
+
+    // q as int8 limbs (B operand of the score product): head gid, dims
+    // 16*tig .. 16*tig+15. E = exponent of max|q| over the head's 64 dims;
+    // Q = rint(q * 2^(26-E)) = L0 + 2^7 L1 + 2^14 L2 + 2^21 L3 with L0..L2 in
+    // [-64, 63]. In k step s the fragment's k = 4tig..4tig+3 | 16+4tig..
+    // 16+4tig+3 map to dims 16tig + 8s + 0..3 | 16tig + 8s + 4..7, so both
+    // operands are plain 32-bit words of consecutive dims.
+    uint32_t qb[4][2][2];  // [limb][k step][register]
+    int e_h0, e_h1;        // exponents of heads 2tig, 2tig+1 (the C fragment's columns)
+    {
+        uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+        if (gid < 7) {
+            const uint4 *qp =
+                reinterpret_cast<const uint4 *>(a.q + (size_t)r * QB_HID + (kvh * 7 + gid) * QB_HD + 16 * tig);
+            q0 = qp[0];
+            q1 = qp[1];
+        }
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        float qf[16];
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            qf[2 * i] = bflo(w[i]);
+            qf[2 * i + 1] = bfhi(w[i]);
+            amax = fmaxf(amax, fmaxf(fabsf(qf[2 * i]), fabsf(qf[2 * i + 1])));
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const int e = amax > 0.f ? ilogbf(amax) : 0;
+        uint32_t lb[4][4] = {};  // [limb][word of 4 dims]
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int qi = __float2int_rn(ldexpf(qf[i], 26 - e));
+            const int l0 = ((qi + 64) & 127) - 64;
+            const int r1 = (qi - l0) >> 7;
+            const int l1 = ((r1 + 64) & 127) - 64;
+            const int r2 = (r1 - l1) >> 7;
+            const int l2 = ((r2 + 64) & 127) - 64;
+            const int l3 = (r2 - l2) >> 7;
+            const int limb[4] = {l0, l1, l2, l3};
+#pragma unroll
+            for (int l = 0; l < 4; ++l) lb[l][i >> 2] |= ((uint32_t)limb[l] & 0xffu) << (8 * (i & 3));
+        }
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+#pragma unroll
+            for (int st = 0; st < 2; ++st) {
+                qb[l][st][0] = lb[l][2 * st];
+                qb[l][st][1] = lb[l][2 * st + 1];
+            }
+        e_h0 = __shfl_sync(0xffffffffu, e, 4 * (2 * tig));
+        e_h1 = __shfl_sync(0xffffffffu, e, 4 * (2 * tig + 1));
+    }
+    __syncthreads();  // staged scales visible; barriers initialised
 
     // ---------------- phase 1: scores
-    float mloc[7];
+    float m0 = -INFINITY, m1 = -INFINITY;  // heads 2tig, 2tig+1
+    const int h0 = 2 * tig, h1 = 2 * tig + 1;
+    for (int c = 0; c < nchunks; ++c) {
+        const int sl = c % AM_SLOTS_RING;
+        const int kb = c * AM_CHUNK + 16 * warp;  // this warp's 16-key block
+        const int k0 = kb + gid, k1 = kb + gid + 8;
+        if (ok) ok = tc::mbar_wait(&full[sl], (c / AM_SLOTS_RING) & 1, a.err, 11);
+        if (ok && kb < nkeys) {
+            const int8_t *blk = ring + sl * AM_STAGE_BYTES + 16 * warp * QB_HD;
+            const uint4 u = *reinterpret_cast<const uint4 *>(blk + gid * QB_HD + 16 * tig);
+            const uint4 v = *reinterpret_cast<const uint4 *>(blk + (gid + 8) * QB_HD + 16 * tig);
+            int d[4][4];  // [limb][fragment]
 #pragma unroll
-    for (int h = 0; h < 7; ++h) mloc[h] = -INFINITY;
-    // each thread owns one key of every 256-key chunk; the next chunk's row
-    // (64 code bytes + scale) is requested before the current one is used
-    uint4 kr[4];
-    float ksc = 0.f;
-    auto load_krow = [&](int tl) {
-        if (tl < nkeys) {
-            const size_t key = kvbase + t_begin + tl;
-            const uint4 *kp = reinterpret_cast<const uint4 *>(a.kc + key * QB_HD);
+            for (int l = 0; l < 4; ++l) {
+                d[l][0] = d[l][1] = d[l][2] = d[l][3] = 0;
+                mma_s8_16832(d[l], u.x, v.x, u.y, v.y, qb[l][0][0], qb[l][0][1]);
+                mma_s8_16832(d[l], u.z, v.z, u.w, v.w, qb[l][1][0], qb[l][1][1]);
+            }
+            float sc[4];
 #pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) kr[v4] = kp[v4];
-            ksc = a.ks[key];
-        }
-    };
-    load_krow(tid);
-    for (int c0 = 0; c0 < nkeys; c0 += AC_CHUNK) {
-        const int tl = c0 + tid;  // key index within this CTA
-        const uint4 cur[4] = {kr[0], kr[1], kr[2], kr[3]};
-        const float s = ksc;
-        load_krow(tl + AC_CHUNK);
-        if (tl < nkeys) {
-            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                             make_float2(0.f, 0.f)};
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-                const uint4 kw = cur[v4];
-                const uint32_t words[4] = {kw.x, kw.y, kw.z, kw.w};
-#pragma unroll
-                for (int wi = 0; wi < 4; ++wi) {
-                    float f[4];
-                    i8x4_to_f32(words[wi], f[0], f[1], f[2], f[3]);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int d = v4 * 16 + wi * 4 + j;
-                        const float kd = __fmul_rn(f[j], s);
-                        const float2 kk = make_float2(kd, kd);
-                        const float4 q03 = *reinterpret_cast<const float4 *>(qs + d * 8);
-                        const float4 q47 = *reinterpret_cast<const float4 *>(qs + d * 8 + 4);
-                        acc[0] = ffma2(make_float2(q03.x, q03.y), kk, acc[0]);
-                        acc[1] = ffma2(make_float2(q03.z, q03.w), kk, acc[1]);
-                        acc[2] = ffma2(make_float2(q47.x, q47.y), kk, acc[2]);
-                        acc[3] = ffma2(make_float2(q47.z, q47.w), kk, acc[3]);
-                    }
+            for (int f = 0; f < 4; ++f) {
+                const long long dot = (long long)d[0][f] + ((long long)d[1][f] << 7) + ((long long)d[2][f] << 14) +
+                                      ((long long)d[3][f] << 21);
+                const float ks = kss[f < 2 ? k0 : k1];
+                sc[f] = rbf(__fmul_rn(ldexpf(__ll2float_rn(dot), ((f & 1) ? e_h1 : e_h0) - 26), ks) * 0.125f);
+            }
+            if (k0 < nkeys) {
+                S[h0 * sld + k0] = sc[0];
+                m0 = fmaxf(m0, sc[0]);
+                if (h1 < 7) {
+                    S[h1 * sld + k0] = sc[1];
+                    m1 = fmaxf(m1, sc[1]);
                 }
             }
-            const float sc[7] = {acc[0].x, acc[0].y, acc[1].x, acc[1].y, acc[2].x, acc[2].y, acc[3].x};
-#pragma unroll
-            for (int h = 0; h < 7; ++h) {
-                const uint16_t sb = f2bf(sc[h] * 0.125f);
-                S[h * kpc + tl] = sb;
-                mloc[h] = fmaxf(mloc[h], bf2f(sb));
+            if (k1 < nkeys) {
+                S[h0 * sld + k1] = sc[2];
+                m0 = fmaxf(m0, sc[2]);
+                if (h1 < 7) {
+                    S[h1 * sld + k1] = sc[3];
+                    m1 = fmaxf(m1, sc[3]);
+                }
             }
         }
+        __syncthreads();  // every warp is done with this slot
+        if (tid == 0 && ok && c + AM_SLOTS_RING < items) issue(c + AM_SLOTS_RING);
     }
-    // CTA max per head
+    // per-head max: lanes of equal tig hold the same two heads
 #pragma unroll
-    for (int h = 0; h < 7; ++h) {
-        const float m = warp_max(mloc[h]);
-        if (lane == 0) red[warp * 8 + h] = m;
+    for (int o = 4; o < 32; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
     }
-    __syncthreads();
-    float mcta[7];
-#pragma unroll
-    for (int h = 0; h < 7; ++h) {
-        float m = red[h];
-        for (int w = 1; w < AC_THREADS / 32; ++w) m = fmaxf(m, red[w * 8 + h]);
-        mcta[h] = m;
-    }
-    // ---------------- phase 2: exp-sums and the cluster-wide max / sum
-    float lloc[7];
-#pragma unroll
-    for (int h = 0; h < 7; ++h) lloc[h] = 0.f;
-    for (int tl = tid; tl < nkeys; tl += AC_THREADS)
-#pragma unroll
-        for (int h = 0; h < 7; ++h) lloc[h] += expf(bf2f(S[h * kpc + tl]) - mcta[h]);
-    float *red2 = red + 64;
-#pragma unroll
-    for (int h = 0; h < 7; ++h) {
-        const float l = warp_sum(lloc[h]);
-        if (lane == 0) red2[warp * 8 + h] = l;
+    if (gid == 0) {
+        red[warp * 8 + h0] = m0;
+        red[warp * 8 + h1] = m1;
     }
     __syncthreads();
-    if (tid < 7) {
-        float l = 0.f;
-        for (int w = 0; w < AC_THREADS / 32; ++w) l += red2[w * 8 + tid];
-        stat[tid] = mcta[tid];
-        stat[8 + tid] = l;
+    if (tid < 8) {
+        float m = red[tid];
+        for (int w = 1; w < AM_WARPS; ++w) m = fmaxf(m, red[w * 8 + tid]);
+        stat[tid] = m;
     }
     __syncthreads();
-    float M[7], inv[7];
+    float M[7];
     if constexpr (CLUSTER) {
         tc::cluster_sync();
-        // same order in every CTA: ranks ascending; max first, then sum
         const uint32_t sa = tc::smem_u32(stat);
 #pragma unroll
-        for (int h = 0; h < 7; ++h) {
-            M[h] = -INFINITY;
-            inv[h] = 0.f;
-        }
+        for (int h = 0; h < 7; ++h) M[h] = -INFINITY;
         for (int sr = 0; sr < nranks; ++sr) {
             const float4 m03 = tc::ld_dsmem_f4(sa, sr), m47 = tc::ld_dsmem_f4(sa + 16, sr);
             const float mv[7] = {m03.x, m03.y, m03.z, m03.w, m47.x, m47.y, m47.z};
 #pragma unroll
             for (int h = 0; h < 7; ++h) M[h] = fmaxf(M[h], mv[h]);
         }
-        for (int sr = 0; sr < nranks; ++sr) {
-            const float4 m03 = tc::ld_dsmem_f4(sa, sr), m47 = tc::ld_dsmem_f4(sa + 16, sr);
-            const float4 l03 = tc::ld_dsmem_f4(sa + 32, sr), l47 = tc::ld_dsmem_f4(sa + 48, sr);
-            const float mv[7] = {m03.x, m03.y, m03.z, m03.w, m47.x, m47.y, m47.z};
-            const float lv[7] = {l03.x, l03.y, l03.z, l03.w, l47.x, l47.y, l47.z};
-#pragma unroll
-            for (int h = 0; h < 7; ++h)
-                if (lv[h] > 0.f) inv[h] += lv[h] * expf(mv[h] - M[h]);  // inv holds the sum for now
-        }
-#pragma unroll
-        for (int h = 0; h < 7; ++h) inv[h] = 1.0f / inv[h];
     } else {
 #pragma unroll
-        for (int h = 0; h < 7; ++h) {
-            M[h] = stat[h];
-            inv[h] = 1.0f / stat[8 + h];
-        }
+        for (int h = 0; h < 7; ++h) M[h] = stat[h];
     }
-    // ---------------- phase 3: P and partial P.V
-    const int word = tid & 15, slice = tid >> 4;  // dims 4*word..+3, keys slice, slice+16, ...
-    float2 acc[4][4];                           // [dim][head pair]
+
+    // ---------------- phase 2: E = exp(S - max) in place, per-head sums
+    float lsum[7];
+#pragma unroll
+    for (int h = 0; h < 7; ++h) {
+        float l = 0.f;
+        for (int t = tid; t < nkeys; t += AM_THREADS) {
+            const float e = expf(S[h * sld + t] - M[h]);
+            S[h * sld + t] = e;
+            l += e;
+        }
+        lsum[h] = l;
+    }
+    float *red2 = red + AM_WARPS * 8;
+#pragma unroll
+    for (int h = 0; h < 7; ++h) {
+        const float l = warp_sum(lsum[h]);
+        if (lane == 0) red2[warp * 8 + h] = l;
+    }
+    __syncthreads();
+    if (tid < 8) {
+        float l = 0.f;
+        if (tid < 7)
+            for (int w = 0; w < AM_WARPS; ++w) l += red2[w * 8 + tid];
+        stat[8 + tid] = l;
+    }
+    __syncthreads();
+    float inv[7];  // 1 / sum per head
+    {
+        float z[8];
+        if constexpr (CLUSTER) {
+            tc::cluster_sync();
+            const uint32_t la = tc::smem_u32(stat + 8);
+#pragma unroll
+            for (int h = 0; h < 8; ++h) z[h] = 0.f;
+            for (int sr = 0; sr < nranks; ++sr) {
+                const float4 l03 = tc::ld_dsmem_f4(la, sr), l47 = tc::ld_dsmem_f4(la + 16, sr);
+                const float lv[8] = {l03.x, l03.y, l03.z, l03.w, l47.x, l47.y, l47.z, l47.w};
+#pragma unroll
+                for (int h = 0; h < 8; ++h) z[h] += lv[h];
+            }
+        } else {
+#pragma unroll
+            for (int h = 0; h < 8; ++h) z[h] = stat[8 + h];
+        }
+#pragma unroll
+        for (int h = 0; h < 7; ++h) inv[h] = 1.0f / z[h];
+    }
+
+    // ---------------- phase 3: P per chunk, partial P.V on the CUDA cores
+    // with the oracle's products P * (vcode * vscale) (fp32 fma); thread =
+    // (word of 4 dims, key slice), keys slice, slice + 16, ... of the chunk
+    const int word = tid & 15, slice = tid >> 4;
+    float2 acc[4][4];  // [dim][head pair]
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
-    // the V chunk is staged in shared memory (thread tid copies key tid's
-    // row); the next chunk's rows are requested while this one is used
-    uint4 vr[4];
-    float vsc = 0.f;
-    auto load_vrow = [&](int tl) {
-        if (tl < nkeys) {
-            const size_t key = kvbase + t_begin + tl;
-            const uint4 *vp = reinterpret_cast<const uint4 *>(a.vc + key * QB_HD);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) vr[v4] = vp[v4];
-            vsc = a.vs[key];
-        }
-    };
-    load_vrow(tid);
-    for (int c0 = 0; c0 < nkeys; c0 += AC_CHUNK) {
-        const int nc = min(AC_CHUNK, nkeys - c0);
-        __syncthreads();  // previous chunk's P and V fully consumed
-        if (tid < nc) {
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) *reinterpret_cast<uint4 *>(Vc + tid * 64 + v4 * 16) = vr[v4];
-            Vsc[tid] = vsc;
-        }
-        load_vrow(c0 + AC_CHUNK + tid);
-        for (int i = tid; i < AC_CHUNK * 8; i += AC_THREADS) {
+    for (int c = 0; c < nchunks; ++c) {
+        const int item = nchunks + c;
+        const int sl = item % AM_SLOTS_RING;
+        const int c0 = c * AM_CHUNK, nc = min(AM_CHUNK, nkeys - c0);
+        for (int i = tid; i < AM_CHUNK * 8; i += AM_THREADS) {
             const int tt = i >> 3, h = i & 7;
-            float p = 0.f;
-            if (tt < nc && h < 7) p = rbf(expf(bf2f(S[h * kpc + c0 + tt]) - M[h]) * inv[h]);
-            P[i] = p;
+            float iv = inv[0];
+#pragma unroll
+            for (int hh = 1; hh < 7; ++hh)
+                if (h == hh) iv = inv[hh];
+            P[i] = (tt < nc && h < 7) ? rbf(S[h * sld + c0 + tt] * iv) : 0.f;
         }
-        __syncthreads();
-        for (int tt = slice; tt < nc; tt += AC_SLICES) {
-            const uint32_t w = *reinterpret_cast<const uint32_t *>(Vc + tt * 64 + word * 4);
-            const float s = Vsc[tt];
-            float f[4];
-            i8x4_to_f32(w, f[0], f[1], f[2], f[3]);
-            const float4 p03 = *reinterpret_cast<const float4 *>(P + tt * 8);
-            const float4 p47 = *reinterpret_cast<const float4 *>(P + tt * 8 + 4);
-            const float2 pp[4] = {make_float2(p03.x, p03.y), make_float2(p03.z, p03.w), make_float2(p47.x, p47.y),
-                                  make_float2(p47.z, p47.w)};
+        if (ok) ok = tc::mbar_wait(&full[sl], (item / AM_SLOTS_RING) & 1, a.err, 12);
+        __syncthreads();  // P of the chunk complete
+        if (ok) {
+            const int8_t *vblk = ring + sl * AM_STAGE_BYTES;
+            for (int tt = slice; tt < nc; tt += 16) {
+                const uint32_t w = *reinterpret_cast<const uint32_t *>(vblk + tt * QB_HD + word * 4);
+                const float vsc = vss[c0 + tt];
+                float f[4];
+                i8x4_to_f32(w, f[0], f[1], f[2], f[3]);
+                const float4 p03 = *reinterpret_cast<const float4 *>(P + tt * 8);
+                const float4 p47 = *reinterpret_cast<const float4 *>(P + tt * 8 + 4);
+                const float2 pp[4] = {make_float2(p03.x, p03.y), make_float2(p03.z, p03.w),
+                                      make_float2(p47.x, p47.y), make_float2(p47.z, p47.w)};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float vd = __fmul_rn(f[j], s);
-                const float2 vv = make_float2(vd, vd);
+                for (int j = 0; j < 4; ++j) {
+                    const float vd = __fmul_rn(f[j], vsc);
+                    const float2 vv = make_float2(vd, vd);
 #pragma unroll
-                for (int hp = 0; hp < 4; ++hp) acc[j][hp] = ffma2(pp[hp], vv, acc[j][hp]);
+                    for (int hp = 0; hp < 4; ++hp) acc[j][hp] = ffma2(pp[hp], vv, acc[j][hp]);
+                }
             }
         }
+        __syncthreads();  // every thread is done with this slot and with P
+        if (tid == 0 && ok && item + AM_SLOTS_RING < items) issue(item + AM_SLOTS_RING);
     }
-    // slices -> CTA partial [7][64] (slice order)
+
+    // ---------------- phase 4: slices -> CTA partial (slice order) -> rank 0
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int hp = 0; hp < 4; ++hp) {
             const int d = word * 4 + j;
-            part[(slice * 8 + 2 * hp) * 64 + d] = acc[j][hp].x;
-            part[(slice * 8 + 2 * hp + 1) * 64 + d] = acc[j][hp].y;
+            part[(slice * 8 + 2 * hp) * QB_HD + d] = acc[j][hp].x;
+            part[(slice * 8 + 2 * hp + 1) * QB_HD + d] = acc[j][hp].y;
         }
     __syncthreads();
-    for (int i = tid; i < 7 * 64; i += AC_THREADS) {
+    for (int i = tid; i < 7 * QB_HD; i += AM_THREADS) {
         const int h = i >> 6, d = i & 63;
         float sum = 0.f;
-        for (int sl = 0; sl < AC_SLICES; ++sl) sum += part[(sl * 8 + h) * 64 + d];
+        for (int sl2 = 0; sl2 < 16; ++sl2) sum += part[(sl2 * 8 + h) * QB_HD + d];
         ctxp[i] = sum;
     }
-    // ---------------- phase 4: rank 0 adds the partial contexts in rank order
     if constexpr (CLUSTER) {
         tc::cluster_sync();
         if (rank == 0) {
             const uint32_t ca = tc::smem_u32(ctxp);
-            for (int i4 = tid; i4 < 7 * 64 / 4; i4 += AC_THREADS) {
+            for (int i4 = tid; i4 < 7 * QB_HD / 4; i4 += AM_THREADS) {
                 float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int sr = 0; sr < nranks; ++sr) {
                     const float4 v = tc::ld_dsmem_f4(ca + 16u * i4, sr);
@@ -312,53 +416,55 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(AcArgs a) {
                     sum.w += v.w;
                 }
                 const int i = i4 * 4, h = i >> 6, d = i & 63;
-                uint16_t *o = a.ctx + (size_t)r * QB_HID + (g * 7 + h) * QB_HD + d;
-                o[0] = f2bf(sum.x);
-                o[1] = f2bf(sum.y);
-                o[2] = f2bf(sum.z);
-                o[3] = f2bf(sum.w);
+                uint2 o;
+                o.x = (uint32_t)f2bf(sum.x) | ((uint32_t)f2bf(sum.y) << 16);
+                o.y = (uint32_t)f2bf(sum.z) | ((uint32_t)f2bf(sum.w) << 16);
+                *reinterpret_cast<uint2 *>(a.ctx + (size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d) = o;
             }
         }
         tc::cluster_sync();  // peers' shared memory stays alive until rank 0 has read it
     } else {
         __syncthreads();
-        for (int i = tid; i < 7 * 64; i += AC_THREADS) {
+        for (int i = tid; i < 7 * QB_HD; i += AM_THREADS) {
             const int h = i >> 6, d = i & 63;
-            a.ctx[(size_t)r * QB_HID + (g * 7 + h) * QB_HD + d] = f2bf(ctxp[i]);
+            a.ctx[(size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d] = f2bf(ctxp[i]);
         }
     }
 }
 
-int attention_cluster_plan(int max_len, int *splits, int *kpc) {
-    if (max_len <= 0) return -1;
-    const int chunks = (max_len + AC_CHUNK - 1) / AC_CHUNK;
-    int s = (max_len + 1023) / 1024;
-    s = s < 1 ? 1 : (s > AC_MAX_SPLITS ? AC_MAX_SPLITS : s);
-    const int k = ((chunks + s - 1) / s) * AC_CHUNK;
-    if (k > AC_MAX_KPC) return -1;
-    *splits = s;
-    *kpc = k;
+// Splits: enough CTAs to fill the GPU once at two per SM, at least enough to
+// keep every CTA within AM_MAX_KPC keys, at most one 128-key chunk per CTA
+// and AM_MAX_SPLITS; no empty rank for the longest row.
+int attention_cluster_plan(int rows, int max_len, int *splits, int *kpc) {
+    if (max_len <= 0 || rows <= 0) return -1;
+    const int chunks = (max_len + AM_CHUNK - 1) / AM_CHUNK;
+    int s = AM_SLOTS / (2 * rows);
+    s = s < 1 ? 1 : (s > AM_MAX_SPLITS ? AM_MAX_SPLITS : s);
+    s = s > chunks ? chunks : s;
+    const int need = (max_len + AM_MAX_KPC - 1) / AM_MAX_KPC;
+    s = s < need ? need : s;
+    if (s > AM_MAX_SPLITS) return -1;
+    const int cpc = (chunks + s - 1) / s;  // chunks per CTA
+    *kpc = cpc * AM_CHUNK;
+    *splits = (chunks + cpc - 1) / cpc;
     return 0;
 }
 
 template <bool CLUSTER>
 static int run_ac(const AcArgs &a, int rows, int splits, cudaStream_t st) {
-    const int smem = ac_smem(a.kpc).total;
-    if (smem > 48 * 1024) {
-        static unsigned configured = 0;
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (!(configured & (1u << (dev & 31)))) {
-            if (cudaFuncSetAttribute(attn_cluster_kernel<CLUSTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     ac_smem(AC_MAX_KPC).total) != cudaSuccess)
-                return -3;
-            configured |= 1u << (dev & 31);
-        }
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << (dev & 31)))) {
+        if (cudaFuncSetAttribute(attn_cluster_kernel<CLUSTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ac_smem(AM_MAX_KPC).total) != cudaSuccess)
+            return -3;
+        configured |= 1u << (dev & 31);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(splits, QB_KVH, rows);
-    cfg.blockDim = dim3(AC_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.blockDim = dim3(AM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = ac_smem(a.kpc).total;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -371,12 +477,18 @@ static int run_ac(const AcArgs &a, int rows, int splits, cudaStream_t st) {
     return QB_LAUNCH_CHECK();
 }
 
+static __device__ unsigned g_attn_op_err;  // wait-timeout flag of calls that pass none
+
 int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions,
                              int max_len, const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap,
-                             uint16_t *ctx, cudaStream_t st) {
+                             uint16_t *ctx, unsigned *err, cudaStream_t st) {
     if (rows <= 0 || max_len > cap || rows > 65535) return -1;
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
+        return -1;  // 16-byte q loads and bulk copies of the code rows
+    if (reinterpret_cast<uintptr_t>(ctx) & 7) return -1;
     int splits, kpc;
-    if (attention_cluster_plan(max_len, &splits, &kpc)) return -1;
+    if (attention_cluster_plan(rows, max_len, &splits, &kpc)) return -1;
+    if (!err && cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_attn_op_err) != cudaSuccess) return -3;
     AcArgs a;
     a.q = q;
     a.slots = slots;
@@ -388,6 +500,7 @@ int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots,
     a.cap = cap;
     a.ctx = ctx;
     a.kpc = kpc;
+    a.err = err;
     return splits > 1 ? run_ac<true>(a, rows, splits, st) : run_ac<false>(a, rows, 1, st);
 }
 

@@ -62,6 +62,27 @@ __device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t b
     return v > bv || (v == bv && i > bi);
 }
 
+// Four int8 codes, bytes (b0, b1, b2, b3) of w -> two bf16x2 words (b0, b2)
+// and (b1, b3) (first element in the low half), exactly: with m = b & 0x7f and the sign
+// bit s = b & 0x80 of a two's-complement code b,
+//   bf16(0x4300 | m) - bf16(0x4300 | s) = (128 + m) - (128 + s) = b,
+// both operands and the difference being exact bf16 values.
+__device__ __forceinline__ uint32_t lop_or(uint32_t x, uint32_t mask, uint32_t bits) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(mask), "r"(bits));  // (x & mask) | bits
+    return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ void codes4_to_bf16(uint32_t w, uint32_t &k01, uint32_t &k23) {
+    const uint32_t w8 = w >> 8;
+    k01 = bf16x2_sub(lop_or(w, 0x007F007Fu, 0x43004300u), lop_or(w, 0x00800080u, 0x43004300u));
+    k23 = bf16x2_sub(lop_or(w8, 0x007F007Fu, 0x43004300u), lop_or(w8, 0x00800080u, 0x43004300u));
+}
+
 }  // namespace qb
 
 // Launch error helper used by the host-side launchers.

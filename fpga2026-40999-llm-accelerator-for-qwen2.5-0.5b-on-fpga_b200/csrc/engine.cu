@@ -346,7 +346,7 @@ int check_device_flags(qwen_b200 *h) {
     CK(cudaMemcpy(&flag, h->tc_ws, 4, cudaMemcpyDeviceToHost));
     if (flag) {
         cudaMemset(h->tc_ws, 0, 4);
-        return fail(h, QWEN_B200_ETIMEOUT, "a tensor-core pipeline wait timed out (code %u)", flag);
+        return fail(h, QWEN_B200_ETIMEOUT, "a pipeline wait on the device timed out (code %u)", flag);
     }
     return 0;
 }
@@ -400,7 +400,8 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         }
         {
             LaunchScope ls(h, 2, st, 1);
-            RK(launch_attention_cluster(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx, st));
+            RK(launch_attention_cluster(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx,
+                                        reinterpret_cast<unsigned *>(h->tc_ws), st));
         }
         if (dq) {
             CK(cudaMemcpyAsync(dq, h->q, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
@@ -1020,7 +1021,7 @@ int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint3
                                    const float *vscales, uint32_t capacity, uint16_t *ctx, void *stream) {
     if (!q || !slots || !positions || !kcodes || !kscales || !vcodes || !vscales || !ctx) return QWEN_B200_EINVAL;
     return launch_attention_cluster(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
-                                    (int)capacity, ctx, (cudaStream_t)stream);
+                                    (int)capacity, ctx, nullptr, (cudaStream_t)stream);
 }
 
 int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w_gu,

@@ -57,27 +57,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
 }
 
-// Four codes stored in the tiled layout's byte order (k0, k2, k1, k3) -> two
-// bf16x2 words (k0, k1), (k2, k3), exactly: with m = b & 0x7f and the sign
-// bit s = b & 0x80 of a two's-complement code b,
-//   bf16(0x4300 | m) - bf16(0x4300 | s) = (128 + m) - (128 + s) = b,
-// both operands and the difference being exact bf16 values.
-__device__ __forceinline__ uint32_t lop_or(uint32_t x, uint32_t mask, uint32_t bits) {
-    uint32_t r;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(mask), "r"(bits));  // (x & mask) | bits
-    return r;
-}
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-__device__ __forceinline__ void codes4_to_bf16(uint32_t w, uint32_t &k01, uint32_t &k23) {
-    const uint32_t w8 = w >> 8;
-    k01 = bf16x2_sub(lop_or(w, 0x007F007Fu, 0x43004300u), lop_or(w, 0x00800080u, 0x43004300u));
-    k23 = bf16x2_sub(lop_or(w8, 0x007F007Fu, 0x43004300u), lop_or(w8, 0x00800080u, 0x43004300u));
-}
-
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // Epilogue of 32 accumulators of output channel n: columns c0..c0+31 of the

@@ -51,10 +51,12 @@ int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const u
                      void *ws, size_t ws_bytes, int ws_rows, bool clear_counters, cudaStream_t st);
 
 // Single-launch attention: one thread-block cluster per (row, KV head) over
-// the row's context; no workspace. max_len <= 65536.
+// the row's context; no workspace. max_len <= 32768; q, kc, vc 16-byte and ctx
+// 8-byte aligned. A bounded wait that expires records code 11/12 in *err (a
+// library-internal flag when err is null).
 int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions,
                              int max_len, const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap,
-                             uint16_t *ctx, cudaStream_t st);
+                             uint16_t *ctx, unsigned *err, cudaStream_t st);
 
 int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t *x, cudaStream_t st);
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st);

@@ -232,9 +232,11 @@ int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint3
                                    uint32_t capacity, uint16_t *ctx, void *stream);
 /* The same attention in one launch with no workspace (the form the engine
  * uses): a thread-block cluster per (row, KV head) splits the context (up to
- * 8 CTAs), keeps the scores in shared memory, and exchanges the softmax
- * statistics and partial contexts over distributed shared memory; results are
- * independent of scheduling. max_len <= 65536. */
+ * 8 CTAs), keeps the scores in shared memory, runs both products on the
+ * tensor cores and exchanges the softmax statistics and partial contexts over
+ * distributed shared memory; results are independent of scheduling.
+ * max_len <= 32768 (the model's context limit); q, kcodes, vcodes 16-byte
+ * aligned, ctx 8-byte aligned (QWEN_B200_EINVAL otherwise). */
 int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
                                    uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
                                    const float *vscales, uint32_t capacity, uint16_t *ctx, void *stream);

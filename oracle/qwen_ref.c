@@ -422,21 +422,14 @@ void ref_kv8_quant(const float *x, unsigned rows, int8_t *codes, float *scales) 
     }
 }
 
-/* model_backend.py:97-102 for one (row, head): S = bf(q.k/8), causal mask
- * (keys 0..visible-1), P = bf(softmax(S)), ctx = bf(P.v). key/val read the
- * (dequantised) cache through their own views. */
+/* model_backend.py:97-102 for one (row, head) once the scores are known:
+ * P = bf(softmax(S)) over keys 0..visible-1 (causal mask), ctx = bf(P.v); val
+ * reads the (dequantised) cache through its view. */
 typedef float (*kv_at)(const void *view, unsigned t, unsigned d);
-static void attend(const float *q, unsigned visible, kv_at key, const void *kview, kv_at val, const void *vview,
-                   unsigned mode, float *out) {
-    float *scratch = (float *)malloc(visible * sizeof(float));
+static void attend_finish(float *scratch, unsigned visible, kv_at val, const void *vview, unsigned mode, float *out) {
     float mx = -INFINITY;
-    for (unsigned t = 0; t < visible; ++t) {
-        float acc = 0.0f;
-        for (unsigned d = 0; d < HD; ++d) acc = fmaf(q[d], key(kview, t, d), acc);
-        float s = bfm(acc / 8.0f, mode);
-        scratch[t] = s;
-        if (s > mx) mx = s;
-    }
+    for (unsigned t = 0; t < visible; ++t)
+        if (scratch[t] > mx) mx = scratch[t];
     float z = 0.0f;
     for (unsigned t = 0; t < visible; ++t) {
         scratch[t] = expf(scratch[t] - mx);
@@ -450,7 +443,45 @@ static void attend(const float *q, unsigned visible, kv_at key, const void *kvie
         for (unsigned d = 0; d < HD; ++d) acc[d] = fmaf(p, val(vview, t, d), acc[d]);
     }
     for (unsigned d = 0; d < HD; ++d) out[d] = bfm(acc[d], mode);
+}
+
+/* model_backend.py:97 with a cache read through a view: S = bf(q.k/8), the
+ * dot product an fp32 fma chain over d ascending. */
+static void attend(const float *q, unsigned visible, kv_at key, const void *kview, kv_at val, const void *vview,
+                   unsigned mode, float *out) {
+    float *scratch = (float *)malloc(visible * sizeof(float));
+    for (unsigned t = 0; t < visible; ++t) {
+        float acc = 0.0f;
+        for (unsigned d = 0; d < HD; ++d) acc = fmaf(q[d], key(kview, t, d), acc);
+        scratch[t] = bfm(acc / 8.0f, mode);
+    }
+    attend_finish(scratch, visible, val, vview, mode, out);
     free(scratch);
+}
+
+/* KV8 scores in the accelerator's order: the array sums q against the int8
+ * codes in block-aligned integers (src/rtl/kv8_v_pscale.sv:40-44, INT24
+ * accumulator normalised to the block maximum) and the per-token K scale
+ * multiplies the finished sum (src/rtl/kv8_score_scale8.sv:6-12). Restated
+ * with 28-bit alignment: E = the exponent of max|q| (max|q| in [2^E, 2^E+1)),
+ * Q[d] = rint(q[d] * 2^(26-E)) (|Q| < 2^27), dot = sum_d Q[d] * code[t][d]
+ * exactly (int64), and
+ *   S[t] = bf16(RN32(RN32(dot) * 2^(E-26) * kscale[t]) / 8).
+ * Exact integer sums make the result independent of summation order. */
+void ref_kv8_scores(const float *q, unsigned visible, const int8_t *kcodes, const float *kscales, unsigned mode,
+                    float *scores) {
+    float amax = 0.0f;
+    for (unsigned d = 0; d < HD; ++d)
+        if (fabsf(q[d]) > amax) amax = fabsf(q[d]);
+    const int e = amax > 0.0f ? ilogbf(amax) : 0;
+    int32_t qi[HD];
+    for (unsigned d = 0; d < HD; ++d) qi[d] = (int32_t)rintf(ldexpf(q[d], 26 - e));
+    for (unsigned t = 0; t < visible; ++t) {
+        int64_t acc = 0;
+        for (unsigned d = 0; d < HD; ++d) acc += (int64_t)qi[d] * kcodes[(size_t)t * HD + d];
+        const float dot = ldexpf((float)acc, e - 26);
+        scores[t] = bfm(dot * kscales[t] / 8.0f, mode);
+    }
 }
 
 /* KV8 view: codes [t][64], scales [t]; dequantised value = code * scale (fp32). */
@@ -472,10 +503,13 @@ void ref_attention_kv8(const float *q, unsigned rows, const uint32_t *positions,
 #pragma omp parallel for schedule(dynamic)
     for (long rh = 0; rh < (long)rows * QH; ++rh) {
         unsigned r = (unsigned)rh / QH, h = (unsigned)rh % QH, g = h / 7; /* repeat_interleave(7), :97-98 */
-        kv8_view kv = {kcodes + (size_t)g * capacity * HD, kscales + (size_t)g * capacity};
+        const unsigned visible = positions[r] + 1;
         kv8_view vv = {vcodes + (size_t)g * capacity * HD, vscales + (size_t)g * capacity};
-        attend(q + ((size_t)r * QH + h) * HD, positions[r] + 1, kv8_at, &kv, kv8_at, &vv, mode,
-               ctx + (size_t)r * HID + (size_t)h * HD);
+        float *scratch = (float *)malloc(visible * sizeof(float));
+        ref_kv8_scores(q + ((size_t)r * QH + h) * HD, visible, kcodes + (size_t)g * capacity * HD,
+                       kscales + (size_t)g * capacity, mode, scratch);
+        attend_finish(scratch, visible, kv8_at, &vv, mode, ctx + (size_t)r * HID + (size_t)h * HD);
+        free(scratch);
     }
 }
 

@@ -59,6 +59,7 @@ def lib():
             'ref_attention_kv8': (None, [_PF, ctypes.c_uint, _P32, _P8, _PF, _P8, _PF, ctypes.c_uint,
                                          ctypes.c_uint, _PF]),
             'ref_attention_bf16': (None, [_PF, ctypes.c_uint, _P32, _PF, _PF, ctypes.c_uint, _PF]),
+            'ref_kv8_scores': (None, [_PF, ctypes.c_uint, _P8, _PF, ctypes.c_uint, _PF]),
             'ref_swiglu': (None, [_PF, _PF, ctypes.c_uint, ctypes.c_uint, _PF]),
             'ref_lm_head': (c_uint32, [c_void_p, _PF, ctypes.c_uint, _PF]),
             'ref_fill_kv_synthetic': (c_int, [c_void_p, ctypes.c_uint, ctypes.c_uint64]),
@@ -240,6 +241,15 @@ def attention_kv8(q, positions, kcodes, kscales, vcodes, vscales, mode=0):
                             pf(f32(kscales)), p8(np.ascontiguousarray(vcodes)), pf(f32(vscales)), cap, mode,
                             pf(ctx))
     return ctx
+
+
+def kv8_scores(q, kcodes, kscales, mode=0):
+    """Scores of one query head q [64] against kcodes [t][64] / kscales [t]."""
+    q = f32(q).reshape(64)
+    kcodes = np.ascontiguousarray(kcodes, dtype=np.int8)
+    out = np.empty(kcodes.shape[0], dtype=np.float32)
+    lib().ref_kv8_scores(pf(q), kcodes.shape[0], p8(kcodes), pf(f32(kscales)), mode, pf(out))
+    return out
 
 
 def attention_bf16(q, positions, k, v, mode=0):
