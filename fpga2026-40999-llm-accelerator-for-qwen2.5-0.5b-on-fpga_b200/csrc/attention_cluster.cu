@@ -148,8 +148,11 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
     if (tid == 0) {
         for (int sl = 0; sl < AM_SLOTS_RING; ++sl) tc::mbar_init(&full[sl], 1);
         tc::mbar_fence_init();
-        for (int i = 0; i < min(items, AM_SLOTS_RING); ++i) issue(i);
     }
+    pdl_wait();  // q and the newest cache entries come from the preceding kernel
+    pdl_trigger();
+    if (tid == 0)
+        for (int i = 0; i < min(items, AM_SLOTS_RING); ++i) issue(i);
     for (int t = tid; t < nkeys; t += AM_THREADS) {
         kss[t] = __ldg(a.ks + kvbase + t);
         vss[t] = __ldg(a.vs + kvbase + t);
@@ -461,20 +464,8 @@ static int run_ac(const AcArgs &a, int rows, int splits, cudaStream_t st) {
             return -3;
         configured |= 1u << (dev & 31);
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(splits, QB_KVH, rows);
-    cfg.blockDim = dim3(AM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = ac_smem(a.kpc).total;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CLUSTER ? (unsigned)splits : 1u;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, attn_cluster_kernel<CLUSTER>, a) != cudaSuccess) return -3;
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(attn_cluster_kernel<CLUSTER>, dim3(splits, QB_KVH, rows), dim3(AM_THREADS),
+                      (size_t)ac_smem(a.kpc).total, st, CLUSTER ? (unsigned)splits : 1u, a);
 }
 
 static __device__ unsigned g_attn_op_err;  // wait-timeout flag of calls that pass none

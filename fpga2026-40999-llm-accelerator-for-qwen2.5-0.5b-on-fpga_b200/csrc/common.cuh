@@ -87,3 +87,81 @@ __device__ __forceinline__ void codes4_to_bf16(uint32_t w, uint32_t &k01, uint32
 
 // Launch error helper used by the host-side launchers.
 #define QB_LAUNCH_CHECK() (cudaGetLastError() == cudaSuccess ? 0 : -3)
+
+namespace qb {
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while the preceding kernel of its stream still
+// runs; pdl_wait() returns once that kernel has completed and its memory
+// operations are visible (a no-op without the launch attribute). Every
+// kernel of the decode chain calls it in every CTA before it reads anything
+// an earlier kernel wrote or writes anything an earlier kernel reads; only
+// loads of constant data (weights) may come first. pdl_trigger() lets the
+// next kernel of the stream launch (it still waits for this one to finish).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host side: a launch may overlap its predecessor only when that
+// predecessor is one of this library's kernels on the same stream, launched
+// inside the same PdlChain scope with nothing (copy, memset, event) enqueued
+// between them. A kernel that overlapped a copy could read the copy's
+// destination too early. Outside a PdlChain (the operator-level entry points)
+// every launch is ordinary.
+struct PdlState {
+    cudaStream_t st = nullptr;
+    int depth = 0;
+    bool prev_ours = false;
+};
+inline PdlState &pdl_state() {
+    static thread_local PdlState s;
+    return s;
+}
+struct PdlChain {
+    PdlChain() {
+        if (pdl_state().depth++ == 0) pdl_state().prev_ours = false;
+    }
+    ~PdlChain() {
+        if (--pdl_state().depth == 0) pdl_state().prev_ours = false;
+    }
+    PdlChain(const PdlChain &) = delete;
+    PdlChain &operator=(const PdlChain &) = delete;
+};
+// Call after enqueuing anything other than one of this library's kernels.
+inline void pdl_break() { pdl_state().prev_ours = false; }
+
+// Launches kernel<<<grid, block, smem, st>>>(args...) (with a cluster shape
+// when cluster_x > 1), with programmatic stream serialisation when the rules
+// above allow it.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      unsigned cluster_x, Args... args) {
+    PdlState &ps = pdl_state();
+    const bool overlap = ps.depth > 0 && ps.prev_ours && ps.st == st;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    unsigned na = 0;
+    if (overlap) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cluster_x > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = cluster_x;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    if (cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) != cudaSuccess) return -3;
+    if (ps.depth > 0) {
+        ps.prev_ours = true;
+        ps.st = st;
+    }
+    return QB_LAUNCH_CHECK();
+}
+}  // namespace qb

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "assets.h"
+#include "common.cuh"
 #include "kernels.h"
 #include "qwen_b200.h"
 
@@ -145,6 +146,7 @@ struct LaunchScope {
             pool.push_back(e);
         }
         cudaEventRecord(pool[h->prof_used[c]++], st);
+        pdl_break();
     }
 };
 
@@ -360,6 +362,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
     const int cap = (int)h->cfg.max_context;
     const float eps = h->cfg.rms_eps;
     const bool dump = h->dump_layer >= 0 && h->d_dump;
+    PdlChain chain;  // consecutive kernels of the forward overlap one another
     {
         LaunchScope ls(h, 0, st, 1);
         RK(launch_embed(h->embed, ids, n, h->x, st));
@@ -406,6 +409,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         if (dq) {
             CK(cudaMemcpyAsync(dq, h->q, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
             CK(cudaMemcpyAsync(dq + (size_t)n * 1152, h->ctx, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+            pdl_break();
         }
         {
             LaunchScope ls(h, 3, st, 1);
@@ -416,7 +420,10 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
                 RK(launch_gemv(EPI_RESIDUAL, h->ctx, n, HID, nullptr, 0.f, W.o, W.s_o, nullptr, HID, h->x, st));
             }
         }
-        if (dq) CK(cudaMemcpyAsync(dq + (size_t)n * 2048, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+        if (dq) {
+            CK(cudaMemcpyAsync(dq + (size_t)n * 2048, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+            pdl_break();
+        }
         if (n >= TC_MIN_ROWS) {
             {
                 LaunchScope ls(h, 4, st, 2);
@@ -438,6 +445,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         if (dq) {
             CK(cudaMemcpyAsync(dq + (size_t)n * 2944, h->mid, (size_t)n * FFN * 2, cudaMemcpyDeviceToDevice, st));
             CK(cudaMemcpyAsync(dq + (size_t)n * 7808, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
+            pdl_break();
         }
     }
     if (nlog > 0) {
@@ -748,6 +756,7 @@ static int enqueue_device_step(qwen_b200 *h, const uint32_t *d_in, int n, int ma
                                cudaStream_t st) {
     uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n;
     h->nlaunch = 0;
+    PdlChain chain;  // prologue, the layers and the epilogue overlap one another
     {
         LaunchScope ls(h, 7, st, 1);
         RK(launch_decode_prologue(d_in, n, h->slot_pos, ids, slots, positions, st));

@@ -486,7 +486,10 @@ int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8
     a.pi = am ? am->pi : nullptr;
     a.nblk = am ? am->nblk : 0;
     a.logits = am ? am->logits : nullptr;
-    if (clear && cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return -3;
+    if (clear) {
+        if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return -3;
+        pdl_break();
+    }
     return bn == 64 ? dispatch_epi<64>(epi, xmap, a, splits, st) : dispatch_epi<128>(epi, xmap, a, splits, st);
 }
 

@@ -53,21 +53,33 @@ __device__ __forceinline__ void load_x_tile(const uint16_t *__restrict__ x, int 
 }
 
 // One warp: acc[r][m] = sum_k xs[m][k] * W[n0 + r][k] for RW rows, MT tile rows.
-// Lane l owns 16-byte chunks l, l+32, ... of each weight row; every chunk of
-// the warp's rows is requested before any arithmetic (deep loads in flight).
-template <int K, int RW, int MT>
-__device__ __forceinline__ void gemv_tile(const int8_t *__restrict__ w, int n0, const uint32_t *xs,
-                                          float (&acc)[RW][MT]) {
-    constexpr int NCH = K / 16, CPL = (NCH + 31) / 32;
-    const int lane = threadIdx.x & 31;
+// Lane l owns 16-byte chunks l, l+32, ... of each weight row. gemv_load
+// requests every chunk of the warp's rows (deep loads in flight; weights are
+// constant, so this may precede pdl_wait), gemv_dot does the arithmetic.
+template <int K, int RW>
+struct GemvRows {
+    static constexpr int NCH = K / 16, CPL = (NCH + 31) / 32;
     uint4 wr[CPL][RW];
+};
+
+template <int K, int RW>
+__device__ __forceinline__ void gemv_load(const int8_t *__restrict__ w, int n0, bool active, GemvRows<K, RW> &g) {
+    constexpr int NCH = GemvRows<K, RW>::NCH, CPL = GemvRows<K, RW>::CPL;
+    const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
         const int ch = lane + 32 * c;
 #pragma unroll
         for (int r = 0; r < RW; ++r)
-            wr[c][r] = (ch < NCH) ? ldg_stream(w + (size_t)(n0 + r) * K + ch * 16) : make_uint4(0u, 0u, 0u, 0u);
+            g.wr[c][r] = (active && ch < NCH) ? ldg_stream(w + (size_t)(n0 + r) * K + ch * 16)
+                                             : make_uint4(0u, 0u, 0u, 0u);
     }
+}
+
+template <int K, int RW, int MT>
+__device__ __forceinline__ void gemv_dot(const GemvRows<K, RW> &g, const uint32_t *xs, float (&acc)[RW][MT]) {
+    constexpr int NCH = GemvRows<K, RW>::NCH, CPL = GemvRows<K, RW>::CPL;
+    const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int r = 0; r < RW; ++r)
 #pragma unroll
@@ -79,10 +91,10 @@ __device__ __forceinline__ void gemv_tile(const int8_t *__restrict__ w, int n0, 
             float wf[RW][16];
 #pragma unroll
             for (int r = 0; r < RW; ++r) {
-                i8x4_to_f32(wr[c][r].x, wf[r][0], wf[r][1], wf[r][2], wf[r][3]);
-                i8x4_to_f32(wr[c][r].y, wf[r][4], wf[r][5], wf[r][6], wf[r][7]);
-                i8x4_to_f32(wr[c][r].z, wf[r][8], wf[r][9], wf[r][10], wf[r][11]);
-                i8x4_to_f32(wr[c][r].w, wf[r][12], wf[r][13], wf[r][14], wf[r][15]);
+                i8x4_to_f32(g.wr[c][r].x, wf[r][0], wf[r][1], wf[r][2], wf[r][3]);
+                i8x4_to_f32(g.wr[c][r].y, wf[r][4], wf[r][5], wf[r][6], wf[r][7]);
+                i8x4_to_f32(g.wr[c][r].z, wf[r][8], wf[r][9], wf[r][10], wf[r][11]);
+                i8x4_to_f32(g.wr[c][r].w, wf[r][12], wf[r][13], wf[r][14], wf[r][15]);
             }
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
@@ -112,12 +124,16 @@ __global__ void __launch_bounds__(NW * 32) gemv_kernel(const uint16_t *__restric
     extern __shared__ __align__(16) uint32_t xs[];
     const int m0 = blockIdx.y * MT;
     const int mrows = min(MT, rows - m0);
-    load_x_tile<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = (blockIdx.x * NW + warp) * RW;
+    GemvRows<K, RW> g;
+    gemv_load<K, RW>(w, n0, n0 < n, g);
+    pdl_wait();
+    pdl_trigger();
+    load_x_tile<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xs);
     if (n0 >= n) return;
     float acc[RW][MT];
-    gemv_tile<K, RW, MT>(w, n0, xs, acc);
+    gemv_dot<K, RW, MT>(g, xs, acc);
     if constexpr (EPI == EPI_SWIGLU) {
         // rows n0+2p (gate j) and n0+2p+1 (up j): model_backend.py:105-106
         const int nh = n >> 1;
@@ -165,8 +181,8 @@ static int run_gemv(const uint16_t *x, int rows, const uint16_t *gamma, float ep
         }
     }
     dim3 grid((n + RW * NW - 1) / (RW * NW), (rows + MT - 1) / MT);
-    gemv_kernel<K, RW, NW, MT, EPI><<<grid, NW * 32, smem, st>>>(x, rows, gamma, eps, w, scale, bias, n, y);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(gemv_kernel<K, RW, NW, MT, EPI>, grid, dim3(NW * 32), smem, st, 1, x, rows, gamma, eps, w, scale,
+                      bias, n, y);
 }
 
 template <int K, int RW, int EPI>
@@ -215,15 +231,20 @@ __global__ void __launch_bounds__(256) qkv_kernel(QkvArgs a) {
     __shared__ float outs[MT][64];
     const int m0 = blockIdx.y * MT;
     const int mrows = min(MT, a.rows - m0);
-    load_x_tile<K, MT, 256>(a.x, m0, mrows, a.gamma, a.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hb = blockIdx.x;
+    GemvRows<K, 4> g[2];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) gemv_load<K, 4>(a.w, hb * 64 + warp * 8 + half * 4, true, g[half]);
+    pdl_wait();
+    pdl_trigger();
+    load_x_tile<K, MT, 256>(a.x, m0, mrows, a.gamma, a.eps, xs);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
         const int local = warp * 8 + half * 4;
         const int n0 = hb * 64 + local;
         float acc[4][MT];
-        gemv_tile<K, 4, MT>(a.w, n0, xs, acc);
+        gemv_dot<K, 4, MT>(g[half], xs, acc);
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -246,8 +267,7 @@ template <int MT>
 static int run_qkv(const QkvArgs &a, cudaStream_t st) {
     const size_t smem = (size_t)MT * QB_HID * 2;
     dim3 grid(QB_QH + 2 * QB_KVH, (a.rows + MT - 1) / MT);
-    qkv_kernel<MT><<<grid, 256, smem, st>>>(a);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(qkv_kernel<MT>, grid, dim3(256), smem, st, 1, a);
 }
 
 int launch_qkv(const QkvArgs &a, cudaStream_t st) {
@@ -274,9 +294,13 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
     __shared__ uint32_t bi[NW][MT];
     const int m0 = blockIdx.y * MT;
     const int mrows = min(MT, rows - m0);
-    load_x_tile<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = (blockIdx.x * NW + warp) * RW;
+    GemvRows<K, RW> g;
+    gemv_load<K, RW>(w, n0, n0 < vocab, g);
+    pdl_wait();
+    pdl_trigger();
+    load_x_tile<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xs);
     float best_v[MT];
     uint32_t best_i[MT];
 #pragma unroll
@@ -286,7 +310,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
     }
     if (n0 < vocab) {
         float acc[RW][MT];
-        gemv_tile<K, RW, MT>(w, n0, xs, acc);
+        gemv_dot<K, RW, MT>(g, xs, acc);
 #pragma unroll
         for (int r = 0; r < RW; ++r)
 #pragma unroll
@@ -325,6 +349,8 @@ __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float *pv, con
                                                             uint32_t *tokens) {
     __shared__ float sv[256];
     __shared__ uint32_t si[256];
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x;
     float v = -INFINITY;
     uint32_t i = 0;
@@ -350,8 +376,7 @@ __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float *pv, con
 }
 
 int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st) {
-    argmax_reduce_kernel<<<rows, 256, 0, st>>>(pv, pi, nblk, tokens);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens);
 }
 
 size_t lm_head_workspace(int rows, int vocab) {
@@ -364,8 +389,8 @@ static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps,
                   int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, cudaStream_t st) {
     const size_t smem = (size_t)MT * QB_HID * 2;
     dim3 grid(nblk, (rows + MT - 1) / MT);
-    lm_head_kernel<MT><<<grid, 256, smem, st>>>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(lm_head_kernel<MT>, grid, dim3(256), smem, st, 1, x, rows, gamma, eps, w, scale, vocab, logits,
+                      pv, pi, nblk);
 }
 
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
@@ -386,8 +411,7 @@ int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps
     else
         rc = run_lm<8>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
     if (rc) return rc;
-    argmax_reduce_kernel<<<rows, 256, 0, st>>>(pv, pi, nblk, tokens);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens);
 }
 
 }  // namespace qb

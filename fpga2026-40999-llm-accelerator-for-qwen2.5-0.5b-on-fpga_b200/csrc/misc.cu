@@ -10,6 +10,8 @@ namespace qb {
 // x[r] = embed[ids[r]] (src/software/main.c:114-125), 8 bf16 per thread.
 __global__ void embed_kernel(const uint16_t *__restrict__ embed, const uint32_t *__restrict__ ids, int rows,
                              uint16_t *__restrict__ x) {
+    pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x;
     const uint32_t id = ids[r];
     const uint4 *src = reinterpret_cast<const uint4 *>(embed + (size_t)id * QB_HID);
@@ -19,8 +21,7 @@ __global__ void embed_kernel(const uint16_t *__restrict__ embed, const uint32_t 
 
 int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t *x, cudaStream_t st) {
     if (rows <= 0) return -1;
-    embed_kernel<<<rows, 128, 0, st>>>(embed, ids, rows, x);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(embed_kernel, dim3(rows), dim3(128), 0, st, 1, embed, ids, rows, x);
 }
 
 // model_backend.py:69-71, one warp per row. The row and gamma are loaded into
@@ -30,6 +31,8 @@ constexpr int RMS_WORDS = QB_HID / 2 / 32;
 __global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict__ x,
                                                      const uint16_t *__restrict__ gamma, int rows, float eps,
                                                      uint16_t *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const uint32_t *xr = reinterpret_cast<const uint32_t *>(x + (size_t)row * QB_HID);
@@ -59,13 +62,14 @@ __global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict_
 
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st) {
     if (rows <= 0) return -1;
-    rmsnorm_kernel<<<(rows + 1) / 2, 64, 0, st>>>(x, gamma, rows, eps, out);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(rmsnorm_kernel, dim3((rows + 1) / 2), dim3(64), 0, st, 1, x, gamma, rows, eps, out);
 }
 
 // model_backend.py:73-78 in place on [rows][heads][64]; one warp per (row, head).
 __global__ void rope_kernel(uint16_t *x, int rows, int heads, const uint32_t *__restrict__ positions,
                             const float *__restrict__ table) {
+    pdl_wait();
+    pdl_trigger();
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (item >= rows * heads) return;
     const int r = item / heads;
@@ -92,6 +96,8 @@ int launch_rope(uint16_t *x, int rows, int heads, const uint32_t *positions, con
 // (row, kv head). scale = amax/127, code = clamp(rne(x/scale), +-127).
 __global__ void kv8_append_kernel(const uint16_t *__restrict__ kv, int rows, const uint32_t *__restrict__ slots,
                                   const uint32_t *__restrict__ positions, int8_t *codes, float *scales, int cap) {
+    pdl_wait();
+    pdl_trigger();
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (item >= rows * QB_KVH) return;
     const int r = item / QB_KVH, g = item % QB_KVH;
@@ -123,6 +129,8 @@ __global__ void rope_kv8_kernel(const uint16_t *__restrict__ qkv, int rows, cons
                                 const uint32_t *__restrict__ positions, const float *__restrict__ table,
                                 uint16_t *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs, int cap,
                                 uint16_t *kv_out) {
+    pdl_wait();
+    pdl_trigger();
     const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     constexpr int HB = QB_QH + 2 * QB_KVH;
     if (item >= rows * HB) return;
@@ -137,13 +145,14 @@ int launch_rope_kv8(const uint16_t *qkv, int rows, const uint32_t *slots, const 
                     uint16_t *kv_out, cudaStream_t st) {
     if (rows <= 0) return -1;
     const int items = rows * (QB_QH + 2 * QB_KVH);
-    rope_kv8_kernel<<<(items + 7) / 8, 256, 0, st>>>(qkv, rows, slots, positions, table, q_out, kc, ks, vc, vs, cap,
-                                                     kv_out);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(rope_kv8_kernel, dim3((items + 7) / 8), dim3(256), 0, st, 1, qkv, rows, slots, positions, table,
+                      q_out, kc, ks, vc, vs, cap, kv_out);
 }
 
 __global__ void gather_rows_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ idx,
                                    uint16_t *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x;
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)idx[r] * QB_HID);
     uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)r * QB_HID);
@@ -152,13 +161,14 @@ __global__ void gather_rows_kernel(const uint16_t *__restrict__ x, const uint32_
 
 int launch_gather_rows(const uint16_t *x, const uint32_t *rows_idx, int n, uint16_t *out, cudaStream_t st) {
     if (n <= 0) return -1;
-    gather_rows_kernel<<<n, 128, 0, st>>>(x, rows_idx, out);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(gather_rows_kernel, dim3(n), dim3(128), 0, st, 1, x, rows_idx, out);
 }
 
 __global__ void decode_prologue_kernel(const uint32_t *__restrict__ tokens_in, int n,
                                        const uint32_t *__restrict__ slot_pos, uint32_t *ids, uint32_t *slots,
                                        uint32_t *positions) {
+    pdl_wait();
+    pdl_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     ids[i] = tokens_in[i];
@@ -167,19 +177,20 @@ __global__ void decode_prologue_kernel(const uint32_t *__restrict__ tokens_in, i
 }
 
 __global__ void decode_epilogue_kernel(int n, uint32_t *slot_pos) {
+    pdl_wait();
+    pdl_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) slot_pos[i] += 1u;
 }
 
 int launch_decode_prologue(const uint32_t *tokens_in, int n, const uint32_t *slot_pos, uint32_t *ids,
                            uint32_t *slots, uint32_t *positions, cudaStream_t st) {
-    decode_prologue_kernel<<<(n + 127) / 128, 128, 0, st>>>(tokens_in, n, slot_pos, ids, slots, positions);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(decode_prologue_kernel, dim3((n + 127) / 128), dim3(128), 0, st, 1, tokens_in, n, slot_pos, ids,
+                      slots, positions);
 }
 
 int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st) {
-    decode_epilogue_kernel<<<(n + 127) / 128, 128, 0, st>>>(n, slot_pos);
-    return QB_LAUNCH_CHECK();
+    return launch_pdl(decode_epilogue_kernel, dim3((n + 127) / 128), dim3(128), 0, st, 1, n, slot_pos);
 }
 
 // Seeded synthetic KV8 entries: codes uniform in [-127, 127], scales in
