@@ -3,22 +3,26 @@
 // 128 output channels of a CTA tile fill the UMMA M dimension and the batch
 // rows (BN of them) the N dimension.
 //
-//   warp 0      TMA producer: the int8 weight tile [128][64] (8 KB, contiguous
-//               in the tiled layout [N/128][K/64][128][64]) by bulk copy into
-//               an 8-deep ring, and the activation tile [BN rows][64 k] bf16 by
-//               a 2D tensor-map load with 128-byte swizzle (zero fill past the
-//               last row)
+//   warp 0      producer: the int8 weight tile [128][64] (8 KB, contiguous in
+//               the tiled layout [N/128][K/64][128][64]) by bulk copy into its
+//               ring, and the activation tile [BN rows][64 k] bf16 by a 2D
+//               tensor-map load with 128-byte swizzle (zero fill past the last
+//               row) into a separate ring. Weights are constant, so the weight
+//               ring is filled before the programmatic-launch wait for the
+//               preceding kernel; activations are loaded after it.
 //   warp 1      owns TMEM (BN fp32 columns) and issues tcgen05.mma (one thread)
-//   warps 2..9  dequantise each weight tile (exact int8 -> bf16) from the ring
-//               into the 128-byte-swizzled K-major A stage; then the epilogue
-//               (tcgen05.ld of the accumulator, per-channel scale, bf16
-//               rounding points of model_backend.py:62-67, bias / residual /
-//               SiLU*mul / LM-head argmax)
-// Split-K: the CTAs of one output tile form a thread-block cluster. Each
-// writes its fp32 partial tile to its own shared memory; after a cluster
-// barrier every CTA reduces its share of the tile (32x32 units) by reading the
-// partials of all CTAs over distributed shared memory in rank order and runs
-// the epilogue on it. No global scratch, no atomics, deterministic.
+//   warps 2..9  dequantise each weight tile (exact int8 -> bf16) into the
+//               128-byte-swizzled K-major A stage; then the epilogue
+// Epilogue: the fp32 accumulator tile is written transposed ([BN][128]) into
+// the CTA's own shared memory (over the drained A/B stages). Split-K: the CTAs
+// of one output tile form a thread-block cluster, and after a cluster barrier
+// the 256 x splits epilogue threads of the cluster each take 4-channel items
+// of the tile, load that item from every CTA's shared memory at once over
+// distributed shared memory, add them in rank order and apply the epilogue
+// (per-channel scale and the bf16 rounding points of model_backend.py:62-67,
+// bias / residual / SiLU*mul) with vector loads and stores. The LM head
+// (argmax epilogue) never splits K and reduces (value, index) per row in the
+// CTA. No global scratch, no atomics, deterministic.
 // Every mbarrier wait is bounded: on timeout the kernel records an error code
 // in a device flag, skips its remaining work and still frees its TMEM.
 #include "common.cuh"
@@ -29,22 +33,36 @@ namespace qb {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;
-constexpr int TC_STAGES = 4;   // bf16 A / B stages consumed by the MMA
-constexpr int TC_WSTAGES = 8;  // int8 weight tiles in flight
 constexpr int TC_CONV = 256;                 // dequant / epilogue threads (warps 2..9)
 constexpr int TC_THREADS = 64 + TC_CONV;
 constexpr int TC_MAX_SPLITS = 8;
+// One CTA per SM. With two co-resident CTAs per SM (smaller rings) a stress
+// test of the 200-row SwiGLU shape returned a wrong 8-channel group (one
+// dequantising warp's rows of one tile) in about 1 run in 10; with one CTA
+// per SM it never did, whatever the ring depths.
+// Split planning counts 2 x 148 CTA slots (a second wave for the largest
+// tile counts).
+constexpr int TC_SLOTS = 2 * 148;
 
+// Shared memory: A (bf16 weights) | B (bf16 activations) | W (int8 weights)
+// rings | mbarriers | TMEM address | argmax partials (about 195 KB). The
+// accumulator tile [BN][128] fp32 of the epilogue reuses the A and B stages
+// once every MMA has completed.
 template <int BN>
 struct TcSmem {
+    static constexpr int A_STAGES = 4;
+    static constexpr int B_STAGES = BN == 64 ? 8 : 4;
+    static constexpr int W_STAGES = 8;
     static constexpr int W_BYTES = TC_BM * TC_BK;      // 8 KB int8 tile
     static constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB bf16 tile
     static constexpr int B_BYTES = BN * TC_BK * 2;
     static constexpr int A_OFF = 0;
-    static constexpr int B_OFF = A_OFF + TC_STAGES * A_BYTES;
-    static constexpr int W_OFF = B_OFF + TC_STAGES * B_BYTES;
-    static constexpr int BAR_OFF = W_OFF + TC_WSTAGES * W_BYTES;
-    static constexpr int NBARS = 3 * TC_STAGES + 2 * TC_WSTAGES + 2;
+    static constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
+    static constexpr int W_OFF = B_OFF + B_STAGES * B_BYTES;
+    static constexpr int TILE_BYTES = BN * TC_BM * 4;
+    static_assert(TILE_BYTES <= W_OFF, "accumulator tile must fit over the A and B stages");
+    static constexpr int BAR_OFF = W_OFF + W_STAGES * W_BYTES;
+    static constexpr int NBARS = 2 * A_STAGES + 2 * B_STAGES + 2 * W_STAGES + 2;
     static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8;
     static constexpr int RED_OFF = SLOT_OFF + 16;
     static constexpr int RED_BYTES = 4 * BN * 8;
@@ -133,15 +151,78 @@ __device__ __forceinline__ void tc_argmax_flush(const TcArgs &a, const uint8_t *
     }
 }
 
+// Item i of the transposed accumulator tile: batch row m = i / 32 of the
+// tile, channels 4*(i % 32) .. +3. The partial tiles of all `splits` CTAs of
+// the cluster are read at once and added in rank order, then the epilogue of
+// model_backend.py:62-67 runs on the four channels.
+template <int BN, int EPI>
+__device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int n0, uint32_t tile_saddr,
+                                             const float *tile) {
+    const int m = i >> 5, nl = 4 * (i & 31), n = n0 + nl, mg = m0 + m;
+    const bool valid = mg < a.M;
+    uint2 res = make_uint2(0u, 0u);
+    if (EPI == EPI_RESIDUAL && valid) res = *reinterpret_cast<const uint2 *>(a.y + (size_t)mg * a.N + n);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.splits > 1) {
+        const uint32_t addr = tile_saddr + (uint32_t)(m * TC_BM + nl) * 4u;
+        float4 part[TC_MAX_SPLITS];
+#pragma unroll
+        for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
+            if (sr < a.splits) part[sr] = tc::ld_dsmem_f4(addr, (uint32_t)sr);
+#pragma unroll
+        for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
+            if (sr < a.splits) {
+                v.x += part[sr].x;
+                v.y += part[sr].y;
+                v.z += part[sr].z;
+                v.w += part[sr].w;
+            }
+    } else {
+        const float4 p = *reinterpret_cast<const float4 *>(tile + m * TC_BM + nl);
+        v.x += p.x;
+        v.y += p.y;
+        v.z += p.z;
+        v.w += p.w;
+    }
+    if (!valid) return;
+    const float4 sc = *reinterpret_cast<const float4 *>(a.scale + n);
+    float o[4] = {rbf(rbf(v.x) * sc.x), rbf(rbf(v.y) * sc.y), rbf(rbf(v.z) * sc.z), rbf(rbf(v.w) * sc.w)};
+    if constexpr (EPI == EPI_SWIGLU) {
+        // channels 2j (gate j) and 2j+1 (up j): model_backend.py:105-106
+        const float s0 = o[0] / (1.0f + expf(-o[0])), s1 = o[2] / (1.0f + expf(-o[2]));
+        const uint32_t w = (uint32_t)f2bf(rbf(s0) * o[1]) | ((uint32_t)f2bf(rbf(s1) * o[3]) << 16);
+        *reinterpret_cast<uint32_t *>(a.y + (size_t)mg * (a.N >> 1) + (n >> 1)) = w;
+    } else {
+        if constexpr (EPI == EPI_BIAS) {
+            const uint2 b = *reinterpret_cast<const uint2 *>(a.bias + n);
+            o[0] = rbf(o[0] + bflo(b.x));
+            o[1] = rbf(o[1] + bfhi(b.x));
+            o[2] = rbf(o[2] + bflo(b.y));
+            o[3] = rbf(o[3] + bfhi(b.y));
+        }
+        if constexpr (EPI == EPI_RESIDUAL) {
+            o[0] = rbf(bflo(res.x) + o[0]);
+            o[1] = rbf(bfhi(res.x) + o[1]);
+            o[2] = rbf(bflo(res.y) + o[2]);
+            o[3] = rbf(bfhi(res.y) + o[3]);
+        }
+        uint2 w;
+        w.x = (uint32_t)f2bf(o[0]) | ((uint32_t)f2bf(o[1]) << 16);
+        w.y = (uint32_t)f2bf(o[2]) | ((uint32_t)f2bf(o[3]) << 16);
+        *reinterpret_cast<uint2 *>(a.y + (size_t)mg * a.N + n) = w;
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
     using L = TcSmem<BN>;
+    constexpr int AS = L::A_STAGES, BS = L::B_STAGES, WS = L::W_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-    uint64_t *full_a = bars, *full_b = bars + TC_STAGES, *empty = bars + 2 * TC_STAGES;
-    uint64_t *w_full = bars + 3 * TC_STAGES, *w_empty = w_full + TC_WSTAGES;
-    uint64_t *accum = w_empty + TC_WSTAGES, *done = accum + 1;
+    uint64_t *full_a = bars, *empty_a = full_a + AS, *full_b = empty_a + AS, *empty_b = full_b + BS;
+    uint64_t *w_full = empty_b + BS, *w_empty = w_full + WS;
+    uint64_t *accum = w_empty + WS, *done = accum + 1;
     uint32_t *slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = a.splits > 1 ? (int)tc::cluster_rank() : 0;
@@ -152,12 +233,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     const int nk = min(KC, kc0 + a.kc_per_split) - kc0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TC_STAGES; ++s) {
+        for (int s = 0; s < AS; ++s) {
             tc::mbar_init(&full_a[s], TC_CONV);
-            tc::mbar_init(&full_b[s], 1);
-            tc::mbar_init(&empty[s], 1);
+            tc::mbar_init(&empty_a[s], 1);
         }
-        for (int s = 0; s < TC_WSTAGES; ++s) {
+        for (int s = 0; s < BS; ++s) {
+            tc::mbar_init(&full_b[s], 1);
+            tc::mbar_init(&empty_b[s], 1);
+        }
+        for (int s = 0; s < WS; ++s) {
             tc::mbar_init(&w_full[s], 1);
             tc::mbar_init(&w_empty[s], TC_CONV);
         }
@@ -171,63 +255,71 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *slot;
+    pdl_trigger();
     bool ok = nk > 0;
 
     if (warp == 0) {
-        if (lane == 0 && ok) {
-            // weight tiles run up to TC_WSTAGES ahead; activation tiles follow
-            // the MMA's stage ring
+        if (lane == 0) {
             const int8_t *wsrc = a.w + ((size_t)n_tile * KC + kc0) * L::W_BYTES;
             int iw = 0, ib = 0;
-            while (ok && ib < nk) {
-                if (iw < nk && iw < ib + TC_WSTAGES) {
-                    const int s = iw % TC_WSTAGES, ph = (iw / TC_WSTAGES) & 1;
+            // weights are constant: fill the weight ring before waiting for the
+            // kernel that produces the activations
+            for (; ok && iw < min(nk, WS); ++iw) {
+                tc::mbar_arrive_expect_tx(&w_full[iw], (uint32_t)L::W_BYTES);
+                tc::bulk_load(smem + L::W_OFF + iw * L::W_BYTES, wsrc + (size_t)iw * L::W_BYTES, (uint32_t)L::W_BYTES,
+                              &w_full[iw]);
+            }
+            pdl_wait();
+            uint32_t idle = 0;
+            while (ok && (ib < nk || iw < nk)) {
+                bool progress = false;
+                if (ib < nk) {
+                    const int s = ib % BS, ph = (ib / BS) & 1;
+                    if (tc::mbar_try_wait(&empty_b[s], ph ^ 1)) {
+                        tc::mbar_arrive_expect_tx(&full_b[s], (uint32_t)L::B_BYTES);
+                        tc::tma_load_2d(smem + L::B_OFF + s * L::B_BYTES, &xmap, &full_b[s], (kc0 + ib) * TC_BK, m0);
+                        ++ib;
+                        progress = true;
+                    }
+                }
+                if (iw < nk) {
+                    const int s = iw % WS, ph = (iw / WS) & 1;
                     if (tc::mbar_try_wait(&w_empty[s], ph ^ 1)) {
                         tc::mbar_arrive_expect_tx(&w_full[s], (uint32_t)L::W_BYTES);
                         tc::bulk_load(smem + L::W_OFF + s * L::W_BYTES, wsrc + (size_t)iw * L::W_BYTES,
                                       (uint32_t)L::W_BYTES, &w_full[s]);
                         ++iw;
-                        continue;
+                        progress = true;
                     }
                 }
-                const int s = ib % TC_STAGES, ph = (ib / TC_STAGES) & 1;
-                if (ib < iw || iw == nk) {
-                    if (!tc::mbar_wait(&empty[s], ph ^ 1, a.err, 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::mbar_arrive_expect_tx(&full_b[s], (uint32_t)L::B_BYTES);
-                    tc::tma_load_2d(smem + L::B_OFF + s * L::B_BYTES, &xmap, &full_b[s], (kc0 + ib) * TC_BK, m0);
-                    ++ib;
-                } else if (!tc::mbar_wait(&w_empty[iw % TC_WSTAGES], ((iw / TC_WSTAGES) & 1) ^ 1, a.err, 7)) {
+                if (progress) {
+                    idle = 0;
+                } else if (++idle > (1u << 21)) {
+                    atomicExch(a.err, 1u);
                     ok = false;
-                    break;
                 }
             }
-            while (ok && iw < nk) {
-                const int s = iw % TC_WSTAGES, ph = (iw / TC_WSTAGES) & 1;
-                if (!tc::mbar_wait(&w_empty[s], ph ^ 1, a.err, 7)) break;
-                tc::mbar_arrive_expect_tx(&w_full[s], (uint32_t)L::W_BYTES);
-                tc::bulk_load(smem + L::W_OFF + s * L::W_BYTES, wsrc + (size_t)iw * L::W_BYTES,
-                              (uint32_t)L::W_BYTES, &w_full[s]);
-                ++iw;
-            }
+        } else {
+            pdl_wait();
         }
     } else if (warp == 1) {
+        pdl_wait();
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_BM, BN);
             int i = 0;
             for (; ok && i < nk; ++i) {
-                const int s = i % TC_STAGES, ph = (i / TC_STAGES) & 1;
-                if (!tc::mbar_wait(&full_a[s], ph, a.err, 2) || !tc::mbar_wait(&full_b[s], ph, a.err, 3)) break;
+                const int sa = i % AS, pa = (i / AS) & 1;
+                const int sb = i % BS, pb = (i / BS) & 1;
+                if (!tc::mbar_wait(&full_a[sa], pa, a.err, 2) || !tc::mbar_wait(&full_b[sb], pb, a.err, 3)) break;
                 tc::tc_fence_after();
-                const uint32_t ab = tc::smem_u32(smem + L::A_OFF + s * L::A_BYTES);
-                const uint32_t bb = tc::smem_u32(smem + L::B_OFF + s * L::B_BYTES);
+                const uint32_t ab = tc::smem_u32(smem + L::A_OFF + sa * L::A_BYTES);
+                const uint32_t bb = tc::smem_u32(smem + L::B_OFF + sb * L::B_BYTES);
 #pragma unroll
                 for (int j = 0; j < TC_BK / 16; ++j)
                     tc::mma_bf16(tmem, tc::smem_desc_sw128(ab + 32 * j), tc::smem_desc_sw128(bb + 32 * j), idesc,
                                  i > 0 || j > 0);
-                tc::mma_commit(&empty[s]);
+                tc::mma_commit(&empty_a[sa]);
+                tc::mma_commit(&empty_b[sb]);
             }
             if (i == nk && ok) tc::mma_commit(accum);
             // all MMAs issued by this thread have finished before TMEM is freed
@@ -240,12 +332,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         const int ct = threadIdx.x - 64;
         constexpr int ITEMS = TC_BM * TC_BK / 16 / TC_CONV;  // 16-byte pieces per thread per tile
         for (int i = 0; ok && i < nk; ++i) {
-            const int s = i % TC_STAGES, ph = (i / TC_STAGES) & 1;
-            const int sw = i % TC_WSTAGES, phw = (i / TC_WSTAGES) & 1;
-            if (!tc::mbar_wait(&w_full[sw], phw, a.err, 8) || !tc::mbar_wait(&empty[s], ph ^ 1, a.err, 5)) {
+            const int s = i % AS, ph = (i / AS) & 1;
+            const int sw = i % WS, phw = (i / WS) & 1;
+            if (!tc::mbar_wait(&w_full[sw], phw, a.err, 8) || !tc::mbar_wait(&empty_a[s], ph ^ 1, a.err, 5)) {
                 ok = false;
                 break;
             }
+            // the tensor core's reads of this A stage (async proxy) are ordered
+            // before the generic-proxy stores that refill it
+            tc::fence_proxy_async_smem();
             const uint4 *src = reinterpret_cast<const uint4 *>(smem + L::W_OFF + sw * L::W_BYTES);
             uint4 wv[ITEMS];
 #pragma unroll
@@ -254,6 +349,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             uint8_t *dst = smem + L::A_OFF + s * L::A_BYTES;
 #pragma unroll
             for (int j = 0; j < ITEMS; ++j) {
+                // the tiled layout stores codes in the byte order (k0, k2, k1,
+                // k3), which codes4_to_bf16 unpacks to (k0, k1), (k2, k3)
                 const int item = ct + TC_CONV * j, row = item >> 2, piece = item & 3;
                 const int c0 = (2 * piece) ^ (row & 7), c1 = (2 * piece + 1) ^ (row & 7);
                 uint4 lo, hi;
@@ -267,35 +364,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&full_a[s]);
         }
-        // ---------------- epilogue: this thread owns output channel n and
-        // half of the tile's columns (two warps per TMEM lane quarter)
+        pdl_wait();  // residual rows and outputs of the preceding kernel
+        // ---------------- epilogue: this thread owns output channel n (TMEM
+        // lane) and half of the tile's columns (two warps per lane quarter)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         constexpr int HALF = BN / 2;
         const int cbeg = ((warp - 2) >> 2) * HALF;
         ok = ok && tc::mbar_wait(accum, 0, a.err, 6);
         tc::tc_fence_after();
-        if (a.splits > 1) {
-            // this warp's 32 x HALF block of the fp32 partial tile -> own shared
-            // memory (the A stages are free once the accumulator is complete),
-            // 16-byte groups rotated by lane to spread shared-memory banks
-            float *part = reinterpret_cast<float *>(smem + L::A_OFF);
-            const int unit = ((warp - 2) >> 2) * 4 + q;  // half * 4 + lane quarter
-#pragma unroll 1
-            for (int c = 0; c < HALF; c += 32) {
-                float v[32];
-                if (ok) {
-                    tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cbeg + c), v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-                }
-                float *row = part + ((size_t)(unit * 32 + lane) * HALF + c);
-#pragma unroll
-                for (int g = 0; g < 8; ++g)
-                    *reinterpret_cast<float4 *>(row + 4 * ((g + lane) & 7)) =
-                        make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-            }
-        } else {
+        tc::fence_proxy_async_smem();  // A/B stages (async-proxy traffic) become the generic accumulator tile
+        if constexpr (EPI == EPI_ARGMAX) {
             const int n = n0 + q * 32 + lane;
 #pragma unroll 1
             for (int c = cbeg; c < cbeg + HALF; c += 32) {
@@ -308,52 +386,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 }
                 tc_epilogue32<BN, EPI>(a, v, n, m0, c, q, lane, smem + L::RED_OFF);
             }
-            if constexpr (EPI == EPI_ARGMAX) {
-                epi_bar();
-                tc_argmax_flush<BN>(a, smem + L::RED_OFF, m0, n_tile, ct);
+            epi_bar();
+            tc_argmax_flush<BN>(a, smem + L::RED_OFF, m0, n_tile, ct);
+        } else {
+            // accumulator -> tile[m][n] (fp32), lanes on consecutive channels
+            float *tile = reinterpret_cast<float *>(smem + L::A_OFF);
+#pragma unroll 1
+            for (int c = 0; c < HALF; c += 32) {
+                float v[32];
+                if (ok) {
+                    tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cbeg + c), v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) tile[(cbeg + c + j) * TC_BM + q * 32 + lane] = v[j];
             }
         }
     }
-    if (EPI != EPI_ARGMAX && a.splits > 1) {  // the LM head (argmax) never splits K
-        tc::cluster_sync();  // every partial tile of the cluster is in shared memory
+    if constexpr (EPI != EPI_ARGMAX) {
+        // every partial tile of the cluster is complete in shared memory
+        if (a.splits > 1)
+            tc::cluster_sync();
+        else
+            __syncthreads();
         if (warp >= 2) {
-            // unit u = (half, quarter) of the tile is reduced by CTA u % splits,
-            // warp 2 + u / splits; sources are added in rank order
-            const int j = warp - 2;
-            const int u = j * a.splits + split;
-            if (u < 8) {
-                const int uq = u & 3, uhalf = u >> 2;
-                const int n = n0 + uq * 32 + lane;
-                constexpr int HALF = BN / 2;
-                const float *part = reinterpret_cast<const float *>(smem + L::A_OFF);
-#pragma unroll 1
-                for (int c = 0; c < HALF; c += 32) {
-                    const uint32_t row =
-                        tc::smem_u32(part + ((size_t)(u * 32 + lane) * HALF + c));
-                    float v[32];
-#pragma unroll
-                    for (int k = 0; k < 32; ++k) v[k] = 0.f;
-                    for (int sr = 0; sr < a.splits; ++sr) {
-#pragma unroll
-                        for (int h = 0; h < 8; h += 4) {
-                            float4 g4[4];
-#pragma unroll
-                            for (int g = 0; g < 4; ++g)
-                                g4[g] = tc::ld_dsmem_f4(row + 16u * ((h + g + lane) & 7), sr);
-#pragma unroll
-                            for (int g = 0; g < 4; ++g) {
-                                v[4 * (h + g)] += g4[g].x;
-                                v[4 * (h + g) + 1] += g4[g].y;
-                                v[4 * (h + g) + 2] += g4[g].z;
-                                v[4 * (h + g) + 3] += g4[g].w;
-                            }
-                        }
-                    }
-                    tc_epilogue32<BN, EPI>(a, v, n, m0, uhalf * HALF + c, uq, lane, smem + L::RED_OFF);
-                }
-            }
+            const float *tile = reinterpret_cast<const float *>(smem + L::A_OFF);
+            const uint32_t tsa = tc::smem_u32(tile);
+            for (int i = split * TC_CONV + (threadIdx.x - 64); i < BN * (TC_BM / 4); i += a.splits * TC_CONV)
+                tc_epilogue4<BN, EPI>(a, i, m0, n0, tsa, tile);
         }
-        tc::cluster_sync();  // no CTA leaves while another may still read its shared memory
+        if (a.splits > 1) tc::cluster_sync();  // no CTA leaves while another may still read its tile
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -405,11 +469,13 @@ size_t tc_gemm_workspace(int rows, int n, int splits) {
     return 256;
 }
 
+// Splits of K so that the tiles fill TC_SLOTS CTA slots, with at least two k
+// chunks per split and no empty split.
 int tc_pick_splits(int rows, int n, int k) {
     const int bn = tc_bn_for_rows(rows);
     const int tiles = (n / TC_BM) * ((rows + bn - 1) / bn);
     const int kc = k / TC_BK;
-    int s = (148 + tiles - 1) / tiles;
+    int s = TC_SLOTS / tiles;
     s = s < 1 ? 1 : s;
     s = s > TC_MAX_SPLITS ? TC_MAX_SPLITS : s;
     s = s > kc / 2 ? kc / 2 : s;  // at least two k chunks per split
@@ -430,20 +496,9 @@ static int run_tc(const CUtensorMap &map, TcArgs &a, int splits, cudaStream_t st
             return -3;
         configured |= 1u << (dev & 31);
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.N / TC_BM) * splits, 1, (a.M + BN - 1) / BN);
-    cfg.blockDim = dim3(TC_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = L::ALLOC;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)splits;  // the split CTAs of a tile share one cluster
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI>, map, a) != cudaSuccess) return -3;
-    return QB_LAUNCH_CHECK();
+    // the split CTAs of a tile share one cluster
+    return launch_pdl(tc_gemm_kernel<BN, EPI>, dim3((a.N / TC_BM) * splits, 1, (a.M + BN - 1) / BN),
+                      dim3(TC_THREADS), (size_t)L::ALLOC, st, (unsigned)splits, map, a);
 }
 
 template <int BN>
@@ -463,6 +518,10 @@ int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8
                    const TcArgmax *am, cudaStream_t st) {
     if (rows <= 0 || n % TC_BM || k % TC_BK || splits < 1 || splits > k / TC_BK || splits > TC_MAX_SPLITS) return -1;
     if (epi == EPI_ARGMAX && (!am || splits != 1)) return -1;
+    // vector loads and stores of the epilogue: 4 scales, 4 bias / output values
+    if ((reinterpret_cast<uintptr_t>(scale) & 15) || (reinterpret_cast<uintptr_t>(bias) & 7) ||
+        (reinterpret_cast<uintptr_t>(y) & 7))
+        return -1;
     if (ws_bytes < tc_gemm_workspace(rows, n, splits)) return -1;
     const int bn = tc_bn_for_rows(rows);
     const int kc = k / TC_BK;
