@@ -159,11 +159,8 @@ def dist_setup():
 def max_over_ranks(value, world):
     if world == 1:
         return value
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device='cuda')
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from qwen_b200.distributed import reduce_over_ranks
+    return reduce_over_ranks(value, 'max')
 
 
 def barrier(world):
