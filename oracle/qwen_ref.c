@@ -327,6 +327,40 @@ static void accum_t(const float *x, unsigned rows, unsigned K, const int8_t *wt,
     }
 }
 
+/* Projection sums in the accelerator's order (REF_EXACT). The RTL GEMM array
+ * multiplies block-aligned activation mantissas by the int8 codes and sums
+ * them as integers (src/rtl/qwen_gemm_array_i.sv header: INT24 segment sums
+ * with a block exponent). Restated with one 28-bit alignment per activation
+ * row: E = exponent of max|x[r][:]| (max in [2^E, 2^E+1)),
+ * X[k] = rint(x[r][k] * 2^(26-E)) (|X| < 2^27), the dot product with the
+ * codes is exact (int64), and acc = RN32(dot) * 2^(E-26). Exact integer sums
+ * make the result independent of summation order and of how K is split. */
+static int align_row(const float *xr, unsigned K, int32_t *X) {
+    float amax = 0.0f;
+    for (unsigned k = 0; k < K; ++k)
+        if (fabsf(xr[k]) > amax) amax = fabsf(xr[k]);
+    const int e = amax > 0.0f ? ilogbf(amax) : 0;
+    for (unsigned k = 0; k < K; ++k) X[k] = (int32_t)rintf(ldexpf(xr[k], 26 - e));
+    return e;
+}
+static void accum_exact(const float *x, unsigned rows, unsigned K, const int8_t *w, int transposed, unsigned N,
+                        float *acc) {
+    for (unsigned r = 0; r < rows; ++r) {
+        int32_t *X = (int32_t *)malloc(K * sizeof(int32_t));
+        const int e = align_row(x + (size_t)r * K, K, X);
+#pragma omp parallel for schedule(static)
+        for (long n = 0; n < (long)N; ++n) {
+            int64_t s = 0;
+            if (transposed)
+                for (unsigned k = 0; k < K; ++k) s += (int64_t)X[k] * w[(size_t)k * N + n];
+            else
+                for (unsigned k = 0; k < K; ++k) s += (int64_t)X[k] * w[(size_t)n * K + k];
+            acc[(size_t)r * N + n] = ldexpf((float)s, e - 26);
+        }
+        free(X);
+    }
+}
+
 /* Same sums from a row-major weight w[n][k] (operator-level entry). */
 static void accum_rowmajor(const float *x, unsigned rows, unsigned K, const int8_t *w, unsigned N, float *acc) {
 #pragma omp parallel for schedule(static)
@@ -355,15 +389,29 @@ static void epi_bias(float *acc, unsigned rows, unsigned N, const float *scale, 
     }
 }
 
+/* Raw sums of a projection from the transposed weight wt[k][n]. */
+static void accum(const float *x, unsigned rows, unsigned K, const int8_t *wt, unsigned N, float *acc, unsigned mode) {
+    if (mode & REF_EXACT)
+        accum_exact(x, rows, K, wt, 1, N, acc);
+    else
+        accum_t(x, rows, K, wt, N, acc);
+}
+
 void ref_linear(const float *x, unsigned rows, unsigned k, const int8_t *w, const float *scale, unsigned n,
                 unsigned mode, float *out) {
-    accum_rowmajor(x, rows, k, w, n, out);
+    if (mode & REF_EXACT)
+        accum_exact(x, rows, k, w, 0, n, out);
+    else
+        accum_rowmajor(x, rows, k, w, n, out);
     epi_linear(out, rows, n, scale, mode);
 }
 
 void ref_linear_bias(const float *x, unsigned rows, unsigned k, const int8_t *w, const float *scale,
                      const float *bias, unsigned n, unsigned mode, float *out) {
-    accum_rowmajor(x, rows, k, w, n, out);
+    if (mode & REF_EXACT)
+        accum_exact(x, rows, k, w, 0, n, out);
+    else
+        accum_rowmajor(x, rows, k, w, n, out);
     epi_bias(out, rows, n, scale, bias, mode);
 }
 
@@ -545,7 +593,7 @@ uint32_t ref_lm_head(const ref_model *m, const float *x, unsigned mode, float *l
     float h[HID];
     ref_rmsnorm(x, 1, m->gamma + 43008, eps_of(mode), mode, h);
     float *acc = (float *)malloc((size_t)VOC * sizeof(float));
-    accum_t(h, 1, HID, m->lmt, VOC, acc);
+    accum(h, 1, HID, m->lmt, VOC, acc, mode);
     const float *s = m->scale + 304128;
     float *pre = (float *)malloc((size_t)VOC * sizeof(float));
     for (unsigned n = 0; n < VOC; ++n) {
@@ -618,11 +666,11 @@ int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned posit
         const float *bias = m->bias + (size_t)l * QKV;
         ref_rmsnorm(x, rows, m->gamma + (size_t)l * 1792, eps, mode, h);
         /* q, k, v projections with bias (model_backend.py:91-93) */
-        accum_t(h, rows, HID, m->wt[l][PQ], 896, q);
+        accum(h, rows, HID, m->wt[l][PQ], 896, q, mode);
         epi_bias(q, rows, 896, sc + P_SCALE[PQ], bias, mode);
-        accum_t(h, rows, HID, m->wt[l][PK], 128, k);
+        accum(h, rows, HID, m->wt[l][PK], 128, k, mode);
         epi_bias(k, rows, 128, sc + P_SCALE[PK], bias + 896, mode);
-        accum_t(h, rows, HID, m->wt[l][PV], 128, v);
+        accum(h, rows, HID, m->wt[l][PV], 128, v, mode);
         epi_bias(v, rows, 128, sc + P_SCALE[PV], bias + 1024, mode);
         rope_rows(q, rows, QH, pos, m->rope, mode, q);
         rope_rows(k, rows, KVH, pos, m->rope, mode, k);
@@ -654,19 +702,19 @@ int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned posit
             if (m->dctx) memcpy(m->dctx, ctx, (size_t)rows * HID * sizeof(float));
         }
         /* O projection + residual (model_backend.py:103) */
-        accum_t(ctx, rows, HID, m->wt[l][PO], HID, tmp);
+        accum(ctx, rows, HID, m->wt[l][PO], HID, tmp, mode);
         epi_linear(tmp, rows, HID, sc + P_SCALE[PO], mode);
         for (size_t i = 0; i < (size_t)rows * HID; ++i) x[i] = bfm(x[i] + tmp[i], mode);
         if (l == m->dump_layer && m->dh) memcpy(m->dh, x, (size_t)rows * HID * sizeof(float));
         /* FFN (model_backend.py:104-107) */
         ref_rmsnorm(x, rows, m->gamma + (size_t)l * 1792 + 896, eps, mode, h);
         float *gate = gu, *up = gu + (size_t)rows * FFN;
-        accum_t(h, rows, HID, m->wt[l][PG], FFN, gate);
+        accum(h, rows, HID, m->wt[l][PG], FFN, gate, mode);
         epi_linear(gate, rows, FFN, sc + P_SCALE[PG], mode);
-        accum_t(h, rows, HID, m->wt[l][PU], FFN, up);
+        accum(h, rows, HID, m->wt[l][PU], FFN, up, mode);
         epi_linear(up, rows, FFN, sc + P_SCALE[PU], mode);
         ref_swiglu(gate, up, rows * FFN, mode, mid);
-        accum_t(mid, rows, FFN, m->wt[l][PD], HID, tmp);
+        accum(mid, rows, FFN, m->wt[l][PD], HID, tmp, mode);
         epi_linear(tmp, rows, HID, sc + P_SCALE[PD], mode);
         for (size_t i = 0; i < (size_t)rows * HID; ++i) x[i] = bfm(x[i] + tmp[i], mode);
         if (l == m->dump_layer) {

@@ -12,7 +12,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB = HERE / '_build' / 'libqwen_ref.so'
 
-KV8, RND8, FUSED_BIAS, CSR_EPS, ARGMAX_F32 = 1, 2, 4, 8, 16
+KV8, RND8, FUSED_BIAS, CSR_EPS, ARGMAX_F32, EXACT = 1, 2, 4, 8, 16, 32
 VOCAB = 151936
 
 _P8 = POINTER(ctypes.c_int8)
