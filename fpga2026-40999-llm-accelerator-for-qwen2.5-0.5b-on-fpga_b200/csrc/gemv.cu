@@ -1,58 +1,173 @@
 // W8A16 GEMV-family kernels for small row counts (decode): int8 weights are
-// streamed from HBM with 16-byte non-allocating loads, dequantised in registers
-// and multiplied with a bf16 activation tile held in shared memory; fp32
-// accumulation, per-output-channel scale in the epilogue.
+// streamed from HBM with 16-byte non-allocating loads and multiplied, as
+// integers, with the activation rows held in shared memory as int8 limbs.
 //
-// Arithmetic contract (legacy_100mhz_closed/src/PC/model_backend.py:62-67):
-//   y = bf16(bf16(sum_k x[k] * code[n][k]) * scale[n])   (+ bias / residual)
-// Every product bf16 x int8 is exact in fp32; only the summation order differs
-// from a sequential sum (per lane in k order, then a fixed butterfly).
+// Arithmetic contract (legacy_100mhz_closed/src/PC/model_backend.py:62-67,
+// with the projection sums in the accelerator's order, oracle REF_EXACT):
+//   E   = exponent of max|x[m][:]|, X[k] = rint(x[m][k] * 2^(26-E))
+//   acc = RN32(sum_k X[k] * code[n][k]) * 2^(E-26)   (exact integer sum)
+//   y   = bf16(bf16(acc) * scale[n])   (+ bias / residual / SiLU*mul)
+// X is held as four signed 7-bit limbs (X = L0 + 2^7 L1 + 2^14 L2 + 2^21 L3);
+// dp4a multiplies four codes by four limb bytes at a time, the limb sums fold
+// in int64 and the lanes' partial sums are added exactly, so the result does
+// not depend on how the sum is split.
 #include "common.cuh"
 #include "kernels.h"
 #include "qkv_epi.cuh"
 
 namespace qb {
 
-// Loads rows [m0, m0+mrows) of x [rows][K] (bf16) into xs [MT][K] (zero rows
-// beyond mrows); with gamma != nullptr applies RMSNorm in place:
-// bf16(bf16(x * 1/sqrt(mean(x^2) + eps)) * gamma) (model_backend.py:69-71).
-template <int K, int MT, int NT>
-__device__ __forceinline__ void load_x_tile(const uint16_t *__restrict__ x, int m0, int mrows,
-                                            const uint16_t *__restrict__ gamma, float eps, uint32_t *xs) {
-    constexpr int V = K / 8;
-    for (int i = threadIdx.x; i < MT * V; i += NT) {
-        const int m = i / V, c = i - m * V;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (m < mrows) v = *reinterpret_cast<const uint4 *>(x + (size_t)(m0 + m) * K + c * 8);
-        reinterpret_cast<uint4 *>(xs)[i] = v;
-    }
-    __syncthreads();
-    if (gamma != nullptr) {
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int m = warp; m < mrows; m += NT / 32) {
-            uint32_t *row = xs + m * (K / 2);
-            float ss = 0.f;
-            for (int i = lane; i < K / 2; i += 32) {
-                const uint32_t w = row[i];
-                const float a = bflo(w), b = bfhi(w);
-                ss += a * a;
-                ss += b * b;
-            }
-            ss = warp_sum(ss);
-            const float rs = 1.0f / sqrtf(ss / (float)K + eps);
-            for (int i = lane; i < K / 2; i += 32) {
-                const uint32_t w = row[i];
-                const uint32_t gw = reinterpret_cast<const uint32_t *>(gamma)[i];
-                const float a = rbf(rbf(bflo(w) * rs) * bflo(gw));
-                const float b = rbf(rbf(bfhi(w) * rs) * bfhi(gw));
-                row[i] = (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
-            }
-        }
-        __syncthreads();
-    }
+// q -> four signed 7-bit limbs, q = l0 + 2^7 l1 + 2^14 l2 + 2^21 l3 (|q| < 2^27).
+__device__ __forceinline__ void limbs4(int q, int (&l)[4]) {
+    l[0] = ((q + 64) & 127) - 64;
+    const int r1 = (q - l[0]) >> 7;
+    l[1] = ((r1 + 64) & 127) - 64;
+    const int r2 = (r1 - l[1]) >> 7;
+    l[2] = ((r2 + 64) & 127) - 64;
+    l[3] = (r2 - l[2]) >> 7;
 }
 
-// One warp: acc[r][m] = sum_k xs[m][k] * W[n0 + r][k] for RW rows, MT tile rows.
+__device__ __forceinline__ uint32_t limb_bytes(const int (&la)[4], const int (&lb)[4], int l) {
+    return ((uint32_t)la[l] & 0xffu) | (((uint32_t)lb[l] & 0xffu) << 8);
+}
+
+// Rows [m0, m0+mrows) of x [rows][K] (bf16) as int8 limb planes
+// xl[m][limb][k] of the row's 28-bit alignment and its exponent ex[m] (zero
+// rows beyond mrows); with gamma != nullptr the row is RMSNormed first:
+// bf16(bf16(x * 1/sqrt(mean(x^2) + eps)) * gamma) (model_backend.py:69-71),
+// the sum of squares in the same order as rmsnorm_kernel. All warps work on
+// each row: for K = 896 every warp loads the whole row into registers (so
+// every warp forms the same sum and maximum) and converts its share of the
+// words; wider rows are split across the warps, the maximum meeting in
+// shared memory.
+template <int K, int MT, int NT>
+__device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int m0, int mrows,
+                                             const uint16_t *__restrict__ gamma, float eps, int8_t *xl, int *ex) {
+    constexpr int NWARP = NT / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float wmax[NWARP];
+    for (int m = 0; m < MT; ++m) {
+        int8_t *row = xl + (size_t)m * 4 * K;
+        if (m >= mrows) {
+            for (int i = threadIdx.x; i < K / 4; i += NT)
+#pragma unroll
+                for (int l = 0; l < 4; ++l) reinterpret_cast<uint32_t *>(row + l * K)[i] = 0u;
+            if (threadIdx.x == 0) ex[m] = 0;
+            continue;
+        }
+        if constexpr (K == QB_HID) {
+            // 14 words (28 values) per lane: words lane + 32 j
+            constexpr int NWD = K / 2 / 32;
+            const uint32_t *xr = reinterpret_cast<const uint32_t *>(x + (size_t)(m0 + m) * K);
+            uint32_t xv[NWD];
+#pragma unroll
+            for (int j = 0; j < NWD; ++j) xv[j] = xr[lane + 32 * j];
+            float a[NWD], b[NWD];
+            if (gamma != nullptr) {
+                const uint32_t *g32 = reinterpret_cast<const uint32_t *>(gamma);
+                uint32_t gv[NWD];
+#pragma unroll
+                for (int j = 0; j < NWD; ++j) gv[j] = __ldg(g32 + lane + 32 * j);
+                float ss = 0.f;
+#pragma unroll
+                for (int j = 0; j < NWD; ++j) {
+                    const float p = bflo(xv[j]), q = bfhi(xv[j]);
+                    ss += p * p;
+                    ss += q * q;
+                }
+                ss = warp_sum(ss);
+                const float rs = 1.0f / sqrtf(ss / (float)K + eps);
+#pragma unroll
+                for (int j = 0; j < NWD; ++j) {
+                    a[j] = rbf(rbf(bflo(xv[j]) * rs) * bflo(gv[j]));
+                    b[j] = rbf(rbf(bfhi(xv[j]) * rs) * bfhi(gv[j]));
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < NWD; ++j) {
+                    a[j] = bflo(xv[j]);
+                    b[j] = bfhi(xv[j]);
+                }
+            }
+            float amax = 0.f;
+#pragma unroll
+            for (int j = 0; j < NWD; ++j) amax = fmaxf(amax, fmaxf(fabsf(a[j]), fabsf(b[j])));
+            amax = warp_max(amax);
+            const int e = amax > 0.f ? ilogbf(amax) : 0;
+#pragma unroll
+            for (int j = 0; j < NWD; ++j) {
+                if (j % NWARP != warp) continue;
+                int la[4], lb[4];
+                limbs4(__float2int_rn(ldexpf(a[j], 26 - e)), la);
+                limbs4(__float2int_rn(ldexpf(b[j], 26 - e)), lb);
+                const int i = lane + 32 * j;
+#pragma unroll
+                for (int l = 0; l < 4; ++l)
+                    *reinterpret_cast<uint16_t *>(row + l * K + 2 * i) = (uint16_t)limb_bytes(la, lb, l);
+            }
+            if (threadIdx.x == 0) ex[m] = e;
+        } else {
+            // 16-byte pieces threadIdx.x + NT j (8 values each); no RMSNorm here
+            constexpr int NPC = K / 8, NP = (NPC + NT - 1) / NT;
+            const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)(m0 + m) * K);
+            uint4 xv[NP];
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const int p = threadIdx.x + NT * j;
+                xv[j] = p < NPC ? xr[p] : make_uint4(0u, 0u, 0u, 0u);
+            }
+            float amax = 0.f;
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) amax = fmaxf(amax, fmaxf(fabsf(bflo(w[t])), fabsf(bfhi(w[t]))));
+            }
+            amax = warp_max(amax);
+            if (lane == 0) wmax[warp] = amax;
+            __syncthreads();
+            amax = wmax[0];
+#pragma unroll
+            for (int w2 = 1; w2 < NWARP; ++w2) amax = fmaxf(amax, wmax[w2]);
+            __syncthreads();  // wmax is reused by the next row
+            const int e = amax > 0.f ? ilogbf(amax) : 0;
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const int p = threadIdx.x + NT * j;
+                if (p >= NPC) continue;
+                const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+                uint32_t pk[4][2];  // [limb][byte quad]
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    int la[4], lb[4];
+                    limbs4(__float2int_rn(ldexpf(bflo(w[t]), 26 - e)), la);
+                    limbs4(__float2int_rn(ldexpf(bfhi(w[t]), 26 - e)), lb);
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) {
+                        const uint32_t two = limb_bytes(la, lb, l);
+                        if (t & 1)
+                            pk[l][t >> 1] |= two << 16;
+                        else
+                            pk[l][t >> 1] = two;
+                    }
+                }
+#pragma unroll
+                for (int l = 0; l < 4; ++l)
+                    *reinterpret_cast<uint2 *>(row + l * K + 8 * p) = make_uint2(pk[l][0], pk[l][1]);
+            }
+            if (threadIdx.x == 0) ex[m] = e;
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ long long warp_sum_ll(long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One warp: the dot products of RW weight rows with MT activation rows.
 // Lane l owns 16-byte chunks l, l+32, ... of each weight row. gemv_load
 // requests every chunk of the warp's rows (deep loads in flight; weights are
 // constant, so this may precede pdl_wait), gemv_dot does the arithmetic.
@@ -76,44 +191,49 @@ __device__ __forceinline__ void gemv_load(const int8_t *__restrict__ w, int n0, 
     }
 }
 
+// acc[r][m] = RN32(sum_k X_m[k] * W[n0 + r][k]) * 2^(ex[m] - 26), exact sum.
 template <int K, int RW, int MT>
-__device__ __forceinline__ void gemv_dot(const GemvRows<K, RW> &g, const uint32_t *xs, float (&acc)[RW][MT]) {
+__device__ __forceinline__ void gemv_dot(const GemvRows<K, RW> &g, const int8_t *xl, const int *ex,
+                                         float (&acc)[RW][MT]) {
     constexpr int NCH = GemvRows<K, RW>::NCH, CPL = GemvRows<K, RW>::CPL;
     const int lane = threadIdx.x & 31;
+    int d[RW][MT][4];
 #pragma unroll
     for (int r = 0; r < RW; ++r)
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+            for (int l = 0; l < 4; ++l) d[r][m][l] = 0;
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
         const int ch = lane + 32 * c;
         if (ch < NCH) {
-            float wf[RW][16];
 #pragma unroll
-            for (int r = 0; r < RW; ++r) {
-                i8x4_to_f32(g.wr[c][r].x, wf[r][0], wf[r][1], wf[r][2], wf[r][3]);
-                i8x4_to_f32(g.wr[c][r].y, wf[r][4], wf[r][5], wf[r][6], wf[r][7]);
-                i8x4_to_f32(g.wr[c][r].z, wf[r][8], wf[r][9], wf[r][10], wf[r][11]);
-                i8x4_to_f32(g.wr[c][r].w, wf[r][12], wf[r][13], wf[r][14], wf[r][15]);
-            }
+            for (int m = 0; m < MT; ++m)
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const uint4 *xp = reinterpret_cast<const uint4 *>(xs + m * (K / 2) + ch * 8);
-                const uint4 a0 = xp[0], a1 = xp[1];
-                const float xf[16] = {bflo(a0.x), bfhi(a0.x), bflo(a0.y), bfhi(a0.y), bflo(a0.z), bfhi(a0.z),
-                                      bflo(a0.w), bfhi(a0.w), bflo(a1.x), bfhi(a1.x), bflo(a1.y), bfhi(a1.y),
-                                      bflo(a1.z), bfhi(a1.z), bflo(a1.w), bfhi(a1.w)};
+                for (int l = 0; l < 4; ++l) {
+                    const uint4 xw = *reinterpret_cast<const uint4 *>(xl + (size_t)(m * 4 + l) * K + ch * 16);
 #pragma unroll
-                for (int r = 0; r < RW; ++r)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[r][m] = fmaf(xf[j], wf[r][j], acc[r][m]);
-            }
+                    for (int r = 0; r < RW; ++r) {
+                        int t = d[r][m][l];
+                        t = __dp4a((int)g.wr[c][r].x, (int)xw.x, t);
+                        t = __dp4a((int)g.wr[c][r].y, (int)xw.y, t);
+                        t = __dp4a((int)g.wr[c][r].z, (int)xw.z, t);
+                        t = __dp4a((int)g.wr[c][r].w, (int)xw.w, t);
+                        d[r][m][l] = t;
+                    }
+                }
         }
     }
 #pragma unroll
     for (int r = 0; r < RW; ++r)
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
+        for (int m = 0; m < MT; ++m) {
+            long long v = (long long)d[r][m][0] + ((long long)d[r][m][1] << 7) + ((long long)d[r][m][2] << 14) +
+                          ((long long)d[r][m][3] << 21);
+            v = warp_sum_ll(v);
+            acc[r][m] = ldexpf(__ll2float_rn(v), ex[m] - 26);
+        }
 }
 
 template <int K, int RW, int NW, int MT, int EPI>
@@ -121,7 +241,9 @@ __global__ void __launch_bounds__(NW * 32) gemv_kernel(const uint16_t *__restric
                                                        const uint16_t *__restrict__ gamma, float eps,
                                                        const int8_t *__restrict__ w, const float *__restrict__ scale,
                                                        const uint16_t *__restrict__ bias, int n, uint16_t *y) {
-    extern __shared__ __align__(16) uint32_t xs[];
+    extern __shared__ __align__(16) uint8_t gsm[];
+    int8_t *xl = reinterpret_cast<int8_t *>(gsm);
+    int *ex = reinterpret_cast<int *>(gsm + MT * 4 * K);
     const int m0 = blockIdx.y * MT;
     const int mrows = min(MT, rows - m0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,10 +252,10 @@ __global__ void __launch_bounds__(NW * 32) gemv_kernel(const uint16_t *__restric
     gemv_load<K, RW>(w, n0, n0 < n, g);
     pdl_wait();
     pdl_trigger();
-    load_x_tile<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xs);
+    load_x_limbs<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xl, ex);
     if (n0 >= n) return;
     float acc[RW][MT];
-    gemv_dot<K, RW, MT>(g, xs, acc);
+    gemv_dot<K, RW, MT>(g, xl, ex, acc);
     if constexpr (EPI == EPI_SWIGLU) {
         // rows n0+2p (gate j) and n0+2p+1 (up j): model_backend.py:105-106
         const int nh = n >> 1;
@@ -167,7 +289,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_kernel(const uint16_t *__restric
 template <int K, int RW, int NW, int MT, int EPI>
 static int run_gemv(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
                     const float *scale, const uint16_t *bias, int n, uint16_t *y, cudaStream_t st) {
-    const size_t smem = (size_t)MT * K * 2;
+    const size_t smem = (size_t)MT * (4 * K + 4);
     if (smem > 48 * 1024) {
         // The opt-in is per device; remember it per device ordinal.
         static unsigned configured = 0;
@@ -190,8 +312,7 @@ static int dispatch_mt(const uint16_t *x, int rows, const uint16_t *gamma, float
                        const float *scale, const uint16_t *bias, int n, uint16_t *y, cudaStream_t st) {
     if (rows <= 1) return run_gemv<K, RW, 8, 1, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
     if (rows <= 2) return run_gemv<K, RW, 8, 2, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
-    if (rows <= 4) return run_gemv<K, RW, 8, 4, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
-    return run_gemv<K, RW, 8, 8, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
+    return run_gemv<K, RW, 8, 4, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);  // 4-row tiles
 }
 
 int launch_gemv(int epi, const uint16_t *x, int rows, int k, const uint16_t *gamma, float eps, const int8_t *w,
@@ -227,7 +348,9 @@ int launch_gemv(int epi, const uint16_t *x, int rows, int k, const uint16_t *gam
 template <int MT>
 __global__ void __launch_bounds__(256) qkv_kernel(QkvArgs a) {
     constexpr int K = QB_HID;
-    extern __shared__ __align__(16) uint32_t xs[];
+    extern __shared__ __align__(16) uint8_t gsm[];
+    int8_t *xl = reinterpret_cast<int8_t *>(gsm);
+    int *ex = reinterpret_cast<int *>(gsm + MT * 4 * K);
     __shared__ float outs[MT][64];
     const int m0 = blockIdx.y * MT;
     const int mrows = min(MT, a.rows - m0);
@@ -238,13 +361,13 @@ __global__ void __launch_bounds__(256) qkv_kernel(QkvArgs a) {
     for (int half = 0; half < 2; ++half) gemv_load<K, 4>(a.w, hb * 64 + warp * 8 + half * 4, true, g[half]);
     pdl_wait();
     pdl_trigger();
-    load_x_tile<K, MT, 256>(a.x, m0, mrows, a.gamma, a.eps, xs);
+    load_x_limbs<K, MT, 256>(a.x, m0, mrows, a.gamma, a.eps, xl, ex);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
         const int local = warp * 8 + half * 4;
         const int n0 = hb * 64 + local;
         float acc[4][MT];
-        gemv_dot<K, 4, MT>(g[half], xs, acc);
+        gemv_dot<K, 4, MT>(g[half], xl, ex, acc);
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -265,7 +388,7 @@ __global__ void __launch_bounds__(256) qkv_kernel(QkvArgs a) {
 
 template <int MT>
 static int run_qkv(const QkvArgs &a, cudaStream_t st) {
-    const size_t smem = (size_t)MT * QB_HID * 2;
+    const size_t smem = (size_t)MT * (4 * QB_HID + 4);
     dim3 grid(QB_QH + 2 * QB_KVH, (a.rows + MT - 1) / MT);
     return launch_pdl(qkv_kernel<MT>, grid, dim3(256), smem, st, 1, a);
 }
@@ -274,8 +397,7 @@ int launch_qkv(const QkvArgs &a, cudaStream_t st) {
     if (a.rows <= 0) return -1;
     if (a.rows <= 1) return run_qkv<1>(a, st);
     if (a.rows <= 2) return run_qkv<2>(a, st);
-    if (a.rows <= 4) return run_qkv<4>(a, st);
-    return run_qkv<8>(a, st);
+    return run_qkv<4>(a, st);  // 4-row tiles
 }
 
 // ------------------------------------------------------------- LM head + argmax
@@ -289,7 +411,9 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
                                                       int vocab, uint16_t *logits, float *pv, uint32_t *pi,
                                                       int nblk) {
     constexpr int K = QB_HID, RW = 4, NW = 8;
-    extern __shared__ __align__(16) uint32_t xs[];
+    extern __shared__ __align__(16) uint8_t gsm[];
+    int8_t *xl = reinterpret_cast<int8_t *>(gsm);
+    int *ex = reinterpret_cast<int *>(gsm + MT * 4 * K);
     __shared__ float bv[NW][MT];
     __shared__ uint32_t bi[NW][MT];
     const int m0 = blockIdx.y * MT;
@@ -300,7 +424,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
     gemv_load<K, RW>(w, n0, n0 < vocab, g);
     pdl_wait();
     pdl_trigger();
-    load_x_tile<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xs);
+    load_x_limbs<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xl, ex);
     float best_v[MT];
     uint32_t best_i[MT];
 #pragma unroll
@@ -310,7 +434,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
     }
     if (n0 < vocab) {
         float acc[RW][MT];
-        gemv_dot<K, RW, MT>(g, xs, acc);
+        gemv_dot<K, RW, MT>(g, xl, ex, acc);
 #pragma unroll
         for (int r = 0; r < RW; ++r)
 #pragma unroll
@@ -387,7 +511,7 @@ size_t lm_head_workspace(int rows, int vocab) {
 template <int MT>
 static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w, const float *scale,
                   int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, cudaStream_t st) {
-    const size_t smem = (size_t)MT * QB_HID * 2;
+    const size_t smem = (size_t)MT * (4 * QB_HID + 4);
     dim3 grid(nblk, (rows + MT - 1) / MT);
     return launch_pdl(lm_head_kernel<MT>, grid, dim3(256), smem, st, 1, x, rows, gamma, eps, w, scale, vocab, logits,
                       pv, pi, nblk);
@@ -406,10 +530,8 @@ int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps
         rc = run_lm<1>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
     else if (rows <= 2)
         rc = run_lm<2>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
-    else if (rows <= 4)
-        rc = run_lm<4>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
     else
-        rc = run_lm<8>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
+        rc = run_lm<4>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);  // 4-row tiles
     if (rc) return rc;
     return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens);
 }

@@ -80,16 +80,13 @@ def test_gemm_w8a16(k, n, rows, epi):
         assert L().qwen_b200_op_gemm_w8a16(*args, bias, vp(yd), stream()) == 0
     sync()
     got = from_bits(host(yd).view(np.uint16))
-    lin = None
+    # projection sums are exact integers (oracle REF_EXACT): bit-identical
     if epi == 'residual':
-        lin = ref.linear(x, w, s)
+        lin = ref.linear(x, w, s, mode=ref.EXACT)
         exp = ref.f32(np.vectorize(lambda a: ref.lib().ref_bf(a, 0))(y0 + lin))
     else:
-        exp = ref.linear(x, w, s, bias=b if epi == 'bias' else None)
-    # residual: a third rounding after a sum that may cancel -> 3 ulps of the
-    # larger of the output and the added linear term
-    assert_bf16_close(got, exp, max_ulps=3 if epi == 'residual' else 2, mag=lin,
-                      what=f'gemm {k}x{n} rows {rows} {epi}')
+        exp = ref.linear(x, w, s, bias=b if epi == 'bias' else None, mode=ref.EXACT)
+    assert np.array_equal(got, exp), f'gemm {k}x{n} rows {rows} {epi}: {np.mean(got == exp):.5f} bit-equal'
 
 
 @pytest.mark.parametrize('rows', [1, 5, 16])
@@ -109,7 +106,8 @@ def test_swiglu(rows):
                                    ctypes.c_float(1e-6), keep((wgu)), keep((sgu)), vp(mid), stream()) == 0
     sync()
     z = ref.rmsnorm(x, g)
-    exp = ref.swiglu(ref.linear(z, wg, sg), ref.linear(z, wu, su))
+    exp = ref.swiglu(ref.linear(z, wg, sg, mode=ref.EXACT), ref.linear(z, wu, su, mode=ref.EXACT))
+    # exact projections; the RMSNorm's fp32 sum of squares runs in another order
     assert_bf16_close(from_bits(host(mid).view(np.uint16)), exp, max_ulps=2, what='swiglu')
 
 
@@ -259,7 +257,7 @@ def test_qkv_fused_against_oracle_chain():
                                 keep(rope_table(cap)), vp(q), vp(kc), vp(ks), vp(vc), vp(vs), cap, stream()) == 0
     sync()
     h = ref.rmsnorm(x, g)
-    y = ref.linear(h, w, s, bias=b)
+    y = ref.linear(h, w, s, bias=b, mode=ref.EXACT)
     eq = ref.rope(y[:, :896].reshape(rows, 14, 64), positions).reshape(rows, 896)
     ek = ref.rope(y[:, 896:1024].reshape(rows, 2, 64), positions)
     ev = y[:, 1024:].reshape(rows, 2, 64)
@@ -276,7 +274,7 @@ def test_qkv_fused_against_oracle_chain():
 
 
 def lm_oracle(x, g, w, s):
-    logits = ref.linear(ref.rmsnorm(x, g), w, s)
+    logits = ref.linear(ref.rmsnorm(x, g), w, s, mode=ref.EXACT)
     toks = [int(len(row) - 1 - np.argmax(row[::-1])) for row in logits]  # highest index on ties
     return logits, toks
 
