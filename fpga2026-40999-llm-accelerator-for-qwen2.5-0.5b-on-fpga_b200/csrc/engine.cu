@@ -31,7 +31,7 @@ constexpr int CSR_IDS = 256;  // ACT_IN rows addressable through the embedding c
 
 struct LayerW {
     int8_t *qkv, *o, *gu, *d;  // [1152][896], [896][896], [9728][896] gate/up interleaved, [896][4864]
-    int8_t *tqkv, *to, *tgu, *td;  // the same weights tiled [n/128][k/64][128][64] for the tensor-core GEMM
+    CUtensorMap mqkv, mo, mgu, md;  // tensor maps of the same weights for the tensor-core GEMM
     float *s_qkv, *s_o, *s_gu, *s_d;
     uint16_t *bias, *g_attn, *g_ffn;
 };
@@ -53,7 +53,8 @@ struct qwen_b200 {
     // model
     LayerW L[NL];
     uint16_t *g_final = nullptr, *embed = nullptr;
-    int8_t *lmw = nullptr, *tlmw = nullptr;
+    int8_t *lmw = nullptr;
+    CUtensorMap mlm;
     float *s_lm = nullptr, *rope = nullptr;
     // KV8 caches: codes [layer][slot][2][cap][64], scales [layer][slot][2][cap]
     int8_t *kc = nullptr, *vc = nullptr;
@@ -61,9 +62,15 @@ struct qwen_b200 {
     // activations
     uint16_t *x = nullptr, *q = nullptr, *ctx = nullptr, *mid = nullptr, *xl = nullptr, *logits = nullptr;
     uint16_t *hn = nullptr, *qkvb = nullptr;  // normalised rows / q|k|v rows of the tensor-core path
-    void *tc_ws = nullptr;                    // error flag | tile counters | split-K partials
+    void *tc_ws = nullptr;                    // error flags of the bounded waits
     size_t tc_ws_bytes = 0;
-    std::map<std::tuple<const void *, int, int>, CUtensorMap> maps;  // (buffer, rows, k)
+    // activation rows as int8 limb planes [4][R][4864] and row exponents [R]
+    // (operand of the tensor-core projections), with their tensor maps for
+    // k = 896 and k = 4864
+    int8_t *limbs = nullptr;
+    int *lex = nullptr;
+    size_t limb_plane = 0;
+    CUtensorMap lmap_hid, lmap_ffn;
     uint32_t *meta = nullptr;  // [4][R]: ids | slots | positions | logit rows
     uint32_t *tokens = nullptr, *slot_pos = nullptr;
     void *lm_ws = nullptr;
@@ -176,13 +183,11 @@ int allocate(qwen_b200 *h) {
         h->L[l].gu = h->L[l].o + (size_t)HID * HID;
         h->L[l].d = h->L[l].gu + (size_t)2 * FFN * HID;
     }
-    if ((rc = dalloc(h, &p, lw * NL))) return rc;
     for (int l = 0; l < NL; ++l) {
-        int8_t *b = (int8_t *)p + lw * l;
-        h->L[l].tqkv = b;
-        h->L[l].to = b + (size_t)QKVN * HID;
-        h->L[l].tgu = h->L[l].to + (size_t)HID * HID;
-        h->L[l].td = h->L[l].tgu + (size_t)2 * FFN * HID;
+        LayerW &W = h->L[l];
+        if (make_weight_map(&W.mqkv, W.qkv, QKVN, HID) || make_weight_map(&W.mo, W.o, HID, HID) ||
+            make_weight_map(&W.mgu, W.gu, 2 * FFN, HID) || make_weight_map(&W.md, W.d, HID, FFN))
+            return fail(h, QWEN_B200_EDEVICE, "cannot encode the weight tensor maps");
     }
     const size_t ls = QKVN + HID + 2 * FFN + HID;
     if ((rc = dalloc(h, &p, ls * NL * sizeof(float)))) return rc;
@@ -204,7 +209,7 @@ int allocate(qwen_b200 *h) {
     h->g_final = (uint16_t *)p + lb * NL;
     if ((rc = dalloc(h, (void **)&h->embed, (size_t)VOC * HID * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->lmw, (size_t)VOC * HID))) return rc;
-    if ((rc = dalloc(h, (void **)&h->tlmw, (size_t)VOC * HID))) return rc;
+    if (make_weight_map(&h->mlm, h->lmw, VOC, HID)) return fail(h, QWEN_B200_EDEVICE, "cannot encode the LM-head map");
     if ((rc = dalloc(h, (void **)&h->s_lm, (size_t)VOC * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->rope, (size_t)c.max_context * 64 * 4))) return rc;
     // KV8 caches
@@ -224,6 +229,12 @@ int allocate(qwen_b200 *h) {
     if ((rc = dalloc(h, (void **)&h->xl, R * HID * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->hn, R * HID * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->qkvb, R * QKVN * 2))) return rc;
+    h->limb_plane = R * FFN;
+    if ((rc = dalloc(h, (void **)&h->limbs, 4 * h->limb_plane))) return rc;
+    if ((rc = dalloc(h, (void **)&h->lex, R * 4))) return rc;
+    if (make_limb_map(&h->lmap_hid, h->limbs, h->R, FFN, h->limb_plane, HID) ||
+        make_limb_map(&h->lmap_ffn, h->limbs, h->R, FFN, h->limb_plane, FFN))
+        return fail(h, QWEN_B200_EDEVICE, "cannot encode the limb tensor maps");
     // worst case over the layer GEMMs: 8 splits of the widest (gate/up) output
     h->tc_ws_bytes = tc_gemm_workspace(h->R, 2 * FFN, 8);
     if ((rc = dalloc(h, &h->tc_ws, h->tc_ws_bytes))) return rc;
@@ -245,35 +256,7 @@ int allocate(qwen_b200 *h) {
     return 0;
 }
 
-// Row-major [n][k] int8 -> [n/128][k/64][128][64] (tensor-core GEMM layout),
-// each group of four codes stored as (k0, k2, k1, k3) so that the dequant
-// produces the bf16 pairs (k0, k1), (k2, k3) without byte shuffles.
-void tile_weights(const int8_t *w, int n, int k, int8_t *t) {
-    const int kc = k / 64;
-    for (int nb = 0; nb < n / 128; ++nb)
-        for (int c = 0; c < kc; ++c)
-            for (int r = 0; r < 128; ++r) {
-                int8_t *dst = t + (((size_t)nb * kc + c) * 128 + r) * 64;
-                const int8_t *src = w + (size_t)(nb * 128 + r) * k + c * 64;
-                for (int g = 0; g < 64; g += 4) {
-                    dst[g] = src[g];
-                    dst[g + 1] = src[g + 2];
-                    dst[g + 2] = src[g + 1];
-                    dst[g + 3] = src[g + 3];
-                }
-            }
-}
-
-int upload_tiled(qwen_b200 *h, int8_t *dst, const int8_t *w, int n, int k, std::vector<int8_t> &tmp) {
-    tmp.resize((size_t)n * k);
-    tile_weights(w, n, k, tmp.data());
-    CK(cudaMemcpy(dst, tmp.data(), tmp.size(), cudaMemcpyHostToDevice));
-    return 0;
-}
-
 int upload(qwen_b200 *h, const qa_model &m) {
-    std::vector<int8_t> tiled;
-    int rc;
     std::vector<int8_t> gu((size_t)2 * FFN * HID), qkv((size_t)QKVN * HID);
     std::vector<float> s(QKVN + HID + 2 * FFN + HID);
     std::vector<uint16_t> b(QKVN + 2 * HID);
@@ -300,17 +283,12 @@ int upload(qwen_b200 *h, const qa_model &m) {
         CK(cudaMemcpy(W.o, m.w[l][QA_O], (size_t)HID * HID, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.gu, gu.data(), gu.size(), cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.d, m.w[l][QA_DOWN], (size_t)HID * FFN, cudaMemcpyHostToDevice));
-        if ((rc = upload_tiled(h, W.tqkv, qkv.data(), QKVN, HID, tiled))) return rc;
-        if ((rc = upload_tiled(h, W.to, m.w[l][QA_O], HID, HID, tiled))) return rc;
-        if ((rc = upload_tiled(h, W.tgu, gu.data(), 2 * FFN, HID, tiled))) return rc;
-        if ((rc = upload_tiled(h, W.td, m.w[l][QA_DOWN], HID, FFN, tiled))) return rc;
         CK(cudaMemcpy(W.s_qkv, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.bias, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
     }
     CK(cudaMemcpy(h->g_final, m.gamma + QA_GAMMA_FINAL, HID * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->embed, m.embed, (size_t)VOC * HID * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->lmw, m.lmw, (size_t)VOC * HID, cudaMemcpyHostToDevice));
-    if ((rc = upload_tiled(h, h->tlmw, m.lmw, VOC, HID, tiled))) return rc;
     std::vector<float> slm(VOC);
     for (int i = 0; i < VOC; ++i) slm[i] = qa_bf2f(m.scale[QA_SCALE_LM + i]);
     CK(cudaMemcpy(h->s_lm, slm.data(), (size_t)VOC * 4, cudaMemcpyHostToDevice));
@@ -323,22 +301,23 @@ int ensure_device(qwen_b200 *h) {
     return 0;
 }
 
-const CUtensorMap *act_map(qwen_b200 *h, const uint16_t *buf, int rows, int k) {
-    const auto key = std::make_tuple((const void *)buf, rows, k);
-    auto it = h->maps.find(key);
-    if (it != h->maps.end()) return &it->second;
-    CUtensorMap m;
-    if (make_act_map(&m, buf, rows, k, tc_bn_for_rows(rows))) return nullptr;
-    return &(h->maps[key] = m);
+// Exact tensor-core GEMM y = epi(x W^T) for n rows whose limbs are in
+// h->limbs (k = 896 or 4864) with exponents h->lex.
+int tc_gemm(qwen_b200 *h, int epi, int n, int k, const CUtensorMap &wmap, const float *scale, const uint16_t *bias,
+            int nout, uint16_t *y, const TcArgmax *am, cudaStream_t st) {
+    const int splits = am ? 1 : tc_pick_splits(n, nout, k);
+    RK(launch_gemm_tc(epi, wmap, k == HID ? h->lmap_hid : h->lmap_ffn, h->lex, n, k, scale, bias, nout, y, splits,
+                      h->tc_ws, h->tc_ws_bytes, false, am, st));
+    return 0;
 }
 
-// Tensor-core GEMM y = epi(x W^T) for n rows of buffer x [R][k].
-int tc_gemm(qwen_b200 *h, int epi, const uint16_t *x, int n, int k, const int8_t *wt, const float *scale,
-            const uint16_t *bias, int nout, uint16_t *y, const TcArgmax *am, cudaStream_t st) {
-    const CUtensorMap *map = act_map(h, x, n, k);
-    if (!map) return fail(h, QWEN_B200_EDEVICE, "cannot encode the activation tensor map");
-    const int splits = am ? 1 : tc_pick_splits(n, nout, k);
-    RK(launch_gemm_tc(epi, *map, n, k, wt, scale, bias, nout, y, splits, h->tc_ws, h->tc_ws_bytes, false, am, st));
+int make_limbs(qwen_b200 *h, const uint16_t *x, int n, int k, cudaStream_t st) {
+    RK(launch_act_quant(x, n, k, h->limbs, h->limb_plane, FFN, h->lex, st));
+    return 0;
+}
+
+int norm_limbs(qwen_b200 *h, const uint16_t *x, const uint16_t *gamma, int n, float eps, cudaStream_t st) {
+    RK(launch_rmsnorm_limbs(x, gamma, n, eps, nullptr, h->limbs, h->limb_plane, FFN, h->lex, st));
     return 0;
 }
 
@@ -393,8 +372,8 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         a.kv_out = dq ? dq + (size_t)n * 896 : nullptr;
         if (n >= TC_MIN_ROWS) {
             LaunchScope ls(h, 1, st, 3);
-            RK(launch_rmsnorm(h->x, W.g_attn, n, eps, h->hn, st));
-            int rc = tc_gemm(h, EPI_BIAS, h->hn, n, HID, W.tqkv, W.s_qkv, W.bias, QKVN, h->qkvb, nullptr, st);
+            int rc = norm_limbs(h, h->x, W.g_attn, n, eps, st);
+            if (!rc) rc = tc_gemm(h, EPI_BIAS, n, HID, W.mqkv, W.s_qkv, W.bias, QKVN, h->qkvb, nullptr, st);
             if (rc) return rc;
             RK(launch_rope_kv8(h->qkvb, n, slots, positions, h->rope, h->q, kc, ks, vc, vs, cap, a.kv_out, st));
         } else {
@@ -412,9 +391,10 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
             pdl_break();
         }
         {
-            LaunchScope ls(h, 3, st, 1);
+            LaunchScope ls(h, 3, st, n >= TC_MIN_ROWS ? 2 : 1);
             if (n >= TC_MIN_ROWS) {
-                int rc = tc_gemm(h, EPI_RESIDUAL, h->ctx, n, HID, W.to, W.s_o, nullptr, HID, h->x, nullptr, st);
+                int rc = make_limbs(h, h->ctx, n, HID, st);
+                if (!rc) rc = tc_gemm(h, EPI_RESIDUAL, n, HID, W.mo, W.s_o, nullptr, HID, h->x, nullptr, st);
                 if (rc) return rc;
             } else {
                 RK(launch_gemv(EPI_RESIDUAL, h->ctx, n, HID, nullptr, 0.f, W.o, W.s_o, nullptr, HID, h->x, st));
@@ -427,12 +407,13 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         if (n >= TC_MIN_ROWS) {
             {
                 LaunchScope ls(h, 4, st, 2);
-                RK(launch_rmsnorm(h->x, W.g_ffn, n, eps, h->hn, st));
-                int rc = tc_gemm(h, EPI_SWIGLU, h->hn, n, HID, W.tgu, W.s_gu, nullptr, 2 * FFN, h->mid, nullptr, st);
+                int rc = norm_limbs(h, h->x, W.g_ffn, n, eps, st);
+                if (!rc) rc = tc_gemm(h, EPI_SWIGLU, n, HID, W.mgu, W.s_gu, nullptr, 2 * FFN, h->mid, nullptr, st);
                 if (rc) return rc;
             }
-            LaunchScope ls(h, 5, st, 1);
-            int rc = tc_gemm(h, EPI_RESIDUAL, h->mid, n, FFN, W.td, W.s_d, nullptr, HID, h->x, nullptr, st);
+            LaunchScope ls(h, 5, st, 2);
+            int rc = make_limbs(h, h->mid, n, FFN, st);
+            if (!rc) rc = tc_gemm(h, EPI_RESIDUAL, n, FFN, W.md, W.s_d, nullptr, HID, h->x, nullptr, st);
             if (rc) return rc;
         } else {
             {
@@ -457,14 +438,15 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         }
         if (nlog >= TC_MIN_ROWS) {
             LaunchScope ls(h, 6, st, 3);
-            RK(launch_rmsnorm(xin, h->g_final, nlog, eps, h->hn, st));
+            int rc = norm_limbs(h, xin, h->g_final, nlog, eps, st);
+            if (rc) return rc;
             const int nblk = VOC / 128;
             TcArgmax am;
             am.pv = reinterpret_cast<float *>(h->lm_ws);
             am.pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(h->lm_ws) + (size_t)nlog * nblk * 4);
             am.nblk = nblk;
             am.logits = want_logits ? h->logits : nullptr;
-            int rc = tc_gemm(h, EPI_ARGMAX, h->hn, nlog, HID, h->tlmw, h->s_lm, nullptr, VOC, nullptr, &am, st);
+            rc = tc_gemm(h, EPI_ARGMAX, nlog, HID, h->mlm, h->s_lm, nullptr, VOC, nullptr, &am, st);
             if (rc) return rc;
             RK(launch_argmax_reduce(am.pv, am.pi, nlog, nblk, tokens_dst, st));
         } else {
@@ -1040,27 +1022,31 @@ int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma,
                        (cudaStream_t)stream);
 }
 
-int qwen_b200_tile_weights(const int8_t *w, uint32_t n, uint32_t k, int8_t *tiled) {
-    if (!w || !tiled || n % 128 || k % 64 || !n || !k) return QWEN_B200_EINVAL;
-    tile_weights(w, (int)n, (int)k, tiled);
-    return QWEN_B200_OK;
-}
-
+// Workspace of the standalone tensor-core GEMM: 256-byte error word, the
+// activation rows' four int8 limb planes [4][rows][k], their exponents [rows].
 size_t qwen_b200_gemm_tc_workspace(uint32_t rows, uint32_t n, uint32_t k) {
-    return tc_gemm_workspace((int)rows, (int)n, tc_pick_splits((int)rows, (int)n, (int)k));
+    return tc_gemm_workspace((int)rows, (int)n, 1) + 4 * (size_t)rows * k + 4 * (size_t)rows;
 }
 
-int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w_tiled,
+int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
                                const float *scale, uint32_t n, const uint16_t *bias, int epi, uint16_t *y,
                                void *workspace, size_t workspace_bytes, void *stream) {
-    if (!x || !w_tiled || !scale || !y || !workspace || epi < EPI_PLAIN || epi > EPI_SWIGLU) return QWEN_B200_EINVAL;
+    if (!x || !w || !scale || !y || !workspace || epi < EPI_PLAIN || epi > EPI_SWIGLU || !rows) return QWEN_B200_EINVAL;
     if (epi == EPI_BIAS && !bias) return QWEN_B200_EINVAL;
-    CUtensorMap map;
-    if (make_act_map(&map, x, (int)rows, (int)k, tc_bn_for_rows((int)rows))) return QWEN_B200_EINVAL;
+    if ((k != HID && k != FFN) || n % 128) return QWEN_B200_EINVAL;
+    if (workspace_bytes < qwen_b200_gemm_tc_workspace(rows, n, k)) return QWEN_B200_EINVAL;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t plane = (size_t)rows * k;
+    int8_t *limbs = reinterpret_cast<int8_t *>(workspace) + 256;
+    int *ex = reinterpret_cast<int *>(limbs + 4 * plane);
+    CUtensorMap wmap, lmap;
+    if (make_weight_map(&wmap, w, (int)n, (int)k) || make_limb_map(&lmap, limbs, (int)rows, (int)k, plane, (int)k))
+        return QWEN_B200_EINVAL;
     const int splits = tc_pick_splits((int)rows, (int)n, (int)k);
-    int rc = launch_gemm_tc(epi, map, (int)rows, (int)k, w_tiled, scale, bias, (int)n, y, splits, workspace,
-                            workspace_bytes, true, nullptr, (cudaStream_t)stream);
-    return rc;
+    int rc = launch_act_quant(x, (int)rows, (int)k, limbs, plane, (int)k, ex, st);
+    if (rc) return rc;
+    return launch_gemm_tc(epi, wmap, lmap, ex, (int)rows, (int)k, scale, bias, (int)n, y, splits, workspace,
+                          workspace_bytes, true, nullptr, st);
 }
 
 size_t qwen_b200_lm_head_workspace(uint32_t rows, uint32_t vocab) { return lm_head_workspace((int)rows, (int)vocab); }

@@ -1,192 +1,191 @@
-// W8A16 GEMM on the 5th-generation tensor cores (tcgen05) for batched decode
-// and prefill. Swap-AB formulation: D^T[n][m] = W[n][:] . X[m][:], so the
-// 128 output channels of a CTA tile fill the UMMA M dimension and the batch
-// rows (BN of them) the N dimension.
+// Exact W8A16 projections on the 5th-generation tensor cores (tcgen05,
+// kind::i8) for batched decode and prefill. The arithmetic is the oracle's
+// REF_EXACT order (the RTL array's block-aligned integer sums,
+// src/rtl/qwen_gemm_array_i.sv, with one 28-bit alignment per activation row):
+//   X[m][k] = L0 + 2^7 L1 + 2^14 L2 + 2^21 L3   (int8 limbs, made by
+//             rmsnorm_kernel / act_quant_kernel, row exponent ex[m])
+//   dot[n][m] = sum_k W[n][k] * X[m][k]          (exact: int32 per limb, int64)
+//   acc = RN32(dot) * 2^(ex[m] - 26), then the bf16 rounding points of
+//   model_backend.py:62-67 (scale, bias / residual / SiLU*mul / argmax)
+// so every CTA shape and split-K plan gives the same bits.
 //
-//   warp 0      producer: the int8 weight tile [128][64] (8 KB, contiguous in
-//               the tiled layout [N/128][K/64][128][64]) by bulk copy into its
-//               ring, and the activation tile [BN rows][64 k] bf16 by a 2D
-//               tensor-map load with 128-byte swizzle (zero fill past the last
-//               row) into a separate ring. Weights are constant, so the weight
-//               ring is filled before the programmatic-launch wait for the
-//               preceding kernel; activations are loaded after it.
-//   warp 1      owns TMEM (BN fp32 columns) and issues tcgen05.mma (one thread)
-//   warps 2..9  dequantise each weight tile (exact int8 -> bf16) into the
-//               128-byte-swizzled K-major A stage; then the epilogue
-// Epilogue: the fp32 accumulator tile is written transposed ([BN][128]) into
-// the CTA's own shared memory (over the drained A/B stages). Split-K: the CTAs
-// of one output tile form a thread-block cluster, and after a cluster barrier
-// the 256 x splits epilogue threads of the cluster each take 4-channel items
-// of the tile, load that item from every CTA's shared memory at once over
-// distributed shared memory, add them in rank order and apply the epilogue
-// (per-channel scale and the bf16 rounding points of model_backend.py:62-67,
-// bias / residual / SiLU*mul) with vector loads and stores. The LM head
-// (argmax epilogue) never splits K and reduces (value, index) per row in the
-// CTA. No global scratch, no atomics, deterministic.
-// Every mbarrier wait is bounded: on timeout the kernel records an error code
-// in a device flag, skips its remaining work and still frees its TMEM.
+// Swap-AB: 128 output channels fill UMMA M; the B operand is the four limb
+// planes of 64 batch rows, 256 rows of 128 bytes (UMMA N = 256), so one
+// tcgen05.mma.kind::i8 (K = 32) covers all limbs; TMEM holds D[128][256]
+// int32 (column l*64 + m).
+//   warp 0     producer: the weight tile [128 n][128 k] (row-major int8, 2D
+//              tensor map) into a 4-deep ring before the programmatic-launch
+//              wait (weights are constant), the limb tile [4][64][128] (3D
+//              tensor map) into a 4-deep ring after it; 128-byte swizzle
+//   warp 1     owns TMEM (256 columns), issues the MMAs (one thread)
+//   warps 2..9 epilogue: the limbs of a row fold into int64; the int64 tile
+//              [64 rows][128 channels] is staged in the CTA's shared memory
+//              (over the drained weight ring). Split-K CTAs of a tile form a
+//              thread-block cluster: after a cluster barrier each of the
+//              256 x splits epilogue threads takes 4-channel items, reads the
+//              item from every rank at once over distributed shared memory
+//              and adds the exact partials. The LM head (argmax) never splits.
+// No global scratch, no atomics, no TMA multicast. Every mbarrier wait is
+// bounded: on timeout the kernel records an error code in a device flag,
+// skips its remaining work and still frees its TMEM.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc05.cuh"
 
 namespace qb {
 
-constexpr int TC_BM = 128;
-constexpr int TC_BK = 64;
-constexpr int TC_CONV = 256;                 // dequant / epilogue threads (warps 2..9)
+constexpr int TC_BM = 128;           // output channels per tile
+constexpr int TC_BN = 64;            // batch rows per tile
+constexpr int TC_BK = 128;           // k per stage (bytes of int8)
+constexpr int TC_NL = 4;             // activation limbs
+constexpr int TC_MN = TC_NL * TC_BN; // UMMA N
+constexpr int TC_CONV = 256;         // epilogue threads (warps 2..9)
 constexpr int TC_THREADS = 64 + TC_CONV;
 constexpr int TC_MAX_SPLITS = 8;
-// One CTA per SM. With two co-resident CTAs per SM (smaller rings) a stress
-// test of the 200-row SwiGLU shape returned a wrong 8-channel group (one
-// dequantising warp's rows of one tile) in about 1 run in 10; with one CTA
-// per SM it never did, whatever the ring depths.
-// Split planning counts 2 x 148 CTA slots (a second wave for the largest
-// tile counts).
-constexpr int TC_SLOTS = 2 * 148;
+constexpr int TC_SLOTS = 148;        // one CTA per SM
 
-// Shared memory: A (bf16 weights) | B (bf16 activations) | W (int8 weights)
-// rings | mbarriers | TMEM address | argmax partials (about 195 KB). The
-// accumulator tile [BN][128] fp32 of the epilogue reuses the A and B stages
-// once every MMA has completed.
-template <int BN>
 struct TcSmem {
-    static constexpr int A_STAGES = 4;
-    static constexpr int B_STAGES = BN == 64 ? 8 : 4;
-    static constexpr int W_STAGES = 8;
-    static constexpr int W_BYTES = TC_BM * TC_BK;      // 8 KB int8 tile
-    static constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB bf16 tile
-    static constexpr int B_BYTES = BN * TC_BK * 2;
+    static constexpr int A_STAGES = 4, B_STAGES = 4;
+    static constexpr int A_BYTES = TC_BM * TC_BK;  // 16 KB weight tile
+    static constexpr int B_BYTES = TC_MN * TC_BK;  // 32 KB limb tile
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
-    static constexpr int W_OFF = B_OFF + B_STAGES * B_BYTES;
-    static constexpr int TILE_BYTES = BN * TC_BM * 4;
-    static_assert(TILE_BYTES <= W_OFF, "accumulator tile must fit over the A and B stages");
-    static constexpr int BAR_OFF = W_OFF + W_STAGES * W_BYTES;
-    static constexpr int NBARS = 2 * A_STAGES + 2 * B_STAGES + 2 * W_STAGES + 2;
+    static constexpr int TILE_BYTES = TC_BN * TC_BM * 8;  // int64 tile
+    static_assert(TILE_BYTES <= B_OFF, "the int64 tile must fit over the weight ring");
+    static constexpr int BAR_OFF = B_OFF + B_STAGES * B_BYTES;
+    static constexpr int NBARS = 2 * A_STAGES + 2 * B_STAGES + 2;
     static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8;
     static constexpr int RED_OFF = SLOT_OFF + 16;
-    static constexpr int RED_BYTES = 4 * BN * 8;
+    static constexpr int RED_BYTES = 4 * TC_BN * 8;
     static constexpr int TOTAL = RED_OFF + RED_BYTES;
     static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment of the stages
-    static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+    static constexpr uint32_t TMEM_COLS = TC_MN;
 };
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+// kind::i8 instruction descriptor: D s32, A and B signed int8, both K-major.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+__device__ __forceinline__ void mma_s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(tc::smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld16i(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float exact_acc(long long dot, int e) { return ldexpf(__ll2float_rn(dot), e - 26); }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// Epilogue of 32 accumulators of output channel n: columns c0..c0+31 of the
-// tile (batch rows m0 + c0 + j). Residual rows are read before any write.
-template <int BN, int EPI>
-__device__ __forceinline__ void tc_epilogue32(const TcArgs &a, const float (&v)[32], int n, int m0, int c0, int q,
-                                              int lane, uint8_t *red) {
+// LM head: 32 accumulators of output channel n (rows m0 + c0 + j), logits
+// bf16(bf16(acc) * scale) (model_backend.py:109), best (value, index) per
+// row over this warp's 32 channels into red (highest index on ties).
+__device__ __forceinline__ void tc_argmax32(const TcArgs &a, const float (&v)[32], int n, int m0, int c0, int q,
+                                            int lane, uint8_t *red) {
     const float sc = a.scale[n];
-    float res[32];
-    if constexpr (EPI == EPI_RESIDUAL) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c0 + j;
-            res[j] = m < a.M ? bf2f(a.y[(size_t)m * a.N + n]) : 0.f;
-        }
-    }
-    float bias = 0.f;
-    if constexpr (EPI == EPI_BIAS) bias = bf2f(a.bias[n]);
     float *red_v = reinterpret_cast<float *>(red);
-    uint32_t *red_i = reinterpret_cast<uint32_t *>(red + 4 * BN * 4);
+    uint32_t *red_i = reinterpret_cast<uint32_t *>(red + 4 * TC_BN * 4);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const int cj = c0 + j, m = m0 + cj;
         const bool valid = m < a.M;
-        float val = rbf(rbf(v[j]) * sc);
-        if constexpr (EPI == EPI_SWIGLU) {
-            // rows 2j (gate) and 2j+1 (up) sit in adjacent lanes
-            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
-            if (valid && !(lane & 1)) {
-                const float sl = val / (1.0f + expf(-val));
-                a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = f2bf(rbf(sl) * other);
-            }
-        } else if constexpr (EPI == EPI_ARGMAX) {
-            if (valid && a.logits) a.logits[(size_t)m * a.N + n] = f2bf(val);
-            float bv = valid ? val : -INFINITY;
-            uint32_t bi = (uint32_t)n;
+        const float val = rbf(rbf(v[j]) * sc);
+        if (valid && a.logits) a.logits[(size_t)m * a.N + n] = f2bf(val);
+        float bv = valid ? val : -INFINITY;
+        uint32_t bi = (uint32_t)n;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (better(ov, oi, bv, bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
             }
-            if (lane == 0) {
-                red_v[q * BN + cj] = bv;
-                red_i[q * BN + cj] = bi;
-            }
-        } else if (valid) {
-            if (EPI == EPI_BIAS) val = rbf(val + bias);
-            if (EPI == EPI_RESIDUAL) val = rbf(res[j] + val);
-            a.y[(size_t)m * a.N + n] = f2bf(val);
+        }
+        if (lane == 0) {
+            red_v[q * TC_BN + cj] = bv;
+            red_i[q * TC_BN + cj] = bi;
         }
     }
 }
 
 // Best (value, index) per batch row over the tile's four lane quarters.
-template <int BN>
 __device__ __forceinline__ void tc_argmax_flush(const TcArgs &a, const uint8_t *red, int m0, int n_tile, int ct) {
     const float *red_v = reinterpret_cast<const float *>(red);
-    const uint32_t *red_i = reinterpret_cast<const uint32_t *>(red + 4 * BN * 4);
-    for (int m = ct; m < BN; m += TC_CONV) {
+    const uint32_t *red_i = reinterpret_cast<const uint32_t *>(red + 4 * TC_BN * 4);
+    for (int m = ct; m < TC_BN; m += TC_CONV) {
         if (m0 + m >= a.M) continue;
         float bv = red_v[m];
         uint32_t bi = red_i[m];
         for (int qq = 1; qq < 4; ++qq)
-            if (better(red_v[qq * BN + m], red_i[qq * BN + m], bv, bi)) {
-                bv = red_v[qq * BN + m];
-                bi = red_i[qq * BN + m];
+            if (better(red_v[qq * TC_BN + m], red_i[qq * TC_BN + m], bv, bi)) {
+                bv = red_v[qq * TC_BN + m];
+                bi = red_i[qq * TC_BN + m];
             }
         a.pv[(size_t)(m0 + m) * a.nblk + n_tile] = bv;
         a.pi[(size_t)(m0 + m) * a.nblk + n_tile] = bi;
     }
 }
 
-// Item i of the transposed accumulator tile: batch row m = i / 32 of the
-// tile, channels 4*(i % 32) .. +3. The partial tiles of all `splits` CTAs of
-// the cluster are read at once and added in rank order, then the epilogue of
-// model_backend.py:62-67 runs on the four channels.
-template <int BN, int EPI>
+// Item i of the int64 tile: batch row m = i / 32, channels 4*(i % 32) .. +3.
+// The exact partials of all `splits` CTAs of the cluster are read at once and
+// added, then the epilogue of model_backend.py:62-67 runs on the four channels.
+template <int EPI>
 __device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int n0, uint32_t tile_saddr,
-                                             const float *tile) {
+                                             const long long *tile) {
     const int m = i >> 5, nl = 4 * (i & 31), n = n0 + nl, mg = m0 + m;
     const bool valid = mg < a.M;
     uint2 res = make_uint2(0u, 0u);
     if (EPI == EPI_RESIDUAL && valid) res = *reinterpret_cast<const uint2 *>(a.y + (size_t)mg * a.N + n);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    long long t[4] = {0, 0, 0, 0};
     if (a.splits > 1) {
-        const uint32_t addr = tile_saddr + (uint32_t)(m * TC_BM + nl) * 4u;
-        float4 part[TC_MAX_SPLITS];
-#pragma unroll
-        for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
-            if (sr < a.splits) part[sr] = tc::ld_dsmem_f4(addr, (uint32_t)sr);
+        const uint32_t addr = tile_saddr + (uint32_t)(m * TC_BM + nl) * 8u;
+        float4 p[TC_MAX_SPLITS][2];
 #pragma unroll
         for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
             if (sr < a.splits) {
-                v.x += part[sr].x;
-                v.y += part[sr].y;
-                v.z += part[sr].z;
-                v.w += part[sr].w;
+                p[sr][0] = tc::ld_dsmem_f4(addr, (uint32_t)sr);
+                p[sr][1] = tc::ld_dsmem_f4(addr + 16u, (uint32_t)sr);
+            }
+#pragma unroll
+        for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
+            if (sr < a.splits) {
+                const longlong2 u = *reinterpret_cast<const longlong2 *>(&p[sr][0]);
+                const longlong2 w = *reinterpret_cast<const longlong2 *>(&p[sr][1]);
+                t[0] += u.x;
+                t[1] += u.y;
+                t[2] += w.x;
+                t[3] += w.y;
             }
     } else {
-        const float4 p = *reinterpret_cast<const float4 *>(tile + m * TC_BM + nl);
-        v.x += p.x;
-        v.y += p.y;
-        v.z += p.z;
-        v.w += p.w;
+        const longlong2 u = *reinterpret_cast<const longlong2 *>(tile + m * TC_BM + nl);
+        const longlong2 w = *reinterpret_cast<const longlong2 *>(tile + m * TC_BM + nl + 2);
+        t[0] = u.x;
+        t[1] = u.y;
+        t[2] = w.x;
+        t[3] = w.y;
     }
     if (!valid) return;
+    const int e = a.ex[mg];
     const float4 sc = *reinterpret_cast<const float4 *>(a.scale + n);
-    float o[4] = {rbf(rbf(v.x) * sc.x), rbf(rbf(v.y) * sc.y), rbf(rbf(v.z) * sc.z), rbf(rbf(v.w) * sc.w)};
+    float o[4] = {rbf(rbf(exact_acc(t[0], e)) * sc.x), rbf(rbf(exact_acc(t[1], e)) * sc.y),
+                  rbf(rbf(exact_acc(t[2], e)) * sc.z), rbf(rbf(exact_acc(t[3], e)) * sc.w)};
     if constexpr (EPI == EPI_SWIGLU) {
         // channels 2j (gate j) and 2j+1 (up j): model_backend.py:105-106
         const float s0 = o[0] / (1.0f + expf(-o[0])), s1 = o[2] / (1.0f + expf(-o[2]));
@@ -213,42 +212,39 @@ __device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int
     }
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
-    using L = TcSmem<BN>;
-    constexpr int AS = L::A_STAGES, BS = L::B_STAGES, WS = L::W_STAGES;
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap lmap, TcArgs a) {
+    using L = TcSmem;
+    constexpr int AS = L::A_STAGES, BS = L::B_STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
     uint64_t *full_a = bars, *empty_a = full_a + AS, *full_b = empty_a + AS, *empty_b = full_b + BS;
-    uint64_t *w_full = empty_b + BS, *w_empty = w_full + WS;
-    uint64_t *accum = w_empty + WS, *done = accum + 1;
+    uint64_t *accum = empty_b + BS, *done = accum + 1;
     uint32_t *slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = a.splits > 1 ? (int)tc::cluster_rank() : 0;
     const int n_tile = blockIdx.x / a.splits, m_tile = blockIdx.z;
-    const int n0 = n_tile * TC_BM, m0 = m_tile * BN;
+    const int n0 = n_tile * TC_BM, m0 = m_tile * TC_BN;
     const int KC = a.K / TC_BK;
     const int kc0 = split * a.kc_per_split;
     const int nk = min(KC, kc0 + a.kc_per_split) - kc0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < AS; ++s) {
-            tc::mbar_init(&full_a[s], TC_CONV);
+            tc::mbar_init(&full_a[s], 1);
             tc::mbar_init(&empty_a[s], 1);
         }
         for (int s = 0; s < BS; ++s) {
             tc::mbar_init(&full_b[s], 1);
             tc::mbar_init(&empty_b[s], 1);
         }
-        for (int s = 0; s < WS; ++s) {
-            tc::mbar_init(&w_full[s], 1);
-            tc::mbar_init(&w_empty[s], TC_CONV);
-        }
         tc::mbar_init(accum, 1);
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
-        tc::tma_prefetch_desc(&xmap);
+        tc::tma_prefetch_desc(&wmap);
+        tc::tma_prefetch_desc(&lmap);
     }
     if (warp == 1) tc::tmem_alloc(slot, L::TMEM_COLS);
     tc::tc_fence_before();
@@ -260,35 +256,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 
     if (warp == 0) {
         if (lane == 0) {
-            const int8_t *wsrc = a.w + ((size_t)n_tile * KC + kc0) * L::W_BYTES;
-            int iw = 0, ib = 0;
+            int ia = 0, ib = 0;
             // weights are constant: fill the weight ring before waiting for the
-            // kernel that produces the activations
-            for (; ok && iw < min(nk, WS); ++iw) {
-                tc::mbar_arrive_expect_tx(&w_full[iw], (uint32_t)L::W_BYTES);
-                tc::bulk_load(smem + L::W_OFF + iw * L::W_BYTES, wsrc + (size_t)iw * L::W_BYTES, (uint32_t)L::W_BYTES,
-                              &w_full[iw]);
+            // kernel that produces the activation limbs
+            for (; ok && ia < min(nk, AS); ++ia) {
+                tc::mbar_arrive_expect_tx(&full_a[ia], (uint32_t)L::A_BYTES);
+                tc::tma_load_2d(smem + L::A_OFF + ia * L::A_BYTES, &wmap, &full_a[ia], (kc0 + ia) * TC_BK, n0);
             }
             pdl_wait();
             uint32_t idle = 0;
-            while (ok && (ib < nk || iw < nk)) {
+            while (ok && (ib < nk || ia < nk)) {
                 bool progress = false;
                 if (ib < nk) {
                     const int s = ib % BS, ph = (ib / BS) & 1;
                     if (tc::mbar_try_wait(&empty_b[s], ph ^ 1)) {
                         tc::mbar_arrive_expect_tx(&full_b[s], (uint32_t)L::B_BYTES);
-                        tc::tma_load_2d(smem + L::B_OFF + s * L::B_BYTES, &xmap, &full_b[s], (kc0 + ib) * TC_BK, m0);
+                        tma_load_3d(smem + L::B_OFF + s * L::B_BYTES, &lmap, &full_b[s], (kc0 + ib) * TC_BK, m0, 0);
                         ++ib;
                         progress = true;
                     }
                 }
-                if (iw < nk) {
-                    const int s = iw % WS, ph = (iw / WS) & 1;
-                    if (tc::mbar_try_wait(&w_empty[s], ph ^ 1)) {
-                        tc::mbar_arrive_expect_tx(&w_full[s], (uint32_t)L::W_BYTES);
-                        tc::bulk_load(smem + L::W_OFF + s * L::W_BYTES, wsrc + (size_t)iw * L::W_BYTES,
-                                      (uint32_t)L::W_BYTES, &w_full[s]);
-                        ++iw;
+                if (ia < nk) {
+                    const int s = ia % AS, ph = (ia / AS) & 1;
+                    if (tc::mbar_try_wait(&empty_a[s], ph ^ 1)) {
+                        tc::mbar_arrive_expect_tx(&full_a[s], (uint32_t)L::A_BYTES);
+                        tc::tma_load_2d(smem + L::A_OFF + s * L::A_BYTES, &wmap, &full_a[s], (kc0 + ia) * TC_BK, n0);
+                        ++ia;
                         progress = true;
                     }
                 }
@@ -305,7 +298,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     } else if (warp == 1) {
         pdl_wait();
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_bf16_f32(TC_BM, BN);
+            constexpr uint32_t idesc = idesc_s8_s32(TC_BM, TC_MN);
             int i = 0;
             for (; ok && i < nk; ++i) {
                 const int sa = i % AS, pa = (i / AS) & 1;
@@ -315,9 +308,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 const uint32_t ab = tc::smem_u32(smem + L::A_OFF + sa * L::A_BYTES);
                 const uint32_t bb = tc::smem_u32(smem + L::B_OFF + sb * L::B_BYTES);
 #pragma unroll
-                for (int j = 0; j < TC_BK / 16; ++j)
-                    tc::mma_bf16(tmem, tc::smem_desc_sw128(ab + 32 * j), tc::smem_desc_sw128(bb + 32 * j), idesc,
-                                 i > 0 || j > 0);
+                for (int j = 0; j < TC_BK / 32; ++j)
+                    mma_s8(tmem, tc::smem_desc_sw128(ab + 32 * j), tc::smem_desc_sw128(bb + 32 * j), idesc,
+                           i > 0 || j > 0);
                 tc::mma_commit(&empty_a[sa]);
                 tc::mma_commit(&empty_b[sb]);
             }
@@ -328,81 +321,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
         __syncwarp();
     } else {
-        // ---------------- weight dequantisation (TC_CONV threads)
-        const int ct = threadIdx.x - 64;
-        constexpr int ITEMS = TC_BM * TC_BK / 16 / TC_CONV;  // 16-byte pieces per thread per tile
-        for (int i = 0; ok && i < nk; ++i) {
-            const int s = i % AS, ph = (i / AS) & 1;
-            const int sw = i % WS, phw = (i / WS) & 1;
-            if (!tc::mbar_wait(&w_full[sw], phw, a.err, 8) || !tc::mbar_wait(&empty_a[s], ph ^ 1, a.err, 5)) {
-                ok = false;
-                break;
-            }
-            // the tensor core's reads of this A stage (async proxy) are ordered
-            // before the generic-proxy stores that refill it
-            tc::fence_proxy_async_smem();
-            const uint4 *src = reinterpret_cast<const uint4 *>(smem + L::W_OFF + sw * L::W_BYTES);
-            uint4 wv[ITEMS];
-#pragma unroll
-            for (int j = 0; j < ITEMS; ++j) wv[j] = src[ct + TC_CONV * j];
-            tc::mbar_arrive(&w_empty[sw]);  // the int8 slot may be refilled
-            uint8_t *dst = smem + L::A_OFF + s * L::A_BYTES;
-#pragma unroll
-            for (int j = 0; j < ITEMS; ++j) {
-                // the tiled layout stores codes in the byte order (k0, k2, k1,
-                // k3), which codes4_to_bf16 unpacks to (k0, k1), (k2, k3)
-                const int item = ct + TC_CONV * j, row = item >> 2, piece = item & 3;
-                const int c0 = (2 * piece) ^ (row & 7), c1 = (2 * piece + 1) ^ (row & 7);
-                uint4 lo, hi;
-                codes4_to_bf16(wv[j].x, lo.x, lo.y);
-                codes4_to_bf16(wv[j].y, lo.z, lo.w);
-                codes4_to_bf16(wv[j].z, hi.x, hi.y);
-                codes4_to_bf16(wv[j].w, hi.z, hi.w);
-                *reinterpret_cast<uint4 *>(dst + row * 128 + c0 * 16) = lo;
-                *reinterpret_cast<uint4 *>(dst + row * 128 + c1 * 16) = hi;
-            }
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive(&full_a[s]);
-        }
-        pdl_wait();  // residual rows and outputs of the preceding kernel
-        // ---------------- epilogue: this thread owns output channel n (TMEM
-        // lane) and half of the tile's columns (two warps per lane quarter)
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
-        constexpr int HALF = BN / 2;
-        const int cbeg = ((warp - 2) >> 2) * HALF;
+        pdl_wait();  // row exponents, residual rows and outputs of earlier kernels
+        // this warp: TMEM lane quarter q (channels 32q..32q+31), rows 32h..32h+31
+        const int q = warp & 3, h = (warp - 2) >> 2, ct = threadIdx.x - 64;
         ok = ok && tc::mbar_wait(accum, 0, a.err, 6);
         tc::tc_fence_after();
-        tc::fence_proxy_async_smem();  // A/B stages (async-proxy traffic) become the generic accumulator tile
+        tc::fence_proxy_async_smem();  // the weight ring (async-proxy writes) becomes the generic int64 tile
+        // the limbs of 16 rows at a time fold into int64 (keeps the fold in registers)
+        float f[32];
+        long long *tile = reinterpret_cast<long long *>(smem + L::A_OFF);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            long long v[16];
+            int d[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0;
+#pragma unroll
+            for (int l = 0; l < TC_NL; ++l) {
+                if (ok) {
+                    tmem_ld16i(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(l * TC_BN + 32 * h + 16 * hh), d);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) d[j] = 0;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] += (long long)d[j] << (7 * l);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int r = 32 * h + 16 * hh + j;
+                if constexpr (EPI == EPI_ARGMAX)
+                    f[16 * hh + j] = m0 + r < a.M ? exact_acc(v[j], a.ex[m0 + r]) : 0.f;
+                else
+                    tile[r * TC_BM + q * 32 + lane] = v[j];
+            }
+        }
         if constexpr (EPI == EPI_ARGMAX) {
-            const int n = n0 + q * 32 + lane;
-#pragma unroll 1
-            for (int c = cbeg; c < cbeg + HALF; c += 32) {
-                float v[32];
-                if (ok) {
-                    tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-                }
-                tc_epilogue32<BN, EPI>(a, v, n, m0, c, q, lane, smem + L::RED_OFF);
-            }
+            tc_argmax32(a, f, n0 + q * 32 + lane, m0, 32 * h, q, lane, smem + L::RED_OFF);
             epi_bar();
-            tc_argmax_flush<BN>(a, smem + L::RED_OFF, m0, n_tile, ct);
-        } else {
-            // accumulator -> tile[m][n] (fp32), lanes on consecutive channels
-            float *tile = reinterpret_cast<float *>(smem + L::A_OFF);
-#pragma unroll 1
-            for (int c = 0; c < HALF; c += 32) {
-                float v[32];
-                if (ok) {
-                    tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cbeg + c), v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-                }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) tile[(cbeg + c + j) * TC_BM + q * 32 + lane] = v[j];
-            }
+            tc_argmax_flush(a, smem + L::RED_OFF, m0, n_tile, ct);
         }
     }
     if constexpr (EPI != EPI_ARGMAX) {
@@ -412,10 +369,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         else
             __syncthreads();
         if (warp >= 2) {
-            const float *tile = reinterpret_cast<const float *>(smem + L::A_OFF);
+            const long long *tile = reinterpret_cast<const long long *>(smem + L::A_OFF);
             const uint32_t tsa = tc::smem_u32(tile);
-            for (int i = split * TC_CONV + (threadIdx.x - 64); i < BN * (TC_BM / 4); i += a.splits * TC_CONV)
-                tc_epilogue4<BN, EPI>(a, i, m0, n0, tsa, tile);
+            for (int i = split * TC_CONV + (threadIdx.x - 64); i < TC_BN * (TC_BM / 4); i += a.splits * TC_CONV)
+                tc_epilogue4<EPI>(a, i, m0, n0, tsa, tile);
         }
         if (a.splits > 1) tc::cluster_sync();  // no CTA leaves while another may still read its tile
     }
@@ -444,22 +401,39 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Activation map: [rows][K] bf16 row-major, box [BN rows][64 k], 128-byte swizzle.
-int make_act_map(CUtensorMap *map, const uint16_t *x, int rows, int K, int BN) {
+// Weight map: W [n][k] int8 row-major, box [128 n][128 k], 128-byte swizzle.
+int make_weight_map(CUtensorMap *map, const int8_t *w, int n, int k) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return -3;
-    if ((reinterpret_cast<uintptr_t>(x) & 15) || K % TC_BK || rows <= 0) return -1;
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)BN};
+    if ((reinterpret_cast<uintptr_t>(w) & 15) || k % TC_BK || n % TC_BM || n <= 0) return -1;
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
+    cuuint64_t strides[1] = {(cuuint64_t)k};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
     cuuint32_t es[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), dims, strides, box, es,
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(w), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : -3;
 }
 
-int tc_bn_for_rows(int rows) { return rows <= 64 ? 64 : 128; }
+// Limb map: limbs[l][row][k] int8 (plane bytes apart, rows ld bytes apart,
+// rows_alloc rows), box [4][64 rows][128 k], 128-byte swizzle; rows past
+// rows_alloc read as zero.
+int make_limb_map(CUtensorMap *map, const int8_t *limbs, int rows_alloc, int ld, size_t plane, int k) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return -3;
+    if ((reinterpret_cast<uintptr_t>(limbs) & 15) || (ld & 15) || (plane & 15) || k % TC_BK || k > ld ||
+        rows_alloc <= 0)
+        return -1;
+    cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)rows_alloc, (cuuint64_t)TC_NL};
+    cuuint64_t strides[2] = {(cuuint64_t)ld, (cuuint64_t)plane};
+    cuuint32_t box[3] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BN, (cuuint32_t)TC_NL};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(limbs), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -3;
+}
 
 // Workspace: the 4-byte error flag of the bounded waits (256 bytes reserved).
 size_t tc_gemm_workspace(int rows, int n, int splits) {
@@ -469,78 +443,61 @@ size_t tc_gemm_workspace(int rows, int n, int splits) {
     return 256;
 }
 
-// Splits of K so that the tiles fill TC_SLOTS CTA slots, with at least two k
-// chunks per split and no empty split.
+// Splits of K so that the tiles fill the GPU once (one CTA per SM), each
+// split owning at least one k chunk; any split gives the same (exact) result.
 int tc_pick_splits(int rows, int n, int k) {
-    const int bn = tc_bn_for_rows(rows);
-    const int tiles = (n / TC_BM) * ((rows + bn - 1) / bn);
+    const int tiles = (n / TC_BM) * ((rows + TC_BN - 1) / TC_BN);
     const int kc = k / TC_BK;
     int s = TC_SLOTS / tiles;
     s = s < 1 ? 1 : s;
     s = s > TC_MAX_SPLITS ? TC_MAX_SPLITS : s;
-    s = s > kc / 2 ? kc / 2 : s;  // at least two k chunks per split
-    if (s < 1) s = 1;
+    s = s > kc ? kc : s;
     while (s > 1 && (s - 1) * ((kc + s - 1) / s) >= kc) --s;  // no empty split
     return s;
 }
 
-template <int BN, int EPI>
-static int run_tc(const CUtensorMap &map, TcArgs &a, int splits, cudaStream_t st) {
-    using L = TcSmem<BN>;
+template <int EPI>
+static int run_tc(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs &a, int splits, cudaStream_t st) {
+    using L = TcSmem;
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured & (1u << (dev & 31)))) {
-        if (cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+        if (cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
             cudaSuccess)
             return -3;
         configured |= 1u << (dev & 31);
     }
     // the split CTAs of a tile share one cluster
-    return launch_pdl(tc_gemm_kernel<BN, EPI>, dim3((a.N / TC_BM) * splits, 1, (a.M + BN - 1) / BN),
-                      dim3(TC_THREADS), (size_t)L::ALLOC, st, (unsigned)splits, map, a);
+    return launch_pdl(tc_gemm_kernel<EPI>, dim3((a.N / TC_BM) * splits, 1, (a.M + TC_BN - 1) / TC_BN),
+                      dim3(TC_THREADS), (size_t)L::ALLOC, st, (unsigned)splits, wmap, lmap, a);
 }
 
-template <int BN>
-static int dispatch_epi(int epi, const CUtensorMap &map, TcArgs &a, int splits, cudaStream_t st) {
-    switch (epi) {
-        case EPI_PLAIN: return run_tc<BN, EPI_PLAIN>(map, a, splits, st);
-        case EPI_BIAS: return run_tc<BN, EPI_BIAS>(map, a, splits, st);
-        case EPI_RESIDUAL: return run_tc<BN, EPI_RESIDUAL>(map, a, splits, st);
-        case EPI_SWIGLU: return run_tc<BN, EPI_SWIGLU>(map, a, splits, st);
-        case EPI_ARGMAX: return run_tc<BN, EPI_ARGMAX>(map, a, splits, st);
-    }
-    return -1;
-}
-
-int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8_t *w_tiled, const float *scale,
-                   const uint16_t *bias, int n, uint16_t *y, int splits, void *ws, size_t ws_bytes, bool clear,
-                   const TcArgmax *am, cudaStream_t st) {
-    if (rows <= 0 || n % TC_BM || k % TC_BK || splits < 1 || splits > k / TC_BK || splits > TC_MAX_SPLITS) return -1;
+int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, const int *ex, int rows, int k,
+                   const float *scale, const uint16_t *bias, int n, uint16_t *y, int splits, void *ws,
+                   size_t ws_bytes, bool clear, const TcArgmax *am, cudaStream_t st) {
+    if (rows <= 0 || n % TC_BM || k % TC_BK || splits < 1 || splits > k / TC_BK || splits > TC_MAX_SPLITS || !ex)
+        return -1;
     if (epi == EPI_ARGMAX && (!am || splits != 1)) return -1;
     // vector loads and stores of the epilogue: 4 scales, 4 bias / output values
     if ((reinterpret_cast<uintptr_t>(scale) & 15) || (reinterpret_cast<uintptr_t>(bias) & 7) ||
         (reinterpret_cast<uintptr_t>(y) & 7))
         return -1;
     if (ws_bytes < tc_gemm_workspace(rows, n, splits)) return -1;
-    const int bn = tc_bn_for_rows(rows);
     const int kc = k / TC_BK;
     const int kcps = (kc + splits - 1) / splits;
     if ((splits - 1) * kcps >= kc) return -1;  // every split owns at least one k chunk
     TcArgs a;
-    a.w = w_tiled;
     a.scale = scale;
     a.bias = bias;
     a.y = y;
+    a.ex = ex;
     a.M = rows;
     a.N = n;
     a.K = k;
-    a.Mpad = ((rows + bn - 1) / bn) * bn;
     a.kc_per_split = kcps;
     a.splits = splits;
     a.err = reinterpret_cast<unsigned *>(ws);
-    a.counters = nullptr;
-    a.part = nullptr;
     a.pv = am ? am->pv : nullptr;
     a.pi = am ? am->pi : nullptr;
     a.nblk = am ? am->nblk : 0;
@@ -549,7 +506,14 @@ int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8
         if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return -3;
         pdl_break();
     }
-    return bn == 64 ? dispatch_epi<64>(epi, xmap, a, splits, st) : dispatch_epi<128>(epi, xmap, a, splits, st);
+    switch (epi) {
+        case EPI_PLAIN: return run_tc<EPI_PLAIN>(wmap, lmap, a, splits, st);
+        case EPI_BIAS: return run_tc<EPI_BIAS>(wmap, lmap, a, splits, st);
+        case EPI_RESIDUAL: return run_tc<EPI_RESIDUAL>(wmap, lmap, a, splits, st);
+        case EPI_SWIGLU: return run_tc<EPI_SWIGLU>(wmap, lmap, a, splits, st);
+        case EPI_ARGMAX: return run_tc<EPI_ARGMAX>(wmap, lmap, a, splits, st);
+    }
+    return -1;
 }
 
 }  // namespace qb

@@ -60,6 +60,14 @@ int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots,
 
 int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t *x, cudaStream_t st);
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st);
+// Activation rows as the int8 limb planes of their 28-bit alignment (the
+// operand of the exact tensor-core projections): limbs[l][row][k] at
+// l * plane + row * ld + k, exponent ex[row]. The RMSNorm variant also writes
+// the bf16 row to out unless out is null.
+int launch_rmsnorm_limbs(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out,
+                         int8_t *limbs, size_t plane, int ld, int *ex, cudaStream_t st);
+int launch_act_quant(const uint16_t *x, int rows, int k, int8_t *limbs, size_t plane, int ld, int *ex,
+                     cudaStream_t st);
 int launch_rope(uint16_t *x, int rows, int heads, const uint32_t *positions, const float *table, cudaStream_t st);
 int launch_kv8_append(const uint16_t *kv, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *codes,
                       float *scales, int cap, cudaStream_t st);
@@ -73,16 +81,15 @@ int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
 int launch_fill_kv(int8_t *kc, float *ks, int8_t *vc, float *vs, int layers, int nslots, int slot, int cap,
                    int length, uint64_t seed, cudaStream_t st);
 
-// ---- tcgen05 W8A16 GEMM (rows > 8). Weights in the tiled layout
-// [n/128][k/64][128][64] int8 (16-byte coalesced loads per dequant thread).
+// ---- tcgen05 exact W8A16 GEMM (rows > 8): row-major int8 weights [n][k] by
+// TMA times the int8 limb planes of the activation rows (see
+// launch_rmsnorm_limbs / launch_act_quant) -> exact int32/int64 sums.
 struct TcArgs {
-    const int8_t *w;
     const float *scale;
     const uint16_t *bias;
     uint16_t *y;
-    int M, N, K, Mpad, kc_per_split, splits;
-    float *part;
-    unsigned *counters;
+    const int *ex;  // row exponents of the activation limbs
+    int M, N, K, kc_per_split, splits;
     unsigned *err;
     float *pv;
     uint32_t *pi;
@@ -95,17 +102,17 @@ struct TcArgmax {
     int nblk;         // = n / 128 partial candidates per row
     uint16_t *logits; // nullable [rows][n]
 };
-// Tensor map of an activation matrix [rows][K] bf16 for the GEMM's B operand.
-int make_act_map(CUtensorMap *map, const uint16_t *x, int rows, int K, int BN);
-int tc_bn_for_rows(int rows);
+// Tensor maps: weights [n][k] int8 row-major; limbs[l][row][k] with planes
+// `plane` bytes apart, rows `ld` bytes apart, rows_alloc rows.
+int make_weight_map(CUtensorMap *map, const int8_t *w, int n, int k);
+int make_limb_map(CUtensorMap *map, const int8_t *limbs, int rows_alloc, int ld, size_t plane, int k);
 int tc_pick_splits(int rows, int n, int k);
-// Workspace: [256 B error flag][tile counters][split partials]; the flag and
-// counters must be zero before the first launch and are left zero (clear
-// zeroes them first).
+// Workspace: a 256-byte error flag (zero before the first launch; clear
+// zeroes it first).
 size_t tc_gemm_workspace(int rows, int n, int splits);
-int launch_gemm_tc(int epi, const CUtensorMap &xmap, int rows, int k, const int8_t *w_tiled, const float *scale,
-                   const uint16_t *bias, int n, uint16_t *y, int splits, void *ws, size_t ws_bytes, bool clear,
-                   const TcArgmax *am, cudaStream_t st);
+int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, const int *ex, int rows, int k,
+                   const float *scale, const uint16_t *bias, int n, uint16_t *y, int splits, void *ws,
+                   size_t ws_bytes, bool clear, const TcArgmax *am, cudaStream_t st);
 int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st);
 // RoPE + KV8 append for the q|k|v rows produced by the tensor-core QKV GEMM
 // (qkv [rows][1152], bias already added).

@@ -24,20 +24,40 @@ int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t 
     return launch_pdl(embed_kernel, dim3(rows), dim3(128), 0, st, 1, embed, ids, rows, x);
 }
 
+// q -> four signed 7-bit limbs, q = l0 + 2^7 l1 + 2^14 l2 + 2^21 l3 (|q| < 2^27).
+__device__ __forceinline__ void limbs_of(int q, int (&l)[4]) {
+    l[0] = ((q + 64) & 127) - 64;
+    const int r1 = (q - l[0]) >> 7;
+    l[1] = ((r1 + 64) & 127) - 64;
+    const int r2 = (r1 - l[1]) >> 7;
+    l[2] = ((r2 + 64) & 127) - 64;
+    l[3] = (r2 - l[2]) >> 7;
+}
+__device__ __forceinline__ uint32_t limb_pair(float a, float b, int e, int l) {
+    int la[4], lb[4];
+    limbs_of(__float2int_rn(ldexpf(a, 26 - e)), la);
+    limbs_of(__float2int_rn(ldexpf(b, 26 - e)), lb);
+    return ((uint32_t)la[l] & 0xffu) | (((uint32_t)lb[l] & 0xffu) << 8);
+}
+
 // model_backend.py:69-71, one warp per row. The row and gamma are loaded into
 // registers up front (14 words per lane, all requests in flight at once); the
-// sum of squares runs in the order lane, lane + 32, ... as before.
+// sum of squares runs in the order lane, lane + 32, ... With limbs != nullptr
+// the normalised row is also written as the four int8 limb planes of its
+// 28-bit alignment (limbs[l][row][k], planes `plane` bytes apart, rows
+// `ld` bytes apart) with its exponent ex[row], the operand of the exact
+// tensor-core projections; out may then be null.
 constexpr int RMS_WORDS = QB_HID / 2 / 32;
 __global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict__ x,
                                                      const uint16_t *__restrict__ gamma, int rows, float eps,
-                                                     uint16_t *__restrict__ out) {
+                                                     uint16_t *__restrict__ out, int8_t *limbs, size_t plane, int ld,
+                                                     int *ex) {
     pdl_wait();
     pdl_trigger();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const uint32_t *xr = reinterpret_cast<const uint32_t *>(x + (size_t)row * QB_HID);
     const uint32_t *gr = reinterpret_cast<const uint32_t *>(gamma);
-    uint32_t *orow = reinterpret_cast<uint32_t *>(out + (size_t)row * QB_HID);
     uint32_t xv[RMS_WORDS], gv[RMS_WORDS];
 #pragma unroll
     for (int j = 0; j < RMS_WORDS; ++j) xv[j] = xr[lane + 32 * j];
@@ -52,17 +72,104 @@ __global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict_
     }
     ss = warp_sum(ss);
     const float rs = 1.0f / sqrtf(ss / (float)QB_HID + eps);
+    float a[RMS_WORDS], b[RMS_WORDS];
+    float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < RMS_WORDS; ++j) {
-        const float a = rbf(rbf(bflo(xv[j]) * rs) * bflo(gv[j]));
-        const float b = rbf(rbf(bfhi(xv[j]) * rs) * bfhi(gv[j]));
-        orow[lane + 32 * j] = (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
+        a[j] = rbf(rbf(bflo(xv[j]) * rs) * bflo(gv[j]));
+        b[j] = rbf(rbf(bfhi(xv[j]) * rs) * bfhi(gv[j]));
+        amax = fmaxf(amax, fmaxf(fabsf(a[j]), fabsf(b[j])));
+    }
+    if (out != nullptr) {
+        uint32_t *orow = reinterpret_cast<uint32_t *>(out + (size_t)row * QB_HID);
+#pragma unroll
+        for (int j = 0; j < RMS_WORDS; ++j) orow[lane + 32 * j] = (uint32_t)f2bf(a[j]) | ((uint32_t)f2bf(b[j]) << 16);
+    }
+    if (limbs != nullptr) {
+        amax = warp_max(amax);
+        const int e = amax > 0.f ? ilogbf(amax) : 0;
+#pragma unroll
+        for (int j = 0; j < RMS_WORDS; ++j) {
+            const int k = 2 * (lane + 32 * j);
+#pragma unroll
+            for (int l = 0; l < 4; ++l)
+                *reinterpret_cast<uint16_t *>(limbs + l * plane + (size_t)row * ld + k) =
+                    (uint16_t)limb_pair(a[j], b[j], e, l);
+        }
+        if (lane == 0) ex[row] = e;
     }
 }
 
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st) {
     if (rows <= 0) return -1;
-    return launch_pdl(rmsnorm_kernel, dim3((rows + 1) / 2), dim3(64), 0, st, 1, x, gamma, rows, eps, out);
+    return launch_pdl(rmsnorm_kernel, dim3((rows + 1) / 2), dim3(64), 0, st, 1, x, gamma, rows, eps, out,
+                      (int8_t *)nullptr, (size_t)0, 0, (int *)nullptr);
+}
+
+int launch_rmsnorm_limbs(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out,
+                         int8_t *limbs, size_t plane, int ld, int *ex, cudaStream_t st) {
+    if (rows <= 0 || !limbs || !ex || (ld & 15) || (plane & 15)) return -1;
+    return launch_pdl(rmsnorm_kernel, dim3((rows + 1) / 2), dim3(64), 0, st, 1, x, gamma, rows, eps, out, limbs,
+                      plane, ld, ex);
+}
+
+// x [rows][K] (bf16) -> the four int8 limb planes of each row's 28-bit
+// alignment (limbs[l][row][k]) and its exponent ex[row]: one CTA per row,
+// 16-byte pieces of 8 values, the maximum reduced through shared memory.
+constexpr int AQ_THREADS = 256;
+template <int K>
+__global__ void __launch_bounds__(AQ_THREADS) act_quant_kernel(const uint16_t *__restrict__ x, int8_t *limbs,
+                                                               size_t plane, int ld, int *ex) {
+    constexpr int NPC = K / 8, NP = (NPC + AQ_THREADS - 1) / AQ_THREADS;
+    __shared__ float wmax[AQ_THREADS / 32];
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)row * K);
+    uint4 xv[NP];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const int p = threadIdx.x + AQ_THREADS * j;
+        xv[j] = p < NPC ? xr[p] : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) amax = fmaxf(amax, fmaxf(fabsf(bflo(w[t])), fabsf(bfhi(w[t]))));
+    }
+    amax = warp_max(amax);
+    if (lane == 0) wmax[warp] = amax;
+    __syncthreads();
+    amax = wmax[0];
+#pragma unroll
+    for (int w2 = 1; w2 < AQ_THREADS / 32; ++w2) amax = fmaxf(amax, wmax[w2]);
+    const int e = amax > 0.f ? ilogbf(amax) : 0;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const int p = threadIdx.x + AQ_THREADS * j;
+        if (p >= NPC) continue;
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            uint2 pk;
+            pk.x = limb_pair(bflo(w[0]), bfhi(w[0]), e, l) | (limb_pair(bflo(w[1]), bfhi(w[1]), e, l) << 16);
+            pk.y = limb_pair(bflo(w[2]), bfhi(w[2]), e, l) | (limb_pair(bflo(w[3]), bfhi(w[3]), e, l) << 16);
+            *reinterpret_cast<uint2 *>(limbs + l * plane + (size_t)row * ld + 8 * p) = pk;
+        }
+    }
+    if (threadIdx.x == 0) ex[row] = e;
+}
+
+int launch_act_quant(const uint16_t *x, int rows, int k, int8_t *limbs, size_t plane, int ld, int *ex,
+                     cudaStream_t st) {
+    if (rows <= 0 || !limbs || !ex || (ld & 15) || (plane & 15)) return -1;
+    if (k == QB_HID)
+        return launch_pdl(act_quant_kernel<QB_HID>, dim3(rows), dim3(AQ_THREADS), 0, st, 1, x, limbs, plane, ld, ex);
+    if (k == QB_FFN)
+        return launch_pdl(act_quant_kernel<QB_FFN>, dim3(rows), dim3(AQ_THREADS), 0, st, 1, x, limbs, plane, ld, ex);
+    return -1;
 }
 
 // model_backend.py:73-78 in place on [rows][heads][64]; one warp per (row, head).

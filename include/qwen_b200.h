@@ -164,16 +164,19 @@ int qwen_b200_op_gemm_w8a16(const uint16_t *x, uint32_t rows, uint32_t k, const 
  * (model_backend.py:103,107). */
 int qwen_b200_op_gemm_w8a16_residual(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
                                      const float *scale, uint32_t n, uint16_t *y, void *stream);
-/* Tensor-core (tcgen05) form of the same GEMM for rows > 8: host helper that
- * re-tiles a row-major int8 weight [n][k] into [n/128][k/64][128][64] with
- * each group of four codes stored as (k0, k2, k1, k3) (n % 128 == 0,
- * k % 64 == 0), the workspace size, and the launch. epi: 0
- * plain, 1 + bias, 2 residual (y in/out), 3 SiLU(gate)*up over interleaved
- * gate/up rows (y [rows][n/2]). The first 4 workspace bytes become non-zero if
- * a bounded pipeline wait expired. */
-int qwen_b200_tile_weights(const int8_t *w, uint32_t n, uint32_t k, int8_t *tiled);
+/* Tensor-core (tcgen05 kind::i8) form of the same projection for rows > 8,
+ * with the GEMV's exact integer sums: every activation row is aligned to the
+ * exponent of its largest |x| as a 28-bit integer held in four int8 limb
+ * planes, each limb plane is multiplied with the row-major int8 weight
+ * [n][k] on the tensor cores into int32 accumulators, the four are folded to
+ * one exact int64 sum per output and rounded once to fp32
+ * (src/rtl/qwen_gemm_array_i.sv header: block-aligned integer sums).
+ * k is 896 or 4864, n % 128 == 0. epi: 0 plain, 1 + bias, 2 residual (y
+ * in/out), 3 SiLU(gate)*up over interleaved gate/up rows (y [rows][n/2]).
+ * The workspace holds the limb planes and exponents; its first 4 bytes become
+ * non-zero if a bounded pipeline wait expired. */
 size_t qwen_b200_gemm_tc_workspace(uint32_t rows, uint32_t n, uint32_t k);
-int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w_tiled,
+int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
                                const float *scale, uint32_t n, const uint16_t *bias, int epi, uint16_t *y,
                                void *workspace, size_t workspace_bytes, void *stream);
 /* Host-side cos/sin table [positions][64] (cos 0..31, sin 32..63) for

@@ -118,13 +118,24 @@ def test_rope_table_matches_oracle():
     assert np.array_equal(t, ref.rope_table(300))
 
 
-def test_weight_tiling_layout():
-    import numpy as np
-    w = np.arange(256 * 128, dtype=np.int64).astype(np.int8).reshape(256, 128)
-    t = np.empty_like(w)
+def test_tensor_core_gemm_workspace_and_argument_checks():
+    """Workspace = 256-byte error word + four int8 limb planes [4][rows][k] +
+    one exponent per row; malformed shapes are rejected before any launch."""
     L = qwen_b200.lib()
-    assert L.qwen_b200_tile_weights(w.ctypes.data_as(ctypes.c_void_p), 256, 128, t.ctypes.data_as(ctypes.c_void_p)) == 0
-    exp = w.reshape(2, 128, 2, 16, 4).transpose(0, 2, 1, 3, 4)[..., [0, 2, 1, 3]]
-    assert np.array_equal(t.reshape(2, 2, 128, 16, 4), exp)
-    assert L.qwen_b200_tile_weights(w.ctypes.data_as(ctypes.c_void_p), 200, 128, t.ctypes.data_as(ctypes.c_void_p)) \
-        == _lib.EINVAL
+    assert L.qwen_b200_gemm_tc_workspace(64, 896, 896) == 256 + 4 * 64 * 896 + 4 * 64
+    assert L.qwen_b200_gemm_tc_workspace(9, 896, 4864) == 256 + 4 * 9 * 4864 + 4 * 9
+    p = ctypes.c_void_p(16)
+    ws = L.qwen_b200_gemm_tc_workspace(16, 896, 896)
+    ok = dict(x=p, rows=16, k=896, w=p, scale=p, n=896, bias=None, epi=0, y=p, ws=p, ws_bytes=ws, st=None)
+
+    def call(**kw):
+        a = dict(ok, **kw)
+        return L.qwen_b200_op_gemm_w8a16_tc(a['x'], a['rows'], a['k'], a['w'], a['scale'], a['n'], a['bias'],
+                                            a['epi'], a['y'], a['ws'], a['ws_bytes'], a['st'])
+    assert call(x=None) == _lib.EINVAL
+    assert call(k=640) == _lib.EINVAL           # only the model's two projection depths
+    assert call(n=200) == _lib.EINVAL           # whole 128-row weight tiles
+    assert call(rows=0) == _lib.EINVAL
+    assert call(epi=1) == _lib.EINVAL           # bias epilogue without a bias
+    assert call(epi=7) == _lib.EINVAL
+    assert call(ws_bytes=ws - 1) == _lib.EINVAL

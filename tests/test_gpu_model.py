@@ -1,5 +1,5 @@
 """Whole-model parity on the B200: the engine (through the C ABI) against the
-oracle in KV8 mode on the seeded synthetic Qwen2.5-0.5B, following the
+oracle in KV8 + exact-projection mode on the seeded synthetic Qwen2.5-0.5B, following the
 reference's own sign-off (legacy_.../tests/compare_rtl_math.py:38 token
 equality on identical histories; compare_all_layers.py given-operand stages).
 
@@ -29,7 +29,7 @@ def engine(sd_root):
 
 @pytest.fixture(scope='module')
 def oracle_kv8(oracle_model):
-    oracle_model.set_mode(ref.KV8)
+    oracle_model.set_mode(ref.KV8 | ref.EXACT)
     yield oracle_model
     oracle_model.set_mode(0)
 
