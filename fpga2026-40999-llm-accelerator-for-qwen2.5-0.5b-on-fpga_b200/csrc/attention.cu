@@ -80,12 +80,12 @@ __global__ void __launch_bounds__(AT) attn_score_kernel(AttnArgs a) {
             const uint16_t *qh = a.q + (size_t)r * QB_HID + (g * 7 + h) * QB_HD;
             const float q0 = bf2f(qh[lane]), q1 = bf2f(qh[lane + 32]);
             const float amax = warp_max(fmaxf(fabsf(q0), fabsf(q1)));
-            const int e = amax > 0.f ? ilogbf(amax) : 0;
+            const int e = row_exponent(amax);
             const float qv[2] = {q0, q1};
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
                 const int d = lane + 32 * k;
-                const int qi = __float2int_rn(ldexpf(qv[k], 26 - e));
+                const int qi = align28_int(qv[k], e);
                 const int l0 = ((qi + 64) & 127) - 64;
                 const int r1 = (qi - l0) >> 7;
                 const int l1 = ((r1 + 64) & 127) - 64;
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(AT) attn_score_kernel(AttnArgs a) {
         for (int h = 0; h < 7; ++h) {
             const long long dot = (long long)acc[h][0] + ((long long)acc[h][1] << 7) + ((long long)acc[h][2] << 14) +
                                   ((long long)acc[h][3] << 21);
-            sc[h] = rbf(__fmul_rn(ldexpf(__ll2float_rn(dot), qe[h] - 26), s) * 0.125f);
+            sc[h] = rbf(__fmul_rn(unalign28(dot, qe[h]), s) * 0.125f);
             a.S[((size_t)r * QB_QH + g * 7 + h) * a.cap + t] = sc[h];
         }
     } else {

@@ -1,33 +1,38 @@
 // GQA decode/prefill attention over the KV8 cache in one launch: one
 // thread-block cluster per (query row, KV head), its CTAs splitting the row's
 // context. Arithmetic of legacy_100mhz_closed/src/PC/model_backend.py:97-102
-// over the KV8 cache in the accelerator's order (oracle ref_kv8_scores):
+// over the KV8 cache in the accelerator's order, every sum exact (the
+// oracle's REF_KV8 | REF_EXACT mode):
 //   S[h][t] = bf16(RN32(RN32(Q_h . kcode[t]) * 2^(E_h-26) * kscale[t]) / 8)
 //             with q_h aligned to its largest exponent E_h as 28-bit integers
 //             Q_h[d] = rint(q_h[d] * 2^(26-E_h)) and an exact integer dot
-//   P[h][t] = bf16(exp(S[h][t] - max_t S[h]) * (1 / sum_t exp(S[h][t] - max S[h])))
-//   ctx[h]  = bf16(sum_t P[h][t] * vscale[t] * vcode[t])
-//
-// The seven query heads of a KV head make the score product a small matrix
-// product on the tensor cores (mma.sync, register fragments):
-//   scores   D[16 keys][8 heads] = Kcode[16][64] . Q^T[64][8] with int8 x int8
-//            -> int32 products (m16n8k32): Q is split into four signed 7-bit
-//            limbs, the raw codes are the A operand as they sit in shared
-//            memory, and the four exact limb sums combine in int64; the
-//            scores are therefore bit-identical to the oracle's
-//   context  on the CUDA cores with the oracle's products P * (vcode * vscale)
-//            (packed f32x2 fmas), keys in 16 slices, slices then ranks added
-//            in order
+//   E[h][t] = qexp(S[h][t] - max_t S[h]),  Z_h = RN32(sum_t rint(E * 2^40)) 2^-40
+//   P[h][t] = bf16(E[h][t] / Z_h),  w[h][t] = RN32(P[h][t] * vscale[t])
+//   ctx[h]  = bf16(RN32(sum_t W[h][t] * vcode[t]) * 2^(F_h-26)),
+//             W = rint(w * 2^(26-F_h)), F_h = exponent of
+//             RN32(bf16(1/Z_h) * max_t vscale[t]) (a bound of every w)
+// (the V scale enters the reduction with the probability, as in
+// src/rtl/kv8_v_pscale.sv:1-20). Both products run on the tensor cores
+// (mma.sync, register fragments), int8 x int8 -> int32:
+//   scores   D[16 keys][8 heads] = Kcode[16][64] . Q^T[64][8] (m16n8k32): Q
+//            is split into four signed 7-bit limbs, the raw codes are the A
+//            operand as they sit in shared memory, the limb sums fold in int64
+//   context  D[16 dims][8 heads] += Vcode^T[16][16 keys] . W[16 keys][8]
+//            (m16n8k16, s8 x u8): W >= 0 is split into its four bytes (one
+//            n-tile each), the V codes are transposed 4 x 4 bytes at a time
+//            with byte permutes into the A fragment; a warp covers all 64
+//            dims of its 16 keys, accumulating int32 per byte plane
+// so the context is bit-identical to the oracle's whatever the split.
 // K and then V stream through one 8-slot shared-memory ring in 128-key chunks
 // (8 KB of codes) by bulk copy, completing on mbarriers (bounded waits); the
 // per-key scales are staged in shared memory once.
-//   phase 1  scores of this CTA's keys -> shared memory (fp32 holding bf16
-//            values), per-head CTA max; the cluster forms the global max
-//   phase 2  E = exp(S - max) in place, per-head sums; the cluster adds the
-//            sums in rank order
-//   phase 3  P = bf16(E / sum) per chunk, partial P.V per key slice
-//   phase 4  slice partials added in slice order, CTA rank 0 adds the ranks'
-//            partials in rank order and writes ctx (bf16)
+//   phase 1  scores of this CTA's keys -> shared memory, per-head CTA max and
+//            the CTA's largest V scale; the cluster forms the global values
+//   phase 2  E = qexp(S - max) in place, exact per-head sums; the cluster
+//            adds them; per-head 1/Z and context alignment F_h
+//   phase 3  per chunk: W from E, the products on the tensor cores
+//   phase 4  byte planes fold to int64, the warps' partials are added, CTA
+//            rank 0 adds the ranks' partials and writes ctx (bf16)
 // No global scratch, no atomics; results do not depend on scheduling.
 #include "common.cuh"
 #include "kernels.h"
@@ -56,13 +61,17 @@ struct AcArgs {
 };
 
 struct AcSmem {
-    int ring, s, sld, kss, vss, p, stat, red, bars, total;
+    int ring, s, sld, kss, vss, stat, red, bars, total;
 };
 
 // ring [8][128][64] int8 | S [7][kpc + 4] fp32 | K scales [kpc] | V scales
-// [kpc] | P of one chunk [128][8] | stat (max[8], sum[8], ctx partial
-// [7][64]) | per-warp reductions [2][8][8] | mbarriers [8]. The per-slice
-// context partials [16][8][64] reuse the ring once the last chunk is consumed.
+// [kpc] | stat | per-warp reductions | mbarriers [8]. stat: max[8] (head 7:
+// largest V scale) | Z[8] int64 | per-head inv, align factors, F [4][8] |
+// context partial [7][64] int64. Per-warp reductions: max [8][8] fp32, Z
+// [8][8] int64. The per-warp context partials [8][8][64] int64 reuse the ring
+// once the last chunk is consumed.
+constexpr int AC_ST_Z = 32, AC_ST_HV = 96, AC_ST_CTX = 224;
+constexpr int AC_STAT_BYTES = AC_ST_CTX + 7 * QB_HD * 8;
 __host__ __device__ inline AcSmem ac_smem(int kpc) {
     AcSmem L;
     L.ring = 0;
@@ -70,13 +79,13 @@ __host__ __device__ inline AcSmem ac_smem(int kpc) {
     L.sld = kpc + 4;  // row stride: the 4 head rows a warp writes fall in distinct banks
     L.kss = L.s + 7 * L.sld * 4;
     L.vss = L.kss + kpc * 4;
-    L.p = L.vss + kpc * 4;
-    L.stat = L.p + AM_CHUNK * 8 * 4;
-    L.red = L.stat + (16 + 7 * QB_HD) * 4;
-    L.bars = L.red + 2 * AM_WARPS * 8 * 4;
+    L.stat = L.vss + kpc * 4;
+    L.red = L.stat + AC_STAT_BYTES;
+    L.bars = L.red + AM_WARPS * 8 * 4 + AM_WARPS * 8 * 8;
     L.total = L.bars + AM_SLOTS_RING * 8;
     return L;
 }
+static_assert(AM_WARPS * 8 * QB_HD * 8 <= AM_SLOTS_RING * AM_STAGE_BYTES, "context partials fit in the ring");
 
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
@@ -87,20 +96,27 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
+__device__ __forceinline__ void mma_s8u8_16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t r;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
     return r;
+}
+
+// 4 x 4 byte transpose: o[j] byte i = r[i] byte j.
+__device__ __forceinline__ void transpose4(const uint32_t (&r)[4], uint32_t (&o)[4]) {
+    const uint32_t t0 = prmt(r[0], r[1], 0x5140u), t1 = prmt(r[0], r[1], 0x7362u);
+    const uint32_t t2 = prmt(r[2], r[3], 0x5140u), t3 = prmt(r[2], r[3], 0x7362u);
+    o[0] = prmt(t0, t2, 0x5410u);
+    o[1] = prmt(t0, t2, 0x7632u);
+    o[2] = prmt(t1, t3, 0x5410u);
+    o[3] = prmt(t1, t3, 0x7632u);
 }
 
 template <bool CLUSTER>
@@ -112,11 +128,13 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
     float *S = reinterpret_cast<float *>(sm + L.s);
     float *kss = reinterpret_cast<float *>(sm + L.kss);
     float *vss = reinterpret_cast<float *>(sm + L.vss);
-    float *part = reinterpret_cast<float *>(sm + L.ring);  // phase 4, after the last chunk
-    float *P = reinterpret_cast<float *>(sm + L.p);
-    float *stat = reinterpret_cast<float *>(sm + L.stat);
-    float *ctxp = stat + 16;
+    long long *part = reinterpret_cast<long long *>(sm + L.ring);  // phase 4, after the last chunk
+    float *stat = reinterpret_cast<float *>(sm + L.stat);             // max[8]
+    long long *statz = reinterpret_cast<long long *>(sm + L.stat + AC_ST_Z);
+    float *hv = reinterpret_cast<float *>(sm + L.stat + AC_ST_HV);    // inv[8] s1[8] s2[8] F[8]
+    long long *ctxp = reinterpret_cast<long long *>(sm + L.stat + AC_ST_CTX);
     float *red = reinterpret_cast<float *>(sm + L.red);
+    long long *redz = reinterpret_cast<long long *>(sm + L.red + AM_WARPS * 8 * 4);
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + L.bars);
     const int sld = L.sld;
 
@@ -153,9 +171,11 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
     pdl_trigger();
     if (tid == 0)
         for (int i = 0; i < min(items, AM_SLOTS_RING); ++i) issue(i);
+    float vmax = 0.f;  // largest V scale of this CTA's keys
     for (int t = tid; t < nkeys; t += AM_THREADS) {
         kss[t] = __ldg(a.ks + kvbase + t);
         vss[t] = __ldg(a.vs + kvbase + t);
+        vmax = fmaxf(vmax, vss[t]);
     }
     bool ok = true;
 
@@ -186,11 +206,11 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
         }
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        const int e = amax > 0.f ? ilogbf(amax) : 0;
+        const int e = row_exponent(amax);
         uint32_t lb[4][4] = {};  // [limb][word of 4 dims]
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const int qi = __float2int_rn(ldexpf(qf[i], 26 - e));
+            const int qi = align28_int(qf[i], e);
             const int l0 = ((qi + 64) & 127) - 64;
             const int r1 = (qi - l0) >> 7;
             const int l1 = ((r1 + 64) & 127) - 64;
@@ -238,7 +258,7 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
                 const long long dot = (long long)d[0][f] + ((long long)d[1][f] << 7) + ((long long)d[2][f] << 14) +
                                       ((long long)d[3][f] << 21);
                 const float ks = kss[f < 2 ? k0 : k1];
-                sc[f] = rbf(__fmul_rn(ldexpf(__ll2float_rn(dot), ((f & 1) ? e_h1 : e_h0) - 26), ks) * 0.125f);
+                sc[f] = rbf(__fmul_rn(unalign28(dot, (f & 1) ? e_h1 : e_h0), ks) * 0.125f);
             }
             if (k0 < nkeys) {
                 S[h0 * sld + k0] = sc[0];
@@ -266,10 +286,12 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
         m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
         m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
     }
+    vmax = warp_max(vmax);
     if (gid == 0) {
         red[warp * 8 + h0] = m0;
-        red[warp * 8 + h1] = m1;
+        if (h1 < 7) red[warp * 8 + h1] = m1;
     }
+    if (lane == 0) red[warp * 8 + 7] = vmax;
     __syncthreads();
     if (tid < 8) {
         float m = red[tid];
@@ -277,152 +299,165 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
         stat[tid] = m;
     }
     __syncthreads();
-    float M[7];
+    float M[8];  // per-head max; M[7] = largest V scale of the row's keys
     if constexpr (CLUSTER) {
         tc::cluster_sync();
         const uint32_t sa = tc::smem_u32(stat);
 #pragma unroll
-        for (int h = 0; h < 7; ++h) M[h] = -INFINITY;
+        for (int h = 0; h < 8; ++h) M[h] = -INFINITY;
         for (int sr = 0; sr < nranks; ++sr) {
             const float4 m03 = tc::ld_dsmem_f4(sa, sr), m47 = tc::ld_dsmem_f4(sa + 16, sr);
-            const float mv[7] = {m03.x, m03.y, m03.z, m03.w, m47.x, m47.y, m47.z};
+            const float mv[8] = {m03.x, m03.y, m03.z, m03.w, m47.x, m47.y, m47.z, m47.w};
 #pragma unroll
-            for (int h = 0; h < 7; ++h) M[h] = fmaxf(M[h], mv[h]);
+            for (int h = 0; h < 8; ++h) M[h] = fmaxf(M[h], mv[h]);
         }
     } else {
 #pragma unroll
-        for (int h = 0; h < 7; ++h) M[h] = stat[h];
+        for (int h = 0; h < 8; ++h) M[h] = stat[h];
     }
 
-    // ---------------- phase 2: E = exp(S - max) in place, per-head sums
-    float lsum[7];
+    // ---------------- phase 2: E = qexp(S - max) in place, exact per-head sums
+    long long zl[7];
 #pragma unroll
     for (int h = 0; h < 7; ++h) {
-        float l = 0.f;
+        long long z = 0;
         for (int t = tid; t < nkeys; t += AM_THREADS) {
-            const float e = expf(S[h * sld + t] - M[h]);
+            const float e = qexp(__fsub_rn(S[h * sld + t], M[h]));
             S[h * sld + t] = e;
-            l += e;
+            z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
         }
-        lsum[h] = l;
+        zl[h] = z;
     }
-    float *red2 = red + AM_WARPS * 8;
 #pragma unroll
     for (int h = 0; h < 7; ++h) {
-        const float l = warp_sum(lsum[h]);
-        if (lane == 0) red2[warp * 8 + h] = l;
+        const long long z = warp_sum_ll(zl[h]);
+        if (lane == 0) redz[warp * 8 + h] = z;
     }
     __syncthreads();
     if (tid < 8) {
-        float l = 0.f;
+        long long z = 0;
         if (tid < 7)
-            for (int w = 0; w < AM_WARPS; ++w) l += red2[w * 8 + tid];
-        stat[8 + tid] = l;
+            for (int w = 0; w < AM_WARPS; ++w) z += redz[w * 8 + tid];
+        statz[tid] = z;
     }
-    __syncthreads();
-    float inv[7];  // 1 / sum per head
-    {
-        float z[8];
+    if constexpr (CLUSTER) {
+        tc::cluster_sync();
+    } else {
+        __syncthreads();
+    }
+    // per-head 1/Z, the bound of w and its alignment factors (every CTA of the
+    // cluster forms the same values from the same totals)
+    if (tid < 8) {
+        long long z = 0;
         if constexpr (CLUSTER) {
-            tc::cluster_sync();
-            const uint32_t la = tc::smem_u32(stat + 8);
-#pragma unroll
-            for (int h = 0; h < 8; ++h) z[h] = 0.f;
+            const uint32_t za = tc::smem_u32(statz) + 8u * (uint32_t)(tid & ~1);
             for (int sr = 0; sr < nranks; ++sr) {
-                const float4 l03 = tc::ld_dsmem_f4(la, sr), l47 = tc::ld_dsmem_f4(la + 16, sr);
-                const float lv[8] = {l03.x, l03.y, l03.z, l03.w, l47.x, l47.y, l47.z, l47.w};
-#pragma unroll
-                for (int h = 0; h < 8; ++h) z[h] += lv[h];
+                const float4 v = tc::ld_dsmem_f4(za, sr);
+                const longlong2 zz = *reinterpret_cast<const longlong2 *>(&v);
+                z += (tid & 1) ? zz.y : zz.x;
             }
         } else {
-#pragma unroll
-            for (int h = 0; h < 8; ++h) z[h] = stat[8 + h];
+            z = statz[tid];
         }
-#pragma unroll
-        for (int h = 0; h < 7; ++h) inv[h] = 1.0f / z[h];
+        float inv = 0.f, s1 = 0.f, s2 = 0.f;
+        int f = 0;
+        if (tid < 7 && z > 0) {
+            inv = __fdiv_rn(1.0f, __fmul_rn(__ll2float_rn(z), 0x1p-40f));
+            f = row_exponent(__fmul_rn(rbf(inv), M[7]));
+            const int sh = 26 - f, sh1 = min(sh, 127);
+            s1 = pow2i(sh1);
+            s2 = pow2i(sh - sh1);
+        }
+        hv[tid] = inv;
+        hv[8 + tid] = s1;
+        hv[16 + tid] = s2;
+        hv[24 + tid] = __int_as_float(f);
     }
+    __syncthreads();
 
-    // ---------------- phase 3: P per chunk, partial P.V on the CUDA cores
-    // with the oracle's products P * (vcode * vscale) (fp32 fma); thread =
-    // (word of 4 dims, key slice), keys slice, slice + 16, ... of the chunk
-    const int word = tid & 15, slice = tid >> 4;
-    float2 acc[4][4];  // [dim][head pair]
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
-    for (int c = 0; c < nchunks; ++c) {
-        const int item = nchunks + c;
-        const int sl = item % AM_SLOTS_RING;
-        const int c0 = c * AM_CHUNK, nc = min(AM_CHUNK, nkeys - c0);
-        for (int i = tid; i < AM_CHUNK * 8; i += AM_THREADS) {
-            const int tt = i >> 3, h = i & 7;
-            float iv = inv[0];
-#pragma unroll
-            for (int hh = 1; hh < 7; ++hh)
-                if (h == hh) iv = inv[hh];
-            P[i] = (tt < nc && h < 7) ? rbf(S[h * sld + c0 + tt] * iv) : 0.f;
-        }
-        if (ok) ok = tc::mbar_wait(&full[sl], (item / AM_SLOTS_RING) & 1, a.err, 12);
-        __syncthreads();  // P of the chunk complete
-        if (ok) {
-            const int8_t *vblk = ring + sl * AM_STAGE_BYTES;
-            for (int tt = slice; tt < nc; tt += 16) {
-                const uint32_t w = *reinterpret_cast<const uint32_t *>(vblk + tt * QB_HD + word * 4);
-                const float vsc = vss[c0 + tt];
-                float f[4];
-                i8x4_to_f32(w, f[0], f[1], f[2], f[3]);
-                const float4 p03 = *reinterpret_cast<const float4 *>(P + tt * 8);
-                const float4 p47 = *reinterpret_cast<const float4 *>(P + tt * 8 + 4);
-                const float2 pp[4] = {make_float2(p03.x, p03.y), make_float2(p03.z, p03.w),
-                                      make_float2(p47.x, p47.y), make_float2(p47.z, p47.w)};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float vd = __fmul_rn(f[j], vsc);
-                    const float2 vv = make_float2(vd, vd);
-#pragma unroll
-                    for (int hp = 0; hp < 4; ++hp) acc[j][hp] = ffma2(pp[hp], vv, acc[j][hp]);
-                }
-            }
-        }
-        __syncthreads();  // every thread is done with this slot and with P
-        if (tid == 0 && ok && item + AM_SLOTS_RING < items) issue(item + AM_SLOTS_RING);
-    }
-
-    // ---------------- phase 4: slices -> CTA partial (slice order) -> rank 0
+    // ---------------- phase 3: context on the tensor cores. Warp w takes keys
+    // 16w..16w+15 of each chunk; lane (gid, tig) supplies k slots 4tig..4tig+3
+    // = keys 16w+4tig+i: the W bytes of head gid (B) and, transposed, the V
+    // codes of dims 4gid..4gid+3 and 4gid+32..4gid+35 (A rows gid and gid+8
+    // of m-tile j hold dims 4gid+j and 4gid+32+j).
+    const bool gv = gid < 7;
+    const float inv_g = hv[gid], s1_g = hv[8 + gid], s2_g = hv[16 + gid];
+    int acc[4][4][4];  // [m-tile j][byte plane l][fragment]
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int hp = 0; hp < 4; ++hp) {
-            const int d = word * 4 + j;
-            part[(slice * 8 + 2 * hp) * QB_HD + d] = acc[j][hp].x;
-            part[(slice * 8 + 2 * hp + 1) * QB_HD + d] = acc[j][hp].y;
+        for (int l = 0; l < 4; ++l) acc[j][l][0] = acc[j][l][1] = acc[j][l][2] = acc[j][l][3] = 0;
+    for (int c = 0; c < nchunks; ++c) {
+        const int item = nchunks + c;
+        const int sl = item % AM_SLOTS_RING;
+        const int c0 = c * AM_CHUNK, kb = 16 * warp;
+        if (ok) ok = tc::mbar_wait(&full[sl], (item / AM_SLOTS_RING) & 1, a.err, 12);
+        if (ok && c0 + kb < nkeys) {
+            const int tb = c0 + kb + 4 * tig;  // first of this lane's keys (CTA-relative)
+            float4 e4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (gv) e4 = *reinterpret_cast<const float4 *>(S + gid * sld + tb);
+            const float4 v4 = *reinterpret_cast<const float4 *>(vss + tb);
+            const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
+            uint32_t wq[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float w = (gv && tb + i < nkeys) ? __fmul_rn(rbf(__fmul_rn(ev[i], inv_g)), vv[i]) : 0.f;
+                wq[i] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1_g), s2_g));
+            }
+            transpose4(wq, b);
+            const uint32_t *vrow =
+                reinterpret_cast<const uint32_t *>(ring + sl * AM_STAGE_BYTES) + (kb + 4 * tig) * (QB_HD / 4);
+            uint32_t rl[4], rh[4], alo[4], ahi[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                rl[i] = vrow[i * (QB_HD / 4) + gid];
+                rh[i] = vrow[i * (QB_HD / 4) + gid + 8];
+            }
+            transpose4(rl, alo);
+            transpose4(rh, ahi);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int l = 0; l < 4; ++l) mma_s8u8_16816(acc[j][l], alo[j], ahi[j], b[l]);
+        }
+        __syncthreads();  // every warp is done with this slot
+        if (tid == 0 && ok && item + AM_SLOTS_RING < items) issue(item + AM_SLOTS_RING);
+    }
+
+    // ---------------- phase 4: byte planes -> int64, warps -> CTA -> rank 0
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            const long long v = (long long)acc[j][0][cc] + (long long)acc[j][1][cc] * 256ll +
+                                (long long)acc[j][2][cc] * 65536ll + (long long)acc[j][3][cc] * 16777216ll;
+            const int h = 2 * tig + (cc & 1), d = 4 * gid + 32 * (cc >> 1) + j;
+            part[(warp * 8 + h) * QB_HD + d] = v;
         }
     __syncthreads();
     for (int i = tid; i < 7 * QB_HD; i += AM_THREADS) {
         const int h = i >> 6, d = i & 63;
-        float sum = 0.f;
-        for (int sl2 = 0; sl2 < 16; ++sl2) sum += part[(sl2 * 8 + h) * QB_HD + d];
+        long long sum = 0;
+#pragma unroll
+        for (int w = 0; w < AM_WARPS; ++w) sum += part[(w * 8 + h) * QB_HD + d];
         ctxp[i] = sum;
     }
     if constexpr (CLUSTER) {
         tc::cluster_sync();
         if (rank == 0) {
             const uint32_t ca = tc::smem_u32(ctxp);
-            for (int i4 = tid; i4 < 7 * QB_HD / 4; i4 += AM_THREADS) {
-                float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += AM_THREADS) {
+                long long s0 = 0, s1 = 0;
                 for (int sr = 0; sr < nranks; ++sr) {
-                    const float4 v = tc::ld_dsmem_f4(ca + 16u * i4, sr);
-                    sum.x += v.x;
-                    sum.y += v.y;
-                    sum.z += v.z;
-                    sum.w += v.w;
+                    const float4 v = tc::ld_dsmem_f4(ca + 16u * i2, sr);
+                    const longlong2 pp = *reinterpret_cast<const longlong2 *>(&v);
+                    s0 += pp.x;
+                    s1 += pp.y;
                 }
-                const int i = i4 * 4, h = i >> 6, d = i & 63;
-                uint2 o;
-                o.x = (uint32_t)f2bf(sum.x) | ((uint32_t)f2bf(sum.y) << 16);
-                o.y = (uint32_t)f2bf(sum.z) | ((uint32_t)f2bf(sum.w) << 16);
-                *reinterpret_cast<uint2 *>(a.ctx + (size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d) = o;
+                const int i = 2 * i2, h = i >> 6, d = i & 63;
+                const int f = __float_as_int(hv[24 + h]);
+                *reinterpret_cast<uint32_t *>(a.ctx + (size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d) =
+                    (uint32_t)f2bf(unalign28(s0, f)) | ((uint32_t)f2bf(unalign28(s1, f)) << 16);
             }
         }
         tc::cluster_sync();  // peers' shared memory stays alive until rank 0 has read it
@@ -430,7 +465,8 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
         __syncthreads();
         for (int i = tid; i < 7 * QB_HD; i += AM_THREADS) {
             const int h = i >> 6, d = i & 63;
-            a.ctx[(size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d] = f2bf(ctxp[i]);
+            a.ctx[(size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d] =
+                f2bf(unalign28(ctxp[i], __float_as_int(hv[24 + h])));
         }
     }
 }

@@ -55,6 +55,11 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+__device__ __forceinline__ long long warp_sum_ll(long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
 
 // (value, index) argmax with the reference's tie rule: the higher index wins
 // (model_backend.py:113-114, CONFIG.JSON "greedy latest-token-index on ties").
@@ -81,6 +86,110 @@ __device__ __forceinline__ void codes4_to_bf16(uint32_t w, uint32_t &k01, uint32
     const uint32_t w8 = w >> 8;
     k01 = bf16x2_sub(lop_or(w, 0x007F007Fu, 0x43004300u), lop_or(w, 0x00800080u, 0x43004300u));
     k23 = bf16x2_sub(lop_or(w8, 0x007F007Fu, 0x43004300u), lop_or(w8, 0x00800080u, 0x43004300u));
+}
+
+
+// ---- 28-bit row alignment of the exact projections and scores
+// A row whose largest magnitude has exponent e (|x| < 2^(e+1)) is held as the
+// integers rint(x * 2^(26 - e)) (|q| < 2^27); an exact integer sum d of such
+// a row against int8 codes returns to fp32 as RN32(d) * 2^(e - 26).
+
+// 2^n for -126 <= n <= 127 (exact)
+__device__ __forceinline__ float pow2i(int n) { return __int_as_float((n + 127) << 23); }
+
+// x * 2^(26 - e) with at most one rounding (only results below 2^-126 round,
+// and those become 0 under rint): two power-of-two factors keep each in range
+// for every bf16 exponent.
+__device__ __forceinline__ float align28(float x, int e) {
+    const int s = 26 - e, s1 = min(s, 127);
+    return (x * pow2i(s1)) * pow2i(s - s1);
+}
+__device__ __forceinline__ int align28_int(float x, int e) { return __float2int_rn(align28(x, e)); }
+
+// RN32(d) * 2^(e - 26), rounded once: the first factor keeps the product
+// normal (RN32(d) >= 1 in magnitude), so only the second can round.
+__device__ __forceinline__ float unalign28(long long d, int e) {
+    const int s = e - 26, s1 = max(s, -126);
+    return (__ll2float_rn(d) * pow2i(s1)) * pow2i(s - s1);
+}
+
+// x * 2^(bits - e) for the 21-bit grid of the RMSNorm sum of squares (same
+// two-factor scaling as align28).
+__device__ __forceinline__ float align21(float x, int e) {
+    const int s = 20 - e, s1 = min(s, 127);
+    return (x * pow2i(s1)) * pow2i(s - s1);
+}
+
+// Exponent of the largest magnitude of a row (0 for an all-zero row).
+__device__ __forceinline__ int row_exponent(float amax) { return amax > 0.f ? ilogbf(amax) : 0; }
+
+// q -> four signed 7-bit limbs, q = l0 + 2^7 l1 + 2^14 l2 + 2^21 l3 (|q| < 2^27).
+__device__ __forceinline__ void limbs4(int q, int (&l)[4]) {
+    l[0] = ((q + 64) & 127) - 64;
+    const int r1 = (q - l[0]) >> 7;
+    l[1] = ((r1 + 64) & 127) - 64;
+    const int r2 = (r1 - l[1]) >> 7;
+    l[2] = ((r2 + 64) & 127) - 64;
+    l[3] = (r2 - l[2]) >> 7;
+}
+// byte l of two values' limbs, as a 16-bit pair (a low, b high)
+__device__ __forceinline__ uint32_t limb_bytes(const int (&la)[4], const int (&lb)[4], int l) {
+    return ((uint32_t)la[l] & 0xffu) | (((uint32_t)lb[l] & 0xffu) << 8);
+}
+
+
+// ---- fixed-operation exp and the exact RMSNorm scale
+// exp(x) by Cody-Waite range reduction and a degree-7 Taylor polynomial
+// (W. J. Cody, W. Waite, Software Manual for the Elementary Functions, 1980):
+// n = rint(x log2 e), r = x - n ln2 with ln2 split into a 15-bit head and a
+// tail, exp(x) = 2^n sum_{k<=7} r^k/k! by Horner's rule. Each step is one
+// IEEE fp32 operation written with an explicit rounding intrinsic, so the
+// result is the same bits as the oracle's ref_qexp (within 1 ulp of exp).
+__device__ __forceinline__ float qexp(float x) {
+    if (!(x >= -104.0f)) return 0.0f;
+    if (x > 88.75f) return __int_as_float(0x7f800000);
+    const float n = rintf(__fmul_rn(x, 1.44269504f));
+    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    r = __fmaf_rn(-n, 1.42860677e-6f, r);
+    float p = 1.98412698e-4f;
+    p = __fmaf_rn(p, r, 1.38888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = (int)n, n1 = min(max(ni, -126), 127);
+    return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(ni - n1));
+}
+
+// SiLU(g) = g / (1 + exp(-g)) with qexp (model_backend.py:106)
+__device__ __forceinline__ float silu_q(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, qexp(-g))); }
+
+// RMSNorm scale 1/sqrt(mean(x^2) + eps) of a row of K values whose lane
+// share is xv (two bf16 per word), the sum of squares exact on the grid of
+// the row's 21-bit alignment: X = rint(x 2^(20-E)), ss = RN32(sum X^2)
+// 2^(2E-40) (model_backend.py:69-71 in the oracle's exact order). e is the
+// row exponent (warp-wide).
+template <int NW>
+__device__ __forceinline__ float rms_scale_exact(const uint32_t (&xv)[NW], int K, float eps, int e) {
+    long long s2 = 0;
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+        const long long a = __float2int_rn(align21(bflo(xv[j]), e));
+        const long long b = __float2int_rn(align21(bfhi(xv[j]), e));
+        s2 += a * a + b * b;
+    }
+    s2 = warp_sum_ll(s2);
+    const float ss = ldexpf(__ll2float_rn(s2), 2 * e - 40);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+}
+template <int NW>
+__device__ __forceinline__ int row_exponent_words(const uint32_t (&xv)[NW]) {
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < NW; ++j) amax = fmaxf(amax, fmaxf(fabsf(bflo(xv[j])), fabsf(bfhi(xv[j]))));
+    return row_exponent(warp_max(amax));
 }
 
 }  // namespace qb

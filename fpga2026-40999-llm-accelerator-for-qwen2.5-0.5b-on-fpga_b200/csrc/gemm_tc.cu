@@ -89,7 +89,7 @@ __device__ __forceinline__ void tmem_ld16i(uint32_t taddr, int (&v)[16]) {
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float exact_acc(long long dot, int e) { return ldexpf(__ll2float_rn(dot), e - 26); }
+__device__ __forceinline__ float exact_acc(long long dot, int e) { return unalign28(dot, e); }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
@@ -188,7 +188,7 @@ __device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int
                   rbf(rbf(exact_acc(t[2], e)) * sc.z), rbf(rbf(exact_acc(t[3], e)) * sc.w)};
     if constexpr (EPI == EPI_SWIGLU) {
         // channels 2j (gate j) and 2j+1 (up j): model_backend.py:105-106
-        const float s0 = o[0] / (1.0f + expf(-o[0])), s1 = o[2] / (1.0f + expf(-o[2]));
+        const float s0 = silu_q(o[0]), s1 = silu_q(o[2]);
         const uint32_t w = (uint32_t)f2bf(rbf(s0) * o[1]) | ((uint32_t)f2bf(rbf(s1) * o[3]) << 16);
         *reinterpret_cast<uint32_t *>(a.y + (size_t)mg * (a.N >> 1) + (n >> 1)) = w;
     } else {

@@ -17,25 +17,11 @@
 
 namespace qb {
 
-// q -> four signed 7-bit limbs, q = l0 + 2^7 l1 + 2^14 l2 + 2^21 l3 (|q| < 2^27).
-__device__ __forceinline__ void limbs4(int q, int (&l)[4]) {
-    l[0] = ((q + 64) & 127) - 64;
-    const int r1 = (q - l[0]) >> 7;
-    l[1] = ((r1 + 64) & 127) - 64;
-    const int r2 = (r1 - l[1]) >> 7;
-    l[2] = ((r2 + 64) & 127) - 64;
-    l[3] = (r2 - l[2]) >> 7;
-}
-
-__device__ __forceinline__ uint32_t limb_bytes(const int (&la)[4], const int (&lb)[4], int l) {
-    return ((uint32_t)la[l] & 0xffu) | (((uint32_t)lb[l] & 0xffu) << 8);
-}
-
 // Rows [m0, m0+mrows) of x [rows][K] (bf16) as int8 limb planes
 // xl[m][limb][k] of the row's 28-bit alignment and its exponent ex[m] (zero
 // rows beyond mrows); with gamma != nullptr the row is RMSNormed first:
 // bf16(bf16(x * 1/sqrt(mean(x^2) + eps)) * gamma) (model_backend.py:69-71),
-// the sum of squares in the same order as rmsnorm_kernel. All warps work on
+// the sum of squares exact as in rmsnorm_kernel. All warps work on
 // each row: for K = 896 every warp loads the whole row into registers (so
 // every warp forms the same sum and maximum) and converts its share of the
 // words; wider rows are split across the warps, the maximum meeting in
@@ -68,15 +54,7 @@ __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int
                 uint32_t gv[NWD];
 #pragma unroll
                 for (int j = 0; j < NWD; ++j) gv[j] = __ldg(g32 + lane + 32 * j);
-                float ss = 0.f;
-#pragma unroll
-                for (int j = 0; j < NWD; ++j) {
-                    const float p = bflo(xv[j]), q = bfhi(xv[j]);
-                    ss += p * p;
-                    ss += q * q;
-                }
-                ss = warp_sum(ss);
-                const float rs = 1.0f / sqrtf(ss / (float)K + eps);
+                const float rs = rms_scale_exact(xv, K, eps, row_exponent_words(xv));
 #pragma unroll
                 for (int j = 0; j < NWD; ++j) {
                     a[j] = rbf(rbf(bflo(xv[j]) * rs) * bflo(gv[j]));
@@ -93,13 +71,13 @@ __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int
 #pragma unroll
             for (int j = 0; j < NWD; ++j) amax = fmaxf(amax, fmaxf(fabsf(a[j]), fabsf(b[j])));
             amax = warp_max(amax);
-            const int e = amax > 0.f ? ilogbf(amax) : 0;
+            const int e = row_exponent(amax);
 #pragma unroll
             for (int j = 0; j < NWD; ++j) {
                 if (j % NWARP != warp) continue;
                 int la[4], lb[4];
-                limbs4(__float2int_rn(ldexpf(a[j], 26 - e)), la);
-                limbs4(__float2int_rn(ldexpf(b[j], 26 - e)), lb);
+                limbs4(align28_int(a[j], e), la);
+                limbs4(align28_int(b[j], e), lb);
                 const int i = lane + 32 * j;
 #pragma unroll
                 for (int l = 0; l < 4; ++l)
@@ -130,7 +108,7 @@ __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int
 #pragma unroll
             for (int w2 = 1; w2 < NWARP; ++w2) amax = fmaxf(amax, wmax[w2]);
             __syncthreads();  // wmax is reused by the next row
-            const int e = amax > 0.f ? ilogbf(amax) : 0;
+            const int e = row_exponent(amax);
 #pragma unroll
             for (int j = 0; j < NP; ++j) {
                 const int p = threadIdx.x + NT * j;
@@ -140,8 +118,8 @@ __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     int la[4], lb[4];
-                    limbs4(__float2int_rn(ldexpf(bflo(w[t]), 26 - e)), la);
-                    limbs4(__float2int_rn(ldexpf(bfhi(w[t]), 26 - e)), lb);
+                    limbs4(align28_int(bflo(w[t]), e), la);
+                    limbs4(align28_int(bfhi(w[t]), e), lb);
 #pragma unroll
                     for (int l = 0; l < 4; ++l) {
                         const uint32_t two = limb_bytes(la, lb, l);
@@ -159,12 +137,6 @@ __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int
         }
     }
     __syncthreads();
-}
-
-__device__ __forceinline__ long long warp_sum_ll(long long v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
 }
 
 // One warp: the dot products of RW weight rows with MT activation rows.
@@ -232,7 +204,7 @@ __device__ __forceinline__ void gemv_dot(const GemvRows<K, RW> &g, const int8_t 
             long long v = (long long)d[r][m][0] + ((long long)d[r][m][1] << 7) + ((long long)d[r][m][2] << 14) +
                           ((long long)d[r][m][3] << 21);
             v = warp_sum_ll(v);
-            acc[r][m] = ldexpf(__ll2float_rn(v), ex[m] - 26);
+            acc[r][m] = unalign28(v, ex[m]);
         }
 }
 
@@ -267,7 +239,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_kernel(const uint16_t *__restric
                 const int ng = n0 + 2 * p;
                 const float g = rbf(rbf(acc[2 * p][m]) * scale[ng]);
                 const float u = rbf(rbf(acc[2 * p + 1][m]) * scale[ng + 1]);
-                const float sl = g / (1.0f + expf(-g));
+                const float sl = silu_q(g);
                 y[(size_t)(m0 + m) * nh + (ng >> 1)] = f2bf(rbf(sl) * u);
             }
     } else {

@@ -24,25 +24,9 @@ int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t 
     return launch_pdl(embed_kernel, dim3(rows), dim3(128), 0, st, 1, embed, ids, rows, x);
 }
 
-// q -> four signed 7-bit limbs, q = l0 + 2^7 l1 + 2^14 l2 + 2^21 l3 (|q| < 2^27).
-__device__ __forceinline__ void limbs_of(int q, int (&l)[4]) {
-    l[0] = ((q + 64) & 127) - 64;
-    const int r1 = (q - l[0]) >> 7;
-    l[1] = ((r1 + 64) & 127) - 64;
-    const int r2 = (r1 - l[1]) >> 7;
-    l[2] = ((r2 + 64) & 127) - 64;
-    l[3] = (r2 - l[2]) >> 7;
-}
-__device__ __forceinline__ uint32_t limb_pair(float a, float b, int e, int l) {
-    int la[4], lb[4];
-    limbs_of(__float2int_rn(ldexpf(a, 26 - e)), la);
-    limbs_of(__float2int_rn(ldexpf(b, 26 - e)), lb);
-    return ((uint32_t)la[l] & 0xffu) | (((uint32_t)lb[l] & 0xffu) << 8);
-}
-
 // model_backend.py:69-71, one warp per row. The row and gamma are loaded into
 // registers up front (14 words per lane, all requests in flight at once); the
-// sum of squares runs in the order lane, lane + 32, ... With limbs != nullptr
+// sum of squares is exact on the row's 21-bit grid (rms_scale_exact). With limbs != nullptr
 // the normalised row is also written as the four int8 limb planes of its
 // 28-bit alignment (limbs[l][row][k], planes `plane` bytes apart, rows
 // `ld` bytes apart) with its exponent ex[row], the operand of the exact
@@ -63,15 +47,7 @@ __global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict_
     for (int j = 0; j < RMS_WORDS; ++j) xv[j] = xr[lane + 32 * j];
 #pragma unroll
     for (int j = 0; j < RMS_WORDS; ++j) gv[j] = __ldg(gr + lane + 32 * j);
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < RMS_WORDS; ++j) {
-        const float a = bflo(xv[j]), b = bfhi(xv[j]);
-        ss += a * a;
-        ss += b * b;
-    }
-    ss = warp_sum(ss);
-    const float rs = 1.0f / sqrtf(ss / (float)QB_HID + eps);
+    const float rs = rms_scale_exact(xv, QB_HID, eps, row_exponent_words(xv));
     float a[RMS_WORDS], b[RMS_WORDS];
     float amax = 0.f;
 #pragma unroll
@@ -87,14 +63,17 @@ __global__ void __launch_bounds__(64) rmsnorm_kernel(const uint16_t *__restrict_
     }
     if (limbs != nullptr) {
         amax = warp_max(amax);
-        const int e = amax > 0.f ? ilogbf(amax) : 0;
+        const int e = row_exponent(amax);
 #pragma unroll
         for (int j = 0; j < RMS_WORDS; ++j) {
+            int la[4], lb[4];
+            limbs4(align28_int(a[j], e), la);
+            limbs4(align28_int(b[j], e), lb);
             const int k = 2 * (lane + 32 * j);
 #pragma unroll
             for (int l = 0; l < 4; ++l)
                 *reinterpret_cast<uint16_t *>(limbs + l * plane + (size_t)row * ld + k) =
-                    (uint16_t)limb_pair(a[j], b[j], e, l);
+                    (uint16_t)limb_bytes(la, lb, l);
         }
         if (lane == 0) ex[row] = e;
     }
@@ -145,19 +124,30 @@ __global__ void __launch_bounds__(AQ_THREADS) act_quant_kernel(const uint16_t *_
     amax = wmax[0];
 #pragma unroll
     for (int w2 = 1; w2 < AQ_THREADS / 32; ++w2) amax = fmaxf(amax, wmax[w2]);
-    const int e = amax > 0.f ? ilogbf(amax) : 0;
+    const int e = row_exponent(amax);
 #pragma unroll
     for (int j = 0; j < NP; ++j) {
         const int p = threadIdx.x + AQ_THREADS * j;
         if (p >= NPC) continue;
         const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+        uint32_t pk[4][2];  // [limb][byte quad]
 #pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            uint2 pk;
-            pk.x = limb_pair(bflo(w[0]), bfhi(w[0]), e, l) | (limb_pair(bflo(w[1]), bfhi(w[1]), e, l) << 16);
-            pk.y = limb_pair(bflo(w[2]), bfhi(w[2]), e, l) | (limb_pair(bflo(w[3]), bfhi(w[3]), e, l) << 16);
-            *reinterpret_cast<uint2 *>(limbs + l * plane + (size_t)row * ld + 8 * p) = pk;
+        for (int t = 0; t < 4; ++t) {
+            int la[4], lb[4];
+            limbs4(align28_int(bflo(w[t]), e), la);
+            limbs4(align28_int(bfhi(w[t]), e), lb);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const uint32_t two = limb_bytes(la, lb, l);
+                if (t & 1)
+                    pk[l][t >> 1] |= two << 16;
+                else
+                    pk[l][t >> 1] = two;
+            }
         }
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+            *reinterpret_cast<uint2 *>(limbs + l * plane + (size_t)row * ld + 8 * p) = make_uint2(pk[l][0], pk[l][1]);
     }
     if (threadIdx.x == 0) ex[row] = e;
 }

@@ -14,6 +14,11 @@
  *   scores:  per (row, head, key), fmaf over d in increasing order
  *   softmax: max, e = expf(s - max), Z = sequential sum, P = bf16(e * (1/Z))
  *   context: per (row, head, d), fmaf over keys in increasing order
+ * REF_EXACT replaces every order-dependent fp32 sum by an exact integer sum
+ * on a grid fixed by the data (projections, the RMSNorm sum of squares, the
+ * softmax sum and, with REF_KV8, the KV8 context) and expf by ref_qexp, a
+ * fixed sequence of IEEE fp32 operations, so that any implementation doing
+ * the same integer sums and the same fp32 operations matches bit for bit.
  * Build with -ffp-contract=off (oracle/Makefile).
  */
 #include "qwen_ref.h"
@@ -287,20 +292,66 @@ static float eps_of(unsigned mode) {
     return (mode & REF_CSR_EPS) ? u2f(0x35860000u) : 1e-6f; /* rtl_numeric_reference.py:18 */
 }
 
-/* model_backend.py:69-71 */
+/* exp(x) in fp32 by Cody-Waite range reduction and a degree-7 Taylor
+ * polynomial (W. J. Cody, W. Waite, Software Manual for the Elementary
+ * Functions, 1980): n = rint(x * log2 e), r = x - n*ln2 with ln2 split into a
+ * 15-bit head and a tail (two fmas), exp(x) = 2^n * sum_{k<=7} r^k/k! by
+ * Horner's rule in fmas, 2^n applied as two exact power-of-two factors. Every
+ * step is one IEEE fp32 operation, so a device version written with the same
+ * operations returns the same bits. |r| <= 0.347, truncation r^8/8! < 2^-27;
+ * within 1 ulp of exp over the range the model uses (tests/test_exact_mode.py). */
+static inline float pow2f(int n) { return u2f((uint32_t)(n + 127) << 23); } /* -126 <= n <= 127 */
+float ref_qexp(float x) {
+    if (!(x >= -104.0f)) return 0.0f; /* exp(-104) is below half the smallest subnormal; NaN -> 0 */
+    if (x > 88.75f) return INFINITY;
+    const float n = rintf(x * 1.44269504f);
+    float r = fmaf(-n, 0.693145751953125f, x);
+    r = fmaf(-n, 1.42860677e-6f, r);
+    float p = 1.98412698e-4f;
+    p = fmaf(p, r, 1.38888889e-3f);
+    p = fmaf(p, r, 8.33333333e-3f);
+    p = fmaf(p, r, 4.16666667e-2f);
+    p = fmaf(p, r, 1.66666667e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = (int)n, n1 = ni < -126 ? -126 : (ni > 127 ? 127 : ni);
+    return (p * pow2f(n1)) * pow2f(ni - n1);
+}
+static inline float exp_m(float x, unsigned mode) { return (mode & REF_EXACT) ? ref_qexp(x) : expf(x); }
+
+/* Exponent of the largest magnitude of v[0..n) (0 when all are zero). */
+static int max_exponent(const float *v, unsigned n) {
+    float amax = 0.0f;
+    for (unsigned i = 0; i < n; ++i)
+        if (fabsf(v[i]) > amax) amax = fabsf(v[i]);
+    return amax > 0.0f ? ilogbf(amax) : 0;
+}
+
+/* model_backend.py:69-71. REF_EXACT: the sum of squares is exact on the grid
+ * of the row's 21-bit alignment: X = rint(x * 2^(20-E)) (|X| < 2^21),
+ * ss = RN32(sum X^2) * 2^(2E-40) (the integer sum is below 2^52). */
 void ref_rmsnorm(const float *x, unsigned rows, const float *gamma, float eps, unsigned mode, float *out) {
     for (unsigned r = 0; r < rows; ++r) {
         const float *xr = x + (size_t)r * HID;
         float ss = 0.0f;
-        for (unsigned i = 0; i < HID; ++i) ss += xr[i] * xr[i];
+        if (mode & REF_EXACT) {
+            const int e = max_exponent(xr, HID);
+            int64_t s2 = 0;
+            for (unsigned i = 0; i < HID; ++i) {
+                const int64_t xi = (int64_t)rintf(ldexpf(xr[i], 20 - e));
+                s2 += xi * xi;
+            }
+            ss = ldexpf((float)s2, 2 * e - 40);
+        } else {
+            for (unsigned i = 0; i < HID; ++i) ss += xr[i] * xr[i];
+        }
         float mean = ss / (float)HID;
         float rs = 1.0f / sqrtf(mean + eps);
         for (unsigned i = 0; i < HID; ++i) out[(size_t)r * HID + i] = bfm(bfm(xr[i] * rs, mode) * gamma[i], mode);
     }
 }
 
-/* Raw fp32 accumulation acc[r][n] = sum_k x[r][k] * w[n][k], k ascending, from
- * the transposed weight wt[k][n]. */
 static void accum_t(const float *x, unsigned rows, unsigned K, const int8_t *wt, unsigned N, float *acc) {
     const unsigned NB = 256, RB = 16;
     long nblocks = (N + NB - 1) / NB;
@@ -474,16 +525,34 @@ void ref_kv8_quant(const float *x, unsigned rows, int8_t *codes, float *scales) 
  * P = bf(softmax(S)) over keys 0..visible-1 (causal mask), ctx = bf(P.v); val
  * reads the (dequantised) cache through its view. */
 typedef float (*kv_at)(const void *view, unsigned t, unsigned d);
-static void attend_finish(float *scratch, unsigned visible, kv_at val, const void *vview, unsigned mode, float *out) {
+
+/* Softmax of scratch[0..visible) in place: E = exp(S - max). REF_EXACT: E by
+ * ref_qexp and the sum exact on the 2^-40 grid, Z = RN32(sum rint(E * 2^40))
+ * * 2^-40 (E <= 1, so the integer sum stays below 2^56); else expf and a
+ * sequential fp32 sum. Returns 1/Z. */
+static float softmax_exp(float *scratch, unsigned visible, unsigned mode) {
     float mx = -INFINITY;
     for (unsigned t = 0; t < visible; ++t)
         if (scratch[t] > mx) mx = scratch[t];
     float z = 0.0f;
-    for (unsigned t = 0; t < visible; ++t) {
-        scratch[t] = expf(scratch[t] - mx);
-        z += scratch[t];
+    if (mode & REF_EXACT) {
+        int64_t zi = 0;
+        for (unsigned t = 0; t < visible; ++t) {
+            scratch[t] = ref_qexp(scratch[t] - mx);
+            zi += (int64_t)llrintf(ldexpf(scratch[t], 40));
+        }
+        z = ldexpf((float)zi, -40);
+    } else {
+        for (unsigned t = 0; t < visible; ++t) {
+            scratch[t] = expf(scratch[t] - mx);
+            z += scratch[t];
+        }
     }
-    float inv = 1.0f / z;
+    return 1.0f / z;
+}
+
+static void attend_finish(float *scratch, unsigned visible, kv_at val, const void *vview, unsigned mode, float *out) {
+    const float inv = softmax_exp(scratch, visible, mode);
     float acc[HD];
     for (unsigned d = 0; d < HD; ++d) acc[d] = 0.0f;
     for (unsigned t = 0; t < visible; ++t) {
@@ -491,6 +560,35 @@ static void attend_finish(float *scratch, unsigned visible, kv_at val, const voi
         for (unsigned d = 0; d < HD; ++d) acc[d] = fmaf(p, val(vview, t, d), acc[d]);
     }
     for (unsigned d = 0; d < HD; ++d) out[d] = bfm(acc[d], mode);
+}
+
+/* KV8 context in the accelerator's order (REF_KV8 | REF_EXACT). The array
+ * folds the per-token V scale into the probability before the reduction over
+ * tokens (src/rtl/kv8_v_pscale.sv:1-20, p'[t] = p[t] * m[t]) and sums p'
+ * against the int8 codes as block-aligned integers. Restated with one 28-bit
+ * alignment per (row, head):
+ *   P[t] = bf16(E[t] / Z),  w[t] = RN32(P[t] * vscale[t])
+ *   E_h  = exponent of RN32(bf16(1/Z) * max_t vscale[t]), a bound of every
+ *          w[t] (E[t] <= 1 and rounding is monotone), known before any w[t]
+ *   W[t] = rint(w[t] * 2^(26-E_h)) (|W| < 2^27)
+ *   ctx[d] = bf16(RN32(sum_t W[t] * code[t][d]) * 2^(E_h-26))
+ * with the sum exact in int64 (below 2^49 for 32768 keys). */
+static void attend_finish_kv8_exact(float *scratch, unsigned visible, const int8_t *vcodes, const float *vscales,
+                                    unsigned mode, float *out) {
+    const float inv = softmax_exp(scratch, visible, mode);
+    float vmax = 0.0f;
+    for (unsigned t = 0; t < visible; ++t)
+        if (vscales[t] > vmax) vmax = vscales[t];
+    const float bound = bfm(inv, mode) * vmax;
+    const int e = bound > 0.0f ? ilogbf(bound) : 0;
+    int64_t acc[HD];
+    for (unsigned d = 0; d < HD; ++d) acc[d] = 0;
+    for (unsigned t = 0; t < visible; ++t) {
+        const float w = bfm(scratch[t] * inv, mode) * vscales[t];
+        const int64_t wi = (int64_t)rintf(ldexpf(w, 26 - e));
+        for (unsigned d = 0; d < HD; ++d) acc[d] += wi * vcodes[(size_t)t * HD + d];
+    }
+    for (unsigned d = 0; d < HD; ++d) out[d] = bfm(ldexpf((float)acc[d], e - 26), mode);
 }
 
 /* model_backend.py:97 with a cache read through a view: S = bf(q.k/8), the
@@ -556,7 +654,11 @@ void ref_attention_kv8(const float *q, unsigned rows, const uint32_t *positions,
         float *scratch = (float *)malloc(visible * sizeof(float));
         ref_kv8_scores(q + ((size_t)r * QH + h) * HD, visible, kcodes + (size_t)g * capacity * HD,
                        kscales + (size_t)g * capacity, mode, scratch);
-        attend_finish(scratch, visible, kv8_at, &vv, mode, ctx + (size_t)r * HID + (size_t)h * HD);
+        if (mode & REF_EXACT)
+            attend_finish_kv8_exact(scratch, visible, vv.codes, vv.scales, mode,
+                                    ctx + (size_t)r * HID + (size_t)h * HD);
+        else
+            attend_finish(scratch, visible, kv8_at, &vv, mode, ctx + (size_t)r * HID + (size_t)h * HD);
         free(scratch);
     }
 }
@@ -572,11 +674,12 @@ void ref_attention_bf16(const float *q, unsigned rows, const uint32_t *positions
     }
 }
 
-/* model_backend.py:106: bf16(bf16(silu(gate)) * up), silu(g) = g / (1 + exp(-g)). */
+/* model_backend.py:106: bf16(bf16(silu(gate)) * up), silu(g) = g / (1 + exp(-g))
+ * (exp by ref_qexp under REF_EXACT). */
 void ref_swiglu(const float *gate, const float *up, unsigned count, unsigned mode, float *out) {
     for (unsigned i = 0; i < count; ++i) {
         float g = gate[i];
-        float s = g / (1.0f + expf(-g));
+        float s = g / (1.0f + exp_m(-g, mode));
         out[i] = bfm(bfm(s, mode) * up[i], mode);
     }
 }

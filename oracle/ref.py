@@ -49,6 +49,7 @@ def lib():
             'ref_embedding': (POINTER(ctypes.c_uint16), [c_void_p]),
             'ref_kv8_state': (c_int, [c_void_p, c_int, _P8, _PF, _P8, _PF]),
             'ref_bf': (c_float, [c_float, ctypes.c_uint]),
+            'ref_qexp': (c_float, [c_float]),
             'ref_rmsnorm': (None, [_PF, ctypes.c_uint, _PF, c_float, ctypes.c_uint, _PF]),
             'ref_linear': (None, [_PF, ctypes.c_uint, ctypes.c_uint, _P8, _PF, ctypes.c_uint, ctypes.c_uint, _PF]),
             'ref_linear_bias': (None, [_PF, ctypes.c_uint, ctypes.c_uint, _P8, _PF, _PF, ctypes.c_uint,
@@ -189,6 +190,12 @@ class RefModel:
 
 
 # ------------------------------------------------------------ operator level
+def qexp(x):
+    """ref_qexp elementwise (the exact mode's exp)."""
+    f = lib().ref_qexp
+    return np.array([f(float(v)) for v in np.ravel(f32(x))], np.float32).reshape(np.shape(x))
+
+
 def rmsnorm(x, gamma, eps=1e-6, mode=0):
     x = f32(x)
     out = np.empty_like(x)

@@ -114,6 +114,30 @@ def test_oracle_teacher_forced_matches_reference(oracle_model, golden):
         assert m.forward([tok], i) == step['token'], f'position {i}'
 
 
+@pytest.mark.parametrize('mode', [ref.EXACT, ref.KV8 | ref.EXACT])
+def test_exact_mode_oracle_reproduces_reference_tokens(oracle_model, golden, mode):
+    """The exact-sum arithmetic the engine implements keeps the reference's
+    greedy tokens: all six free-running tokens in both cache modes, all 16
+    teacher-forced tokens with the bf16 cache (the KV8 cache alone moves two
+    near-tied positions, as in plain KV8 mode)."""
+    m = oracle_model
+    m.set_mode(mode)
+    try:
+        m.clear()
+        ids, pos = list(golden['prompt']), 0
+        for i, step in enumerate(golden['generate']):
+            tok = m.forward(ids, pos)
+            assert tok == step['token'], f'step {i}'
+            pos += len(ids)
+            ids = [tok]
+        if not mode & ref.KV8:
+            m.clear()
+            for i, (tok, step) in enumerate(zip(golden['prompt'], golden['teacher_forced'])):
+                assert m.forward([tok], i) == step['token'], f'position {i}'
+    finally:
+        m.set_mode(0)
+
+
 def test_oracle_rtl_boundaries_match_reference(oracle_model, golden):
     m = oracle_model
     m.set_mode(ref.RND8 | ref.FUSED_BIAS | ref.CSR_EPS)
