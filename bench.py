@@ -41,7 +41,7 @@ SEED = 2026
 HID, FFN, QKV, VOCAB, LAYERS = 896, 4864, 1152, 151936, 24
 KV_BYTES_PER_TOKEN_LAYER = 2 * 2 * (64 + 4)  # K and V, 2 heads, 64 codes + fp32 scale
 CLASSES = ['embedding', 'qkv_rope_kv8', 'attention', 'o_proj_residual', 'gate_up_swiglu', 'down_residual',
-           'lm_head_argmax', 'bookkeeping']
+           'lm_head_argmax', 'bookkeeping', 'persistent_decode']
 # kernels behind each class: rows <= 8 run the GEMV family, more rows the
 # tcgen05 GEMM (qkv/o/gate_up/down/LM head), attention is one cluster launch
 KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_cluster_kernel',
@@ -49,7 +49,8 @@ KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_cluster_ke
                      'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
                      'down_residual': 'gemv_kernel<4864,EPI_RESIDUAL>',
                      'lm_head_argmax': 'lm_head_kernel + argmax_reduce_kernel',
-                     'embedding': 'embed_kernel', 'bookkeeping': 'decode_prologue/epilogue_kernel'}
+                     'embedding': 'embed_kernel', 'bookkeeping': 'decode_prologue/epilogue_kernel',
+                     'persistent_decode': 'decode1_kernel'}
 KERNEL_NAMES_TC = dict(KERNEL_NAMES_GEMV,
                        qkv_rope_kv8='rmsnorm_kernel + tc_gemm_kernel<EPI_BIAS> + rope_kv8_kernel',
                        o_proj_residual='tc_gemm_kernel<EPI_RESIDUAL>',
@@ -302,8 +303,8 @@ def run_ours(args):
            'api': 'qwen_b200_decode_step (host buffers)'}
 
     # per-kernel-class device times of a real step (events on the launching stream)
-    ms_cls = np.zeros(8, np.float32)
-    n_cls = np.zeros(8, np.uint32)
+    ms_cls = np.zeros(len(CLASSES), np.float32)
+    n_cls = np.zeros(len(CLASSES), np.uint32)
     out = np.empty(S, np.uint32)
     for rep in range(2):
         rc = qwen_b200.lib().qwen_b200_profile_decode(
@@ -386,8 +387,8 @@ def bs1_decode(eng, args, stream, sp, hbm):
     sb = step_bytes([ctx0 + args.steps // 2])
     ach = sb / (ms / 1000) / 1e9
     # device time per kernel class of one bs1 step (events around each launch)
-    ms_cls = np.zeros(8, np.float32)
-    n_cls = np.zeros(8, np.uint32)
+    ms_cls = np.zeros(len(CLASSES), np.float32)
+    n_cls = np.zeros(len(CLASSES), np.uint32)
     tok_in = np.array([int(bufs[(args.warmup + args.steps) % 2][0].item())], np.uint32)
     out = np.empty(1, np.uint32)
     qwen_b200.lib().qwen_b200_profile_decode(eng.h, tok_in.ctypes.data_as(qwen_b200._lib._P32), 1,

@@ -1,0 +1,968 @@
+// One batch-1 decode step (all 24 layers, final RMSNorm, LM head and greedy
+// argmax of legacy_100mhz_closed/src/PC/model_backend.py:57-115) in a single
+// persistent cooperative launch of one CTA per SM, in the same exact
+// arithmetic as the multi-kernel path (the oracle's REF_KV8 | REF_EXACT mode),
+// so both give the same bits.
+//
+// Weights stream continuously: every CTA owns a fixed slice of rows of each
+// projection (QKV, O, gate/up pairs, down, then its share of the LM head in
+// 32-row pieces). One thread keeps a 172 KB shared-memory ring filled with the
+// upcoming slices by bulk copies, each slice together with everything its
+// phase reads besides the activations (the slice's per-channel scales and
+// biases, the RMSNorm gains), completing on one mbarrier per slice; slices are
+// issued as soon as ring space frees, so the next layers' weights arrive while
+// the current phase computes or waits. Phases are separated by grid barriers
+// (an arrival counter in global memory, bounded spin):
+//   A  every CTA: RMSNorm of x (exact sum of squares) -> limb planes in shared
+//      memory; its QKV rows + bias -> qkv (pre-RoPE, bf16). The same thread
+//      also starts the bulk copies of this layer's KV8 history (short contexts)
+//   B+C short contexts (<= 64 keys): every CTA computes the attention of all
+//      14 heads itself from the prefetched history and the new key/value (RoPE,
+//      KV8 quantise; CTA 0 appends them to the cache), then its O rows +
+//      residual -> x. Longer contexts: B on CTAs 0 and 1 (one KV head each,
+//      history read from the cache), a grid barrier, then C on every CTA
+//   D  RMSNorm of x -> limbs; its gate/up pairs + SiLU*mul -> mid
+//   E  mid -> limbs; its down rows + residual -> x
+//   LM final RMSNorm -> limbs; its LM-head rows -> logits and its best (value,
+//      index); after a last barrier CTA 0 picks the token (highest index on
+//      ties, model_backend.py:113-114)
+// Activations written by other CTAs of the launch are read through L2 only.
+// Every wait is bounded: on timeout a code goes to the error flag and the CTA
+// stops waiting (its results are then garbage, and the host reports the flag).
+#include "common.cuh"
+#include "kernels.h"
+#include "tc05.cuh"
+#include "xlimbs.cuh"
+
+namespace qb {
+
+constexpr int D1_THREADS = 256;
+constexpr int D1_WARPS = D1_THREADS / 32;
+constexpr int D1_RING = 172 * 1024;
+constexpr int D1_SEGS = 16;      // slices in flight at most (one mbarrier each)
+constexpr int D1_LM_ROWS = 32;   // LM-head rows per slice
+constexpr int D1_MAXROWS = 72;   // largest projection slice of one CTA (gate/up pairs)
+constexpr int D1_SHORT = 64;     // contexts up to this many keys use the fused B+C phase
+
+// long-context attention scratch (phase B on CTAs 0 and 1), inside the work area
+constexpr int D1A_QF = 0;                              // float [7][64] q after RoPE
+constexpr int D1A_QL = D1A_QF + 7 * 64 * 4;            // int8 [7][4][64] q limb planes
+constexpr int D1A_NEW = D1A_QL + 7 * 4 * 64;           // int8 [2][64] new k / v codes
+constexpr int D1A_MISC = D1A_NEW + 128;                // qe[8] int, M[8], inv[8], s1[8], s2[8], F[8], new scales[2], vmax
+constexpr int D1A_RED = D1A_MISC + 64 * 4;             // (unused: reductions use the shared red area)
+constexpr int D1A_KS = D1A_RED + D1_WARPS * 8 * 8;     // float [maxkeys] K scales, V scales, S [7][maxkeys]
+constexpr int D1_LONG_BYTES = D1A_KS + 4 * QB_D1_MAX_KEYS * 9;
+
+// short-context area (after the limb planes): prefetched history and scratch
+constexpr int D1S_KC = 0;                                  // int8 [2][64 keys][64] K codes
+constexpr int D1S_VC = D1S_KC + 2 * D1_SHORT * 64;         // int8 [2][64][64] V codes
+constexpr int D1S_KS = D1S_VC + 2 * D1_SHORT * 64;         // float [2][64 + 8] K scales (16-byte aligned superset)
+constexpr int D1S_VS = D1S_KS + 2 * (D1_SHORT + 8) * 4;    // float [2][64 + 8] V scales
+constexpr int D1S_QL = D1S_VS + 2 * (D1_SHORT + 8) * 4;    // int8 [14][4][64] q limb planes
+constexpr int D1S_NEW = D1S_QL + 14 * 4 * 64;              // int8 [2 k|v][2 heads][64] new codes
+constexpr int D1S_S = D1S_NEW + 4 * 64;                    // float [14][64] scores -> E -> W (u32)
+constexpr int D1S_CTX = D1S_S + 14 * D1_SHORT * 4;         // bf16 [896] context
+constexpr int D1S_MISC = D1S_CTX + QB_HID * 2;             // qe[16], M[16], inv[16], s1[16], s2[16], F[16], nsc[4], vmax[2]
+constexpr int D1_SHORT_BYTES = D1S_MISC + 128 * 4;
+constexpr int D1_LIMB_BYTES = 4 * QB_FFN + 16;
+
+struct D1Smem {
+    int ring, work, shortw, bars, segs, layers, red, accs, total;
+};
+__host__ __device__ inline D1Smem d1_smem() {
+    D1Smem L;
+    L.ring = 0;
+    L.work = L.ring + D1_RING;
+    L.shortw = L.work + D1_LIMB_BYTES;
+    const int work = D1_LIMB_BYTES + D1_SHORT_BYTES > D1_LONG_BYTES ? D1_LIMB_BYTES + D1_SHORT_BYTES : D1_LONG_BYTES;
+    L.bars = (L.work + work + 15) & ~15;
+    L.segs = L.bars + (D1_SEGS + 2) * 8;  // slice mbarriers, then the KV-history mbarrier
+    L.layers = L.segs + 512;              // per slot: ring offset, virtual end, side offsets; producer state
+    L.red = L.layers + QB_NL * (int)sizeof(D1Layer);
+    L.red = (L.red + 15) & ~15;
+    L.accs = L.red + D1_WARPS * 16 * 8;
+    L.total = L.accs + D1_MAXROWS * 4;
+    return L;
+}
+
+// [begin, end) of part c of n items split over g parts
+__device__ __forceinline__ void d1_part(int n, int c, int g, int &b, int &e) {
+    b = (int)((unsigned)(n * c) / (unsigned)g);  // n * (c + 1) < 2^31 for every n here
+    e = (int)((unsigned)(n * (c + 1)) / (unsigned)g);
+}
+
+// One ring slice: up to four contiguous pieces placed back to back (each a
+// multiple of 16 bytes); side data is copied as the 16-byte-aligned superset
+// of its range and found at rel[i] + delta[i].
+struct D1Seg {
+    const uint8_t *src[4];
+    uint32_t bytes[4], rel[4], delta[4];
+    int n;
+    uint32_t total;
+};
+__device__ __forceinline__ void d1_piece(D1Seg &g, const void *p, uint32_t len) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p), al = a & ~(uintptr_t)15;
+    const uintptr_t end = (a + len + 15) & ~(uintptr_t)15;
+    g.src[g.n] = reinterpret_cast<const uint8_t *>(al);
+    g.bytes[g.n] = (uint32_t)(end - al);
+    g.rel[g.n] = g.total;
+    g.delta[g.n] = (uint32_t)(a - al);
+    g.total += g.bytes[g.n];
+    ++g.n;
+}
+
+// Slice s of this CTA: layer s / 4, phase s % 4 (QKV, O, gate/up, down), then
+// the LM-head pieces. Piece 0 is always the weight rows, piece 1 their scales.
+__device__ __forceinline__ bool d1_seg(const D1Args &a, const D1Layer *layers, int s, D1Seg &g) {
+    const int c = blockIdx.x, G = gridDim.x;
+    int b, e;
+    g.n = 0;
+    g.total = 0;
+    if (s < 4 * QB_NL) {
+        const D1Layer &W = layers[s >> 2];
+        switch (s & 3) {
+            case 0:
+                d1_part(QB_QKV, c, G, b, e);
+                d1_piece(g, W.qkv + (size_t)b * QB_HID, (e - b) * QB_HID);
+                d1_piece(g, W.s_qkv + b, (e - b) * 4);
+                d1_piece(g, W.bias + b, (e - b) * 2);
+                d1_piece(g, W.g_attn, QB_HID * 2);
+                break;
+            case 1:
+                d1_part(QB_HID, c, G, b, e);
+                d1_piece(g, W.o + (size_t)b * QB_HID, (e - b) * QB_HID);
+                d1_piece(g, W.s_o + b, (e - b) * 4);
+                break;
+            case 2:
+                d1_part(QB_FFN, c, G, b, e);
+                d1_piece(g, W.gu + (size_t)2 * b * QB_HID, 2 * (e - b) * QB_HID);
+                d1_piece(g, W.s_gu + 2 * b, 2 * (e - b) * 4);
+                d1_piece(g, W.g_ffn, QB_HID * 2);
+                break;
+            default:
+                d1_part(QB_HID, c, G, b, e);
+                d1_piece(g, W.d + (size_t)b * QB_FFN, (e - b) * QB_FFN);
+                d1_piece(g, W.s_d + b, (e - b) * 4);
+                break;
+        }
+        return true;
+    }
+    d1_part(QB_VOCAB, c, G, b, e);
+    const int p = s - 4 * QB_NL, r0 = b + p * D1_LM_ROWS;
+    if (r0 >= e) return false;
+    const int nr = min(D1_LM_ROWS, e - r0);
+    d1_piece(g, a.lmw + (size_t)r0 * QB_HID, nr * QB_HID);
+    d1_piece(g, a.s_lm + r0, nr * 4);
+    if (p == 0) d1_piece(g, a.g_final, QB_HID * 2);
+    return true;
+}
+
+struct D1Ring {
+    uint8_t *ring;
+    uint64_t *bars;
+    uint32_t *off, *vend;  // per slot
+    uint32_t *side;        // per slot: byte offsets (from the slice base) of pieces 1..3' data
+    uint32_t *st;          // [0] next to issue, [1] next to release, [2] virtual head, [3] virtual tail
+    const D1Layer *layers; // shared-memory copy
+};
+
+// Producer (one thread): issue upcoming slices while ring space and mbarrier
+// slots allow. Slices never wrap: one that does not fit before the end of the
+// ring starts at offset 0.
+__device__ void d1_issue(const D1Args &a, D1Ring &R) {
+    tc::fence_proxy_async_smem();  // earlier generic reads of the freed space come first
+    uint32_t s = R.st[0];
+    while (s - R.st[1] < (uint32_t)D1_SEGS) {
+        D1Seg g;
+        if (!d1_seg(a, R.layers, (int)s, g)) break;
+        uint32_t v = R.st[2];
+        if ((v % D1_RING) + g.total > (uint32_t)D1_RING) v += D1_RING - (v % D1_RING);
+        if (v + g.total - R.st[3] > (uint32_t)D1_RING) break;
+        const int slot = (int)(s % D1_SEGS);
+        R.off[slot] = v % D1_RING;
+        R.vend[slot] = v + g.total;
+        for (int i = 1; i < 4; ++i) R.side[slot * 4 + i] = i < g.n ? g.rel[i] + g.delta[i] : 0u;
+        tc::mbar_arrive_expect_tx(&R.bars[slot], g.total);
+        for (int i = 0; i < g.n; ++i) tc::bulk_load(R.ring + v % D1_RING + g.rel[i], g.src[i], g.bytes[i], &R.bars[slot]);
+        R.st[2] = v + g.total;
+        ++s;
+    }
+    R.st[0] = s;
+}
+
+// Slice s is complete in the ring (all threads); returns its base, and in
+// side[1..3] the offsets of its side pieces. The producer wrote the slot's
+// offsets before its arrive on the slot's mbarrier (release), so they are
+// visible once the wait has observed the phase (acquire).
+__device__ __forceinline__ const uint8_t *d1_wait(const D1Args &a, D1Ring &R, int s, uint32_t (&side)[4], bool &ok) {
+    const int slot = s % D1_SEGS;
+    if (ok) ok = tc::mbar_wait(&R.bars[slot], (uint32_t)(s / D1_SEGS) & 1u, a.err, 21);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) side[i] = R.side[slot * 4 + i];
+    return R.ring + R.off[slot];
+}
+
+// After every thread is done with slice s: release it and refill (the other
+// threads go on; they meet the new slices through their mbarriers).
+__device__ __forceinline__ void d1_release(const D1Args &a, D1Ring &R, int s) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        R.st[3] = R.vend[s % D1_SEGS];
+        R.st[1] = (uint32_t)s + 1;
+        d1_issue(a, R);
+    }
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier number k (1-based) of the launch: the CTA's writes are made
+// visible (fence, then one arrival), thread 0 polls the counter with acquire
+// loads, the CTA proceeds together.
+__device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &ok) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(a.bar, 1u);
+        bool good = ok;
+        if (good) {
+            const unsigned target = k * gridDim.x;
+            uint32_t spins = 0;
+            while (ld_acquire_gpu(a.bar) < target) {
+                if (++spins > (1u << 24)) {
+                    atomicExch(a.err, 20u);
+                    good = false;
+                    break;
+                }
+            }
+        }
+        s_ok = good;
+    }
+    __syncthreads();
+    ok = s_ok != 0;
+}
+
+// The four int8 limb planes xl[4][896] of one 896-wide row and its exponent,
+// with the CTA's 256 threads at once (thread t < 224 owns values 4t..4t+3);
+// with NORM the row is RMSNormed first (exact sum of squares on the 21-bit
+// grid, model_backend.py:69-71). The same values as load_x_limbs, with three
+// CTA-wide reductions instead of one warp's serial chain. CG: x was written by
+// other CTAs of this launch (read through L2); otherwise x may be shared memory.
+template <bool NORM, bool CG>
+__device__ void d1_row896(const uint16_t *x, const uint16_t *gamma, float eps, int8_t *xl, int *ex, uint8_t *red) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *r0 = reinterpret_cast<float *>(red), *r2 = r0 + 16;
+    long long *r1 = reinterpret_cast<long long *>(red + 128);
+    const bool act = tid < QB_HID / 4;
+    uint2 xv = make_uint2(0u, 0u);
+    if (act) {
+        const uint2 *p = reinterpret_cast<const uint2 *>(x) + tid;
+        if constexpr (CG)
+            xv = __ldcg(p);
+        else
+            xv = *p;
+    }
+    float v[4] = {bflo(xv.x), bfhi(xv.x), bflo(xv.y), bfhi(xv.y)};
+    if constexpr (NORM) {
+        float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        m = warp_max(m);
+        if (lane == 0) r0[warp] = m;
+        __syncthreads();
+        m = r0[0];
+#pragma unroll
+        for (int w = 1; w < D1_WARPS; ++w) m = fmaxf(m, r0[w]);
+        const int e0 = row_exponent(m);
+        long long s2 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const long long q = __float2int_rn(align21(v[i], e0));
+            s2 += q * q;
+        }
+        s2 = warp_sum_ll(s2);
+        if (lane == 0) r1[warp] = s2;
+        __syncthreads();
+        s2 = r1[0];
+#pragma unroll
+        for (int w = 1; w < D1_WARPS; ++w) s2 += r1[w];
+        const float ss = ldexpf(__ll2float_rn(s2), 2 * e0 - 40);
+        const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)QB_HID), eps)));
+        uint2 gv = make_uint2(0u, 0u);
+        if (act) gv = reinterpret_cast<const uint2 *>(gamma)[tid];
+        const float gg[4] = {bflo(gv.x), bfhi(gv.x), bflo(gv.y), bfhi(gv.y)};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = rbf(rbf(v[i] * rs) * gg[i]);
+    }
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    m = warp_max(m);
+    if (lane == 0) r2[warp] = m;
+    __syncthreads();
+    m = r2[0];
+#pragma unroll
+    for (int w = 1; w < D1_WARPS; ++w) m = fmaxf(m, r2[w]);
+    const int e = row_exponent(m);
+    if (act) {
+        int lv[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) limbs4(align28_int(v[i], e), lv[i]);
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+            reinterpret_cast<uint32_t *>(xl + l * QB_HID)[tid] = ((uint32_t)lv[0][l] & 0xffu) |
+                                                                  (((uint32_t)lv[1][l] & 0xffu) << 8) |
+                                                                  (((uint32_t)lv[2][l] & 0xffu) << 16) |
+                                                                  ((uint32_t)lv[3][l] << 24);
+    }
+    if (tid == 0) ex[0] = e;
+    __syncthreads();
+}
+
+// acc[r] = RN32(sum_k X[k] * W[r][k]) * 2^(ex - 26) for the nrows rows of a
+// ring segment (row-major, K bytes each): warp w takes rows w*RW.., lanes
+// split the row into 16-byte chunks, dp4a against the four limb planes.
+template <int K, int RW>
+__device__ __forceinline__ void d1_dot(const int8_t *w, int nrows, const int8_t *xl, int ex, float *accs) {
+    constexpr int NCH = K / 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r0 = warp * RW; r0 < nrows; r0 += D1_WARPS * RW) {
+        int d[RW][4];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) d[r][0] = d[r][1] = d[r][2] = d[r][3] = 0;
+        for (int ch = lane; ch < NCH; ch += 32) {
+            uint4 xw[4];
+#pragma unroll
+            for (int l = 0; l < 4; ++l) xw[l] = *reinterpret_cast<const uint4 *>(xl + l * K + ch * 16);
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                if (r0 + r >= nrows) break;
+                const uint4 wv = *reinterpret_cast<const uint4 *>(w + (size_t)(r0 + r) * K + ch * 16);
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    int t = d[r][l];
+                    t = __dp4a((int)wv.x, (int)xw[l].x, t);
+                    t = __dp4a((int)wv.y, (int)xw[l].y, t);
+                    t = __dp4a((int)wv.z, (int)xw[l].z, t);
+                    t = __dp4a((int)wv.w, (int)xw[l].w, t);
+                    d[r][l] = t;
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            long long v = (long long)d[r][0] + (long long)d[r][1] * 128ll + (long long)d[r][2] * 16384ll +
+                          (long long)d[r][3] * 2097152ll;
+            v = warp_sum_ll(v);
+            if (lane == 0 && r0 + r < nrows) accs[r0 + r] = unalign28(v, ex);
+        }
+    }
+}
+
+// Phase B for KV head g: see the file comment. L = pos + 1 keys.
+__device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, uint32_t pos, uint8_t *work,
+                             uint8_t *red8) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int L = (int)pos + 1;
+    float *qf = reinterpret_cast<float *>(work + D1A_QF);
+    int8_t *ql = reinterpret_cast<int8_t *>(work + D1A_QL);
+    int8_t *knew = reinterpret_cast<int8_t *>(work + D1A_NEW), *vnew = knew + 64;
+    int *qe = reinterpret_cast<int *>(work + D1A_MISC);
+    float *M = reinterpret_cast<float *>(work + D1A_MISC) + 8, *inv = M + 8, *s1 = M + 16, *s2 = M + 24;
+    int *F = reinterpret_cast<int *>(M + 32);
+    float *nsc = M + 40;  // new k, v scales, [2] = vmax
+    long long *red = reinterpret_cast<long long *>(red8);
+    float *kss = reinterpret_cast<float *>(work + D1A_KS);
+    float *vss = kss + QB_D1_MAX_KEYS;
+    float *S = vss + QB_D1_MAX_KEYS;  // [7][maxkeys]: scores, then E, then W (as u32)
+    const size_t lc = (size_t)a.codes_per_layer * layer, ls = (size_t)a.scales_per_layer * layer;
+    const size_t base = ((size_t)slot * 2 + g) * a.cap;  // key 0 of this (slot, head)
+    const int8_t *kc = a.kc + lc + base * 64, *vc = a.vc + lc + base * 64;
+    const float *ks = a.ks + ls + base, *vs = a.vs + ls + base;
+    const uint16_t *qkv = a.qkv;
+
+    // RoPE (model_backend.py:73-78) of q heads 7g..7g+6 (warps 0..6) and of
+    // k; KV8 quantise-append of k and v (warp 7)
+    const float *cs = a.rope + (size_t)pos * 64;
+    const float c = cs[lane & 31], sn = cs[32 + (lane & 31)];
+    if (warp < 7) {
+        const uint16_t *qp = qkv + (size_t)(7 * g + warp) * 64;
+        const float lo = bf2f(__ldcg(qp + lane)), hi = bf2f(__ldcg(qp + lane + 32));
+        const float nlo = rbf(__fadd_rn(__fmul_rn(lo, c), __fmul_rn(-hi, sn)));
+        const float nhi = rbf(__fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, sn)));
+        qf[warp * 64 + lane] = nlo;
+        qf[warp * 64 + lane + 32] = nhi;
+        // 28-bit alignment of the head, four limb planes
+        const int e = row_exponent(warp_max(fmaxf(fabsf(nlo), fabsf(nhi))));
+        int l0[4], l1[4];
+        limbs4(align28_int(nlo, e), l0);
+        limbs4(align28_int(nhi, e), l1);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            ql[(warp * 4 + l) * 64 + lane] = (int8_t)l0[l];
+            ql[(warp * 4 + l) * 64 + lane + 32] = (int8_t)l1[l];
+        }
+        if (lane == 0) qe[warp] = e;
+    } else {
+#pragma unroll
+        for (int isv = 0; isv < 2; ++isv) {
+            const uint16_t *p = qkv + QB_HID + isv * 128 + g * 64;
+            float lo = bf2f(__ldcg(p + lane)), hi = bf2f(__ldcg(p + lane + 32));
+            if (!isv) {
+                const float nlo = rbf(__fadd_rn(__fmul_rn(lo, c), __fmul_rn(-hi, sn)));
+                const float nhi = rbf(__fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, sn)));
+                lo = nlo;
+                hi = nhi;
+            }
+            const float amax = warp_max(fmaxf(fabsf(lo), fabsf(hi)));
+            const float s = __fdiv_rn(amax, 127.0f);
+            int clo = 0, chi = 0;
+            if (s > 0.f) {
+                clo = (int)fminf(fmaxf(rintf(__fdiv_rn(lo, s)), -127.f), 127.f);
+                chi = (int)fminf(fmaxf(rintf(__fdiv_rn(hi, s)), -127.f), 127.f);
+            }
+            int8_t *gc = const_cast<int8_t *>(isv ? vc : kc) + (size_t)pos * 64;
+            int8_t *nc = isv ? vnew : knew;
+            gc[lane] = (int8_t)clo;
+            gc[lane + 32] = (int8_t)chi;
+            nc[lane] = (int8_t)clo;
+            nc[lane + 32] = (int8_t)chi;
+            if (lane == 0) {
+                const_cast<float *>(isv ? vs : ks)[pos] = s;
+                nsc[isv] = s;
+            }
+        }
+    }
+    for (int t = tid; t < L - 1; t += D1_THREADS) {
+        kss[t] = __ldg(ks + t);
+        vss[t] = __ldg(vs + t);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        kss[L - 1] = nsc[0];
+        vss[L - 1] = nsc[1];
+    }
+    __syncthreads();
+
+    // scores: thread (key t = tid/8 + 32 i, head h = tid % 8)
+    const int h = tid & 7, tl = tid >> 3;
+    float mloc = -INFINITY, vloc = 0.f;
+    for (int t = tl; t < L; t += D1_THREADS / 8) {
+        vloc = fmaxf(vloc, vss[t]);
+        if (h == 7) continue;
+        const uint32_t *kr = reinterpret_cast<const uint32_t *>(t == L - 1 ? knew : kc + (size_t)t * 64);
+        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * 4 * 64);
+        int d4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int wi = 0; wi < 16; ++wi) {
+            const int kw = (int)(t == L - 1 ? kr[wi] : __ldg(kr + wi));
+#pragma unroll
+            for (int l = 0; l < 4; ++l) d4[l] = __dp4a(kw, (int)qr[l * 16 + wi], d4[l]);
+        }
+        const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
+                              (long long)d4[3] * 2097152ll;
+        const float sc = rbf(__fmul_rn(unalign28(dot, qe[h]), kss[t]) * 0.125f);
+        S[h * QB_D1_MAX_KEYS + t] = sc;
+        mloc = fmaxf(mloc, sc);
+    }
+    // per-head max and the largest V scale
+    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 8));
+    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 16));
+    vloc = warp_max(vloc);
+    float *redf = reinterpret_cast<float *>(red);
+    if (lane < 8) redf[warp * 8 + lane] = (lane == 7) ? vloc : mloc;
+    __syncthreads();
+    if (tid < 8) {
+        float m = redf[tid];
+        for (int w = 1; w < D1_WARPS; ++w) m = fmaxf(m, redf[w * 8 + tid]);
+        if (tid < 7)
+            M[tid] = m;
+        else
+            nsc[2] = m;
+    }
+    __syncthreads();
+    // E = qexp(S - max) in place, exact sums
+    long long z = 0;
+    if (h < 7)
+        for (int t = tl; t < L; t += D1_THREADS / 8) {
+            const float e = qexp(__fsub_rn(S[h * QB_D1_MAX_KEYS + t], M[h]));
+            S[h * QB_D1_MAX_KEYS + t] = e;
+            z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
+        }
+    z += __shfl_xor_sync(0xffffffffu, z, 8);
+    z += __shfl_xor_sync(0xffffffffu, z, 16);
+    if (lane < 8) red[warp * 8 + lane] = z;
+    __syncthreads();
+    if (tid < 7) {
+        long long zt = 0;
+        for (int w = 0; w < D1_WARPS; ++w) zt += red[w * 8 + tid];
+        const float iv = __fdiv_rn(1.0f, __fmul_rn(__ll2float_rn(zt), 0x1p-40f));
+        const int f = row_exponent(__fmul_rn(rbf(iv), nsc[2]));
+        const int sh = 26 - f, sh1 = min(sh, 127);
+        inv[tid] = iv;
+        F[tid] = f;
+        s1[tid] = pow2i(sh1);
+        s2[tid] = pow2i(sh - sh1);
+    }
+    __syncthreads();
+    // W = rint(RN32(P * vscale) * 2^(26-F)), P = bf16(E / Z)
+    if (h < 7)
+        for (int t = tl; t < L; t += D1_THREADS / 8) {
+            const float w = __fmul_rn(rbf(__fmul_rn(S[h * QB_D1_MAX_KEYS + t], inv[h])), vss[t]);
+            reinterpret_cast<uint32_t *>(S)[h * QB_D1_MAX_KEYS + t] =
+                __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
+        }
+    __syncthreads();
+    // context: thread (half, head, 4 dims), keys t = half, half + 2, ...
+    long long acc[4] = {0, 0, 0, 0};
+    const int half = tid / 112, rem = tid % 112, hh = rem >> 4, d4 = rem & 15;
+    if (tid < 224) {
+        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * QB_D1_MAX_KEYS;
+        for (int t = half; t < L; t += 2) {
+            const uint32_t cw = t == L - 1 ? reinterpret_cast<const uint32_t *>(vnew)[d4]
+                                           : __ldg(reinterpret_cast<const uint32_t *>(vc + (size_t)t * 64) + d4);
+            const long long wt = (long long)W[t];
+            acc[0] += wt * (int)(int8_t)(cw & 0xffu);
+            acc[1] += wt * (int)(int8_t)((cw >> 8) & 0xffu);
+            acc[2] += wt * (int)(int8_t)((cw >> 16) & 0xffu);
+            acc[3] += wt * (int)(int8_t)(cw >> 24);
+        }
+    }
+    long long *part = reinterpret_cast<long long *>(kss);  // kss/vss are no longer needed
+    __syncthreads();
+    if (tid >= 112 && tid < 224)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) part[rem * 4 + i] = acc[i];
+    __syncthreads();
+    if (tid < 112) {
+        uint16_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = f2bf(unalign28(acc[i] + part[rem * 4 + i], F[hh]));
+        uint2 pk;
+        pk.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+        pk.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+        *reinterpret_cast<uint2 *>(a.ctx + (size_t)(7 * g + hh) * 64 + 4 * d4) = pk;
+    }
+}
+
+
+// KV8 history of this layer for the fused short-context phase: K and V codes
+// of keys [0, pos) of both KV heads and their scales, into the short area
+// (one thread; completes on kvbar).
+__device__ void d1_issue_history(const D1Args &a, int layer, uint32_t slot, uint32_t pos, uint8_t *sw,
+                                 uint64_t *kvbar) {
+    uint32_t total = 0;
+    const uint8_t *src[8];
+    uint32_t bytes[8], dst[8];
+    int n = 0;
+    const size_t lc = (size_t)a.codes_per_layer * layer, ls = (size_t)a.scales_per_layer * layer;
+    for (int g = 0; g < QB_KVH && pos > 0; ++g) {
+        const size_t base = ((size_t)slot * 2 + g) * a.cap;
+        src[n] = reinterpret_cast<const uint8_t *>(a.kc + lc + base * 64);
+        bytes[n] = pos * 64;
+        dst[n++] = D1S_KC + g * D1_SHORT * 64;
+        src[n] = reinterpret_cast<const uint8_t *>(a.vc + lc + base * 64);
+        bytes[n] = pos * 64;
+        dst[n++] = D1S_VC + g * D1_SHORT * 64;
+        for (int isv = 0; isv < 2; ++isv) {
+            const uintptr_t p = reinterpret_cast<uintptr_t>((isv ? a.vs : a.ks) + ls + base);
+            const uintptr_t al = p & ~(uintptr_t)15, end = (p + 4 * pos + 15) & ~(uintptr_t)15;
+            src[n] = reinterpret_cast<const uint8_t *>(al);
+            bytes[n] = (uint32_t)(end - al);
+            dst[n++] = (isv ? D1S_VS : D1S_KS) + g * (D1_SHORT + 8) * 4;
+        }
+    }
+    for (int i = 0; i < n; ++i) total += bytes[i];
+    tc::fence_proxy_async_smem();  // the previous layer's generic reads of the area come first
+    tc::mbar_arrive_expect_tx(kvbar, total);
+    for (int i = 0; i < n; ++i) tc::bulk_load(sw + dst[i], src[i], bytes[i], kvbar);
+}
+
+// Fused short-context attention (every CTA, all 14 heads): see the file
+// comment; leaves ctx (bf16 [896]) in shared memory.
+__device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, uint32_t pos, uint8_t *sw,
+                                   uint64_t *kvbar, long long *red, bool &ok) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int L = (int)pos + 1;
+    int8_t *ql = reinterpret_cast<int8_t *>(sw + D1S_QL);
+    int8_t *nw = reinterpret_cast<int8_t *>(sw + D1S_NEW);  // [k|v][g][64]
+    float *S = reinterpret_cast<float *>(sw + D1S_S);       // [14][64]
+    uint16_t *ctx = reinterpret_cast<uint16_t *>(sw + D1S_CTX);
+    int *qe = reinterpret_cast<int *>(sw + D1S_MISC);
+    float *M = reinterpret_cast<float *>(qe + 16), *inv = M + 16, *s1 = M + 32, *s2 = M + 48;
+    int *F = reinterpret_cast<int *>(M + 64);
+    float *nsc = M + 80;  // new scales [k|v][g]
+    float *vmx = M + 84;  // [g]
+    const uint16_t *qkv = a.qkv;
+    const float *cs = a.rope + (size_t)pos * 64;
+    const float c = cs[lane], sn = cs[32 + lane];
+    // 18 head vectors: q heads 0..13, k heads (14, 15), v heads (16, 17)
+    for (int hv = warp; hv < 18; hv += D1_WARPS) {
+        const uint16_t *p = qkv + hv * 64;
+        float lo = bf2f(__ldcg(p + lane)), hi = bf2f(__ldcg(p + lane + 32));
+        if (hv < 16) {  // RoPE on q and k (model_backend.py:73-78)
+            const float nlo = rbf(__fadd_rn(__fmul_rn(lo, c), __fmul_rn(-hi, sn)));
+            const float nhi = rbf(__fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, sn)));
+            lo = nlo;
+            hi = nhi;
+        }
+        if (hv < QB_QH) {
+            const int e = row_exponent(warp_max(fmaxf(fabsf(lo), fabsf(hi))));
+            int l0[4], l1[4];
+            limbs4(align28_int(lo, e), l0);
+            limbs4(align28_int(hi, e), l1);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                ql[(hv * 4 + l) * 64 + lane] = (int8_t)l0[l];
+                ql[(hv * 4 + l) * 64 + lane + 32] = (int8_t)l1[l];
+            }
+            if (lane == 0) qe[hv] = e;
+        } else {
+            const int isv = hv >= 16, g = (hv - 14) & 1;
+            const float amax = warp_max(fmaxf(fabsf(lo), fabsf(hi)));
+            const float s = __fdiv_rn(amax, 127.0f);
+            int clo = 0, chi = 0;
+            if (s > 0.f) {
+                clo = (int)fminf(fmaxf(rintf(__fdiv_rn(lo, s)), -127.f), 127.f);
+                chi = (int)fminf(fmaxf(rintf(__fdiv_rn(hi, s)), -127.f), 127.f);
+            }
+            int8_t *nc = nw + (isv * 2 + g) * 64;
+            nc[lane] = (int8_t)clo;
+            nc[lane + 32] = (int8_t)chi;
+            if (lane == 0) nsc[isv * 2 + g] = s;
+            if (blockIdx.x == 0) {  // the one writer of the cache entry
+                const size_t base = ((size_t)slot * 2 + g) * a.cap + pos;
+                int8_t *gc = (isv ? a.vc : a.kc) + (size_t)a.codes_per_layer * layer + base * 64;
+                gc[lane] = (int8_t)clo;
+                gc[lane + 32] = (int8_t)chi;
+                if (lane == 0) (isv ? a.vs : a.ks)[(size_t)a.scales_per_layer * layer + base] = s;
+            }
+        }
+    }
+    if (ok) ok = tc::mbar_wait(kvbar, (uint32_t)layer & 1u, a.err, 22);
+    __syncthreads();
+    // scale of key t of head g (history from the aligned superset copies)
+    auto kscale = [&](int g, int t) -> float {
+        if (t == L - 1) return nsc[g];
+        const uintptr_t p = reinterpret_cast<uintptr_t>(a.ks + (size_t)a.scales_per_layer * layer +
+                                                        ((size_t)slot * 2 + g) * a.cap);
+        return reinterpret_cast<const float *>(sw + D1S_KS + g * (D1_SHORT + 8) * 4 + (p & 15))[t];
+    };
+    auto vscale = [&](int g, int t) -> float {
+        if (t == L - 1) return nsc[2 + g];
+        const uintptr_t p = reinterpret_cast<uintptr_t>(a.vs + (size_t)a.scales_per_layer * layer +
+                                                        ((size_t)slot * 2 + g) * a.cap);
+        return reinterpret_cast<const float *>(sw + D1S_VS + g * (D1_SHORT + 8) * 4 + (p & 15))[t];
+    };
+    // scores: thread (head h = tid % 16, key t = tid / 16 + 16 i)
+    const int h = tid & 15, tl = tid >> 4, g = h / 7;
+    float mloc = -INFINITY, vloc = 0.f;
+    if (h < QB_QH) {
+        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * 4 * 64);
+        for (int t = tl; t < L; t += 16) {
+            vloc = fmaxf(vloc, vscale(g, t));
+            const uint32_t *kr = reinterpret_cast<const uint32_t *>(
+                t == L - 1 ? nw + g * 64 : reinterpret_cast<const int8_t *>(sw + D1S_KC) + (g * D1_SHORT + t) * 64);
+            int d4[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int wi = 0; wi < 16; ++wi) {
+                const int kw = (int)kr[wi];
+#pragma unroll
+                for (int l = 0; l < 4; ++l) d4[l] = __dp4a(kw, (int)qr[l * 16 + wi], d4[l]);
+            }
+            const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
+                                  (long long)d4[3] * 2097152ll;
+            const float sc = rbf(__fmul_rn(unalign28(dot, qe[h]), kscale(g, t)) * 0.125f);
+            S[h * D1_SHORT + t] = sc;
+            mloc = fmaxf(mloc, sc);
+        }
+    }
+    // lanes h and h + 16 of a warp share a head
+    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 16));
+    vloc = fmaxf(vloc, __shfl_xor_sync(0xffffffffu, vloc, 16));
+    float *redf = reinterpret_cast<float *>(red);
+    if (lane < 16) {
+        redf[warp * 32 + lane] = mloc;
+        redf[warp * 32 + 16 + lane] = vloc;
+    }
+    __syncthreads();
+    if (tid < 16) {
+        float m = -INFINITY, v = 0.f;
+        for (int w = 0; w < D1_WARPS; ++w) {
+            m = fmaxf(m, redf[w * 32 + tid]);
+            v = fmaxf(v, redf[w * 32 + 16 + tid]);
+        }
+        M[tid] = m;
+        if (tid == 0 || tid == 7) vmx[tid / 7] = v;  // heads 0 and 7 saw every key of KV heads 0 and 1
+    }
+    __syncthreads();
+    // E = qexp(S - max), exact sums
+    long long z = 0;
+    if (h < QB_QH)
+        for (int t = tl; t < L; t += 16) {
+            const float e = qexp(__fsub_rn(S[h * D1_SHORT + t], M[h]));
+            S[h * D1_SHORT + t] = e;
+            z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
+        }
+    z += __shfl_xor_sync(0xffffffffu, z, 16);
+    __syncthreads();
+    if (lane < 16) red[warp * 16 + lane] = z;
+    __syncthreads();
+    if (tid < QB_QH) {
+        long long zt = 0;
+        for (int w = 0; w < D1_WARPS; ++w) zt += red[w * 16 + tid];
+        const float iv = __fdiv_rn(1.0f, __fmul_rn(__ll2float_rn(zt), 0x1p-40f));
+        const int f = row_exponent(__fmul_rn(rbf(iv), vmx[tid / 7]));
+        const int sh = 26 - f, sh1 = min(sh, 127);
+        inv[tid] = iv;
+        F[tid] = f;
+        s1[tid] = pow2i(sh1);
+        s2[tid] = pow2i(sh - sh1);
+    }
+    __syncthreads();
+    // W = rint(RN32(P * vscale) * 2^(26-F)), P = bf16(E / Z)
+    if (h < QB_QH)
+        for (int t = tl; t < L; t += 16) {
+            const float w = __fmul_rn(rbf(__fmul_rn(S[h * D1_SHORT + t], inv[h])), vscale(g, t));
+            reinterpret_cast<uint32_t *>(S)[h * D1_SHORT + t] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
+        }
+    __syncthreads();
+    // context: thread (head, 4 dims), exact int64 sums over the keys
+    if (tid < QB_QH * 16) {
+        const int hh = tid >> 4, d4 = tid & 15, gg = hh / 7;
+        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1_SHORT;
+        long long acc[4] = {0, 0, 0, 0};
+        for (int t = 0; t < L; ++t) {
+            const uint32_t cw = t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + gg) * 64)[d4]
+                                           : reinterpret_cast<const uint32_t *>(sw + D1S_VC)[(gg * D1_SHORT + t) * 16 + d4];
+            const long long wt = (long long)W[t];
+            acc[0] += wt * (int)(int8_t)(cw & 0xffu);
+            acc[1] += wt * (int)(int8_t)((cw >> 8) & 0xffu);
+            acc[2] += wt * (int)(int8_t)((cw >> 16) & 0xffu);
+            acc[3] += wt * (int)(int8_t)(cw >> 24);
+        }
+        uint2 pk;
+        pk.x = (uint32_t)f2bf(unalign28(acc[0], F[hh])) | ((uint32_t)f2bf(unalign28(acc[1], F[hh])) << 16);
+        pk.y = (uint32_t)f2bf(unalign28(acc[2], F[hh])) | ((uint32_t)f2bf(unalign28(acc[3], F[hh])) << 16);
+        *reinterpret_cast<uint2 *>(ctx + hh * 64 + 4 * d4) = pk;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(D1_THREADS, 1) decode1_kernel(D1Args a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const D1Smem Ls = d1_smem();
+    D1Ring R;
+    R.ring = sm + Ls.ring;
+    R.bars = reinterpret_cast<uint64_t *>(sm + Ls.bars);
+    uint64_t *kvbar = R.bars + D1_SEGS;
+    R.off = reinterpret_cast<uint32_t *>(sm + Ls.segs);
+    R.vend = R.off + D1_SEGS;
+    R.side = R.vend + D1_SEGS;
+    R.st = R.side + 4 * D1_SEGS;
+    D1Layer *lay = reinterpret_cast<D1Layer *>(sm + Ls.layers);
+    R.layers = lay;
+    uint8_t *work = sm + Ls.work, *sw = sm + Ls.shortw;
+    int8_t *xl = reinterpret_cast<int8_t *>(work);
+    int *ex = reinterpret_cast<int *>(work + 4 * QB_FFN);
+    float *accs = reinterpret_cast<float *>(sm + Ls.accs);
+    long long *red = reinterpret_cast<long long *>(sm + Ls.red);
+    uint8_t *rd = sm + Ls.red;
+    const int tid = threadIdx.x, c = blockIdx.x, G = gridDim.x;
+    for (int i = tid; i < QB_NL * (int)(sizeof(D1Layer) / 8); i += D1_THREADS)
+        reinterpret_cast<uint64_t *>(lay)[i] = reinterpret_cast<const uint64_t *>(a.layers)[i];
+    __syncthreads();
+    if (tid == 0) {
+        for (int s = 0; s < D1_SEGS + 1; ++s) tc::mbar_init(&R.bars[s], 1);
+        tc::mbar_fence_init();
+        R.st[0] = R.st[1] = R.st[2] = R.st[3] = 0;
+        d1_issue(a, R);  // weights are constant: start streaming at once
+    }
+    __syncthreads();
+    const uint32_t slot = __ldcg(a.meta + 1), pos = __ldcg(a.meta + 2);
+    const bool shortctx = pos + 1 <= (uint32_t)D1_SHORT;
+    bool ok = true;
+    unsigned nbar = 0;
+    int s = 0;
+    uint32_t g[4];
+    for (int l = 0; l < QB_NL; ++l) {
+        int b, e;
+        if (shortctx && tid == 0) d1_issue_history(a, l, slot, pos, sw, kvbar);
+        // A: RMSNorm + QKV rows + bias (pre-RoPE)
+        d1_part(QB_QKV, c, G, b, e);
+        {
+            const uint8_t *seg = d1_wait(a, R, s, g, ok);
+            d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[3]), a.eps, xl, ex, rd);
+            d1_dot<QB_HID, 2>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], accs);
+            __syncthreads();
+            const float *sc = reinterpret_cast<const float *>(seg + g[1]);
+            const uint16_t *bs = reinterpret_cast<const uint16_t *>(seg + g[2]);
+            for (int i = tid; i < e - b; i += D1_THREADS)
+                a.qkv[b + i] = f2bf(rbf(rbf(rbf(accs[i]) * sc[i]) + bf2f(bs[i])));
+            d1_release(a, R, s++);
+        }
+        d1_grid_sync(a, ++nbar, ok);
+        // B + C: attention, then O + residual
+        if (shortctx) {
+            d1_attention_short(a, l, slot, pos, sw, kvbar, red, ok);
+            d1_row896<false, false>(reinterpret_cast<const uint16_t *>(sw + D1S_CTX), nullptr, 0.f, xl, ex, rd);
+        } else {
+            if (c < QB_KVH) d1_attention(a, l, c, slot, pos, work, reinterpret_cast<uint8_t *>(red));
+            d1_grid_sync(a, ++nbar, ok);
+            d1_row896<false, true>(a.ctx, nullptr, 0.f, xl, ex, rd);
+        }
+        __syncthreads();
+        d1_part(QB_HID, c, G, b, e);
+        {
+            const uint8_t *seg = d1_wait(a, R, s, g, ok);
+            d1_dot<QB_HID, 2>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], accs);
+            __syncthreads();
+            const float *sc = reinterpret_cast<const float *>(seg + g[1]);
+            for (int i = tid; i < e - b; i += D1_THREADS) {
+                const int n = b + i;
+                a.x[n] = f2bf(rbf(bf2f(__ldcg(a.x + n)) + rbf(rbf(accs[i]) * sc[i])));
+            }
+            d1_release(a, R, s++);
+        }
+        d1_grid_sync(a, ++nbar, ok);
+        // D: RMSNorm + gate/up pairs + SiLU*mul
+        d1_part(QB_FFN, c, G, b, e);
+        {
+            const uint8_t *seg = d1_wait(a, R, s, g, ok);
+            d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[2]), a.eps, xl, ex, rd);
+            d1_dot<QB_HID, 2>(reinterpret_cast<const int8_t *>(seg), 2 * (e - b), xl, ex[0], accs);
+            __syncthreads();
+            const float *sc = reinterpret_cast<const float *>(seg + g[1]);
+            for (int i = tid; i < e - b; i += D1_THREADS) {
+                const float gt = rbf(rbf(accs[2 * i]) * sc[2 * i]);
+                const float up = rbf(rbf(accs[2 * i + 1]) * sc[2 * i + 1]);
+                a.mid[b + i] = f2bf(rbf(silu_q(gt)) * up);
+            }
+            d1_release(a, R, s++);
+        }
+        d1_grid_sync(a, ++nbar, ok);
+        // E: down + residual
+        load_x_limbs<QB_FFN, 1, D1_THREADS, true>(a.mid, 0, 1, nullptr, 0.f, xl, ex);
+        __syncthreads();
+        d1_part(QB_HID, c, G, b, e);
+        {
+            const uint8_t *seg = d1_wait(a, R, s, g, ok);
+            d1_dot<QB_FFN, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], accs);
+            __syncthreads();
+            const float *sc = reinterpret_cast<const float *>(seg + g[1]);
+            for (int i = tid; i < e - b; i += D1_THREADS) {
+                const int n = b + i;
+                a.x[n] = f2bf(rbf(bf2f(__ldcg(a.x + n)) + rbf(rbf(accs[i]) * sc[i])));
+            }
+            d1_release(a, R, s++);
+        }
+        d1_grid_sync(a, ++nbar, ok);
+    }
+    // LM head: final RMSNorm (gains come with the first piece), this CTA's
+    // rows in 32-row pieces, best (value, index)
+    {
+        const uint8_t *seg = d1_wait(a, R, s, g, ok);
+        d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[2]), a.eps, xl, ex, rd);
+    }
+    int lb, le;
+    d1_part(QB_VOCAB, c, G, lb, le);
+    float bv = -INFINITY;
+    uint32_t bi = 0;
+    for (int r0 = lb; r0 < le; r0 += D1_LM_ROWS) {
+        const int nr = min(D1_LM_ROWS, le - r0);
+        const uint8_t *seg = d1_wait(a, R, s, g, ok);
+        d1_dot<QB_HID, 4>(reinterpret_cast<const int8_t *>(seg), nr, xl, ex[0], accs);
+        __syncthreads();
+        if (tid < nr) {
+            const int n = r0 + tid;
+            const float v = rbf(rbf(accs[tid]) * reinterpret_cast<const float *>(seg + g[1])[tid]);
+            if (a.logits) a.logits[n] = f2bf(v);
+            if (better(v, (uint32_t)n, bv, bi)) {
+                bv = v;
+                bi = (uint32_t)n;
+            }
+        }
+        d1_release(a, R, s++);
+    }
+    // best of the CTA (threads < 32 hold candidates)
+    if (tid < 32) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (tid == 0) {
+            a.cand_v[c] = bv;
+            a.cand_i[c] = bi;
+        }
+    }
+    d1_grid_sync(a, ++nbar, ok);
+    if (c == 0 && tid < 32) {
+        float v = -INFINITY;
+        uint32_t i = 0;
+        for (int k = tid; k < G; k += 32) {
+            const float cv = __ldcg(a.cand_v + k);
+            const uint32_t ci = __ldcg(a.cand_i + k);
+            if (better(cv, ci, v, i)) {
+                v = cv;
+                i = ci;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+            if (better(ov, oi, v, i)) {
+                v = ov;
+                i = oi;
+            }
+        }
+        if (tid == 0) a.tokens[0] = i;
+    }
+}
+
+static int d1_grid = 0;
+
+int decode1_supported(int max_len) { return max_len >= 1 && max_len <= QB_D1_MAX_KEYS; }
+
+size_t decode1_smem_bytes() { return (size_t)d1_smem().total; }
+
+int launch_decode1(const D1Args &a, cudaStream_t st) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -3;
+    static unsigned configured = 0;
+    if (!(configured & (1u << (dev & 31)))) {
+        if (cudaFuncSetAttribute(decode1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)decode1_smem_bytes()) != cudaSuccess)
+            return -3;
+        int sms = 0, per_sm = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -3;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode1_kernel, D1_THREADS,
+                                                          decode1_smem_bytes()) != cudaSuccess ||
+            per_sm < 1)
+            return -3;
+        d1_grid = sms;
+        configured |= 1u << (dev & 31);
+    }
+    if (cudaMemsetAsync(a.bar, 0, 4, st) != cudaSuccess) return -3;
+    pdl_break();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(d1_grid);
+    cfg.blockDim = dim3(D1_THREADS);
+    cfg.dynamicSmemBytes = decode1_smem_bytes();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, decode1_kernel, a) != cudaSuccess) return -3;
+    pdl_break();
+    return QB_LAUNCH_CHECK();
+}
+
+}  // namespace qb

@@ -72,6 +72,13 @@ struct qwen_b200 {
     size_t limb_plane = 0;
     CUtensorMap lmap_hid, lmap_ffn;
     uint32_t *meta = nullptr;  // [4][R]: ids | slots | positions | logit rows
+    // persistent batch-1 decode: per-layer pointers, barrier counter and the
+    // per-CTA argmax candidates
+    bool persistent = true;
+    D1Layer *d1_layers = nullptr;
+    unsigned *d1_bar = nullptr;
+    float *d1_cand_v = nullptr;
+    uint32_t *d1_cand_i = nullptr;
     uint32_t *tokens = nullptr, *slot_pos = nullptr;
     void *lm_ws = nullptr;
     size_t lm_ws_bytes = 0;
@@ -241,6 +248,10 @@ int allocate(qwen_b200 *h) {
     CK(cudaMemset(h->tc_ws, 0, h->tc_ws_bytes));
     if ((rc = dalloc(h, (void **)&h->logits, (size_t)VOC * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->meta, R * 4 * 4))) return rc;
+    if ((rc = dalloc(h, (void **)&h->d1_layers, NL * sizeof(D1Layer)))) return rc;
+    if ((rc = dalloc(h, (void **)&h->d1_bar, 256))) return rc;
+    if ((rc = dalloc(h, (void **)&h->d1_cand_v, 1024 * 4))) return rc;
+    if ((rc = dalloc(h, (void **)&h->d1_cand_i, 1024 * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->tokens, R * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->slot_pos, (size_t)c.max_seqs * 4))) return rc;
     CK(cudaMemset(h->slot_pos, 0, (size_t)c.max_seqs * 4));
@@ -286,6 +297,12 @@ int upload(qwen_b200 *h, const qa_model &m) {
         CK(cudaMemcpy(W.s_qkv, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(W.bias, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
     }
+    D1Layer d1[NL];
+    for (int l = 0; l < NL; ++l) {
+        const LayerW &W = h->L[l];
+        d1[l] = D1Layer{W.qkv, W.o, W.gu, W.d, W.s_qkv, W.s_o, W.s_gu, W.s_d, W.bias, W.g_attn, W.g_ffn};
+    }
+    CK(cudaMemcpy(h->d1_layers, d1, sizeof(d1), cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->g_final, m.gamma + QA_GAMMA_FINAL, HID * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->embed, m.embed, (size_t)VOC * HID * 2, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->lmw, m.lmw, (size_t)VOC * HID, cudaMemcpyHostToDevice));
@@ -345,6 +362,37 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
     {
         LaunchScope ls(h, 0, st, 1);
         RK(launch_embed(h->embed, ids, n, h->x, st));
+    }
+    if (n == 1 && nlog == 1 && identity && !dump && h->persistent && decode1_supported(max_len)) {
+        // one row: every layer, the LM head and the argmax in one persistent launch
+        D1Args a;
+        a.layers = h->d1_layers;
+        a.lmw = h->lmw;
+        a.s_lm = h->s_lm;
+        a.g_final = h->g_final;
+        a.rope = h->rope;
+        a.kc = h->kc;
+        a.vc = h->vc;
+        a.ks = h->ks;
+        a.vs = h->vs;
+        a.codes_per_layer = kv_layer_codes(h);
+        a.scales_per_layer = kv_layer_scales(h);
+        a.cap = cap;
+        a.meta = h->meta;
+        a.x = h->x;
+        a.qkv = h->qkvb;
+        a.ctx = h->ctx;
+        a.mid = h->mid;
+        a.logits = want_logits ? h->logits : nullptr;
+        a.tokens = tokens_dst;
+        a.cand_v = h->d1_cand_v;
+        a.cand_i = h->d1_cand_i;
+        a.bar = h->d1_bar;
+        a.err = reinterpret_cast<unsigned *>(h->tc_ws);
+        a.eps = eps;
+        LaunchScope ls(h, 8, st, 1);
+        RK(launch_decode1(a, st));
+        return 0;
     }
     for (int l = 0; l < NL; ++l) {
         const LayerW &W = h->L[l];
@@ -635,6 +683,12 @@ void qwen_b200_rope_table(uint32_t positions, float *table) {
             table[(size_t)p * 64 + i] = (float)cos((double)phase);
             table[(size_t)p * 64 + 32 + i] = (float)sin((double)phase);
         }
+}
+
+int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable) {
+    if (!h) return QWEN_B200_EINVAL;
+    h->persistent = enable != 0;
+    return QWEN_B200_OK;
 }
 
 int qwen_b200_reset(qwen_b200 *h, uint32_t slot) {

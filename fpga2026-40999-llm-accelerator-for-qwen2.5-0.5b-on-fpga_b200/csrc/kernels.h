@@ -35,6 +35,39 @@ struct QkvArgs {
 };
 int launch_qkv(const QkvArgs &a, cudaStream_t st);
 
+// Persistent batch-1 decode step (decode1.cu): every layer, the LM head and
+// the argmax in one cooperative launch of one CTA per SM.
+#define QB_NL 24
+#define QB_D1_MAX_KEYS 1024  // context keys held in shared memory by the attention phase
+struct D1Layer {
+    const int8_t *qkv, *o, *gu, *d;
+    const float *s_qkv, *s_o, *s_gu, *s_d;
+    const uint16_t *bias, *g_attn, *g_ffn;
+};
+struct D1Args {
+    const D1Layer *layers;  // [24], device memory
+    const int8_t *lmw;
+    const float *s_lm;
+    const uint16_t *g_final;
+    const float *rope;                 // [capacity][64]
+    int8_t *kc, *vc;                   // layer 0 of [layer][slot][2][cap][64]
+    float *ks, *vs;                    // layer 0 of [layer][slot][2][cap]
+    size_t codes_per_layer, scales_per_layer;
+    int cap;
+    const uint32_t *meta;              // ids | slots | positions of the row (n = 1)
+    uint16_t *x, *qkv, *ctx, *mid;     // [896] residual, [1152], [896], [4864]
+    uint16_t *logits;                  // nullable [151936]
+    uint32_t *tokens;                  // [1]
+    float *cand_v;                     // [grid] per-CTA best value
+    uint32_t *cand_i;                  // [grid] per-CTA best index
+    unsigned *bar;                     // grid barrier counter (reset by the launch)
+    unsigned *err;                     // error flag of the bounded waits
+    float eps;
+};
+int decode1_supported(int max_len);
+size_t decode1_smem_bytes();
+int launch_decode1(const D1Args &a, cudaStream_t st);
+
 // Final RMSNorm + LM head + argmax. part: [rows][nblocks] (value, index).
 size_t lm_head_workspace(int rows, int vocab);
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,

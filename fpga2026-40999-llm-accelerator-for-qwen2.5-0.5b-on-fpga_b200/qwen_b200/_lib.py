@@ -53,6 +53,7 @@ _SIGNATURES = {
                                         c_void_p, c_void_p]),
     'qwen_b200_op_gemm_w8a16_residual': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32,
                                                  c_void_p, c_void_p]),
+    'qwen_b200_set_persistent_decode': (c_int, [c_void_p, c_int]),
     'qwen_b200_gemm_tc_workspace': (c_size_t, [c_uint32, c_uint32, c_uint32]),
     'qwen_b200_op_gemm_w8a16_tc': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p,
                                            c_int, c_void_p, c_void_p, c_size_t, c_void_p]),

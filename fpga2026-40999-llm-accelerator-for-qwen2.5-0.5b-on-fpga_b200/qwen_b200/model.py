@@ -55,6 +55,11 @@ class Engine:
         check(lib().qwen_b200_position(self.h, slot, ctypes.byref(p)), self.h)
         return p.value
 
+    def set_persistent(self, enable):
+        """Single-row steps as one persistent launch (default) or per kernel."""
+        check(lib().qwen_b200_set_persistent_decode(self.h, 1 if enable else 0), self.h)
+        return self
+
     def reset(self, slot=0):
         check(lib().qwen_b200_reset(self.h, slot), self.h)
 

@@ -123,10 +123,18 @@ int qwen_b200_read_kv(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, i
 int qwen_b200_set_dump(qwen_b200 *h, int layer, uint16_t *q, uint16_t *k, uint16_t *v, uint16_t *ctx,
                        uint16_t *hbuf, uint16_t *mid, uint16_t *y);
 
+/* Single-row forwards and decode steps (context up to 1024 keys) run as one
+ * persistent cooperative launch of one CTA per SM: every layer, the LM head
+ * and the argmax, weights streamed into shared memory ahead of use, phases
+ * separated by grid barriers; same arithmetic (and bits) as the per-kernel
+ * path. enable = 0 selects the per-kernel path (default 1). */
+int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable);
+
 /* Kernel classes reported by qwen_b200_profile_decode. */
-#define QWEN_B200_KCLASSES 8 /* 0 embedding, 1 RMSNorm+QKV+RoPE+KV8 append, 2 attention,
+#define QWEN_B200_KCLASSES 9 /* 0 embedding, 1 RMSNorm+QKV+RoPE+KV8 append, 2 attention,
                                 3 O proj+residual, 4 RMSNorm+gate/up+SiLU*mul, 5 down+residual,
-                                6 LM head+argmax, 7 bookkeeping (row gathers, position updates) */
+                                6 LM head+argmax, 7 bookkeeping (row gathers, position updates),
+                                8 persistent batch-1 step (every layer + LM head + argmax) */
 /* One decode step of slots 0..n-1 (host buffers, like qwen_b200_decode_step)
  * with CUDA events around every kernel launch on the launching stream: ms[c]
  * is the summed device time of class c, launches[c] its launch count. */
