@@ -36,34 +36,40 @@
 
 namespace qb {
 
-constexpr int D1_THREADS = 256;
+constexpr int D1_THREADS = 256;                  // compute threads (warps 0..7)
 constexpr int D1_WARPS = D1_THREADS / 32;
+constexpr int D1_BLOCK = D1_THREADS + 32;        // + warp 8: the ring producer
 constexpr int D1_RING = 172 * 1024;
 constexpr int D1_SEGS = 16;      // slices in flight at most (one mbarrier each)
 constexpr int D1_LM_ROWS = 32;   // LM-head rows per slice
 constexpr int D1_MAXROWS = 72;   // largest projection slice of one CTA (gate/up pairs)
 constexpr int D1_SHORT = 64;     // contexts up to this many keys use the fused B+C phase
 
+constexpr int D1S_QLS = 4 * 64 + 4;  // q limb planes per head, padded against bank conflicts
+
 // long-context attention scratch (phase B on CTAs 0 and 1), inside the work area
 constexpr int D1A_QF = 0;                              // float [7][64] q after RoPE
-constexpr int D1A_QL = D1A_QF + 7 * 64 * 4;            // int8 [7][4][64] q limb planes
-constexpr int D1A_NEW = D1A_QL + 7 * 4 * 64;           // int8 [2][64] new k / v codes
+constexpr int D1A_QL = D1A_QF + 7 * 64 * 4;            // int8 [7][260] q limb planes (padded rows)
+constexpr int D1A_NEW = D1A_QL + 7 * (4 * 64 + 4) + 4; // int8 [2][64] new k / v codes
 constexpr int D1A_MISC = D1A_NEW + 128;                // qe[8] int, M[8], inv[8], s1[8], s2[8], F[8], new scales[2], vmax
 constexpr int D1A_RED = D1A_MISC + 64 * 4;             // (unused: reductions use the shared red area)
-constexpr int D1A_KS = D1A_RED + D1_WARPS * 8 * 8;     // float [maxkeys] K scales, V scales, S [7][maxkeys]
-constexpr int D1_LONG_BYTES = D1A_KS + 4 * QB_D1_MAX_KEYS * 9;
+constexpr int D1A_KS = D1A_RED + D1_WARPS * 8 * 8;     // float [maxkeys] K scales, V scales, S [7][maxkeys + 1]
+constexpr int D1A_SS = QB_D1_MAX_KEYS + 1;             // score row stride (padded against bank conflicts)
+constexpr int D1_LONG_BYTES = D1A_KS + 4 * (2 * QB_D1_MAX_KEYS + 7 * D1A_SS);
 
 // short-context area (after the limb planes): prefetched history and scratch
 constexpr int D1S_KC = 0;                                  // int8 [2][64 keys][64] K codes
 constexpr int D1S_VC = D1S_KC + 2 * D1_SHORT * 64;         // int8 [2][64][64] V codes
 constexpr int D1S_KS = D1S_VC + 2 * D1_SHORT * 64;         // float [2][64 + 8] K scales (16-byte aligned superset)
 constexpr int D1S_VS = D1S_KS + 2 * (D1_SHORT + 8) * 4;    // float [2][64 + 8] V scales
-constexpr int D1S_QL = D1S_VS + 2 * (D1_SHORT + 8) * 4;    // int8 [14][4][64] q limb planes
-constexpr int D1S_NEW = D1S_QL + 14 * 4 * 64;              // int8 [2 k|v][2 heads][64] new codes
-constexpr int D1S_S = D1S_NEW + 4 * 64;                    // float [14][64] scores -> E -> W (u32)
-constexpr int D1S_CTX = D1S_S + 14 * D1_SHORT * 4;         // bf16 [896] context
+constexpr int D1S_QL = D1S_VS + 2 * (D1_SHORT + 8) * 4;    // int8 [14][260] q limb planes
+constexpr int D1S_NEW = D1S_QL + 14 * D1S_QLS;             // int8 [2 k|v][2 heads][64] new codes
+constexpr int D1S_SS = D1_SHORT + 1;                        // scores per head, padded
+constexpr int D1S_S = D1S_NEW + 4 * 64;                    // float [14][65] scores -> E -> W (u32)
+constexpr int D1S_CTX = D1S_S + 14 * D1S_SS * 4;           // bf16 [896] context
 constexpr int D1S_MISC = D1S_CTX + QB_HID * 2;             // qe[16], M[16], inv[16], s1[16], s2[16], F[16], nsc[4], vmax[2]
-constexpr int D1_SHORT_BYTES = D1S_MISC + 128 * 4;
+constexpr int D1S_QKV = D1S_MISC + 128 * 4;                // bf16 [1152] this step's q | k | v (pre-RoPE)
+constexpr int D1_SHORT_BYTES = D1S_QKV + QB_QKV * 2;
 constexpr int D1_LIMB_BYTES = 4 * QB_FFN + 16;
 
 struct D1Smem {
@@ -76,7 +82,7 @@ __host__ __device__ inline D1Smem d1_smem() {
     L.shortw = L.work + D1_LIMB_BYTES;
     const int work = D1_LIMB_BYTES + D1_SHORT_BYTES > D1_LONG_BYTES ? D1_LIMB_BYTES + D1_SHORT_BYTES : D1_LONG_BYTES;
     L.bars = (L.work + work + 15) & ~15;
-    L.segs = L.bars + (D1_SEGS + 2) * 8;  // slice mbarriers, then the KV-history mbarrier
+    L.segs = L.bars + (2 * D1_SEGS + 2) * 8;  // full / empty mbarriers per slot, then the KV-history one
     L.layers = L.segs + 512;              // per slot: ring offset, virtual end, side offsets; producer state
     L.red = L.layers + QB_NL * (int)sizeof(D1Layer);
     L.red = (L.red + 15) & ~15;
@@ -84,6 +90,9 @@ __host__ __device__ inline D1Smem d1_smem() {
     L.total = L.accs + D1_MAXROWS * 4;
     return L;
 }
+
+// Barrier of the 256 compute threads (the producer warp never joins).
+__device__ __forceinline__ void d1_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // [begin, end) of part c of n items split over g parts
 __device__ __forceinline__ void d1_part(int n, int c, int g, int &b, int &e) {
@@ -159,58 +168,56 @@ __device__ __forceinline__ bool d1_seg(const D1Args &a, const D1Layer *layers, i
 
 struct D1Ring {
     uint8_t *ring;
-    uint64_t *bars;
-    uint32_t *off, *vend;  // per slot
-    uint32_t *side;        // per slot: byte offsets (from the slice base) of pieces 1..3' data
-    uint32_t *st;          // [0] next to issue, [1] next to release, [2] virtual head, [3] virtual tail
-    const D1Layer *layers; // shared-memory copy
+    uint64_t *full, *empty;  // per slot: data landed / all 8 compute warps done with it
+    uint32_t *off;           // per slot: ring offset of the slice
+    uint32_t *side;          // per slot: byte offsets (from the slice base) of pieces 1..3' data
+    const D1Layer *layers;   // shared-memory copy
 };
 
-// Producer (one thread): issue upcoming slices while ring space and mbarrier
-// slots allow. Slices never wrap: one that does not fit before the end of the
-// ring starts at offset 0.
-__device__ void d1_issue(const D1Args &a, D1Ring &R) {
-    tc::fence_proxy_async_smem();  // earlier generic reads of the freed space come first
-    uint32_t s = R.st[0];
-    while (s - R.st[1] < (uint32_t)D1_SEGS) {
+// The producer (lane 0 of warp 8): issues every slice of the launch in order,
+// each as soon as its mbarrier slot and enough ring space are free, i.e. once
+// the compute warps have released the older slices. Slices never wrap: one
+// that does not fit before the end of the ring starts at offset 0.
+__device__ void d1_produce(const D1Args &a, D1Ring &R) {
+    uint32_t head = 0, tail = 0, vend[D1_SEGS];
+    int oldest = 0;  // first slice not yet known to be released
+    for (int s = 0;; ++s) {
         D1Seg g;
-        if (!d1_seg(a, R.layers, (int)s, g)) break;
-        uint32_t v = R.st[2];
+        if (!d1_seg(a, R.layers, s, g)) break;
+        uint32_t v = head;
         if ((v % D1_RING) + g.total > (uint32_t)D1_RING) v += D1_RING - (v % D1_RING);
-        if (v + g.total - R.st[3] > (uint32_t)D1_RING) break;
-        const int slot = (int)(s % D1_SEGS);
+        while (oldest < s && (oldest <= s - D1_SEGS || v + g.total - tail > (uint32_t)D1_RING)) {
+            if (!tc::mbar_wait(&R.empty[oldest % D1_SEGS], (uint32_t)(oldest / D1_SEGS) & 1u, a.err, 23, 1u << 24))
+                return;
+            tail = vend[oldest % D1_SEGS];
+            ++oldest;
+        }
+        const int slot = s % D1_SEGS;
         R.off[slot] = v % D1_RING;
-        R.vend[slot] = v + g.total;
         for (int i = 1; i < 4; ++i) R.side[slot * 4 + i] = i < g.n ? g.rel[i] + g.delta[i] : 0u;
-        tc::mbar_arrive_expect_tx(&R.bars[slot], g.total);
-        for (int i = 0; i < g.n; ++i) tc::bulk_load(R.ring + v % D1_RING + g.rel[i], g.src[i], g.bytes[i], &R.bars[slot]);
-        R.st[2] = v + g.total;
-        ++s;
+        vend[slot] = v + g.total;
+        tc::mbar_arrive_expect_tx(&R.full[slot], g.total);
+        for (int i = 0; i < g.n; ++i) tc::bulk_load(R.ring + v % D1_RING + g.rel[i], g.src[i], g.bytes[i], &R.full[slot]);
+        head = v + g.total;
     }
-    R.st[0] = s;
 }
 
-// Slice s is complete in the ring (all threads); returns its base, and in
+// Slice s is complete in the ring (compute threads); returns its base, and in
 // side[1..3] the offsets of its side pieces. The producer wrote the slot's
 // offsets before its arrive on the slot's mbarrier (release), so they are
 // visible once the wait has observed the phase (acquire).
 __device__ __forceinline__ const uint8_t *d1_wait(const D1Args &a, D1Ring &R, int s, uint32_t (&side)[4], bool &ok) {
     const int slot = s % D1_SEGS;
-    if (ok) ok = tc::mbar_wait(&R.bars[slot], (uint32_t)(s / D1_SEGS) & 1u, a.err, 21);
+    if (ok) ok = tc::mbar_wait(&R.full[slot], (uint32_t)(s / D1_SEGS) & 1u, a.err, 21);
 #pragma unroll
     for (int i = 0; i < 4; ++i) side[i] = R.side[slot * 4 + i];
     return R.ring + R.off[slot];
 }
 
-// After every thread is done with slice s: release it and refill (the other
-// threads go on; they meet the new slices through their mbarriers).
-__device__ __forceinline__ void d1_release(const D1Args &a, D1Ring &R, int s) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        R.st[3] = R.vend[s % D1_SEGS];
-        R.st[1] = (uint32_t)s + 1;
-        d1_issue(a, R);
-    }
+// This warp is done with slice s (every warp calls it once per slice).
+__device__ __forceinline__ void d1_done(D1Ring &R, int s) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) tc::mbar_arrive(&R.empty[s % D1_SEGS]);
 }
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
@@ -219,15 +226,15 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
     return v;
 }
 
-// Grid barrier number k (1-based) of the launch: the CTA's writes are made
-// visible (fence, then one arrival), thread 0 polls the counter with acquire
+// Grid barrier number k (1-based) of the launch: one release arrival per CTA
+// (its writes become visible first), thread 0 polls the counter with acquire
 // loads, the CTA proceeds together.
 __device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &ok) {
     __shared__ int s_ok;
-    __syncthreads();
+    d1_sync();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(a.bar, 1u);
+        // release: the CTA's writes (ordered before this thread by the CTA barrier) become visible first
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         bool good = ok;
         if (good) {
             const unsigned target = k * gridDim.x;
@@ -242,7 +249,7 @@ __device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &
         }
         s_ok = good;
     }
-    __syncthreads();
+    d1_sync();
     ok = s_ok != 0;
 }
 
@@ -271,7 +278,7 @@ __device__ void d1_row896(const uint16_t *x, const uint16_t *gamma, float eps, i
         float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
         m = warp_max(m);
         if (lane == 0) r0[warp] = m;
-        __syncthreads();
+        d1_sync();
         m = r0[0];
 #pragma unroll
         for (int w = 1; w < D1_WARPS; ++w) m = fmaxf(m, r0[w]);
@@ -284,7 +291,7 @@ __device__ void d1_row896(const uint16_t *x, const uint16_t *gamma, float eps, i
         }
         s2 = warp_sum_ll(s2);
         if (lane == 0) r1[warp] = s2;
-        __syncthreads();
+        d1_sync();
         s2 = r1[0];
 #pragma unroll
         for (int w = 1; w < D1_WARPS; ++w) s2 += r1[w];
@@ -299,7 +306,7 @@ __device__ void d1_row896(const uint16_t *x, const uint16_t *gamma, float eps, i
     float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     m = warp_max(m);
     if (lane == 0) r2[warp] = m;
-    __syncthreads();
+    d1_sync();
     m = r2[0];
 #pragma unroll
     for (int w = 1; w < D1_WARPS; ++w) m = fmaxf(m, r2[w]);
@@ -316,47 +323,103 @@ __device__ void d1_row896(const uint16_t *x, const uint16_t *gamma, float eps, i
                                                                   ((uint32_t)lv[3][l] << 24);
     }
     if (tid == 0) ex[0] = e;
-    __syncthreads();
+    d1_sync();
 }
 
 // acc[r] = RN32(sum_k X[k] * W[r][k]) * 2^(ex - 26) for the nrows rows of a
-// ring segment (row-major, K bytes each): warp w takes rows w*RW.., lanes
-// split the row into 16-byte chunks, dp4a against the four limb planes.
-template <int K, int RW>
-__device__ __forceinline__ void d1_dot(const int8_t *w, int nrows, const int8_t *xl, int ex, float *accs) {
+// ring slice (row-major, K bytes each): warp w takes rows w*RW .. w*RW+RW-1
+// (one pass), lanes split the rows into 16-byte chunks, dp4a against the four
+// limb planes; lane 0 of the warp then runs epi(r0, nr, acc) on its rows.
+template <int K, int RW, class Epi>
+__device__ __forceinline__ void d1_dot(const int8_t *w, int nrows, const int8_t *xl, int ex, Epi epi) {
     constexpr int NCH = K / 16;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r0 = warp * RW; r0 < nrows; r0 += D1_WARPS * RW) {
-        int d[RW][4];
+    const int r0 = warp * RW, nr = min(RW, nrows - r0);
+    if (nr <= 0) return;
+    int d[RW][4];
 #pragma unroll
-        for (int r = 0; r < RW; ++r) d[r][0] = d[r][1] = d[r][2] = d[r][3] = 0;
-        for (int ch = lane; ch < NCH; ch += 32) {
-            uint4 xw[4];
+    for (int r = 0; r < RW; ++r) d[r][0] = d[r][1] = d[r][2] = d[r][3] = 0;
+    for (int ch = lane; ch < NCH; ch += 32) {
+        uint4 xw[4];
 #pragma unroll
-            for (int l = 0; l < 4; ++l) xw[l] = *reinterpret_cast<const uint4 *>(xl + l * K + ch * 16);
+        for (int l = 0; l < 4; ++l) xw[l] = *reinterpret_cast<const uint4 *>(xl + l * K + ch * 16);
 #pragma unroll
-            for (int r = 0; r < RW; ++r) {
-                if (r0 + r >= nrows) break;
-                const uint4 wv = *reinterpret_cast<const uint4 *>(w + (size_t)(r0 + r) * K + ch * 16);
+        for (int r = 0; r < RW; ++r) {
+            if (r >= nr) break;
+            const uint4 wv = *reinterpret_cast<const uint4 *>(w + (size_t)(r0 + r) * K + ch * 16);
 #pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    int t = d[r][l];
-                    t = __dp4a((int)wv.x, (int)xw[l].x, t);
-                    t = __dp4a((int)wv.y, (int)xw[l].y, t);
-                    t = __dp4a((int)wv.z, (int)xw[l].z, t);
-                    t = __dp4a((int)wv.w, (int)xw[l].w, t);
-                    d[r][l] = t;
-                }
+            for (int l = 0; l < 4; ++l) {
+                int t = d[r][l];
+                t = __dp4a((int)wv.x, (int)xw[l].x, t);
+                t = __dp4a((int)wv.y, (int)xw[l].y, t);
+                t = __dp4a((int)wv.z, (int)xw[l].z, t);
+                t = __dp4a((int)wv.w, (int)xw[l].w, t);
+                d[r][l] = t;
+            }
+        }
+    }
+    float acc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        long long v = (long long)d[r][0] + (long long)d[r][1] * 128ll + (long long)d[r][2] * 16384ll +
+                      (long long)d[r][3] * 2097152ll;
+        acc[r] = unalign28(warp_sum_ll(v), ex);
+    }
+    if (lane == 0) epi(r0, nr, acc);
+}
+
+// The four int8 limb planes of one 4864-wide row (plain conversion), every
+// compute thread on 16-byte pieces; the maximum meets in shared memory.
+__device__ void d1_row4864(const uint16_t *x, int8_t *xl, int *ex, uint8_t *red) {
+    constexpr int K = QB_FFN, NPC = K / 8, NP = (NPC + D1_THREADS - 1) / D1_THREADS;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *r0 = reinterpret_cast<float *>(red);
+    uint4 xv[NP];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const int p = tid + D1_THREADS * j;
+        xv[j] = p < NPC ? __ldcg(reinterpret_cast<const uint4 *>(x) + p) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) amax = fmaxf(amax, fmaxf(fabsf(bflo(w[t])), fabsf(bfhi(w[t]))));
+    }
+    amax = warp_max(amax);
+    if (lane == 0) r0[warp] = amax;
+    d1_sync();
+    amax = r0[0];
+#pragma unroll
+    for (int w2 = 1; w2 < D1_WARPS; ++w2) amax = fmaxf(amax, r0[w2]);
+    const int e = row_exponent(amax);
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const int p = tid + D1_THREADS * j;
+        if (p >= NPC) continue;
+        const uint32_t w[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+        uint32_t pk[4][2];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            int la[4], lb[4];
+            limbs4(align28_int(bflo(w[t]), e), la);
+            limbs4(align28_int(bfhi(w[t]), e), lb);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const uint32_t two = limb_bytes(la, lb, l);
+                if (t & 1)
+                    pk[l][t >> 1] |= two << 16;
+                else
+                    pk[l][t >> 1] = two;
             }
         }
 #pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            long long v = (long long)d[r][0] + (long long)d[r][1] * 128ll + (long long)d[r][2] * 16384ll +
-                          (long long)d[r][3] * 2097152ll;
-            v = warp_sum_ll(v);
-            if (lane == 0 && r0 + r < nrows) accs[r0 + r] = unalign28(v, ex);
-        }
+        for (int l = 0; l < 4; ++l)
+            *reinterpret_cast<uint2 *>(xl + l * K + 8 * p) = make_uint2(pk[l][0], pk[l][1]);
     }
+    if (tid == 0) ex[0] = e;
+    d1_sync();
 }
 
 // Phase B for KV head g: see the file comment. L = pos + 1 keys.
@@ -399,8 +462,8 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         limbs4(align28_int(nhi, e), l1);
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
-            ql[(warp * 4 + l) * 64 + lane] = (int8_t)l0[l];
-            ql[(warp * 4 + l) * 64 + lane + 32] = (int8_t)l1[l];
+            ql[warp * D1S_QLS + l * 64 + lane] = (int8_t)l0[l];
+            ql[warp * D1S_QLS + l * 64 + lane + 32] = (int8_t)l1[l];
         }
         if (lane == 0) qe[warp] = e;
     } else {
@@ -437,12 +500,12 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         kss[t] = __ldg(ks + t);
         vss[t] = __ldg(vs + t);
     }
-    __syncthreads();
+    d1_sync();
     if (tid == 0) {
         kss[L - 1] = nsc[0];
         vss[L - 1] = nsc[1];
     }
-    __syncthreads();
+    d1_sync();
 
     // scores: thread (key t = tid/8 + 32 i, head h = tid % 8)
     const int h = tid & 7, tl = tid >> 3;
@@ -451,7 +514,7 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         vloc = fmaxf(vloc, vss[t]);
         if (h == 7) continue;
         const uint32_t *kr = reinterpret_cast<const uint32_t *>(t == L - 1 ? knew : kc + (size_t)t * 64);
-        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * 4 * 64);
+        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * D1S_QLS);
         int d4[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int wi = 0; wi < 16; ++wi) {
@@ -462,7 +525,7 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
                               (long long)d4[3] * 2097152ll;
         const float sc = rbf(__fmul_rn(unalign28(dot, qe[h]), kss[t]) * 0.125f);
-        S[h * QB_D1_MAX_KEYS + t] = sc;
+        S[h * D1A_SS + t] = sc;
         mloc = fmaxf(mloc, sc);
     }
     // per-head max and the largest V scale
@@ -471,7 +534,7 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
     vloc = warp_max(vloc);
     float *redf = reinterpret_cast<float *>(red);
     if (lane < 8) redf[warp * 8 + lane] = (lane == 7) ? vloc : mloc;
-    __syncthreads();
+    d1_sync();
     if (tid < 8) {
         float m = redf[tid];
         for (int w = 1; w < D1_WARPS; ++w) m = fmaxf(m, redf[w * 8 + tid]);
@@ -480,19 +543,19 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         else
             nsc[2] = m;
     }
-    __syncthreads();
+    d1_sync();
     // E = qexp(S - max) in place, exact sums
     long long z = 0;
     if (h < 7)
         for (int t = tl; t < L; t += D1_THREADS / 8) {
-            const float e = qexp(__fsub_rn(S[h * QB_D1_MAX_KEYS + t], M[h]));
-            S[h * QB_D1_MAX_KEYS + t] = e;
+            const float e = qexp(__fsub_rn(S[h * D1A_SS + t], M[h]));
+            S[h * D1A_SS + t] = e;
             z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
         }
     z += __shfl_xor_sync(0xffffffffu, z, 8);
     z += __shfl_xor_sync(0xffffffffu, z, 16);
     if (lane < 8) red[warp * 8 + lane] = z;
-    __syncthreads();
+    d1_sync();
     if (tid < 7) {
         long long zt = 0;
         for (int w = 0; w < D1_WARPS; ++w) zt += red[w * 8 + tid];
@@ -504,20 +567,20 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         s1[tid] = pow2i(sh1);
         s2[tid] = pow2i(sh - sh1);
     }
-    __syncthreads();
+    d1_sync();
     // W = rint(RN32(P * vscale) * 2^(26-F)), P = bf16(E / Z)
     if (h < 7)
         for (int t = tl; t < L; t += D1_THREADS / 8) {
-            const float w = __fmul_rn(rbf(__fmul_rn(S[h * QB_D1_MAX_KEYS + t], inv[h])), vss[t]);
-            reinterpret_cast<uint32_t *>(S)[h * QB_D1_MAX_KEYS + t] =
+            const float w = __fmul_rn(rbf(__fmul_rn(S[h * D1A_SS + t], inv[h])), vss[t]);
+            reinterpret_cast<uint32_t *>(S)[h * D1A_SS + t] =
                 __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
         }
-    __syncthreads();
+    d1_sync();
     // context: thread (half, head, 4 dims), keys t = half, half + 2, ...
     long long acc[4] = {0, 0, 0, 0};
     const int half = tid / 112, rem = tid % 112, hh = rem >> 4, d4 = rem & 15;
     if (tid < 224) {
-        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * QB_D1_MAX_KEYS;
+        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1A_SS;
         for (int t = half; t < L; t += 2) {
             const uint32_t cw = t == L - 1 ? reinterpret_cast<const uint32_t *>(vnew)[d4]
                                            : __ldg(reinterpret_cast<const uint32_t *>(vc + (size_t)t * 64) + d4);
@@ -529,11 +592,11 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         }
     }
     long long *part = reinterpret_cast<long long *>(kss);  // kss/vss are no longer needed
-    __syncthreads();
+    d1_sync();
     if (tid >= 112 && tid < 224)
 #pragma unroll
         for (int i = 0; i < 4; ++i) part[rem * 4 + i] = acc[i];
-    __syncthreads();
+    d1_sync();
     if (tid < 112) {
         uint16_t o[4];
 #pragma unroll
@@ -573,7 +636,6 @@ __device__ void d1_issue_history(const D1Args &a, int layer, uint32_t slot, uint
         }
     }
     for (int i = 0; i < n; ++i) total += bytes[i];
-    tc::fence_proxy_async_smem();  // the previous layer's generic reads of the area come first
     tc::mbar_arrive_expect_tx(kvbar, total);
     for (int i = 0; i < n; ++i) tc::bulk_load(sw + dst[i], src[i], bytes[i], kvbar);
 }
@@ -593,13 +655,15 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
     int *F = reinterpret_cast<int *>(M + 64);
     float *nsc = M + 80;  // new scales [k|v][g]
     float *vmx = M + 84;  // [g]
-    const uint16_t *qkv = a.qkv;
+    uint16_t *qkv = reinterpret_cast<uint16_t *>(sw + D1S_QKV);
+    if (tid < QB_QKV / 8) reinterpret_cast<uint4 *>(qkv)[tid] = __ldcg(reinterpret_cast<const uint4 *>(a.qkv) + tid);
     const float *cs = a.rope + (size_t)pos * 64;
     const float c = cs[lane], sn = cs[32 + lane];
+    d1_sync();
     // 18 head vectors: q heads 0..13, k heads (14, 15), v heads (16, 17)
     for (int hv = warp; hv < 18; hv += D1_WARPS) {
         const uint16_t *p = qkv + hv * 64;
-        float lo = bf2f(__ldcg(p + lane)), hi = bf2f(__ldcg(p + lane + 32));
+        float lo = bf2f(p[lane]), hi = bf2f(p[lane + 32]);
         if (hv < 16) {  // RoPE on q and k (model_backend.py:73-78)
             const float nlo = rbf(__fadd_rn(__fmul_rn(lo, c), __fmul_rn(-hi, sn)));
             const float nhi = rbf(__fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, sn)));
@@ -613,8 +677,8 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
             limbs4(align28_int(hi, e), l1);
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
-                ql[(hv * 4 + l) * 64 + lane] = (int8_t)l0[l];
-                ql[(hv * 4 + l) * 64 + lane + 32] = (int8_t)l1[l];
+                ql[hv * D1S_QLS + l * 64 + lane] = (int8_t)l0[l];
+                ql[hv * D1S_QLS + l * 64 + lane + 32] = (int8_t)l1[l];
             }
             if (lane == 0) qe[hv] = e;
         } else {
@@ -640,25 +704,24 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         }
     }
     if (ok) ok = tc::mbar_wait(kvbar, (uint32_t)layer & 1u, a.err, 22);
-    __syncthreads();
-    // scale of key t of head g (history from the aligned superset copies)
-    auto kscale = [&](int g, int t) -> float {
-        if (t == L - 1) return nsc[g];
-        const uintptr_t p = reinterpret_cast<uintptr_t>(a.ks + (size_t)a.scales_per_layer * layer +
-                                                        ((size_t)slot * 2 + g) * a.cap);
-        return reinterpret_cast<const float *>(sw + D1S_KS + g * (D1_SHORT + 8) * 4 + (p & 15))[t];
-    };
-    auto vscale = [&](int g, int t) -> float {
-        if (t == L - 1) return nsc[2 + g];
-        const uintptr_t p = reinterpret_cast<uintptr_t>(a.vs + (size_t)a.scales_per_layer * layer +
-                                                        ((size_t)slot * 2 + g) * a.cap);
-        return reinterpret_cast<const float *>(sw + D1S_VS + g * (D1_SHORT + 8) * 4 + (p & 15))[t];
-    };
+    d1_sync();
+    // scales of the history keys (inside the aligned superset copies)
+    const float *ksh[2], *vsh[2];
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+        const size_t o = (size_t)a.scales_per_layer * layer + ((size_t)slot * 2 + gg) * a.cap;
+        ksh[gg] = reinterpret_cast<const float *>(sw + D1S_KS + gg * (D1_SHORT + 8) * 4 +
+                                                  (reinterpret_cast<uintptr_t>(a.ks + o) & 15));
+        vsh[gg] = reinterpret_cast<const float *>(sw + D1S_VS + gg * (D1_SHORT + 8) * 4 +
+                                                  (reinterpret_cast<uintptr_t>(a.vs + o) & 15));
+    }
+    auto kscale = [&](int gg, int t) -> float { return t == L - 1 ? nsc[gg] : ksh[gg][t]; };
+    auto vscale = [&](int gg, int t) -> float { return t == L - 1 ? nsc[2 + gg] : vsh[gg][t]; };
     // scores: thread (head h = tid % 16, key t = tid / 16 + 16 i)
     const int h = tid & 15, tl = tid >> 4, g = h / 7;
     float mloc = -INFINITY, vloc = 0.f;
     if (h < QB_QH) {
-        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * 4 * 64);
+        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * D1S_QLS);
         for (int t = tl; t < L; t += 16) {
             vloc = fmaxf(vloc, vscale(g, t));
             const uint32_t *kr = reinterpret_cast<const uint32_t *>(
@@ -673,7 +736,7 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
             const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
                                   (long long)d4[3] * 2097152ll;
             const float sc = rbf(__fmul_rn(unalign28(dot, qe[h]), kscale(g, t)) * 0.125f);
-            S[h * D1_SHORT + t] = sc;
+            S[h * D1S_SS + t] = sc;
             mloc = fmaxf(mloc, sc);
         }
     }
@@ -685,7 +748,7 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         redf[warp * 32 + lane] = mloc;
         redf[warp * 32 + 16 + lane] = vloc;
     }
-    __syncthreads();
+    d1_sync();
     if (tid < 16) {
         float m = -INFINITY, v = 0.f;
         for (int w = 0; w < D1_WARPS; ++w) {
@@ -695,19 +758,19 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         M[tid] = m;
         if (tid == 0 || tid == 7) vmx[tid / 7] = v;  // heads 0 and 7 saw every key of KV heads 0 and 1
     }
-    __syncthreads();
+    d1_sync();
     // E = qexp(S - max), exact sums
     long long z = 0;
     if (h < QB_QH)
         for (int t = tl; t < L; t += 16) {
-            const float e = qexp(__fsub_rn(S[h * D1_SHORT + t], M[h]));
-            S[h * D1_SHORT + t] = e;
+            const float e = qexp(__fsub_rn(S[h * D1S_SS + t], M[h]));
+            S[h * D1S_SS + t] = e;
             z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
         }
     z += __shfl_xor_sync(0xffffffffu, z, 16);
-    __syncthreads();
+    d1_sync();
     if (lane < 16) red[warp * 16 + lane] = z;
-    __syncthreads();
+    d1_sync();
     if (tid < QB_QH) {
         long long zt = 0;
         for (int w = 0; w < D1_WARPS; ++w) zt += red[w * 16 + tid];
@@ -719,18 +782,18 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         s1[tid] = pow2i(sh1);
         s2[tid] = pow2i(sh - sh1);
     }
-    __syncthreads();
+    d1_sync();
     // W = rint(RN32(P * vscale) * 2^(26-F)), P = bf16(E / Z)
     if (h < QB_QH)
         for (int t = tl; t < L; t += 16) {
-            const float w = __fmul_rn(rbf(__fmul_rn(S[h * D1_SHORT + t], inv[h])), vscale(g, t));
-            reinterpret_cast<uint32_t *>(S)[h * D1_SHORT + t] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
+            const float w = __fmul_rn(rbf(__fmul_rn(S[h * D1S_SS + t], inv[h])), vscale(g, t));
+            reinterpret_cast<uint32_t *>(S)[h * D1S_SS + t] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
         }
-    __syncthreads();
+    d1_sync();
     // context: thread (head, 4 dims), exact int64 sums over the keys
     if (tid < QB_QH * 16) {
         const int hh = tid >> 4, d4 = tid & 15, gg = hh / 7;
-        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1_SHORT;
+        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1S_SS;
         long long acc[4] = {0, 0, 0, 0};
         for (int t = 0; t < L; ++t) {
             const uint32_t cw = t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + gg) * 64)[d4]
@@ -746,41 +809,52 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         pk.y = (uint32_t)f2bf(unalign28(acc[2], F[hh])) | ((uint32_t)f2bf(unalign28(acc[3], F[hh])) << 16);
         *reinterpret_cast<uint2 *>(ctx + hh * 64 + 4 * d4) = pk;
     }
-    __syncthreads();
+    d1_sync();
 }
 
-__global__ void __launch_bounds__(D1_THREADS, 1) decode1_kernel(D1Args a) {
+__global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     extern __shared__ __align__(128) uint8_t sm[];
     const D1Smem Ls = d1_smem();
     D1Ring R;
     R.ring = sm + Ls.ring;
-    R.bars = reinterpret_cast<uint64_t *>(sm + Ls.bars);
-    uint64_t *kvbar = R.bars + D1_SEGS;
+    R.full = reinterpret_cast<uint64_t *>(sm + Ls.bars);
+    R.empty = R.full + D1_SEGS;
+    uint64_t *kvbar = R.empty + D1_SEGS;
     R.off = reinterpret_cast<uint32_t *>(sm + Ls.segs);
-    R.vend = R.off + D1_SEGS;
-    R.side = R.vend + D1_SEGS;
-    R.st = R.side + 4 * D1_SEGS;
+    R.side = R.off + D1_SEGS;
     D1Layer *lay = reinterpret_cast<D1Layer *>(sm + Ls.layers);
     R.layers = lay;
     uint8_t *work = sm + Ls.work, *sw = sm + Ls.shortw;
     int8_t *xl = reinterpret_cast<int8_t *>(work);
     int *ex = reinterpret_cast<int *>(work + 4 * QB_FFN);
-    float *accs = reinterpret_cast<float *>(sm + Ls.accs);
     long long *red = reinterpret_cast<long long *>(sm + Ls.red);
     uint8_t *rd = sm + Ls.red;
-    const int tid = threadIdx.x, c = blockIdx.x, G = gridDim.x;
-    for (int i = tid; i < QB_NL * (int)(sizeof(D1Layer) / 8); i += D1_THREADS)
+    const int tid = threadIdx.x, c = blockIdx.x, G = gridDim.x, warp = tid >> 5;
+    for (int i = tid; i < QB_NL * (int)(sizeof(D1Layer) / 8); i += D1_BLOCK)
         reinterpret_cast<uint64_t *>(lay)[i] = reinterpret_cast<const uint64_t *>(a.layers)[i];
-    __syncthreads();
     if (tid == 0) {
-        for (int s = 0; s < D1_SEGS + 1; ++s) tc::mbar_init(&R.bars[s], 1);
+        for (int s = 0; s < D1_SEGS; ++s) {
+            tc::mbar_init(&R.full[s], 1);
+            tc::mbar_init(&R.empty[s], D1_WARPS);
+        }
+        tc::mbar_init(kvbar, 1);
         tc::mbar_fence_init();
-        R.st[0] = R.st[1] = R.st[2] = R.st[3] = 0;
-        d1_issue(a, R);  // weights are constant: start streaming at once
     }
-    __syncthreads();
+    __syncthreads();  // the last barrier of all 288 threads
+    if (warp == D1_WARPS) {
+        if ((tid & 31) == 0) d1_produce(a, R);  // weights are constant: stream from the start
+        return;
+    }
     const uint32_t slot = __ldcg(a.meta + 1), pos = __ldcg(a.meta + 2);
     const bool shortctx = pos + 1 <= (uint32_t)D1_SHORT;
+    // this CTA's rows of the residual stream (the O and down rows are the same
+    // partition), kept here so the residual additions need no global read
+    float *xo = reinterpret_cast<float *>(sm + Ls.accs);
+    {
+        int b, e;
+        d1_part(QB_HID, c, G, b, e);
+        if (tid < e - b) xo[tid] = bf2f(__ldcg(a.x + b + tid));
+    }
     bool ok = true;
     unsigned nbar = 0;
     int s = 0;
@@ -793,13 +867,13 @@ __global__ void __launch_bounds__(D1_THREADS, 1) decode1_kernel(D1Args a) {
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
             d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[3]), a.eps, xl, ex, rd);
-            d1_dot<QB_HID, 2>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], accs);
-            __syncthreads();
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
             const uint16_t *bs = reinterpret_cast<const uint16_t *>(seg + g[2]);
-            for (int i = tid; i < e - b; i += D1_THREADS)
-                a.qkv[b + i] = f2bf(rbf(rbf(rbf(accs[i]) * sc[i]) + bf2f(bs[i])));
-            d1_release(a, R, s++);
+            d1_dot<QB_HID, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0],
+                              [&](int r0, int nr, const float (&acc)[1]) {
+                                  a.qkv[b + r0] = f2bf(rbf(rbf(rbf(acc[0]) * sc[r0]) + bf2f(bs[r0])));
+                              });
+            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
         // B + C: attention, then O + residual
@@ -807,59 +881,60 @@ __global__ void __launch_bounds__(D1_THREADS, 1) decode1_kernel(D1Args a) {
             d1_attention_short(a, l, slot, pos, sw, kvbar, red, ok);
             d1_row896<false, false>(reinterpret_cast<const uint16_t *>(sw + D1S_CTX), nullptr, 0.f, xl, ex, rd);
         } else {
-            if (c < QB_KVH) d1_attention(a, l, c, slot, pos, work, reinterpret_cast<uint8_t *>(red));
+            if (c < QB_KVH) d1_attention(a, l, c, slot, pos, work, rd);
             d1_grid_sync(a, ++nbar, ok);
             d1_row896<false, true>(a.ctx, nullptr, 0.f, xl, ex, rd);
         }
-        __syncthreads();
         d1_part(QB_HID, c, G, b, e);
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
-            d1_dot<QB_HID, 2>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], accs);
-            __syncthreads();
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-            for (int i = tid; i < e - b; i += D1_THREADS) {
-                const int n = b + i;
-                a.x[n] = f2bf(rbf(bf2f(__ldcg(a.x + n)) + rbf(rbf(accs[i]) * sc[i])));
-            }
-            d1_release(a, R, s++);
+            d1_dot<QB_HID, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0],
+                              [&](int r0, int nr, const float (&acc)[1]) {
+                                  const float v = rbf(xo[r0] + rbf(rbf(acc[0]) * sc[r0]));
+                                  xo[r0] = v;
+                                  a.x[b + r0] = f2bf(v);
+                              });
+            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
-        // D: RMSNorm + gate/up pairs + SiLU*mul
+        // D: RMSNorm + gate/up pairs + SiLU*mul (rows 2j, 2j+1 stay in one warp)
         d1_part(QB_FFN, c, G, b, e);
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
             d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[2]), a.eps, xl, ex, rd);
-            d1_dot<QB_HID, 2>(reinterpret_cast<const int8_t *>(seg), 2 * (e - b), xl, ex[0], accs);
-            __syncthreads();
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-            for (int i = tid; i < e - b; i += D1_THREADS) {
-                const float gt = rbf(rbf(accs[2 * i]) * sc[2 * i]);
-                const float up = rbf(rbf(accs[2 * i + 1]) * sc[2 * i + 1]);
-                a.mid[b + i] = f2bf(rbf(silu_q(gt)) * up);
-            }
-            d1_release(a, R, s++);
+            d1_dot<QB_HID, 10>(reinterpret_cast<const int8_t *>(seg), 2 * (e - b), xl, ex[0],
+                               [&](int r0, int nr, const float (&acc)[10]) {
+#pragma unroll
+                                   for (int r = 0; r < 10; r += 2) {
+                                       if (r >= nr) break;
+                                       const float gt = rbf(rbf(acc[r]) * sc[r0 + r]);
+                                       const float up = rbf(rbf(acc[r + 1]) * sc[r0 + r + 1]);
+                                       a.mid[b + (r0 + r) / 2] = f2bf(rbf(silu_q(gt)) * up);
+                                   }
+                               });
+            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
         // E: down + residual
-        load_x_limbs<QB_FFN, 1, D1_THREADS, true>(a.mid, 0, 1, nullptr, 0.f, xl, ex);
-        __syncthreads();
+        d1_row4864(a.mid, xl, ex, rd);
         d1_part(QB_HID, c, G, b, e);
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
-            d1_dot<QB_FFN, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], accs);
-            __syncthreads();
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-            for (int i = tid; i < e - b; i += D1_THREADS) {
-                const int n = b + i;
-                a.x[n] = f2bf(rbf(bf2f(__ldcg(a.x + n)) + rbf(rbf(accs[i]) * sc[i])));
-            }
-            d1_release(a, R, s++);
+            d1_dot<QB_FFN, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0],
+                              [&](int r0, int nr, const float (&acc)[1]) {
+                                  const float v = rbf(xo[r0] + rbf(rbf(acc[0]) * sc[r0]));
+                                  xo[r0] = v;
+                                  a.x[b + r0] = f2bf(v);
+                              });
+            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
     }
     // LM head: final RMSNorm (gains come with the first piece), this CTA's
-    // rows in 32-row pieces, best (value, index)
+    // rows in 32-row pieces (4 per warp), the warp's best (value, index)
     {
         const uint8_t *seg = d1_wait(a, R, s, g, ok);
         d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[2]), a.eps, xl, ex, rd);
@@ -871,45 +946,52 @@ __global__ void __launch_bounds__(D1_THREADS, 1) decode1_kernel(D1Args a) {
     for (int r0 = lb; r0 < le; r0 += D1_LM_ROWS) {
         const int nr = min(D1_LM_ROWS, le - r0);
         const uint8_t *seg = d1_wait(a, R, s, g, ok);
-        d1_dot<QB_HID, 4>(reinterpret_cast<const int8_t *>(seg), nr, xl, ex[0], accs);
-        __syncthreads();
-        if (tid < nr) {
-            const int n = r0 + tid;
-            const float v = rbf(rbf(accs[tid]) * reinterpret_cast<const float *>(seg + g[1])[tid]);
-            if (a.logits) a.logits[n] = f2bf(v);
-            if (better(v, (uint32_t)n, bv, bi)) {
-                bv = v;
-                bi = (uint32_t)n;
-            }
-        }
-        d1_release(a, R, s++);
-    }
-    // best of the CTA (threads < 32 hold candidates)
-    if (tid < 32) {
+        const float *sc = reinterpret_cast<const float *>(seg + g[1]);
+        d1_dot<QB_HID, 4>(reinterpret_cast<const int8_t *>(seg), nr, xl, ex[0],
+                          [&](int q0, int qn, const float (&acc)[4]) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
+                              for (int r = 0; r < 4; ++r) {
+                                  if (r >= qn) break;
+                                  const int n = r0 + q0 + r;
+                                  const float v = rbf(rbf(acc[r]) * sc[q0 + r]);
+                                  if (a.logits) a.logits[n] = f2bf(v);
+                                  if (better(v, (uint32_t)n, bv, bi)) {
+                                      bv = v;
+                                      bi = (uint32_t)n;
+                                  }
+                              }
+                          });
+        d1_done(R, s++);
+    }
+    // best of the CTA: lane 0 of each warp holds its warp's candidate
+    float *cv = reinterpret_cast<float *>(rd);
+    uint32_t *ci = reinterpret_cast<uint32_t *>(rd + 64);
+    if ((tid & 31) == 0) {
+        cv[warp] = bv;
+        ci[warp] = bi;
+    }
+    d1_sync();
+    if (tid == 0) {
+        float v = cv[0];
+        uint32_t i = ci[0];
+        for (int w = 1; w < D1_WARPS; ++w)
+            if (better(cv[w], ci[w], v, i)) {
+                v = cv[w];
+                i = ci[w];
             }
-        }
-        if (tid == 0) {
-            a.cand_v[c] = bv;
-            a.cand_i[c] = bi;
-        }
+        a.cand_v[c] = v;
+        a.cand_i[c] = i;
     }
     d1_grid_sync(a, ++nbar, ok);
     if (c == 0 && tid < 32) {
         float v = -INFINITY;
         uint32_t i = 0;
         for (int k = tid; k < G; k += 32) {
-            const float cv = __ldcg(a.cand_v + k);
-            const uint32_t ci = __ldcg(a.cand_i + k);
-            if (better(cv, ci, v, i)) {
-                v = cv;
-                i = ci;
+            const float cv2 = __ldcg(a.cand_v + k);
+            const uint32_t ci2 = __ldcg(a.cand_i + k);
+            if (better(cv2, ci2, v, i)) {
+                v = cv2;
+                i = ci2;
             }
         }
 #pragma unroll
@@ -927,7 +1009,19 @@ __global__ void __launch_bounds__(D1_THREADS, 1) decode1_kernel(D1Args a) {
 
 static int d1_grid = 0;
 
-int decode1_supported(int max_len) { return max_len >= 1 && max_len <= QB_D1_MAX_KEYS; }
+// The per-warp row tiling covers one CTA's slice only with at least 144 CTAs
+// (QKV: 8 rows, O / down: 8 rows, gate/up: 80 rows per CTA at most).
+constexpr int D1_MIN_GRID = 144;
+
+int decode1_supported(int max_len) {
+    static int sms = -1;
+    if (sms < 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            sms = 0;
+    }
+    return sms >= D1_MIN_GRID && max_len >= 1 && max_len <= QB_D1_MAX_KEYS;
+}
 
 size_t decode1_smem_bytes() { return (size_t)d1_smem().total; }
 
@@ -941,10 +1035,11 @@ int launch_decode1(const D1Args &a, cudaStream_t st) {
             return -3;
         int sms = 0, per_sm = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -3;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode1_kernel, D1_THREADS,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode1_kernel, D1_BLOCK,
                                                           decode1_smem_bytes()) != cudaSuccess ||
             per_sm < 1)
             return -3;
+        if (sms < D1_MIN_GRID) return -1;
         d1_grid = sms;
         configured |= 1u << (dev & 31);
     }
@@ -952,7 +1047,7 @@ int launch_decode1(const D1Args &a, cudaStream_t st) {
     pdl_break();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d1_grid);
-    cfg.blockDim = dim3(D1_THREADS);
+    cfg.blockDim = dim3(D1_BLOCK);
     cfg.dynamicSmemBytes = decode1_smem_bytes();
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
