@@ -73,7 +73,7 @@ constexpr int D1_SHORT_BYTES = D1S_QKV + QB_QKV * 2;
 constexpr int D1_LIMB_BYTES = 4 * QB_FFN + 16;
 
 struct D1Smem {
-    int ring, work, shortw, bars, segs, layers, red, accs, total;
+    int ring, work, shortw, bars, segs, layers, red, accs, part, total;
 };
 __host__ __device__ inline D1Smem d1_smem() {
     D1Smem L;
@@ -87,7 +87,8 @@ __host__ __device__ inline D1Smem d1_smem() {
     L.red = L.layers + QB_NL * (int)sizeof(D1Layer);
     L.red = (L.red + 15) & ~15;
     L.accs = L.red + D1_WARPS * 16 * 8;
-    L.total = L.accs + D1_MAXROWS * 4;
+    L.part = L.accs + D1_MAXROWS * 4;  // split-K partial sums [8 slices][16 rows][4 limbs] int32
+    L.total = L.part + D1_WARPS * 16 * 4 * 4;
     return L;
 }
 
@@ -366,6 +367,79 @@ __device__ __forceinline__ void d1_dot(const int8_t *w, int nrows, const int8_t 
         acc[r] = unalign28(warp_sum_ll(v), ex);
     }
     if (lane == 0) epi(r0, nr, acc);
+}
+
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Tensor-core form of the exact projection dot products: one m-tile of 16
+// weight rows [row0, row0 + 16) (rows >= nrows read as 0) against the four
+// limb planes (the N columns 0..3 of m16n8k32, s8 x s8 -> s32) over the 64-k
+// blocks [kb0, kb1). Thread (gid, tig) loads 16 bytes of rows gid and gid + 8
+// at k = 64 kb + 16 tig; MMA step s uses bytes 8s..8s+7 of them, and the limb
+// words at the same k, so both operands are plain words of consecutive k.
+// c[0..3] = the m16n8 accumulator fragment (rows gid | gid + 8, limbs 2 tig,
+// 2 tig + 1; tig >= 2 holds the unused columns).
+template <int K>
+__device__ __forceinline__ void d1_mma_tile(const int8_t *w, int nrows, int row0, int kb0, int kb1, const int8_t *xl,
+                                            int (&c)[4]) {
+    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int ra = row0 + gid, rb = ra + 8;
+    const int8_t *pa = w + (size_t)ra * K + 16 * tig, *pb = w + (size_t)rb * K + 16 * tig;
+    const int8_t *px = xl + (size_t)(gid & 3) * K + 16 * tig;
+    c[0] = c[1] = c[2] = c[3] = 0;
+    for (int kb = kb0; kb < kb1; ++kb) {
+        const uint4 u = ra < nrows ? *reinterpret_cast<const uint4 *>(pa + 64 * kb) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 v = rb < nrows ? *reinterpret_cast<const uint4 *>(pb + 64 * kb) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 x = gid < 4 ? *reinterpret_cast<const uint4 *>(px + 64 * kb) : make_uint4(0u, 0u, 0u, 0u);
+        mma_s8_16832(c, u.x, v.x, u.y, v.y, x.x, x.y);
+        mma_s8_16832(c, u.z, v.z, u.w, v.w, x.z, x.w);
+    }
+}
+
+// Exact sums of rows gid and gid + 8 of a fragment, on the lanes with tig == 0
+// (limbs 2 and 3 come from the tig == 1 lane).
+__device__ __forceinline__ void d1_fold(const int (&c)[4], long long &lo, long long &hi) {
+    const int c0 = __shfl_down_sync(0xffffffffu, c[0], 1), c1 = __shfl_down_sync(0xffffffffu, c[1], 1);
+    const int c2 = __shfl_down_sync(0xffffffffu, c[2], 1), c3 = __shfl_down_sync(0xffffffffu, c[3], 1);
+    lo = (long long)c[0] + (long long)c[1] * 128ll + (long long)c0 * 16384ll + (long long)c1 * 2097152ll;
+    hi = (long long)c[2] + (long long)c[3] * 128ll + (long long)c2 * 16384ll + (long long)c3 * 2097152ll;
+}
+
+// Rows [0, nrows) (nrows <= 16) of a slice, K split over the 8 compute warps
+// into `part`; after the compute barrier, thread r < nrows runs epi(r, acc).
+template <int K, class Epi>
+__device__ __forceinline__ void d1_mma_rows16(const int8_t *w, int nrows, const int8_t *xl, int ex, int *part, Epi epi) {
+    constexpr int NB = K / 64;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int kb0 = NB * warp / D1_WARPS, kb1 = NB * (warp + 1) / D1_WARPS;
+    int c[4];
+    d1_mma_tile<K>(w, nrows, 0, kb0, kb1, xl, c);
+    if (tig < 2) {
+        int *p = part + warp * 64;
+        p[gid * 4 + 2 * tig] = c[0];
+        p[gid * 4 + 2 * tig + 1] = c[1];
+        p[(gid + 8) * 4 + 2 * tig] = c[2];
+        p[(gid + 8) * 4 + 2 * tig + 1] = c[3];
+    }
+    d1_sync();
+    if (threadIdx.x < nrows) {
+        const int r = threadIdx.x;
+        int l4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int sl = 0; sl < D1_WARPS; ++sl)
+#pragma unroll
+            for (int l = 0; l < 4; ++l) l4[l] += part[sl * 64 + r * 4 + l];
+        const long long v = (long long)l4[0] + (long long)l4[1] * 128ll + (long long)l4[2] * 16384ll +
+                            (long long)l4[3] * 2097152ll;
+        epi(r, unalign28(v, ex));
+    }
 }
 
 // The four int8 limb planes of one 4864-wide row (plain conversion), every
@@ -829,6 +903,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     int *ex = reinterpret_cast<int *>(work + 4 * QB_FFN);
     long long *red = reinterpret_cast<long long *>(sm + Ls.red);
     uint8_t *rd = sm + Ls.red;
+    int *part = reinterpret_cast<int *>(sm + Ls.part);
     const int tid = threadIdx.x, c = blockIdx.x, G = gridDim.x, warp = tid >> 5;
     for (int i = tid; i < QB_NL * (int)(sizeof(D1Layer) / 8); i += D1_BLOCK)
         reinterpret_cast<uint64_t *>(lay)[i] = reinterpret_cast<const uint64_t *>(a.layers)[i];
@@ -869,10 +944,10 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
             d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[3]), a.eps, xl, ex, rd);
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
             const uint16_t *bs = reinterpret_cast<const uint16_t *>(seg + g[2]);
-            d1_dot<QB_HID, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0],
-                              [&](int r0, int nr, const float (&acc)[1]) {
-                                  a.qkv[b + r0] = f2bf(rbf(rbf(rbf(acc[0]) * sc[r0]) + bf2f(bs[r0])));
-                              });
+            d1_mma_rows16<QB_HID>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], part,
+                                  [&](int r, float acc) {
+                                      a.qkv[b + r] = f2bf(rbf(rbf(rbf(acc) * sc[r]) + bf2f(bs[r])));
+                                  });
             d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
@@ -889,12 +964,12 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-            d1_dot<QB_HID, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0],
-                              [&](int r0, int nr, const float (&acc)[1]) {
-                                  const float v = rbf(xo[r0] + rbf(rbf(acc[0]) * sc[r0]));
-                                  xo[r0] = v;
-                                  a.x[b + r0] = f2bf(v);
-                              });
+            d1_mma_rows16<QB_HID>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], part,
+                                  [&](int r, float acc) {
+                                      const float v = rbf(xo[r] + rbf(rbf(acc) * sc[r]));
+                                      xo[r] = v;
+                                      a.x[b + r] = f2bf(v);
+                                  });
             d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
@@ -904,16 +979,25 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
             d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[2]), a.eps, xl, ex, rd);
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-            d1_dot<QB_HID, 10>(reinterpret_cast<const int8_t *>(seg), 2 * (e - b), xl, ex[0],
-                               [&](int r0, int nr, const float (&acc)[10]) {
+            const int nrows = 2 * (e - b), lane = tid & 31, gid = lane >> 2;
+            if (16 * warp < nrows) {
+                int cf[4];
+                d1_mma_tile<QB_HID>(reinterpret_cast<const int8_t *>(seg), nrows, 16 * warp, 0, QB_HID / 64, xl, cf);
+                long long lo, hi;
+                d1_fold(cf, lo, hi);
+                // rows 16w + gid (gate when gid is even) and the next row (up) of the lane 4 above
+                const long long lo1 = __shfl_down_sync(0xffffffffu, lo, 4), hi1 = __shfl_down_sync(0xffffffffu, hi, 4);
+                if ((lane & 3) == 0 && (gid & 1) == 0) {
 #pragma unroll
-                                   for (int r = 0; r < 10; r += 2) {
-                                       if (r >= nr) break;
-                                       const float gt = rbf(rbf(acc[r]) * sc[r0 + r]);
-                                       const float up = rbf(rbf(acc[r + 1]) * sc[r0 + r + 1]);
-                                       a.mid[b + (r0 + r) / 2] = f2bf(rbf(silu_q(gt)) * up);
-                                   }
-                               });
+                    for (int half = 0; half < 2; ++half) {
+                        const int r = 16 * warp + gid + 8 * half;
+                        if (r >= nrows) break;
+                        const float gt = rbf(rbf(unalign28(half ? hi : lo, ex[0])) * sc[r]);
+                        const float up = rbf(rbf(unalign28(half ? hi1 : lo1, ex[0])) * sc[r + 1]);
+                        a.mid[b + r / 2] = f2bf(rbf(silu_q(gt)) * up);
+                    }
+                }
+            }
             d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
@@ -923,12 +1007,12 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-            d1_dot<QB_FFN, 1>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0],
-                              [&](int r0, int nr, const float (&acc)[1]) {
-                                  const float v = rbf(xo[r0] + rbf(rbf(acc[0]) * sc[r0]));
-                                  xo[r0] = v;
-                                  a.x[b + r0] = f2bf(v);
-                              });
+            d1_mma_rows16<QB_FFN>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], part,
+                                  [&](int r, float acc) {
+                                      const float v = rbf(xo[r] + rbf(rbf(acc) * sc[r]));
+                                      xo[r] = v;
+                                      a.x[b + r] = f2bf(v);
+                                  });
             d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
@@ -943,25 +1027,47 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     d1_part(QB_VOCAB, c, G, lb, le);
     float bv = -INFINITY;
     uint32_t bi = 0;
-    for (int r0 = lb; r0 < le; r0 += D1_LM_ROWS) {
+    // piece p is computed by warps 2 (p % 4) and 2 (p % 4) + 1 (one 16-row
+    // m-tile each); every warp still waits for every piece before releasing
+    // it, so releases stay in order per ring slot
+    const int lane = tid & 31, gid = lane >> 2;
+    for (int r0 = lb, p = 0; r0 < le; r0 += D1_LM_ROWS, ++p) {
         const int nr = min(D1_LM_ROWS, le - r0);
         const uint8_t *seg = d1_wait(a, R, s, g, ok);
-        const float *sc = reinterpret_cast<const float *>(seg + g[1]);
-        d1_dot<QB_HID, 4>(reinterpret_cast<const int8_t *>(seg), nr, xl, ex[0],
-                          [&](int q0, int qn, const float (&acc)[4]) {
+        if ((p & 3) == (warp >> 1)) {
+            const float *sc = reinterpret_cast<const float *>(seg + g[1]);
+            const int m0 = 16 * (warp & 1);
+            int cf[4];
+            d1_mma_tile<QB_HID>(reinterpret_cast<const int8_t *>(seg), nr, m0, 0, QB_HID / 64, xl, cf);
+            long long lo, hi;
+            d1_fold(cf, lo, hi);
+            if ((lane & 3) == 0) {
 #pragma unroll
-                              for (int r = 0; r < 4; ++r) {
-                                  if (r >= qn) break;
-                                  const int n = r0 + q0 + r;
-                                  const float v = rbf(rbf(acc[r]) * sc[q0 + r]);
-                                  if (a.logits) a.logits[n] = f2bf(v);
-                                  if (better(v, (uint32_t)n, bv, bi)) {
-                                      bv = v;
-                                      bi = (uint32_t)n;
-                                  }
-                              }
-                          });
+                for (int half = 0; half < 2; ++half) {
+                    const int rr = m0 + gid + 8 * half;
+                    if (rr < nr) {
+                        const int n = r0 + rr;
+                        const float v = rbf(rbf(unalign28(half ? hi : lo, ex[0])) * sc[rr]);
+                        if (a.logits) a.logits[n] = f2bf(v);
+                        if (better(v, (uint32_t)n, bv, bi)) {
+                            bv = v;
+                            bi = (uint32_t)n;
+                        }
+                    }
+                }
+            }
+        }
         d1_done(R, s++);
+    }
+    // best of the warp (lanes 0, 4, 8, ... hold candidates)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
     }
     // best of the CTA: lane 0 of each warp holds its warp's candidate
     float *cv = reinterpret_cast<float *>(rd);
