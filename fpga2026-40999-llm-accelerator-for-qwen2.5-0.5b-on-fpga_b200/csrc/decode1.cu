@@ -45,55 +45,85 @@ constexpr int D1_LM_ROWS = 32;   // LM-head rows per slice
 constexpr int D1_MAXROWS = 72;   // largest projection slice of one CTA (gate/up pairs)
 constexpr int D1_SHORT = 64;     // contexts up to this many keys use the fused B+C phase
 
-constexpr int D1S_QLS = 4 * 64 + 4;  // q limb planes per head, padded against bank conflicts
+constexpr int D1S_QLS = 4 * 64 + 16;  // q limb planes per head: 16-byte aligned, padded against bank conflicts
 
 // long-context attention scratch (phase B on CTAs 0 and 1), inside the work area
 constexpr int D1A_QF = 0;                              // float [7][64] q after RoPE
 constexpr int D1A_QL = D1A_QF + 7 * 64 * 4;            // int8 [7][260] q limb planes (padded rows)
-constexpr int D1A_NEW = D1A_QL + 7 * (4 * 64 + 4) + 4; // int8 [2][64] new k / v codes
+constexpr int D1A_NEW = D1A_QL + 7 * D1S_QLS;          // int8 [2][64] new k / v codes
 constexpr int D1A_MISC = D1A_NEW + 128;                // qe[8] int, M[8], inv[8], s1[8], s2[8], F[8], new scales[2], vmax
 constexpr int D1A_RED = D1A_MISC + 64 * 4;             // (unused: reductions use the shared red area)
 constexpr int D1A_KS = D1A_RED + D1_WARPS * 8 * 8;     // float [maxkeys] K scales, V scales, S [7][maxkeys + 1]
 constexpr int D1A_SS = QB_D1_MAX_KEYS + 1;             // score row stride (padded against bank conflicts)
 constexpr int D1_LONG_BYTES = D1A_KS + 4 * (2 * QB_D1_MAX_KEYS + 7 * D1A_SS);
 
-// short-context area (after the limb planes): prefetched history and scratch
-constexpr int D1S_KC = 0;                                  // int8 [2][64 keys][64] K codes
-constexpr int D1S_VC = D1S_KC + 2 * D1_SHORT * 64;         // int8 [2][64][64] V codes
-constexpr int D1S_KS = D1S_VC + 2 * D1_SHORT * 64;         // float [2][64 + 8] K scales (16-byte aligned superset)
-constexpr int D1S_VS = D1S_KS + 2 * (D1_SHORT + 8) * 4;    // float [2][64 + 8] V scales
-constexpr int D1S_QL = D1S_VS + 2 * (D1_SHORT + 8) * 4;    // int8 [14][260] q limb planes
-constexpr int D1S_NEW = D1S_QL + 14 * D1S_QLS;             // int8 [2 k|v][2 heads][64] new codes
-constexpr int D1S_SS = D1_SHORT + 1;                        // scores per head, padded
-constexpr int D1S_S = D1S_NEW + 4 * 64;                    // float [14][65] scores -> E -> W (u32)
-constexpr int D1S_CTX = D1S_S + 14 * D1S_SS * 4;           // bf16 [896] context
-constexpr int D1S_MISC = D1S_CTX + QB_HID * 2;             // qe[16], M[16], inv[16], s1[16], s2[16], F[16], nsc[4], vmax[2]
-constexpr int D1S_QKV = D1S_MISC + 128 * 4;                // bf16 [1152] this step's q | k | v (pre-RoPE)
-constexpr int D1_SHORT_BYTES = D1S_QKV + QB_QKV * 2;
-constexpr int D1_LIMB_BYTES = 4 * QB_FFN + 16;
+// short-context area (after the limb planes): prefetched history and scratch;
+// every region starts on a 16-byte boundary (vector and bulk-copy accesses)
+constexpr int d1_al16(int x) { return (x + 15) & ~15; }
+constexpr int D1S_KC = 0;                                            // int8 [2][64 keys][64] K codes, later V^T [2][64 dims][64 keys]
+constexpr int D1S_VC = d1_al16(D1S_KC + 2 * D1_SHORT * 64);          // int8 [2][64][64] V codes
+constexpr int D1S_KS = d1_al16(D1S_VC + 2 * D1_SHORT * 64);          // float [2][64 + 8] K scales (16-byte aligned superset)
+constexpr int D1S_VS = d1_al16(D1S_KS + 2 * (D1_SHORT + 8) * 4);     // float [2][64 + 8] V scales
+constexpr int D1S_QL = d1_al16(D1S_VS + 2 * (D1_SHORT + 8) * 4);     // int8 [14][272] q limb planes, later W byte planes [14][16] x 16 B
+constexpr int D1S_NEW = d1_al16(D1S_QL + 14 * D1S_QLS);              // int8 [2 k|v][2 heads][64] new codes
+constexpr int D1S_SS = D1_SHORT + 1;                                  // scores per head, padded
+constexpr int D1S_S = d1_al16(D1S_NEW + 4 * 64);                     // float [14][65] scores -> E -> W (u32)
+constexpr int D1S_CTX = d1_al16(D1S_S + 14 * D1S_SS * 4);            // bf16 [896] context
+constexpr int D1S_MISC = d1_al16(D1S_CTX + QB_HID * 2);              // qe[16], M[16], inv[16], s1[16], s2[16], F[16], nsc[4], vmax[2]
+constexpr int D1S_QKV = d1_al16(D1S_MISC + 128 * 4);                 // bf16 [1152] this step's q | k | v (pre-RoPE)
+constexpr int D1_SHORT_BYTES = d1_al16(D1S_QKV + QB_QKV * 2);
+constexpr int D1_LIMB_BYTES = d1_al16(4 * QB_FFN + 16);
+static_assert(D1S_QLS % 16 == 0 && D1_RING % 16 == 0, "16-byte aligned rows");
+static_assert(14 * 16 * 16 <= D1S_NEW - D1S_QL, "W byte planes fit in the q limb area");
+static_assert(2 * 64 * 64 <= D1S_VC - D1S_KC, "V^T fits in the K history area");
 
 struct D1Smem {
     int ring, work, shortw, bars, segs, layers, red, accs, part, total;
 };
-__host__ __device__ inline D1Smem d1_smem() {
-    D1Smem L;
+__host__ __device__ constexpr D1Smem d1_smem() {
+    D1Smem L{};
     L.ring = 0;
     L.work = L.ring + D1_RING;
     L.shortw = L.work + D1_LIMB_BYTES;
     const int work = D1_LIMB_BYTES + D1_SHORT_BYTES > D1_LONG_BYTES ? D1_LIMB_BYTES + D1_SHORT_BYTES : D1_LONG_BYTES;
-    L.bars = (L.work + work + 15) & ~15;
+    L.bars = d1_al16(L.work + work);
     L.segs = L.bars + (2 * D1_SEGS + 2) * 8;  // full / empty mbarriers per slot, then the KV-history one
-    L.layers = L.segs + 512;              // per slot: ring offset, virtual end, side offsets; producer state
-    L.red = L.layers + QB_NL * (int)sizeof(D1Layer);
-    L.red = (L.red + 15) & ~15;
+    L.layers = L.segs + 512;                  // per slot: ring offset, side offsets
+    L.red = d1_al16(L.layers + QB_NL * (int)sizeof(D1Layer));
     L.accs = L.red + D1_WARPS * 16 * 8;
     L.part = L.accs + D1_MAXROWS * 4;  // split-K partial sums [8 slices][16 rows][4 limbs] int32
     L.total = L.part + D1_WARPS * 16 * 4 * 4;
     return L;
 }
+// 227 KB per CTA, less 256 bytes for the static shared variables (128 used)
+static_assert(d1_smem().total <= 232448 - 256, "shared memory of the persistent decode CTA");
+static_assert(d1_smem().shortw % 16 == 0 && d1_smem().work % 16 == 0 && d1_smem().red % 16 == 0 &&
+                  d1_smem().part % 16 == 0,
+              "16-byte aligned regions");
 
 // Barrier of the 256 compute threads (the producer warp never joins).
 __device__ __forceinline__ void d1_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+// 4 x 4 byte transpose: o[j] byte i = r[i] byte j.
+__device__ __forceinline__ void transpose4(const uint32_t (&r)[4], uint32_t (&o)[4]) {
+    const uint32_t t0 = prmt(r[0], r[1], 0x5140u), t1 = prmt(r[0], r[1], 0x7362u);
+    const uint32_t t2 = prmt(r[2], r[3], 0x5140u), t3 = prmt(r[2], r[3], 0x7362u);
+    o[0] = prmt(t0, t2, 0x5410u);
+    o[1] = prmt(t0, t2, 0x7632u);
+    o[2] = prmt(t1, t3, 0x5410u);
+    o[3] = prmt(t1, t3, 0x7632u);
+}
+// sum of 4 signed bytes of a times 4 unsigned bytes of b, plus c
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
 // [begin, end) of part c of n items split over g parts
 __device__ __forceinline__ void d1_part(int n, int c, int g, int &b, int &e) {
@@ -802,10 +832,16 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
                 t == L - 1 ? nw + g * 64 : reinterpret_cast<const int8_t *>(sw + D1S_KC) + (g * D1_SHORT + t) * 64);
             int d4[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int wi = 0; wi < 16; ++wi) {
-                const int kw = (int)kr[wi];
+            for (int w4 = 0; w4 < 4; ++w4) {
+                const uint4 k4 = reinterpret_cast<const uint4 *>(kr)[w4];
 #pragma unroll
-                for (int l = 0; l < 4; ++l) d4[l] = __dp4a(kw, (int)qr[l * 16 + wi], d4[l]);
+                for (int l = 0; l < 4; ++l) {
+                    const uint4 q4 = reinterpret_cast<const uint4 *>(qr + l * 16)[w4];
+                    d4[l] = __dp4a((int)k4.x, (int)q4.x, d4[l]);
+                    d4[l] = __dp4a((int)k4.y, (int)q4.y, d4[l]);
+                    d4[l] = __dp4a((int)k4.z, (int)q4.z, d4[l]);
+                    d4[l] = __dp4a((int)k4.w, (int)q4.w, d4[l]);
+                }
             }
             const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
                                   (long long)d4[3] * 2097152ll;
@@ -864,24 +900,53 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
             reinterpret_cast<uint32_t *>(S)[h * D1S_SS + t] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
         }
     d1_sync();
-    // context: thread (head, 4 dims), exact int64 sums over the keys
-    if (tid < QB_QH * 16) {
-        const int hh = tid >> 4, d4 = tid & 15, gg = hh / 7;
-        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1S_SS;
-        long long acc[4] = {0, 0, 0, 0};
-        for (int t = 0; t < L; ++t) {
-            const uint32_t cw = t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + gg) * 64)[d4]
-                                           : reinterpret_cast<const uint32_t *>(sw + D1S_VC)[(gg * D1_SHORT + t) * 16 + d4];
-            const long long wt = (long long)W[t];
-            acc[0] += wt * (int)(int8_t)(cw & 0xffu);
-            acc[1] += wt * (int)(int8_t)((cw >> 8) & 0xffu);
-            acc[2] += wt * (int)(int8_t)((cw >> 16) & 0xffu);
-            acc[3] += wt * (int)(int8_t)(cw >> 24);
+    // context on the integer dot-product units: V^T [g][dim][key] (4 keys per
+    // word, word index swizzled by dim against bank conflicts) and the four
+    // byte planes of W [h][key / 4] (16 bytes: planes 0..3 of 4 keys), then
+    // dp4a (V codes signed x W bytes unsigned) per plane, exact in int32
+    const int L4 = (L + 3) >> 2;
+    uint32_t *vt = reinterpret_cast<uint32_t *>(sw + D1S_KC);
+    uint4 *wp = reinterpret_cast<uint4 *>(sw + D1S_QL);
+    for (int i = tid; i < 2 * 16 * L4; i += D1_THREADS) {
+        const int gg = i / (16 * L4), t4 = (i / 16) % L4, d4 = i & 15;
+        uint32_t r[4], o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int t = 4 * t4 + j;
+            r[j] = t < L - 1 ? reinterpret_cast<const uint32_t *>(sw + D1S_VC)[(gg * D1_SHORT + t) * 16 + d4]
+                 : t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + gg) * 64)[d4] : 0u;
         }
-        uint2 pk;
-        pk.x = (uint32_t)f2bf(unalign28(acc[0], F[hh])) | ((uint32_t)f2bf(unalign28(acc[1], F[hh])) << 16);
-        pk.y = (uint32_t)f2bf(unalign28(acc[2], F[hh])) | ((uint32_t)f2bf(unalign28(acc[3], F[hh])) << 16);
-        *reinterpret_cast<uint2 *>(ctx + hh * 64 + 4 * d4) = pk;
+        transpose4(r, o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int d = 4 * d4 + j;
+            vt[(gg * 64 + d) * 16 + (t4 ^ (d & 15))] = o[j];
+        }
+    }
+    for (int i = tid; i < QB_QH * L4; i += D1_THREADS) {
+        const int hh = i / L4, t4 = i % L4;
+        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1S_SS;
+        uint32_t r[4], o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = 4 * t4 + j < L ? W[4 * t4 + j] : 0u;
+        transpose4(r, o);
+        wp[hh * 16 + t4] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    d1_sync();
+    for (int i = tid; i < QB_QH * 64; i += D1_THREADS) {
+        const int hh = i >> 6, d = i & 63, gg = hh / 7;
+        int acc[4] = {0, 0, 0, 0};
+        for (int t4 = 0; t4 < L4; ++t4) {
+            const uint32_t v = vt[(gg * 64 + d) * 16 + (t4 ^ (d & 15))];
+            const uint4 w = wp[hh * 16 + t4];
+            acc[0] = dp4a_su(v, w.x, acc[0]);
+            acc[1] = dp4a_su(v, w.y, acc[1]);
+            acc[2] = dp4a_su(v, w.z, acc[2]);
+            acc[3] = dp4a_su(v, w.w, acc[3]);
+        }
+        const long long dot = (long long)acc[0] + (long long)acc[1] * 256ll + (long long)acc[2] * 65536ll +
+                              (long long)acc[3] * 16777216ll;
+        ctx[hh * 64 + d] = f2bf(unalign28(dot, F[hh]));
     }
     d1_sync();
 }
