@@ -242,8 +242,9 @@ int allocate(qwen_b200 *h) {
     if (make_limb_map(&h->lmap_hid, h->limbs, h->R, FFN, h->limb_plane, HID) ||
         make_limb_map(&h->lmap_ffn, h->limbs, h->R, FFN, h->limb_plane, FFN))
         return fail(h, QWEN_B200_EDEVICE, "cannot encode the limb tensor maps");
-    // worst case over the layer GEMMs: 8 splits of the widest (gate/up) output
-    h->tc_ws_bytes = tc_gemm_workspace(h->R, 2 * FFN, 8);
+    // error word + split-K partial tiles: the split plan keeps tiles x splits
+    // within one CTA per SM whenever it splits
+    h->tc_ws_bytes = 256 + (size_t)148 * 64 * 128 * 8;
     if ((rc = dalloc(h, &h->tc_ws, h->tc_ws_bytes))) return rc;
     CK(cudaMemset(h->tc_ws, 0, h->tc_ws_bytes));
     if ((rc = dalloc(h, (void **)&h->logits, (size_t)VOC * 2))) return rc;
@@ -1077,9 +1078,12 @@ int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma,
 }
 
 // Workspace of the standalone tensor-core GEMM: 256-byte error word, the
-// activation rows' four int8 limb planes [4][rows][k], their exponents [rows].
+// split-K partial tiles of its split plan, the activation rows' four int8
+// limb planes [4][rows][k] and their exponents [rows].
 size_t qwen_b200_gemm_tc_workspace(uint32_t rows, uint32_t n, uint32_t k) {
-    return tc_gemm_workspace((int)rows, (int)n, 1) + 4 * (size_t)rows * k + 4 * (size_t)rows;
+    if (!rows || n % 128 || (k != HID && k != FFN)) return 256 + 4 * (size_t)rows * k + 4 * (size_t)rows;
+    return tc_gemm_workspace((int)rows, (int)n, tc_pick_splits((int)rows, (int)n, (int)k)) + 4 * (size_t)rows * k +
+           4 * (size_t)rows;
 }
 
 int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
@@ -1091,12 +1095,12 @@ int qwen_b200_op_gemm_w8a16_tc(const uint16_t *x, uint32_t rows, uint32_t k, con
     if (workspace_bytes < qwen_b200_gemm_tc_workspace(rows, n, k)) return QWEN_B200_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t plane = (size_t)rows * k;
-    int8_t *limbs = reinterpret_cast<int8_t *>(workspace) + 256;
+    const int splits = tc_pick_splits((int)rows, (int)n, (int)k);
+    int8_t *limbs = reinterpret_cast<int8_t *>(workspace) + tc_gemm_workspace((int)rows, (int)n, splits);
     int *ex = reinterpret_cast<int *>(limbs + 4 * plane);
     CUtensorMap wmap, lmap;
     if (make_weight_map(&wmap, w, (int)n, (int)k) || make_limb_map(&lmap, limbs, (int)rows, (int)k, plane, (int)k))
         return QWEN_B200_EINVAL;
-    const int splits = tc_pick_splits((int)rows, (int)n, (int)k);
     int rc = launch_act_quant(x, (int)rows, (int)k, limbs, plane, (int)k, ex, st);
     if (rc) return rc;
     return launch_gemm_tc(epi, wmap, lmap, ex, (int)rows, (int)k, scale, bias, (int)n, y, splits, workspace,

@@ -13,21 +13,30 @@
 // planes of 64 batch rows, 256 rows of 128 bytes (UMMA N = 256), so one
 // tcgen05.mma.kind::i8 (K = 32) covers all limbs; TMEM holds D[128][256]
 // int32 (column l*64 + m).
-//   warp 0     producer: the weight tile [128 n][128 k] (row-major int8, 2D
-//              tensor map) into a 4-deep ring before the programmatic-launch
-//              wait (weights are constant), the limb tile [4][64][128] (3D
-//              tensor map) into a 4-deep ring after it; 128-byte swizzle
+//   warp 0     producer: the weight tiles [128 n][128 k] (row-major int8, 2D
+//              tensor map) into a 7-deep ring, the CTA's first 7 k chunks
+//              (all of them for K = 896 and for the down projection's
+//              splits) issued before the programmatic-launch wait, so they
+//              load while the preceding kernel runs; the limb tiles
+//              [4][64][128] (3D tensor map, from L2) into a 3-deep ring after
+//              it; 128-byte swizzle
 //   warp 1     owns TMEM (256 columns), issues the MMAs (one thread)
-//   warps 2..9 epilogue: the limbs of a row fold into int64; the int64 tile
+//   warps 2..9 epilogue: the four limb column groups of 16 rows are read from
+//              TMEM together and fold into int64. Unsplit, the int64 tile
 //              [64 rows][128 channels] is staged in the CTA's shared memory
 //              (over the drained weight ring). Split-K CTAs of a tile form a
-//              thread-block cluster: after a cluster barrier each of the
-//              256 x splits epilogue threads takes 4-channel items, reads the
-//              item from every rank at once over distributed shared memory
-//              and adds the exact partials. The LM head (argmax) never splits.
-// No global scratch, no atomics, no TMA multicast. Every mbarrier wait is
-// bounded: on timeout the kernel records an error code in a device flag,
-// skips its remaining work and still frees its TMEM.
+//              thread-block cluster and write their partial tiles straight
+//              to an L2-resident workspace; after the cluster barrier each of
+//              the 256 x splits epilogue threads takes 4-channel items, reads
+//              the item's partials of every split at once and adds them
+//              exactly (pulling the partials over distributed shared memory
+//              instead measured ~4 us per tile). Per-channel scales and biases
+//              are staged in shared memory before the launch wait, every
+//              residual row a thread adds is requested before any is used.
+//              The LM head (argmax) never splits.
+// No atomics, no TMA multicast. Every mbarrier wait is bounded: on timeout
+// the kernel records an error code in a device flag, skips its remaining work
+// and still frees its TMEM.
 #include "common.cuh"
 #include "kernels.h"
 #include "tc05.cuh"
@@ -45,7 +54,7 @@ constexpr int TC_MAX_SPLITS = 8;
 constexpr int TC_SLOTS = 148;        // one CTA per SM
 
 struct TcSmem {
-    static constexpr int A_STAGES = 4, B_STAGES = 4;
+    static constexpr int A_STAGES = 7, B_STAGES = 3;  // every weight chunk of a 7-chunk split in flight before the launch wait
     static constexpr int A_BYTES = TC_BM * TC_BK;  // 16 KB weight tile
     static constexpr int B_BYTES = TC_MN * TC_BK;  // 32 KB limb tile
     static constexpr int A_OFF = 0;
@@ -57,7 +66,9 @@ struct TcSmem {
     static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8;
     static constexpr int RED_OFF = SLOT_OFF + 16;
     static constexpr int RED_BYTES = 4 * TC_BN * 8;
-    static constexpr int TOTAL = RED_OFF + RED_BYTES;
+    static constexpr int SC_OFF = RED_OFF + RED_BYTES;  // the tile's 128 scales, 128 biases (bf16), 64 row exponents
+    static constexpr int SC_BYTES = TC_BM * 4 + TC_BM * 2 + TC_BN * 4;
+    static constexpr int TOTAL = SC_OFF + SC_BYTES;
     static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment of the stages
     static constexpr uint32_t TMEM_COLS = TC_MN;
 };
@@ -81,14 +92,15 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
 }
-__device__ __forceinline__ void tmem_ld16i(uint32_t taddr, int (&v)[16]) {
+// 16 columns of this warp's TMEM lane quarter; tmem_ld_wait() completes them
+__device__ __forceinline__ void tmem_ld16i_nowait(uint32_t taddr, int (&v)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ float exact_acc(long long dot, int e) { return unalign28(dot, e); }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -147,31 +159,29 @@ __device__ __forceinline__ void tc_argmax_flush(const TcArgs &a, const uint8_t *
 // The exact partials of all `splits` CTAs of the cluster are read at once and
 // added, then the epilogue of model_backend.py:62-67 runs on the four channels.
 template <int EPI>
-__device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int n0, uint32_t tile_saddr,
-                                             const long long *tile) {
+__device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int n0, int tile_lin,
+                                             const long long *tile, const uint8_t *sc_smem, uint2 res) {
     const int m = i >> 5, nl = 4 * (i & 31), n = n0 + nl, mg = m0 + m;
     const bool valid = mg < a.M;
-    uint2 res = make_uint2(0u, 0u);
-    if (EPI == EPI_RESIDUAL && valid) res = *reinterpret_cast<const uint2 *>(a.y + (size_t)mg * a.N + n);
     long long t[4] = {0, 0, 0, 0};
     if (a.splits > 1) {
-        const uint32_t addr = tile_saddr + (uint32_t)(m * TC_BM + nl) * 8u;
-        float4 p[TC_MAX_SPLITS][2];
+        // the split CTAs' partials of these four channels, all requested at once
+        const longlong2 *pp = reinterpret_cast<const longlong2 *>(
+            a.part + (size_t)tile_lin * a.splits * (TC_BN * TC_BM) + m * TC_BM + nl);
+        longlong2 p[TC_MAX_SPLITS][2];
 #pragma unroll
         for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
             if (sr < a.splits) {
-                p[sr][0] = tc::ld_dsmem_f4(addr, (uint32_t)sr);
-                p[sr][1] = tc::ld_dsmem_f4(addr + 16u, (uint32_t)sr);
+                p[sr][0] = __ldcg(pp + (size_t)sr * (TC_BN * TC_BM / 2));
+                p[sr][1] = __ldcg(pp + (size_t)sr * (TC_BN * TC_BM / 2) + 1);
             }
 #pragma unroll
         for (int sr = 0; sr < TC_MAX_SPLITS; ++sr)
             if (sr < a.splits) {
-                const longlong2 u = *reinterpret_cast<const longlong2 *>(&p[sr][0]);
-                const longlong2 w = *reinterpret_cast<const longlong2 *>(&p[sr][1]);
-                t[0] += u.x;
-                t[1] += u.y;
-                t[2] += w.x;
-                t[3] += w.y;
+                t[0] += p[sr][0].x;
+                t[1] += p[sr][0].y;
+                t[2] += p[sr][1].x;
+                t[3] += p[sr][1].y;
             }
     } else {
         const longlong2 u = *reinterpret_cast<const longlong2 *>(tile + m * TC_BM + nl);
@@ -182,8 +192,8 @@ __device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int
         t[3] = w.y;
     }
     if (!valid) return;
-    const int e = a.ex[mg];
-    const float4 sc = *reinterpret_cast<const float4 *>(a.scale + n);
+    const int e = reinterpret_cast<const int *>(sc_smem + TC_BM * 6)[m];
+    const float4 sc = reinterpret_cast<const float4 *>(sc_smem)[nl >> 2];
     float o[4] = {rbf(rbf(exact_acc(t[0], e)) * sc.x), rbf(rbf(exact_acc(t[1], e)) * sc.y),
                   rbf(rbf(exact_acc(t[2], e)) * sc.z), rbf(rbf(exact_acc(t[3], e)) * sc.w)};
     if constexpr (EPI == EPI_SWIGLU) {
@@ -193,7 +203,7 @@ __device__ __forceinline__ void tc_epilogue4(const TcArgs &a, int i, int m0, int
         *reinterpret_cast<uint32_t *>(a.y + (size_t)mg * (a.N >> 1) + (n >> 1)) = w;
     } else {
         if constexpr (EPI == EPI_BIAS) {
-            const uint2 b = *reinterpret_cast<const uint2 *>(a.bias + n);
+            const uint2 b = *reinterpret_cast<const uint2 *>(sc_smem + TC_BM * 4 + nl * 2);
             o[0] = rbf(o[0] + bflo(b.x));
             o[1] = rbf(o[1] + bfhi(b.x));
             o[2] = rbf(o[2] + bflo(b.y));
@@ -321,37 +331,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         __syncwarp();
     } else {
-        pdl_wait();  // row exponents, residual rows and outputs of earlier kernels
         // this warp: TMEM lane quarter q (channels 32q..32q+31), rows 32h..32h+31
         const int q = warp & 3, h = (warp - 2) >> 2, ct = threadIdx.x - 64;
+        // per-channel scales and biases are constants: staged before the wait
+        float *scs = reinterpret_cast<float *>(smem + L::SC_OFF);
+        uint16_t *bss = reinterpret_cast<uint16_t *>(smem + L::SC_OFF + TC_BM * 4);
+        int *exs = reinterpret_cast<int *>(smem + L::SC_OFF + TC_BM * 6);
+        if (ct < TC_BM) {
+            scs[ct] = a.scale[n0 + ct];
+            if (EPI == EPI_BIAS) bss[ct] = a.bias[n0 + ct];
+        }
+        pdl_wait();  // row exponents, residual rows and outputs of earlier kernels
+        if (ct < TC_BN) exs[ct] = m0 + ct < a.M ? a.ex[m0 + ct] : 0;
         ok = ok && tc::mbar_wait(accum, 0, a.err, 6);
         tc::tc_fence_after();
         tc::fence_proxy_async_smem();  // the weight ring (async-proxy writes) becomes the generic int64 tile
         // the limbs of 16 rows at a time fold into int64 (keeps the fold in registers)
         float f[32];
         long long *tile = reinterpret_cast<long long *>(smem + L::A_OFF);
+        long long *pt = a.part + ((size_t)(m_tile * (a.N / TC_BM) + n_tile) * a.splits + split) * (TC_BN * TC_BM);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             long long v[16];
-            int d[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0;
+            int d[TC_NL][16];
+            // the four limb column groups in flight together, one wait
 #pragma unroll
             for (int l = 0; l < TC_NL; ++l) {
                 if (ok) {
-                    tmem_ld16i(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(l * TC_BN + 32 * h + 16 * hh), d);
+                    tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(l * TC_BN + 32 * h + 16 * hh), d[l]);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) d[j] = 0;
+                    for (int j = 0; j < 16; ++j) d[l][j] = 0;
                 }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] += (long long)d[j] << (7 * l);
             }
+            if (ok) tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                v[j] = (long long)d[0][j] + (long long)d[1][j] * 128ll + (long long)d[2][j] * 16384ll +
+                       (long long)d[3][j] * 2097152ll;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int r = 32 * h + 16 * hh + j;
                 if constexpr (EPI == EPI_ARGMAX)
                     f[16 * hh + j] = m0 + r < a.M ? exact_acc(v[j], a.ex[m0 + r]) : 0.f;
+                else if (a.splits > 1)
+                    pt[r * TC_BM + q * 32 + lane] = v[j];  // 256 contiguous bytes per warp and row
                 else
                     tile[r * TC_BM + q * 32 + lane] = v[j];
             }
@@ -363,18 +387,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     }
     if constexpr (EPI != EPI_ARGMAX) {
-        // every partial tile of the cluster is complete in shared memory
+        // every partial tile of the cluster is complete (in L2 when split,
+        // cluster release/acquire orders the global writes; else in this CTA)
         if (a.splits > 1)
             tc::cluster_sync();
         else
             __syncthreads();
         if (warp >= 2) {
             const long long *tile = reinterpret_cast<const long long *>(smem + L::A_OFF);
-            const uint32_t tsa = tc::smem_u32(tile);
-            for (int i = split * TC_CONV + (threadIdx.x - 64); i < TC_BN * (TC_BM / 4); i += a.splits * TC_CONV)
-                tc_epilogue4<EPI>(a, i, m0, n0, tsa, tile);
+            const int tile_lin = m_tile * (a.N / TC_BM) + n_tile;
+            const uint8_t *sc = smem + L::SC_OFF;
+            constexpr int ITEMS = TC_BN * (TC_BM / 4);  // 4-channel items of the tile
+            constexpr int MAXK = ITEMS / TC_CONV;       // items per thread when the tile is not split
+            const int i0 = split * TC_CONV + (threadIdx.x - 64), di = a.splits * TC_CONV;
+            // every residual row this thread adds is requested before any is used
+            uint2 res[MAXK];
+#pragma unroll
+            for (int k = 0; k < MAXK; ++k) {
+                const int i = i0 + k * di, mg = m0 + (i >> 5);
+                res[k] = make_uint2(0u, 0u);
+                if (EPI == EPI_RESIDUAL && i < ITEMS && mg < a.M)
+                    res[k] = *reinterpret_cast<const uint2 *>(a.y + (size_t)mg * a.N + n0 + 4 * (i & 31));
+            }
+#pragma unroll
+            for (int k = 0; k < MAXK; ++k) {
+                const int i = i0 + k * di;
+                if (i < ITEMS) tc_epilogue4<EPI>(a, i, m0, n0, tile_lin, tile, sc, res[k]);
+            }
         }
-        if (a.splits > 1) tc::cluster_sync();  // no CTA leaves while another may still read its tile
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -436,11 +476,12 @@ int make_limb_map(CUtensorMap *map, const int8_t *limbs, int rows_alloc, int ld,
 }
 
 // Workspace: the 4-byte error flag of the bounded waits (256 bytes reserved).
+// 256-byte error word, then (split K only) the partial tiles: the split CTAs
+// of a tile write their exact int64 partials to L2 and each reduces its own
+// share of the tile after the cluster barrier.
 size_t tc_gemm_workspace(int rows, int n, int splits) {
-    (void)rows;
-    (void)n;
-    (void)splits;
-    return 256;
+    const size_t tiles = (size_t)(n / TC_BM) * ((rows + TC_BN - 1) / TC_BN);
+    return 256 + (splits > 1 ? tiles * splits * (size_t)TC_BN * TC_BM * 8 : 0);
 }
 
 // Splits of K so that the tiles fill the GPU once (one CTA per SM), each
@@ -498,6 +539,7 @@ int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, co
     a.kc_per_split = kcps;
     a.splits = splits;
     a.err = reinterpret_cast<unsigned *>(ws);
+    a.part = reinterpret_cast<long long *>(reinterpret_cast<char *>(ws) + 256);
     a.pv = am ? am->pv : nullptr;
     a.pi = am ? am->pi : nullptr;
     a.nblk = am ? am->nblk : 0;

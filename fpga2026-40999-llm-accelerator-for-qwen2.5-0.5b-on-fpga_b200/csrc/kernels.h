@@ -124,6 +124,7 @@ struct TcArgs {
     const int *ex;  // row exponents of the activation limbs
     int M, N, K, kc_per_split, splits;
     unsigned *err;
+    long long *part;  // split-K partial tiles [tile][split][64 rows][128 channels] (splits > 1)
     float *pv;
     uint32_t *pi;
     int nblk;

@@ -119,11 +119,17 @@ def test_rope_table_matches_oracle():
 
 
 def test_tensor_core_gemm_workspace_and_argument_checks():
-    """Workspace = 256-byte error word + four int8 limb planes [4][rows][k] +
-    one exponent per row; malformed shapes are rejected before any launch."""
+    """Workspace = 256-byte error word + the split-K partial tiles of the
+    split plan (64 x 128 int64 per tile and split) + four int8 limb planes
+    [4][rows][k] + one exponent per row; malformed shapes are rejected before
+    any launch."""
     L = qwen_b200.lib()
-    assert L.qwen_b200_gemm_tc_workspace(64, 896, 896) == 256 + 4 * 64 * 896 + 4 * 64
-    assert L.qwen_b200_gemm_tc_workspace(9, 896, 4864) == 256 + 4 * 9 * 4864 + 4 * 9
+    tile = 64 * 128 * 8
+    # 7 channel tiles, K = 896 (7 chunks): 7 splits; K = 4864: 8 splits
+    assert L.qwen_b200_gemm_tc_workspace(64, 896, 896) == 256 + 7 * 7 * tile + 4 * 64 * 896 + 4 * 64
+    assert L.qwen_b200_gemm_tc_workspace(9, 896, 4864) == 256 + 7 * 8 * tile + 4 * 9 * 4864 + 4 * 9
+    # 76 gate/up tiles: one split, no partial tiles
+    assert L.qwen_b200_gemm_tc_workspace(64, 9728, 896) == 256 + 4 * 64 * 896 + 4 * 64
     p = ctypes.c_void_p(16)
     ws = L.qwen_b200_gemm_tc_workspace(16, 896, 896)
     ok = dict(x=p, rows=16, k=896, w=p, scale=p, n=896, bias=None, epi=0, y=p, ws=p, ws_bytes=ws, st=None)
