@@ -172,10 +172,12 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
     if (tid == 0)
         for (int i = 0; i < min(items, AM_SLOTS_RING); ++i) issue(i);
     float vmax = 0.f;  // largest V scale of this CTA's keys
+#pragma unroll 4
     for (int t = tid; t < nkeys; t += AM_THREADS) {
-        kss[t] = __ldg(a.ks + kvbase + t);
-        vss[t] = __ldg(a.vs + kvbase + t);
-        vmax = fmaxf(vmax, vss[t]);
+        const float kv = __ldg(a.ks + kvbase + t), vv = __ldg(a.vs + kvbase + t);
+        kss[t] = kv;
+        vss[t] = vv;
+        vmax = fmaxf(vmax, vv);
     }
     bool ok = true;
 
@@ -324,7 +326,7 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
         for (int t = tid; t < nkeys; t += AM_THREADS) {
             const float e = qexp(__fsub_rn(S[h * sld + t], M[h]));
             S[h * sld + t] = e;
-            z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
+            z += rint_2p40(e);
         }
         zl[h] = z;
     }

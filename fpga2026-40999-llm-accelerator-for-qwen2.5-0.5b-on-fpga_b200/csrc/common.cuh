@@ -148,7 +148,10 @@ __device__ __forceinline__ uint32_t limb_bytes(const int (&la)[4], const int (&l
 __device__ __forceinline__ float qexp(float x) {
     if (!(x >= -104.0f)) return 0.0f;
     if (x > 88.75f) return __int_as_float(0x7f800000);
-    const float n = rintf(__fmul_rn(x, 1.44269504f));
+    // rint by the 1.5 * 2^23 shift (exact round-to-nearest-even for |v| < 2^22,
+    // the same value as rintf here); the integer comes from the same sum's bits
+    const float sh = __fadd_rn(__fmul_rn(x, 1.44269504f), 12582912.0f);
+    const float n = __fsub_rn(sh, 12582912.0f);
     float r = __fmaf_rn(-n, 0.693145751953125f, x);
     r = __fmaf_rn(-n, 1.42860677e-6f, r);
     float p = 1.98412698e-4f;
@@ -159,8 +162,18 @@ __device__ __forceinline__ float qexp(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    const int ni = (int)n, n1 = min(max(ni, -126), 127);
+    const int ni = __float_as_int(sh) - 0x4B400000, n1 = min(max(ni, -126), 127);
     return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(ni - n1));
+}
+
+// rint(e * 2^40) for 0 <= e <= 1 (the exact softmax sum's grid) without a
+// conversion instruction: below 2^23 the 2^23 shift rounds to nearest even,
+// above it the product is already an integer read from its bits.
+__device__ __forceinline__ long long rint_2p40(float e) {
+    const float v = __fmul_rn(e, 0x1p40f);
+    if (v < 8388608.0f) return (long long)(__float_as_int(__fadd_rn(v, 8388608.0f)) - 0x4B000000);
+    const int b = __float_as_int(v);
+    return (long long)((b & 0x7FFFFF) | 0x800000) << ((b >> 23) - 150);
 }
 
 // SiLU(g) = g / (1 + exp(-g)) with qexp (model_backend.py:106)

@@ -654,7 +654,7 @@ __device__ void d1_attention(const D1Args &a, int layer, int g, uint32_t slot, u
         for (int t = tl; t < L; t += D1_THREADS / 8) {
             const float e = qexp(__fsub_rn(S[h * D1A_SS + t], M[h]));
             S[h * D1A_SS + t] = e;
-            z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
+            z += rint_2p40(e);
         }
     z += __shfl_xor_sync(0xffffffffu, z, 8);
     z += __shfl_xor_sync(0xffffffffu, z, 16);
@@ -875,7 +875,7 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         for (int t = tl; t < L; t += 16) {
             const float e = qexp(__fsub_rn(S[h * D1S_SS + t], M[h]));
             S[h * D1S_SS + t] = e;
-            z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
+            z += rint_2p40(e);
         }
     z += __shfl_xor_sync(0xffffffffu, z, 16);
     d1_sync();
