@@ -52,11 +52,11 @@ KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_cluster_ke
                      'embedding': 'embed_kernel', 'bookkeeping': 'decode_prologue/epilogue_kernel',
                      'persistent_decode': 'decode1_kernel'}
 KERNEL_NAMES_TC = dict(KERNEL_NAMES_GEMV,
-                       qkv_rope_kv8='rmsnorm_kernel + tc_gemm_kernel<EPI_BIAS> + rope_kv8_kernel',
-                       o_proj_residual='tc_gemm_kernel<EPI_RESIDUAL>',
-                       gate_up_swiglu='rmsnorm_kernel + tc_gemm_kernel<EPI_SWIGLU>',
-                       down_residual='tc_gemm_kernel<EPI_RESIDUAL>',
-                       lm_head_argmax='rmsnorm_kernel + tc_gemm_kernel<EPI_ARGMAX> + argmax_reduce_kernel')
+                       qkv_rope_kv8='rmsnorm_limbs_kernel + tc_gemm_kernel<EPI_BIAS> + rope_kv8_kernel',
+                       o_proj_residual='act_quant_kernel<896> + tc_gemm_kernel<EPI_RESIDUAL>',
+                       gate_up_swiglu='rmsnorm_limbs_kernel + tc_gemm_kernel<EPI_SWIGLU>',
+                       down_residual='act_quant_kernel<4864> + tc_gemm_kernel<EPI_RESIDUAL>',
+                       lm_head_argmax='rmsnorm_limbs_kernel + tc_gemm_kernel<EPI_ARGMAX> + argmax_reduce_kernel')
 
 
 def kernel_names(rows):

@@ -85,11 +85,79 @@ int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps
                       (int8_t *)nullptr, (size_t)0, 0, (int *)nullptr);
 }
 
+// RMSNorm + limb planes of one row per CTA of 256 threads (thread t < 224
+// owns values 4t..4t+3): the row maximum, the exact sum of squares and the
+// normalised maximum each meet in one CTA-wide reduction, instead of the
+// serial chain of a single warp. Same values as rmsnorm_kernel.
+constexpr int RL_THREADS = 256, RL_WARPS = RL_THREADS / 32;
+__global__ void __launch_bounds__(RL_THREADS) rmsnorm_limbs_kernel(const uint16_t *__restrict__ x,
+                                                                   const uint16_t *__restrict__ gamma, float eps,
+                                                                   uint16_t *__restrict__ out, int8_t *limbs,
+                                                                   size_t plane, int ld, int *ex) {
+    __shared__ float r0[RL_WARPS], r2[RL_WARPS];
+    __shared__ long long r1[RL_WARPS];
+    const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool act = tid < QB_HID / 4;
+    uint2 gv = make_uint2(0u, 0u);
+    if (act) gv = __ldg(reinterpret_cast<const uint2 *>(gamma) + tid);  // constant: before the wait
+    pdl_wait();
+    pdl_trigger();
+    uint2 xv = make_uint2(0u, 0u);
+    if (act) xv = reinterpret_cast<const uint2 *>(x + (size_t)row * QB_HID)[tid];
+    float v[4] = {bflo(xv.x), bfhi(xv.x), bflo(xv.y), bfhi(xv.y)};
+    float m = warp_max(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+    if (lane == 0) r0[warp] = m;
+    __syncthreads();
+    m = r0[0];
+#pragma unroll
+    for (int w = 1; w < RL_WARPS; ++w) m = fmaxf(m, r0[w]);
+    const int e0 = row_exponent(m);
+    long long s2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const long long q = __float2int_rn(align21(v[i], e0));
+        s2 += q * q;
+    }
+    s2 = warp_sum_ll(s2);
+    if (lane == 0) r1[warp] = s2;
+    __syncthreads();
+    s2 = r1[0];
+#pragma unroll
+    for (int w = 1; w < RL_WARPS; ++w) s2 += r1[w];
+    const float ss = ldexpf(__ll2float_rn(s2), 2 * e0 - 40);
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)QB_HID), eps)));
+    const float gg[4] = {bflo(gv.x), bfhi(gv.x), bflo(gv.y), bfhi(gv.y)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = rbf(rbf(v[i] * rs) * gg[i]);
+    if (out != nullptr && act)
+        reinterpret_cast<uint2 *>(out + (size_t)row * QB_HID)[tid] =
+            make_uint2((uint32_t)f2bf(v[0]) | ((uint32_t)f2bf(v[1]) << 16),
+                       (uint32_t)f2bf(v[2]) | ((uint32_t)f2bf(v[3]) << 16));
+    m = warp_max(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+    if (lane == 0) r2[warp] = m;
+    __syncthreads();
+    m = r2[0];
+#pragma unroll
+    for (int w = 1; w < RL_WARPS; ++w) m = fmaxf(m, r2[w]);
+    const int e = row_exponent(m);
+    if (act) {
+        int lv[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) limbs4(align28_int(v[i], e), lv[i]);
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+            *reinterpret_cast<uint32_t *>(limbs + l * plane + (size_t)row * ld + 4 * tid) =
+                ((uint32_t)lv[0][l] & 0xffu) | (((uint32_t)lv[1][l] & 0xffu) << 8) |
+                (((uint32_t)lv[2][l] & 0xffu) << 16) | ((uint32_t)lv[3][l] << 24);
+    }
+    if (tid == 0) ex[row] = e;
+}
+
 int launch_rmsnorm_limbs(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out,
                          int8_t *limbs, size_t plane, int ld, int *ex, cudaStream_t st) {
     if (rows <= 0 || !limbs || !ex || (ld & 15) || (plane & 15)) return -1;
-    return launch_pdl(rmsnorm_kernel, dim3((rows + 1) / 2), dim3(64), 0, st, 1, x, gamma, rows, eps, out, limbs,
-                      plane, ld, ex);
+    return launch_pdl(rmsnorm_limbs_kernel, dim3(rows), dim3(RL_THREADS), 0, st, 1, x, gamma, eps, out, limbs, plane,
+                      ld, ex);
 }
 
 // x [rows][K] (bf16) -> the four int8 limb planes of each row's 28-bit
