@@ -149,22 +149,26 @@ def test_small_capacity_engine_matches_oracle(sd_root, oracle_kv8, golden):
     assert g_toks == o_toks
 
 
-def test_chunked_prefill_matches_single_chunk(sd_root, golden):
-    """A 16-token prompt as chunks of 5 rows (GEMV path, rows <= 8) against one
-    chunk of 16 rows (tensor-core path): both paths form the same exact
-    integer sums, so the logits are bit-identical."""
-    e = qwen_b200.Engine(device=0, max_seqs=1, max_context=64, max_rows=5).load_assets(sd_root)
-    try:
-        tok, logits = e.forward(0, golden['prompt'], 0, want_logits=True)
-    finally:
-        e.close()
-    e2 = qwen_b200.Engine(device=0, max_seqs=1, max_context=64, max_rows=64).load_assets(sd_root)
-    try:
-        tok2, logits2 = e2.forward(0, golden['prompt'], 0, want_logits=True)
-    finally:
-        e2.close()
-    assert tok == tok2
-    assert np.array_equal(from_bits(logits), from_bits(logits2))
+@pytest.mark.parametrize('length,rows', [(16, 64), (70, 128)])
+def test_chunked_prefill_matches_single_chunk(sd_root, golden, length, rows):
+    """A prompt as chunks of 5 rows (GEMV path, rows <= 8; its q|k|v epilogue
+    is the per-head-block one) against one chunk (tensor-core path, whose
+    GEMM epilogue applies RoPE and writes q and the KV8 cache; 70 rows span
+    a full and a partial 64-row tile): both paths form the same exact integer
+    sums, so the logits and the next step's logits are bit-identical."""
+    prompt = (list(golden['prompt']) * 5)[:length]
+    out = []
+    for max_rows in (5, rows):
+        e = qwen_b200.Engine(device=0, max_seqs=1, max_context=128, max_rows=max_rows).load_assets(sd_root)
+        try:
+            tok, logits = e.forward(0, prompt, 0, want_logits=True)
+            tok2, logits2 = e.forward(0, [tok], length, want_logits=True)
+        finally:
+            e.close()
+        out.append((tok, tok2, from_bits(logits), from_bits(logits2)))
+    assert out[0][:2] == out[1][:2]
+    assert np.array_equal(out[0][2], out[1][2])
+    assert np.array_equal(out[0][3], out[1][3])
 
 
 def test_device_decode_graph_equals_host_decode(engine, golden):

@@ -245,6 +245,20 @@ def test_attention_cluster_long_context(length):
     check_attention(got, q, slots, positions, cache, True, f'attention L={length}')
 
 
+@pytest.mark.parametrize('cap', [1001, 1002])
+def test_attention_cluster_unaligned_capacity(cap):
+    """Capacities that are not a multiple of 4 put the per-key scale rows off
+    16-byte boundaries: the kernel stages them with plain loads instead of
+    bulk copies, with the same bits."""
+    r = rng(cap)
+    positions = np.array([cap - 1, 37, 512, 0], np.uint32)
+    slots = np.array([2, 0, 1, 3], np.uint32)
+    cache = random_cache(r, 4, cap)
+    q = rand_bf16(r, (4, 14, 64))
+    got = run_attention(q, slots, positions, cache, cap, cluster=True)
+    check_attention(got, q, slots, positions, cache, True, f'attention cap={cap}')
+
+
 def test_qkv_fused_against_oracle_chain():
     keep = Keep()
     r = rng(21)
