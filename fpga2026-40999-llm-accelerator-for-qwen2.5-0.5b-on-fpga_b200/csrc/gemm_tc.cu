@@ -33,7 +33,8 @@
 //              instead measured ~4 us per tile). Per-channel scales and biases
 //              are staged in shared memory before the launch wait, every
 //              residual row a thread adds is requested before any is used.
-//              The LM head (argmax) never splits.
+// The LM head (argmax epilogue) is tc_lmhead_kernel below: the same roles in a
+// persistent loop over tiles.
 // No atomics, no TMA multicast. Every mbarrier wait is bounded: on timeout
 // the kernel records an error code in a device flag, skips its remaining work
 // and still frees its TMEM.
@@ -64,9 +65,7 @@ struct TcSmem {
     static constexpr int BAR_OFF = B_OFF + B_STAGES * B_BYTES;
     static constexpr int NBARS = 2 * A_STAGES + 2 * B_STAGES + 2;
     static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8;
-    static constexpr int RED_OFF = SLOT_OFF + 16;
-    static constexpr int RED_BYTES = 4 * TC_BN * 8;
-    static constexpr int SC_OFF = RED_OFF + RED_BYTES;  // the tile's 128 scales, 128 biases (bf16), 64 row exponents
+    static constexpr int SC_OFF = SLOT_OFF + 16;  // the tile's 128 scales, 128 biases (bf16), 64 row exponents
     static constexpr int SC_BYTES = TC_BM * 4 + TC_BM * 2 + TC_BN * 4;
     static constexpr int TOTAL = SC_OFF + SC_BYTES;
     static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment of the stages
@@ -103,18 +102,18 @@ __device__ __forceinline__ void tmem_ld16i_nowait(uint32_t taddr, int (&v)[16]) 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ float exact_acc(long long dot, int e) { return unalign28(dot, e); }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// LM head: 32 accumulators of output channel n (rows m0 + c0 + j), logits
+// LM head: NR accumulators of output channel n (rows m0 + c0 + j), logits
 // bf16(bf16(acc) * scale) (model_backend.py:109), best (value, index) per
 // row over this warp's 32 channels into red (highest index on ties).
-__device__ __forceinline__ void tc_argmax32(const TcArgs &a, const float (&v)[32], int n, int m0, int c0, int q,
-                                            int lane, uint8_t *red) {
+template <int NR>
+__device__ __forceinline__ void tc_argmax_rows(const TcArgs &a, const float (&v)[NR], int n, int m0, int c0, int q,
+                                               int lane, uint8_t *red) {
     const float sc = a.scale[n];
     float *red_v = reinterpret_cast<float *>(red);
     uint32_t *red_i = reinterpret_cast<uint32_t *>(red + 4 * TC_BN * 4);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < NR; ++j) {
         const int cj = c0 + j, m = m0 + cj;
         const bool valid = m < a.M;
         const float val = rbf(rbf(v[j]) * sc);
@@ -347,7 +346,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc::tc_fence_after();
         tc::fence_proxy_async_smem();  // the weight ring (async-proxy writes) becomes the generic int64 tile
         // the limbs of 16 rows at a time fold into int64 (keeps the fold in registers)
-        float f[32];
         long long *tile = reinterpret_cast<long long *>(smem + L::A_OFF);
         long long *pt = a.part + ((size_t)(m_tile * (a.N / TC_BM) + n_tile) * a.splits + split) * (TC_BN * TC_BM);
 #pragma unroll
@@ -372,21 +370,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int r = 32 * h + 16 * hh + j;
-                if constexpr (EPI == EPI_ARGMAX)
-                    f[16 * hh + j] = m0 + r < a.M ? exact_acc(v[j], a.ex[m0 + r]) : 0.f;
-                else if (a.splits > 1)
+                if (a.splits > 1)
                     pt[r * TC_BM + q * 32 + lane] = v[j];  // 256 contiguous bytes per warp and row
                 else
                     tile[r * TC_BM + q * 32 + lane] = v[j];
             }
         }
-        if constexpr (EPI == EPI_ARGMAX) {
-            tc_argmax32(a, f, n0 + q * 32 + lane, m0, 32 * h, q, lane, smem + L::RED_OFF);
-            epi_bar();
-            tc_argmax_flush(a, smem + L::RED_OFF, m0, n_tile, ct);
-        }
     }
-    if constexpr (EPI != EPI_ARGMAX) {
+    {
         // every partial tile of the cluster is complete (in L2 when split,
         // cluster release/acquire orders the global writes; else in this CTA)
         if (a.splits > 1)
@@ -414,6 +405,229 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int i = i0 + k * di;
                 if (i < ITEMS) tc_epilogue4<EPI>(a, i, m0, n0, tile_lin, tile, sc, res[k]);
             }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, L::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------- LM head (argmax)
+// The vocabulary projection as a persistent kernel: one CTA per SM walks the
+// (row tile, 128-channel tile) list with a stride of the grid, so weight and
+// limb tiles stream without a gap between tiles. The accumulator is double
+// buffered in TMEM (2 x 256 columns): the MMA warp fills one buffer while the
+// epilogue warps fold, scale and reduce the other to per-row (value, index)
+// candidates. Same roles and arithmetic as tc_gemm_kernel.
+struct LhSmem {
+    static constexpr int A_STAGES = 4, B_STAGES = 4;
+    static constexpr int A_BYTES = TC_BM * TC_BK;
+    static constexpr int B_BYTES = TC_MN * TC_BK;
+    static constexpr int A_OFF = 0;
+    static constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
+    static constexpr int BAR_OFF = B_OFF + B_STAGES * B_BYTES;
+    static constexpr int NBARS = 2 * A_STAGES + 2 * B_STAGES + 4 + 1;
+    static constexpr int SLOT_OFF = BAR_OFF + ((NBARS * 8 + 15) / 16) * 16;
+    static constexpr int RED_OFF = SLOT_OFF + 16;
+    static constexpr int RED_BYTES = 4 * TC_BN * 8;  // per buffer: best value and index per (quarter, row)
+    static constexpr int TOTAL = RED_OFF + 2 * RED_BYTES;
+    static constexpr int ALLOC = TOTAL + 1024;
+    static constexpr uint32_t TMEM_COLS = 2 * TC_MN;
+    static_assert(ALLOC <= 227 * 1024, "shared memory of one CTA");
+};
+
+// Barrier 1 over the 256 epilogue threads, returning the AND of v over them
+// (every epilogue thread leaves a tile loop at the same iteration).
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_lmhead_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap lmap, TcArgs a) {
+    using L = LhSmem;
+    constexpr int AS = L::A_STAGES, BS = L::B_STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+    uint64_t *full_a = bars, *empty_a = full_a + AS, *full_b = empty_a + AS, *empty_b = full_b + BS;
+    uint64_t *acc_full = empty_b + BS, *acc_empty = acc_full + 2, *done = acc_empty + 2;
+    uint32_t *slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntn = a.N / TC_BM;                               // channel tiles
+    const int total = ntn * ((a.M + TC_BN - 1) / TC_BN);       // (row tile, channel tile) pairs
+    const int G = (int)gridDim.x;
+    const int nt = total > (int)blockIdx.x ? (total - (int)blockIdx.x + G - 1) / G : 0;  // this CTA's tiles
+    const int KC = a.K / TC_BK;
+    const int nchunks = nt * KC;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < AS; ++s) {
+            tc::mbar_init(&full_a[s], 1);
+            tc::mbar_init(&empty_a[s], 1);
+        }
+        for (int s = 0; s < BS; ++s) {
+            tc::mbar_init(&full_b[s], 1);
+            tc::mbar_init(&empty_b[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&acc_full[b], 1);
+            tc::mbar_init(&acc_empty[b], TC_CONV / 32);  // one arrival per epilogue warp
+        }
+        tc::mbar_init(done, 1);
+        tc::mbar_fence_init();
+        tc::tma_prefetch_desc(&wmap);
+        tc::tma_prefetch_desc(&lmap);
+    }
+    if (warp == 1) tc::tmem_alloc(slot, L::TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *slot;
+    pdl_trigger();
+    bool ok = nt > 0;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            auto tile_of = [&](int g, int &n0, int &m0) {
+                const int t = (int)blockIdx.x + (g / KC) * G;
+                n0 = (t % ntn) * TC_BM;
+                m0 = (t / ntn) * TC_BN;
+            };
+            auto issue_a = [&](int g) {
+                int n0, m0;
+                tile_of(g, n0, m0);
+                const int s = g % AS;
+                tc::mbar_arrive_expect_tx(&full_a[s], (uint32_t)L::A_BYTES);
+                tc::tma_load_2d(smem + L::A_OFF + s * L::A_BYTES, &wmap, &full_a[s], (g % KC) * TC_BK, n0);
+            };
+            int ia = 0, ib = 0;
+            // weights are constant: the first stages load before the wait for
+            // the kernel that writes the limb planes
+            for (; ok && ia < min(nchunks, AS); ++ia) issue_a(ia);
+            pdl_wait();
+            uint32_t idle = 0;
+            while (ok && (ib < nchunks || ia < nchunks)) {
+                bool progress = false;
+                if (ib < nchunks) {
+                    const int s = ib % BS, ph = (ib / BS) & 1;
+                    if (tc::mbar_try_wait(&empty_b[s], ph ^ 1)) {
+                        int n0, m0;
+                        tile_of(ib, n0, m0);
+                        tc::mbar_arrive_expect_tx(&full_b[s], (uint32_t)L::B_BYTES);
+                        tma_load_3d(smem + L::B_OFF + s * L::B_BYTES, &lmap, &full_b[s], (ib % KC) * TC_BK, m0, 0);
+                        ++ib;
+                        progress = true;
+                    }
+                }
+                if (ia < nchunks) {
+                    const int s = ia % AS, ph = (ia / AS) & 1;
+                    if (tc::mbar_try_wait(&empty_a[s], ph ^ 1)) {
+                        issue_a(ia);
+                        ++ia;
+                        progress = true;
+                    }
+                }
+                if (progress) {
+                    idle = 0;
+                } else if (++idle > (1u << 22)) {
+                    atomicExch(a.err, 21u);
+                    ok = false;
+                }
+            }
+        } else {
+            pdl_wait();
+        }
+    } else if (warp == 1) {
+        pdl_wait();
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_s8_s32(TC_BM, TC_MN);
+            for (int j = 0; ok && j < nt; ++j) {
+                const int buf = j & 1;
+                // the epilogue has read this buffer's previous tile
+                if (j >= 2 && !tc::mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1, a.err, 22)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * TC_MN);
+                for (int kc = 0; kc < KC; ++kc) {
+                    const int g = j * KC + kc;
+                    const int sa = g % AS, sb = g % BS;
+                    if (!tc::mbar_wait(&full_a[sa], (g / AS) & 1, a.err, 23) ||
+                        !tc::mbar_wait(&full_b[sb], (g / BS) & 1, a.err, 24)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t ab = tc::smem_u32(smem + L::A_OFF + sa * L::A_BYTES);
+                    const uint32_t bb = tc::smem_u32(smem + L::B_OFF + sb * L::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 32; ++k)
+                        mma_s8(d, tc::smem_desc_sw128(ab + 32 * k), tc::smem_desc_sw128(bb + 32 * k), idesc,
+                               kc > 0 || k > 0);
+                    tc::mma_commit(&empty_a[sa]);
+                    tc::mma_commit(&empty_b[sb]);
+                }
+                if (ok) tc::mma_commit(&acc_full[buf]);
+            }
+            // every MMA issued by this thread has finished before TMEM is freed
+            tc::mma_commit(done);
+            tc::mbar_wait(done, 0, a.err, 25);
+        }
+        __syncwarp();
+    } else {
+        // lane quarter q (channels 32q..32q+31 of a tile), rows 32h..32h+31
+        const int q = warp & 3, h = (warp - 2) >> 2, ct = threadIdx.x - 64;
+        pdl_wait();  // row exponents come from the preceding kernel
+        for (int j = 0; j < nt; ++j) {
+            const int buf = j & 1;
+            const int t = (int)blockIdx.x + j * G;
+            const int n_tile = t % ntn, n0 = n_tile * TC_BM, m0 = (t / ntn) * TC_BN;
+            ok = ok && tc::mbar_wait(&acc_full[buf], (j >> 1) & 1, a.err, 26);
+            tc::tc_fence_after();
+            uint8_t *red = smem + L::RED_OFF + buf * L::RED_BYTES;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                float f[16];
+                int d[TC_NL][16];
+#pragma unroll
+                for (int l = 0; l < TC_NL; ++l) {
+                    if (ok) {
+                        tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) +
+                                              (uint32_t)(buf * TC_MN + l * TC_BN + 32 * h + 16 * hh),
+                                          d[l]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) d[l][jj] = 0;
+                    }
+                }
+                if (ok) tmem_ld_wait();
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) {
+                    const long long v = (long long)d[0][jj] + (long long)d[1][jj] * 128ll +
+                                        (long long)d[2][jj] * 16384ll + (long long)d[3][jj] * 2097152ll;
+                    const int r = 32 * h + 16 * hh + jj;
+                    f[jj] = m0 + r < a.M ? exact_acc(v, a.ex[m0 + r]) : 0.f;
+                }
+                if (hh == 1) {
+                    // this warp's TMEM reads are complete: the buffer may be refilled
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
+                }
+                tc_argmax_rows<16>(a, f, n0 + q * 32 + lane, m0, 32 * h + 16 * hh, q, lane, red);
+            }
+            if (!epi_bar_and(ok)) break;
+            tc_argmax_flush(a, red, m0, n_tile, ct);
         }
     }
     tc::tc_fence_before();
@@ -514,6 +728,24 @@ static int run_tc(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs &a, i
                       dim3(TC_THREADS), (size_t)L::ALLOC, st, (unsigned)splits, wmap, lmap, a);
 }
 
+// The persistent LM head: one CTA per SM at most, each walking its share of
+// the tile list.
+static int run_lmhead(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs &a, cudaStream_t st) {
+    using L = LhSmem;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << (dev & 31)))) {
+        if (cudaFuncSetAttribute(tc_lmhead_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+            cudaSuccess)
+            return -3;
+        configured |= 1u << (dev & 31);
+    }
+    const int tiles = (a.N / TC_BM) * ((a.M + TC_BN - 1) / TC_BN);
+    return launch_pdl(tc_lmhead_kernel, dim3(tiles < TC_SLOTS ? tiles : TC_SLOTS), dim3(TC_THREADS), (size_t)L::ALLOC,
+                      st, 1u, wmap, lmap, a);
+}
+
 int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, const int *ex, int rows, int k,
                    const float *scale, const uint16_t *bias, int n, uint16_t *y, int splits, void *ws,
                    size_t ws_bytes, bool clear, const TcArgmax *am, cudaStream_t st) {
@@ -553,7 +785,7 @@ int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, co
         case EPI_BIAS: return run_tc<EPI_BIAS>(wmap, lmap, a, splits, st);
         case EPI_RESIDUAL: return run_tc<EPI_RESIDUAL>(wmap, lmap, a, splits, st);
         case EPI_SWIGLU: return run_tc<EPI_SWIGLU>(wmap, lmap, a, splits, st);
-        case EPI_ARGMAX: return run_tc<EPI_ARGMAX>(wmap, lmap, a, splits, st);
+        case EPI_ARGMAX: return run_lmhead(wmap, lmap, a, st);
     }
     return -1;
 }

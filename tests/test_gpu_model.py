@@ -137,6 +137,29 @@ def test_batched_decode_equals_single_sequences(engine, golden):
     assert batched == singles
 
 
+def test_batched_decode_tensor_core_lm_head(sd_root, golden):
+    """Twelve sequences decode together, so the vocabulary projection and its
+    argmax run on the tensor-core path (9 or more rows) while each sequence
+    alone takes the single-row path: the tokens must be identical."""
+    p = list(golden['prompt'])
+    prompts = [p[i:] + p[:i] for i in range(12)]
+    e = qwen_b200.Engine(device=0, max_seqs=12, max_context=64, max_rows=64).load_assets(sd_root)
+    try:
+        singles = [generate_gpu(e, q, 4, slot=0)[0] for q in prompts]
+        firsts = []
+        for s, q in enumerate(prompts):
+            e.reset(s)
+            firsts.append(e.forward(s, q, 0)[0])
+        toks = np.array(firsts, np.uint32)
+        out = [toks.tolist()]
+        for _ in range(3):
+            toks = e.decode_step(list(range(12)), toks)
+            out.append(toks.tolist())
+    finally:
+        e.close()
+    assert [[step[i] for step in out] for i in range(12)] == singles
+
+
 def test_small_capacity_engine_matches_oracle(sd_root, oracle_kv8, golden):
     """Capacity below one 128-key attention chunk, as in the reference's
     256-token firmware cap and the smoke check (capacity 64)."""
