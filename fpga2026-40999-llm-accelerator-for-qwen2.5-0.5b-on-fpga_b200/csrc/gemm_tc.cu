@@ -105,34 +105,65 @@ __device__ __forceinline__ float exact_acc(long long dot, int e) { return unalig
 
 // LM head: NR accumulators of output channel n (rows m0 + c0 + j), logits
 // bf16(bf16(acc) * scale) (model_backend.py:109), best (value, index) per
-// row over this warp's 32 channels into red (highest index on ties).
+// row over this warp's 32 channels into red (highest index on ties). The
+// cross-lane reduction is a butterfly that halves the rows at each level
+// (lanes exchange the half they do not keep), so a warp does NR - 1 + the
+// remaining levels' exchanges instead of 5 per row; (value, index) order is
+// a total order, so the result does not depend on the reduction order.
 template <int NR>
 __device__ __forceinline__ void tc_argmax_rows(const TcArgs &a, const float (&v)[NR], int n, int m0, int c0, int q,
                                                int lane, uint8_t *red) {
+    static_assert(NR == 16 || NR == 32, "rows per call");
     const float sc = a.scale[n];
     float *red_v = reinterpret_cast<float *>(red);
     uint32_t *red_i = reinterpret_cast<uint32_t *>(red + 4 * TC_BN * 4);
+    float bv[NR];
+    uint32_t bi[NR];
 #pragma unroll
     for (int j = 0; j < NR; ++j) {
-        const int cj = c0 + j, m = m0 + cj;
+        const int m = m0 + c0 + j;
         const bool valid = m < a.M;
         const float val = rbf(rbf(v[j]) * sc);
         if (valid && a.logits) a.logits[(size_t)m * a.N + n] = f2bf(val);
-        float bv = valid ? val : -INFINITY;
-        uint32_t bi = (uint32_t)n;
+        bv[j] = valid ? val : -INFINITY;
+        bi[j] = (uint32_t)n;
+    }
+    int row = 0;  // first row (of the NR) this lane holds after the halvings
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
+    for (int lv = 0; lv < 5; ++lv) {
+        const int o = 16 >> lv, cnt = NR >> lv;
+        if (cnt > 1) {
+            const int half = cnt >> 1;
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int k = 0; k < half; ++k) {
+                const float sv = up ? bv[k] : bv[k + half];
+                const uint32_t si = up ? bi[k] : bi[k + half];
+                float kv = up ? bv[k + half] : bv[k];
+                uint32_t ki = up ? bi[k + half] : bi[k];
+                const float rv = __shfl_xor_sync(0xffffffffu, sv, o);
+                const uint32_t ri = __shfl_xor_sync(0xffffffffu, si, o);
+                if (better(rv, ri, kv, ki)) {
+                    kv = rv;
+                    ki = ri;
+                }
+                bv[k] = kv;
+                bi[k] = ki;
+            }
+            if (up) row += half;
+        } else {
+            const float rv = __shfl_xor_sync(0xffffffffu, bv[0], o);
+            const uint32_t ri = __shfl_xor_sync(0xffffffffu, bi[0], o);
+            if (better(rv, ri, bv[0], bi[0])) {
+                bv[0] = rv;
+                bi[0] = ri;
             }
         }
-        if (lane == 0) {
-            red_v[q * TC_BN + cj] = bv;
-            red_i[q * TC_BN + cj] = bi;
-        }
+    }
+    // NR = 32: lane l holds row l; NR = 16: lanes 2r and 2r + 1 both hold row r
+    if (NR == 32 || (lane & 1) == 0) {
+        red_v[q * TC_BN + c0 + row] = bv[0];
+        red_i[q * TC_BN + c0 + row] = bi[0];
     }
 }
 
