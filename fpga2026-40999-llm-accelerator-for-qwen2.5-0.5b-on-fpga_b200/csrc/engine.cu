@@ -83,10 +83,13 @@ struct qwen_b200 {
     void *lm_ws = nullptr;
     size_t lm_ws_bytes = 0;
     // pinned staging
-    uint32_t *h_meta = nullptr, *h_tokens = nullptr, *h_slot_pos = nullptr;
+    uint32_t *h_meta = nullptr, *h_tokens = nullptr, *h_slot_pos = nullptr, *h_flag = nullptr;
     std::vector<uint32_t> pos;  // host mirror of every slot's position
     // decode graphs keyed by (n, context chunks, tokens_in, tokens_out)
     std::map<std::tuple<uint32_t, uint32_t, const void *, const void *>, cudaGraphExec_t> graphs;
+    // host-buffer decode steps: the forward over the staged ids / slots /
+    // positions, keyed by (n, context chunks), with its launch count
+    std::map<std::pair<uint32_t, uint32_t>, std::pair<cudaGraphExec_t, uint32_t>> host_graphs;
     // layer dump (tests): device buffers and host destinations
     int dump_layer = -1;
     uint16_t *dump_host[7] = {};
@@ -261,6 +264,7 @@ int allocate(qwen_b200 *h) {
     CK(cudaMallocHost((void **)&h->h_meta, R * 4 * 4));
     CK(cudaMallocHost((void **)&h->h_tokens, R * 4));
     CK(cudaMallocHost((void **)&h->h_slot_pos, (size_t)c.max_seqs * 4));
+    CK(cudaMallocHost((void **)&h->h_flag, 16));
     h->pos.assign(c.max_seqs, 0);
     std::vector<float> table((size_t)c.max_context * 64);
     qwen_b200_rope_table(c.max_context, table.data());
@@ -605,6 +609,7 @@ int qwen_b200_close(qwen_b200 *h) {
         cudaSetDevice(h->cfg.device);
         cudaDeviceSynchronize();
         for (auto &kv : h->graphs) cudaGraphExecDestroy(kv.second);
+        for (auto &kv : h->host_graphs) cudaGraphExecDestroy(kv.second.first);
         for (auto &pool : h->prof_ev)
             for (cudaEvent_t e : pool) cudaEventDestroy(e);
         for (void *p : h->dev_allocs) cudaFree(p);
@@ -612,6 +617,7 @@ int qwen_b200_close(qwen_b200 *h) {
         cudaFreeHost(h->h_meta);
         cudaFreeHost(h->h_tokens);
         cudaFreeHost(h->h_slot_pos);
+        cudaFreeHost(h->h_flag);
         if (h->csr_event) cudaEventDestroy(h->csr_event);
         if (h->staged) cudaEventDestroy(h->staged);
         if (h->stream) cudaStreamDestroy(h->stream);
@@ -688,7 +694,17 @@ void qwen_b200_rope_table(uint32_t positions, float *table) {
 
 int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable) {
     if (!h) return QWEN_B200_EINVAL;
-    h->persistent = enable != 0;
+    const bool p = enable != 0;
+    if (p != h->persistent && h->loaded) {
+        // captured steps have the previous choice built in
+        cudaSetDevice(h->cfg.device);
+        cudaDeviceSynchronize();
+        for (auto &kv : h->graphs) cudaGraphExecDestroy(kv.second);
+        for (auto &kv : h->host_graphs) cudaGraphExecDestroy(kv.second.first);
+        h->graphs.clear();
+        h->host_graphs.clear();
+    }
+    h->persistent = p;
     return QWEN_B200_OK;
 }
 
@@ -774,11 +790,43 @@ int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *t
         h->h_meta[2 * n + i] = h->pos[slots[i]];
     }
     CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)3 * n * 4, cudaMemcpyHostToDevice, st));
-    h->nlaunch = 0;
-    if ((rc = run_forward(h, (int)n, (int)max_len, (int)n, true, false, h->tokens, st))) return rc;
+    // steps of one batch size and 128-key context bucket replay one graph of
+    // the forward (it reads the staged ids / slots / positions on the device);
+    // the first such step runs the launches directly and captures them (a
+    // profiled step always runs them directly, between its events)
+    const uint32_t chunks = (max_len + 127) / 128;
+    const int bucket_len = (int)std::min<uint32_t>(chunks * 128, h->cfg.max_context);
+    const auto key = std::make_pair(n, chunks);
+    auto it = h->prof ? h->host_graphs.end() : h->host_graphs.find(key);
+    if (it != h->host_graphs.end()) {
+        CK(cudaGraphLaunch(it->second.first, st));
+        h->nlaunch = it->second.second;
+    } else if (h->prof) {
+        h->nlaunch = 0;
+        if ((rc = run_forward(h, (int)n, bucket_len, (int)n, true, false, h->tokens, st))) return rc;
+    } else {
+        h->nlaunch = 0;
+        if ((rc = run_forward(h, (int)n, bucket_len, (int)n, true, false, h->tokens, st))) return rc;
+        cudaGraph_t graph;
+        CK(cudaStreamBeginCapture(h->cap_stream, cudaStreamCaptureModeThreadLocal));
+        h->nlaunch = 0;
+        rc = run_forward(h, (int)n, bucket_len, (int)n, true, false, h->tokens, h->cap_stream);
+        cudaError_t e = cudaStreamEndCapture(h->cap_stream, &graph);
+        if (rc) return rc;
+        if (e != cudaSuccess) return fail(h, QWEN_B200_EDEVICE, "graph capture: %s", cudaGetErrorString(e));
+        cudaGraphExec_t exec;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail(h, QWEN_B200_EDEVICE, "graph instantiate: %s", cudaGetErrorString(e));
+        h->host_graphs[key] = std::make_pair(exec, h->nlaunch);
+    }
     CK(cudaMemcpyAsync(h->h_tokens, h->tokens, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(h->h_flag, h->tc_ws, 4, cudaMemcpyDeviceToHost, st));  // bounded-wait error flag
     CK(cudaStreamSynchronize(st));
-    if ((rc = check_device_flags(h))) return rc;
+    if (*h->h_flag) {
+        cudaMemset(h->tc_ws, 0, 4);
+        return fail(h, QWEN_B200_ETIMEOUT, "a pipeline wait on the device timed out (code %u)", *h->h_flag);
+    }
     for (uint32_t i = 0; i < n; ++i) {
         h->pos[slots[i]] += 1;
         tokens_out[i] = h->h_tokens[i];

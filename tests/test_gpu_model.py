@@ -220,6 +220,34 @@ def test_device_decode_graph_equals_host_decode(engine, golden):
     assert engine.position(0) == len(prompts[0]) + 4
 
 
+def test_host_decode_graph_replay_across_context_buckets(sd_root, golden):
+    """Host-buffer decode steps replay one captured graph per (batch size,
+    128-key context bucket). Ten sequences (tensor-core path) with synthetic
+    caches of 124-126 keys step across the 128-key boundary, so the step
+    switches graphs mid-run; each sequence alone (single-row path) must give
+    the same tokens."""
+    e = qwen_b200.Engine(device=0, max_seqs=10, max_context=300, max_rows=64).load_assets(sd_root)
+    try:
+        start = [int(golden['prompt'][i % len(golden['prompt'])]) for i in range(10)]
+        for s in range(10):
+            e.reset(s)
+            e.fill_kv_synthetic(s, 124 + s % 3, 7 + s)
+        toks, out = np.array(start, np.uint32), []
+        for _ in range(8):
+            toks = e.decode_step(list(range(10)), toks)
+            out.append(toks.tolist())
+        for s in range(10):
+            e.reset(s)
+            e.fill_kv_synthetic(s, 124 + s % 3, 7 + s)
+            tok, seq = start[s], []
+            for i in range(8):
+                tok, _ = e.forward(s, [tok], 124 + s % 3 + i)
+                seq.append(tok)
+            assert seq == [o[s] for o in out], s
+    finally:
+        e.close()
+
+
 def test_csr_protocol_drives_generation(engine, golden):
     L = qwen_b200.lib()
     expect, _ = generate_gpu(engine, golden['prompt'], 5)
