@@ -14,10 +14,10 @@
 // tcgen05.mma.kind::i8 (K = 32) covers all limbs; TMEM holds D[128][256]
 // int32 (column l*64 + m).
 //   warp 0     producer: the weight tiles [128 n][128 k] (row-major int8, 2D
-//              tensor map) into a 7-deep ring, the CTA's first 7 k chunks
-//              (all of them for K = 896 and for the down projection's
-//              splits) issued before the programmatic-launch wait, so they
-//              load while the preceding kernel runs; the limb tiles
+//              tensor map) into a 4-deep ring, the CTA's first 4 k chunks
+//              (all of them for the split projections) issued before the
+//              programmatic-launch wait, so they load while the preceding
+//              kernel runs; the limb tiles
 //              [4][64][128] (3D tensor map, from L2) into a 3-deep ring after
 //              it; 128-byte swizzle
 //   warp 1     owns TMEM (256 columns), issues the MMAs (one thread)
@@ -55,7 +55,10 @@ constexpr int TC_MAX_SPLITS = 8;
 constexpr int TC_SLOTS = 148;        // one CTA per SM
 
 struct TcSmem {
-    static constexpr int A_STAGES = 7, B_STAGES = 3;  // every weight chunk of a 7-chunk split in flight before the launch wait
+    // 4 + 3 stages: measured against 7 + 3, 6 + 3, 5 + 3 and 6 + 2 (bs64 decode
+    // 1.748 ms per step against 1.767, 1.752, 1.749 and 1.766); the smaller
+    // footprint lets more of the neighbouring kernels overlap
+    static constexpr int A_STAGES = 4, B_STAGES = 3;
     static constexpr int A_BYTES = TC_BM * TC_BK;  // 16 KB weight tile
     static constexpr int B_BYTES = TC_MN * TC_BK;  // 32 KB limb tile
     static constexpr int A_OFF = 0;
