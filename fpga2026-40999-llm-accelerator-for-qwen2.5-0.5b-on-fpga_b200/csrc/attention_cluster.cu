@@ -23,7 +23,7 @@
 //            with byte permutes into the A fragment; a warp covers all 64
 //            dims of its 16 keys, accumulating int32 per byte plane
 // so the context is bit-identical to the oracle's whatever the split.
-// K and then V stream through one 8-slot shared-memory ring in 128-key chunks
+// K and then V stream through one 4-slot shared-memory ring in 128-key chunks
 // (8 KB of codes) by bulk copy, completing on mbarriers (bounded waits); the
 // per-key scales are staged in shared memory once.
 //   phase 1  scores of this CTA's keys -> shared memory, per-head CTA max and
@@ -44,7 +44,7 @@ constexpr int AM_THREADS = 256;
 constexpr int AM_WARPS = AM_THREADS / 32;
 constexpr int AM_CHUNK = 16 * AM_WARPS;  // keys per ring stage: a 16-key block per warp
 constexpr int AM_STAGE_BYTES = AM_CHUNK * QB_HD;
-constexpr int AM_SLOTS_RING = 8;  // ring slots (K chunks, then V chunks)
+constexpr int AM_SLOTS_RING = 4;  // ring slots (K chunks, then V chunks)
 constexpr int AM_MAX_SPLITS = 8;
 constexpr int AM_MAX_KPC = 4096;  // keys per CTA (shared-memory score budget)
 constexpr int AM_SLOTS = 2 * 148;  // resident CTAs the split plan aims at (2 per SM)
@@ -64,8 +64,8 @@ struct AcSmem {
     int ring, s, sld, kss, vss, stat, red, bars, total;
 };
 
-// ring [8][128][64] int8 | S [7][kpc + 4] fp32 | K scales [kpc] | V scales
-// [kpc] | stat | per-warp reductions | mbarriers [8]. stat: max[8] (head 7:
+// ring [4][128][64] int8 | S [7][kpc + 4] fp32 | K scales [kpc] | V scales
+// [kpc] | stat | per-warp reductions | mbarriers [4]. stat: max[8] (head 7:
 // largest V scale) | Z[8] int64 | per-head inv, align factors, F [4][8] |
 // context partial [7][64] int64. Per-warp reductions: max [8][8] fp32, Z
 // [8][8] int64. The per-warp context partials [8][8][64] int64 reuse the ring
