@@ -100,7 +100,10 @@ int qwen_b200_position(const qwen_b200 *h, uint32_t slot, uint32_t *position);
 int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t rows, uint32_t position,
                       uint32_t *token, uint16_t *logits);
 /* One decode step for n slots (one token each, each at its own position).
- * Host buffers; the host->device and device->host copies are inside the call. */
+ * Host buffers; the host->device and device->host copies are inside the call.
+ * The forward is replayed from a CUDA graph per (n, context bucket of 128):
+ * the first step of a bucket launches the kernels directly and captures them.
+ * Changing qwen_b200_set_persistent_decode drops the captured graphs. */
 int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
                           uint32_t *tokens_out);
 /* The same step for slots 0..n-1 with device-resident token arrays, enqueued
