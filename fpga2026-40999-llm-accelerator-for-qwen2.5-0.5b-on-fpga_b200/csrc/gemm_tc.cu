@@ -397,10 +397,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
             if (ok) tmem_ld_wait();
+            if (nk <= 14) {
+                // |limb sum| <= 64 * 128 * 128 * nk < 2^24: limb pairs fold in
+                // int32 (|l0 + 128 l1| < 2^31), then one int64 step
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-                v[j] = (long long)d[0][j] + (long long)d[1][j] * 128ll + (long long)d[2][j] * 16384ll +
-                       (long long)d[3][j] * 2097152ll;
+                for (int j = 0; j < 16; ++j) {
+                    const int lo = d[0][j] + d[1][j] * 128, hi = d[2][j] + d[3][j] * 128;
+                    v[j] = (long long)lo + (long long)hi * 16384ll;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    v[j] = (long long)d[0][j] + (long long)d[1][j] * 128ll + (long long)d[2][j] * 16384ll +
+                           (long long)d[3][j] * 2097152ll;
+            }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int r = 32 * h + 16 * hh + j;
@@ -647,8 +657,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (ok) tmem_ld_wait();
 #pragma unroll
                 for (int jj = 0; jj < 16; ++jj) {
-                    const long long v = (long long)d[0][jj] + (long long)d[1][jj] * 128ll +
-                                        (long long)d[2][jj] * 16384ll + (long long)d[3][jj] * 2097152ll;
+                    // K = 896: limb pairs fold in int32 as in tc_gemm_kernel
+                    const long long v = KC <= 14 ? (long long)(d[0][jj] + d[1][jj] * 128) +
+                                                       (long long)(d[2][jj] + d[3][jj] * 128) * 16384ll
+                                                 : (long long)d[0][jj] + (long long)d[1][jj] * 128ll +
+                                                       (long long)d[2][jj] * 16384ll + (long long)d[3][jj] * 2097152ll;
                     const int r = 32 * h + 16 * hh + jj;
                     f[jj] = m0 + r < a.M ? exact_acc(v, a.ex[m0 + r]) : 0.f;
                 }
