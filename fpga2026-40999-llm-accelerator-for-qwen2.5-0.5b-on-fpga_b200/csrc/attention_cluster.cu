@@ -257,8 +257,9 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
             float sc[4];
 #pragma unroll
             for (int f = 0; f < 4; ++f) {
-                const long long dot = (long long)d[0][f] + ((long long)d[1][f] << 7) + ((long long)d[2][f] << 14) +
-                                      ((long long)d[3][f] << 21);
+                // per-limb sums over 64 dims are below 2^20: pairs add in int32
+                const long long dot =
+                    (long long)(d[0][f] + d[1][f] * 128) + (long long)(d[2][f] + d[3][f] * 128) * 16384ll;
                 const float ks = kss[f < 2 ? k0 : k1];
                 sc[f] = rbf(__fmul_rn(unalign28(dot, (f & 1) ? e_h1 : e_h0), ks) * 0.125f);
             }
