@@ -163,7 +163,8 @@ int launch_rmsnorm_limbs(const uint16_t *x, const uint16_t *gamma, int rows, flo
 // x [rows][K] (bf16) -> the four int8 limb planes of each row's 28-bit
 // alignment (limbs[l][row][k]) and its exponent ex[row]: one CTA per row,
 // 16-byte pieces of 8 values, the maximum reduced through shared memory.
-constexpr int AQ_THREADS = 256;
+// 512 threads: bs64 step 1.669 ms against 1.681 with 256 and 1.700 with 128.
+constexpr int AQ_THREADS = 512;
 template <int K>
 __global__ void __launch_bounds__(AQ_THREADS) act_quant_kernel(const uint16_t *__restrict__ x, int8_t *limbs,
                                                                size_t plane, int ld, int *ex) {
