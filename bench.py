@@ -173,65 +173,75 @@ def barrier(world):
     torch.cuda.synchronize()
 
 
-def cpu_decode_sample(min_seconds, max_seconds, context, threads):
-    """The oracle (plain-C port of the reference's behavioural model, KV8 mode)
-    decoding one sequence at `context` on the host cores. Returns tokens/s."""
+def oracle_batch(seqs, context, extra, threads):
+    """The oracle (plain-C port of the reference's behavioural model, KV8
+    mode) holding `seqs` sequences at contexts `context`..`context`+4 with the
+    seeded synthetic caches of the GPU arm. Its assets come from the oracle's
+    own link of the seeded generator (no product library is loaded)."""
     from oracle import ref
-    import qwen_b200
     with tempfile.TemporaryDirectory() as tmp:
-        assert qwen_b200.lib().qwen_b200_synth_write(tmp.encode(), SEED) == 0
-        m = ref.RefModel(tmp, capacity=context + 512, mode=ref.KV8, threads=threads)
-    m.fill_kv_synthetic(context, SEED)
-    tok, n, pos = 1, 0, context
-    m.forward([tok], pos)  # warm
-    pos += 1
-    t0 = time.perf_counter()
+        ref.synth_write(tmp, SEED)
+        m = ref.RefModel(tmp, capacity=context + 8 + extra, mode=ref.KV8, threads=threads)
+    m.set_slots(seqs)
+    for s in range(seqs):
+        m.fill_kv_synthetic_slot(s, context + s % 5, SEED + 17 * s)
+    return m
+
+
+def cpu_decode_sample(seqs, context, min_seconds, max_seconds, threads):
+    """Batched decode steps of `seqs` sequences on the host cores (each step
+    one forward of seqs rows, weights streamed once), for min..max seconds.
+    Returns (tokens/s, steps timed)."""
+    m = oracle_batch(seqs, context, 64, threads)
+    slots = np.arange(seqs, dtype=np.uint32)
+    toks = np.random.default_rng(SEED).integers(0, VOCAB, seqs).astype(np.uint32)
+    toks, _ = m.decode_batch(slots, toks)  # warm
+    n, t0 = 0, time.perf_counter()
     while True:
-        tok = m.forward([tok], pos)
-        pos, n = pos + 1, n + 1
+        toks, _ = m.decode_batch(slots, toks)
+        n += 1
         el = time.perf_counter() - t0
-        if (el >= min_seconds and n >= 3) or el >= max_seconds or pos >= context + 500:
+        if (el >= min_seconds and n >= 2) or el >= max_seconds or n >= 60:
             break
     m.close()
-    return n / el, n
+    return seqs * n / el, n
 
 
 def run_reference(args):
+    """The CPU reference of the path (the oracle port: the reference's model
+    is Python over torch and its C code holds no model math) on the same
+    workload as the GPU arm: one step = one greedy decode step of args.seqs
+    sequences at context args.context+, as one batched forward."""
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return 0
-    from oracle import ref
-    import qwen_b200
     threads = os.cpu_count() or 1
-    tokens_per_step = 4
-    with tempfile.TemporaryDirectory() as tmp:
-        assert qwen_b200.lib().qwen_b200_synth_write(tmp.encode(), SEED) == 0
-        m = ref.RefModel(tmp, capacity=args.context + tokens_per_step * (args.steps + args.warmup) + 8,
-                         mode=ref.KV8, threads=threads)
-    m.fill_kv_synthetic(args.context, SEED)
-    tok, pos = 1, args.context
-    for _ in range(args.warmup * tokens_per_step):
-        tok = m.forward([tok], pos)
-        pos += 1
+    m = oracle_batch(args.seqs, args.context, args.steps + args.warmup, threads)
+    slots = np.arange(args.seqs, dtype=np.uint32)
+    toks = np.random.default_rng(SEED).integers(0, VOCAB, args.seqs).astype(np.uint32)
+    for _ in range(args.warmup):
+        toks, _ = m.decode_batch(slots, toks)
     t0 = time.perf_counter()
-    for _ in range(args.steps * tokens_per_step):
-        tok = m.forward([tok], pos)
-        pos += 1
+    for _ in range(args.steps):
+        toks, _ = m.decode_batch(slots, toks)
     el = time.perf_counter() - t0
-    value = args.steps * tokens_per_step / el
-    sample = (f'oracle/qwen_ref.c (KV8 mode) decoding {tokens_per_step} tokens per step of one sequence '
-              f'at context {args.context}+ (one request at a time, as src/software/main.c serves them), '
-              f'{threads} OpenMP threads')
+    m.close()
+    value = args.seqs * args.steps / el
+    sample = (f'oracle/qwen_ref.c (KV8 mode, the reference model\'s arithmetic) decoding {args.seqs} sequences '
+              f'at context {args.context}..{args.context + 4}+ as one batched forward per step, '
+              f'{args.steps} steps after {args.warmup} warm-up, {threads} OpenMP threads')
+    cfg = workload_config(args)
+    cfg['global_batch'] = args.seqs  # rank 0 alone runs the CPU arm
+    cfg['parallelism'] = 'one host process (rank 0), all host cores'
     line = {'metric': 'decode tokens/s', 'value': round(value, 3), 'unit': 'tokens/s', 'impl': 'reference',
             'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
             'ms_per_step': round(1000 * el / args.steps, 3), 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'int8 weights x bf16 activations, fp32 accumulate, int8 KV',
-            'data': 'synthetic (seeded random-init int8 weights, seeded KV8 fill)',
-            'config': workload_config(args),
+            'data': 'synthetic (seeded random-init int8 weights, seeded KV8 fill, random token ids)',
+            'config': cfg,
             'cpu_baseline': {'value': round(value, 3), 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
                              'sample': sample},
             'e2e': {'value': round(value, 3), 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
-    m.close()
     print(json.dumps(line), flush=True)
     return 0
 
@@ -241,6 +251,8 @@ def workload_config(args):
                         'Qwen2.5-0.5B W8A16 with KV8 cache',
             'model': 'Qwen2.5-0.5B (24 layers, hidden 896, seeded random int8 weights)',
             'seqs_per_gpu': args.seqs, 'global_batch': args.seqs * args.gpus, 'context': args.context,
+            'contexts': f'{args.context}..{args.context + 4} at the first timed step (sequence s at '
+                        f'{args.context} + s % 5)',
             'parallelism': f'request-sharded replicas x{args.gpus} (no inter-GPU traffic)',
             'l2': 'inputs larger than L2 (weights 496 MB + KV ~0.88 GB per step)'}
 
@@ -255,8 +267,13 @@ def run_ours(args):
     S, C = args.seqs, args.context
     cap = C + 2 * (args.steps + args.warmup) + 64
     eng = qwen_b200.Engine(device=local, max_seqs=S, max_context=cap, max_rows=256).load_synthetic(SEED)
-    for s in range(S):
-        eng.fill_kv_synthetic(s, C, SEED + 17 * s + rank)
+
+    def fill(n):
+        # contexts C..C+4 (ragged), the caches of the oracle's batched step
+        for s in range(n):
+            eng.fill_kv_synthetic(s, C + s % 5, SEED + 17 * s + rank)
+
+    fill(S)
     rng = np.random.default_rng(SEED + rank)
     first = rng.integers(0, VOCAB, S).astype(np.int32)
     bufs = [torch.tensor(first, device='cuda'), torch.zeros(S, dtype=torch.int32, device='cuda')]
@@ -326,10 +343,17 @@ def run_ours(args):
     achieved = cb[dom] / (dom_us / 1e6) / 1e9
     roofline = {'kernel': kernel_names(S)[dom], 'class': dom, 'bound': 'hbm', 'achieved': round(achieved, 1),
                 'peak': hbm, 'peak_kind': peak_kind, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4),
-                'algorithmic_bytes_per_launch': cb[dom], 'traffic': committed_traffic(dom)}
+                'algorithmic_bytes_per_launch': cb[dom], 'traffic': committed_traffic(dom),
+                'traffic_source': ('ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel class at this '
+                                   'workload, from the committed capture summarised in profiles/traffic.json '
+                                   '(not measured in this run)') if committed_traffic(dom) else None}
     step_ms = ms_max / args.steps
     step_roof = {'bytes_per_step': sbytes, 'achieved': round(sbytes / (step_ms / 1000) / 1e9, 1), 'peak': hbm,
                  'unit': 'GB/s', 'frac': round(sbytes / (step_ms / 1000) / 1e9 / hbm, 4)}
+
+    # fixed global batch (strong scaling): the same 64 sequences split over
+    # the ranks, 64 / N per GPU; each GPU still streams every weight per step
+    strong = strong_scaling(eng, args, world, value, step_ms_of(ms_max, args), fill, stream, sp)
 
     # bs1 decode at short context (16-token prompt), slot 0
     bs1 = bs1_decode(eng, args, stream, sp, hbm)
@@ -343,13 +367,14 @@ def run_ours(args):
             'dtype': 'int8 weights x bf16 activations, fp32 accumulate, int8 KV',
             'data': 'synthetic (seeded random-init int8 weights, seeded KV8 fill, random token ids)',
             'config': workload_config(args), 'roofline': roofline, 'step_roofline': step_roof,
-            'kernels': kernels, 'e2e': e2e, 'gpu_launches': int(launches), 'bs1': bs1, 'clocks': clk}
+            'kernels': kernels, 'e2e': e2e, 'gpu_launches': int(launches), 'bs1': bs1, 'strong': strong,
+            'clocks': clk}
     if world == 1 and not args.no_cpu_baseline:
-        tps, n = cpu_decode_sample(10.0, 30.0, C, os.cpu_count() or 1)
+        tps, n = cpu_decode_sample(S, C, 10.0, 30.0, os.cpu_count() or 1)
         result['cpu_baseline'] = {'value': round(tps, 3), 'unit': 'tokens/s', 'cores': os.cpu_count() or 1,
                                   'kind': 'port',
-                                  'sample': f'oracle/qwen_ref.c KV8 decode of {n} tokens of one sequence at '
-                                            f'context {C}+ (one request at a time)'}
+                                  'sample': f'oracle/qwen_ref.c (KV8 mode) decoding {S} sequences at context '
+                                            f'{C}..{C + 4}+, {n} batched steps (one {S}-row forward each)'}
     eng.close()
     if world > 1:
         import torch.distributed as dist
@@ -358,6 +383,50 @@ def run_ours(args):
     if result is not None:
         print(json.dumps(result), flush=True)
     return 0
+
+
+def step_ms_of(ms_max, args):
+    return ms_max / args.steps
+
+
+# HBM-roofline ceiling of a fixed global batch of 64 at context 2048 split
+# over N GPUs (every GPU streams the 496 MB of weights each step), relative
+# to one GPU: roofline tokens/s ratios 1, 1.47, 1.92, 2.27.
+STRONG_CEILING = {1: 1.0, 2: 1.47, 4: 1.92, 8: 2.27}
+
+
+def strong_scaling(eng, args, world, value, step_ms, fill, stream, sp):
+    """Fixed global batch: args.seqs sequences over all ranks (seqs / N per
+    GPU), timed like the main step (device events, max over ranks)."""
+    import torch
+    S = args.seqs
+    if world == 1:
+        return {'global_batch': S, 'seqs_per_gpu': S, 'value': round(value, 1), 'ms_per_step': round(step_ms, 4),
+                'roofline_ceiling_vs_1gpu': 1.0, 'note': 'one GPU: the main measurement'}
+    if S % world:
+        return {'global_batch': S, 'unavailable': f'{S} sequences do not split evenly over {world} GPUs'}
+    n = S // world
+    fill(n)  # slots 0..n-1 back at contexts C..C+4
+    bufs = [torch.randint(0, VOCAB, (n,), dtype=torch.int32, device='cuda'),
+            torch.zeros(n, dtype=torch.int32, device='cuda')]
+
+    def step(i):
+        eng.decode_step_device(ctypes.c_void_p(bufs[i % 2].data_ptr()), n,
+                               ctypes.c_void_p(bufs[(i + 1) % 2].data_ptr()), sp)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    t1.record(stream)
+    barrier(world)
+    ms_max = max_over_ranks(t0.elapsed_time(t1), world)
+    return {'global_batch': S, 'seqs_per_gpu': n, 'value': round(world * n * args.steps / (ms_max / 1000.0), 1),
+            'ms_per_step': round(ms_max / args.steps, 4),
+            'roofline_ceiling_vs_1gpu': STRONG_CEILING.get(world)}
 
 
 def bs1_decode(eng, args, stream, sp, hbm):

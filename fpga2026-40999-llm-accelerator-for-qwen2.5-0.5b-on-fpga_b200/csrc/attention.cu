@@ -284,23 +284,60 @@ static __device__ __align__(256) uint8_t g_attn_scratch[QWEN_B200_NOALLOC_SCRATC
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
+// per device: the address and the unique id of the context it belongs to
 void *g_scratch_addr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
+
+// Unique id (cuCtxGetId: never reused within the process) of the context
+// current on this thread; 0 when it cannot be read.
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static bool resolved = false;
+    if (!resolved) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+        resolved = true;
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
 }  // namespace
 
-// Device address of g_attn_scratch on the current device. Host code only sees
-// a host-side stand-in under that name, so the address is looked up once per
-// device (with that device current) and cached.
+// Device address of g_attn_scratch in the current context. Host code only
+// sees a host-side stand-in under that name, so the address is looked up with
+// the device current, once per device and context: after cudaDeviceReset, or
+// when the caller makes another driver context current on the same device,
+// the context id changes and the address is looked up again.
 static int noalloc_scratch(void **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QWEN_B200_EDEVICE;
+    unsigned long long ctx = current_context_id();  // 0 before the runtime has bound a context
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
+    if (!ctx || !g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
         void *p = nullptr;
+        // (binds the device's primary context first when none is current)
         if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess || !p) {
             cudaGetLastError();
             return QWEN_B200_EDEVICE;
         }
+        ctx = current_context_id();
+        if (!ctx) return QWEN_B200_EDEVICE;
         g_scratch_addr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_addr[dev];
     return QWEN_B200_OK;

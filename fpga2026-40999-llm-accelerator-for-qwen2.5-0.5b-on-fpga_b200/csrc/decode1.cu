@@ -59,7 +59,7 @@ constexpr int D1_LONG_BYTES = D1A_KS + 4 * (2 * QB_D1_MAX_KEYS + 7 * D1A_SS);
 
 // short-context area (after the limb planes): prefetched history and scratch;
 // every region starts on a 16-byte boundary (vector and bulk-copy accesses)
-constexpr int d1_al16(int x) { return (x + 15) & ~15; }
+__host__ __device__ constexpr int d1_al16(int x) { return (x + 15) & ~15; }
 constexpr int D1S_KC = 0;                                            // int8 [2][64 keys][64] K codes, later V^T [2][64 dims][64 keys]
 constexpr int D1S_VC = d1_al16(D1S_KC + 2 * D1_SHORT * 64);          // int8 [2][64][64] V codes
 constexpr int D1S_KS = d1_al16(D1S_VC + 2 * D1_SHORT * 64);          // float [2][64 + 8] K scales (16-byte aligned superset)
@@ -259,8 +259,11 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
 
 // Grid barrier number k (1-based) of the launch: one release arrival per CTA
 // (its writes become visible first), thread 0 polls the counter with acquire
-// loads, the CTA proceeds together.
-__device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &ok) {
+// loads, the CTA proceeds together. After `limit` polls the wait gives up
+// with code 20 in the error flag; `extra` raises the target (a host-set test
+// switch makes the last barrier unreachable that way, see D1Args).
+__device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &ok, unsigned extra = 0,
+                                             uint32_t limit = 1u << 24) {
     __shared__ int s_ok;
     d1_sync();
     if (threadIdx.x == 0) {
@@ -268,10 +271,10 @@ __device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         bool good = ok;
         if (good) {
-            const unsigned target = k * gridDim.x;
+            const unsigned target = k * gridDim.x + extra;
             uint32_t spins = 0;
             while (ld_acquire_gpu(a.bar) < target) {
-                if (++spins > (1u << 24)) {
+                if (++spins > limit) {
                     atomicExch(a.err, 20u);
                     good = false;
                     break;
@@ -1153,7 +1156,9 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
         a.cand_v[c] = v;
         a.cand_i[c] = i;
     }
-    d1_grid_sync(a, ++nbar, ok);
+    // every slice has been consumed (no bulk copy is in flight) and the
+    // projections run on mma.sync: nothing asynchronous is outstanding here
+    d1_grid_sync(a, ++nbar, ok, a.expire_last_barrier ? 1u : 0u, a.expire_last_barrier ? (1u << 14) : (1u << 24));
     if (c == 0 && tid < 32) {
         float v = -INFINITY;
         uint32_t i = 0;

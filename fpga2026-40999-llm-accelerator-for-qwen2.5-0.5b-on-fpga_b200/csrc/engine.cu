@@ -61,6 +61,7 @@ struct qwen_b200 {
     float *ks = nullptr, *vs = nullptr;
     // activations
     uint16_t *x = nullptr, *q = nullptr, *ctx = nullptr, *mid = nullptr, *xl = nullptr, *logits = nullptr;
+    uint16_t *blogits = nullptr;  // [R][vocab] logits of batched steps that return them
     uint16_t *hn = nullptr, *qkvb = nullptr;  // normalised rows / q|k|v rows of the tensor-core path
     void *tc_ws = nullptr;                    // error flags of the bounded waits
     size_t tc_ws_bytes = 0;
@@ -75,6 +76,7 @@ struct qwen_b200 {
     // persistent batch-1 decode: per-layer pointers, barrier counter and the
     // per-CTA argmax candidates
     bool persistent = true;
+    bool expire_wait = false;  // test switch: the persistent step's last barrier times out
     D1Layer *d1_layers = nullptr;
     unsigned *d1_bar = nullptr;
     float *d1_cand_v = nullptr;
@@ -357,7 +359,7 @@ int check_device_flags(qwen_b200 *h) {
 // One forward over R rows whose ids/slots/positions are at meta[0..3R) with
 // stride n (ids n | slots n | positions n | logit rows n). nlog rows get the
 // LM head: rows listed at meta+3n, or all rows when identity.
-int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool want_logits, uint32_t *tokens_dst,
+int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint16_t *logits_dst, uint32_t *tokens_dst,
                 cudaStream_t st) {
     const uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n, *lrows = h->meta + 3 * n;
     const int cap = (int)h->cfg.max_context;
@@ -388,13 +390,14 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
         a.qkv = h->qkvb;
         a.ctx = h->ctx;
         a.mid = h->mid;
-        a.logits = want_logits ? h->logits : nullptr;
+        a.logits = logits_dst;
         a.tokens = tokens_dst;
         a.cand_v = h->d1_cand_v;
         a.cand_i = h->d1_cand_i;
         a.bar = h->d1_bar;
         a.err = reinterpret_cast<unsigned *>(h->tc_ws);
         a.eps = eps;
+        a.expire_last_barrier = h->expire_wait ? 1 : 0;
         LaunchScope ls(h, 8, st, 1);
         RK(launch_decode1(a, st));
         return 0;
@@ -498,13 +501,13 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, bool 
             am.pv = reinterpret_cast<float *>(h->lm_ws);
             am.pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(h->lm_ws) + (size_t)nlog * nblk * 4);
             am.nblk = nblk;
-            am.logits = want_logits ? h->logits : nullptr;
+            am.logits = logits_dst;
             rc = tc_gemm(h, EPI_ARGMAX, nlog, HID, h->mlm, h->s_lm, nullptr, VOC, nullptr, &am, st);
             if (rc) return rc;
             RK(launch_argmax_reduce(am.pv, am.pi, nlog, nblk, tokens_dst, st));
         } else {
             LaunchScope ls(h, 6, st, 2);
-            RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw, h->s_lm, VOC, want_logits ? h->logits : nullptr,
+            RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw, h->s_lm, VOC, logits_dst,
                               tokens_dst, h->lm_ws, h->lm_ws_bytes, st));
         }
     }
@@ -543,7 +546,8 @@ void csr_start(qwen_b200 *h) {
         h->csr_error = code;
     };
     // Error codes at 0x30: 1 malformed request, 2 CUDA error, 3 no model
-    // loaded, 4 START while busy.
+    // loaded, 4 START while busy, 5 a bounded device wait expired (the
+    // reference's PL-error path, generation.c:21-25).
     if (h->csr_state == CSR_BUSY) return error(4);
     const uint64_t mode = h->regs[0x80 / 8] & 1, rows = h->regs[0x88 / 8], ctxlen = h->regs[0x90 / 8],
                    position = h->regs[0x98 / 8];
@@ -565,8 +569,10 @@ void csr_start(qwen_b200 *h) {
     h->h_meta[3 * n] = (uint32_t)(n - 1);
     cudaStream_t st = h->stream;
     bool ok = cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * n + 1) * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
-    ok = ok && run_forward(h, n, (int)(position + rows), 1, false, false, h->tokens, st) == 0;
+    ok = ok && run_forward(h, n, (int)(position + rows), 1, n == 1, nullptr, h->tokens, st) == 0;
     ok = ok && cudaMemcpyAsync(h->h_tokens, h->tokens, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    // the bounded-wait error flag travels with the token
+    ok = ok && cudaMemcpyAsync(h->h_flag + 1, h->tc_ws, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     ok = ok && cudaEventRecord(h->csr_event, st) == cudaSuccess;
     if (!ok) return error(2);
     h->pos[0] = (uint32_t)(position + rows);
@@ -692,19 +698,30 @@ void qwen_b200_rope_table(uint32_t positions, float *table) {
         }
 }
 
+// Captured steps have the engine's switches built in: drops them.
+static void drop_graphs(qwen_b200 *h) {
+    if (!h->loaded) return;
+    cudaSetDevice(h->cfg.device);
+    cudaDeviceSynchronize();
+    for (auto &kv : h->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto &kv : h->host_graphs) cudaGraphExecDestroy(kv.second.first);
+    h->graphs.clear();
+    h->host_graphs.clear();
+}
+
 int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable) {
     if (!h) return QWEN_B200_EINVAL;
     const bool p = enable != 0;
-    if (p != h->persistent && h->loaded) {
-        // captured steps have the previous choice built in
-        cudaSetDevice(h->cfg.device);
-        cudaDeviceSynchronize();
-        for (auto &kv : h->graphs) cudaGraphExecDestroy(kv.second);
-        for (auto &kv : h->host_graphs) cudaGraphExecDestroy(kv.second.first);
-        h->graphs.clear();
-        h->host_graphs.clear();
-    }
+    if (p != h->persistent) drop_graphs(h);  // captured steps have the previous choice built in
     h->persistent = p;
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_test_expire_wait(qwen_b200 *h, int enable) {
+    if (!h) return QWEN_B200_EINVAL;
+    const bool e = enable != 0;
+    if (e != h->expire_wait) drop_graphs(h);
+    h->expire_wait = e;
     return QWEN_B200_OK;
 }
 
@@ -748,8 +765,8 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
         h->h_meta[3 * n] = (uint32_t)(n - 1);
         CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * n + 1) * 4, cudaMemcpyHostToDevice, st));
         CK(cudaEventRecord(h->staged, st));
-        rc = run_forward(h, n, (int)(position + c0 + (uint32_t)n), last ? 1 : 0, n == 1, last && logits, h->tokens,
-                         st);
+        rc = run_forward(h, n, (int)(position + c0 + (uint32_t)n), last ? 1 : 0, n == 1,
+                         last && logits ? h->logits : nullptr, h->tokens, st);
         if (rc) return rc;
         if (h->dump_layer >= 0 && h->d_dump) {
             CK(cudaStreamSynchronize(st));
@@ -767,8 +784,10 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
     return QWEN_B200_OK;
 }
 
-int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
-                          uint32_t *tokens_out) {
+// One decode step of n slots from host buffers; with logits != NULL the
+// forward runs directly (no graph) and every row's logits come back too.
+static int decode_step_impl(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
+                            uint32_t *tokens_out, uint16_t *logits) {
     if (!h) return QWEN_B200_EINVAL;
     int rc = ensure_device(h);
     if (rc) return rc;
@@ -797,20 +816,25 @@ int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *t
     const uint32_t chunks = (max_len + 127) / 128;
     const int bucket_len = (int)std::min<uint32_t>(chunks * 128, h->cfg.max_context);
     const auto key = std::make_pair(n, chunks);
-    auto it = h->prof ? h->host_graphs.end() : h->host_graphs.find(key);
+    auto it = (h->prof || logits) ? h->host_graphs.end() : h->host_graphs.find(key);
+    if (logits && !h->blogits) {
+        // every row's logits: allocated at the first such step
+        if ((rc = dalloc(h, (void **)&h->blogits, (size_t)h->R * VOC * 2))) return rc;
+    }
     if (it != h->host_graphs.end()) {
         CK(cudaGraphLaunch(it->second.first, st));
         h->nlaunch = it->second.second;
-    } else if (h->prof) {
+    } else if (h->prof || logits) {
         h->nlaunch = 0;
-        if ((rc = run_forward(h, (int)n, bucket_len, (int)n, true, false, h->tokens, st))) return rc;
+        if ((rc = run_forward(h, (int)n, bucket_len, (int)n, true, logits ? h->blogits : nullptr, h->tokens, st)))
+            return rc;
     } else {
         h->nlaunch = 0;
-        if ((rc = run_forward(h, (int)n, bucket_len, (int)n, true, false, h->tokens, st))) return rc;
+        if ((rc = run_forward(h, (int)n, bucket_len, (int)n, true, nullptr, h->tokens, st))) return rc;
         cudaGraph_t graph;
         CK(cudaStreamBeginCapture(h->cap_stream, cudaStreamCaptureModeThreadLocal));
         h->nlaunch = 0;
-        rc = run_forward(h, (int)n, bucket_len, (int)n, true, false, h->tokens, h->cap_stream);
+        rc = run_forward(h, (int)n, bucket_len, (int)n, true, nullptr, h->tokens, h->cap_stream);
         cudaError_t e = cudaStreamEndCapture(h->cap_stream, &graph);
         if (rc) return rc;
         if (e != cudaSuccess) return fail(h, QWEN_B200_EDEVICE, "graph capture: %s", cudaGetErrorString(e));
@@ -827,6 +851,7 @@ int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *t
         cudaMemset(h->tc_ws, 0, 4);
         return fail(h, QWEN_B200_ETIMEOUT, "a pipeline wait on the device timed out (code %u)", *h->h_flag);
     }
+    if (logits) CK(cudaMemcpy(logits, h->blogits, (size_t)n * VOC * 2, cudaMemcpyDeviceToHost));
     for (uint32_t i = 0; i < n; ++i) {
         h->pos[slots[i]] += 1;
         tokens_out[i] = h->h_tokens[i];
@@ -835,6 +860,17 @@ int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *t
     for (uint32_t i = 0; i < n; ++i)
         if (tokens_out[i] >= (uint32_t)VOC) return fail(h, QWEN_B200_ETOKEN, "token %u", tokens_out[i]);
     return QWEN_B200_OK;
+}
+
+int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
+                          uint32_t *tokens_out) {
+    return decode_step_impl(h, slots, tokens_in, n, tokens_out, nullptr);
+}
+
+int qwen_b200_decode_step_logits(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
+                                 uint32_t *tokens_out, uint16_t *logits) {
+    if (!logits) return h ? fail(h, QWEN_B200_EINVAL, "logits buffer is NULL") : QWEN_B200_EINVAL;
+    return decode_step_impl(h, slots, tokens_in, n, tokens_out, logits);
 }
 
 static int enqueue_device_step(qwen_b200 *h, const uint32_t *d_in, int n, int max_len, uint32_t *d_out,
@@ -846,7 +882,7 @@ static int enqueue_device_step(qwen_b200 *h, const uint32_t *d_in, int n, int ma
         LaunchScope ls(h, 7, st, 1);
         RK(launch_decode_prologue(d_in, n, h->slot_pos, ids, slots, positions, st));
     }
-    int rc = run_forward(h, n, max_len, n, true, false, d_out, st);
+    int rc = run_forward(h, n, max_len, n, true, nullptr, d_out, st);
     if (rc) return rc;
     LaunchScope ls(h, 7, st, 1);
     RK(launch_decode_epilogue(n, h->slot_pos, st));
@@ -999,6 +1035,12 @@ uint64_t qwen_b200_csr_read(void *ctx, unsigned offset) {
                 if (e != cudaSuccess) {
                     h->csr_state = CSR_ERROR;
                     h->csr_error = 2;
+                } else if (h->h_flag[1]) {
+                    // a bounded wait on the device expired: the token is not valid
+                    cudaMemsetAsync(h->tc_ws, 0, 4, h->stream);
+                    h->h_flag[1] = 0;
+                    h->csr_state = CSR_ERROR;
+                    h->csr_error = 5;
                 } else {
                     h->csr_token = h->h_tokens[0];
                     h->csr_state = CSR_DONE;

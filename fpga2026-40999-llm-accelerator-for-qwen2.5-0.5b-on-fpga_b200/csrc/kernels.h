@@ -63,6 +63,10 @@ struct D1Args {
     unsigned *bar;                     // grid barrier counter (reset by the launch)
     unsigned *err;                     // error flag of the bounded waits
     float eps;
+    // test switch (host-set): the last grid barrier waits for one arrival
+    // more than the grid makes, with a short limit, so that bounded wait
+    // expires (code 20) with nothing asynchronous in flight
+    int expire_last_barrier;
 };
 int decode1_supported(int max_len);
 size_t decode1_smem_bytes();

@@ -1,7 +1,9 @@
 // sm_100a building blocks written as inline PTX: mbarriers with bounded waits,
-// TMA 2D tile loads (no multicast), TMEM allocation, tcgen05.mma (kind::f16,
-// bf16 x bf16 -> fp32, operands in shared memory), tcgen05.commit / ld and the
-// shared-memory matrix descriptor for the 128-byte-swizzled K-major layout.
+// TMA 2D tile loads and contiguous bulk copies (no multicast), TMEM
+// allocation, tcgen05.commit, the shared-memory matrix descriptor for the
+// 128-byte-swizzled K-major layout, and thread-block cluster helpers. The
+// tcgen05.mma instructions themselves (kind::i8, int8 x int8 -> int32) and
+// the TMEM loads live with their kernels (gemm_tc.cu).
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -90,7 +92,7 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 // ---------------------------------------------------------------- UMMA
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
-// layout: rows of 128 bytes (64 bf16), 8-row groups 1024 bytes apart (stride
+// layout: rows of 128 bytes (128 int8), 8-row groups 1024 bytes apart (stride
 // byte offset), version 1 (sm_100), layout type 2 (SWIZZLE_128B).
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     uint64_t d = 0;
@@ -101,40 +103,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     d |= (uint64_t)2 << 61;             // SWIZZLE_128B
     return d;
 }
-// Instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-// D[tmem] (+)= A[smem] * B[smem]^T; issued by a single thread.
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
-}
 // Arrives on *bar once every tcgen05.mma issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
                  : "memory");
 }
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // ---------------------------------------------------------------- clusters
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;

@@ -37,6 +37,7 @@ _SIGNATURES = {
     'qwen_b200_position': (c_int, [c_void_p, c_uint32, _P32]),
     'qwen_b200_forward': (c_int, [c_void_p, c_uint32, _P32, c_uint32, c_uint32, _P32, _P16]),
     'qwen_b200_decode_step': (c_int, [c_void_p, _P32, _P32, c_uint32, _P32]),
+    'qwen_b200_decode_step_logits': (c_int, [c_void_p, _P32, _P32, c_uint32, _P32, _P16]),
     'qwen_b200_decode_step_device': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
     'qwen_b200_fill_kv_synthetic': (c_int, [c_void_p, c_uint32, c_uint32, c_uint64]),
     'qwen_b200_read_kv': (c_int, [c_void_p, c_uint32, c_uint32, c_uint32, _P8, _PF, _P8, _PF]),
@@ -54,6 +55,7 @@ _SIGNATURES = {
     'qwen_b200_op_gemm_w8a16_residual': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32,
                                                  c_void_p, c_void_p]),
     'qwen_b200_set_persistent_decode': (c_int, [c_void_p, c_int]),
+    'qwen_b200_test_expire_wait': (c_int, [c_void_p, c_int]),
     'qwen_b200_gemm_tc_workspace': (c_size_t, [c_uint32, c_uint32, c_uint32]),
     'qwen_b200_op_gemm_w8a16_tc': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p,
                                            c_int, c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -80,6 +80,16 @@ class Engine:
                                           ptr(out, c_uint32)), self.h)
         return out
 
+    def decode_step_logits(self, slots, tokens):
+        """decode_step that also returns every row's logits [n][151936] (bf16 bits)."""
+        slots = np.ascontiguousarray(slots, dtype=np.uint32)
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(len(slots), dtype=np.uint32)
+        logits = np.empty((len(slots), _lib.VOCAB), dtype=np.uint16)
+        check(lib().qwen_b200_decode_step_logits(self.h, ptr(slots, c_uint32), ptr(tokens, c_uint32), len(slots),
+                                                 ptr(out, c_uint32), ptr(logits, c_uint16)), self.h)
+        return out, logits
+
     def decode_step_device(self, tokens_in_ptr, n, tokens_out_ptr, stream=None):
         check(lib().qwen_b200_decode_step_device(self.h, tokens_in_ptr, n, tokens_out_ptr, stream), self.h)
 

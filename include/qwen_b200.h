@@ -48,7 +48,8 @@ extern "C" {
 #define QWEN_B200_CSR_VERSION 0x0008
 #define QWEN_B200_CSR_CONTROL 0x0010 /* bit0 START, bit3 CLEAR */
 #define QWEN_B200_CSR_STATUS 0x0018  /* done <=> (s & 0x46) == 0x44; bit3 error */
-#define QWEN_B200_CSR_ERROR 0x0030
+#define QWEN_B200_CSR_ERROR 0x0030  /* 1 bad request, 2 CUDA error, 3 no model, 4 START while busy,
+                                        5 a bounded device wait expired */
 #define QWEN_B200_CSR_RUN_MODE 0x0080 /* 0 prefill (clears the context), 1 decode */
 #define QWEN_B200_CSR_SEQ_LEN 0x0088
 #define QWEN_B200_CSR_CONTEXT_LEN 0x0090
@@ -106,6 +107,11 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
  * Changing qwen_b200_set_persistent_decode drops the captured graphs. */
 int qwen_b200_decode_step(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
                           uint32_t *tokens_out);
+/* The same step, also returning every row's 151936 bf16 logits in
+ * logits[n][151936] (host buffer). Runs the kernels directly (no graph);
+ * the device buffer for the logits is allocated at the first call. */
+int qwen_b200_decode_step_logits(qwen_b200 *h, const uint32_t *slots, const uint32_t *tokens_in, uint32_t n,
+                                 uint32_t *tokens_out, uint16_t *logits);
 /* The same step for slots 0..n-1 with device-resident token arrays, enqueued
  * on `stream` (a cudaStream_t; NULL is the CUDA default stream); d_tokens_out is written on the
  * device and ids are not range-checked on the host. The first call for a given
@@ -132,6 +138,15 @@ int qwen_b200_set_dump(qwen_b200 *h, int layer, uint16_t *q, uint16_t *k, uint16
  * separated by grid barriers; same arithmetic (and bits) as the per-kernel
  * path. enable = 0 selects the per-kernel path (default 1). */
 int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable);
+/* Test switch for the error path of the bounded device waits (reference:
+ * the -2 / -3 returns of src/software/generation.c:21-25). While enabled, the
+ * persistent single-row step waits at its last grid barrier for one arrival
+ * more than its CTAs make, with a short limit (a few milliseconds), at a
+ * point where no bulk copy or tensor-core operation is in flight: the wait
+ * expires, the kernel returns normally, and the call reports
+ * QWEN_B200_ETIMEOUT (qwen_b200_forward) or CSR status 8 with error code 5.
+ * The device stays usable. Default off; toggling drops captured graphs. */
+int qwen_b200_test_expire_wait(qwen_b200 *h, int enable);
 
 /* Kernel classes reported by qwen_b200_profile_decode. */
 #define QWEN_B200_KCLASSES 9 /* 0 embedding, 1 RMSNorm+QKV+RoPE+KV8 append, 2 attention,
@@ -151,7 +166,8 @@ uint32_t qwen_b200_step_launches(const qwen_b200 *h);
 /* ops.context = handle; ops.write = qwen_b200_csr_write; ops.read =
  * qwen_b200_csr_read; ops.embedding = qwen_b200_embedding. Slot 0 is used.
  * START (0x10 bit0) enqueues the forward and returns at once; 0x18 reads 2
- * while it runs, 0x44 when the token is ready, 8 on error. */
+ * while it runs, 0x44 when the token is ready, 8 on error (code at 0x30; a
+ * device wait that expired during the forward reads 8 with code 5). */
 void qwen_b200_csr_write(void *h, unsigned offset, uint64_t value);
 uint64_t qwen_b200_csr_read(void *h, unsigned offset);
 /* main.c:114-125 copy_embedding: records token id for ACT_IN row `row`. */
@@ -232,7 +248,11 @@ int qwen_b200_op_attention(const uint16_t *q, uint32_t rows, const uint32_t *slo
  * size are rejected with QWEN_B200_ESCRATCH before anything is launched (for
  * example 64 rows at capacity 2048 fit; 64 rows at capacity 8192 do not).
  * The first call on each device looks up the scratch's device address with
- * that device current; make that first call before any stream capture. All
+ * that device current; make that first call before any stream capture. The
+ * address is remembered per device and CUDA context: a call in a new context
+ * (after cudaDeviceReset, or with another driver context made current on the
+ * device) looks it up again, so that call too should come before any
+ * capture. All
  * calls on a device share the one array and it keeps the last call's
  * contents: each call zeroes the parts that must start at zero, but calls
  * whose executions overlap on the GPU (different streams, or different host

@@ -23,6 +23,8 @@
  */
 #include "qwen_ref.h"
 
+#include "assets.h"
+
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -59,6 +61,10 @@ struct ref_model {
     float *kf[NL], *vf[NL];         /* bf16 KV: [cap][2][64] */
     int8_t *kc[NL], *vc[NL];        /* KV8: [2][cap][64] */
     float *ks[NL], *vs[NL];         /* KV8: [2][cap] */
+    /* KV8 caches of nslots sequences: kc/vc [slot][2][cap][64], ks/vs
+     * [slot][2][cap]; slot 0 is the sequence of the single-sequence calls,
+     * whose position is `position`; spos[s] holds the others' */
+    unsigned nslots, *spos;
     int dump_layer;
     float *dq, *dk, *dv, *dctx, *dh, *dm, *dy;
 };
@@ -177,6 +183,8 @@ ref_model *ref_open(const char *root, unsigned capacity, char *err, size_t errle
     if (!m) return NULL;
     m->capacity = capacity ? capacity : 256;
     m->dump_layer = -1;
+    m->nslots = 1;
+    m->spos = (unsigned *)calloc(1, sizeof(unsigned));
     char *cfg = (char *)slurp(root, "CONFIG.JSON", 0, err, errlen);
     if (!cfg) goto fail;
     /* model_backend.py:19 asserts hidden/layers/vocab. */
@@ -262,6 +270,7 @@ void ref_close(ref_model *m) {
     free(m->gamma);
     free(m->embed);
     free(m->rope);
+    free(m->spos);
     free(m);
 }
 
@@ -692,21 +701,11 @@ static uint32_t argmax_last(const float *v, unsigned n) {
     return best;
 }
 
+static void lm_head_rows(const ref_model *m, const float *x, unsigned n, unsigned mode, uint32_t *tokens,
+                         float *logits);
 uint32_t ref_lm_head(const ref_model *m, const float *x, unsigned mode, float *logits) {
-    float h[HID];
-    ref_rmsnorm(x, 1, m->gamma + 43008, eps_of(mode), mode, h);
-    float *acc = (float *)malloc((size_t)VOC * sizeof(float));
-    accum(h, 1, HID, m->lmt, VOC, acc, mode);
-    const float *s = m->scale + 304128;
-    float *pre = (float *)malloc((size_t)VOC * sizeof(float));
-    for (unsigned n = 0; n < VOC; ++n) {
-        pre[n] = bfm(acc[n], mode) * s[n];
-        acc[n] = bfm(pre[n], mode);
-    }
-    uint32_t tok = (mode & REF_ARGMAX_F32) ? argmax_last(pre, VOC) : argmax_last(acc, VOC);
-    if (logits) memcpy(logits, acc, (size_t)VOC * sizeof(float));
-    free(acc);
-    free(pre);
+    uint32_t tok = 0;
+    lm_head_rows(m, x, 1, mode, &tok, logits);
     return tok;
 }
 
@@ -721,37 +720,132 @@ int ref_kv8_state(const ref_model *m, int layer, int8_t *kcodes, float *kscales,
     return (int)n;
 }
 
-int ref_fill_kv_synthetic(ref_model *m, unsigned length, uint64_t seed) {
-    if (length > m->capacity) return -1;
+/* The engine's seeded KV8 fill (its fill_kv_kernel), restated so both sides
+ * hold identical caches: per (layer, K|V, kv head) a key
+ * seed * 0x100000001B3 + (4 layer + 2 (V?1:0) + head) * 0x9E3779B9, code of
+ * (t, d) = hash(key + 64 t + d) % 255 - 127, scale of t =
+ * 0.01 + 0.02 * (hash(~key + t) & 0xffff) / 65536, with the SplitMix64
+ * finaliser as the hash (upper 32 bits of its output). */
+static uint32_t fill_hash(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ULL;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBULL;
+    return (uint32_t)((x ^ (x >> 31)) >> 16);
+}
+
+static size_t slot_codes(const ref_model *m, unsigned slot) { return (size_t)slot * KVH * m->capacity * HD; }
+static size_t slot_scales(const ref_model *m, unsigned slot) { return (size_t)slot * KVH * m->capacity; }
+
+static int fill_slot(ref_model *m, unsigned slot, unsigned length, uint64_t seed) {
+    if (length > m->capacity || slot >= m->nslots) return -1;
+#pragma omp parallel for schedule(static)
     for (int l = 0; l < NL; ++l)
-        for (int g = 0; g < KVH; ++g)
-            for (unsigned t = 0; t < length; ++t) {
-                uint64_t z = seed * 0x9E3779B97F4A7C15ULL + ((uint64_t)l * 2 + g) * 0x100000001B3ULL + t;
-                for (int d = 0; d < HD; ++d) {
-                    z ^= z >> 33;
-                    z *= 0xff51afd7ed558ccdULL;
-                    z ^= z >> 29;
-                    m->kc[l][((size_t)g * m->capacity + t) * HD + d] = (int8_t)((int)(z % 255u) - 127);
-                    m->vc[l][((size_t)g * m->capacity + t) * HD + d] = (int8_t)((int)((z >> 16) % 255u) - 127);
+        for (int which = 0; which < 2; ++which)
+            for (int g = 0; g < KVH; ++g) {
+                const uint64_t key = seed * 0x100000001B3ULL + ((uint64_t)l * 4 + (uint64_t)which * 2 + g) * 0x9E3779B9ULL;
+                int8_t *codes = (which ? m->vc[l] : m->kc[l]) + slot_codes(m, slot) + (size_t)g * m->capacity * HD;
+                float *scales = (which ? m->vs[l] : m->ks[l]) + slot_scales(m, slot) + (size_t)g * m->capacity;
+                for (unsigned t = 0; t < length; ++t) {
+                    for (int d = 0; d < HD; ++d)
+                        codes[(size_t)t * HD + d] = (int8_t)((int)(fill_hash(key + (uint64_t)t * HD + d) % 255u) - 127);
+                    scales[t] = 0.01f + 0.02f * (float)(fill_hash(~key + t) & 0xffff) / 65536.0f;
                 }
-                m->ks[l][(size_t)g * m->capacity + t] = 0.01f + 0.02f * (float)((z >> 40) & 0xffff) / 65536.0f;
-                m->vs[l][(size_t)g * m->capacity + t] = 0.01f + 0.02f * (float)((z >> 24) & 0xffff) / 65536.0f;
             }
-    m->position = length;
+    if (slot == 0)
+        m->position = length;
+    else
+        m->spos[slot] = length;
+    return 0;
+}
+
+int ref_fill_kv_synthetic(ref_model *m, unsigned length, uint64_t seed) { return fill_slot(m, 0, length, seed); }
+int ref_fill_kv_synthetic_slot(ref_model *m, unsigned slot, unsigned length, uint64_t seed) {
+    return fill_slot(m, slot, length, seed);
+}
+
+int ref_set_slots(ref_model *m, unsigned nslots) {
+    if (!nslots) return -1;
+    unsigned *sp = (unsigned *)calloc(nslots, sizeof(unsigned));
+    if (!sp) return -1;
+    for (int l = 0; l < NL; ++l) {
+        free(m->kc[l]);
+        free(m->vc[l]);
+        free(m->ks[l]);
+        free(m->vs[l]);
+        m->kc[l] = (int8_t *)calloc((size_t)nslots * m->capacity * KVH * HD, 1);
+        m->vc[l] = (int8_t *)calloc((size_t)nslots * m->capacity * KVH * HD, 1);
+        m->ks[l] = (float *)calloc((size_t)nslots * m->capacity * KVH, sizeof(float));
+        m->vs[l] = (float *)calloc((size_t)nslots * m->capacity * KVH, sizeof(float));
+        if (!m->kc[l] || !m->vc[l] || !m->ks[l] || !m->vs[l]) {
+            free(sp);
+            return -1;
+        }
+    }
+    free(m->spos);
+    m->spos = sp;
+    m->nslots = nslots;
+    m->position = 0;
     return 0;
 }
 
 /* ------------------------------------------------------------------ forward */
-int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned position, uint32_t *token,
-                float *logits) {
-    if (position != m->position || rows == 0 || position + rows > m->capacity) return -8;
-    for (unsigned r = 0; r < rows; ++r)
-        if (ids[r] >= VOC) return -1;
+/* KV8 attention of rows whose sequences sit in different slots. */
+static void attention_slots(const ref_model *m, int l, const float *q, unsigned rows, const uint32_t *pos,
+                            const uint32_t *slot, unsigned mode, float *ctx) {
+#pragma omp parallel for schedule(dynamic)
+    for (long rh = 0; rh < (long)rows * QH; ++rh) {
+        const unsigned r = (unsigned)rh / QH, h = (unsigned)rh % QH;
+        const unsigned g = h / 7, visible = pos[r] + 1; /* repeat_interleave(7), model_backend.py:97-98 */
+        const int8_t *kc = m->kc[l] + slot_codes(m, slot[r]) + (size_t)g * m->capacity * HD;
+        const int8_t *vc = m->vc[l] + slot_codes(m, slot[r]) + (size_t)g * m->capacity * HD;
+        const float *ks = m->ks[l] + slot_scales(m, slot[r]) + (size_t)g * m->capacity;
+        const float *vs = m->vs[l] + slot_scales(m, slot[r]) + (size_t)g * m->capacity;
+        kv8_view vv = {vc, vs};
+        float *scratch = (float *)malloc(visible * sizeof(float));
+        float *out = ctx + (size_t)r * HID + (size_t)h * HD;
+        ref_kv8_scores(q + ((size_t)r * QH + h) * HD, visible, kc, ks, mode, scratch);
+        if (mode & REF_EXACT)
+            attend_finish_kv8_exact(scratch, visible, vc, vs, mode, out);
+        else
+            attend_finish(scratch, visible, kv8_at, &vv, mode, out);
+        free(scratch);
+    }
+}
+
+/* Final norm + LM head + greedy argmax of n rows x [n][896] (weights
+ * streamed once for all rows; each row's sums are those of a one-row call). */
+static void lm_head_rows(const ref_model *m, const float *x, unsigned n, unsigned mode, uint32_t *tokens,
+                         float *logits) {
+    float *h = (float *)malloc((size_t)n * HID * sizeof(float));
+    ref_rmsnorm(x, n, m->gamma + 43008, eps_of(mode), mode, h);
+    float *acc = (float *)malloc((size_t)n * VOC * sizeof(float));
+    float *pre = (float *)malloc((size_t)VOC * sizeof(float));
+    accum(h, n, HID, m->lmt, VOC, acc, mode);
+    const float *s = m->scale + 304128;
+    for (unsigned r = 0; r < n; ++r) {
+        float *a = acc + (size_t)r * VOC;
+        for (unsigned j = 0; j < VOC; ++j) {
+            pre[j] = bfm(a[j], mode) * s[j];
+            a[j] = bfm(pre[j], mode);
+        }
+        tokens[r] = (mode & REF_ARGMAX_F32) ? argmax_last(pre, VOC) : argmax_last(a, VOC);
+        if (logits) memcpy(logits + (size_t)r * VOC, a, (size_t)VOC * sizeof(float));
+    }
+    free(h);
+    free(acc);
+    free(pre);
+}
+
+/* The forward of model_backend.py:80-115 over `rows` rows, row r being token
+ * ids[r] of the sequence in slot slot[r] at position pos[r] (rows of one
+ * sequence in increasing positions); the LM head runs on the nlm rows listed
+ * in lm_rows. */
+static void run_rows(ref_model *m, unsigned rows, const uint32_t *ids, const uint32_t *pos, const uint32_t *slot,
+                     unsigned nlm, const uint32_t *lm_rows, uint32_t *tokens, float *logits) {
     const unsigned mode = m->mode;
     const float eps = eps_of(mode);
     float *x = (float *)malloc((size_t)rows * HID * sizeof(float));
     float *h = (float *)malloc((size_t)rows * HID * sizeof(float));
-    float *qkv = (float *)malloc((size_t)rows * QKV * sizeof(float));
     float *q = (float *)malloc((size_t)rows * HID * sizeof(float));
     float *k = (float *)malloc((size_t)rows * KVH * HD * sizeof(float));
     float *v = (float *)malloc((size_t)rows * KVH * HD * sizeof(float));
@@ -759,11 +853,8 @@ int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned posit
     float *gu = (float *)malloc((size_t)rows * FFN * 2 * sizeof(float));
     float *mid = (float *)malloc((size_t)rows * FFN * sizeof(float));
     float *tmp = (float *)malloc((size_t)rows * FFN * sizeof(float));
-    uint32_t *pos = (uint32_t *)malloc(rows * sizeof(uint32_t));
-    for (unsigned r = 0; r < rows; ++r) {
-        pos[r] = position + r;
+    for (unsigned r = 0; r < rows; ++r)
         for (unsigned i = 0; i < HID; ++i) x[(size_t)r * HID + i] = bf2f(m->embed[(size_t)ids[r] * HID + i]);
-    }
     for (int l = 0; l < NL; ++l) {
         const float *sc = m->scale + (size_t)l * 12672;
         const float *bias = m->bias + (size_t)l * QKV;
@@ -781,14 +872,18 @@ int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned posit
         for (unsigned r = 0; r < rows; ++r)
             for (int g = 0; g < KVH; ++g) {
                 const float *kr = k + ((size_t)r * KVH + g) * HD, *vr = v + ((size_t)r * KVH + g) * HD;
-                size_t t = pos[r];
-                memcpy(m->kf[l] + (t * KVH + g) * HD, kr, HD * sizeof(float));
-                memcpy(m->vf[l] + (t * KVH + g) * HD, vr, HD * sizeof(float));
-                ref_kv8_quant(kr, 1, m->kc[l] + ((size_t)g * m->capacity + t) * HD, m->ks[l] + (size_t)g * m->capacity + t);
-                ref_kv8_quant(vr, 1, m->vc[l] + ((size_t)g * m->capacity + t) * HD, m->vs[l] + (size_t)g * m->capacity + t);
+                const size_t t = pos[r];
+                if (slot[r] == 0) {
+                    memcpy(m->kf[l] + (t * KVH + g) * HD, kr, HD * sizeof(float));
+                    memcpy(m->vf[l] + (t * KVH + g) * HD, vr, HD * sizeof(float));
+                }
+                const size_t cs = slot_codes(m, slot[r]) + ((size_t)g * m->capacity + t) * HD;
+                const size_t ss = slot_scales(m, slot[r]) + (size_t)g * m->capacity + t;
+                ref_kv8_quant(kr, 1, m->kc[l] + cs, m->ks[l] + ss);
+                ref_kv8_quant(vr, 1, m->vc[l] + cs, m->vs[l] + ss);
             }
         if (mode & REF_KV8) {
-            ref_attention_kv8(q, rows, pos, m->kc[l], m->ks[l], m->vc[l], m->vs[l], m->capacity, mode, ctx);
+            attention_slots(m, l, q, rows, pos, slot, mode, ctx);
         } else {
 #pragma omp parallel for schedule(dynamic)
             for (long rh = 0; rh < (long)rows * QH; ++rh) {
@@ -825,13 +920,13 @@ int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned posit
             if (m->dy) memcpy(m->dy, x, (size_t)rows * HID * sizeof(float));
         }
     }
-    /* final norm on the last row + LM head + argmax (model_backend.py:108-114) */
-    uint32_t tok = ref_lm_head(m, x + (size_t)(rows - 1) * HID, mode, logits);
-    m->position = position + rows;
-    if (token) *token = tok;
+    /* final norm + LM head + argmax (model_backend.py:108-114) */
+    float *xl = (float *)malloc((size_t)nlm * HID * sizeof(float));
+    for (unsigned i = 0; i < nlm; ++i) memcpy(xl + (size_t)i * HID, x + (size_t)lm_rows[i] * HID, HID * sizeof(float));
+    lm_head_rows(m, xl, nlm, mode, tokens, logits);
+    free(xl);
     free(x);
     free(h);
-    free(qkv);
     free(q);
     free(k);
     free(v);
@@ -839,6 +934,67 @@ int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned posit
     free(gu);
     free(mid);
     free(tmp);
+}
+
+int ref_forward(ref_model *m, const uint32_t *ids, unsigned rows, unsigned position, uint32_t *token,
+                float *logits) {
+    if (position != m->position || rows == 0 || position + rows > m->capacity) return -8;
+    for (unsigned r = 0; r < rows; ++r)
+        if (ids[r] >= VOC) return -1;
+    uint32_t *pos = (uint32_t *)malloc(rows * sizeof(uint32_t));
+    uint32_t *slot = (uint32_t *)calloc(rows, sizeof(uint32_t));
+    for (unsigned r = 0; r < rows; ++r) pos[r] = position + r;
+    const uint32_t last = rows - 1;
+    uint32_t tok = 0;
+    run_rows(m, rows, ids, pos, slot, 1, &last, &tok, logits);
+    m->position = position + rows;
+    if (token) *token = tok;
     free(pos);
+    free(slot);
     return 0;
 }
+
+int ref_decode_batch(ref_model *m, unsigned n, const uint32_t *slots, const uint32_t *ids, uint32_t *tokens,
+                     float *logits) {
+    if (!n || !(m->mode & REF_KV8)) return -1;
+    uint32_t *pos = (uint32_t *)malloc(n * sizeof(uint32_t));
+    uint32_t *rows = (uint32_t *)malloc(n * sizeof(uint32_t));
+    char *seen = (char *)calloc(m->nslots, 1);
+    int rc = 0;
+    for (unsigned r = 0; r < n && !rc; ++r) {
+        if (slots[r] >= m->nslots || seen[slots[r]] || ids[r] >= VOC) rc = -1;
+        else {
+            seen[slots[r]] = 1;
+            pos[r] = slots[r] == 0 ? m->position : m->spos[slots[r]];
+            if (pos[r] >= m->capacity) rc = -8;
+        }
+        rows[r] = r;
+    }
+    if (!rc) {
+        run_rows(m, n, ids, pos, slots, n, rows, tokens, logits);
+        for (unsigned r = 0; r < n; ++r) {
+            if (slots[r] == 0)
+                m->position += 1;
+            else
+                m->spos[slots[r]] += 1;
+        }
+    }
+    free(pos);
+    free(rows);
+    free(seen);
+    return rc;
+}
+
+int ref_synth_write(const char *root, uint64_t seed) {
+    qa_model m;
+    if (qa_alloc(&m)) {
+        qa_free(&m);
+        return -6;
+    }
+    qa_generate(seed, &m);
+    const int rc = qa_write(&m, root, seed);
+    qa_free(&m);
+    return rc;
+}
+
+void ref_synth_prompt(uint64_t seed, unsigned n, uint32_t *ids) { qa_prompt(seed, n, ids); }

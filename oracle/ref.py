@@ -64,6 +64,11 @@ def lib():
             'ref_swiglu': (None, [_PF, _PF, ctypes.c_uint, ctypes.c_uint, _PF]),
             'ref_lm_head': (c_uint32, [c_void_p, _PF, ctypes.c_uint, _PF]),
             'ref_fill_kv_synthetic': (c_int, [c_void_p, ctypes.c_uint, ctypes.c_uint64]),
+            'ref_set_slots': (c_int, [c_void_p, ctypes.c_uint]),
+            'ref_synth_write': (c_int, [c_char_p, ctypes.c_uint64]),
+            'ref_synth_prompt': (None, [ctypes.c_uint64, ctypes.c_uint, _P32]),
+            'ref_fill_kv_synthetic_slot': (c_int, [c_void_p, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint64]),
+            'ref_decode_batch': (c_int, [c_void_p, ctypes.c_uint, _P32, _P32, _P32, _PF]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -98,6 +103,19 @@ def f32_to_bf16_bits(a):
     bits = a.view(np.uint32)
     assert not (bits & 0xffff).any(), 'array is not bf16-valued'
     return (bits >> 16).astype(np.uint16)
+
+
+def synth_write(root, seed):
+    """Writes the seeded synthetic model in the reference's SD format."""
+    rc = lib().ref_synth_write(str(root).encode(), seed)
+    if rc:
+        raise RuntimeError(f'synthetic asset writer failed ({rc})')
+
+
+def synth_prompt(seed, n):
+    ids = np.empty(n, np.uint32)
+    lib().ref_synth_prompt(seed, n, p32(ids))
+    return ids
 
 
 class RefModel:
@@ -148,6 +166,29 @@ class RefModel:
     def fill_kv_synthetic(self, length, seed):
         if lib().ref_fill_kv_synthetic(self.h, length, seed):
             raise ValueError('length exceeds capacity')
+
+    def set_slots(self, nslots):
+        """KV8 caches for nslots independent sequences (slot 0 = the forward() sequence)."""
+        if lib().ref_set_slots(self.h, nslots):
+            raise MemoryError(f'oracle could not hold {nslots} sequences')
+        self.nslots = nslots
+
+    def fill_kv_synthetic_slot(self, slot, length, seed):
+        if lib().ref_fill_kv_synthetic_slot(self.h, slot, length, seed):
+            raise ValueError('bad slot or length')
+
+    def decode_batch(self, slots, ids, want_logits=False):
+        """One decode step of distinct slots (one token each, at each slot's
+        position); returns the tokens and, optionally, logits [n][151936]."""
+        slots = np.ascontiguousarray(slots, dtype=np.uint32)
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        toks = np.empty(len(slots), np.uint32)
+        logits = np.empty((len(slots), VOCAB), np.float32) if want_logits else None
+        rc = lib().ref_decode_batch(self.h, len(slots), p32(slots), p32(ids), p32(toks),
+                                    pf(logits) if want_logits else None)
+        if rc:
+            raise ValueError(f'oracle decode_batch failed ({rc})')
+        return toks, logits
 
     def kv8_state(self, layer):
         n = self.position
