@@ -516,9 +516,12 @@ int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots,
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
         return -1;  // 16-byte q loads and bulk copies of the code rows
     if (reinterpret_cast<uintptr_t>(ctx) & 7) return -1;
+    if (!err && cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_attn_op_err) != cudaSuccess) return -3;
+    // contexts up to 8 x 2304 keys: scores in registers (attention_rs.cu)
+    const int rc = launch_attention_rs(q, rows, slots, positions, max_len, kc, ks, vc, vs, cap, ctx, err, st);
+    if (rc != 1) return rc;
     int splits, kpc;
     if (attention_cluster_plan(rows, max_len, &splits, &kpc)) return -1;
-    if (!err && cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_attn_op_err) != cudaSuccess) return -3;
     AcArgs a;
     a.q = q;
     a.slots = slots;

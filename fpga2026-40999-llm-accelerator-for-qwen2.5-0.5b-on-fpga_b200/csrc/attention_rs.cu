@@ -1,0 +1,548 @@
+// GQA decode/prefill attention over the KV8 cache with the scores held in
+// registers: one CTA (or a thread-block cluster of up to 8 CTAs splitting the
+// context) per (query row, KV head), 12 warps.
+// Arithmetic: the oracle's REF_KV8 | REF_EXACT attention, the same as
+// attention_cluster.cu (legacy_100mhz_closed/src/PC/model_backend.py:97-102 in
+// the accelerator's order, src/rtl/kv8_score_scale8.sv:6-12 for the K scale,
+// src/rtl/kv8_v_pscale.sv:1-20 for the V scale), every sum exact:
+//   S[h][t] = bf16(RN32(RN32(Q_h . kcode[t]) * 2^(E_h-26) * kscale[t]) / 8)
+//   E[h][t] = qexp(S[h][t] - max_t S[h]),  Z_h = RN32(sum_t rint(E * 2^40)) 2^-40
+//   W[h][t] = rint(RN32(bf16(E / Z_h) * vscale[t]) * 2^(26-F_h))
+//   ctx[h]  = bf16(RN32(sum_t W[h][t] * vcode[t]) * 2^(F_h-26))
+// so the context is bit-identical to the oracle's whatever the split.
+//
+// Layout of the work. A chunk is 192 keys, one 16-key block per warp; warp w
+// owns block w of every chunk of its CTA's key range (at most 12 chunks, 2304
+// keys, per CTA).
+//   scores   computed transposed on the tensor cores, D[16][8 keys] =
+//            Qlimb[16][64] . Kcode^T (m16n8k32, s8): rows 0-7 of m-tile 0
+//            are limb 0 of heads 0-6 (row 7 unused), rows 8-15 limb 1; m-tile
+//            1 holds limbs 2 and 3. Lane (g, i) then holds all four limbs of
+//            head g for keys 2i, 2i+1 of each 8-key n-tile and folds them in
+//            registers; its four keys of a block, {2i, 2i+1, 8+2i, 9+2i}, are
+//            exactly the k slots it supplies to the P.V product below, so a
+//            lane only ever reads back its own scores: they are kept in shared
+//            memory as one float4 per lane and chunk (lane-private,
+//            conflict-free, no exchange between warps).
+//   softmax  per-head max and exact sum: lanes -> warp (shuffles) -> CTA
+//            (shared memory) -> cluster (distributed shared memory)
+//   context  D[16 dims][8 heads] += Vcode^T[16][16 keys] . Wbyte[16][8]
+//            (m16n8k16, s8 x u8): W >= 0 split into four byte planes, the V
+//            codes transposed 4 x 4 bytes with byte permutes; int32 per plane,
+//            folded to int64 at the end, warps then cluster ranks added.
+// Memory: the K chunks and then the V chunks stream through one 6-slot ring
+// of bulk copies completing on mbarriers. There is no producer warp and no
+// CTA-wide barrier in the loops: each warp counts its release of a slot on an
+// acquire-release shared-memory counter and the warp that releases it last
+// refills it six items ahead. The chunk loops are not unrolled: a kernel
+// that kept the scores in registers (unrolling every chunk) measured 33 us
+// at 64 rows x 2049 keys, its warps stalled on instruction fetch. Every wait
+// is bounded (error codes 32-33).
+#include "common.cuh"
+#include "kernels.h"
+#include "tc05.cuh"
+
+namespace qb {
+
+constexpr int AR_WARPS = 12;
+constexpr int AR_THREADS = 32 * AR_WARPS;
+constexpr int AR_NB = 12;                          // chunks (blocks per warp) per CTA at most
+constexpr int AR_CHUNK = 16 * AR_WARPS;            // keys per chunk
+constexpr int AR_CHUNK_BYTES = AR_CHUNK * QB_HD;   // 12 KB of codes
+constexpr int AR_MAX_KPC = AR_CHUNK * AR_NB;       // 2304 keys per CTA
+constexpr int AR_RING = 6;                         // ring slots (K chunks, then V chunks)
+constexpr int AR_MAX_SPLITS = 8;
+constexpr int AR_SMS = 148;
+constexpr int AR_STAGE_LOADS = (AR_MAX_KPC + AR_THREADS - 1) / AR_THREADS;  // scale loads per thread
+
+struct ArArgs {
+    const uint16_t *q;
+    const uint32_t *slots, *positions;
+    const int8_t *kc, *vc;
+    const float *ks, *vs;
+    int cap;
+    uint16_t *ctx;
+    int kpc;  // keys per CTA (multiple of AR_CHUNK)
+    unsigned *err;
+};
+
+// ring [6][192][64] int8 (reused for the per-warp context partials
+// [12][8][64] int64) | S [12 warps][12 chunks][32 lanes] float4 | K scales
+// [kpc] | V scales [kpc] | stat: max[8] (slot 7: largest V scale) | Z[8]
+// int64 | inv, s1, s2, F [4][8] | context partial [7][64] int64 | per-warp
+// max [12][8], Z [12][8] int64, V-scale max [12] | slot release counters [6]
+// | mbarriers [6]
+struct ArSmem {
+    int ring, s, kss, vss, stat, red, bars, total;
+};
+constexpr int AR_ST_Z = 32, AR_ST_HV = 96, AR_ST_CTX = 224;
+constexpr int AR_STAT_BYTES = AR_ST_CTX + 7 * QB_HD * 8;
+constexpr int AR_RED_BYTES = AR_WARPS * 8 * 4 + AR_WARPS * 8 * 8 + AR_WARPS * 4 + AR_RING * 4;
+__host__ __device__ inline ArSmem ar_smem(int kpc) {
+    ArSmem L;
+    L.ring = 0;
+    L.s = L.ring + AR_RING * AR_CHUNK_BYTES;
+    L.kss = L.s + AR_WARPS * AR_NB * 32 * 16;
+    L.vss = L.kss + kpc * 4;
+    L.stat = L.vss + kpc * 4;
+    L.red = L.stat + AR_STAT_BYTES;
+    L.bars = (L.red + AR_RED_BYTES + 7) & ~7;
+    L.total = L.bars + AR_RING * 8;
+    return L;
+}
+static_assert(AR_WARPS * 8 * QB_HD * 8 <= AR_RING * AR_CHUNK_BYTES, "context partials fit in the ring");
+static_assert(AR_STAT_BYTES % 16 == 0 && AR_RED_BYTES % 8 == 0, "aligned sub-areas");
+
+__device__ __forceinline__ void ar_mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ar_mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ uint32_t ar_prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+// 4 x 4 byte transpose: o[j] byte i = r[i] byte j.
+__device__ __forceinline__ void ar_transpose4(const uint32_t (&r)[4], uint32_t (&o)[4]) {
+    const uint32_t t0 = ar_prmt(r[0], r[1], 0x5140u), t1 = ar_prmt(r[0], r[1], 0x7362u);
+    const uint32_t t2 = ar_prmt(r[2], r[3], 0x5140u), t3 = ar_prmt(r[2], r[3], 0x7362u);
+    o[0] = ar_prmt(t0, t2, 0x5410u);
+    o[1] = ar_prmt(t0, t2, 0x7632u);
+    o[2] = ar_prmt(t1, t3, 0x5410u);
+    o[3] = ar_prmt(t1, t3, 0x7632u);
+}
+// One fp32 of CTA `rank`'s shared memory at this CTA's address of it.
+__device__ __forceinline__ float ar_ld_dsmem(uint32_t local_saddr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+// *p += 1 with acquire-release order at CTA scope; returns the old value.
+__device__ __forceinline__ unsigned ar_release_count(unsigned *p) {
+    unsigned old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;" : "=r"(old) : "r"(tc::smem_u32(p)) : "memory");
+    return old;
+}
+
+template <bool CLUSTER>
+__global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int kpc = a.kpc;
+    const ArSmem L = ar_smem(kpc);
+    uint8_t *ring = sm + L.ring;
+    float4 *S = reinterpret_cast<float4 *>(sm + L.s);
+    float *kss = reinterpret_cast<float *>(sm + L.kss);
+    float *vss = reinterpret_cast<float *>(sm + L.vss);
+    float *stat = reinterpret_cast<float *>(sm + L.stat);
+    long long *statz = reinterpret_cast<long long *>(sm + L.stat + AR_ST_Z);
+    float *hv = reinterpret_cast<float *>(sm + L.stat + AR_ST_HV);
+    long long *ctxp = reinterpret_cast<long long *>(sm + L.stat + AR_ST_CTX);
+    float *red_m = reinterpret_cast<float *>(sm + L.red);
+    long long *red_z = reinterpret_cast<long long *>(sm + L.red + AR_WARPS * 8 * 4);
+    float *red_v = reinterpret_cast<float *>(sm + L.red + AR_WARPS * 8 * 12);
+    unsigned *released = reinterpret_cast<unsigned *>(sm + L.red + AR_WARPS * 8 * 12 + AR_WARPS * 4);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + L.bars);
+    long long *part = reinterpret_cast<long long *>(sm + L.ring);  // after the last chunk
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int kvh = blockIdx.y, r = blockIdx.z;
+    const int rank = CLUSTER ? (int)tc::cluster_rank() : 0;
+    const int nranks = CLUSTER ? (int)gridDim.x : 1;
+    float4 *Sl = S + warp * AR_NB * 32 + lane;  // this lane's scores, one float4 per chunk (stride 32)
+
+    if (tid == 0) {
+        for (int i = 0; i < AR_RING; ++i) {
+            tc::mbar_init(&full[i], 1);
+            released[i] = 0;
+        }
+        tc::mbar_fence_init();
+    }
+    pdl_wait();  // q, positions and the newest cache entries come from earlier kernels
+    pdl_trigger();
+    const int L_row = (int)a.positions[r] + 1;
+    const int slot = (int)a.slots[r];
+    const int t_begin = rank * kpc;
+    const int nkeys = max(0, min(L_row, t_begin + kpc) - t_begin);
+    const int nchunks = (nkeys + AR_CHUNK - 1) / AR_CHUNK;
+    const int items = 2 * nchunks;  // ring items: K chunks 0..n-1, then V chunks
+    const size_t kvbase = ((size_t)slot * QB_KVH + kvh) * a.cap + t_begin;  // first key of this CTA
+    __syncthreads();  // barriers and counters initialised
+    const int8_t *kg = a.kc + kvbase * QB_HD;
+    const int8_t *vg = a.vc + kvbase * QB_HD;
+    auto issue = [&](int i) {
+        const int c = i < nchunks ? i : i - nchunks, sl = i % AR_RING;
+        const uint32_t bytes = (uint32_t)(min(AR_CHUNK, nkeys - c * AR_CHUNK) * QB_HD);
+        tc::mbar_arrive_expect_tx(&full[sl], bytes);
+        tc::bulk_load(ring + sl * AR_CHUNK_BYTES, (i < nchunks ? kg : vg) + (size_t)c * AR_CHUNK_BYTES, bytes,
+                      &full[sl]);
+    };
+    // this warp is done reading item i's slot; the last warp to say so
+    // refills it with item i + AR_RING
+    auto release = [&](int i) {
+        __syncwarp();
+        if (lane == 0 && ar_release_count(&released[i % AR_RING]) == AR_WARPS - 1) {
+            atomicExch(&released[i % AR_RING], 0u);
+            tc::fence_proxy_async_smem();  // generic reads of the slot before the bulk copy's writes
+            if (i + AR_RING < items) issue(i + AR_RING);
+        }
+    };
+    if (tid == 0)
+        for (int i = 0; i < min(AR_RING, items); ++i) issue(i);
+
+    // ---------------- stage the scales (every load in flight at once), q as int8 limbs
+    float vmax = 0.f;
+    {
+        float kv[AR_STAGE_LOADS], vv[AR_STAGE_LOADS];
+#pragma unroll
+        for (int j = 0; j < AR_STAGE_LOADS; ++j) {
+            const int t = tid + j * AR_THREADS;
+            kv[j] = t < nkeys ? __ldg(a.ks + kvbase + t) : 0.f;
+            vv[j] = t < nkeys ? __ldg(a.vs + kvbase + t) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < AR_STAGE_LOADS; ++j) {
+            const int t = tid + j * AR_THREADS;
+            if (t < nkeys) {
+                kss[t] = kv[j];
+                vss[t] = vv[j];
+                vmax = fmaxf(vmax, vv[j]);
+            }
+        }
+    }
+    // q of head g = gid, dims 16 tig .. 16 tig + 15, aligned to the head's
+    // largest exponent E as 28-bit integers split into four signed 7-bit limbs;
+    // word i of limb plane l holds dims 16 tig + 4i .. +3 (the same dims the
+    // lane's K words cover, so q and K share one k-slot permutation)
+    uint32_t qa[2][2][4];  // [m-tile: limbs 0,1 | 2,3][k step][a0..a3]
+    int e_g;
+    {
+        uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+        if (gid < 7) {
+            const uint4 *qp =
+                reinterpret_cast<const uint4 *>(a.q + (size_t)r * QB_HID + (kvh * 7 + gid) * QB_HD + 16 * tig);
+            q0 = qp[0];
+            q1 = qp[1];
+        }
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        float qf[16];
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            qf[2 * i] = bflo(w[i]);
+            qf[2 * i + 1] = bfhi(w[i]);
+            amax = fmaxf(amax, fmaxf(fabsf(qf[2 * i]), fabsf(qf[2 * i + 1])));
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        e_g = row_exponent(amax);
+        uint32_t lb[4][4] = {};  // [limb][word of 4 dims]
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            int l4[4];
+            limbs4(align28_int(qf[i], e_g), l4);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) lb[l][i >> 2] |= ((uint32_t)l4[l] & 0xffu) << (8 * (i & 3));
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+                qa[mt][s][0] = lb[2 * mt][2 * s];
+                qa[mt][s][1] = lb[2 * mt + 1][2 * s];
+                qa[mt][s][2] = lb[2 * mt][2 * s + 1];
+                qa[mt][s][3] = lb[2 * mt + 1][2 * s + 1];
+            }
+    }
+    __syncthreads();  // staged scales visible to every warp
+    bool ok = true;
+
+    // ---------------- phase 1: scores of this warp's blocks -> Sl[c]
+    // Sl[c] = head gid, keys 192 c + 16 warp + {2tig, 2tig+1, 8+2tig, 9+2tig}
+    float mrun = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+        const int sl = c % AR_RING;
+        if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(c / AR_RING) & 1u, a.err, 32);
+        const int kb = c * AR_CHUNK + 16 * warp;  // first key of this warp's block
+        float sc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (ok && kb < nkeys) {
+            const int8_t *blk = reinterpret_cast<const int8_t *>(ring + sl * AR_CHUNK_BYTES) + 16 * warp * QB_HD;
+            int d[2][2][4];  // [n-tile][m-tile][fragment]
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(blk + (8 * nt + gid) * QB_HD + 16 * tig);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    d[nt][mt][0] = d[nt][mt][1] = d[nt][mt][2] = d[nt][mt][3] = 0;
+                    ar_mma_s8(d[nt][mt], qa[mt][0][0], qa[mt][0][1], qa[mt][0][2], qa[mt][0][3], u.x, u.y);
+                    ar_mma_s8(d[nt][mt], qa[mt][1][0], qa[mt][1][1], qa[mt][1][2], qa[mt][1][3], u.z, u.w);
+                }
+            }
+            const float2 k01 = *reinterpret_cast<const float2 *>(kss + kb + 2 * tig);
+            const float2 k23 = *reinterpret_cast<const float2 *>(kss + kb + 8 + 2 * tig);
+            const float kk[4] = {k01.x, k01.y, k23.x, k23.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int nt = i >> 1, cc = i & 1;
+                const int key = kb + 8 * nt + 2 * tig + cc;
+                // per-limb sums over 64 dims are below 2^20: pairs add in int32
+                const long long dot = (long long)(d[nt][0][cc] + d[nt][0][cc + 2] * 128) +
+                                      (long long)(d[nt][1][cc] + d[nt][1][cc + 2] * 128) * 16384ll;
+                const float v = rbf(__fmul_rn(unalign28(dot, e_g), kk[i]) * 0.125f);
+                sc[i] = key < nkeys ? v : -INFINITY;
+                mrun = fmaxf(mrun, sc[i]);
+            }
+        }
+        Sl[c * 32] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+        release(c);
+    }
+    // per-head max: the four lanes of a group hold the same head
+    mrun = fmaxf(mrun, __shfl_xor_sync(0xffffffffu, mrun, 1));
+    mrun = fmaxf(mrun, __shfl_xor_sync(0xffffffffu, mrun, 2));
+    vmax = warp_max(vmax);
+    if (tig == 0) red_m[warp * 8 + gid] = mrun;
+    if (lane == 0) red_v[warp] = vmax;
+    __syncthreads();
+    if (tid < 8) {
+        float m = -INFINITY;
+        if (tid < 7) {
+            for (int w = 0; w < AR_WARPS; ++w) m = fmaxf(m, red_m[w * 8 + tid]);
+        } else {
+            m = 0.f;
+            for (int w = 0; w < AR_WARPS; ++w) m = fmaxf(m, red_v[w]);
+        }
+        stat[tid] = m;
+    }
+    float Mg, Mv;  // the row's max of head gid; its largest V scale
+    if constexpr (CLUSTER) {
+        tc::cluster_sync();  // (1)
+        const uint32_t sa = tc::smem_u32(stat);
+        Mg = -INFINITY;
+        Mv = 0.f;
+        for (int sr = 0; sr < nranks; ++sr) {
+            Mg = fmaxf(Mg, ar_ld_dsmem(sa + 4u * (uint32_t)gid, sr));
+            Mv = fmaxf(Mv, ar_ld_dsmem(sa + 28u, sr));
+        }
+    } else {
+        __syncthreads();
+        Mg = stat[gid];
+        Mv = stat[7];
+    }
+
+    // ---------------- phase 2: E = qexp(S - max) in place, exact sums
+    long long z = 0;
+#pragma unroll 2
+    for (int c = 0; c < nchunks; ++c) {
+        const float4 s4 = Sl[c * 32];
+        const float e0 = qexp(__fsub_rn(s4.x, Mg)), e1 = qexp(__fsub_rn(s4.y, Mg));
+        const float e2 = qexp(__fsub_rn(s4.z, Mg)), e3 = qexp(__fsub_rn(s4.w, Mg));
+        z += rint_2p40(e0) + rint_2p40(e1) + rint_2p40(e2) + rint_2p40(e3);
+        Sl[c * 32] = make_float4(e0, e1, e2, e3);
+    }
+    z += __shfl_xor_sync(0xffffffffu, z, 1);
+    z += __shfl_xor_sync(0xffffffffu, z, 2);
+    if (tig == 0) red_z[warp * 8 + gid] = z;
+    __syncthreads();
+    if (tid < 8) {
+        long long zz = 0;
+        for (int w = 0; w < AR_WARPS; ++w) zz += red_z[w * 8 + tid];
+        statz[tid] = zz;
+    }
+    if constexpr (CLUSTER) {
+        tc::cluster_sync();  // (2)
+    } else {
+        __syncthreads();
+    }
+    // per-head 1/Z, the bound of w and its alignment factors (every CTA of
+    // the cluster forms the same values from the same totals)
+    if (tid < 8) {
+        long long zt = 0;
+        if constexpr (CLUSTER) {
+            const uint32_t za = tc::smem_u32(statz) + 8u * (uint32_t)(tid & ~1);
+            for (int sr = 0; sr < nranks; ++sr) {
+                const float4 v = tc::ld_dsmem_f4(za, sr);
+                const longlong2 zz = *reinterpret_cast<const longlong2 *>(&v);
+                zt += (tid & 1) ? zz.y : zz.x;
+            }
+        } else {
+            zt = statz[tid];
+        }
+        float inv = 0.f, s1 = 0.f, s2 = 0.f;
+        int f = 0;
+        if (tid < 7 && zt > 0) {
+            inv = __fdiv_rn(1.0f, __fmul_rn(__ll2float_rn(zt), 0x1p-40f));
+            f = row_exponent(__fmul_rn(rbf(inv), Mv));
+            const int sh = 26 - f, sh1 = min(sh, 127);
+            s1 = pow2i(sh1);
+            s2 = pow2i(sh - sh1);
+        }
+        hv[tid] = inv;
+        hv[8 + tid] = s1;
+        hv[16 + tid] = s2;
+        hv[24 + tid] = __int_as_float(f);
+    }
+    __syncthreads();
+
+    // ---------------- phase 3: context on the tensor cores, V from the ring
+    const float inv_g = hv[gid], s1_g = hv[8 + gid], s2_g = hv[16 + gid];
+    const bool gv = gid < 7;
+    int acc[4][4][4];  // [m-tile j: dims 4gid+j | 32+4gid+j][byte plane l][fragment]
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int l = 0; l < 4; ++l) acc[j][l][0] = acc[j][l][1] = acc[j][l][2] = acc[j][l][3] = 0;
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+        const int item = nchunks + c, sl = item % AR_RING;
+        if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(item / AR_RING) & 1u, a.err, 33);
+        const int kb = c * AR_CHUNK + 16 * warp;
+        if (ok && kb < nkeys) {
+            const float4 e4 = Sl[c * 32];
+            const float2 v01 = *reinterpret_cast<const float2 *>(vss + kb + 2 * tig);
+            const float2 v23 = *reinterpret_cast<const float2 *>(vss + kb + 8 + 2 * tig);
+            const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, vv[4] = {v01.x, v01.y, v23.x, v23.y};
+            const int koff[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
+            uint32_t wq[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float w = (gv && kb + koff[i] < nkeys) ? __fmul_rn(rbf(__fmul_rn(ev[i], inv_g)), vv[i]) : 0.f;
+                wq[i] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1_g), s2_g));
+            }
+            ar_transpose4(wq, b);
+            const uint32_t *vb =
+                reinterpret_cast<const uint32_t *>(ring + sl * AR_CHUNK_BYTES) + 16 * warp * (QB_HD / 4);
+            uint32_t rl[4], rh[4], alo[4], ahi[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                rl[i] = vb[koff[i] * (QB_HD / 4) + gid];
+                rh[i] = vb[koff[i] * (QB_HD / 4) + gid + 8];
+            }
+            ar_transpose4(rl, alo);
+            ar_transpose4(rh, ahi);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int l = 0; l < 4; ++l) ar_mma_s8u8(acc[j][l], alo[j], ahi[j], b[l]);
+        }
+        release(item);
+    }
+
+    // ---------------- phase 4: byte planes -> int64, warps -> CTA -> rank 0
+    tc::fence_proxy_async_smem();  // the ring (bulk-copy writes) becomes generic int64 partials
+    __syncthreads();               // every warp is past its last read of the ring
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            const long long v = (long long)acc[j][0][cc] + (long long)acc[j][1][cc] * 256ll +
+                                (long long)acc[j][2][cc] * 65536ll + (long long)acc[j][3][cc] * 16777216ll;
+            const int h = 2 * tig + (cc & 1), d = 4 * gid + 32 * (cc >> 1) + j;
+            part[(warp * 8 + h) * QB_HD + d] = v;
+        }
+    __syncthreads();
+    for (int i = tid; i < 7 * QB_HD; i += AR_THREADS) {
+        const int h = i >> 6, d = i & 63;
+        long long sum = 0;
+#pragma unroll
+        for (int w = 0; w < AR_WARPS; ++w) sum += part[(w * 8 + h) * QB_HD + d];
+        ctxp[i] = sum;
+    }
+    if constexpr (CLUSTER) {
+        tc::cluster_sync();  // (3)
+        if (rank == 0) {
+            const uint32_t ca = tc::smem_u32(ctxp);
+            for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += AR_THREADS) {
+                long long s0 = 0, s1 = 0;
+                for (int sr = 0; sr < nranks; ++sr) {
+                    const float4 v = tc::ld_dsmem_f4(ca + 16u * i2, sr);
+                    const longlong2 pp = *reinterpret_cast<const longlong2 *>(&v);
+                    s0 += pp.x;
+                    s1 += pp.y;
+                }
+                const int i = 2 * i2, h = i >> 6, d = i & 63;
+                const int f = __float_as_int(hv[24 + h]);
+                *reinterpret_cast<uint32_t *>(a.ctx + (size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d) =
+                    (uint32_t)f2bf(unalign28(s0, f)) | ((uint32_t)f2bf(unalign28(s1, f)) << 16);
+            }
+        }
+        tc::cluster_sync();  // (4) peers' shared memory stays alive until rank 0 has read it
+    } else {
+        __syncthreads();
+        for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += AR_THREADS) {
+            const int i = 2 * i2, h = i >> 6, d = i & 63;
+            const int f = __float_as_int(hv[24 + h]);
+            *reinterpret_cast<uint32_t *>(a.ctx + (size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d) =
+                (uint32_t)f2bf(unalign28(ctxp[i], f)) | ((uint32_t)f2bf(unalign28(ctxp[i + 1], f)) << 16);
+        }
+    }
+}
+
+// Split plan: one CTA per SM when rows are few (contexts split up to 8 ways),
+// at least enough CTAs to keep each within AR_MAX_KPC keys. Returns -1 when
+// a row needs more than 8 CTAs (the caller uses the shared-memory-score
+// kernel, which holds 4096 keys per CTA).
+int attention_rs_plan(int rows, int max_len, int *splits, int *kpc) {
+    if (max_len <= 0 || rows <= 0) return -1;
+    const int chunks = (max_len + AR_CHUNK - 1) / AR_CHUNK;
+    int s = AR_SMS / (2 * rows);
+    s = s < 1 ? 1 : (s > AR_MAX_SPLITS ? AR_MAX_SPLITS : s);
+    s = s > chunks ? chunks : s;
+    const int need = (chunks + AR_NB - 1) / AR_NB;
+    s = s < need ? need : s;
+    if (s > AR_MAX_SPLITS) return -1;
+    const int cpc = (chunks + s - 1) / s;  // chunks per CTA
+    *kpc = cpc * AR_CHUNK;
+    *splits = (chunks + cpc - 1) / cpc;
+    return 0;
+}
+
+template <bool CLUSTER>
+static int run_ar(const ArArgs &a, int rows, int splits, cudaStream_t st) {
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << (dev & 31)))) {
+        if (cudaFuncSetAttribute(attn_rs_kernel<CLUSTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ar_smem(AR_MAX_KPC).total) != cudaSuccess)
+            return -3;
+        configured |= 1u << (dev & 31);
+    }
+    return launch_pdl(attn_rs_kernel<CLUSTER>, dim3(splits, QB_KVH, rows), dim3(AR_THREADS),
+                      (size_t)ar_smem(a.kpc).total, st, CLUSTER ? (unsigned)splits : 1u, a);
+}
+
+// 0 when launched; 1 when the context needs the shared-memory-score kernel.
+int launch_attention_rs(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
+                        const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
+                        unsigned *err, cudaStream_t st) {
+    int splits, kpc;
+    if (attention_rs_plan(rows, max_len, &splits, &kpc)) return 1;
+    ArArgs a;
+    a.q = q;
+    a.slots = slots;
+    a.positions = positions;
+    a.kc = kc;
+    a.vc = vc;
+    a.ks = ks;
+    a.vs = vs;
+    a.cap = cap;
+    a.ctx = ctx;
+    a.kpc = kpc;
+    a.err = err;
+    return splits > 1 ? run_ar<true>(a, rows, splits, st) : run_ar<false>(a, rows, 1, st);
+}
+
+}  // namespace qb

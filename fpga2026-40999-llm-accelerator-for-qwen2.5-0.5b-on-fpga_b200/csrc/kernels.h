@@ -94,6 +94,13 @@ int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const u
 int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions,
                              int max_len, const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap,
                              uint16_t *ctx, unsigned *err, cudaStream_t st);
+// The same attention with the scores held in registers (one CTA of 12 + 1
+// warps per (row, KV head), up to 8 per row for long contexts); 0 when
+// launched, 1 when a row needs more than 8 x 2304 keys per cluster (the
+// caller then uses the kernel above), negative on a launch error.
+int launch_attention_rs(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
+                        const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
+                        unsigned *err, cudaStream_t st);
 
 int launch_embed(const uint16_t *embed, const uint32_t *ids, int rows, uint16_t *x, cudaStream_t st);
 int launch_rmsnorm(const uint16_t *x, const uint16_t *gamma, int rows, float eps, uint16_t *out, cudaStream_t st);
