@@ -30,11 +30,13 @@
 //            (m16n8k16, s8 x u8): W >= 0 split into four byte planes, the V
 //            codes transposed 4 x 4 bytes with byte permutes; int32 per plane,
 //            folded to int64 at the end, warps then cluster ranks added.
-// Memory: the K chunks and then the V chunks stream through one 6-slot ring
-// of bulk copies completing on mbarriers. There is no producer warp and no
+// Memory: the K chunks and then the V chunks stream through one 8-slot ring
+// of bulk copies completing on mbarriers; a K chunk's item also copies the
+// chunk's K and V scales into shared memory (when the cache rows are 16-byte
+// aligned; otherwise every thread stages them with plain loads first). There is no producer warp and no
 // CTA-wide barrier in the loops: each warp counts its release of a slot on an
 // acquire-release shared-memory counter and the warp that releases it last
-// refills it six items ahead. The chunk loops are not unrolled: a kernel
+// refills it eight items ahead. The chunk loops are not unrolled: a kernel
 // that kept the scores in registers (unrolling every chunk) measured 33 us
 // at 64 rows x 2049 keys, its warps stalled on instruction fetch. Every wait
 // is bounded (error codes 32-33).
@@ -50,7 +52,7 @@ constexpr int AR_NB = 12;                          // chunks (blocks per warp) p
 constexpr int AR_CHUNK = 16 * AR_WARPS;            // keys per chunk
 constexpr int AR_CHUNK_BYTES = AR_CHUNK * QB_HD;   // 12 KB of codes
 constexpr int AR_MAX_KPC = AR_CHUNK * AR_NB;       // 2304 keys per CTA
-constexpr int AR_RING = 6;                         // ring slots (K chunks, then V chunks)
+constexpr int AR_RING = 8;                         // ring slots (K chunks, then V chunks)
 constexpr int AR_MAX_SPLITS = 8;
 constexpr int AR_SMS = 148;
 constexpr int AR_STAGE_LOADS = (AR_MAX_KPC + AR_THREADS - 1) / AR_THREADS;  // scale loads per thread
@@ -66,12 +68,12 @@ struct ArArgs {
     unsigned *err;
 };
 
-// ring [6][192][64] int8 (reused for the per-warp context partials
+// ring [8][192][64] int8 (reused for the per-warp context partials
 // [12][8][64] int64) | S [12 warps][12 chunks][32 lanes] float4 | K scales
 // [kpc] | V scales [kpc] | stat: max[8] (slot 7: largest V scale) | Z[8]
 // int64 | inv, s1, s2, F [4][8] | context partial [7][64] int64 | per-warp
-// max [12][8], Z [12][8] int64, V-scale max [12] | slot release counters [6]
-// | mbarriers [6]
+// max [12][8], Z [12][8] int64, V-scale max [12] | slot release counters [8]
+// | mbarriers [8]
 struct ArSmem {
     int ring, s, kss, vss, stat, red, bars, total;
 };
@@ -136,6 +138,63 @@ __device__ __forceinline__ unsigned ar_release_count(unsigned *p) {
     return old;
 }
 
+// Packed pairs of fp32 (Blackwell's f32x2 arithmetic: two IEEE fp32
+// operations, each rounded to nearest even, in one instruction).
+__device__ __forceinline__ unsigned long long ar_pk(float lo, float hi) {
+    unsigned long long d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void ar_unpk(unsigned long long v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long ar_add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long ar_mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long ar_fma2(unsigned long long a, unsigned long long b,
+                                                      unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long ar_dup(float v) { return ar_pk(v, v); }
+
+// qexp (common.cuh) of two values at once, operation for operation: the
+// same IEEE fp32 operations in the same order on each half (a - b taken as
+// a + (-b) and fma(-n, c, x) as fma(n, -c, x), which are the same IEEE
+// results), so each half is bit-identical to qexp of that value.
+__device__ __forceinline__ void ar_qexp2(float x0, float x1, float &e0, float &e1) {
+    const unsigned long long x = ar_pk(x0, x1);
+    const unsigned long long sh = ar_add2(ar_mul2(x, ar_dup(1.44269504f)), ar_dup(12582912.0f));
+    const unsigned long long n = ar_add2(sh, ar_dup(-12582912.0f));
+    unsigned long long r = ar_fma2(n, ar_dup(-0.693145751953125f), x);
+    r = ar_fma2(n, ar_dup(-1.42860677e-6f), r);
+    unsigned long long q = ar_dup(1.98412698e-4f);
+    q = ar_fma2(q, r, ar_dup(1.38888889e-3f));
+    q = ar_fma2(q, r, ar_dup(8.33333333e-3f));
+    q = ar_fma2(q, r, ar_dup(4.16666667e-2f));
+    q = ar_fma2(q, r, ar_dup(1.66666667e-1f));
+    q = ar_fma2(q, r, ar_dup(0.5f));
+    q = ar_fma2(q, r, ar_dup(1.0f));
+    q = ar_fma2(q, r, ar_dup(1.0f));
+    float s0, s1;
+    ar_unpk(sh, s0, s1);
+    const int ni0 = __float_as_int(s0) - 0x4B400000, n10 = min(max(ni0, -126), 127);
+    const int ni1 = __float_as_int(s1) - 0x4B400000, n11 = min(max(ni1, -126), 127);
+    q = ar_mul2(ar_mul2(q, ar_pk(pow2i(n10), pow2i(n11))), ar_pk(pow2i(ni0 - n10), pow2i(ni1 - n11)));
+    float q0, q1;
+    ar_unpk(q, q0, q1);
+    e0 = !(x0 >= -104.0f) ? 0.0f : (x0 > 88.75f ? __int_as_float(0x7f800000) : q0);
+    e1 = !(x1 >= -104.0f) ? 0.0f : (x1 > 88.75f ? __int_as_float(0x7f800000) : q1);
+}
+
 template <bool CLUSTER>
 __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -172,6 +231,14 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     }
     pdl_wait();  // q, positions and the newest cache entries come from earlier kernels
     pdl_trigger();
+    // q of head g = gid, dims 16 tig .. 16 tig + 15 (requested first: it does
+    // not depend on the row's position)
+    uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+    if (gid < 7) {
+        const uint4 *qp = reinterpret_cast<const uint4 *>(a.q + (size_t)r * QB_HID + (kvh * 7 + gid) * QB_HD + 16 * tig);
+        q0 = qp[0];
+        q1 = qp[1];
+    }
     const int L_row = (int)a.positions[r] + 1;
     const int slot = (int)a.slots[r];
     const int t_begin = rank * kpc;
@@ -182,12 +249,23 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     __syncthreads();  // barriers and counters initialised
     const int8_t *kg = a.kc + kvbase * QB_HD;
     const int8_t *vg = a.vc + kvbase * QB_HD;
+    // scales come with the K chunks when their rows start on 16 bytes (the
+    // copied rows are rounded up to 4 keys, which stay inside a row whose
+    // capacity is a multiple of 4)
+    const bool bulk_scales = ((a.cap & 3) == 0) &&
+                             ((reinterpret_cast<uintptr_t>(a.ks) | reinterpret_cast<uintptr_t>(a.vs)) & 15) == 0;
     auto issue = [&](int i) {
         const int c = i < nchunks ? i : i - nchunks, sl = i % AR_RING;
-        const uint32_t bytes = (uint32_t)(min(AR_CHUNK, nkeys - c * AR_CHUNK) * QB_HD);
-        tc::mbar_arrive_expect_tx(&full[sl], bytes);
+        const int n = min(AR_CHUNK, nkeys - c * AR_CHUNK);
+        const uint32_t bytes = (uint32_t)(n * QB_HD), sbytes = (uint32_t)(((n + 3) & ~3) * 4);
+        const bool with_scales = bulk_scales && i < nchunks;
+        tc::mbar_arrive_expect_tx(&full[sl], bytes + (with_scales ? 2 * sbytes : 0u));
         tc::bulk_load(ring + sl * AR_CHUNK_BYTES, (i < nchunks ? kg : vg) + (size_t)c * AR_CHUNK_BYTES, bytes,
                       &full[sl]);
+        if (with_scales) {
+            tc::bulk_load(kss + c * AR_CHUNK, a.ks + kvbase + c * AR_CHUNK, sbytes, &full[sl]);
+            tc::bulk_load(vss + c * AR_CHUNK, a.vs + kvbase + c * AR_CHUNK, sbytes, &full[sl]);
+        }
     };
     // this warp is done reading item i's slot; the last warp to say so
     // refills it with item i + AR_RING
@@ -202,9 +280,9 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     if (tid == 0)
         for (int i = 0; i < min(AR_RING, items); ++i) issue(i);
 
-    // ---------------- stage the scales (every load in flight at once), q as int8 limbs
+    // ---------------- q as int8 limbs; the scales staged here unless they come with the K chunks
     float vmax = 0.f;
-    {
+    if (!bulk_scales) {
         float kv[AR_STAGE_LOADS], vv[AR_STAGE_LOADS];
 #pragma unroll
         for (int j = 0; j < AR_STAGE_LOADS; ++j) {
@@ -218,24 +296,15 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
             if (t < nkeys) {
                 kss[t] = kv[j];
                 vss[t] = vv[j];
-                vmax = fmaxf(vmax, vv[j]);
             }
         }
     }
-    // q of head g = gid, dims 16 tig .. 16 tig + 15, aligned to the head's
-    // largest exponent E as 28-bit integers split into four signed 7-bit limbs;
+    // q aligned to the head's largest exponent E as 28-bit integers split into four signed 7-bit limbs;
     // word i of limb plane l holds dims 16 tig + 4i .. +3 (the same dims the
     // lane's K words cover, so q and K share one k-slot permutation)
     uint32_t qa[2][2][4];  // [m-tile: limbs 0,1 | 2,3][k step][a0..a3]
     int e_g;
     {
-        uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
-        if (gid < 7) {
-            const uint4 *qp =
-                reinterpret_cast<const uint4 *>(a.q + (size_t)r * QB_HID + (kvh * 7 + gid) * QB_HD + 16 * tig);
-            q0 = qp[0];
-            q1 = qp[1];
-        }
         const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         float qf[16];
         float amax = 0.f;
@@ -278,6 +347,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
         if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(c / AR_RING) & 1u, a.err, 32);
         const int kb = c * AR_CHUNK + 16 * warp;  // first key of this warp's block
         float sc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (ok && lane < 16 && kb + lane < nkeys) vmax = fmaxf(vmax, vss[kb + lane]);
         if (ok && kb < nkeys) {
             const int8_t *blk = reinterpret_cast<const int8_t *>(ring + sl * AR_CHUNK_BYTES) + 16 * warp * QB_HD;
             int d[2][2][4];  // [n-tile][m-tile][fragment]
@@ -347,8 +417,9 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
 #pragma unroll 2
     for (int c = 0; c < nchunks; ++c) {
         const float4 s4 = Sl[c * 32];
-        const float e0 = qexp(__fsub_rn(s4.x, Mg)), e1 = qexp(__fsub_rn(s4.y, Mg));
-        const float e2 = qexp(__fsub_rn(s4.z, Mg)), e3 = qexp(__fsub_rn(s4.w, Mg));
+        float e0, e1, e2, e3;
+        ar_qexp2(__fsub_rn(s4.x, Mg), __fsub_rn(s4.y, Mg), e0, e1);
+        ar_qexp2(__fsub_rn(s4.z, Mg), __fsub_rn(s4.w, Mg), e2, e3);
         z += rint_2p40(e0) + rint_2p40(e1) + rint_2p40(e2) + rint_2p40(e3);
         Sl[c * 32] = make_float4(e0, e1, e2, e3);
     }
