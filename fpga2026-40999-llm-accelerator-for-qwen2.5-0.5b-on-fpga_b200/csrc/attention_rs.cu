@@ -30,13 +30,13 @@
 //            (m16n8k16, s8 x u8): W >= 0 split into four byte planes, the V
 //            codes transposed 4 x 4 bytes with byte permutes; int32 per plane,
 //            folded to int64 at the end, warps then cluster ranks added.
-// Memory: the K chunks and then the V chunks stream through one 8-slot ring
+// Memory: the K chunks and then the V chunks stream through one 10-slot ring
 // of bulk copies completing on mbarriers; a K chunk's item also copies the
 // chunk's K and V scales into shared memory (when the cache rows are 16-byte
 // aligned; otherwise every thread stages them with plain loads first). There is no producer warp and no
 // CTA-wide barrier in the loops: each warp counts its release of a slot on an
 // acquire-release shared-memory counter and the warp that releases it last
-// refills it eight items ahead. The chunk loops are not unrolled: a kernel
+// refills it ten items ahead. The chunk loops are not unrolled: a kernel
 // that kept the scores in registers (unrolling every chunk) measured 33 us
 // at 64 rows x 2049 keys, its warps stalled on instruction fetch. Every wait
 // is bounded (error codes 32-33).
@@ -46,16 +46,26 @@
 
 namespace qb {
 
-constexpr int AR_WARPS = 12;
-constexpr int AR_THREADS = 32 * AR_WARPS;
-constexpr int AR_NB = 12;                          // chunks (blocks per warp) per CTA at most
-constexpr int AR_CHUNK = 16 * AR_WARPS;            // keys per chunk
-constexpr int AR_CHUNK_BYTES = AR_CHUNK * QB_HD;   // 12 KB of codes
-constexpr int AR_MAX_KPC = AR_CHUNK * AR_NB;       // 2304 keys per CTA
-constexpr int AR_RING = 8;                         // ring slots (K chunks, then V chunks)
+// The kernel's shape: 12 warps and one CTA per SM, up to 12 chunks (2304
+// keys) per CTA. (Measured against two 8-warp CTAs per SM of up to 1152 keys
+// each, at 64 rows x 2049 keys: 22.6 against 26.6 us.)
+template <int NW>
+struct ArCfg {
+    static constexpr int WARPS = NW;
+    static constexpr int THREADS = 32 * NW;
+    static constexpr int NB = 12;                         // chunks (blocks per warp) per CTA at most
+    static constexpr int CHUNK = 16 * NW;                 // keys per chunk
+    static constexpr int CHUNK_BYTES = CHUNK * QB_HD;
+    static constexpr int MAX_KPC = CHUNK * NB;            // keys per CTA
+    static constexpr int RING = 10;                       // ring slots (K chunks, then V chunks)
+    static constexpr int STAGE_LOADS = (MAX_KPC + THREADS - 1) / THREADS;  // scale loads per thread
+    static constexpr int RED_BYTES = NW * 8 * 4 + NW * 8 * 8 + NW * 4 + RING * 4;
+    static_assert(NW * 8 * QB_HD * 8 <= RING * CHUNK_BYTES, "context partials fit in the ring");
+    static_assert(RED_BYTES % 8 == 0, "aligned sub-areas");
+};
+constexpr int AR_NW = 12;
 constexpr int AR_MAX_SPLITS = 8;
 constexpr int AR_SMS = 148;
-constexpr int AR_STAGE_LOADS = (AR_MAX_KPC + AR_THREADS - 1) / AR_THREADS;  // scale loads per thread
 
 struct ArArgs {
     const uint16_t *q;
@@ -64,36 +74,36 @@ struct ArArgs {
     const float *ks, *vs;
     int cap;
     uint16_t *ctx;
-    int kpc;  // keys per CTA (multiple of AR_CHUNK)
+    int kpc;  // keys per CTA (multiple of the chunk)
     unsigned *err;
 };
 
-// ring [8][192][64] int8 (reused for the per-warp context partials
-// [12][8][64] int64) | S [12 warps][12 chunks][32 lanes] float4 | K scales
+// ring [RING][CHUNK][64] int8 (reused for the per-warp context partials
+// [WARPS][8][64] int64) | S [WARPS][NB chunks][32 lanes] float4 | K scales
 // [kpc] | V scales [kpc] | stat: max[8] (slot 7: largest V scale) | Z[8]
 // int64 | inv, s1, s2, F [4][8] | context partial [7][64] int64 | per-warp
-// max [12][8], Z [12][8] int64, V-scale max [12] | slot release counters [8]
-// | mbarriers [8]
+// max [WARPS][8], Z [WARPS][8] int64, V-scale max [WARPS] | slot release
+// counters [RING] | mbarriers [RING]
 struct ArSmem {
     int ring, s, kss, vss, stat, red, bars, total;
 };
 constexpr int AR_ST_Z = 32, AR_ST_HV = 96, AR_ST_CTX = 224;
 constexpr int AR_STAT_BYTES = AR_ST_CTX + 7 * QB_HD * 8;
-constexpr int AR_RED_BYTES = AR_WARPS * 8 * 4 + AR_WARPS * 8 * 8 + AR_WARPS * 4 + AR_RING * 4;
+static_assert(AR_STAT_BYTES % 16 == 0, "aligned sub-areas");
+template <int NW>
 __host__ __device__ inline ArSmem ar_smem(int kpc) {
+    using C = ArCfg<NW>;
     ArSmem L;
     L.ring = 0;
-    L.s = L.ring + AR_RING * AR_CHUNK_BYTES;
-    L.kss = L.s + AR_WARPS * AR_NB * 32 * 16;
+    L.s = L.ring + C::RING * C::CHUNK_BYTES;
+    L.kss = L.s + C::WARPS * C::NB * 32 * 16;
     L.vss = L.kss + kpc * 4;
     L.stat = L.vss + kpc * 4;
     L.red = L.stat + AR_STAT_BYTES;
-    L.bars = (L.red + AR_RED_BYTES + 7) & ~7;
-    L.total = L.bars + AR_RING * 8;
+    L.bars = (L.red + C::RED_BYTES + 7) & ~7;
+    L.total = L.bars + C::RING * 8;
     return L;
 }
-static_assert(AR_WARPS * 8 * QB_HD * 8 <= AR_RING * AR_CHUNK_BYTES, "context partials fit in the ring");
-static_assert(AR_STAT_BYTES % 16 == 0 && AR_RED_BYTES % 8 == 0, "aligned sub-areas");
 
 __device__ __forceinline__ void ar_mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -195,11 +205,12 @@ __device__ __forceinline__ void ar_qexp2(float x0, float x1, float &e0, float &e
     e1 = !(x1 >= -104.0f) ? 0.0f : (x1 > 88.75f ? __int_as_float(0x7f800000) : q1);
 }
 
-template <bool CLUSTER>
-__global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
+template <int NW, bool CLUSTER>
+__global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
+    using C = ArCfg<NW>;
     extern __shared__ __align__(128) uint8_t sm[];
     const int kpc = a.kpc;
-    const ArSmem L = ar_smem(kpc);
+    const ArSmem L = ar_smem<NW>(kpc);
     uint8_t *ring = sm + L.ring;
     float4 *S = reinterpret_cast<float4 *>(sm + L.s);
     float *kss = reinterpret_cast<float *>(sm + L.kss);
@@ -209,9 +220,9 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     float *hv = reinterpret_cast<float *>(sm + L.stat + AR_ST_HV);
     long long *ctxp = reinterpret_cast<long long *>(sm + L.stat + AR_ST_CTX);
     float *red_m = reinterpret_cast<float *>(sm + L.red);
-    long long *red_z = reinterpret_cast<long long *>(sm + L.red + AR_WARPS * 8 * 4);
-    float *red_v = reinterpret_cast<float *>(sm + L.red + AR_WARPS * 8 * 12);
-    unsigned *released = reinterpret_cast<unsigned *>(sm + L.red + AR_WARPS * 8 * 12 + AR_WARPS * 4);
+    long long *red_z = reinterpret_cast<long long *>(sm + L.red + C::WARPS * 8 * 4);
+    float *red_v = reinterpret_cast<float *>(sm + L.red + C::WARPS * 8 * 12);
+    unsigned *released = reinterpret_cast<unsigned *>(sm + L.red + C::WARPS * 8 * 12 + C::WARPS * 4);
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + L.bars);
     long long *part = reinterpret_cast<long long *>(sm + L.ring);  // after the last chunk
 
@@ -220,10 +231,10 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     const int kvh = blockIdx.y, r = blockIdx.z;
     const int rank = CLUSTER ? (int)tc::cluster_rank() : 0;
     const int nranks = CLUSTER ? (int)gridDim.x : 1;
-    float4 *Sl = S + warp * AR_NB * 32 + lane;  // this lane's scores, one float4 per chunk (stride 32)
+    float4 *Sl = S + warp * C::NB * 32 + lane;  // this lane's scores, one float4 per chunk (stride 32)
 
     if (tid == 0) {
-        for (int i = 0; i < AR_RING; ++i) {
+        for (int i = 0; i < C::RING; ++i) {
             tc::mbar_init(&full[i], 1);
             released[i] = 0;
         }
@@ -243,7 +254,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     const int slot = (int)a.slots[r];
     const int t_begin = rank * kpc;
     const int nkeys = max(0, min(L_row, t_begin + kpc) - t_begin);
-    const int nchunks = (nkeys + AR_CHUNK - 1) / AR_CHUNK;
+    const int nchunks = (nkeys + C::CHUNK - 1) / C::CHUNK;
     const int items = 2 * nchunks;  // ring items: K chunks 0..n-1, then V chunks
     const size_t kvbase = ((size_t)slot * QB_KVH + kvh) * a.cap + t_begin;  // first key of this CTA
     __syncthreads();  // barriers and counters initialised
@@ -255,44 +266,44 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     const bool bulk_scales = ((a.cap & 3) == 0) &&
                              ((reinterpret_cast<uintptr_t>(a.ks) | reinterpret_cast<uintptr_t>(a.vs)) & 15) == 0;
     auto issue = [&](int i) {
-        const int c = i < nchunks ? i : i - nchunks, sl = i % AR_RING;
-        const int n = min(AR_CHUNK, nkeys - c * AR_CHUNK);
+        const int c = i < nchunks ? i : i - nchunks, sl = i % C::RING;
+        const int n = min(C::CHUNK, nkeys - c * C::CHUNK);
         const uint32_t bytes = (uint32_t)(n * QB_HD), sbytes = (uint32_t)(((n + 3) & ~3) * 4);
         const bool with_scales = bulk_scales && i < nchunks;
         tc::mbar_arrive_expect_tx(&full[sl], bytes + (with_scales ? 2 * sbytes : 0u));
-        tc::bulk_load(ring + sl * AR_CHUNK_BYTES, (i < nchunks ? kg : vg) + (size_t)c * AR_CHUNK_BYTES, bytes,
+        tc::bulk_load(ring + sl * C::CHUNK_BYTES, (i < nchunks ? kg : vg) + (size_t)c * C::CHUNK_BYTES, bytes,
                       &full[sl]);
         if (with_scales) {
-            tc::bulk_load(kss + c * AR_CHUNK, a.ks + kvbase + c * AR_CHUNK, sbytes, &full[sl]);
-            tc::bulk_load(vss + c * AR_CHUNK, a.vs + kvbase + c * AR_CHUNK, sbytes, &full[sl]);
+            tc::bulk_load(kss + c * C::CHUNK, a.ks + kvbase + c * C::CHUNK, sbytes, &full[sl]);
+            tc::bulk_load(vss + c * C::CHUNK, a.vs + kvbase + c * C::CHUNK, sbytes, &full[sl]);
         }
     };
     // this warp is done reading item i's slot; the last warp to say so
-    // refills it with item i + AR_RING
+    // refills it with item i + C::RING
     auto release = [&](int i) {
         __syncwarp();
-        if (lane == 0 && ar_release_count(&released[i % AR_RING]) == AR_WARPS - 1) {
-            atomicExch(&released[i % AR_RING], 0u);
+        if (lane == 0 && ar_release_count(&released[i % C::RING]) == C::WARPS - 1) {
+            atomicExch(&released[i % C::RING], 0u);
             tc::fence_proxy_async_smem();  // generic reads of the slot before the bulk copy's writes
-            if (i + AR_RING < items) issue(i + AR_RING);
+            if (i + C::RING < items) issue(i + C::RING);
         }
     };
     if (tid == 0)
-        for (int i = 0; i < min(AR_RING, items); ++i) issue(i);
+        for (int i = 0; i < min(C::RING, items); ++i) issue(i);
 
     // ---------------- q as int8 limbs; the scales staged here unless they come with the K chunks
     float vmax = 0.f;
     if (!bulk_scales) {
-        float kv[AR_STAGE_LOADS], vv[AR_STAGE_LOADS];
+        float kv[C::STAGE_LOADS], vv[C::STAGE_LOADS];
 #pragma unroll
-        for (int j = 0; j < AR_STAGE_LOADS; ++j) {
-            const int t = tid + j * AR_THREADS;
+        for (int j = 0; j < C::STAGE_LOADS; ++j) {
+            const int t = tid + j * C::THREADS;
             kv[j] = t < nkeys ? __ldg(a.ks + kvbase + t) : 0.f;
             vv[j] = t < nkeys ? __ldg(a.vs + kvbase + t) : 0.f;
         }
 #pragma unroll
-        for (int j = 0; j < AR_STAGE_LOADS; ++j) {
-            const int t = tid + j * AR_THREADS;
+        for (int j = 0; j < C::STAGE_LOADS; ++j) {
+            const int t = tid + j * C::THREADS;
             if (t < nkeys) {
                 kss[t] = kv[j];
                 vss[t] = vv[j];
@@ -343,13 +354,13 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     float mrun = -INFINITY;
 #pragma unroll 1
     for (int c = 0; c < nchunks; ++c) {
-        const int sl = c % AR_RING;
-        if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(c / AR_RING) & 1u, a.err, 32);
-        const int kb = c * AR_CHUNK + 16 * warp;  // first key of this warp's block
+        const int sl = c % C::RING;
+        if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(c / C::RING) & 1u, a.err, 32);
+        const int kb = c * C::CHUNK + 16 * warp;  // first key of this warp's block
         float sc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (ok && lane < 16 && kb + lane < nkeys) vmax = fmaxf(vmax, vss[kb + lane]);
         if (ok && kb < nkeys) {
-            const int8_t *blk = reinterpret_cast<const int8_t *>(ring + sl * AR_CHUNK_BYTES) + 16 * warp * QB_HD;
+            const int8_t *blk = reinterpret_cast<const int8_t *>(ring + sl * C::CHUNK_BYTES) + 16 * warp * QB_HD;
             int d[2][2][4];  // [n-tile][m-tile][fragment]
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
@@ -389,10 +400,10 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     if (tid < 8) {
         float m = -INFINITY;
         if (tid < 7) {
-            for (int w = 0; w < AR_WARPS; ++w) m = fmaxf(m, red_m[w * 8 + tid]);
+            for (int w = 0; w < C::WARPS; ++w) m = fmaxf(m, red_m[w * 8 + tid]);
         } else {
             m = 0.f;
-            for (int w = 0; w < AR_WARPS; ++w) m = fmaxf(m, red_v[w]);
+            for (int w = 0; w < C::WARPS; ++w) m = fmaxf(m, red_v[w]);
         }
         stat[tid] = m;
     }
@@ -420,7 +431,10 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
         float e0, e1, e2, e3;
         ar_qexp2(__fsub_rn(s4.x, Mg), __fsub_rn(s4.y, Mg), e0, e1);
         ar_qexp2(__fsub_rn(s4.z, Mg), __fsub_rn(s4.w, Mg), e2, e3);
-        z += rint_2p40(e0) + rint_2p40(e1) + rint_2p40(e2) + rint_2p40(e3);
+        // rint(e * 2^40) (0 <= e <= 1, the product exact): the conversion
+        // rounds to nearest even, as rint does
+        z += __float2ll_rn(__fmul_rn(e0, 0x1p40f)) + __float2ll_rn(__fmul_rn(e1, 0x1p40f)) +
+             __float2ll_rn(__fmul_rn(e2, 0x1p40f)) + __float2ll_rn(__fmul_rn(e3, 0x1p40f));
         Sl[c * 32] = make_float4(e0, e1, e2, e3);
     }
     z += __shfl_xor_sync(0xffffffffu, z, 1);
@@ -429,7 +443,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     __syncthreads();
     if (tid < 8) {
         long long zz = 0;
-        for (int w = 0; w < AR_WARPS; ++w) zz += red_z[w * 8 + tid];
+        for (int w = 0; w < C::WARPS; ++w) zz += red_z[w * 8 + tid];
         statz[tid] = zz;
     }
     if constexpr (CLUSTER) {
@@ -477,9 +491,9 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
         for (int l = 0; l < 4; ++l) acc[j][l][0] = acc[j][l][1] = acc[j][l][2] = acc[j][l][3] = 0;
 #pragma unroll 1
     for (int c = 0; c < nchunks; ++c) {
-        const int item = nchunks + c, sl = item % AR_RING;
-        if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(item / AR_RING) & 1u, a.err, 33);
-        const int kb = c * AR_CHUNK + 16 * warp;
+        const int item = nchunks + c, sl = item % C::RING;
+        if (ok) ok = tc::mbar_wait(&full[sl], (uint32_t)(item / C::RING) & 1u, a.err, 33);
+        const int kb = c * C::CHUNK + 16 * warp;
         if (ok && kb < nkeys) {
             const float4 e4 = Sl[c * 32];
             const float2 v01 = *reinterpret_cast<const float2 *>(vss + kb + 2 * tig);
@@ -494,7 +508,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
             }
             ar_transpose4(wq, b);
             const uint32_t *vb =
-                reinterpret_cast<const uint32_t *>(ring + sl * AR_CHUNK_BYTES) + 16 * warp * (QB_HD / 4);
+                reinterpret_cast<const uint32_t *>(ring + sl * C::CHUNK_BYTES) + 16 * warp * (QB_HD / 4);
             uint32_t rl[4], rh[4], alo[4], ahi[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -524,18 +538,18 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
             part[(warp * 8 + h) * QB_HD + d] = v;
         }
     __syncthreads();
-    for (int i = tid; i < 7 * QB_HD; i += AR_THREADS) {
+    for (int i = tid; i < 7 * QB_HD; i += C::THREADS) {
         const int h = i >> 6, d = i & 63;
         long long sum = 0;
 #pragma unroll
-        for (int w = 0; w < AR_WARPS; ++w) sum += part[(w * 8 + h) * QB_HD + d];
+        for (int w = 0; w < C::WARPS; ++w) sum += part[(w * 8 + h) * QB_HD + d];
         ctxp[i] = sum;
     }
     if constexpr (CLUSTER) {
         tc::cluster_sync();  // (3)
         if (rank == 0) {
             const uint32_t ca = tc::smem_u32(ctxp);
-            for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += AR_THREADS) {
+            for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += C::THREADS) {
                 long long s0 = 0, s1 = 0;
                 for (int sr = 0; sr < nranks; ++sr) {
                     const float4 v = tc::ld_dsmem_f4(ca + 16u * i2, sr);
@@ -552,7 +566,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
         tc::cluster_sync();  // (4) peers' shared memory stays alive until rank 0 has read it
     } else {
         __syncthreads();
-        for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += AR_THREADS) {
+        for (int i2 = tid; i2 < 7 * QB_HD / 2; i2 += C::THREADS) {
             const int i = 2 * i2, h = i >> 6, d = i & 63;
             const int f = __float_as_int(hv[24 + h]);
             *reinterpret_cast<uint32_t *>(a.ctx + (size_t)r * QB_HID + (kvh * 7 + h) * QB_HD + d) =
@@ -561,46 +575,46 @@ __global__ void __launch_bounds__(AR_THREADS, 1) attn_rs_kernel(ArArgs a) {
     }
 }
 
-// Split plan: one CTA per SM when rows are few (contexts split up to 8 ways),
-// at least enough CTAs to keep each within AR_MAX_KPC keys. Returns -1 when
-// a row needs more than 8 CTAs (the caller uses the shared-memory-score
-// kernel, which holds 4096 keys per CTA).
+// Split plan: as many CTAs per row as fill the GPU once at one CTA per SM
+// (contexts split up to 8 ways), at least enough to keep each within the key
+// limit. -1 when a row needs more than 8 CTAs.
+template <int NW>
 int attention_rs_plan(int rows, int max_len, int *splits, int *kpc) {
+    using C = ArCfg<NW>;
     if (max_len <= 0 || rows <= 0) return -1;
-    const int chunks = (max_len + AR_CHUNK - 1) / AR_CHUNK;
+    const int chunks = (max_len + C::CHUNK - 1) / C::CHUNK;
     int s = AR_SMS / (2 * rows);
     s = s < 1 ? 1 : (s > AR_MAX_SPLITS ? AR_MAX_SPLITS : s);
     s = s > chunks ? chunks : s;
-    const int need = (chunks + AR_NB - 1) / AR_NB;
+    const int need = (chunks + C::NB - 1) / C::NB;
     s = s < need ? need : s;
     if (s > AR_MAX_SPLITS) return -1;
     const int cpc = (chunks + s - 1) / s;  // chunks per CTA
-    *kpc = cpc * AR_CHUNK;
+    *kpc = cpc * C::CHUNK;
     *splits = (chunks + cpc - 1) / cpc;
     return 0;
 }
 
-template <bool CLUSTER>
+template <int NW, bool CLUSTER>
 static int run_ar(const ArArgs &a, int rows, int splits, cudaStream_t st) {
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(configured & (1u << (dev & 31)))) {
-        if (cudaFuncSetAttribute(attn_rs_kernel<CLUSTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 ar_smem(AR_MAX_KPC).total) != cudaSuccess)
+        if (cudaFuncSetAttribute(attn_rs_kernel<NW, CLUSTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ar_smem<NW>(ArCfg<NW>::MAX_KPC).total) != cudaSuccess)
             return -3;
         configured |= 1u << (dev & 31);
     }
-    return launch_pdl(attn_rs_kernel<CLUSTER>, dim3(splits, QB_KVH, rows), dim3(AR_THREADS),
-                      (size_t)ar_smem(a.kpc).total, st, CLUSTER ? (unsigned)splits : 1u, a);
+    return launch_pdl(attn_rs_kernel<NW, CLUSTER>, dim3(splits, QB_KVH, rows), dim3(32 * NW),
+                      (size_t)ar_smem<NW>(a.kpc).total, st, CLUSTER ? (unsigned)splits : 1u, a);
 }
 
-// 0 when launched; 1 when the context needs the shared-memory-score kernel.
 int launch_attention_rs(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
                         const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
                         unsigned *err, cudaStream_t st) {
     int splits, kpc;
-    if (attention_rs_plan(rows, max_len, &splits, &kpc)) return 1;
+    if (attention_rs_plan<AR_NW>(rows, max_len, &splits, &kpc)) return 1;
     ArArgs a;
     a.q = q;
     a.slots = slots;
@@ -613,7 +627,7 @@ int launch_attention_rs(const uint16_t *q, int rows, const uint32_t *slots, cons
     a.ctx = ctx;
     a.kpc = kpc;
     a.err = err;
-    return splits > 1 ? run_ar<true>(a, rows, splits, st) : run_ar<false>(a, rows, 1, st);
+    return splits > 1 ? run_ar<AR_NW, true>(a, rows, splits, st) : run_ar<AR_NW, false>(a, rows, 1, st);
 }
 
 }  // namespace qb

@@ -94,9 +94,9 @@ int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const u
 int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions,
                              int max_len, const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap,
                              uint16_t *ctx, unsigned *err, cudaStream_t st);
-// The same attention with the scores held in registers (one CTA of 12 + 1
-// warps per (row, KV head), up to 8 per row for long contexts); 0 when
-// launched, 1 when a row needs more than 8 x 2304 keys per cluster (the
+// The same attention with transposed tensor-core scores kept lane-private in
+// shared memory (attention_rs.cu: CTAs of 12 warps, up to 8 per row for
+// long contexts); 0 when launched, 1 when a row needs more than 8 CTAs (the
 // caller then uses the kernel above), negative on a launch error.
 int launch_attention_rs(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions, int max_len,
                         const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
