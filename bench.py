@@ -357,6 +357,10 @@ def run_ours(args):
 
     # bs1 decode at short context (16-token prompt), slot 0
     bs1 = bs1_decode(eng, args, stream, sp, hbm)
+    eng.close()
+
+    # prefill of 8 x 4096-token prompts with the vocabulary-sharded LM head
+    prefill = None if args.no_prefill else prefill_sharded(args, rank, world, local)
 
     result = None
     if rank == 0:
@@ -368,14 +372,13 @@ def run_ours(args):
             'data': 'synthetic (seeded random-init int8 weights, seeded KV8 fill, random token ids)',
             'config': workload_config(args), 'roofline': roofline, 'step_roofline': step_roof,
             'kernels': kernels, 'e2e': e2e, 'gpu_launches': int(launches), 'bs1': bs1, 'strong': strong,
-            'clocks': clk}
+            'prefill': prefill, 'clocks': clk}
     if world == 1 and not args.no_cpu_baseline:
         tps, n = cpu_decode_sample(S, C, 10.0, 30.0, os.cpu_count() or 1)
         result['cpu_baseline'] = {'value': round(tps, 3), 'unit': 'tokens/s', 'cores': os.cpu_count() or 1,
                                   'kind': 'port',
                                   'sample': f'oracle/qwen_ref.c (KV8 mode) decoding {S} sequences at context '
                                             f'{C}..{C + 4}+, {n} batched steps (one {S}-row forward each)'}
-    eng.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -383,6 +386,93 @@ def run_ours(args):
     if result is not None:
         print(json.dumps(result), flush=True)
     return 0
+
+
+def prefill_sharded(args, rank, world, local):
+    """Prefill of args.prefill_prompts prompts of args.prefill_len seeded random
+    ids through all 24 layers (tensor-core projections in 4096-row chunks),
+    request-sharded (prompts / N per GPU), then the LM head split by
+    vocabulary over the GPUs: an NCCL all-gather of every prompt's last hidden
+    row, each GPU's (value, index) per row over its vocabulary range, an NCCL
+    all-gather of those candidates and the highest-value / highest-index
+    combine (model_backend.py:113-114). Timed on the host around the whole
+    sequence (the prefill call synchronises), max over ranks."""
+    import torch
+    import qwen_b200
+    import qwen_b200.distributed as D
+    P, T = args.prefill_prompts, args.prefill_len
+    if P % world:
+        return {'unavailable': f'{P} prompts do not split evenly over {world} GPUs'}
+    mine = list(D.shard_requests(P, world, rank))
+    rng = np.random.default_rng(SEED + 99)
+    prompts = [rng.integers(0, VOCAB, T).astype(np.uint32) for _ in range(P)]  # the same on every rank
+    eng = qwen_b200.Engine(device=local, max_seqs=P, max_context=T + 8, max_rows=4096).load_synthetic(SEED)
+    vb, ve = D.vocab_shard(VOCAB, world, rank)
+    hid_local = torch.empty((len(mine), HID), dtype=torch.int16, device='cuda')
+    hid_all = torch.empty((P, HID), dtype=torch.int16, device='cuda')
+    vals = torch.empty(P, dtype=torch.float32, device='cuda')
+    idx = torch.empty(P, dtype=torch.int32, device='cuda')
+    vals_all = torch.empty(world * P, dtype=torch.float32, device='cuda')
+    idx_all = torch.empty(world * P, dtype=torch.int32, device='cuda')
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def run():
+        for s in mine:
+            eng.reset(s)
+        _, hidden = eng.prefill(mine, [prompts[i] for i in mine], want_tokens=False, want_hidden=True)
+        hid_local.copy_(torch.from_numpy(hidden.view(np.int16)))
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(hid_all, hid_local)
+        else:
+            hid_all.copy_(hid_local)
+        eng.lm_head_range(ctypes.c_void_p(hid_all.data_ptr()), P, vb, ve, ctypes.c_void_p(vals.data_ptr()),
+                          ctypes.c_void_p(idx.data_ptr()), sp)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(vals_all, vals)
+            dist.all_gather_into_tensor(idx_all, idx)
+        else:
+            vals_all.copy_(vals)
+            idx_all.copy_(idx)
+        return D.combine_candidates(vals_all.cpu().numpy().reshape(world, P),
+                                    idx_all.cpu().numpy().reshape(world, P).astype(np.int64))
+
+    tokens = run()  # warm-up (captures nothing: prefill launches directly)
+    times = []
+    for _ in range(args.prefill_reps):
+        barrier(world)
+        t0 = time.perf_counter()
+        tokens = run()
+        torch.cuda.synchronize()
+        times.append(max_over_ranks(time.perf_counter() - t0, world))
+    # the sharded head agrees with each rank's own full-vocabulary head
+    for s in mine:
+        eng.reset(s)
+    own, _ = eng.prefill(mine, [prompts[i] for i in mine], want_tokens=True, want_hidden=False)
+    agree = reduce_agree(bool(np.array_equal(own.astype(np.int64), tokens[mine])), world)
+    eng.close()
+    sec = min(times)
+    return {'metric': 'prefill tokens/s', 'value': round(P * T / sec, 1), 'unit': 'tokens/s',
+            'ms_per_run': round(1000 * sec, 2), 'runs': args.prefill_reps, 'prompts': P, 'prompt_len': T,
+            'prompts_per_gpu': len(mine), 'vocab_shard_rows': ve - vb,
+            'collectives': ('NCCL all-gather of the last hidden rows, then of the per-shard (value, index)'
+                            if world > 1 else 'none (one GPU holds the whole vocabulary)'),
+            'sharded_tokens_equal_full_head': agree,
+            'timing': 'host wall clock around the synchronous prefill call, gathers and sharded LM head, '
+                      'max over ranks, best of the runs'}
+
+
+def reduce_agree(flag, world):
+    return bool(reduce_over_ranks_min(1.0 if flag else 0.0, world) == 1.0)
+
+
+def reduce_over_ranks_min(value, world):
+    if world == 1:
+        return value
+    from qwen_b200.distributed import reduce_over_ranks
+    return -reduce_over_ranks(-value, 'max')
 
 
 def step_ms_of(ms_max, args):
@@ -499,6 +589,10 @@ def main():
     ap.add_argument('--seqs', type=int, default=64)
     ap.add_argument('--context', type=int, default=2048)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-prefill', action='store_true')
+    ap.add_argument('--prefill-prompts', type=int, default=8)
+    ap.add_argument('--prefill-len', type=int, default=4096)
+    ap.add_argument('--prefill-reps', type=int, default=2)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')

@@ -356,11 +356,42 @@ int check_device_flags(qwen_b200 *h) {
     return 0;
 }
 
+// Final RMSNorm + LM head over the vocabulary rows [begin, end) + greedy
+// argmax (highest index on ties, model_backend.py:108-114) for nlog rows of
+// xin: tokens_dst[r] the best global index, values_dst[r] (nullable) its bf16
+// logit as fp32, logits_dst (nullable) [nlog][end - begin].
+int lm_head_rows(qwen_b200 *h, const uint16_t *xin, int nlog, int begin, int end, uint16_t *logits_dst,
+                 uint32_t *tokens_dst, float *values_dst, cudaStream_t st) {
+    const float eps = h->cfg.rms_eps;
+    const int width = end - begin;
+    if (nlog >= TC_MIN_ROWS) {
+        LaunchScope ls(h, 6, st, 3);
+        int rc = norm_limbs(h, xin, h->g_final, nlog, eps, st);
+        if (rc) return rc;
+        const int nblk = width / 128;
+        TcArgmax am;
+        am.pv = reinterpret_cast<float *>(h->lm_ws);
+        am.pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(h->lm_ws) + (size_t)nlog * nblk * 4);
+        am.nblk = nblk;
+        am.logits = logits_dst;
+        am.n_base = begin;
+        rc = tc_gemm(h, EPI_ARGMAX, nlog, HID, h->mlm, h->s_lm + begin, nullptr, width, nullptr, &am, st);
+        if (rc) return rc;
+        RK(launch_argmax_reduce(am.pv, am.pi, nlog, nblk, tokens_dst, st, values_dst));
+    } else {
+        LaunchScope ls(h, 6, st, 2);
+        RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw + (size_t)begin * HID, h->s_lm + begin, width,
+                          logits_dst, tokens_dst, h->lm_ws, h->lm_ws_bytes, st, begin, values_dst));
+    }
+    return 0;
+}
+
 // One forward over R rows whose ids/slots/positions are at meta[0..3R) with
 // stride n (ids n | slots n | positions n | logit rows n). nlog rows get the
-// LM head: rows listed at meta+3n, or all rows when identity.
+// LM head: rows listed at meta+3n, or all rows when identity. Without
+// lm_head the nlog rows are only gathered into h->xl (identity false).
 int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint16_t *logits_dst, uint32_t *tokens_dst,
-                cudaStream_t st) {
+                cudaStream_t st, bool lm_head = true) {
     const uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n, *lrows = h->meta + 3 * n;
     const int cap = (int)h->cfg.max_context;
     const float eps = h->cfg.rms_eps;
@@ -492,24 +523,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
             RK(launch_gather_rows(h->x, lrows, nlog, h->xl, st));
             xin = h->xl;
         }
-        if (nlog >= TC_MIN_ROWS) {
-            LaunchScope ls(h, 6, st, 3);
-            int rc = norm_limbs(h, xin, h->g_final, nlog, eps, st);
-            if (rc) return rc;
-            const int nblk = VOC / 128;
-            TcArgmax am;
-            am.pv = reinterpret_cast<float *>(h->lm_ws);
-            am.pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(h->lm_ws) + (size_t)nlog * nblk * 4);
-            am.nblk = nblk;
-            am.logits = logits_dst;
-            rc = tc_gemm(h, EPI_ARGMAX, nlog, HID, h->mlm, h->s_lm, nullptr, VOC, nullptr, &am, st);
-            if (rc) return rc;
-            RK(launch_argmax_reduce(am.pv, am.pi, nlog, nblk, tokens_dst, st));
-        } else {
-            LaunchScope ls(h, 6, st, 2);
-            RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw, h->s_lm, VOC, logits_dst,
-                              tokens_dst, h->lm_ws, h->lm_ws_bytes, st));
-        }
+        if (lm_head) return lm_head_rows(h, xin, nlog, 0, VOC, logits_dst, tokens_dst, nullptr, st);
     }
     return 0;
 }
@@ -871,6 +885,92 @@ int qwen_b200_decode_step_logits(qwen_b200 *h, const uint32_t *slots, const uint
                                  uint32_t *tokens_out, uint16_t *logits) {
     if (!logits) return h ? fail(h, QWEN_B200_EINVAL, "logits buffer is NULL") : QWEN_B200_EINVAL;
     return decode_step_impl(h, slots, tokens_in, n, tokens_out, logits);
+}
+
+int qwen_b200_prefill(qwen_b200 *h, uint32_t n, const uint32_t *slots, const uint32_t *lens, const uint32_t *ids,
+                      uint32_t *tokens_out, uint16_t *hidden_out) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (!slots || !lens || !ids || n == 0 || n > h->cfg.max_seqs || (!tokens_out && !hidden_out))
+        return fail(h, QWEN_B200_EINVAL, "bad prefill request");
+    std::vector<char> seen(h->cfg.max_seqs, 0);
+    size_t total = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (slots[i] >= h->cfg.max_seqs || seen[slots[i]] || lens[i] == 0)
+            return fail(h, QWEN_B200_EINVAL, "bad or repeated slot, or empty sequence");
+        seen[slots[i]] = 1;
+        if ((uint64_t)h->pos[slots[i]] + lens[i] > h->cfg.max_context)
+            return fail(h, QWEN_B200_ESTATE, "slot %u: %u + %u tokens exceed the capacity", slots[i], h->pos[slots[i]],
+                        lens[i]);
+        total += lens[i];
+    }
+    for (size_t t = 0; t < total; ++t)
+        if (ids[t] >= (uint32_t)VOC) return fail(h, QWEN_B200_EINVAL, "token id %u >= vocab", ids[t]);
+    // every row: (sequence, position); rows of all sequences go through the
+    // layers together, max_rows at a time
+    std::vector<uint32_t> rseq(total), rpos(total);
+    for (uint32_t i = 0, t = 0; i < n; ++i)
+        for (uint32_t j = 0; j < lens[i]; ++j, ++t) {
+            rseq[t] = i;
+            rpos[t] = h->pos[slots[i]] + j;
+        }
+    cudaStream_t st = h->stream;
+    const size_t chunk = h->cfg.max_rows;
+    uint32_t done = 0;
+    for (size_t c0 = 0; c0 < total; c0 += chunk) {
+        const int m = (int)std::min(chunk, total - c0);
+        if (c0) CK(cudaEventSynchronize(h->staged));  // the pinned staging buffer is free again
+        int nl = 0, max_len = 0;
+        for (int r = 0; r < m; ++r) {
+            const size_t t = c0 + r;
+            h->h_meta[r] = ids[t];
+            h->h_meta[m + r] = slots[rseq[t]];
+            h->h_meta[2 * m + r] = rpos[t];
+            max_len = std::max(max_len, (int)rpos[t] + 1);
+            if (t + 1 == total || rseq[t + 1] != rseq[t]) h->h_meta[3 * m + nl++] = (uint32_t)r;  // a last row
+        }
+        CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * m + nl) * 4, cudaMemcpyHostToDevice, st));
+        CK(cudaEventRecord(h->staged, st));
+        h->nlaunch = 0;
+        if ((rc = run_forward(h, m, max_len, nl, false, nullptr, h->tokens + done, st, tokens_out != nullptr)))
+            return rc;
+        if (hidden_out && nl)
+            CK(cudaMemcpyAsync(hidden_out + (size_t)done * HID, h->xl, (size_t)nl * HID * 2, cudaMemcpyDeviceToHost,
+                               st));
+        done += (uint32_t)nl;
+    }
+    if (tokens_out) CK(cudaMemcpyAsync(h->h_tokens, h->tokens, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(h->h_flag, h->tc_ws, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (*h->h_flag) {
+        cudaMemset(h->tc_ws, 0, 4);
+        return fail(h, QWEN_B200_ETIMEOUT, "a pipeline wait on the device timed out (code %u)", *h->h_flag);
+    }
+    for (uint32_t i = 0; i < n; ++i) h->pos[slots[i]] += lens[i];
+    if ((rc = sync_slot_positions(h, st))) return rc;
+    if (tokens_out)
+        for (uint32_t i = 0; i < n; ++i) {
+            if (h->h_tokens[i] >= (uint32_t)VOC) return fail(h, QWEN_B200_ETOKEN, "token %u", h->h_tokens[i]);
+            tokens_out[i] = h->h_tokens[i];
+        }
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_lm_head_range(qwen_b200 *h, const uint16_t *d_hidden, uint32_t rows, uint32_t begin, uint32_t end,
+                            float *d_values, uint32_t *d_indices, void *stream) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (!d_hidden || !d_values || !d_indices || rows == 0 || (int)rows > h->R)
+        return fail(h, QWEN_B200_EINVAL, "bad LM-head request");
+    if (begin >= end || end > (uint32_t)VOC || begin % 128 || end % 128)
+        return fail(h, QWEN_B200_EINVAL, "vocabulary range [%u, %u) is not whole 128-row tiles of [0, %d)", begin,
+                    end, VOC);
+    cudaStream_t st = (cudaStream_t)stream;
+    CK(cudaMemcpyAsync(h->xl, d_hidden, (size_t)rows * HID * 2, cudaMemcpyDeviceToDevice, st));
+    h->nlaunch = 0;
+    return lm_head_rows(h, h->xl, (int)rows, (int)begin, (int)end, nullptr, d_indices, d_values, st);
 }
 
 static int enqueue_device_step(qwen_b200 *h, const uint32_t *d_in, int n, int max_len, uint32_t *d_out,

@@ -129,7 +129,7 @@ __device__ __forceinline__ void tc_argmax_rows(const TcArgs &a, const float (&v)
         const float val = rbf(rbf(v[j]) * sc);
         if (valid && a.logits) a.logits[(size_t)m * a.N + n] = f2bf(val);
         bv[j] = valid ? val : -INFINITY;
-        bi[j] = (uint32_t)n;
+        bi[j] = (uint32_t)(a.n_base + n);
     }
     int row = 0;  // first row (of the NR) this lane holds after the halvings
 #pragma unroll
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tile_of(g, n0, m0);
                 const int s = g % AS;
                 tc::mbar_arrive_expect_tx(&full_a[s], (uint32_t)L::A_BYTES);
-                tc::tma_load_2d(smem + L::A_OFF + s * L::A_BYTES, &wmap, &full_a[s], (g % KC) * TC_BK, n0);
+                tc::tma_load_2d(smem + L::A_OFF + s * L::A_BYTES, &wmap, &full_a[s], (g % KC) * TC_BK, a.n_base + n0);
             };
             int ia = 0, ib = 0;
             // weights are constant: the first stages load before the wait for
@@ -823,6 +823,7 @@ int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, co
     a.pi = am ? am->pi : nullptr;
     a.nblk = am ? am->nblk : 0;
     a.logits = am ? am->logits : nullptr;
+    a.n_base = am ? am->n_base : 0;
     if (clear) {
         if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return -3;
         pdl_break();

@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
                                                       const uint16_t *__restrict__ gamma, float eps,
                                                       const int8_t *__restrict__ w, const float *__restrict__ scale,
                                                       int vocab, uint16_t *logits, float *pv, uint32_t *pi,
-                                                      int nblk) {
+                                                      int nblk, int n_base) {
     constexpr int K = QB_HID, RW = 4, NW = 8;
     extern __shared__ __align__(16) uint8_t gsm[];
     int8_t *xl = reinterpret_cast<int8_t *>(gsm);
@@ -291,9 +291,9 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 const float v = rbf(rbf(acc[r][m]) * scale[n0 + r]);
-                if (better(v, (uint32_t)(n0 + r), best_v[m], best_i[m])) {
+                if (better(v, (uint32_t)(n_base + n0 + r), best_v[m], best_i[m])) {
                     best_v[m] = v;
-                    best_i[m] = (uint32_t)(n0 + r);
+                    best_i[m] = (uint32_t)(n_base + n0 + r);
                 }
                 if (logits && ((r * MT + m) & 31) == lane && m < mrows)
                     logits[(size_t)(m0 + m) * vocab + n0 + r] = f2bf(v);
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
 }
 
 __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float *pv, const uint32_t *pi, int nblk,
-                                                            uint32_t *tokens) {
+                                                            uint32_t *tokens, float *values) {
     __shared__ float sv[256];
     __shared__ uint32_t si[256];
     pdl_wait();
@@ -347,11 +347,15 @@ __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float *pv, con
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) tokens[row] = si[0];
+    if (threadIdx.x == 0) {
+        tokens[row] = si[0];
+        if (values) values[row] = sv[0];
+    }
 }
 
-int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st) {
-    return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens);
+int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st,
+                         float *values) {
+    return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens, values);
 }
 
 size_t lm_head_workspace(int rows, int vocab) {
@@ -361,16 +365,16 @@ size_t lm_head_workspace(int rows, int vocab) {
 
 template <int MT>
 static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w, const float *scale,
-                  int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, cudaStream_t st) {
+                  int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, int n_base, cudaStream_t st) {
     const size_t smem = (size_t)MT * (4 * QB_HID + 4);
     dim3 grid(nblk, (rows + MT - 1) / MT);
     return launch_pdl(lm_head_kernel<MT>, grid, dim3(256), smem, st, 1, x, rows, gamma, eps, w, scale, vocab, logits,
-                      pv, pi, nblk);
+                      pv, pi, nblk, n_base);
 }
 
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
                    const float *scale, int vocab, uint16_t *logits, uint32_t *tokens, void *ws, size_t ws_bytes,
-                   cudaStream_t st) {
+                   cudaStream_t st, int n_base, float *values) {
     if (rows <= 0 || vocab <= 0 || vocab % 4) return -1;
     if (ws_bytes < lm_head_workspace(rows, vocab)) return -1;
     const int nblk = (vocab + 31) / 32;
@@ -378,13 +382,13 @@ int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps
     uint32_t *pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(ws) + (size_t)rows * nblk * 4);
     int rc;
     if (rows <= 1)
-        rc = run_lm<1>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
+        rc = run_lm<1>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);
     else if (rows <= 2)
-        rc = run_lm<2>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);
+        rc = run_lm<2>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);
     else
-        rc = run_lm<4>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, st);  // 4-row tiles
+        rc = run_lm<4>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);  // 4-row tiles
     if (rc) return rc;
-    return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens);
+    return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens, values);
 }
 
 }  // namespace qb

@@ -74,9 +74,12 @@ int launch_decode1(const D1Args &a, cudaStream_t st);
 
 // Final RMSNorm + LM head + argmax. part: [rows][nblocks] (value, index).
 size_t lm_head_workspace(int rows, int vocab);
+// n_base is added to every reported index (w, scale and logits are those of
+// the rows [n_base, n_base + vocab) of a larger head); values (nullable)
+// receives each row's best logit.
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
                    const float *scale, int vocab, uint16_t *logits, uint32_t *tokens, void *ws, size_t ws_bytes,
-                   cudaStream_t st);
+                   cudaStream_t st, int n_base = 0, float *values = nullptr);
 
 // Attention over a KV8 cache (two passes + last-block combine). The
 // workspace is laid out for ws_rows rows (>= rows); its completion counters
@@ -140,12 +143,14 @@ struct TcArgs {
     uint32_t *pi;
     int nblk;
     uint16_t *logits;
+    int n_base;  // LM head: first row of the weight map this launch covers
 };
 struct TcArgmax {
     float *pv;
     uint32_t *pi;
     int nblk;         // = n / 128 partial candidates per row
     uint16_t *logits; // nullable [rows][n]
+    int n_base = 0;   // the n channels are rows [n_base, n_base + n) of the weight map
 };
 // Tensor maps: weights [n][k] int8 row-major; limbs[l][row][k] with planes
 // `plane` bytes apart, rows `ld` bytes apart, rows_alloc rows.
@@ -158,7 +163,8 @@ size_t tc_gemm_workspace(int rows, int n, int splits);
 int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, const int *ex, int rows, int k,
                    const float *scale, const uint16_t *bias, int n, uint16_t *y, int splits, void *ws,
                    size_t ws_bytes, bool clear, const TcArgmax *am, cudaStream_t st);
-int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st);
+int launch_argmax_reduce(const float *pv, const uint32_t *pi, int rows, int nblk, uint32_t *tokens, cudaStream_t st,
+                         float *values = nullptr);
 // RoPE + KV8 append for the q|k|v rows produced by the tensor-core QKV GEMM
 // (qkv [rows][1152], bias already added).
 int launch_rope_kv8(const uint16_t *qkv, int rows, const uint32_t *slots, const uint32_t *positions,

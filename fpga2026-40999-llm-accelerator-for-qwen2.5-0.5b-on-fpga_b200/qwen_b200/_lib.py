@@ -37,6 +37,9 @@ _SIGNATURES = {
     'qwen_b200_position': (c_int, [c_void_p, c_uint32, _P32]),
     'qwen_b200_forward': (c_int, [c_void_p, c_uint32, _P32, c_uint32, c_uint32, _P32, _P16]),
     'qwen_b200_decode_step': (c_int, [c_void_p, _P32, _P32, c_uint32, _P32]),
+    'qwen_b200_prefill': (c_int, [c_void_p, c_uint32, _P32, _P32, _P32, _P32, _P16]),
+    'qwen_b200_lm_head_range': (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
+                                        c_void_p]),
     'qwen_b200_decode_step_logits': (c_int, [c_void_p, _P32, _P32, c_uint32, _P32, _P16]),
     'qwen_b200_decode_step_device': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
     'qwen_b200_fill_kv_synthetic': (c_int, [c_void_p, c_uint32, c_uint32, c_uint64]),

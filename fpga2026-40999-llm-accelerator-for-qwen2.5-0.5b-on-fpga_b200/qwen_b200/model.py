@@ -80,6 +80,24 @@ class Engine:
                                           ptr(out, c_uint32)), self.h)
         return out
 
+    def prefill(self, slots, prompts, want_tokens=True, want_hidden=False):
+        """Batched prefill: prompts[i] appended to slot slots[i]. Returns
+        (tokens [n] or None, last hidden rows [n][896] bf16 bits or None)."""
+        slots = np.ascontiguousarray(slots, dtype=np.uint32)
+        lens = np.array([len(p) for p in prompts], dtype=np.uint32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.uint32) for p in prompts]))
+        toks = np.empty(len(slots), dtype=np.uint32) if want_tokens else None
+        hidden = np.empty((len(slots), _lib.HIDDEN), dtype=np.uint16) if want_hidden else None
+        check(lib().qwen_b200_prefill(self.h, len(slots), ptr(slots, c_uint32), ptr(lens, c_uint32), ptr(ids, c_uint32),
+                                      ptr(toks, c_uint32) if want_tokens else None,
+                                      ptr(hidden, c_uint16) if want_hidden else None), self.h)
+        return toks, hidden
+
+    def lm_head_range(self, d_hidden, rows, begin, end, d_values, d_indices, stream=None):
+        """Vocabulary rows [begin, end) of the LM head for device rows d_hidden
+        (pointers as ctypes.c_void_p); per row best value and global index."""
+        check(lib().qwen_b200_lm_head_range(self.h, d_hidden, rows, begin, end, d_values, d_indices, stream), self.h)
+
     def decode_step_logits(self, slots, tokens):
         """decode_step that also returns every row's logits [n][151936] (bf16 bits)."""
         slots = np.ascontiguousarray(slots, dtype=np.uint32)

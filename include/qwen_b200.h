@@ -100,6 +100,31 @@ int qwen_b200_position(const qwen_b200 *h, uint32_t slot, uint32_t *position);
  * the slot's position or the capacity would overflow. Host buffers. */
 int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t rows, uint32_t position,
                       uint32_t *token, uint16_t *logits);
+/* Prefill of n sequences in one call (batched prompt processing): sequence
+ * i is lens[i] ids (the sequences' ids concatenated in `ids`) appended to slot
+ * slots[i] at its current position (0 after qwen_b200_reset). The rows of all
+ * sequences go through the layers together, max_rows at a time (a chunk may
+ * hold rows of several sequences; each row attends to its own slot's keys
+ * up to its position). tokens_out (nullable) [n]: the greedy token after each
+ * sequence; hidden_out (nullable, host) [n][896] bf16: each sequence's last
+ * hidden row before the final RMSNorm (the input of qwen_b200_lm_head_range,
+ * e.g. on other GPUs). At least one of the two. With tokens_out NULL the LM
+ * head is not run. The reference feeds a prompt in row groups through the
+ * same layer sequence (src/rtl/storage/qwen25_qkv_controller.v:400-474;
+ * model_backend.py:80-115 for several ids at once). Host buffers. */
+int qwen_b200_prefill(qwen_b200 *h, uint32_t n, const uint32_t *slots, const uint32_t *lens, const uint32_t *ids,
+                      uint32_t *tokens_out, uint16_t *hidden_out);
+/* Final RMSNorm + LM head over the vocabulary rows [begin, end) of the
+ * resident tied head + greedy argmax, for rows hidden rows (d_hidden: device
+ * bf16 [rows][896], before the final norm): d_values[r] is the best bf16
+ * logit of row r (as fp32) and d_indices[r] its global token id, highest id
+ * on ties (model_backend.py:108-114). begin and end are multiples of 128
+ * (151936 is one). Shards of the vocabulary combine by taking, per row, the
+ * largest value and then the highest index: the vocab-sharded LM head of
+ * several GPUs. Enqueued on `stream` (device buffers, no synchronisation);
+ * calls on one handle must not overlap other work of that handle. */
+int qwen_b200_lm_head_range(qwen_b200 *h, const uint16_t *d_hidden, uint32_t rows, uint32_t begin, uint32_t end,
+                            float *d_values, uint32_t *d_indices, void *stream);
 /* One decode step for n slots (one token each, each at its own position).
  * Host buffers; the host->device and device->host copies are inside the call.
  * The forward is replayed from a CUDA graph per (n, context bucket of 128):
