@@ -35,7 +35,7 @@
 //              residual row a thread adds is requested before any is used.
 // The LM head (argmax epilogue) is tc_lmhead_kernel below: the same roles in a
 // persistent loop over tiles.
-// No atomics, no TMA multicast. Every mbarrier wait is bounded: on timeout
+// No atomics; every TMA load fills this CTA's own shared memory. Every mbarrier wait is bounded: on timeout
 // the kernel records an error code in a device flag, skips its remaining work
 // and still frees its TMEM.
 #include "common.cuh"

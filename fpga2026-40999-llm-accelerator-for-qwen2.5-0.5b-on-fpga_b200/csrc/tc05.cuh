@@ -1,5 +1,5 @@
 // sm_100a building blocks written as inline PTX: mbarriers with bounded waits,
-// TMA 2D tile loads and contiguous bulk copies (no multicast), TMEM
+// TMA 2D tile loads and contiguous bulk copies into this CTA's own shared memory, TMEM
 // allocation, tcgen05.commit, the shared-memory matrix descriptor for the
 // 128-byte-swizzled K-major layout, and thread-block cluster helpers. The
 // tcgen05.mma instructions themselves (kind::i8, int8 x int8 -> int32) and
