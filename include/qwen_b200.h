@@ -83,7 +83,7 @@ int qwen_b200_load_synthetic(qwen_b200 *h, uint64_t seed);
 const char *qwen_b200_last_error(const qwen_b200 *h);
 
 /* ---- seeded synthetic assets (no checkpoint is available offline) ---------- */
-/* Writes <sd_root>/QWEN25/* in the reference format from a seed: fp32
+/* Writes the <sd_root>/QWEN25 files in the reference format from a seed: fp32
  * N(0,0.02) weights quantised per output channel with the rule of
  * legacy_.../tests/validate_model_weights.py:38-39, gains 1.0, bf16 biases. */
 int qwen_b200_synth_write(const char *sd_root, uint64_t seed);
