@@ -408,8 +408,9 @@ def prefill_sharded(args, rank, world, local):
     prompts = [rng.integers(0, VOCAB, T).astype(np.uint32) for _ in range(P)]  # the same on every rank
     eng = qwen_b200.Engine(device=local, max_seqs=P, max_context=T + 8, max_rows=4096).load_synthetic(SEED)
     vb, ve = D.vocab_shard(VOCAB, world, rank)
-    hid_local = torch.empty((len(mine), HID), dtype=torch.int16, device='cuda')
-    hid_all = torch.empty((P, HID), dtype=torch.int16, device='cuda')
+    # bf16 bit patterns, gathered as bfloat16 (NCCL has no 16-bit integer type)
+    hid_local = torch.empty((len(mine), HID), dtype=torch.bfloat16, device='cuda')
+    hid_all = torch.empty((P, HID), dtype=torch.bfloat16, device='cuda')
     vals = torch.empty(P, dtype=torch.float32, device='cuda')
     idx = torch.empty(P, dtype=torch.int32, device='cuda')
     vals_all = torch.empty(world * P, dtype=torch.float32, device='cuda')
@@ -421,7 +422,7 @@ def prefill_sharded(args, rank, world, local):
         for s in mine:
             eng.reset(s)
         _, hidden = eng.prefill(mine, [prompts[i] for i in mine], want_tokens=False, want_hidden=True)
-        hid_local.copy_(torch.from_numpy(hidden.view(np.int16)))
+        hid_local.copy_(torch.from_numpy(hidden.view(np.int16)).view(torch.bfloat16))
         if world > 1:
             import torch.distributed as dist
             dist.all_gather_into_tensor(hid_all, hid_local)
