@@ -594,11 +594,25 @@ def main():
     ap.add_argument('--prefill-prompts', type=int, default=8)
     ap.add_argument('--prefill-len', type=int, default=4096)
     ap.add_argument('--prefill-reps', type=int, default=2)
+    ap.add_argument('--prefill-only', action='store_true',
+                    help='run only the prefill record (prints its own JSON object)')
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
     if args.impl == 'reference':
         return run_reference(args)
+    if args.prefill_only:
+        import torch
+        rank, world, local = dist_setup()
+        torch.cuda.set_device(local)
+        rec = prefill_sharded(args, rank, world, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(rec), flush=True)
+        return 0
     return run_ours(args)
 
 
