@@ -649,6 +649,12 @@ int qwen_b200_close(qwen_b200 *h) {
 
 const char *qwen_b200_last_error(const qwen_b200 *h) { return h ? h->err.c_str() : "null handle"; }
 
+int qwen_b200_get_config(const qwen_b200 *h, qwen_b200_config *cfg) {
+    if (!h || !cfg) return QWEN_B200_EINVAL;
+    *cfg = h->cfg;
+    return QWEN_B200_OK;
+}
+
 static int load_model(qwen_b200 *h, qa_model &m) {
     int rc = allocate(h);
     if (!rc) rc = upload(h, m);

@@ -2,4 +2,4 @@
 an in-tree build script, and `Model`, the mirror of the reference's
 behavioural-model interface (legacy_100mhz_closed/src/PC/model_backend.py)."""
 from ._lib import LIB_PATH, QwenError, lib  # noqa: F401
-from .model import Engine, Model, bf16_to_f32  # noqa: F401
+from .model import Engine, Model, Scheduler, bf16_to_f32  # noqa: F401

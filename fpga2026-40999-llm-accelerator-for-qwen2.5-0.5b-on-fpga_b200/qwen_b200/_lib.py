@@ -31,6 +31,12 @@ _SIGNATURES = {
     'qwen_b200_load_assets': (c_int, [c_void_p, c_char_p]),
     'qwen_b200_load_synthetic': (c_int, [c_void_p, c_uint64]),
     'qwen_b200_last_error': (c_char_p, [c_void_p]),
+    'qwen_b200_get_config': (c_int, [c_void_p, POINTER(Config)]),
+    'qwen_b200_sched_open': (c_int, [c_void_p, c_uint32, POINTER(c_void_p)]),
+    'qwen_b200_sched_close': (c_int, [c_void_p]),
+    'qwen_b200_sched_submit': (c_int, [c_void_p, _P32, c_uint32, c_uint32, _P32]),
+    'qwen_b200_sched_step': (c_int, [c_void_p, _P32]),
+    'qwen_b200_sched_result': (c_int, [c_void_p, c_uint32, _P32, c_uint32, _P32, POINTER(c_int)]),
     'qwen_b200_synth_write': (c_int, [c_char_p, c_uint64]),
     'qwen_b200_synth_prompt': (None, [c_uint64, c_uint32, _P32]),
     'qwen_b200_reset': (c_int, [c_void_p, c_uint32]),

@@ -43,7 +43,7 @@ def _run(cmd):
 
 
 def sources():
-    return sorted(CSRC.glob('*.cu')) + sorted(CSRC.glob('*.c'))
+    return sorted(CSRC.glob('*.cu')) + sorted(CSRC.glob('*.c')) + sorted(CSRC.glob('*.cpp'))
 
 
 def build(verbose_ptxas=False, force=False):
@@ -63,6 +63,10 @@ def build(verbose_ptxas=False, force=False):
             cmd = [nvcc, *ARCH, *NVCC_FLAGS, '-ccbin', _gcc(), '-c', str(src), '-o', str(obj)]
             if verbose_ptxas:
                 cmd[1:1] = ['-Xptxas', '-v']
+        elif src.suffix == '.cpp':
+            gxx = '/usr/bin/g++' if os.path.exists('/usr/bin/g++') else 'g++'
+            cmd = [gxx, '-O3', '-fPIC', '-Wall', '-Wextra', '-std=c++17', f'-I{INCLUDE}', f'-I{CSRC}', '-c', str(src),
+                   '-o', str(obj)]
         else:
             cmd = [_gcc(), '-O3', '-fPIC', '-fopenmp', '-Wall', '-Wextra', '-Wno-format-truncation', '-std=c11', f'-I{INCLUDE}',
                    f'-I{CSRC}', '-c', str(src), '-o', str(obj)]

@@ -137,6 +137,46 @@ class Engine:
         check(lib().qwen_b200_set_dump(self.h, -1, None, None, None, None, None, None, None), self.h)
 
 
+class Scheduler:
+    """Continuous batching over one Engine (qwen_b200_sched_*): submit
+    prompts, step until done, read each request's tokens."""
+
+    def __init__(self, engine, prefill_budget=256):
+        handle = ctypes.c_void_p()
+        check(lib().qwen_b200_sched_open(engine.h, prefill_budget, ctypes.byref(handle)), engine.h)
+        self.s, self.engine = handle, engine
+
+    def submit(self, ids, max_new):
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        rid = c_uint32()
+        check(lib().qwen_b200_sched_submit(self.s, ptr(ids, c_uint32), len(ids), max_new, ctypes.byref(rid)))
+        return rid.value
+
+    def step(self):
+        """One scheduling step; returns the number of unfinished requests."""
+        n = c_uint32()
+        check(lib().qwen_b200_sched_step(self.s, ctypes.byref(n)), self.engine.h)
+        return n.value
+
+    def result(self, rid, cap=1024):
+        toks = np.empty(cap, dtype=np.uint32)
+        count, done = c_uint32(), ctypes.c_int()
+        check(lib().qwen_b200_sched_result(self.s, rid, ptr(toks, c_uint32), cap, ctypes.byref(count),
+                                           ctypes.byref(done)))
+        return toks[:min(count.value, cap)].tolist(), bool(done.value)
+
+    def close(self):
+        if self.s:
+            lib().qwen_b200_sched_close(self.s)
+            self.s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Model:
     """model_backend.Model with the math on a B200 (one sequence, slot 0)."""
 

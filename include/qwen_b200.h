@@ -81,6 +81,8 @@ int qwen_b200_load_assets(qwen_b200 *h, const char *sd_root);
 /* Same model as qwen_b200_synth_write(seed) would write, generated in memory. */
 int qwen_b200_load_synthetic(qwen_b200 *h, uint64_t seed);
 const char *qwen_b200_last_error(const qwen_b200 *h);
+/* The configuration the handle was opened with (defaults filled in). */
+int qwen_b200_get_config(const qwen_b200 *h, qwen_b200_config *cfg);
 
 /* ---- seeded synthetic assets (no checkpoint is available offline) ---------- */
 /* Writes the <sd_root>/QWEN25 files in the reference format from a seed: fp32
@@ -186,6 +188,30 @@ int qwen_b200_profile_decode(qwen_b200 *h, const uint32_t *tokens_in, uint32_t n
 /* Kernels enqueued by the last forward / decode step (a replayed graph
  * launches the same number). */
 uint32_t qwen_b200_step_launches(const qwen_b200 *h);
+
+/* ---- continuous batching (beyond the reference's one request at a time) ---- */
+/* A scheduler over one handle. The reference serves one request at a time
+ * (src/software/main.c:243-265). Here requests queue and share the GPU: each
+ * qwen_b200_sched_step admits waiting requests into free slots (first come,
+ * first served), prefills up to prefill_budget prompt tokens of admitted
+ * requests together (a longer prompt continues in the next steps), runs one
+ * batched decode step for every request that has a token, and retires
+ * requests at max_new tokens or at an end-of-text id (151643 / 151645, the
+ * stop ids of src/software/generation.c). Every request's tokens equal those
+ * of the request run alone. Single-threaded, like the handle; an error
+ * returned by a step leaves the scheduler unusable. */
+typedef struct qwen_b200_sched qwen_b200_sched;
+int qwen_b200_sched_open(qwen_b200 *h, uint32_t prefill_budget, qwen_b200_sched **out);
+int qwen_b200_sched_close(qwen_b200_sched *s);
+/* Queues a prompt; QWEN_B200_ESTATE when n + max_new exceeds a slot's capacity. */
+int qwen_b200_sched_submit(qwen_b200_sched *s, const uint32_t *ids, uint32_t n, uint32_t max_new,
+                           uint32_t *request_id);
+/* One scheduling step; *running (nullable) = requests not yet finished. */
+int qwen_b200_sched_step(qwen_b200_sched *s, uint32_t *running);
+/* Tokens produced so far (up to cap copied), and whether the request is
+ * finished; a finished request's result can be read once. */
+int qwen_b200_sched_result(qwen_b200_sched *s, uint32_t request_id, uint32_t *tokens, uint32_t cap,
+                           uint32_t *count, int *done);
 
 /* ---- CSR protocol: drop-in for struct qgen_ops (generation.h:5-14) ---------- */
 /* ops.context = handle; ops.write = qwen_b200_csr_write; ops.read =
