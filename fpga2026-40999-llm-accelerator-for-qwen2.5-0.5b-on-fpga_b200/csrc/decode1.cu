@@ -1189,14 +1189,14 @@ static int d1_grid = 0;
 // (QKV: 8 rows, O / down: 8 rows, gate/up: 80 rows per CTA at most).
 constexpr int D1_MIN_GRID = 144;
 
-int decode1_supported(int max_len) {
+int decode1_supported(int max_len, int limit) {
     static int sms = -1;
     if (sms < 0) {
         int dev = 0;
         if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             sms = 0;
     }
-    return sms >= D1_MIN_GRID && max_len >= 1 && max_len <= QB_D1_MAX_KEYS;
+    return sms >= D1_MIN_GRID && max_len >= 1 && max_len <= limit && max_len <= QB_D1_MAX_KEYS;
 }
 
 size_t decode1_smem_bytes() { return (size_t)d1_smem().total; }

@@ -75,7 +75,7 @@ struct qwen_b200 {
     uint32_t *meta = nullptr;  // [4][R]: ids | slots | positions | logit rows
     // persistent batch-1 decode: per-layer pointers, barrier counter and the
     // per-CTA argmax candidates
-    bool persistent = true;
+    int persistent = 1;  // 0 per-kernel, 1 persistent up to QB_D1_AUTO_KEYS keys, 2 up to QB_D1_MAX_KEYS
     bool expire_wait = false;  // test switch: the persistent step's last barrier times out
     D1Layer *d1_layers = nullptr;
     unsigned *d1_bar = nullptr;
@@ -401,7 +401,8 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
         LaunchScope ls(h, 0, st, 1);
         RK(launch_embed(h->embed, ids, n, h->x, st));
     }
-    if (n == 1 && nlog == 1 && identity && !dump && h->persistent && decode1_supported(max_len)) {
+    if (n == 1 && nlog == 1 && identity && !dump && h->persistent &&
+        decode1_supported(max_len, h->persistent == 1 ? QB_D1_AUTO_KEYS : QB_D1_MAX_KEYS)) {
         // one row: every layer, the LM head and the argmax in one persistent launch
         D1Args a;
         a.layers = h->d1_layers;
@@ -731,7 +732,7 @@ static void drop_graphs(qwen_b200 *h) {
 
 int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable) {
     if (!h) return QWEN_B200_EINVAL;
-    const bool p = enable != 0;
+    const int p = enable <= 0 ? 0 : (enable == 1 ? 1 : 2);
     if (p != h->persistent) drop_graphs(h);  // captured steps have the previous choice built in
     h->persistent = p;
     return QWEN_B200_OK;

@@ -39,6 +39,11 @@ int launch_qkv(const QkvArgs &a, cudaStream_t st);
 // the argmax in one cooperative launch of one CTA per SM.
 #define QB_NL 24
 #define QB_D1_MAX_KEYS 1024  // context keys held in shared memory by the attention phase
+// Default limit of the persistent path: beyond about 100 keys its attention
+// phase (two CTAs) is slower than the per-kernel path (measured single-row
+// step, host timed: 0.76 against 0.85 ms at 65 keys, 0.91 against 0.85 at
+// 128, 3.02 against 0.92 at 1001).
+#define QB_D1_AUTO_KEYS 96
 struct D1Layer {
     const int8_t *qkv, *o, *gu, *d;
     const float *s_qkv, *s_o, *s_gu, *s_d;
@@ -68,7 +73,8 @@ struct D1Args {
     // expires (code 20) with nothing asynchronous in flight
     int expire_last_barrier;
 };
-int decode1_supported(int max_len);
+// max_len within [1, limit] (limit <= QB_D1_MAX_KEYS) and a grid of enough SMs.
+int decode1_supported(int max_len, int limit = QB_D1_MAX_KEYS);
 size_t decode1_smem_bytes();
 int launch_decode1(const D1Args &a, cudaStream_t st);
 

@@ -56,8 +56,9 @@ class Engine:
         return p.value
 
     def set_persistent(self, enable):
-        """Single-row steps as one persistent launch (default) or per kernel."""
-        check(lib().qwen_b200_set_persistent_decode(self.h, 1 if enable else 0), self.h)
+        """Single-row steps as one persistent launch: True / 1 up to 96 keys
+        (the default), 2 up to 1024 keys, False / 0 never."""
+        check(lib().qwen_b200_set_persistent_decode(self.h, int(enable)), self.h)
         return self
 
     def reset(self, slot=0):

@@ -159,11 +159,13 @@ int qwen_b200_read_kv(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, i
 int qwen_b200_set_dump(qwen_b200 *h, int layer, uint16_t *q, uint16_t *k, uint16_t *v, uint16_t *ctx,
                        uint16_t *hbuf, uint16_t *mid, uint16_t *y);
 
-/* Single-row forwards and decode steps (context up to 1024 keys) run as one
- * persistent cooperative launch of one CTA per SM: every layer, the LM head
- * and the argmax, weights streamed into shared memory ahead of use, phases
- * separated by grid barriers; same arithmetic (and bits) as the per-kernel
- * path. enable = 0 selects the per-kernel path (default 1). */
+/* Single-row forwards and decode steps can run as one persistent
+ * cooperative launch of one CTA per SM: every layer, the LM head and the
+ * argmax, weights streamed into shared memory ahead of use, phases separated
+ * by grid barriers; same arithmetic (and bits) as the per-kernel path.
+ * enable = 1 (default): the persistent launch for contexts up to 96 keys,
+ * where it is the faster path; 2: up to 1024 keys; 0: always the per-kernel
+ * path. */
 int qwen_b200_set_persistent_decode(qwen_b200 *h, int enable);
 /* Test switch for the error path of the bounded device waits (reference:
  * the -2 / -3 returns of src/software/generation.c:21-25). While enabled, the

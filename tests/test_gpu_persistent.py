@@ -46,12 +46,13 @@ def test_persistent_forward_equals_per_kernel(engine, golden):
         assert np.array_equal(a, b), f'step {i}'
 
 
-@pytest.mark.parametrize('length', [300, 1023])
+@pytest.mark.parametrize('length', [90, 300, 1023])
 def test_persistent_long_context_equals_per_kernel(engine, golden, length):
     """Synthetic caches of `length` keys, then single-row steps up to the
-    1024-key limit of the persistent path."""
+    1024-key limit of the persistent path (setting 2; the default setting
+    hands contexts beyond 96 keys to the per-kernel path)."""
     out = {}
-    for persistent in (True, False):
+    for persistent in (2, False):
         engine.set_persistent(persistent)
         engine.reset(1)
         engine.fill_kv_synthetic(1, length, 99)
@@ -62,8 +63,8 @@ def test_persistent_long_context_equals_per_kernel(engine, golden, length):
             logits.append(from_bits(lg))
         out[persistent] = (toks, logits)
     engine.set_persistent(True)
-    assert out[True][0] == out[False][0]
-    for a, b in zip(out[True][1], out[False][1]):
+    assert out[2][0] == out[False][0]
+    for a, b in zip(out[2][1], out[False][1]):
         assert np.array_equal(a, b)
 
 
