@@ -1217,6 +1217,12 @@ int qwen_b200_op_kv8_append(const uint16_t *kv, uint32_t rows, const uint32_t *s
     return launch_kv8_append(kv, (int)rows, slots, positions, codes, scales, (int)capacity, (cudaStream_t)stream);
 }
 
+int qwen_b200_op_k16_append(const uint16_t *k, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                            int8_t *hi, int8_t *lo, uint16_t *m16, uint8_t *lock, uint32_t capacity, void *stream) {
+    if (!k || !slots || !positions || !hi || !lo || !m16 || !lock || !rows || !capacity) return QWEN_B200_EINVAL;
+    return launch_k16_append(k, (int)rows, slots, positions, hi, lo, m16, lock, (int)capacity, (cudaStream_t)stream);
+}
+
 int qwen_b200_op_qkv(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w,
                      const float *scale, const uint16_t *bias, const uint32_t *slots, const uint32_t *positions,
                      const float *table, uint16_t *q_out, int8_t *kcodes, float *kscales, int8_t *vcodes,

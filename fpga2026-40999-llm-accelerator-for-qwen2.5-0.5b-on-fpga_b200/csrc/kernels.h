@@ -130,6 +130,11 @@ int launch_gather_rows(const uint16_t *x, const uint32_t *rows_idx, int n, uint1
 int launch_decode_prologue(const uint32_t *tokens_in, int n, const uint32_t *slot_pos, uint32_t *ids,
                            uint32_t *slots, uint32_t *positions, cudaStream_t st);
 int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
+// The accelerator's own K cache format (kv8_rtl.cu): hi/lo code planes
+// [slot][2][cap][64], 16-bit mantissas [slot][2][cap], one exponent lock per
+// 256-token block [slot][2][ceil(cap / 256)].
+int launch_k16_append(const uint16_t *k, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *hi,
+                      int8_t *lo, uint16_t *m16, uint8_t *lock, int cap, cudaStream_t st);
 // Seeded synthetic KV8 contents for positions [0, length) of one slot, all layers.
 int launch_fill_kv(int8_t *kc, float *ks, int8_t *vc, float *vs, int layers, int nslots, int slot, int cap,
                    int length, uint64_t seed, cudaStream_t st);

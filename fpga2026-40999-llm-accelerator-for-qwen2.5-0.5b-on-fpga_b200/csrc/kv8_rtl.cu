@@ -1,0 +1,114 @@
+// The accelerator's own K cache format (its "K16" KV8 K path), as a second
+// cache format beside the engine's per-token-per-head int8 rule: the K
+// quantiser of src/rtl/kv8_k_quant.sv with the K chain's parameters (MARGIN 8,
+// MTOP 65535, RSHIFT 24, CODE_EXTRA 8) and the block-exponent lock of
+// src/rtl/kv8_k_write_chain.sv:503-600 (the first token of each 256-token
+// block fixes the exponent of that (head, block); later tokens of the block
+// are quantised against it):
+//   maxmag = max_d (k & 0x7fff), E = maxmag >> 7, M8 = 0x80 | (maxmag & 0x7f)
+//   block start: eb = E > 9 ? E - 8 : 1, m = ceil(M8 * 2^8 / 127),
+//                lock = (eb > 10 ? eb - 10 : 0) + 10 (255 at the top)
+//   later token: s = E - lock, n = M8 * 2^s (0x7fffff above s = 15, 0 below
+//                s = -15), m = min(ceil(n / 127), 65535)
+//   R = floor((2^24 + floor(m / 2)) / m), 2^24 for m = 0
+//   per dim:     N = M8d * 2^(Ed - lock) (0 when Ed = 0, 0xffffff above 15),
+//                q16 = min((N * R + 2^15) >> 16, 32639)
+//   planes:      hi = (q16 + 128) >> 8, lo = q16 mod 256, both negated (as
+//                bytes) for a negative k
+// Integer arithmetic only, so the codes are the oracle's (ref_k16_quant) bit
+// for bit. Two launches: the block starts among the rows publish their locks,
+// then every row is quantised (a later token reads its block's lock).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+// Largest |k| bit pattern (sign dropped) over one head's 64 dims: thread d
+// holds dim d; two warps.
+__device__ __forceinline__ unsigned k16_maxmag(unsigned kk, unsigned *red) {
+    unsigned m = kk & 0x7fffu;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    return max(red[0], red[1]);
+}
+
+__device__ __forceinline__ uint8_t k16_lock_of(unsigned maxmag) {
+    const unsigned E = maxmag >> 7;
+    const unsigned eb_r = E > 9 ? E - 8 : 1;
+    const unsigned ob = eb_r > 10 ? eb_r - 10 : 0;
+    return (uint8_t)(ob > 245 ? 255 : ob + 10);
+}
+
+struct K16Args {
+    const uint16_t *k;  // [rows][2][64]
+    const uint32_t *slots, *positions;
+    int8_t *hi, *lo;    // [slot][2][cap][64]
+    uint16_t *m16;      // [slot][2][cap]
+    uint8_t *lock;      // [slot][2][nblk]
+    int cap, nblk;
+};
+
+// grid (2 heads, rows), 64 threads: locks of the rows that start a block
+__global__ void __launch_bounds__(64) k16_lock_kernel(K16Args a) {
+    __shared__ unsigned red[2];
+    const int g = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
+    const uint32_t pos = a.positions[r];
+    if (pos % 256u) return;
+    const unsigned kk = a.k[((size_t)r * 2 + g) * QB_HD + d];
+    const unsigned maxmag = k16_maxmag(kk, red);
+    if (d == 0) a.lock[((size_t)a.slots[r] * 2 + g) * a.nblk + pos / 256u] = k16_lock_of(maxmag);
+}
+
+// grid (2 heads, rows), 64 threads: the codes and the mantissa of every row
+__global__ void __launch_bounds__(64) k16_quant_kernel(K16Args a) {
+    __shared__ unsigned red[2];
+    const int g = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
+    const uint32_t pos = a.positions[r], slot = a.slots[r];
+    const unsigned kk = a.k[((size_t)r * 2 + g) * QB_HD + d];
+    const unsigned maxmag = k16_maxmag(kk, red);
+    const unsigned E = maxmag >> 7, M8 = 0x80u | (maxmag & 0x7fu);
+    unsigned eb, m;
+    if (pos % 256u == 0) {
+        eb = k16_lock_of(maxmag);
+        const unsigned num = M8 << 8;
+        m = num / 127u + (num % 127u != 0);
+    } else {
+        eb = a.lock[((size_t)slot * 2 + g) * a.nblk + pos / 256u];
+        const int s = (int)E - (int)eb;
+        uint32_t n;
+        if (s > 15) n = 0x7fffffu;
+        else if (s < -15) n = 0;
+        else if (s < 0) n = M8 >> (-s);
+        else n = M8 << s;
+        const uint32_t quo = n / 127u, rem = n % 127u;
+        m = (quo > 65535u || (quo == 65535u && rem != 0)) ? 65535u : quo + (rem != 0);
+    }
+    const uint64_t R = m == 0 ? (1ull << 24) : ((1ull << 24) + (m >> 1)) / m;
+    const unsigned e = (kk >> 7) & 0xffu, mm = 0x80u | (kk & 0x7fu);
+    const int dd = (int)e - (int)eb;
+    uint32_t nn;
+    if (e == 0) nn = 0;
+    else if (dd >= 0) nn = dd > 15 ? 0xffffffu : mm << dd;
+    else nn = (-dd) >= 8 ? 0 : mm >> (-dd);
+    const uint64_t qv = ((uint64_t)nn * R + (1ull << 15)) >> 16;
+    const unsigned qmag = ((qv >> 16) != 0 || (qv & 0xffffu) > 32639u) ? 32639u : (unsigned)qv;
+    const unsigned hu = ((qmag + 128u) >> 8) & 0xffu, lu = qmag & 0xffu;
+    const bool neg = (kk >> 15) & 1u;
+    const size_t tok = ((size_t)slot * 2 + g) * a.cap + pos;
+    a.hi[tok * QB_HD + d] = (int8_t)(uint8_t)(neg ? (0u - hu) : hu);
+    a.lo[tok * QB_HD + d] = (int8_t)(uint8_t)(neg ? (0u - lu) : lu);
+    if (d == 0) a.m16[tok] = (uint16_t)m;
+}
+
+int launch_k16_append(const uint16_t *k, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *hi,
+                      int8_t *lo, uint16_t *m16, uint8_t *lock, int cap, cudaStream_t st) {
+    if (rows <= 0 || rows > 65535 || cap <= 0) return -1;
+    K16Args a{k, slots, positions, hi, lo, m16, lock, cap, (cap + 255) / 256};
+    k16_lock_kernel<<<dim3(2, rows), 64, 0, st>>>(a);
+    k16_quant_kernel<<<dim3(2, rows), 64, 0, st>>>(a);
+    return QB_LAUNCH_CHECK();
+}
+
+}  // namespace qb

@@ -72,6 +72,8 @@ _SIGNATURES = {
     'qwen_b200_op_rope': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
     'qwen_b200_op_kv8_append': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
                                         c_void_p]),
+    'qwen_b200_op_k16_append': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_uint32, c_void_p]),
     'qwen_b200_op_qkv': (c_int, [c_void_p, c_uint32, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p]),

@@ -271,6 +271,19 @@ int qwen_b200_op_rope(uint16_t *x, uint32_t rows, uint32_t heads, const uint32_t
  * clamp(rne(x/scale), +-127)). */
 int qwen_b200_op_kv8_append(const uint16_t *kv, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
                             int8_t *codes, float *scales, uint32_t capacity, void *stream);
+/* The accelerator's own K cache format (its K16 KV8 path,
+ * src/rtl/kv8_k_quant.sv with the K chain's parameters and the 256-token
+ * block lock of src/rtl/kv8_k_write_chain.sv:503-600), as an alternative
+ * cache format for RTL numeric parity: k [rows][2][64] bf16 (post-RoPE) of
+ * rows at positions[r] < capacity of slot slots[r] -> two int8 code planes
+ * hi, lo [slot][2][capacity][64] (k ~ (256 hi + lo) * m * 2^(lock - 142)),
+ * 16-bit mantissas m16 [slot][2][capacity] and the block exponent locks
+ * lock [slot][2][ceil(capacity / 256)], set by each block's first token. A
+ * call may hold a block's later tokens only if its first token is in the same
+ * call or was appended before. Integer arithmetic, bit-identical to the
+ * oracle's restatement. */
+int qwen_b200_op_k16_append(const uint16_t *k, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                            int8_t *hi, int8_t *lo, uint16_t *m16, uint8_t *lock, uint32_t capacity, void *stream);
 /* Fused attention block input: RMSNorm + QKV GEMM + bias + RoPE + KV8 append.
  * x [rows][896]; w [1152][896] (q|k|v rows); q_out [rows][896] post-RoPE. */
 int qwen_b200_op_qkv(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w,
