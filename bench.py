@@ -43,8 +43,9 @@ KV_BYTES_PER_TOKEN_LAYER = 2 * 2 * (64 + 4)  # K and V, 2 heads, 64 codes + fp32
 CLASSES = ['embedding', 'qkv_rope_kv8', 'attention', 'o_proj_residual', 'gate_up_swiglu', 'down_residual',
            'lm_head_argmax', 'bookkeeping', 'persistent_decode']
 # kernels behind each class: rows <= 8 run the GEMV family, more rows the
-# tcgen05 GEMM (qkv/o/gate_up/down/LM head), attention is one cluster launch
-KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_cluster_kernel',
+# tcgen05 GEMM (qkv/o/gate_up/down/LM head); attention is one launch of the
+# register-layout kernel (rows of up to 8 x 2304 keys, every workload here)
+KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_rs_kernel',
                      'o_proj_residual': 'gemv_kernel<896,EPI_RESIDUAL>',
                      'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
                      'down_residual': 'gemv_kernel<4864,EPI_RESIDUAL>',
@@ -56,7 +57,7 @@ KERNEL_NAMES_TC = dict(KERNEL_NAMES_GEMV,
                        o_proj_residual='act_quant_kernel<896> + tc_gemm_kernel<EPI_RESIDUAL>',
                        gate_up_swiglu='rmsnorm_limbs_kernel + tc_gemm_kernel<EPI_SWIGLU>',
                        down_residual='act_quant_kernel<4864> + tc_gemm_kernel<EPI_RESIDUAL>',
-                       lm_head_argmax='rmsnorm_limbs_kernel + tc_gemm_kernel<EPI_ARGMAX> + argmax_reduce_kernel')
+                       lm_head_argmax='rmsnorm_limbs_kernel + tc_lmhead_kernel + argmax_reduce_kernel')
 
 
 def kernel_names(rows):

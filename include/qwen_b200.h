@@ -331,10 +331,12 @@ int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint3
                                    const float *kscales, const int8_t *vcodes, const float *vscales,
                                    uint32_t capacity, uint16_t *ctx, void *stream);
 /* The same attention in one launch with no workspace (the form the engine
- * uses): a thread-block cluster per (row, KV head) splits the context (up to
- * 8 CTAs), keeps the scores in shared memory, runs both products on the
- * tensor cores and exchanges the softmax statistics and partial contexts over
- * distributed shared memory; results are independent of scheduling.
+ * uses): one CTA, or a thread-block cluster of up to 8 splitting the context,
+ * per (row, KV head); both products run on the tensor cores and the clusters
+ * exchange the softmax statistics and partial contexts over distributed
+ * shared memory; results are independent of scheduling. Rows of up to
+ * 8 x 2304 keys keep each lane's scores in its own shared-memory words (a
+ * 12-warp CTA), longer rows a 4-warp CTA with a shared score array.
  * max_len <= 32768 (the model's context limit); q, kcodes, vcodes 16-byte
  * aligned, ctx 8-byte aligned (QWEN_B200_EINVAL otherwise). */
 int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
