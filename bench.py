@@ -582,6 +582,171 @@ def committed_traffic(cls):
     return json.loads(p.read_text()).get(cls)
 
 
+# The operator microbenchmarks: the model's projection shapes [K x N] at
+# M rows, and KV8 GQA decode attention at context L for B rows.
+GEMM_SHAPES = [('qkv', HID, QKV, 'bias'), ('o', HID, HID, 'residual'), ('gate_up', HID, 2 * FFN, 'swiglu'),
+               ('down', FFN, HID, 'residual'), ('lm_head', HID, VOCAB, 'argmax')]
+GEMM_ROWS = [1, 8, 64, 512, 4096]
+ATTN_CONTEXTS = [512, 2048, 8192, 32768]
+ATTN_BATCHES = [1, 16, 64]
+INT8_DENSE_NOMINAL = 4.5e15  # int8 tensor ops/s, dense, nominal
+
+
+def micro_timer(torch, stream, reps):
+    """Median CUDA-event time (us) of one launch of fn after an L2 flush
+    (a 256 MB write, larger than the 126 MB L2) before every timed launch."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device='cuda')
+
+    def run(fn):
+        for _ in range(3):
+            assert fn() == 0
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            rc = fn()
+            e1.record(stream)
+            assert rc == 0, rc
+            e1.synchronize()
+            times.append(1000.0 * e0.elapsed_time(e1))
+        return statistics.median(times)
+    return run
+
+
+def micro_gemm(torch, L, stream, sp, timed, hbm):
+    """W8A16 projections through the C ABI: rows <= 8 on the GEMV family
+    (qwen_b200_op_gemm_w8a16 / _residual, op_swiglu, op_lm_head_argmax), more
+    rows on the tcgen05 GEMM (qwen_b200_op_gemm_w8a16_tc, which also builds the
+    activation limb planes; the LM head shape writes its bf16 logits). Weights
+    int8 per-output-channel from N(0, 0.02), activations bf16 N(0, 1)."""
+    g = torch.Generator(device='cuda').manual_seed(SEED)
+    out = []
+    for name, K, N, epi in GEMM_SHAPES:
+        wf = torch.randn(N, K, device='cuda', generator=g) * 0.02
+        scale = (wf.abs().amax(1) / 127).clamp_min(1e-12)
+        w = torch.round(wf / scale[:, None]).clamp(-127, 127).to(torch.int8).contiguous()
+        scale = scale.to(torch.bfloat16).float().contiguous()
+        del wf
+        bias = (torch.randn(N, device='cuda', generator=g) * 0.02).to(torch.bfloat16)
+        for M in GEMM_ROWS:
+            x = torch.randn(M, K, device='cuda', generator=g).to(torch.bfloat16)
+            n_out = N // 2 if epi == 'swiglu' else N
+            y = torch.zeros(M, n_out, device='cuda', dtype=torch.bfloat16)
+            ws = None
+            if M <= 8:
+                if epi == 'argmax':
+                    wsb = L.qwen_b200_lm_head_workspace(M, N)
+                    ws = torch.zeros(wsb, dtype=torch.uint8, device='cuda')
+                    tok = torch.zeros(M, dtype=torch.int32, device='cuda')
+                    fn = lambda: L.qwen_b200_op_lm_head_argmax(x.data_ptr(), M, None, 1e-6, w.data_ptr(),
+                                                               scale.data_ptr(), N, None, tok.data_ptr(),
+                                                               ws.data_ptr(), wsb, sp)
+                    kernel = 'lm_head_kernel + argmax_reduce_kernel'
+                elif epi == 'swiglu':
+                    fn = lambda: L.qwen_b200_op_swiglu(x.data_ptr(), M, None, 1e-6, w.data_ptr(), scale.data_ptr(),
+                                                       y.data_ptr(), sp)
+                    kernel = 'gemv_kernel<896,EPI_SWIGLU>'
+                elif epi == 'residual':
+                    fn = lambda: L.qwen_b200_op_gemm_w8a16_residual(x.data_ptr(), M, K, w.data_ptr(),
+                                                                    scale.data_ptr(), N, y.data_ptr(), sp)
+                    kernel = f'gemv_kernel<{K},EPI_RESIDUAL>'
+                else:
+                    fn = lambda: L.qwen_b200_op_gemm_w8a16(x.data_ptr(), M, K, w.data_ptr(), scale.data_ptr(), N,
+                                                           bias.data_ptr(), y.data_ptr(), sp)
+                    kernel = f'gemv_kernel<{K},EPI_BIAS>'
+            else:
+                code = {'bias': 1, 'residual': 2, 'swiglu': 3, 'argmax': 0}[epi]
+                wsb = L.qwen_b200_gemm_tc_workspace(M, N, K)
+                ws = torch.zeros(wsb, dtype=torch.uint8, device='cuda')
+                fn = lambda: L.qwen_b200_op_gemm_w8a16_tc(x.data_ptr(), M, K, w.data_ptr(), scale.data_ptr(), N,
+                                                          bias.data_ptr() if code == 1 else None, code, y.data_ptr(),
+                                                          ws.data_ptr(), wsb, sp)
+                kernel = 'act_quant_kernel + tc_gemm_kernel'
+            us = timed(fn)
+            if M > 8:
+                assert int(ws[:4].view(torch.int32)[0].item()) == 0, 'pipeline wait expired'
+            out_bytes = (0 if epi == 'argmax' and M <= 8 else M * n_out * 2) * (2 if epi == 'residual' else 1)
+            nbytes = N * K + 4 * N + (2 * N if epi == 'bias' else 0) + M * K * 2 + out_bytes
+            flops = 2.0 * M * N * K
+            rec = {'shape': f'{K}x{N}', 'name': name, 'rows': M, 'kernel': kernel, 'us': round(us, 2),
+                   'bytes': nbytes, 'gbs': round(nbytes / us / 1e3, 1), 'hbm_frac': round(nbytes / us / 1e3 / hbm, 4),
+                   'tops': round(flops / us / 1e6, 2)}
+            if M > 8:
+                # exact mode: four int8 limb planes, i.e. 4 x 2MNK tensor ops executed
+                rec['int8_tensor_frac_nominal'] = round(4 * flops / (us * 1e-6) / INT8_DENSE_NOMINAL, 4)
+            out.append(rec)
+            del x, y, ws
+        del w, scale, bias
+        torch.cuda.empty_cache()
+    return out
+
+
+def micro_attention(torch, L, stream, sp, timed, hbm):
+    """KV8 GQA decode attention (qwen_b200_op_attention_cluster, the engine's
+    form): B rows, each in its own slot at context L (keys 0..L-1); K and V
+    drawn bf16 N(0, 1), RoPE applied to K (qwen_b200_op_rope), quantised per
+    token and head by qwen_b200_op_kv8_append; q bf16 N(0, 1)."""
+    g = torch.Generator(device='cuda').manual_seed(SEED + 1)
+    out = []
+    for C in ATTN_CONTEXTS:
+        table_h = (ctypes.c_float * (C * 64))()
+        L.qwen_b200_rope_table(C, table_h)
+        table = torch.tensor(np.frombuffer(table_h, dtype=np.float32), device='cuda')
+        for B in ATTN_BATCHES:
+            rows = B * C
+            slots = torch.arange(B, dtype=torch.int32, device='cuda').repeat_interleave(C)
+            pos = torch.arange(C, dtype=torch.int32, device='cuda').repeat(B)
+            kc = torch.empty(B, 2, C, 64, dtype=torch.int8, device='cuda')
+            vc = torch.empty_like(kc)
+            ks = torch.empty(B, 2, C, dtype=torch.float32, device='cuda')
+            vs = torch.empty_like(ks)
+            for codes, scales, rope in ((kc, ks, True), (vc, vs, False)):
+                raw = torch.randn(rows, 2, 64, device='cuda', generator=g).to(torch.bfloat16)
+                if rope:
+                    assert L.qwen_b200_op_rope(raw.data_ptr(), rows, 2, pos.data_ptr(), table.data_ptr(), sp) == 0
+                assert L.qwen_b200_op_kv8_append(raw.data_ptr(), rows, slots.data_ptr(), pos.data_ptr(),
+                                                 codes.data_ptr(), scales.data_ptr(), C, sp) == 0
+                del raw
+            q = torch.randn(B, 14, 64, device='cuda', generator=g).to(torch.bfloat16)
+            ctx = torch.zeros(B, HID, dtype=torch.bfloat16, device='cuda')
+            qs = torch.arange(B, dtype=torch.int32, device='cuda')
+            qp = torch.full((B,), C - 1, dtype=torch.int32, device='cuda')
+            fn = lambda: L.qwen_b200_op_attention_cluster(q.data_ptr(), B, qs.data_ptr(), qp.data_ptr(), C,
+                                                          kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(),
+                                                          C, ctx.data_ptr(), sp)
+            us = timed(fn)
+            nbytes = B * C * KV_BYTES_PER_TOKEN_LAYER + B * HID * 2 * 2
+            out.append({'context': C, 'batch': B, 'kernel': 'attn_rs_kernel' if C <= 8 * 2304 else 'attn_cluster_kernel',
+                        'us': round(us, 2), 'bytes': nbytes, 'gbs': round(nbytes / us / 1e3, 1),
+                        'hbm_frac': round(nbytes / us / 1e3 / hbm, 4)})
+            del kc, vc, ks, vs, q, ctx, slots, pos
+            torch.cuda.empty_cache()
+    return out
+
+
+def run_micro(args):
+    import torch
+    import qwen_b200
+    torch.cuda.set_device(0)
+    L = qwen_b200.lib()
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    hbm, peak_kind = peaks()
+    timed = micro_timer(torch, stream, args.micro_reps)
+    clocks = Clocks(gpu_index(0))
+    clocks.start()
+    gemm = micro_gemm(torch, L, stream, sp, timed, hbm)
+    attn = micro_attention(torch, L, stream, sp, timed, hbm)
+    clk = clocks.stop()
+    print(json.dumps({'record': 'operator microbenchmarks', 'n_gpus': 1, 'hbm_peak_gbs': hbm,
+                      'peak_kind': peak_kind, 'reps': args.micro_reps,
+                      'timing': 'median of per-launch CUDA events on the launching stream, L2 flushed '
+                                '(256 MB write) before every timed launch, after 3 warm-up launches',
+                      'gemm': gemm, 'attention': attn, 'clocks': clk}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -597,11 +762,17 @@ def main():
     ap.add_argument('--prefill-reps', type=int, default=2)
     ap.add_argument('--prefill-only', action='store_true',
                     help='run only the prefill record (prints its own JSON object)')
+    ap.add_argument('--micro', action='store_true',
+                    help='run only the operator microbenchmarks (projection shapes x rows, attention '
+                         'contexts x batches; one GPU; prints its own JSON object)')
+    ap.add_argument('--micro-reps', type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
     if args.impl == 'reference':
         return run_reference(args)
+    if args.micro:
+        return run_micro(args)
     if args.prefill_only:
         import torch
         rank, world, local = dist_setup()

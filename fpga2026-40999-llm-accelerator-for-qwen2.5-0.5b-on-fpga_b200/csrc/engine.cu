@@ -1223,6 +1223,12 @@ int qwen_b200_op_k16_append(const uint16_t *k, uint32_t rows, const uint32_t *sl
     return launch_k16_append(k, (int)rows, slots, positions, hi, lo, m16, lock, (int)capacity, (cudaStream_t)stream);
 }
 
+int qwen_b200_op_v8_append(const uint16_t *v, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                           int8_t *codes, uint8_t *m8, uint8_t *lock, uint32_t capacity, void *stream) {
+    if (!v || !slots || !positions || !codes || !m8 || !lock || !rows || !capacity) return QWEN_B200_EINVAL;
+    return launch_v8_append(v, (int)rows, slots, positions, codes, m8, lock, (int)capacity, (cudaStream_t)stream);
+}
+
 int qwen_b200_op_qkv(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w,
                      const float *scale, const uint16_t *bias, const uint32_t *slots, const uint32_t *positions,
                      const float *table, uint16_t *q_out, int8_t *kcodes, float *kscales, int8_t *vcodes,

@@ -135,6 +135,10 @@ int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
 // 256-token block [slot][2][ceil(cap / 256)].
 int launch_k16_append(const uint16_t *k, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *hi,
                       int8_t *lo, uint16_t *m16, uint8_t *lock, int cap, cudaStream_t st);
+// The accelerator's own V cache format (kv8_rtl.cu): codes [slot][2][cap][64],
+// per-token mantissas m8 [slot][2][cap], layer locks [slot][2].
+int launch_v8_append(const uint16_t *v, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *codes,
+                     uint8_t *m8, uint8_t *lock, int cap, cudaStream_t st);
 // Seeded synthetic KV8 contents for positions [0, length) of one slot, all layers.
 int launch_fill_kv(int8_t *kc, float *ks, int8_t *vc, float *vs, int layers, int nslots, int slot, int cap,
                    int length, uint64_t seed, cudaStream_t st);

@@ -1,5 +1,6 @@
-// The accelerator's own K cache format (its "K16" KV8 K path), as a second
-// cache format beside the engine's per-token-per-head int8 rule: the K
+// The accelerator's own KV cache format (its "K16" K path; the V path is at
+// the end), as a second cache format beside the engine's per-token-per-head
+// int8 rule: the K
 // quantiser of src/rtl/kv8_k_quant.sv with the K chain's parameters (MARGIN 8,
 // MTOP 65535, RSHIFT 24, CODE_EXTRA 8) and the block-exponent lock of
 // src/rtl/kv8_k_write_chain.sv:503-600 (the first token of each 256-token
@@ -108,6 +109,95 @@ int launch_k16_append(const uint16_t *k, int rows, const uint32_t *slots, const 
     K16Args a{k, slots, positions, hi, lo, m16, lock, cap, (cap + 255) / 256};
     k16_lock_kernel<<<dim3(2, rows), 64, 0, st>>>(a);
     k16_quant_kernel<<<dim3(2, rows), 64, 0, st>>>(a);
+    return QB_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------ V path
+// The accelerator's own V cache format: the V quantiser of
+// src/rtl/kv8_v_quant.sv at the V chain's margin (MARGIN 2,
+// src/rtl/storage/qwen25_qkv_controller.v:1951) with the layer lock of
+// src/rtl/kv8_v_write_chain.sv:387-468 (a request's first token fixes the
+// exponent of each (layer, head); every token keeps its own 8-bit mantissa):
+//   maxmag, E, M8 as for K
+//   first token:  eb = E > 3 ? E - 2 : 1, m = ceil(M8 * 2^2 / 127),
+//                 lock = max(eb, 10) (the table convention floor)
+//   later token:  s = E - lock, n = M8 * 2^s (0x7fffff above 15, 0 below -15),
+//                 m = ceil(n / 127), 255 when larger
+//   R = floor((2^16 + floor(m / 2)) / m), 2^16 for m = 0
+//   per dim:      N = (M8d * 2^(Ed - lock)) mod 2^24 (no clamp), 0 for Ed = 0,
+//                 q = min((N * R + 2^15) >> 16, 127), negated for a negative v
+// value = code * m * 2^(lock - 134). The lock of a slot is taken by its token
+// at position 0; a later token of a slot whose lock is still 0 is quantised
+// as a first token and leaves the lock unset.
+struct V8Args {
+    const uint16_t *v;  // [rows][2][64]
+    const uint32_t *slots, *positions;
+    int8_t *codes;      // [slot][2][cap][64]
+    uint8_t *m8;        // [slot][2][cap]
+    uint8_t *lock;      // [slot][2]
+    int cap;
+};
+
+__device__ __forceinline__ unsigned v8_first_lock(unsigned maxmag) {
+    const unsigned E = maxmag >> 7;
+    const unsigned eb = E > 3 ? E - 2 : 1;
+    return eb > 10 ? eb : 10;
+}
+
+// grid (2 heads, rows), 64 threads: locks of the rows at position 0
+__global__ void __launch_bounds__(64) v8_lock_kernel(V8Args a) {
+    __shared__ unsigned red[2];
+    const int g = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
+    if (a.positions[r] != 0) return;
+    const unsigned vv = a.v[((size_t)r * 2 + g) * QB_HD + d];
+    const unsigned maxmag = k16_maxmag(vv, red);
+    if (d == 0) a.lock[(size_t)a.slots[r] * 2 + g] = (uint8_t)v8_first_lock(maxmag);
+}
+
+// grid (2 heads, rows), 64 threads: the codes and the mantissa of every row
+__global__ void __launch_bounds__(64) v8_quant_kernel(V8Args a) {
+    __shared__ unsigned red[2];
+    const int g = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
+    const uint32_t pos = a.positions[r], slot = a.slots[r];
+    const unsigned vv = a.v[((size_t)r * 2 + g) * QB_HD + d];
+    const unsigned maxmag = k16_maxmag(vv, red);
+    const unsigned E = maxmag >> 7, M8 = 0x80u | (maxmag & 0x7fu);
+    unsigned eb = pos == 0 ? 0u : a.lock[(size_t)slot * 2 + g];
+    unsigned m;
+    if (eb == 0) {  // the layer's first token (or no lock yet)
+        eb = v8_first_lock(maxmag);
+        const unsigned num = M8 << 2;
+        m = num / 127u + (num % 127u != 0);
+    } else {
+        const int s = (int)E - (int)eb;
+        uint32_t n;
+        if (s > 15) n = 0x7fffffu;
+        else if (s < -15) n = 0;
+        else if (s < 0) n = M8 >> (-s);
+        else n = M8 << s;
+        const uint32_t quo = n / 127u, rem = n % 127u;
+        m = (quo > 255u || (quo == 255u && rem != 0)) ? 255u : quo + (rem != 0);
+    }
+    const uint64_t R = m == 0 ? (1ull << 16) : ((1ull << 16) + (m >> 1)) / m;
+    const unsigned e = (vv >> 7) & 0xffu, mm = 0x80u | (vv & 0x7fu);
+    const int dd = (int)e - (int)eb;
+    uint32_t nn;
+    if (e == 0) nn = 0;
+    else if (dd >= 0) nn = dd >= 24 ? 0 : (mm << dd) & 0xffffffu;
+    else nn = (-dd) >= 8 ? 0 : mm >> (-dd);
+    const uint64_t qv = ((uint64_t)nn * R + (1ull << 15)) >> 16;
+    const unsigned q = qv > 127 ? 127u : (unsigned)qv;
+    const size_t tok = ((size_t)slot * 2 + g) * a.cap + pos;
+    a.codes[tok * QB_HD + d] = (int8_t)(uint8_t)(((vv >> 15) & 1u) ? (0u - q) : q);
+    if (d == 0) a.m8[tok] = (uint8_t)m;
+}
+
+int launch_v8_append(const uint16_t *v, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *codes,
+                     uint8_t *m8, uint8_t *lock, int cap, cudaStream_t st) {
+    if (rows <= 0 || rows > 65535 || cap <= 0) return -1;
+    V8Args a{v, slots, positions, codes, m8, lock, cap};
+    v8_lock_kernel<<<dim3(2, rows), 64, 0, st>>>(a);
+    v8_quant_kernel<<<dim3(2, rows), 64, 0, st>>>(a);
     return QB_LAUNCH_CHECK();
 }
 

@@ -74,6 +74,8 @@ _SIGNATURES = {
                                         c_void_p]),
     'qwen_b200_op_k16_append': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_uint32, c_void_p]),
+    'qwen_b200_op_v8_append': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_uint32, c_void_p]),
     'qwen_b200_op_qkv': (c_int, [c_void_p, c_uint32, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
                                  c_void_p]),

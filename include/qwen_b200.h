@@ -284,6 +284,19 @@ int qwen_b200_op_kv8_append(const uint16_t *kv, uint32_t rows, const uint32_t *s
  * oracle's restatement. */
 int qwen_b200_op_k16_append(const uint16_t *k, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
                             int8_t *hi, int8_t *lo, uint16_t *m16, uint8_t *lock, uint32_t capacity, void *stream);
+/* The accelerator's own V cache format (its KV8 V path, src/rtl/kv8_v_quant.sv
+ * at the V chain's margin 2, src/rtl/storage/qwen25_qkv_controller.v:1951,
+ * with the layer lock of src/rtl/kv8_v_write_chain.sv:387-468), the partner
+ * of qwen_b200_op_k16_append: v [rows][2][64] bf16 of rows at positions[r] <
+ * capacity of slot slots[r] -> int8 codes [slot][2][capacity][64], 8-bit
+ * per-token mantissas m8 [slot][2][capacity] and the layer's exponent lock
+ * lock [slot][2] (v ~ code * m * 2^(lock - 134)). The lock is set by the
+ * slot's token at position 0 (the RTL restarts it at a request's token 0);
+ * later tokens need it set, in the same call or before (a later token whose
+ * lock is still 0 is quantised as a first token and sets nothing). Integer
+ * arithmetic, bit-identical to the oracle's restatement. */
+int qwen_b200_op_v8_append(const uint16_t *v, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
+                           int8_t *codes, uint8_t *m8, uint8_t *lock, uint32_t capacity, void *stream);
 /* Fused attention block input: RMSNorm + QKV GEMM + bias + RoPE + KV8 append.
  * x [rows][896]; w [1152][896] (q|k|v rows); q_out [rows][896] post-RoPE. */
 int qwen_b200_op_qkv(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w,

@@ -1068,3 +1068,66 @@ void ref_k16_quant(const uint16_t *k, int first, uint8_t *lock, int8_t *hi, int8
     *etab = (uint8_t)k16_kexp(eb);
     *clip = m == 0 || m == 65535u || k16_norm_exp(eb) == 255;
 }
+
+/* ------------------------------------------------ RTL-format V quantiser
+ * The accelerator's own KV8 V format, restated from src/rtl/kv8_v_quant.sv
+ * with the V chain's margin (MARGIN 2: src/rtl/storage/
+ * qwen25_qkv_controller.v:1951, and the V case of
+ * src/verification/tb_kv8_quant_pipeline.sv) and the layer lock of
+ * src/rtl/kv8_v_write_chain.sv:387-468 (the first token of a request fixes
+ * the exponent of that (layer, head); every token keeps its own 8-bit
+ * mantissa):
+ *   maxmag = max_d (v & 0x7fff), E = maxmag >> 7, M8 = 0x80 | (maxmag & 0x7f)
+ *   first : eb = E > 3 ? E - 2 : 1, m = ceil(M8 * 2^2 / 127) (5..9),
+ *           lock = max(eb, 10) (the table convention round trip of
+ *           kv8_v_quant.sv:110 and kv8_v_write_chain.sv:302: eb - 10
+ *           floored at 0, plus 10)
+ *   later : s = E - lock, n = M8 * 2^s (0x7fffff above s = 15, 0 below -15),
+ *           m = ceil(n / 127), 255 when that exceeds 255
+ *   R = floor((2^16 + floor(m / 2)) / m) (2^16 when m = 0)
+ *   per dim: N = (M8d * 2^(Ed - lock)) mod 2^24 (the 24-bit shifter of
+ *   kv8_v_quant.sv:279-281, without a clamp; 0 for Ed = 0),
+ *   q = min((N * R + 2^15) >> 16, 127), negated for a negative v.
+ * The dequantised value is code * m * 2^(lock - 134); the layer's published
+ * scale is the bf16 2^(lock - 134) (m = 1, kv8_v_write_chain.sv:306-332,
+ * 421-437). clip: m == 0 or m == 255 (the chain's witness). */
+void ref_v8_quant(const uint16_t *v, int first, uint8_t *lock, int8_t *codes, uint8_t *m8, uint16_t *scale_bf16,
+                  int *clip) {
+    unsigned maxmag = 0;
+    for (int d = 0; d < HD; ++d)
+        if ((v[d] & 0x7fffu) > maxmag) maxmag = v[d] & 0x7fffu;
+    const unsigned E = maxmag >> 7, M8 = 0x80u | (maxmag & 0x7fu);
+    unsigned eb, m;
+    if (first) {
+        const unsigned eb_calc = E > 3 ? E - 2 : 1;
+        const unsigned num = M8 << 2;
+        m = num / 127 + (num % 127 != 0);
+        eb = eb_calc > 10 ? eb_calc : 10;
+        *lock = (uint8_t)eb;
+    } else {
+        eb = *lock;
+        const int s = (int)E - (int)eb;
+        uint32_t n;
+        if (s > 15) n = 0x7fffffu;
+        else if (s < -15) n = 0;
+        else if (s < 0) n = M8 >> (-s);
+        else n = M8 << s;
+        const uint32_t quo = n / 127, rem = n % 127;
+        m = (quo > 255u || (quo == 255u && rem != 0)) ? 255u : quo + (rem != 0);
+    }
+    const uint64_t R = m == 0 ? (1ull << 16) : ((1ull << 16) + (m >> 1)) / m;
+    for (int i = 0; i < HD; ++i) {
+        const unsigned vv = v[i], e = (vv >> 7) & 0xffu, mm = 0x80u | (vv & 0x7fu);
+        const int d = (int)e - (int)eb;
+        uint32_t nn;
+        if (e == 0) nn = 0;
+        else if (d >= 0) nn = d >= 24 ? 0 : (mm << d) & 0xffffffu;
+        else nn = (-d) >= 8 ? 0 : mm >> (-d);
+        const uint64_t qv = ((uint64_t)nn * R + (1ull << 15)) >> 16;
+        const uint8_t q = (uint8_t)(qv > 127 ? 127 : qv);
+        codes[i] = (int8_t)((vv >> 15) & 1u ? (uint8_t)(0u - q) : q);
+    }
+    *m8 = (uint8_t)m;
+    *scale_bf16 = (uint16_t)(eb > 7 ? (eb - 7u) << 7 : 0);
+    *clip = m == 0 || m == 255u;
+}
