@@ -53,6 +53,7 @@ struct AcArgs {
     const uint16_t *q;
     const uint32_t *slots, *positions;
     const int8_t *kc, *vc;
+    const int8_t *klo;  // nullable: low planes of 16-bit K codes (256 * kc + klo), same layout as kc
     const float *ks, *vs;
     int cap;
     uint16_t *ctx;
@@ -254,14 +255,35 @@ __global__ void __launch_bounds__(AM_THREADS, 2) attn_cluster_kernel(AcArgs a) {
                 mma_s8_16832(d[l], u.x, v.x, u.y, v.y, qb[l][0][0], qb[l][0][1]);
                 mma_s8_16832(d[l], u.z, v.z, u.w, v.w, qb[l][1][0], qb[l][1][1]);
             }
+            long long dot[4];
+#pragma unroll
+            for (int f = 0; f < 4; ++f)  // per-limb sums over 64 dims are below 2^20: pairs add in int32
+                dot[f] = (long long)(d[0][f] + d[1][f] * 128) + (long long)(d[2][f] + d[3][f] * 128) * 16384ll;
+            if (a.klo) {
+                // 16-bit codes: dot = 256 * (Q . high) + Q . low, the low plane
+                // read straight from the cache (keys past the end read as 0)
+                const int8_t *lg = a.klo + (kvbase + kb) * QB_HD;
+                const uint4 z4 = make_uint4(0, 0, 0, 0);
+                const uint4 ul = k0 < nkeys ? *reinterpret_cast<const uint4 *>(lg + gid * QB_HD + 16 * tig) : z4;
+                const uint4 vl =
+                    k1 < nkeys ? *reinterpret_cast<const uint4 *>(lg + (gid + 8) * QB_HD + 16 * tig) : z4;
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    int e[4] = {0, 0, 0, 0};
+                    mma_s8_16832(e, ul.x, vl.x, ul.y, vl.y, qb[l][0][0], qb[l][0][1]);
+                    mma_s8_16832(e, ul.z, vl.z, ul.w, vl.w, qb[l][1][0], qb[l][1][1]);
+#pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const long long wl = 1ll << (7 * l);
+                        dot[f] += (long long)d[l][f] * 255ll * wl + (long long)e[f] * wl;
+                    }
+                }
+            }
             float sc[4];
 #pragma unroll
             for (int f = 0; f < 4; ++f) {
-                // per-limb sums over 64 dims are below 2^20: pairs add in int32
-                const long long dot =
-                    (long long)(d[0][f] + d[1][f] * 128) + (long long)(d[2][f] + d[3][f] * 128) * 16384ll;
                 const float ks = kss[f < 2 ? k0 : k1];
-                sc[f] = rbf(__fmul_rn(unalign28(dot, (f & 1) ? e_h1 : e_h0), ks) * 0.125f);
+                sc[f] = rbf(__fmul_rn(unalign28(dot[f], (f & 1) ? e_h1 : e_h0), ks) * 0.125f);
             }
             if (k0 < nkeys) {
                 S[h0 * sld + k0] = sc[0];
@@ -511,15 +533,19 @@ static __device__ unsigned g_attn_op_err;  // wait-timeout flag of calls that pa
 
 int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions,
                              int max_len, const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap,
-                             uint16_t *ctx, unsigned *err, cudaStream_t st) {
+                             uint16_t *ctx, unsigned *err, cudaStream_t st, const int8_t *klo) {
     if (rows <= 0 || max_len > cap || rows > 65535) return -1;
-    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc) |
+         reinterpret_cast<uintptr_t>(klo)) & 15)
         return -1;  // 16-byte q loads and bulk copies of the code rows
     if (reinterpret_cast<uintptr_t>(ctx) & 7) return -1;
     if (!err && cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_attn_op_err) != cudaSuccess) return -3;
-    // contexts up to 8 x 2304 keys: scores in registers (attention_rs.cu)
-    const int rc = launch_attention_rs(q, rows, slots, positions, max_len, kc, ks, vc, vs, cap, ctx, err, st);
-    if (rc != 1) return rc;
+    // contexts up to 8 x 2304 keys with 8-bit K codes: scores in registers
+    // (attention_rs.cu)
+    if (!klo) {
+        const int rc = launch_attention_rs(q, rows, slots, positions, max_len, kc, ks, vc, vs, cap, ctx, err, st);
+        if (rc != 1) return rc;
+    }
     int splits, kpc;
     if (attention_cluster_plan(rows, max_len, &splits, &kpc)) return -1;
     AcArgs a;
@@ -528,6 +554,7 @@ int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots,
     a.positions = positions;
     a.kc = kc;
     a.vc = vc;
+    a.klo = klo;
     a.ks = ks;
     a.vs = vs;
     a.cap = cap;

@@ -59,6 +59,13 @@ struct qwen_b200 {
     // KV8 caches: codes [layer][slot][2][cap][64], scales [layer][slot][2][cap]
     int8_t *kc = nullptr, *vc = nullptr;
     float *ks = nullptr, *vs = nullptr;
+    // QWEN_B200_FLAG_RTL_KV: low K planes (layout of kc), K block locks
+    // [layer][slot][2][nblk], V layer locks [layer][slot][2], and the
+    // post-RoPE k | v rows [R][256] the append reads
+    bool rtl = false;
+    int8_t *klo = nullptr;
+    uint8_t *klock = nullptr, *vlock = nullptr;
+    uint16_t *rtl_kv = nullptr;
     // activations
     uint16_t *x = nullptr, *q = nullptr, *ctx = nullptr, *mid = nullptr, *xl = nullptr, *logits = nullptr;
     uint16_t *blogits = nullptr;  // [R][vocab] logits of batched steps that return them
@@ -173,6 +180,7 @@ constexpr size_t DUMP_COLS = 896 + 256 + 896 + 896 + 4864 + 896;
 
 size_t kv_layer_codes(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * h->cfg.max_context * 64; }
 size_t kv_layer_scales(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * h->cfg.max_context; }
+size_t rtl_klock_layer(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * ((h->cfg.max_context + 255) / 256); }
 
 int allocate(qwen_b200 *h) {
     const qwen_b200_config &c = h->cfg;
@@ -233,6 +241,15 @@ int allocate(qwen_b200 *h) {
     CK(cudaMemset(h->vc, 0, kv_layer_codes(h) * NL));
     CK(cudaMemset(h->ks, 0, kv_layer_scales(h) * NL * 4));
     CK(cudaMemset(h->vs, 0, kv_layer_scales(h) * NL * 4));
+    if (h->rtl) {
+        if ((rc = dalloc(h, (void **)&h->klo, kv_layer_codes(h) * NL))) return rc;
+        if ((rc = dalloc(h, (void **)&h->klock, rtl_klock_layer(h) * NL))) return rc;
+        if ((rc = dalloc(h, (void **)&h->vlock, (size_t)c.max_seqs * 2 * NL))) return rc;
+        if ((rc = dalloc(h, (void **)&h->rtl_kv, R * 256 * 2))) return rc;
+        CK(cudaMemset(h->klo, 0, kv_layer_codes(h) * NL));
+        CK(cudaMemset(h->klock, 0, rtl_klock_layer(h) * NL));
+        CK(cudaMemset(h->vlock, 0, (size_t)c.max_seqs * 2 * NL));
+    }
     // activations
     if ((rc = dalloc(h, (void **)&h->x, R * HID * 2))) return rc;
     if ((rc = dalloc(h, (void **)&h->q, R * HID * 2))) return rc;
@@ -401,7 +418,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
         LaunchScope ls(h, 0, st, 1);
         RK(launch_embed(h->embed, ids, n, h->x, st));
     }
-    if (n == 1 && nlog == 1 && identity && !dump && h->persistent &&
+    if (n == 1 && nlog == 1 && identity && !dump && h->persistent && !h->rtl &&
         decode1_supported(max_len, h->persistent == 1 ? QB_D1_AUTO_KEYS : QB_D1_MAX_KEYS)) {
         // one row: every layer, the LM head and the argmax in one persistent launch
         D1Args a;
@@ -457,7 +474,8 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
         a.ks = ks;
         a.vs = vs;
         a.cap = cap;
-        a.kv_out = dq ? dq + (size_t)n * 896 : nullptr;
+        a.kv_out = dq ? dq + (size_t)n * 896 : (h->rtl ? h->rtl_kv : nullptr);
+        int8_t *klo = h->rtl ? h->klo + kv_layer_codes(h) * l : nullptr;
         if (n >= TC_MIN_ROWS) {
             LaunchScope ls(h, 1, st, 3);
             int rc = norm_limbs(h, h->x, W.g_attn, n, eps, st);
@@ -468,10 +486,17 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
             LaunchScope ls(h, 1, st, 1);
             RK(launch_qkv(a, st));
         }
+        if (h->rtl) {
+            // the accelerator's formats over the engine-format codes just written
+            LaunchScope ls(h, 1, st, 2);
+            RK(launch_rtl_kv_append(a.kv_out, n, slots, positions, kc, klo, ks,
+                                    h->klock + rtl_klock_layer(h) * l, vc, vs,
+                                    h->vlock + (size_t)h->cfg.max_seqs * 2 * l, cap, st));
+        }
         {
             LaunchScope ls(h, 2, st, 1);
             RK(launch_attention_cluster(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx,
-                                        reinterpret_cast<unsigned *>(h->tc_ws), st));
+                                        reinterpret_cast<unsigned *>(h->tc_ws), st, klo));
         }
         if (dq) {
             CK(cudaMemcpyAsync(dq, h->q, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
@@ -615,11 +640,13 @@ int qwen_b200_open(const qwen_b200_config *cfg, qwen_b200 **out) {
     qwen_b200_config c;
     qwen_b200_default_config(&c);
     if (cfg) c = *cfg;
-    if (c.max_seqs == 0 || c.max_context == 0 || c.max_rows == 0 || c.device < 0 || !(c.rms_eps > 0.f))
+    if (c.max_seqs == 0 || c.max_context == 0 || c.max_rows == 0 || c.device < 0 || !(c.rms_eps > 0.f) ||
+        (c.flags & ~QWEN_B200_FLAG_RTL_KV))
         return QWEN_B200_EINVAL;
     qwen_b200 *h = new (std::nothrow) qwen_b200();
     if (!h) return QWEN_B200_ENOMEM;
     h->cfg = c;
+    h->rtl = (c.flags & QWEN_B200_FLAG_RTL_KV) != 0;
     *out = h;
     return QWEN_B200_OK;
 }
@@ -1039,11 +1066,37 @@ int qwen_b200_fill_kv_synthetic(qwen_b200 *h, uint32_t slot, uint32_t length, ui
     if (rc) return rc;
     if (slot >= h->cfg.max_seqs || length == 0 || length > h->cfg.max_context)
         return fail(h, QWEN_B200_EINVAL, "bad slot or length");
+    if (h->rtl) return fail(h, QWEN_B200_ESTATE, "synthetic KV fill is not available in the RTL KV format");
     RK(launch_fill_kv(h->kc, h->ks, h->vc, h->vs, NL, (int)h->cfg.max_seqs, (int)slot, (int)h->cfg.max_context,
                       (int)length, seed, h->stream));
     h->pos[slot] = length;
     if ((rc = sync_slot_positions(h, h->stream))) return rc;
     CK(cudaStreamSynchronize(h->stream));
+    return QWEN_B200_OK;
+}
+
+int qwen_b200_read_kv_rtl(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, int8_t *klo, uint8_t *klock,
+                          uint8_t *vlock) {
+    if (!h) return QWEN_B200_EINVAL;
+    int rc = ensure_device(h);
+    if (rc) return rc;
+    if (!h->rtl) return fail(h, QWEN_B200_ESTATE, "the handle does not hold the RTL KV format");
+    if (slot >= h->cfg.max_seqs || layer >= (uint32_t)NL || n > h->cfg.max_context)
+        return fail(h, QWEN_B200_EINVAL, "bad slot/layer/length");
+    CK(cudaStreamSynchronize(h->stream));
+    const size_t cap = h->cfg.max_context, nblk = (cap + 255) / 256;
+    for (int g = 0; g < 2; ++g) {
+        const size_t row = ((size_t)slot * 2 + g) * cap;
+        if (klo)
+            CK(cudaMemcpy(klo + (size_t)g * n * 64, h->klo + kv_layer_codes(h) * layer + row * 64, (size_t)n * 64,
+                          cudaMemcpyDeviceToHost));
+        if (klock)
+            CK(cudaMemcpy(klock + (size_t)g * nblk, h->klock + rtl_klock_layer(h) * layer + ((size_t)slot * 2 + g) * nblk,
+                          nblk, cudaMemcpyDeviceToHost));
+    }
+    if (vlock)
+        CK(cudaMemcpy(vlock, h->vlock + (size_t)h->cfg.max_seqs * 2 * layer + (size_t)slot * 2, 2,
+                      cudaMemcpyDeviceToHost));
     return QWEN_B200_OK;
 }
 

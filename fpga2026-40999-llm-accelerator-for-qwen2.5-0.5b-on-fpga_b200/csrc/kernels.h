@@ -99,10 +99,12 @@ int launch_attention(const uint16_t *q, int rows, const uint32_t *slots, const u
 // Single-launch attention: one thread-block cluster per (row, KV head) over
 // the row's context; no workspace. max_len <= 32768; q, kc, vc 16-byte and ctx
 // 8-byte aligned. A bounded wait that expires records code 11/12 in *err (a
-// library-internal flag when err is null).
+// library-internal flag when err is null). klo (nullable, 16-byte aligned):
+// the low planes of 16-bit K codes (the accelerator's K16 format: the code
+// of a dim is 256 * kc + klo); such calls always take this kernel.
 int launch_attention_cluster(const uint16_t *q, int rows, const uint32_t *slots, const uint32_t *positions,
                              int max_len, const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap,
-                             uint16_t *ctx, unsigned *err, cudaStream_t st);
+                             uint16_t *ctx, unsigned *err, cudaStream_t st, const int8_t *klo = nullptr);
 // The same attention with transposed tensor-core scores kept lane-private in
 // shared memory (attention_rs.cu: CTAs of 12 warps, up to 8 per row for
 // long contexts); 0 when launched, 1 when a row needs more than 8 CTAs (the
@@ -135,6 +137,13 @@ int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
 // 256-token block [slot][2][ceil(cap / 256)].
 int launch_k16_append(const uint16_t *k, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *hi,
                       int8_t *lo, uint16_t *m16, uint8_t *lock, int cap, cudaStream_t st);
+// The engine's RTL KV mode (kv8_rtl.cu): kv [rows][256] post-RoPE k | v (bf16)
+// appended in the accelerator's K16 and V formats into one layer's caches:
+// kc / klo the high / low K planes, ks = m16 * 2^(lock - 142), vc, vs = m8 *
+// 2^(lock - 134); klock [slot][2][ceil(cap / 256)], vlock [slot][2].
+int launch_rtl_kv_append(const uint16_t *kv, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *kc,
+                         int8_t *klo, float *ks, uint8_t *klock, int8_t *vc, float *vs, uint8_t *vlock, int cap,
+                         cudaStream_t st);
 // The accelerator's own V cache format (kv8_rtl.cu): codes [slot][2][cap][64],
 // per-token mantissas m8 [slot][2][cap], layer locks [slot][2].
 int launch_v8_append(const uint16_t *v, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *codes,

@@ -11,6 +11,7 @@ LIB_PATH = Path(__file__).resolve().parents[1] / 'libqwen_b200.so'
 
 OK, EINVAL, ETIMEOUT, EDEVICE, ETOKEN, EOUTPUT, ENOMEM, EIO, ESTATE, ESCRATCH = 0, -1, -2, -3, -4, -5, -6, -7, -8, -9
 NOALLOC_SCRATCH_BYTES = 16 << 20
+FLAG_RTL_KV = 1
 VOCAB, HIDDEN, FFN, LAYERS = 151936, 896, 4864, 24
 
 
@@ -50,6 +51,8 @@ _SIGNATURES = {
     'qwen_b200_decode_step_device': (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
     'qwen_b200_fill_kv_synthetic': (c_int, [c_void_p, c_uint32, c_uint32, c_uint64]),
     'qwen_b200_read_kv': (c_int, [c_void_p, c_uint32, c_uint32, c_uint32, _P8, _PF, _P8, _PF]),
+    'qwen_b200_read_kv_rtl': (c_int, [c_void_p, c_uint32, c_uint32, c_uint32, _P8, POINTER(ctypes.c_uint8),
+                                      POINTER(ctypes.c_uint8)]),
     'qwen_b200_set_dump': (c_int, [c_void_p, c_int, _P16, _P16, _P16, _P16, _P16, _P16, _P16]),
     'qwen_b200_profile_decode': (c_int, [c_void_p, _P32, c_uint32, _P32, _PF, _P32]),
     'qwen_b200_step_launches': (c_uint32, [c_void_p]),

@@ -21,11 +21,12 @@ def bf16_to_f32(bits):
 class Engine:
     """One libqwen_b200 handle (one GPU). Owns device memory until close()."""
 
-    def __init__(self, device=0, max_seqs=1, max_context=256, max_rows=256, rms_eps=1e-6):
+    def __init__(self, device=0, max_seqs=1, max_context=256, max_rows=256, rms_eps=1e-6, flags=0):
+        """flags: 0, or qwen_b200.FLAG_RTL_KV for the accelerator's own KV format."""
         cfg = _lib.Config()
         lib().qwen_b200_default_config(ctypes.byref(cfg))
-        cfg.device, cfg.max_seqs, cfg.max_context, cfg.max_rows, cfg.rms_eps = (
-            device, max_seqs, max_context, max_rows, rms_eps)
+        cfg.device, cfg.max_seqs, cfg.max_context, cfg.max_rows, cfg.rms_eps, cfg.flags = (
+            device, max_seqs, max_context, max_rows, rms_eps, flags)
         handle = ctypes.c_void_p()
         check(lib().qwen_b200_open(ctypes.byref(cfg), ctypes.byref(handle)))
         self.h = handle
@@ -124,6 +125,16 @@ class Engine:
         check(lib().qwen_b200_read_kv(self.h, slot, layer, n, ptr(kc, i8), ptr(ks, ctypes.c_float), ptr(vc, i8),
                                       ptr(vs, ctypes.c_float)), self.h)
         return kc, ks, vc, vs
+
+    def read_kv_rtl(self, slot, layer, n):
+        """FLAG_RTL_KV handles: (klo [2][n][64], K block locks [2][blocks], V locks [2])."""
+        klo = np.empty((2, n, 64), dtype=np.int8)
+        klock = np.empty((2, (self.cfg.max_context + 255) // 256), dtype=np.uint8)
+        vlock = np.empty(2, dtype=np.uint8)
+        u8 = ctypes.c_uint8
+        check(lib().qwen_b200_read_kv_rtl(self.h, slot, layer, n, ptr(klo, ctypes.c_int8), ptr(klock, u8),
+                                          ptr(vlock, u8)), self.h)
+        return klo, klock, vlock
 
     def set_dump(self, layer, rows):
         """Arms the per-layer dump; returns the dict of host arrays it fills."""

@@ -66,8 +66,22 @@ typedef struct qwen_b200_config {
     uint32_t max_context; /* KV capacity per slot, tokens (reference firmware: 256) */
     uint32_t max_rows;    /* rows per forward chunk; longer prompts are chunked */
     float rms_eps;        /* RMSNorm epsilon, 1e-6 (model_backend.py:71) */
-    uint32_t flags;       /* reserved, 0 */
+    uint32_t flags;       /* 0, or QWEN_B200_FLAG_RTL_KV */
 } qwen_b200_config;
+
+/* The accelerator's own KV cache format instead of the engine's KV8 rule:
+ * K as 16-bit codes in two int8 planes with a 16-bit mantissa per (token,
+ * head) and an exponent locked per 256-token block (src/rtl/kv8_k_quant.sv,
+ * kv8_k_write_chain.sv), V as 8-bit codes with an 8-bit mantissa per (token,
+ * head) and an exponent locked per (layer, head) by a request's first token
+ * (kv8_v_quant.sv at margin 2, kv8_v_write_chain.sv), the same rules as
+ * qwen_b200_op_k16_append / qwen_b200_op_v8_append. Attention reads them
+ * with the engine's exact arithmetic (the K code of a dim is 256 * high +
+ * low, the scales m16 * 2^(lock - 142) and m8 * 2^(lock - 134)), so tokens and
+ * logits equal the oracle's in the same mode. For RTL numeric comparisons:
+ * every step takes the per-kernel path and the attention kernel for long
+ * rows, and qwen_b200_fill_kv_synthetic is not available. */
+#define QWEN_B200_FLAG_RTL_KV 1u
 
 /* ---- handle lifecycle ------------------------------------------------------ */
 /* Fills defaults: device 0, 1 slot, 256-token context, 256 rows, eps 1e-6. */
@@ -153,6 +167,11 @@ int qwen_b200_fill_kv_synthetic(qwen_b200 *h, uint32_t slot, uint32_t length, ui
 /* Copies one layer's KV8 cache of a slot to host: codes [2][n][64], scales [2][n]. */
 int qwen_b200_read_kv(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, int8_t *kcodes, float *kscales,
                       int8_t *vcodes, float *vscales);
+/* QWEN_B200_FLAG_RTL_KV handles: the low K planes klo [2][n][64], the K
+ * block locks klock [2][ceil(max_context / 256)] and the V layer locks
+ * vlock [2] of one layer and slot (nullable outputs). */
+int qwen_b200_read_kv_rtl(qwen_b200 *h, uint32_t slot, uint32_t layer, uint32_t n, int8_t *klo, uint8_t *klock,
+                          uint8_t *vlock);
 /* Records the bf16 tensors of one layer (q k v context h m y, rows x dims) at
  * the next forward into host buffers (the reference's RTL_DUMP_LAYERS names,
  * src/verification/rtl_bridge.cpp:109-171). layer < 0 disables. */

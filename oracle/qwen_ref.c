@@ -65,6 +65,11 @@ struct ref_model {
      * [slot][2][cap]; slot 0 is the sequence of the single-sequence calls,
      * whose position is `position`; spos[s] holds the others' */
     unsigned nslots, *spos;
+    /* REF_RTL_KV (allocated when the mode is set): the low K16 plane klo
+     * [slot][2][cap][64] beside kc (the high plane), the K block locks
+     * klock [slot][2][cap/256 rounded up] and the V layer locks vlock [slot][2] */
+    int8_t *klo[NL];
+    uint8_t *klock[NL], *vlock[NL];
     int dump_layer;
     float *dq, *dk, *dv, *dctx, *dh, *dm, *dy;
 };
@@ -262,6 +267,9 @@ void ref_close(ref_model *m) {
         free(m->vc[l]);
         free(m->ks[l]);
         free(m->vs[l]);
+        free(m->klo[l]);
+        free(m->klock[l]);
+        free(m->vlock[l]);
     }
     free(m->lm);
     free(m->lmt);
@@ -274,7 +282,24 @@ void ref_close(ref_model *m) {
     free(m);
 }
 
-void ref_set_mode(ref_model *m, unsigned mode) { m->mode = mode; }
+static unsigned rtl_blocks(const ref_model *m) { return (m->capacity + 255) / 256; }
+/* (Re)allocates the RTL-format arrays for the current slots, zeroed. */
+static int rtl_alloc(ref_model *m) {
+    for (int l = 0; l < NL; ++l) {
+        free(m->klo[l]);
+        free(m->klock[l]);
+        free(m->vlock[l]);
+        m->klo[l] = (int8_t *)calloc((size_t)m->nslots * m->capacity * KVH * HD, 1);
+        m->klock[l] = (uint8_t *)calloc((size_t)m->nslots * KVH * rtl_blocks(m), 1);
+        m->vlock[l] = (uint8_t *)calloc((size_t)m->nslots * KVH, 1);
+        if (!m->klo[l] || !m->klock[l] || !m->vlock[l]) return -1;
+    }
+    return 0;
+}
+void ref_set_mode(ref_model *m, unsigned mode) {
+    if ((mode & REF_RTL_KV) && !m->klo[0] && rtl_alloc(m)) mode &= ~REF_RTL_KV;
+    m->mode = mode;
+}
 void ref_clear(ref_model *m) { m->position = 0; } /* model_backend.py:57-60 */
 unsigned ref_position(const ref_model *m) { return m->position; }
 const int8_t *ref_weight(const ref_model *m, int layer, int proj) { return m->w[layer][proj]; }
@@ -623,8 +648,10 @@ static void attend(const float *q, unsigned visible, kv_at key, const void *kvie
  * exactly (int64), and
  *   S[t] = bf16(RN32(RN32(dot) * 2^(E-26) * kscale[t]) / 8).
  * Exact integer sums make the result independent of summation order. */
-void ref_kv8_scores(const float *q, unsigned visible, const int8_t *kcodes, const float *kscales, unsigned mode,
-                    float *scores) {
+/* With klo (REF_RTL_KV) the K code of dim d is the 16-bit 256 * kcodes[d] +
+ * klo[d] of the accelerator's two planes, the same formula otherwise. */
+static void kv_scores(const float *q, unsigned visible, const int8_t *kcodes, const int8_t *klo, const float *kscales,
+                      unsigned mode, float *scores) {
     float amax = 0.0f;
     for (unsigned d = 0; d < HD; ++d)
         if (fabsf(q[d]) > amax) amax = fabsf(q[d]);
@@ -633,10 +660,18 @@ void ref_kv8_scores(const float *q, unsigned visible, const int8_t *kcodes, cons
     for (unsigned d = 0; d < HD; ++d) qi[d] = (int32_t)rintf(ldexpf(q[d], 26 - e));
     for (unsigned t = 0; t < visible; ++t) {
         int64_t acc = 0;
-        for (unsigned d = 0; d < HD; ++d) acc += (int64_t)qi[d] * kcodes[(size_t)t * HD + d];
+        if (klo)
+            for (unsigned d = 0; d < HD; ++d)
+                acc += (int64_t)qi[d] * (256 * (int32_t)kcodes[(size_t)t * HD + d] + klo[(size_t)t * HD + d]);
+        else
+            for (unsigned d = 0; d < HD; ++d) acc += (int64_t)qi[d] * kcodes[(size_t)t * HD + d];
         const float dot = ldexpf((float)acc, e - 26);
         scores[t] = bfm(dot * kscales[t] / 8.0f, mode);
     }
+}
+void ref_kv8_scores(const float *q, unsigned visible, const int8_t *kcodes, const float *kscales, unsigned mode,
+                    float *scores) {
+    kv_scores(q, visible, kcodes, NULL, kscales, mode, scores);
 }
 
 /* KV8 view: codes [t][64], scales [t]; dequantised value = code * scale (fp32). */
@@ -785,6 +820,7 @@ int ref_set_slots(ref_model *m, unsigned nslots) {
     m->spos = sp;
     m->nslots = nslots;
     m->position = 0;
+    if (m->klo[0] && rtl_alloc(m)) return -1;
     return 0;
 }
 
@@ -803,7 +839,9 @@ static void attention_slots(const ref_model *m, int l, const float *q, unsigned 
         kv8_view vv = {vc, vs};
         float *scratch = (float *)malloc(visible * sizeof(float));
         float *out = ctx + (size_t)r * HID + (size_t)h * HD;
-        ref_kv8_scores(q + ((size_t)r * QH + h) * HD, visible, kc, ks, mode, scratch);
+        const int8_t *klo =
+            (mode & REF_RTL_KV) ? m->klo[l] + slot_codes(m, slot[r]) + (size_t)g * m->capacity * HD : NULL;
+        kv_scores(q + ((size_t)r * QH + h) * HD, visible, kc, klo, ks, mode, scratch);
         if (mode & REF_EXACT)
             attend_finish_kv8_exact(scratch, visible, vc, vs, mode, out);
         else
@@ -834,6 +872,52 @@ static void lm_head_rows(const ref_model *m, const float *x, unsigned n, unsigne
     free(h);
     free(acc);
     free(pre);
+}
+
+/* REF_RTL_KV append of one (token, KV head): the accelerator's K16 and V
+ * formats (ref_k16_quant, ref_v8_quant below) into the caches, the K code as
+ * its two planes kc (high) / klo (low) with the scale m16 * 2^(lock - 142),
+ * V as codes with the scale m8 * 2^(lock - 134). A 256-token block's first
+ * token sets its K lock, the token at position 0 the V lock; a later V token
+ * of a slot without a V lock is quantised as a first token and sets none. */
+static void rtl_append(ref_model *m, int l, unsigned slot, int g, unsigned t, const float *kr, const float *vr) {
+    uint16_t kb[HD], vb[HD];
+    for (int d = 0; d < HD; ++d) {
+        kb[d] = (uint16_t)(f2u(kr[d]) >> 16);
+        vb[d] = (uint16_t)(f2u(vr[d]) >> 16);
+    }
+    const size_t cs = slot_codes(m, slot) + ((size_t)g * m->capacity + t) * HD;
+    const size_t ss = slot_scales(m, slot) + (size_t)g * m->capacity + t;
+    uint8_t *klk = m->klock[l] + ((size_t)slot * KVH + g) * rtl_blocks(m) + t / 256;
+    uint16_t m16;
+    uint8_t etab, m8;
+    int clip;
+    ref_k16_quant(kb, t % 256 == 0, klk, m->kc[l] + cs, m->klo[l] + cs, &m16, &etab, &clip);
+    m->ks[l][ss] = ldexpf((float)m16, (int)*klk - 142);
+    uint8_t *vlk = m->vlock[l] + (size_t)slot * KVH + g;
+    uint8_t lock = *vlk;
+    uint16_t vsc;
+    const int first = t == 0 || lock == 0;
+    ref_v8_quant(vb, first, &lock, m->vc[l] + cs, &m8, &vsc, &clip);
+    if (t == 0) *vlk = lock;
+    m->vs[l][ss] = ldexpf((float)m8, (int)lock - 134);
+}
+
+/* The RTL-format K planes and locks of one layer's first n tokens of a slot:
+ * klo [2][n][64], klock [2][cap/256 rounded up], vlock [2]. */
+int ref_rtl_kv_state(const ref_model *m, int layer, unsigned slot, unsigned n, int8_t *klo, uint8_t *klock,
+                     uint8_t *vlock) {
+    if (!m->klo[0] || layer < 0 || layer >= NL || slot >= m->nslots || n > m->capacity) return -1;
+    for (int g = 0; g < KVH; ++g) {
+        if (klo)
+            memcpy(klo + (size_t)g * n * HD, m->klo[layer] + slot_codes(m, slot) + (size_t)g * m->capacity * HD,
+                   (size_t)n * HD);
+        if (klock)
+            memcpy(klock + (size_t)g * rtl_blocks(m), m->klock[layer] + ((size_t)slot * KVH + g) * rtl_blocks(m),
+                   rtl_blocks(m));
+        if (vlock) vlock[g] = m->vlock[layer][(size_t)slot * KVH + g];
+    }
+    return 0;
 }
 
 /* The forward of model_backend.py:80-115 over `rows` rows, row r being token
@@ -879,8 +963,12 @@ static void run_rows(ref_model *m, unsigned rows, const uint32_t *ids, const uin
                 }
                 const size_t cs = slot_codes(m, slot[r]) + ((size_t)g * m->capacity + t) * HD;
                 const size_t ss = slot_scales(m, slot[r]) + (size_t)g * m->capacity + t;
-                ref_kv8_quant(kr, 1, m->kc[l] + cs, m->ks[l] + ss);
-                ref_kv8_quant(vr, 1, m->vc[l] + cs, m->vs[l] + ss);
+                if (mode & REF_RTL_KV)
+                    rtl_append(m, l, slot[r], g, (unsigned)t, kr, vr);
+                else {
+                    ref_kv8_quant(kr, 1, m->kc[l] + cs, m->ks[l] + ss);
+                    ref_kv8_quant(vr, 1, m->vc[l] + cs, m->vs[l] + ss);
+                }
             }
         if (mode & REF_KV8) {
             attention_slots(m, l, q, rows, pos, slot, mode, ctx);

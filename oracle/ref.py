@@ -12,7 +12,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB = HERE / '_build' / 'libqwen_ref.so'
 
-KV8, RND8, FUSED_BIAS, CSR_EPS, ARGMAX_F32, EXACT = 1, 2, 4, 8, 16, 32
+KV8, RND8, FUSED_BIAS, CSR_EPS, ARGMAX_F32, EXACT, RTL_KV = 1, 2, 4, 8, 16, 32, 64
 VOCAB = 151936
 
 _P8 = POINTER(ctypes.c_int8)
@@ -48,6 +48,8 @@ def lib():
             'ref_lm_weight': (_P8, [c_void_p]),
             'ref_embedding': (POINTER(ctypes.c_uint16), [c_void_p]),
             'ref_kv8_state': (c_int, [c_void_p, c_int, _P8, _PF, _P8, _PF]),
+            'ref_rtl_kv_state': (c_int, [c_void_p, c_int, ctypes.c_uint, ctypes.c_uint, _P8, POINTER(ctypes.c_uint8),
+                                         POINTER(ctypes.c_uint8)]),
             'ref_bf': (c_float, [c_float, ctypes.c_uint]),
             'ref_qexp': (c_float, [c_float]),
             'ref_rmsnorm': (None, [_PF, ctypes.c_uint, _PF, c_float, ctypes.c_uint, _PF]),
@@ -202,6 +204,18 @@ class RefModel:
         vs = np.empty((2, n), dtype=np.float32)
         lib().ref_kv8_state(self.h, layer, p8(kc), pf(ks), p8(vc), pf(vs))
         return kc, ks, vc, vs
+
+    def rtl_kv_state(self, layer, slot, n):
+        """REF_RTL_KV: (klo [2][n][64], K block locks [2][blocks], V locks [2])."""
+        klo = np.empty((2, n, 64), dtype=np.int8)
+        nblk = (self.capacity + 255) // 256
+        klock = np.empty((2, nblk), dtype=np.uint8)
+        vlock = np.empty(2, dtype=np.uint8)
+        rc = lib().ref_rtl_kv_state(self.h, layer, slot, n, p8(klo),
+                                    klock.ctypes.data_as(POINTER(ctypes.c_uint8)),
+                                    vlock.ctypes.data_as(POINTER(ctypes.c_uint8)))
+        assert rc == 0
+        return klo, klock, vlock
 
     def weight(self, layer, proj, shape):
         p = lib().ref_weight(self.h, layer, proj)
