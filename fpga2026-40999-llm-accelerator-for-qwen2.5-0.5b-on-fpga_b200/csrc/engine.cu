@@ -94,10 +94,10 @@ struct qwen_b200 {
     // pinned staging
     uint32_t *h_meta = nullptr, *h_tokens = nullptr, *h_slot_pos = nullptr, *h_flag = nullptr;
     std::vector<uint32_t> pos;  // host mirror of every slot's position
-    // decode graphs keyed by (n, context chunks, tokens_in, tokens_out)
+    // decode graphs keyed by (n, context bucket, tokens_in, tokens_out)
     std::map<std::tuple<uint32_t, uint32_t, const void *, const void *>, cudaGraphExec_t> graphs;
     // host-buffer decode steps: the forward over the staged ids / slots /
-    // positions, keyed by (n, context chunks), with its launch count
+    // positions, keyed by (n, context bucket), with its launch count
     std::map<std::pair<uint32_t, uint32_t>, std::pair<cudaGraphExec_t, uint32_t>> host_graphs;
     // layer dump (tests): device buffers and host destinations
     int dump_layer = -1;
@@ -180,6 +180,10 @@ constexpr size_t DUMP_COLS = 896 + 256 + 896 + 896 + 4864 + 896;
 
 size_t kv_layer_codes(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * h->cfg.max_context * 64; }
 size_t kv_layer_scales(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * h->cfg.max_context; }
+// Context bucket of a captured decode step (the upper bound of its longest
+// row's keys that the graph was recorded for): 64 keys, within which a
+// single-row step takes the persistent kernel, then multiples of 128.
+uint32_t context_bucket(uint32_t max_len) { return max_len <= 64 ? 64u : (max_len + 127) / 128 * 128; }
 size_t rtl_klock_layer(const qwen_b200 *h) { return (size_t)h->cfg.max_seqs * 2 * ((h->cfg.max_context + 255) / 256); }
 
 int allocate(qwen_b200 *h) {
@@ -857,13 +861,13 @@ static int decode_step_impl(qwen_b200 *h, const uint32_t *slots, const uint32_t 
         h->h_meta[2 * n + i] = h->pos[slots[i]];
     }
     CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)3 * n * 4, cudaMemcpyHostToDevice, st));
-    // steps of one batch size and 128-key context bucket replay one graph of
-    // the forward (it reads the staged ids / slots / positions on the device);
+    // steps of one batch size and context bucket replay one graph of the
+    // forward (it reads the staged ids / slots / positions on the device);
     // the first such step runs the launches directly and captures them (a
     // profiled step always runs them directly, between its events)
-    const uint32_t chunks = (max_len + 127) / 128;
-    const int bucket_len = (int)std::min<uint32_t>(chunks * 128, h->cfg.max_context);
-    const auto key = std::make_pair(n, chunks);
+    const uint32_t bound = context_bucket(max_len);
+    const int bucket_len = (int)std::min<uint32_t>(bound, h->cfg.max_context);
+    const auto key = std::make_pair(n, bound);
     auto it = (h->prof || logits) ? h->host_graphs.end() : h->host_graphs.find(key);
     if (logits && !h->blogits) {
         // every row's logits: allocated at the first such step
@@ -1035,10 +1039,10 @@ int qwen_b200_decode_step_device(qwen_b200 *h, const uint32_t *d_tokens_in, uint
         if (h->pos[i] >= h->cfg.max_context) return fail(h, QWEN_B200_ESTATE, "slot %u is full", i);
         max_len = std::max(max_len, h->pos[i] + 1);
     }
-    const uint32_t chunks = (max_len + 127) / 128;
-    const int bucket_len = (int)std::min<uint32_t>(chunks * 128, h->cfg.max_context);
+    const uint32_t bound = context_bucket(max_len);
+    const int bucket_len = (int)std::min<uint32_t>(bound, h->cfg.max_context);
     cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
-    const auto key = std::make_tuple(n, chunks, (const void *)d_tokens_in, (const void *)d_tokens_out);
+    const auto key = std::make_tuple(n, bound, (const void *)d_tokens_in, (const void *)d_tokens_out);
     auto it = h->graphs.find(key);
     if (it != h->graphs.end()) {
         CK(cudaGraphLaunch(it->second, st));

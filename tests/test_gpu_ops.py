@@ -91,7 +91,7 @@ def test_gemm_w8a16(k, n, rows, epi):
     assert np.array_equal(got, exp), f'gemm {k}x{n} rows {rows} {epi}: {np.mean(got == exp):.5f} bit-equal'
 
 
-@pytest.mark.parametrize('rows', [1, 5, 16])
+@pytest.mark.parametrize('rows', [1, 5, 8, 16])
 def test_swiglu(rows):
     keep = Keep()
     r = rng(100 + rows)
@@ -259,10 +259,11 @@ def test_attention_cluster_unaligned_capacity(cap):
     check_attention(got, q, slots, positions, cache, True, f'attention cap={cap}')
 
 
-def test_qkv_fused_against_oracle_chain():
+@pytest.mark.parametrize('rows', [3, 8, 9])
+def test_qkv_fused_against_oracle_chain(rows):
     keep = Keep()
-    r = rng(21)
-    rows, cap = 9, 64
+    r = rng(21 + rows)
+    cap = 64
     x = rand_bf16(r, (rows, 896), 2.0)
     g = bf16_round(r.uniform(0.5, 1.5, 896).astype(np.float32))
     w, s = rand_weights(r, 1152, 896)
@@ -296,7 +297,7 @@ def lm_oracle(x, g, w, s):
     return logits, toks
 
 
-@pytest.mark.parametrize('rows', [1, 5])
+@pytest.mark.parametrize('rows', [1, 5, 8, 12])
 def test_lm_head_argmax_with_planted_ties(rows):
     keep = Keep()
     r = rng(30 + rows)
