@@ -158,17 +158,12 @@ static int run_gemv(const uint16_t *x, int rows, const uint16_t *gamma, float ep
                       bias, n, y);
 }
 
-// Row tiles: 1, 2, 4 or 8 activation rows per CTA, so that up to 8 rows
-// stream the weights once; the 8-row tile halves the weight rows per warp
-// (RW) to keep the accumulators in registers.
 template <int K, int RW, int EPI>
 static int dispatch_mt(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
                        const float *scale, const uint16_t *bias, int n, uint16_t *y, cudaStream_t st) {
     if (rows <= 1) return run_gemv<K, RW, 8, 1, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
     if (rows <= 2) return run_gemv<K, RW, 8, 2, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
-    if (rows <= 4) return run_gemv<K, RW, 8, 4, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);
-    constexpr int RW8 = RW / 2 > 0 ? RW / 2 : 1;
-    return run_gemv<K, RW8, 8, 8, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);  // 8-row tiles
+    return run_gemv<K, RW, 8, 4, EPI>(x, rows, gamma, eps, w, scale, bias, n, y, st);  // 4-row tiles
 }
 
 int launch_gemv(int epi, const uint16_t *x, int rows, int k, const uint16_t *gamma, float eps, const int8_t *w,
@@ -212,22 +207,20 @@ __global__ void __launch_bounds__(256) qkv_kernel(QkvArgs a) {
     const int mrows = min(MT, a.rows - m0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hb = blockIdx.x;
-    // a warp's 8 weight rows in parts of RP rows (2 for 8-row tiles: registers)
-    constexpr int RP = MT >= 8 ? 2 : 4, NP = 8 / RP;
-    GemvRows<K, RP> g[NP];
+    GemvRows<K, 4> g[2];
 #pragma unroll
-    for (int part = 0; part < NP; ++part) gemv_load<K, RP>(a.w, hb * 64 + warp * 8 + part * RP, true, g[part]);
+    for (int half = 0; half < 2; ++half) gemv_load<K, 4>(a.w, hb * 64 + warp * 8 + half * 4, true, g[half]);
     pdl_wait();
     pdl_trigger();
     load_x_limbs<K, MT, 256>(a.x, m0, mrows, a.gamma, a.eps, xl, ex);
 #pragma unroll
-    for (int part = 0; part < NP; ++part) {
-        const int local = warp * 8 + part * RP;
+    for (int half = 0; half < 2; ++half) {
+        const int local = warp * 8 + half * 4;
         const int n0 = hb * 64 + local;
-        float acc[RP][MT];
-        gemv_dot<K, RP, MT>(g[part], xl, ex, acc);
+        float acc[4][MT];
+        gemv_dot<K, 4, MT>(g[half], xl, ex, acc);
 #pragma unroll
-        for (int r = 0; r < RP; ++r)
+        for (int r = 0; r < 4; ++r)
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 if (((r * MT + m) & 31) != lane || m >= mrows) continue;
@@ -255,24 +248,20 @@ int launch_qkv(const QkvArgs &a, cudaStream_t st) {
     if (a.rows <= 0) return -1;
     if (a.rows <= 1) return run_qkv<1>(a, st);
     if (a.rows <= 2) return run_qkv<2>(a, st);
-    if (a.rows <= 4) return run_qkv<4>(a, st);
-    return run_qkv<8>(a, st);  // 8-row tiles
+    return run_qkv<4>(a, st);  // 4-row tiles
 }
 
 // ------------------------------------------------------------- LM head + argmax
 // logits = bf16(bf16(acc) * scale) (model_backend.py:109); each CTA reduces
 // its 32 rows to a (value, index) candidate per tile row; argmax_reduce picks
 // the best per row with the highest index on ties (model_backend.py:113-114).
-// A CTA covers 32 vocabulary rows: 8 warps x 4 rows for tiles of up to 4
-// activation rows, 16 warps x 2 rows for 8-row tiles (registers).
 template <int MT>
-__global__ void __launch_bounds__(MT >= 8 ? 512 : 256) lm_head_kernel(const uint16_t *__restrict__ x, int rows,
+__global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict__ x, int rows,
                                                       const uint16_t *__restrict__ gamma, float eps,
                                                       const int8_t *__restrict__ w, const float *__restrict__ scale,
                                                       int vocab, uint16_t *logits, float *pv, uint32_t *pi,
                                                       int nblk, int n_base) {
-    constexpr int K = QB_HID, RW = MT >= 8 ? 2 : 4, NW = MT >= 8 ? 16 : 8;
-    static_assert(RW * NW == 32, "32 vocabulary rows per CTA");
+    constexpr int K = QB_HID, RW = 4, NW = 8;
     extern __shared__ __align__(16) uint8_t gsm[];
     int8_t *xl = reinterpret_cast<int8_t *>(gsm);
     int *ex = reinterpret_cast<int *>(gsm + MT * 4 * K);
@@ -379,8 +368,8 @@ static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps,
                   int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, int n_base, cudaStream_t st) {
     const size_t smem = (size_t)MT * (4 * QB_HID + 4);
     dim3 grid(nblk, (rows + MT - 1) / MT);
-    return launch_pdl(lm_head_kernel<MT>, grid, dim3(MT >= 8 ? 512 : 256), smem, st, 1, x, rows, gamma, eps, w, scale,
-                      vocab, logits, pv, pi, nblk, n_base);
+    return launch_pdl(lm_head_kernel<MT>, grid, dim3(256), smem, st, 1, x, rows, gamma, eps, w, scale, vocab, logits,
+                      pv, pi, nblk, n_base);
 }
 
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
@@ -396,10 +385,8 @@ int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps
         rc = run_lm<1>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);
     else if (rows <= 2)
         rc = run_lm<2>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);
-    else if (rows <= 4)
-        rc = run_lm<4>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);
     else
-        rc = run_lm<8>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);  // 8-row tiles
+        rc = run_lm<4>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);  // 4-row tiles
     if (rc) return rc;
     return launch_pdl(argmax_reduce_kernel, dim3(rows), dim3(256), 0, st, 1, pv, pi, nblk, tokens, values);
 }

@@ -1,8 +1,9 @@
-// The accelerator's own KV cache format (its "K16" K path; the V path is at
-// the end), as a second cache format beside the engine's per-token-per-head
-// int8 rule: the K
-// quantiser of src/rtl/kv8_k_quant.sv with the K chain's parameters (MARGIN 8,
-// MTOP 65535, RSHIFT 24, CODE_EXTRA 8) and the block-exponent lock of
+// The accelerator's own KV cache format (its "K16" K path; the V path and the
+// engine's RTL KV mode follow), as a second cache format beside the engine's
+// per-token-per-head int8 rule: the K quantiser of src/rtl/kv8_k_quant.sv with
+// the K chain's parameters (MARGIN 8 as src/rtl/storage/
+// qwen25_qkv_controller.v:1908 instantiates it, MTOP 65535, RSHIFT 24,
+// CODE_EXTRA 8) and the block-exponent lock of
 // src/rtl/kv8_k_write_chain.sv:503-600 (the first token of each 256-token
 // block fixes the exponent of that (head, block); later tokens of the block
 // are quantised against it):
