@@ -42,9 +42,9 @@ HID, FFN, QKV, VOCAB, LAYERS = 896, 4864, 1152, 151936, 24
 KV_BYTES_PER_TOKEN_LAYER = 2 * 2 * (64 + 4)  # K and V, 2 heads, 64 codes + fp32 scale
 CLASSES = ['embedding', 'qkv_rope_kv8', 'attention', 'o_proj_residual', 'gate_up_swiglu', 'down_residual',
            'lm_head_argmax', 'bookkeeping', 'persistent_decode']
-# kernels behind each class: rows <= 8 run the GEMV family, more rows the
+# kernels behind each class: one row runs the GEMV family, more rows the
 # tcgen05 GEMM (qkv/o/gate_up/down/LM head); attention is one launch of the
-# register-layout kernel (rows of up to 8 x 2304 keys, every workload here)
+# register-layout kernel (every workload here)
 KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_rs_kernel',
                      'o_proj_residual': 'gemv_kernel<896,EPI_RESIDUAL>',
                      'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
@@ -61,7 +61,7 @@ KERNEL_NAMES_TC = dict(KERNEL_NAMES_GEMV,
 
 
 def kernel_names(rows):
-    return KERNEL_NAMES_TC if rows > 8 else KERNEL_NAMES_GEMV
+    return KERNEL_NAMES_TC if rows > 1 else KERNEL_NAMES_GEMV
 
 
 def weight_bytes():
@@ -682,6 +682,16 @@ def micro_gemm(torch, L, stream, sp, timed, hbm):
     return out
 
 
+def attention_kernel_name(rows, keys, max_splits=16):
+    """The kernel the engine's attention launch picks (the split plan of
+    attention_rs.cu; 16-way clusters where the GPU places them)."""
+    chunks = -(-keys // 192)
+    s = max(min(148 // (2 * rows), max_splits, chunks), 1, -(-chunks // 12))
+    if s > max_splits or (s > 8 and rows * 2 * s > 4 * 148):
+        return 'attn_cluster_kernel'
+    return 'attn_rs_kernel'
+
+
 def micro_attention(torch, L, stream, sp, timed, hbm):
     """KV8 GQA decode attention (qwen_b200_op_attention_cluster, the engine's
     form): B rows, each in its own slot at context L (keys 0..L-1); K and V
@@ -717,7 +727,7 @@ def micro_attention(torch, L, stream, sp, timed, hbm):
                                                           C, ctx.data_ptr(), sp)
             us = timed(fn)
             nbytes = B * C * KV_BYTES_PER_TOKEN_LAYER + B * HID * 2 * 2
-            out.append({'context': C, 'batch': B, 'kernel': 'attn_rs_kernel' if C <= 8 * 2304 else 'attn_cluster_kernel',
+            out.append({'context': C, 'batch': B, 'kernel': attention_kernel_name(B, C),
                         'us': round(us, 2), 'bytes': nbytes, 'gbs': round(nbytes / us / 1e3, 1),
                         'hbm_frac': round(nbytes / us / 1e3 / hbm, 4)})
             del kc, vc, ks, vs, q, ctx, slots, pos

@@ -64,7 +64,7 @@ struct ArCfg {
     static_assert(RED_BYTES % 8 == 0, "aligned sub-areas");
 };
 constexpr int AR_NW = 12;
-constexpr int AR_MAX_SPLITS = 8;
+constexpr int AR_MAX_SPLITS = 16;  // 9-16: non-portable clusters, when the GPU can place one
 constexpr int AR_SMS = 148;
 
 struct ArArgs {
@@ -576,19 +576,23 @@ __global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
 }
 
 // Split plan: as many CTAs per row as fill the GPU once at one CTA per SM
-// (contexts split up to 8 ways), at least enough to keep each within the key
-// limit. -1 when a row needs more than 8 CTAs.
+// (contexts split up to max_splits ways), at least enough to keep each within
+// the key limit. -1 when a row needs more than max_splits CTAs.
 template <int NW>
-int attention_rs_plan(int rows, int max_len, int *splits, int *kpc) {
+int attention_rs_plan(int rows, int max_len, int *splits, int *kpc, int max_splits = 8) {
     using C = ArCfg<NW>;
     if (max_len <= 0 || rows <= 0) return -1;
     const int chunks = (max_len + C::CHUNK - 1) / C::CHUNK;
     int s = AR_SMS / (2 * rows);
-    s = s < 1 ? 1 : (s > AR_MAX_SPLITS ? AR_MAX_SPLITS : s);
+    s = s < 1 ? 1 : (s > max_splits ? max_splits : s);
     s = s > chunks ? chunks : s;
     const int need = (chunks + C::NB - 1) / C::NB;
     s = s < need ? need : s;
-    if (s > AR_MAX_SPLITS) return -1;
+    if (s > max_splits) return -1;
+    // beyond 8 splits only while the CTAs fill at most four waves: larger
+    // batches of such rows run faster on the two-CTAs-per-SM kernel (64 rows
+    // x 32768 keys: 469 against 434 us; 16 rows: 129 against 148 us)
+    if (s > 8 && rows * QB_KVH * s > 4 * AR_SMS) return -1;
     const int cpc = (chunks + s - 1) / s;  // chunks per CTA
     *kpc = cpc * C::CHUNK;
     *splits = (chunks + cpc - 1) / cpc;
@@ -596,7 +600,7 @@ int attention_rs_plan(int rows, int max_len, int *splits, int *kpc) {
 }
 
 template <int NW, bool CLUSTER>
-static int run_ar(const ArArgs &a, int rows, int splits, cudaStream_t st) {
+static int configure_ar() {
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -604,8 +608,48 @@ static int run_ar(const ArArgs &a, int rows, int splits, cudaStream_t st) {
         if (cudaFuncSetAttribute(attn_rs_kernel<NW, CLUSTER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  ar_smem<NW>(ArCfg<NW>::MAX_KPC).total) != cudaSuccess)
             return -3;
+        if (CLUSTER &&
+            cudaFuncSetAttribute(attn_rs_kernel<NW, CLUSTER>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                cudaSuccess)
+            return -3;
         configured |= 1u << (dev & 31);
     }
+    return 0;
+}
+
+// Largest split this device can place as one cluster of full-size CTAs (one
+// per SM): 16 when a 16-CTA cluster fits in a GPC, else the portable 8;
+// decided once per device.
+template <int NW>
+static int ar_max_splits() {
+    static int cached[32] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int &m = cached[dev & 31];
+    if (m) return m;
+    m = 8;
+    if (configure_ar<NW, true>()) return m;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(AR_MAX_SPLITS, QB_KVH, 1);
+    cfg.blockDim = dim3(32 * NW);
+    cfg.dynamicSmemBytes = (size_t)ar_smem<NW>(ArCfg<NW>::MAX_KPC).total;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = AR_MAX_SPLITS;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, attn_rs_kernel<NW, true>, &cfg) == cudaSuccess && clusters >= 2)
+        m = AR_MAX_SPLITS;
+    cudaGetLastError();
+    return m;
+}
+
+template <int NW, bool CLUSTER>
+static int run_ar(const ArArgs &a, int rows, int splits, cudaStream_t st) {
+    if (configure_ar<NW, CLUSTER>()) return -3;
     return launch_pdl(attn_rs_kernel<NW, CLUSTER>, dim3(splits, QB_KVH, rows), dim3(32 * NW),
                       (size_t)ar_smem<NW>(a.kpc).total, st, CLUSTER ? (unsigned)splits : 1u, a);
 }
@@ -614,7 +658,7 @@ int launch_attention_rs(const uint16_t *q, int rows, const uint32_t *slots, cons
                         const int8_t *kc, const float *ks, const int8_t *vc, const float *vs, int cap, uint16_t *ctx,
                         unsigned *err, cudaStream_t st) {
     int splits, kpc;
-    if (attention_rs_plan<AR_NW>(rows, max_len, &splits, &kpc)) return 1;
+    if (attention_rs_plan<AR_NW>(rows, max_len, &splits, &kpc, ar_max_splits<AR_NW>())) return 1;
     ArArgs a;
     a.q = q;
     a.slots = slots;

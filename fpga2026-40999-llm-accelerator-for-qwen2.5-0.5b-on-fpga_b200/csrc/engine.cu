@@ -37,13 +37,13 @@ struct LayerW {
 };
 
 // Rows at or above which a step uses the tcgen05 GEMMs instead of the GEMVs.
-// The GEMV family streams the weights once per 4-row tile, so from 5 rows the
-// two widest projections, gate/up and the LM head, are cheaper on the
-// tensor cores (measured, L2 flushed, 8 rows: gate/up 32.8 us as GEMVs
-// against 20.5 us as a tcgen05 GEMM at 64 rows, the LM head 300 against 90 us);
-// q|k|v, O and down stay GEMVs up to 8 rows (fused RMSNorm / RoPE / KV8).
-constexpr int TC_MIN_ROWS = 9;
-constexpr int TC_MIN_ROWS_WIDE = 5;
+// The GEMV family's integer work grows with every row (four limb planes per
+// row and weight word) and it streams the weights once per 4-row tile, while
+// the tensor-core step costs the same from 1 to 64 rows: batched decode steps
+// at 500-key contexts measured 1.26 / 2.18 / 2.76 ms with GEMVs at 2 / 4 / 8
+// rows against 1.18 ms at 16 rows on the tensor cores (0.86 ms for one row
+// with GEMVs). Single rows keep the GEMVs (and the persistent kernel).
+constexpr int TC_MIN_ROWS = 2;
 
 enum CsrState { CSR_IDLE = 0, CSR_BUSY = 1, CSR_DONE = 2, CSR_ERROR = 3 };
 
@@ -391,7 +391,7 @@ int lm_head_rows(qwen_b200 *h, const uint16_t *xin, int nlog, int begin, int end
                  uint32_t *tokens_dst, float *values_dst, cudaStream_t st) {
     const float eps = h->cfg.rms_eps;
     const int width = end - begin;
-    if (nlog >= TC_MIN_ROWS_WIDE) {
+    if (nlog >= TC_MIN_ROWS) {
         LaunchScope ls(h, 6, st, 3);
         int rc = norm_limbs(h, xin, h->g_final, nlog, eps, st);
         if (rc) return rc;
@@ -527,7 +527,7 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
             CK(cudaMemcpyAsync(dq + (size_t)n * 2048, h->x, (size_t)n * 896 * 2, cudaMemcpyDeviceToDevice, st));
             pdl_break();
         }
-        if (n >= TC_MIN_ROWS_WIDE) {
+        if (n >= TC_MIN_ROWS) {
             LaunchScope ls(h, 4, st, 2);
             int rc = norm_limbs(h, h->x, W.g_ffn, n, eps, st);
             if (!rc) rc = tc_gemm(h, EPI_SWIGLU, n, HID, W.mgu, W.s_gu, nullptr, 2 * FFN, h->mid, nullptr, st);
