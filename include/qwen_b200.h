@@ -263,7 +263,8 @@ int qwen_b200_op_gemm_w8a16(const uint16_t *x, uint32_t rows, uint32_t k, const 
  * (model_backend.py:103,107). */
 int qwen_b200_op_gemm_w8a16_residual(const uint16_t *x, uint32_t rows, uint32_t k, const int8_t *w,
                                      const float *scale, uint32_t n, uint16_t *y, void *stream);
-/* Tensor-core (tcgen05 kind::i8) form of the same projection for rows > 8,
+/* Tensor-core (tcgen05 kind::i8) form of the same projection (the engine's
+ * form for 2 rows and more; rows >= 1 accepted),
  * with the GEMV's exact integer sums: every activation row is aligned to the
  * exponent of its largest |x| as a 28-bit integer held in four int8 limb
  * planes, each limb plane is multiplied with the row-major int8 weight
@@ -363,12 +364,13 @@ int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint3
                                    const float *kscales, const int8_t *vcodes, const float *vscales,
                                    uint32_t capacity, uint16_t *ctx, void *stream);
 /* The same attention in one launch with no workspace (the form the engine
- * uses): one CTA, or a thread-block cluster of up to 8 splitting the context,
- * per (row, KV head); both products run on the tensor cores and the clusters
- * exchange the softmax statistics and partial contexts over distributed
- * shared memory; results are independent of scheduling. Rows of up to
- * 8 x 2304 keys keep each lane's scores in its own shared-memory words (a
- * 12-warp CTA), longer rows a 4-warp CTA with a shared score array.
+ * uses): one CTA, or a thread-block cluster of up to 16 splitting the
+ * context, per (row, KV head); both products run on the tensor cores and the
+ * clusters exchange the softmax statistics and partial contexts over
+ * distributed shared memory; results are independent of scheduling. Rows of
+ * up to 8 x 2304 keys (16 x 2304 for small batches, where the GPU places a
+ * 16-CTA cluster) keep each lane's scores in its own shared-memory words (a
+ * 12-warp CTA), others a 4-warp CTA with a shared score array.
  * max_len <= 32768 (the model's context limit); q, kcodes, vcodes 16-byte
  * aligned, ctx 8-byte aligned (QWEN_B200_EINVAL otherwise). */
 int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,

@@ -43,7 +43,7 @@ def expected(x, w, s, b, y0, epi):
 
 @pytest.mark.parametrize('k,n,epi', [(896, 896, 'plain'), (896, 1152, 'bias'), (896, 896, 'residual'),
                                      (4864, 896, 'residual'), (896, 9728, 'swiglu')])
-@pytest.mark.parametrize('rows', [9, 16, 64, 100, 200])
+@pytest.mark.parametrize('rows', [1, 2, 5, 9, 16, 64, 100, 200])
 def test_gemm_tc(k, n, epi, rows):
     r = np.random.default_rng(k + n + rows)
     x = bf16_round(r.standard_normal((rows, k)).astype(np.float32))
