@@ -1,4 +1,4 @@
-"""tcgen05 kind::i8 W8A16 projection (the batched-decode path for rows > 8)
+"""tcgen05 kind::i8 W8A16 projection (the batched-decode path from 2 rows)
 against the oracle's exact projection order (REF_EXACT) on identical seeded
 inputs, through the C ABI. The sums are exact integers and SiLU uses the
 fixed-operation exp of both sides, so every epilogue's output is
