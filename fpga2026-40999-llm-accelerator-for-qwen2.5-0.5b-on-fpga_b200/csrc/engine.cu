@@ -72,6 +72,14 @@ struct qwen_b200 {
     int8_t *klo = nullptr;
     uint8_t *klock = nullptr, *vlock = nullptr;
     uint16_t *rtl_kv = nullptr;
+    // query-tiled prefill attention: the K caches of all layers as one tensor
+    // map, and the tile plan of the forward being enqueued (host staging,
+    // device copy, launch groups)
+    CUtensorMap kmap;
+    bool kmap_ok = false;
+    AtTile *d_tiles = nullptr, *h_tiles = nullptr;
+    std::vector<AtGroup> tgroups;
+    bool tplan = false;
     // activations
     uint16_t *x = nullptr, *q = nullptr, *ctx = nullptr, *mid = nullptr, *xl = nullptr, *logits = nullptr;
     uint16_t *blogits = nullptr;  // [R][vocab] logits of batched steps that return them
@@ -251,6 +259,9 @@ int allocate(qwen_b200 *h) {
     CK(cudaMemset(h->vc, 0, kv_layer_codes(h) * NL));
     CK(cudaMemset(h->ks, 0, kv_layer_scales(h) * NL * 4));
     CK(cudaMemset(h->vs, 0, kv_layer_scales(h) * NL * 4));
+    h->kmap_ok = make_kcache_map(&h->kmap, h->kc, (long long)(kv_layer_codes(h) / 64) * NL) == 0;
+    if ((rc = dalloc(h, (void **)&h->d_tiles, R * sizeof(AtTile)))) return rc;
+    CK(cudaMallocHost((void **)&h->h_tiles, R * sizeof(AtTile)));
     if (h->rtl) {
         if ((rc = dalloc(h, (void **)&h->klo, kv_layer_codes(h) * NL))) return rc;
         if ((rc = dalloc(h, (void **)&h->klock, rtl_klock_layer(h) * NL))) return rc;
@@ -413,6 +424,25 @@ int lm_head_rows(qwen_b200 *h, const uint16_t *xin, int nlog, int begin, int end
     return 0;
 }
 
+// Rows per forward chunk from which prompt rows take the query-tiled
+// attention (shorter chunks keep the per-row kernels).
+constexpr int TILE_MIN_ROWS = 16;
+
+// Plans the query tiles of a forward chunk of m rows (host slots and
+// positions) and enqueues the copy of the tile list; the next run_forward
+// uses them. Needs the rows' pinned staging to stay untouched until the
+// chunk's staging event.
+int prepare_tiles(qwen_b200 *h, int m, const uint32_t *slots, const uint32_t *positions, cudaStream_t st) {
+    h->tplan = false;
+    if (m < TILE_MIN_ROWS || h->rtl || !h->kmap_ok) return 0;
+    if (attention_tile_plan(m, slots, positions, h->h_tiles, h->tgroups)) return 0;
+    int ntiles = 0;
+    for (const AtGroup &g : h->tgroups) ntiles += g.count;
+    CK(cudaMemcpyAsync(h->d_tiles, h->h_tiles, (size_t)ntiles * sizeof(AtTile), cudaMemcpyHostToDevice, st));
+    h->tplan = true;
+    return 0;
+}
+
 // One forward over R rows whose ids/slots/positions are at meta[0..3R) with
 // stride n (ids n | slots n | positions n | logit rows n). nlog rows get the
 // LM head: rows listed at meta+3n, or all rows when identity. Without
@@ -503,7 +533,14 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
                                     h->klock + rtl_klock_layer(h) * l, vc, vs,
                                     h->vlock + (size_t)h->cfg.max_seqs * 2 * l, cap, st));
         }
-        {
+        if (h->tplan) {
+            // prefill rows: query tiles on the tensor cores, one launch per split group
+            LaunchScope ls(h, 2, st, (uint32_t)h->tgroups.size());
+            const long long krow0 = (long long)(kv_layer_codes(h) / 64) * l;
+            for (const AtGroup &grp : h->tgroups)
+                RK(launch_attention_tiles(h->kmap, krow0, h->d_tiles, grp, h->q, vc, ks, vs, cap, h->ctx,
+                                          reinterpret_cast<unsigned *>(h->tc_ws), st));
+        } else {
             LaunchScope ls(h, 2, st, 1);
             RK(launch_attention_cluster(h->q, n, slots, positions, max_len, kc, ks, vc, vs, cap, h->ctx,
                                         reinterpret_cast<unsigned *>(h->tc_ws), st, klo));
@@ -675,6 +712,7 @@ int qwen_b200_close(qwen_b200 *h) {
         cudaFreeHost(h->h_tokens);
         cudaFreeHost(h->h_slot_pos);
         cudaFreeHost(h->h_flag);
+        cudaFreeHost(h->h_tiles);
         if (h->csr_event) cudaEventDestroy(h->csr_event);
         if (h->staged) cudaEventDestroy(h->staged);
         if (h->stream) cudaStreamDestroy(h->stream);
@@ -821,9 +859,11 @@ int qwen_b200_forward(qwen_b200 *h, uint32_t slot, const uint32_t *ids, uint32_t
         }
         h->h_meta[3 * n] = (uint32_t)(n - 1);
         CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * n + 1) * 4, cudaMemcpyHostToDevice, st));
+        if ((rc = prepare_tiles(h, n, h->h_meta + n, h->h_meta + 2 * n, st))) return rc;
         CK(cudaEventRecord(h->staged, st));
         rc = run_forward(h, n, (int)(position + c0 + (uint32_t)n), last ? 1 : 0, n == 1,
                          last && logits ? h->logits : nullptr, h->tokens, st);
+        h->tplan = false;
         if (rc) return rc;
         if (h->dump_layer >= 0 && h->d_dump) {
             CK(cudaStreamSynchronize(st));
@@ -974,10 +1014,12 @@ int qwen_b200_prefill(qwen_b200 *h, uint32_t n, const uint32_t *slots, const uin
             if (t + 1 == total || rseq[t + 1] != rseq[t]) h->h_meta[3 * m + nl++] = (uint32_t)r;  // a last row
         }
         CK(cudaMemcpyAsync(h->meta, h->h_meta, (size_t)(3 * m + nl) * 4, cudaMemcpyHostToDevice, st));
+        if ((rc = prepare_tiles(h, m, h->h_meta + m, h->h_meta + 2 * m, st))) return rc;
         CK(cudaEventRecord(h->staged, st));
         h->nlaunch = 0;
-        if ((rc = run_forward(h, m, max_len, nl, false, nullptr, h->tokens + done, st, tokens_out != nullptr)))
-            return rc;
+        rc = run_forward(h, m, max_len, nl, false, nullptr, h->tokens + done, st, tokens_out != nullptr);
+        h->tplan = false;
+        if (rc) return rc;
         if (hidden_out && nl)
             CK(cudaMemcpyAsync(hidden_out + (size_t)done * HID, h->xl, (size_t)nl * HID * 2, cudaMemcpyDeviceToHost,
                                st));
@@ -1339,6 +1381,38 @@ int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint3
     if (!q || !slots || !positions || !kcodes || !kscales || !vcodes || !vscales || !ctx) return QWEN_B200_EINVAL;
     return launch_attention_cluster(q, (int)rows, slots, positions, (int)max_len, kcodes, kscales, vcodes, vscales,
                                     (int)capacity, ctx, nullptr, (cudaStream_t)stream);
+}
+
+size_t qwen_b200_attention_prefill_workspace(uint32_t rows) { return 256 + (size_t)rows * sizeof(AtTile); }
+
+int qwen_b200_op_attention_prefill(const uint16_t *q, uint32_t rows, uint32_t pos0, const int8_t *kcodes,
+                                   const float *kscales, const int8_t *vcodes, const float *vscales, uint32_t capacity,
+                                   uint16_t *ctx, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!q || !kcodes || !kscales || !vcodes || !vscales || !ctx || !workspace || !rows || !capacity)
+        return QWEN_B200_EINVAL;
+    if ((uint64_t)pos0 + rows > capacity || workspace_bytes < qwen_b200_attention_prefill_workspace(rows))
+        return QWEN_B200_EINVAL;
+    std::vector<uint32_t> slots(rows, 0u), pos(rows);
+    for (uint32_t r = 0; r < rows; ++r) pos[r] = pos0 + r;
+    std::vector<AtTile> tiles(rows);
+    std::vector<AtGroup> groups;
+    if (attention_tile_plan((int)rows, slots.data(), pos.data(), tiles.data(), groups)) return QWEN_B200_EINVAL;
+    CUtensorMap kmap;
+    if (make_kcache_map(&kmap, kcodes, 2ll * capacity)) return QWEN_B200_EINVAL;
+    cudaStream_t st = (cudaStream_t)stream;
+    AtTile *d_tiles = reinterpret_cast<AtTile *>(reinterpret_cast<char *>(workspace) + 256);
+    int ntiles = 0;
+    for (const AtGroup &g : groups) ntiles += g.count;
+    if (cudaMemcpyAsync(d_tiles, tiles.data(), (size_t)ntiles * sizeof(AtTile), cudaMemcpyHostToDevice, st) !=
+        cudaSuccess)
+        return QWEN_B200_EDEVICE;
+    for (const AtGroup &g : groups) {
+        const int rc = launch_attention_tiles(kmap, 0, d_tiles, g, q, vcodes, kscales, vscales, (int)capacity, ctx,
+                                              reinterpret_cast<unsigned *>(workspace), st);
+        if (rc) return rc == -1 ? QWEN_B200_EINVAL : QWEN_B200_EDEVICE;
+    }
+    // the host tile list must outlive the copy out of it
+    return cudaStreamSynchronize(st) == cudaSuccess ? QWEN_B200_OK : QWEN_B200_EDEVICE;
 }
 
 int qwen_b200_op_swiglu(const uint16_t *x, uint32_t rows, const uint16_t *gamma, float eps, const int8_t *w_gu,

@@ -717,6 +717,23 @@ int make_weight_map(CUtensorMap *map, const int8_t *w, int n, int k) {
     return r == CUDA_SUCCESS ? 0 : -3;
 }
 
+// K-cache map: rows of 64 int8 codes (one key of one KV head), box 128 rows,
+// 64-byte swizzle (the score operand of attention_tile.cu); rows past the end
+// read as zero.
+int make_kcache_map(CUtensorMap *map, const int8_t *kc, long long rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return -3;
+    if ((reinterpret_cast<uintptr_t>(kc) & 15) || rows <= 0) return -1;
+    cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {64};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(kc), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -3;
+}
+
 // Limb map: limbs[l][row][k] int8 (plane bytes apart, rows ld bytes apart,
 // rows_alloc rows), box [4][64 rows][128 k], 128-byte swizzle; rows past
 // rows_alloc read as zero.

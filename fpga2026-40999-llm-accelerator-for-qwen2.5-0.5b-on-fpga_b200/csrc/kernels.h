@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace qb {
 
 enum Epi { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
@@ -137,6 +139,25 @@ int launch_decode_epilogue(int n, uint32_t *slot_pos, cudaStream_t st);
 // 256-token block [slot][2][ceil(cap / 256)].
 int launch_k16_append(const uint16_t *k, int rows, const uint32_t *slots, const uint32_t *positions, int8_t *hi,
                       int8_t *lo, uint16_t *m16, uint8_t *lock, int cap, cudaStream_t st);
+// Query-tiled prefill attention (attention_tile.cu): a tile is up to 4
+// consecutive positions of one slot (row0: its first row in q / ctx); tiles
+// are grouped by the number of 1024-key CTAs their prefix needs (splits),
+// each group one launch of clusters of that size. The K codes are read
+// through kmap, a 2D tensor map of [rows][64] int8 (64-byte swizzle, box
+// 128 rows) in which key t of (slot, KV head g) is row krow0 + (slot * 2 + g)
+// * cap + t.
+struct AtTile {
+    int row0, nq, slot, pos0;
+};
+struct AtGroup {
+    int splits, kpc, first, count;
+};
+int attention_tile_plan(int rows, const uint32_t *slots, const uint32_t *positions, AtTile *tiles,
+                        std::vector<AtGroup> &groups);
+int launch_attention_tiles(const CUtensorMap &kmap, long long krow0, const AtTile *d_tiles, const AtGroup &grp,
+                           const uint16_t *q, const int8_t *vc, const float *ks, const float *vs, int cap,
+                           uint16_t *ctx, unsigned *err, cudaStream_t st);
+int make_kcache_map(CUtensorMap *map, const int8_t *kc, long long rows);
 // The engine's RTL KV mode (kv8_rtl.cu): kv [rows][256] post-RoPE k | v (bf16)
 // appended in the accelerator's K16 and V formats into one layer's caches:
 // kc / klo the high / low K planes, ks = m16 * 2^(lock - 142), vc, vs = m8 *

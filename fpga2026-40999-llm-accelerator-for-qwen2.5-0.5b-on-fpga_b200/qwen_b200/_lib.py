@@ -89,6 +89,9 @@ _SIGNATURES = {
                                                c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
     'qwen_b200_op_attention_cluster': (c_int, [c_void_p, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p,
                                                c_void_p, c_void_p, c_void_p, c_uint32, c_void_p, c_void_p]),
+    'qwen_b200_attention_prefill_workspace': (c_size_t, [c_uint32]),
+    'qwen_b200_op_attention_prefill': (c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                               c_uint32, c_void_p, c_void_p, c_size_t, c_void_p]),
     'qwen_b200_op_swiglu': (c_int, [c_void_p, c_uint32, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
     'qwen_b200_lm_head_workspace': (c_size_t, [c_uint32, c_uint32]),
     'qwen_b200_op_lm_head_argmax': (c_int, [c_void_p, c_uint32, c_void_p, c_float, c_void_p, c_void_p, c_uint32,

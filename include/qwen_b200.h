@@ -376,6 +376,23 @@ int qwen_b200_op_attention_noalloc(const uint16_t *q, uint32_t rows, const uint3
 int qwen_b200_op_attention_cluster(const uint16_t *q, uint32_t rows, const uint32_t *slots, const uint32_t *positions,
                                    uint32_t max_len, const int8_t *kcodes, const float *kscales, const int8_t *vcodes,
                                    const float *vscales, uint32_t capacity, uint16_t *ctx, void *stream);
+/* Attention of the prefill rows of one sequence, query tiles on the tensor
+ * cores (the engine's form for prompt chunks of 16 rows and more): rows
+ * r = 0 .. rows-1 are positions pos0 + r (each sees keys 0 .. pos0 + r), q
+ * [rows][14][64] post-RoPE, the sequence's KV8 cache of this layer kcodes /
+ * vcodes [2][capacity][64], kscales / vscales [2][capacity] with the rows' own
+ * keys already appended; ctx [rows][896]. Query tiles of 4 rows x 7 heads
+ * score against 128-key chunks with tcgen05.mma (kind::i8), and the context
+ * is a second tcgen05 product of the softmax weights' byte planes with the V
+ * codes; a cluster of up to 8 CTAs splits a prefix, so pos0 + rows <= 8192.
+ * Bit-identical to qwen_b200_op_attention_cluster. Workspace from
+ * qwen_b200_attention_prefill_workspace (zeroed once: its first 4 bytes
+ * become non-zero if a bounded wait expired); the call synchronises the
+ * stream. */
+size_t qwen_b200_attention_prefill_workspace(uint32_t rows);
+int qwen_b200_op_attention_prefill(const uint16_t *q, uint32_t rows, uint32_t pos0, const int8_t *kcodes,
+                                   const float *kscales, const int8_t *vcodes, const float *vscales, uint32_t capacity,
+                                   uint16_t *ctx, void *workspace, size_t workspace_bytes, void *stream);
 /* SwiGLU FFN input half: mid = bf16(bf16(silu(g)) * u) with g, u from
  * RMSNorm(x) (gamma NULL: no norm) times the interleaved gate/up weight
  * w_gu [2*4864][896] (row 2j gate j, row 2j+1 up j) and scales s_gu [2*4864]
