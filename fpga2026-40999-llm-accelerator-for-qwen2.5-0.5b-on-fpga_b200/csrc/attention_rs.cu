@@ -148,63 +148,6 @@ __device__ __forceinline__ unsigned ar_release_count(unsigned *p) {
     return old;
 }
 
-// Packed pairs of fp32 (Blackwell's f32x2 arithmetic: two IEEE fp32
-// operations, each rounded to nearest even, in one instruction).
-__device__ __forceinline__ unsigned long long ar_pk(float lo, float hi) {
-    unsigned long long d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-    return d;
-}
-__device__ __forceinline__ void ar_unpk(unsigned long long v, float &lo, float &hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long ar_add2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ unsigned long long ar_mul2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ unsigned long long ar_fma2(unsigned long long a, unsigned long long b,
-                                                      unsigned long long c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ unsigned long long ar_dup(float v) { return ar_pk(v, v); }
-
-// qexp (common.cuh) of two values at once, operation for operation: the
-// same IEEE fp32 operations in the same order on each half (a - b taken as
-// a + (-b) and fma(-n, c, x) as fma(n, -c, x), which are the same IEEE
-// results), so each half is bit-identical to qexp of that value.
-__device__ __forceinline__ void ar_qexp2(float x0, float x1, float &e0, float &e1) {
-    const unsigned long long x = ar_pk(x0, x1);
-    const unsigned long long sh = ar_add2(ar_mul2(x, ar_dup(1.44269504f)), ar_dup(12582912.0f));
-    const unsigned long long n = ar_add2(sh, ar_dup(-12582912.0f));
-    unsigned long long r = ar_fma2(n, ar_dup(-0.693145751953125f), x);
-    r = ar_fma2(n, ar_dup(-1.42860677e-6f), r);
-    unsigned long long q = ar_dup(1.98412698e-4f);
-    q = ar_fma2(q, r, ar_dup(1.38888889e-3f));
-    q = ar_fma2(q, r, ar_dup(8.33333333e-3f));
-    q = ar_fma2(q, r, ar_dup(4.16666667e-2f));
-    q = ar_fma2(q, r, ar_dup(1.66666667e-1f));
-    q = ar_fma2(q, r, ar_dup(0.5f));
-    q = ar_fma2(q, r, ar_dup(1.0f));
-    q = ar_fma2(q, r, ar_dup(1.0f));
-    float s0, s1;
-    ar_unpk(sh, s0, s1);
-    const int ni0 = __float_as_int(s0) - 0x4B400000, n10 = min(max(ni0, -126), 127);
-    const int ni1 = __float_as_int(s1) - 0x4B400000, n11 = min(max(ni1, -126), 127);
-    q = ar_mul2(ar_mul2(q, ar_pk(pow2i(n10), pow2i(n11))), ar_pk(pow2i(ni0 - n10), pow2i(ni1 - n11)));
-    float q0, q1;
-    ar_unpk(q, q0, q1);
-    e0 = !(x0 >= -104.0f) ? 0.0f : (x0 > 88.75f ? __int_as_float(0x7f800000) : q0);
-    e1 = !(x1 >= -104.0f) ? 0.0f : (x1 > 88.75f ? __int_as_float(0x7f800000) : q1);
-}
-
 template <int NW, bool CLUSTER>
 __global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
     using C = ArCfg<NW>;
@@ -429,8 +372,8 @@ __global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
     for (int c = 0; c < nchunks; ++c) {
         const float4 s4 = Sl[c * 32];
         float e0, e1, e2, e3;
-        ar_qexp2(__fsub_rn(s4.x, Mg), __fsub_rn(s4.y, Mg), e0, e1);
-        ar_qexp2(__fsub_rn(s4.z, Mg), __fsub_rn(s4.w, Mg), e2, e3);
+        qexp2(__fsub_rn(s4.x, Mg), __fsub_rn(s4.y, Mg), e0, e1);
+        qexp2(__fsub_rn(s4.z, Mg), __fsub_rn(s4.w, Mg), e2, e3);
         // rint(e * 2^40) (0 <= e <= 1, the product exact): the conversion
         // rounds to nearest even, as rint does
         z += __float2ll_rn(__fmul_rn(e0, 0x1p40f)) + __float2ll_rn(__fmul_rn(e1, 0x1p40f)) +

@@ -430,9 +430,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 float *row = S + qh * AT_SLD;
                 int t = cw;
                 for (; t + 3 * AT_CW < lim; t += 4 * AT_CW) {
-                    const float e0 = qexp(__fsub_rn(row[t], Mrow)), e1 = qexp(__fsub_rn(row[t + AT_CW], Mrow));
-                    const float e2 = qexp(__fsub_rn(row[t + 2 * AT_CW], Mrow));
-                    const float e3 = qexp(__fsub_rn(row[t + 3 * AT_CW], Mrow));
+                    float e0, e1, e2, e3;
+                    qexp2(__fsub_rn(row[t], Mrow), __fsub_rn(row[t + AT_CW], Mrow), e0, e1);
+                    qexp2(__fsub_rn(row[t + 2 * AT_CW], Mrow), __fsub_rn(row[t + 3 * AT_CW], Mrow), e2, e3);
                     row[t] = e0;
                     row[t + AT_CW] = e1;
                     row[t + 2 * AT_CW] = e2;

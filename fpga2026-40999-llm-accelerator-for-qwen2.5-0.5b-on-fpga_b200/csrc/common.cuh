@@ -166,6 +166,63 @@ __device__ __forceinline__ float qexp(float x) {
     return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(ni - n1));
 }
 
+// Packed pairs of fp32 (Blackwell's f32x2 arithmetic: two IEEE fp32
+// operations, each rounded to nearest even, in one instruction).
+__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
+    unsigned long long d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void unpk2(unsigned long long v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                      unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long dup2(float v) { return pk2(v, v); }
+
+// qexp (common.cuh) of two values at once, operation for operation: the
+// same IEEE fp32 operations in the same order on each half (a - b taken as
+// a + (-b) and fma(-n, c, x) as fma(n, -c, x), which are the same IEEE
+// results), so each half is bit-identical to qexp of that value.
+__device__ __forceinline__ void qexp2(float x0, float x1, float &e0, float &e1) {
+    const unsigned long long x = pk2(x0, x1);
+    const unsigned long long sh = add2(mul2(x, dup2(1.44269504f)), dup2(12582912.0f));
+    const unsigned long long n = add2(sh, dup2(-12582912.0f));
+    unsigned long long r = fma2(n, dup2(-0.693145751953125f), x);
+    r = fma2(n, dup2(-1.42860677e-6f), r);
+    unsigned long long q = dup2(1.98412698e-4f);
+    q = fma2(q, r, dup2(1.38888889e-3f));
+    q = fma2(q, r, dup2(8.33333333e-3f));
+    q = fma2(q, r, dup2(4.16666667e-2f));
+    q = fma2(q, r, dup2(1.66666667e-1f));
+    q = fma2(q, r, dup2(0.5f));
+    q = fma2(q, r, dup2(1.0f));
+    q = fma2(q, r, dup2(1.0f));
+    float s0, s1;
+    unpk2(sh, s0, s1);
+    const int ni0 = __float_as_int(s0) - 0x4B400000, n10 = min(max(ni0, -126), 127);
+    const int ni1 = __float_as_int(s1) - 0x4B400000, n11 = min(max(ni1, -126), 127);
+    q = mul2(mul2(q, pk2(pow2i(n10), pow2i(n11))), pk2(pow2i(ni0 - n10), pow2i(ni1 - n11)));
+    float q0, q1;
+    unpk2(q, q0, q1);
+    e0 = !(x0 >= -104.0f) ? 0.0f : (x0 > 88.75f ? __int_as_float(0x7f800000) : q0);
+    e1 = !(x1 >= -104.0f) ? 0.0f : (x1 > 88.75f ? __int_as_float(0x7f800000) : q1);
+}
+
 // rint(e * 2^40) for 0 <= e <= 1 (the exact softmax sum's grid) without a
 // conversion instruction: below 2^23 the 2^23 shift rounds to nearest even,
 // above it the product is already an integer read from its bits.
