@@ -18,11 +18,12 @@
 // Products:
 //   scores  D1[128 keys][128] = Kchunk[128][64] . B1[128][64]^T, B1 row
 //           l*32 + q*8 + h = limb l of query row q, head h (h = 7 and rows
-//           beyond the tile are zero), K = 64 dims; D1 in TMEM columns 0-127,
-//           one thread per key folds the four limb columns into int64
+//           beyond the tile are zero), K = 64 dims; D1 in TMEM columns 0-127 /
+//           128-255 for even / odd chunks, one thread per key folds the four
+//           limb columns into int64
 //   context D2[128][64 dims] += A2[128][128 keys] . B2[64][128 keys]^T with
 //           A2 row p*32 + q*8 + h = byte p of W (unsigned), B2 = the V chunk
-//           transposed (signed); D2 in TMEM columns 128-191, int32 per byte
+//           transposed (signed); D2 in TMEM columns 0-63, int32 per byte
 //           plane (at most 1024 x 255 x 127 < 2^31), folded to int64 at the end
 // Operands: K chunks by TMA (64-byte swizzle), V chunks by bulk copy through
 // the same 4-slot ring; B1, A2 and B2 written by the compute warps in the
@@ -50,7 +51,7 @@ constexpr int AT_CW = 16;                 // compute warps: 4 per TMEM lane quar
 constexpr int AT_CT = 32 * AT_CW;         // compute threads
 constexpr int AT_THREADS = 64 + AT_CT;
 constexpr int AT_MAX_SPLITS = 8;
-constexpr uint32_t AT_TMEM_COLS = 256;    // D1: 0-127, D2: 128-191
+constexpr uint32_t AT_TMEM_COLS = 256;    // D1 double-buffered: 0-127 / 128-255; D2 over the first (cols 0-63)
 
 struct AtSmem {
     static constexpr int B1 = 0;                          // [128][64] sw64
@@ -70,7 +71,7 @@ struct AtSmem {
     static constexpr int ST_M = 0, ST_V = 28, ST_Z = 32, ST_INV = 88, ST_S1 = 120, ST_S2 = 152, ST_F = 184;
     static constexpr int ST_WORDS = 216;
     static constexpr int BARS = ST + ST_WORDS * 4;
-    static constexpr int NBARS = 2 * AT_RING + 9;  // ring full / empty, d1 full / empty, ops full / empty x 2, d2, done, b1
+    static constexpr int NBARS = 2 * AT_RING + 12;  // ring full / empty, d1 full / empty x 2, ops full / empty x 2, d2, done, b1, scales
     static constexpr int SLOT = BARS + NBARS * 8;
     static constexpr int TOTAL = SLOT + 16;
     static constexpr int ALLOC = TOTAL + 1024;            // 1024-byte alignment of the base
@@ -187,8 +188,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const int rank = CLUSTER ? (int)tc::cluster_rank() : 0;
     const int nranks = CLUSTER ? (int)gridDim.x : 1;
     const int keys = tile.pos0 + tile.nq;  // the tile's prefix: keys 0 .. last position
-    const int k_begin = rank * a.kpc;
-    const int nkeys = max(0, min(a.kpc, keys - k_begin));
+    // the prefix split evenly over the cluster, in whole chunks (at most 1024 keys a CTA)
+    const int kpc = min(AT_KPC, ((keys + nranks - 1) / nranks + AT_CH - 1) / AT_CH * AT_CH);
+    const int k_begin = rank * kpc;
+    const int nkeys = max(0, min(kpc, keys - k_begin));
     const int nch = (nkeys + AT_CH - 1) / AT_CH;
     const size_t kvrow = ((size_t)tile.slot * QB_KVH + g) * a.cap + k_begin;  // this CTA's first key
 
@@ -206,10 +209,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tc::mbar_init(d1full + 6, 1);  // D2 complete
         tc::mbar_init(d1full + 7, 1);  // every MMA complete (TMEM may be freed)
         tc::mbar_init(d1full + 8, 1);  // B1 written
+        tc::mbar_init(d1full + 9, 1);  // the CTA's key and V scales copied
+        tc::mbar_init(d1full + 10, 1);  // second D1 buffer full
+        tc::mbar_init(d1full + 11, AT_CW);  // second D1 buffer read
         tc::mbar_fence_init();
         tc::tma_prefetch_desc(&kmap);
     }
-    uint64_t *d2full = d1full + 6, *mdone = d1full + 7, *b1ready = d1full + 8;
+    uint64_t *d2full = d1full + 6, *mdone = d1full + 7, *b1ready = d1full + 8, *sbar = d1full + 9;
+    uint64_t *d1f[2] = {d1full, d1full + 10}, *d1e[2] = {d1empty, d1full + 11};
+    // scales by bulk copy when both rows are 16-byte aligned and whole 16-byte runs stay inside the slot's row
+    const int nk4 = (nkeys + 3) & ~3;
+    const bool bulk_scales = nkeys > 0 && ((kvrow & 3) == 0) && k_begin + nk4 <= a.cap &&
+                             ((reinterpret_cast<uintptr_t>(a.ks) | reinterpret_cast<uintptr_t>(a.vs)) & 15) == 0;
     if (warp == 1) tc::tmem_alloc(slot_p, AT_TMEM_COLS);
     tc::tc_fence_before();
     __syncthreads();
@@ -220,8 +231,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     bool ok = true;
 
     if (warp == 0) {
-        // ---------------- producer: K chunks (TMA, swizzled), then V chunks
+        // ---------------- producer: the scales, K chunks (TMA, swizzled), then V chunks
         if (lane == 0) {
+            if (bulk_scales) {
+                tc::mbar_arrive_expect_tx(sbar, (uint32_t)(2 * nk4 * 4));
+                tc::bulk_load(kss, a.ks + kvrow, (uint32_t)(nk4 * 4), sbar);
+                tc::bulk_load(vss, a.vs + kvrow, (uint32_t)(nk4 * 4), sbar);
+            }
             for (int c = 0; c < nch; ++c) {
                 const int s = c % AT_RING;
                 if (ok) ok = tc::mbar_wait(&empty[s], ((c / AT_RING) & 1) ^ 1, a.err, 40);
@@ -256,12 +272,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             for (int c = 0; c < nch && ok; ++c) {
                 const int s = c % AT_RING;
                 if (!tc::mbar_wait(&full[s], (c / AT_RING) & 1, a.err, 42)) { ok = false; break; }
-                if (c > 0 && !tc::mbar_wait(d1empty, (c - 1) & 1, a.err, 43)) { ok = false; break; }
+                const int b = c & 1, use = c >> 1;  // D1 buffer and its use
+                if (use > 0 && !tc::mbar_wait(d1e[b], (use - 1) & 1, a.err, 43)) { ok = false; break; }
                 tc::tc_fence_after();
                 const uint32_t ka = tc::smem_u32(sm + L::RING + s * AT_CH * 64), qb = tc::smem_u32(sm + L::B1);
 #pragma unroll
-                for (int j = 0; j < 2; ++j) at_mma(tmem, at_desc_sw64(ka + 32 * j), at_desc_sw64(qb + 32 * j), id1, j > 0);
-                tc::mma_commit(d1full);
+                for (int j = 0; j < 2; ++j)
+                    at_mma(tmem + 128 * b, at_desc_sw64(ka + 32 * j), at_desc_sw64(qb + 32 * j), id1, j > 0);
+                tc::mma_commit(d1f[b]);
                 tc::mma_commit(&empty[s]);
             }
         }
@@ -280,7 +298,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 const uint32_t aa = tc::smem_u32(sm + L::A2 + b * 128 * 128), bb = tc::smem_u32(sm + L::B2 + b * 64 * 128);
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    at_mma(tmem + 128, tc::smem_desc_sw128(aa + 32 * j), tc::smem_desc_sw128(bb + 32 * j), id2,
+                    at_mma(tmem, tc::smem_desc_sw128(aa + 32 * j), tc::smem_desc_sw128(bb + 32 * j), id2,
                            c > 0 || j > 0);
                 tc::mma_commit(&opsempty[b]);
                 tc::mma_commit(&empty[(nch + c) % AT_RING]);  // the compute warps read that V chunk before opsfull
@@ -332,12 +350,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 *reinterpret_cast<uint2 *>(sm + L::B1 + at_sw64(n, dg >> 1) + 8 * (dg & 1)) = make_uint2(lb[l][0], lb[l][1]);
             }
         }
-        // scales of this CTA's keys; largest V scale of each query row's keys
+        // scales of this CTA's keys (bulk copies of the producer, or plain
+        // loads); largest V scale of each query row's keys
+        if (!bulk_scales)
+            for (int t = ct; t < nkeys; t += AT_CT) {
+                kss[t] = __ldg(a.ks + kvrow + t);
+                vss[t] = __ldg(a.vs + kvrow + t);
+            }
+        tc::fence_proxy_async_smem();  // B1 (generic writes) is read by the MMAs
+        at_csync();
+        if (ct == 0) tc::mbar_arrive(b1ready);
+        if (bulk_scales && ok) ok = tc::mbar_wait(sbar, 0, a.err, 46);
         float vm[AT_QT] = {0.f, 0.f, 0.f, 0.f};
         for (int t = ct; t < nkeys; t += AT_CT) {
-            const float kv = __ldg(a.ks + kvrow + t), vv = __ldg(a.vs + kvrow + t);
-            kss[t] = kv;
-            vss[t] = vv;
+            const float vv = vss[t];
 #pragma unroll
             for (int q = 0; q < AT_QT; ++q)
                 if (k_begin + t <= tile.pos0 + q) vm[q] = fmaxf(vm[q], vv);
@@ -347,21 +373,28 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             const float m = warp_max(vm[q]);
             if (lane == 0) wv[cw * 4 + q] = m;
         }
-        tc::fence_proxy_async_smem();  // B1 (generic writes) is read by the MMAs
-        at_csync();
-        if (ct == 0) tc::mbar_arrive(b1ready);
         // ---------------- phase 1: scores (thread: one key, query row `part`, 7 heads)
+        // the two power-of-two factors of unalign28 for this row's heads
+        float uc1[7], uc2[7];
+#pragma unroll
+        for (int h8 = 0; h8 < 7; ++h8) {
+            const int e = part < tile.nq ? qe[part * 7 + h8] : 0;
+            const int sh = e - 26, sh1 = max(sh, -126);
+            uc1[h8] = pow2i(sh1);
+            uc2[h8] = pow2i(sh - sh1);
+        }
         float mx[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) mx[j] = -INFINITY;
         for (int c = 0; c < nch; ++c) {
             int d[4][8];
-            if (ok) ok = tc::mbar_wait(d1full, c & 1, a.err, 46);
+            const int b = c & 1;
+            if (ok) ok = tc::mbar_wait(d1f[b], (c >> 1) & 1, a.err, 46);
             tc::tc_fence_after();
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
                 if (ok) {
-                    at_ld8(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(l * 32 + part * 8), d[l]);
+                    at_ld8(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(128 * b + l * 32 + part * 8), d[l]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 8; ++j) d[l][j] = 0;
@@ -370,7 +403,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             if (ok) at_ld_wait();
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(d1empty);  // this warp's part of D1 may be overwritten
+            if (lane == 0) tc::mbar_arrive(d1e[b]);  // this warp's part of the D1 buffer may be overwritten
             const int kk = c * AT_CH + quarter * 32 + lane;  // CTA-local key
             const int q = part;
             const bool in = kk < nkeys && q < tile.nq;
@@ -380,7 +413,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             for (int h8 = 0; h8 < 7; ++h8) {
                 const long long dot =
                     (long long)(d[0][h8] + d[1][h8] * 128) + (long long)(d[2][h8] + d[3][h8] * 128) * 16384ll;
-                const float s = vis ? rbf(__fmul_rn(unalign28(dot, qe[q * 7 + h8]), ksc) * 0.125f) : -INFINITY;
+                // unalign28(dot, e): (RN32(dot) * 2^s1) * 2^(s - s1)
+                const float u = (__ll2float_rn(dot) * uc1[h8]) * uc2[h8];
+                const float s = vis ? rbf(__fmul_rn(u, ksc) * 0.125f) : -INFINITY;
                 if (in) S[(q * 7 + h8) * AT_SLD + kk] = s;
                 mx[h8] = fmaxf(mx[h8], s);
             }
@@ -437,12 +472,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     row[t + AT_CW] = e1;
                     row[t + 2 * AT_CW] = e2;
                     row[t + 3 * AT_CW] = e3;
-                    z += (rint_2p40(e0) + rint_2p40(e1)) + (rint_2p40(e2) + rint_2p40(e3));
+                    // rint(e * 2^40): the scaling is exact, one conversion rounds to nearest even
+                    z += (__float2ll_rn(__fmul_rn(e0, 0x1p40f)) + __float2ll_rn(__fmul_rn(e1, 0x1p40f))) +
+                         (__float2ll_rn(__fmul_rn(e2, 0x1p40f)) + __float2ll_rn(__fmul_rn(e3, 0x1p40f)));
                 }
                 for (; t < lim; t += AT_CW) {
                     const float e = qexp(__fsub_rn(row[t], Mrow));
                     row[t] = e;
-                    z += rint_2p40(e);
+                    z += __float2ll_rn(__fmul_rn(e, 0x1p40f));
                 }
             }
             wz[cw * 32 + lane] = z;
@@ -515,20 +552,31 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     const float *row = S + qh * AT_SLD;
                     const int k0 = c * AT_CH + 8 * cw;
                     const int vis = min(nkeys, tile.pos0 + q + 1 - k_begin) - k0;  // keys of this group it sees
+                    // w = rint(RN32(bf16(E * inv) * vscale) * s1 * s2), two keys per
+                    // packed fp32 operation (each half one IEEE operation)
+                    const float4 v0 = *reinterpret_cast<const float4 *>(vss + k0);
+                    const float4 v1 = *reinterpret_cast<const float4 *>(vss + k0 + 4);
+                    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                    uint32_t wq[8];
+#pragma unroll
+                    for (int t = 0; t < 8; t += 2) {
+                        const unsigned long long e = mul2(pk2(row[k0 + t], row[k0 + t + 1]), dup2(inv));
+                        float e0, e1;
+                        unpk2(e, e0, e1);
+                        const __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+                        const unsigned long long w =
+                            mul2(mul2(mul2(pk2(__low2float(bb), __high2float(bb)), pk2(vv[t], vv[t + 1])), dup2(s1)),
+                                 dup2(s2));
+                        float w0, w1;
+                        unpk2(w, w0, w1);
+                        wq[t] = t < vis ? __float2uint_rn(w0) : 0u;
+                        wq[t + 1] = t + 1 < vis ? __float2uint_rn(w1) : 0u;
+                    }
 #pragma unroll
                     for (int i4 = 0; i4 < 2; ++i4) {
-                        uint32_t wq[4];
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const int t = 4 * i4 + k;
-                            wq[k] = 0;
-                            if (t < vis) {
-                                const float w = __fmul_rn(rbf(__fmul_rn(row[k0 + t], inv)), vss[k0 + t]);
-                                wq[k] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1), s2));
-                            }
-                        }
                         uint32_t pl[4];
-                        at_transpose4(wq[0], wq[1], wq[2], wq[3], pl);  // pl[p] byte k = byte p of key 4 i4 + k
+                        // pl[p] byte k = byte p of key 4 i4 + k
+                        at_transpose4(wq[4 * i4], wq[4 * i4 + 1], wq[4 * i4 + 2], wq[4 * i4 + 3], pl);
 #pragma unroll
                         for (int pp = 0; pp < 4; ++pp) pw[pp][i4] = pl[pp];
                     }
@@ -539,6 +587,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                         make_uint2(pw[pp][0], pw[pp][1]);
             }
             tc::fence_proxy_async_smem();
+            tc::tc_fence_before();  // D1 reads of phase 1 precede the D2 MMAs over the same columns
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&opsfull[b]);
         }
@@ -552,7 +601,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             // lane quarter p = byte plane, lane = row (q, h8); columns: dims 16 part .. + 15
             int v[16];
             if (ok && nch > 0) {
-                at_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(128 + 16 * part), v);
+                at_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(16 * part), v);
                 at_ld_wait();
             } else {
 #pragma unroll
