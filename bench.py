@@ -735,6 +735,42 @@ def micro_attention(torch, L, stream, sp, timed, hbm):
     return out
 
 
+def micro_prefill_attention(torch, L, stream, sp, timed):
+    """Attention of one 4096-token prompt's rows (positions 0..4095 of one
+    slot, causal): the query-tiled tensor-core kernel
+    (qwen_b200_op_attention_prefill, the engine's prefill form) against the
+    per-row kernel (qwen_b200_op_attention_cluster) on the same rows; both
+    give the same bits. Codes uniform in [-127, 127], scales in [0, 0.02], q
+    bf16 N(0, 1)."""
+    T = 4096
+    cap = T + 8
+    g = torch.Generator(device='cuda').manual_seed(SEED + 2)
+    kc = torch.randint(-127, 128, (2, cap, 64), dtype=torch.int8, device='cuda', generator=g)
+    vc = torch.randint(-127, 128, (2, cap, 64), dtype=torch.int8, device='cuda', generator=g)
+    ks = torch.rand(2, cap, device='cuda', generator=g) * 0.02
+    vs = torch.rand(2, cap, device='cuda', generator=g) * 0.02
+    q = torch.randn(T, 14, 64, device='cuda', generator=g).to(torch.bfloat16)
+    ctx_t = torch.zeros(T, HID, dtype=torch.bfloat16, device='cuda')
+    ctx_r = torch.zeros_like(ctx_t)
+    slots = torch.zeros(T, dtype=torch.int32, device='cuda')
+    pos = torch.arange(T, dtype=torch.int32, device='cuda')
+    wsb = L.qwen_b200_attention_prefill_workspace(T)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device='cuda')
+    tiled = lambda: L.qwen_b200_op_attention_prefill(q.data_ptr(), T, 0, kc.data_ptr(), ks.data_ptr(), vc.data_ptr(),
+                                                     vs.data_ptr(), cap, ctx_t.data_ptr(), ws.data_ptr(), wsb, sp)
+    per_row = lambda: L.qwen_b200_op_attention_cluster(q.data_ptr(), T, slots.data_ptr(), pos.data_ptr(), T,
+                                                       kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(), cap,
+                                                       ctx_r.data_ptr(), sp)
+    us_t = timed(tiled)
+    us_r = timed(per_row)
+    assert int(ws[:4].view(torch.int32)[0].item()) == 0, 'a bounded wait expired'
+    elements = T * (T + 1) // 2 * 14
+    return {'rows': T, 'positions': '0..4095 of one slot', 'tiled_us': round(us_t, 1), 'per_row_us': round(us_r, 1),
+            'tiled_kernel': 'attn_tile_kernel', 'per_row_kernel': attention_kernel_name(T, T),
+            'same_bits': bool(torch.equal(ctx_t, ctx_r)),
+            'row_head_key_elements': elements, 'tiled_g_elements_per_s': round(elements / us_t / 1e3, 1)}
+
+
 def run_micro(args):
     import torch
     import qwen_b200
@@ -746,14 +782,16 @@ def run_micro(args):
     timed = micro_timer(torch, stream, args.micro_reps)
     clocks = Clocks(gpu_index(0))
     clocks.start()
-    gemm = micro_gemm(torch, L, stream, sp, timed, hbm)
-    attn = micro_attention(torch, L, stream, sp, timed, hbm)
+    part = args.micro_part
+    gemm = micro_gemm(torch, L, stream, sp, timed, hbm) if part in ('all', 'gemm') else None
+    attn = micro_attention(torch, L, stream, sp, timed, hbm) if part in ('all', 'attention') else None
+    pre = micro_prefill_attention(torch, L, stream, sp, timed) if part in ('all', 'prefill') else None
     clk = clocks.stop()
     print(json.dumps({'record': 'operator microbenchmarks', 'n_gpus': 1, 'hbm_peak_gbs': hbm,
                       'peak_kind': peak_kind, 'reps': args.micro_reps,
                       'timing': 'median of per-launch CUDA events on the launching stream, L2 flushed '
                                 '(256 MB write) before every timed launch, after 3 warm-up launches',
-                      'gemm': gemm, 'attention': attn, 'clocks': clk}), flush=True)
+                      'gemm': gemm, 'attention': attn, 'prefill_attention': pre, 'clocks': clk}), flush=True)
     return 0
 
 
@@ -776,6 +814,7 @@ def main():
                     help='run only the operator microbenchmarks (projection shapes x rows, attention '
                          'contexts x batches; one GPU; prints its own JSON object)')
     ap.add_argument('--micro-reps', type=int, default=20)
+    ap.add_argument('--micro-part', choices=['all', 'gemm', 'attention', 'prefill'], default='all')
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
