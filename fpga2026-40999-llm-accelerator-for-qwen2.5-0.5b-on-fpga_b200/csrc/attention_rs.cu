@@ -291,6 +291,9 @@ __global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
     }
     __syncthreads();  // staged scales visible to every warp
     bool ok = true;
+    // unalign28(., e_g) = (RN32(.) * 2^s1) * 2^(s - s1): the two factors once
+    const int ush = e_g - 26, ush1 = max(ush, -126);
+    const float uc1 = pow2i(ush1), uc2 = pow2i(ush - ush1);
 
     // ---------------- phase 1: scores of this warp's blocks -> Sl[c]
     // Sl[c] = head gid, keys 192 c + 16 warp + {2tig, 2tig+1, 8+2tig, 9+2tig}
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
                 // per-limb sums over 64 dims are below 2^20: pairs add in int32
                 const long long dot = (long long)(d[nt][0][cc] + d[nt][0][cc + 2] * 128) +
                                       (long long)(d[nt][1][cc] + d[nt][1][cc + 2] * 128) * 16384ll;
-                const float v = rbf(__fmul_rn(unalign28(dot, e_g), kk[i]) * 0.125f);
+                const float v = rbf(__fmul_rn((__ll2float_rn(dot) * uc1) * uc2, kk[i]) * 0.125f);
                 sc[i] = key < nkeys ? v : -INFINITY;
                 mrun = fmaxf(mrun, sc[i]);
             }
@@ -443,11 +446,20 @@ __global__ void __launch_bounds__(32 * NW, 1) attn_rs_kernel(ArArgs a) {
             const float2 v23 = *reinterpret_cast<const float2 *>(vss + kb + 8 + 2 * tig);
             const float ev[4] = {e4.x, e4.y, e4.z, e4.w}, vv[4] = {v01.x, v01.y, v23.x, v23.y};
             const int koff[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
+            // w = rint(RN32(bf16(E * inv) * vscale) * s1 * s2), two keys per
+            // packed fp32 operation (each half one IEEE operation)
             uint32_t wq[4], b[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float w = (gv && kb + koff[i] < nkeys) ? __fmul_rn(rbf(__fmul_rn(ev[i], inv_g)), vv[i]) : 0.f;
-                wq[i] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1_g), s2_g));
+            for (int i = 0; i < 4; i += 2) {
+                float p0, p1;
+                unpk2(mul2(pk2(ev[i], ev[i + 1]), dup2(inv_g)), p0, p1);
+                const __nv_bfloat162 bb = __floats2bfloat162_rn(p0, p1);
+                float w0, w1;
+                unpk2(mul2(mul2(mul2(pk2(__low2float(bb), __high2float(bb)), pk2(vv[i], vv[i + 1])), dup2(s1_g)),
+                           dup2(s2_g)),
+                      w0, w1);
+                wq[i] = (gv && kb + koff[i] < nkeys) ? __float2uint_rn(w0) : 0u;
+                wq[i + 1] = (gv && kb + koff[i + 1] < nkeys) ? __float2uint_rn(w1) : 0u;
             }
             ar_transpose4(wq, b);
             const uint32_t *vb =
