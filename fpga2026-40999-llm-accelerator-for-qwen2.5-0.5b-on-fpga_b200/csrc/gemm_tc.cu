@@ -685,6 +685,225 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// ------------------------------------------------- persistent projections
+// The projections at prefill sizes (enough (row tile, channel tile) pairs to
+// fill the GPU twice) as a persistent kernel with the LM head's roles: one
+// CTA per SM walks the tile list with a stride of the grid, the weight and
+// limb tiles stream without a gap between tiles, and the accumulator is double
+// buffered in TMEM so the epilogue warps fold, scale and write one tile while
+// the MMA warp computes the next. The epilogue works from registers: TMEM lane
+// = output channel, so for each row the 32 lanes of a warp write 32
+// consecutive channels; SiLU(gate) * up pairs the channels of neighbouring
+// lanes. Same arithmetic as tc_gemm_kernel (bit-identical outputs).
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_persist_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap lmap, TcArgs a) {
+    using L = LhSmem;
+    constexpr int AS = L::A_STAGES, BS = L::B_STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+    uint64_t *full_a = bars, *empty_a = full_a + AS, *full_b = empty_a + AS, *empty_b = full_b + BS;
+    uint64_t *acc_full = empty_b + BS, *acc_empty = acc_full + 2, *done = acc_empty + 2;
+    uint32_t *slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntn = a.N / TC_BM;                          // channel tiles
+    const int total = ntn * ((a.M + TC_BN - 1) / TC_BN);  // (row tile, channel tile) pairs
+    const int G = (int)gridDim.x;
+    const int nt = total > (int)blockIdx.x ? (total - (int)blockIdx.x + G - 1) / G : 0;  // this CTA's tiles
+    const int KC = a.K / TC_BK;
+    const int nchunks = nt * KC;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < AS; ++s) {
+            tc::mbar_init(&full_a[s], 1);
+            tc::mbar_init(&empty_a[s], 1);
+        }
+        for (int s = 0; s < BS; ++s) {
+            tc::mbar_init(&full_b[s], 1);
+            tc::mbar_init(&empty_b[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&acc_full[b], 1);
+            tc::mbar_init(&acc_empty[b], TC_CONV / 32);  // one arrival per epilogue warp
+        }
+        tc::mbar_init(done, 1);
+        tc::mbar_fence_init();
+        tc::tma_prefetch_desc(&wmap);
+        tc::tma_prefetch_desc(&lmap);
+    }
+    if (warp == 1) tc::tmem_alloc(slot, L::TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *slot;
+    pdl_trigger();
+    bool ok = nt > 0;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            auto tile_of = [&](int g, int &n0, int &m0) {
+                const int t = (int)blockIdx.x + (g / KC) * G;
+                n0 = (t % ntn) * TC_BM;
+                m0 = (t / ntn) * TC_BN;
+            };
+            auto issue_a = [&](int g) {
+                int n0, m0;
+                tile_of(g, n0, m0);
+                const int s = g % AS;
+                tc::mbar_arrive_expect_tx(&full_a[s], (uint32_t)L::A_BYTES);
+                tc::tma_load_2d(smem + L::A_OFF + s * L::A_BYTES, &wmap, &full_a[s], (g % KC) * TC_BK, n0);
+            };
+            int ia = 0, ib = 0;
+            // weights are constant: the first stages load before the wait for
+            // the kernel that writes the limb planes
+            for (; ok && ia < min(nchunks, AS); ++ia) issue_a(ia);
+            pdl_wait();
+            uint32_t idle = 0;
+            while (ok && (ib < nchunks || ia < nchunks)) {
+                bool progress = false;
+                if (ib < nchunks) {
+                    const int s = ib % BS, ph = (ib / BS) & 1;
+                    if (tc::mbar_try_wait(&empty_b[s], ph ^ 1)) {
+                        int n0, m0;
+                        tile_of(ib, n0, m0);
+                        tc::mbar_arrive_expect_tx(&full_b[s], (uint32_t)L::B_BYTES);
+                        tma_load_3d(smem + L::B_OFF + s * L::B_BYTES, &lmap, &full_b[s], (ib % KC) * TC_BK, m0, 0);
+                        ++ib;
+                        progress = true;
+                    }
+                }
+                if (ia < nchunks) {
+                    const int s = ia % AS, ph = (ia / AS) & 1;
+                    if (tc::mbar_try_wait(&empty_a[s], ph ^ 1)) {
+                        issue_a(ia);
+                        ++ia;
+                        progress = true;
+                    }
+                }
+                if (progress) {
+                    idle = 0;
+                } else if (++idle > (1u << 22)) {
+                    atomicExch(a.err, 27u);
+                    ok = false;
+                }
+            }
+        } else {
+            pdl_wait();
+        }
+    } else if (warp == 1) {
+        pdl_wait();
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_s8_s32(TC_BM, TC_MN);
+            for (int j = 0; ok && j < nt; ++j) {
+                const int buf = j & 1;
+                // the epilogue has read this buffer's previous tile
+                if (j >= 2 && !tc::mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1, a.err, 28)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * TC_MN);
+                for (int kc = 0; kc < KC; ++kc) {
+                    const int g = j * KC + kc;
+                    const int sa = g % AS, sb = g % BS;
+                    if (!tc::mbar_wait(&full_a[sa], (g / AS) & 1, a.err, 29) ||
+                        !tc::mbar_wait(&full_b[sb], (g / BS) & 1, a.err, 30)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t ab = tc::smem_u32(smem + L::A_OFF + sa * L::A_BYTES);
+                    const uint32_t bb = tc::smem_u32(smem + L::B_OFF + sb * L::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 32; ++k)
+                        mma_s8(d, tc::smem_desc_sw128(ab + 32 * k), tc::smem_desc_sw128(bb + 32 * k), idesc,
+                               kc > 0 || k > 0);
+                    tc::mma_commit(&empty_a[sa]);
+                    tc::mma_commit(&empty_b[sb]);
+                }
+                if (ok) tc::mma_commit(&acc_full[buf]);
+            }
+            // every MMA issued by this thread has finished before TMEM is freed
+            tc::mma_commit(done);
+            tc::mbar_wait(done, 0, a.err, 31);
+        }
+        __syncwarp();
+    } else {
+        // lane quarter q: channels 32q..32q+31 of a tile (this thread: one
+        // channel), rows 32h..32h+31
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        pdl_wait();  // row exponents and residual rows come from preceding kernels
+        for (int j = 0; j < nt; ++j) {
+            const int buf = j & 1;
+            const int t = (int)blockIdx.x + j * G;
+            const int n = (t % ntn) * TC_BM + q * 32 + lane, m0 = (t / ntn) * TC_BN;
+            const float scn = __ldg(a.scale + n);
+            const float bn = EPI == EPI_BIAS ? bf2f(a.bias[n]) : 0.f;
+            ok = ok && tc::mbar_wait(&acc_full[buf], (j >> 1) & 1, a.err, 26);
+            tc::tc_fence_after();
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                const int r0 = m0 + 32 * h + 16 * hh;  // first of this pass's 16 rows
+                int d[TC_NL][16];
+#pragma unroll
+                for (int l = 0; l < TC_NL; ++l) {
+                    if (ok) {
+                        tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) +
+                                              (uint32_t)(buf * TC_MN + l * TC_BN + 32 * h + 16 * hh),
+                                          d[l]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) d[l][jj] = 0;
+                    }
+                }
+                // residual rows, requested before the TMEM data is used
+                float res[16];
+                if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj)
+                        res[jj] = r0 + jj < a.M ? bf2f(a.y[(size_t)(r0 + jj) * a.N + n]) : 0.f;
+                }
+                if (ok) tmem_ld_wait();
+                if (hh == 1) {
+                    // this warp's TMEM reads are complete: the buffer may be refilled
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
+                }
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) {
+                    const int m = r0 + jj;
+                    // K = 896: limb pairs fold in int32 as in tc_gemm_kernel
+                    const long long v = KC <= 14 ? (long long)(d[0][jj] + d[1][jj] * 128) +
+                                                       (long long)(d[2][jj] + d[3][jj] * 128) * 16384ll
+                                                 : (long long)d[0][jj] + (long long)d[1][jj] * 128ll +
+                                                       (long long)d[2][jj] * 16384ll + (long long)d[3][jj] * 2097152ll;
+                    const bool live = m < a.M;  // the same for every lane of the warp
+                    const float o = live ? rbf(rbf(exact_acc(v, __ldg(a.ex + m))) * scn) : 0.f;
+                    if constexpr (EPI == EPI_SWIGLU) {
+                        // channels 2i (gate i) and 2i+1 (up i): model_backend.py:105-106
+                        const float up = __shfl_xor_sync(0xffffffffu, o, 1);
+                        if (live && !(lane & 1))
+                            a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = f2bf(rbf(silu_q(o)) * up);
+                    } else if (live) {
+                        float w = o;
+                        if constexpr (EPI == EPI_BIAS) w = rbf(o + bn);
+                        if constexpr (EPI == EPI_RESIDUAL) w = rbf(res[jj] + o);
+                        a.y[(size_t)m * a.N + n] = f2bf(w);
+                    }
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, L::TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------- host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -810,6 +1029,23 @@ static int run_lmhead(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs &
                       st, 1u, wmap, lmap, a);
 }
 
+template <int EPI>
+static int run_persist(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs &a, cudaStream_t st) {
+    using L = LhSmem;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << (dev & 31)))) {
+        if (cudaFuncSetAttribute(tc_persist_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+            cudaSuccess)
+            return -3;
+        configured |= 1u << (dev & 31);
+    }
+    const int tiles = (a.N / TC_BM) * ((a.M + TC_BN - 1) / TC_BN);
+    return launch_pdl(tc_persist_kernel<EPI>, dim3(tiles < TC_SLOTS ? tiles : TC_SLOTS), dim3(TC_THREADS),
+                      (size_t)L::ALLOC, st, 1u, wmap, lmap, a);
+}
+
 int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, const int *ex, int rows, int k,
                    const float *scale, const uint16_t *bias, int n, uint16_t *y, int splits, void *ws,
                    size_t ws_bytes, bool clear, const TcArgmax *am, cudaStream_t st) {
@@ -844,6 +1080,17 @@ int launch_gemm_tc(int epi, const CUtensorMap &wmap, const CUtensorMap &lmap, co
     if (clear) {
         if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return -3;
         pdl_break();
+    }
+    // prefill sizes (the tiles fill the GPU at least twice, no split): the
+    // persistent form overlaps each tile's epilogue with the next tile's MMAs
+    const int tiles = (n / TC_BM) * ((rows + TC_BN - 1) / TC_BN);
+    if (splits == 1 && tiles >= 2 * TC_SLOTS && epi != EPI_ARGMAX) {
+        switch (epi) {
+            case EPI_PLAIN: return run_persist<EPI_PLAIN>(wmap, lmap, a, st);
+            case EPI_BIAS: return run_persist<EPI_BIAS>(wmap, lmap, a, st);
+            case EPI_RESIDUAL: return run_persist<EPI_RESIDUAL>(wmap, lmap, a, st);
+            case EPI_SWIGLU: return run_persist<EPI_SWIGLU>(wmap, lmap, a, st);
+        }
     }
     switch (epi) {
         case EPI_PLAIN: return run_tc<EPI_PLAIN>(wmap, lmap, a, splits, st);

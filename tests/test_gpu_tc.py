@@ -79,18 +79,24 @@ def test_gemm_tc_extreme_rows(rows):
     assert np.array_equal(got, exp), f'{np.mean(got == exp):.5f} bit-equal'
 
 
-@pytest.mark.parametrize('k,n,epi', [(896, 1152, 'bias'), (896, 9728, 'swiglu')])
-@pytest.mark.parametrize('rows', [256, 512, 4096])
+@pytest.mark.parametrize('k,n,epi,rows', [(896, 1152, 'bias', 256), (896, 1152, 'bias', 512),
+                                          (896, 1152, 'bias', 4096), (896, 9728, 'swiglu', 256),
+                                          (896, 9728, 'swiglu', 512), (896, 9728, 'swiglu', 4096),
+                                          (896, 896, 'residual', 3000), (4864, 896, 'residual', 4096),
+                                          (896, 896, 'plain', 4096)])
 def test_gemm_tc_prefill_rows(k, n, epi, rows):
-    """The microbenchmark's M = 512 / 4096 and the engine's 256-row prefill
-    chunk, on the fused q|k|v and gate/up shapes: many row tiles per channel
-    tile (no split-K), still bit-identical to the exact projection."""
+    """The microbenchmark's M = 512 / 4096 and prefill chunks on the
+    projection shapes: many row tiles per channel tile (no split-K; from 296
+    tiles the persistent double-buffered kernel, with a ragged last row tile
+    at 3000 rows), still bit-identical to the exact projection."""
     r = np.random.default_rng(k + n + rows + 1)
     x = bf16_round(r.standard_normal((rows, k)).astype(np.float32))
     w = r.integers(-127, 128, size=(n, k), dtype=np.int8)
     s = bf16_round(r.uniform(2e-4, 4e-4, size=n).astype(np.float32))
     b = bf16_round(r.standard_normal(n).astype(np.float32) * 0.02)
     y0 = np.zeros((rows, n // 2 if epi == 'swiglu' else n), np.float32)
+    if epi == 'residual':
+        y0 = bf16_round(r.standard_normal(y0.shape).astype(np.float32))
     got = run_tc(x, w, s, b, y0, epi)
     exp = expected(x, w, s, b, y0, epi)
     assert np.array_equal(got, exp), f'tc gemm {k}x{n} rows {rows} {epi}: {np.mean(got == exp):.5f} bit-equal'
