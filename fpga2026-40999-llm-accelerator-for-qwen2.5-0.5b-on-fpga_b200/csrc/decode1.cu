@@ -60,16 +60,16 @@ constexpr int D1_LONG_BYTES = D1A_KS + 4 * (2 * QB_D1_MAX_KEYS + 7 * D1A_SS);
 // short-context area (after the limb planes): prefetched history and scratch;
 // every region starts on a 16-byte boundary (vector and bulk-copy accesses)
 __host__ __device__ constexpr int d1_al16(int x) { return (x + 15) & ~15; }
-constexpr int D1S_KC = 0;                                            // int8 [2][64 keys][64] K codes, later V^T [2][64 dims][64 keys]
+constexpr int D1S_KC = 0;                                            // int8 [2][64 keys][64] K codes
 constexpr int D1S_VC = d1_al16(D1S_KC + 2 * D1_SHORT * 64);          // int8 [2][64][64] V codes
 constexpr int D1S_KS = d1_al16(D1S_VC + 2 * D1_SHORT * 64);          // float [2][64 + 8] K scales (16-byte aligned superset)
 constexpr int D1S_VS = d1_al16(D1S_KS + 2 * (D1_SHORT + 8) * 4);     // float [2][64 + 8] V scales
-constexpr int D1S_QL = d1_al16(D1S_VS + 2 * (D1_SHORT + 8) * 4);     // int8 [14][272] q limb planes, later W byte planes [14][16] x 16 B
+constexpr int D1S_QL = d1_al16(D1S_VS + 2 * (D1_SHORT + 8) * 4);     // int8 [14][272] q limb planes
 constexpr int D1S_NEW = d1_al16(D1S_QL + 14 * D1S_QLS);              // int8 [2 k|v][2 heads][64] new codes
-constexpr int D1S_SS = D1_SHORT + 1;                                  // scores per head, padded
-constexpr int D1S_S = d1_al16(D1S_NEW + 4 * 64);                     // float [14][65] scores -> E -> W (u32)
-constexpr int D1S_CTX = d1_al16(D1S_S + 14 * D1S_SS * 4);            // bf16 [896] context
-constexpr int D1S_MISC = d1_al16(D1S_CTX + QB_HID * 2);              // qe[16], M[16], inv[16], s1[16], s2[16], F[16], nsc[4], vmax[2]
+constexpr int D1S_WS = D1_SHORT + 1;                                  // softmax weights per head, padded
+constexpr int D1S_W = d1_al16(D1S_NEW + 4 * 64);                     // u32 [14][65] softmax weights W
+constexpr int D1S_CTX = d1_al16(D1S_W + 14 * D1S_WS * 4);            // bf16 [896] context
+constexpr int D1S_MISC = d1_al16(D1S_CTX + QB_HID * 2);              // qe[16], nsc[4]
 constexpr int D1S_QKV = d1_al16(D1S_MISC + 128 * 4);                 // bf16 [1152] this step's q | k | v (pre-RoPE)
 constexpr int D1_SHORT_BYTES = d1_al16(D1S_QKV + QB_QKV * 2);
 constexpr int D1_LIMB_BYTES = d1_al16(4 * QB_FFN + 16);
@@ -103,27 +103,6 @@ static_assert(d1_smem().shortw % 16 == 0 && d1_smem().work % 16 == 0 && d1_smem(
 
 // Barrier of the 256 compute threads (the producer warp never joins).
 __device__ __forceinline__ void d1_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
-// 4 x 4 byte transpose: o[j] byte i = r[i] byte j.
-__device__ __forceinline__ void transpose4(const uint32_t (&r)[4], uint32_t (&o)[4]) {
-    const uint32_t t0 = prmt(r[0], r[1], 0x5140u), t1 = prmt(r[0], r[1], 0x7362u);
-    const uint32_t t2 = prmt(r[2], r[3], 0x5140u), t3 = prmt(r[2], r[3], 0x7362u);
-    o[0] = prmt(t0, t2, 0x5410u);
-    o[1] = prmt(t0, t2, 0x7632u);
-    o[2] = prmt(t1, t3, 0x5410u);
-    o[3] = prmt(t1, t3, 0x7632u);
-}
-// sum of 4 signed bytes of a times 4 unsigned bytes of b, plus c
-__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
 
 // [begin, end) of part c of n items split over g parts
 __device__ __forceinline__ void d1_part(int n, int c, int g, int &b, int &e) {
@@ -755,13 +734,9 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
     const int L = (int)pos + 1;
     int8_t *ql = reinterpret_cast<int8_t *>(sw + D1S_QL);
     int8_t *nw = reinterpret_cast<int8_t *>(sw + D1S_NEW);  // [k|v][g][64]
-    float *S = reinterpret_cast<float *>(sw + D1S_S);       // [14][64]
     uint16_t *ctx = reinterpret_cast<uint16_t *>(sw + D1S_CTX);
     int *qe = reinterpret_cast<int *>(sw + D1S_MISC);
-    float *M = reinterpret_cast<float *>(qe + 16), *inv = M + 16, *s1 = M + 32, *s2 = M + 48;
-    int *F = reinterpret_cast<int *>(M + 64);
-    float *nsc = M + 80;  // new scales [k|v][g]
-    float *vmx = M + 84;  // [g]
+    float *nsc = reinterpret_cast<float *>(qe + 16);  // new scales [k|v][g]
     uint16_t *qkv = reinterpret_cast<uint16_t *>(sw + D1S_QKV);
     if (tid < QB_QKV / 8) reinterpret_cast<uint4 *>(qkv)[tid] = __ldcg(reinterpret_cast<const uint4 *>(a.qkv) + tid);
     const float *cs = a.rope + (size_t)pos * 64;
@@ -824,132 +799,88 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
     }
     auto kscale = [&](int gg, int t) -> float { return t == L - 1 ? nsc[gg] : ksh[gg][t]; };
     auto vscale = [&](int gg, int t) -> float { return t == L - 1 ? nsc[2 + gg] : vsh[gg][t]; };
-    // scores: thread (head h = tid % 16, key t = tid / 16 + 16 i)
-    const int h = tid & 15, tl = tid >> 4, g = h / 7;
-    float mloc = -INFINITY, vloc = 0.f;
-    if (h < QB_QH) {
-        const uint32_t *qr = reinterpret_cast<const uint32_t *>(ql + h * D1S_QLS);
-        for (int t = tl; t < L; t += 16) {
-            vloc = fmaxf(vloc, vscale(g, t));
-            const uint32_t *kr = reinterpret_cast<const uint32_t *>(
-                t == L - 1 ? nw + g * 64 : reinterpret_cast<const int8_t *>(sw + D1S_KC) + (g * D1_SHORT + t) * 64);
-            int d4[4] = {0, 0, 0, 0};
+    // one half-warp per query head (warps 0..6), every step inside the half
+    // (shuffles and one warp-synchronous buffer, no CTA barrier): lane hl takes
+    // keys hl, hl + 16, hl + 32, hl + 48 for the scores and the softmax and
+    // dims 4 hl .. 4 hl + 3 for the context
+    if (warp < QB_QH / 2) {
+        const int h = tid >> 4, hl = tid & 15, g = h / 7;
+        const uint4 *qr = reinterpret_cast<const uint4 *>(ql + h * D1S_QLS);
+        uint32_t *W = reinterpret_cast<uint32_t *>(sw + D1S_W) + h * D1S_WS;
+        float sc[4], vsj[4];
 #pragma unroll
-            for (int w4 = 0; w4 < 4; ++w4) {
-                const uint4 k4 = reinterpret_cast<const uint4 *>(kr)[w4];
+        for (int j = 0; j < 4; ++j) {
+            const int t = hl + 16 * j;
+            sc[j] = -INFINITY;
+            vsj[j] = 0.f;
+            if (t < L) {
+                const uint4 *kr = reinterpret_cast<const uint4 *>(
+                    t == L - 1 ? nw + g * 64 : reinterpret_cast<const int8_t *>(sw + D1S_KC) + (g * D1_SHORT + t) * 64);
+                int d4[4] = {0, 0, 0, 0};
 #pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    const uint4 q4 = reinterpret_cast<const uint4 *>(qr + l * 16)[w4];
-                    d4[l] = __dp4a((int)k4.x, (int)q4.x, d4[l]);
-                    d4[l] = __dp4a((int)k4.y, (int)q4.y, d4[l]);
-                    d4[l] = __dp4a((int)k4.z, (int)q4.z, d4[l]);
-                    d4[l] = __dp4a((int)k4.w, (int)q4.w, d4[l]);
+                for (int i = 0; i < 4; ++i) {
+                    const int w4 = (i + (hl >> 1)) & 3;  // 16-byte chunk order rotated by lane: no bank conflicts
+                    const uint4 k4 = kr[w4];
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) {
+                        const uint4 q4 = qr[l * 4 + w4];
+                        d4[l] = __dp4a((int)k4.x, (int)q4.x, d4[l]);
+                        d4[l] = __dp4a((int)k4.y, (int)q4.y, d4[l]);
+                        d4[l] = __dp4a((int)k4.z, (int)q4.z, d4[l]);
+                        d4[l] = __dp4a((int)k4.w, (int)q4.w, d4[l]);
+                    }
                 }
+                const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
+                                      (long long)d4[3] * 2097152ll;
+                sc[j] = rbf(__fmul_rn(unalign28(dot, qe[h]), kscale(g, t)) * 0.125f);
+                vsj[j] = vscale(g, t);
             }
-            const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
-                                  (long long)d4[3] * 2097152ll;
-            const float sc = rbf(__fmul_rn(unalign28(dot, qe[h]), kscale(g, t)) * 0.125f);
-            S[h * D1S_SS + t] = sc;
-            mloc = fmaxf(mloc, sc);
         }
-    }
-    // lanes h and h + 16 of a warp share a head
-    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 16));
-    vloc = fmaxf(vloc, __shfl_xor_sync(0xffffffffu, vloc, 16));
-    float *redf = reinterpret_cast<float *>(red);
-    if (lane < 16) {
-        redf[warp * 32 + lane] = mloc;
-        redf[warp * 32 + 16 + lane] = vloc;
-    }
-    d1_sync();
-    if (tid < 16) {
-        float m = -INFINITY, v = 0.f;
-        for (int w = 0; w < D1_WARPS; ++w) {
-            m = fmaxf(m, redf[w * 32 + tid]);
-            v = fmaxf(v, redf[w * 32 + 16 + tid]);
+        float M = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+        float vmax = fmaxf(fmaxf(vsj[0], vsj[1]), fmaxf(vsj[2], vsj[3]));
+#pragma unroll
+        for (int o = 8; o; o >>= 1) {
+            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
         }
-        M[tid] = m;
-        if (tid == 0 || tid == 7) vmx[tid / 7] = v;  // heads 0 and 7 saw every key of KV heads 0 and 1
-    }
-    d1_sync();
-    // E = qexp(S - max), exact sums
-    long long z = 0;
-    if (h < QB_QH)
-        for (int t = tl; t < L; t += 16) {
-            const float e = qexp(__fsub_rn(S[h * D1S_SS + t], M[h]));
-            S[h * D1S_SS + t] = e;
-            z += rint_2p40(e);
+        // E = qexp(S - max), exact sum
+        float e[4];
+        long long z = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            e[j] = hl + 16 * j < L ? qexp(__fsub_rn(sc[j], M)) : 0.f;
+            z += rint_2p40(e[j]);
         }
-    z += __shfl_xor_sync(0xffffffffu, z, 16);
-    d1_sync();
-    if (lane < 16) red[warp * 16 + lane] = z;
-    d1_sync();
-    if (tid < QB_QH) {
-        long long zt = 0;
-        for (int w = 0; w < D1_WARPS; ++w) zt += red[w * 16 + tid];
-        const float iv = __fdiv_rn(1.0f, __fmul_rn(__ll2float_rn(zt), 0x1p-40f));
-        const int f = row_exponent(__fmul_rn(rbf(iv), vmx[tid / 7]));
+#pragma unroll
+        for (int o = 8; o; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        const float iv = __fdiv_rn(1.0f, __fmul_rn(__ll2float_rn(z), 0x1p-40f));
+        const int f = row_exponent(__fmul_rn(rbf(iv), vmax));
         const int sh = 26 - f, sh1 = min(sh, 127);
-        inv[tid] = iv;
-        F[tid] = f;
-        s1[tid] = pow2i(sh1);
-        s2[tid] = pow2i(sh - sh1);
-    }
-    d1_sync();
-    // W = rint(RN32(P * vscale) * 2^(26-F)), P = bf16(E / Z)
-    if (h < QB_QH)
-        for (int t = tl; t < L; t += 16) {
-            const float w = __fmul_rn(rbf(__fmul_rn(S[h * D1S_SS + t], inv[h])), vscale(g, t));
-            reinterpret_cast<uint32_t *>(S)[h * D1S_SS + t] = __float2uint_rn(__fmul_rn(__fmul_rn(w, s1[h]), s2[h]));
-        }
-    d1_sync();
-    // context on the integer dot-product units: V^T [g][dim][key] (4 keys per
-    // word, word index swizzled by dim against bank conflicts) and the four
-    // byte planes of W [h][key / 4] (16 bytes: planes 0..3 of 4 keys), then
-    // dp4a (V codes signed x W bytes unsigned) per plane, exact in int32
-    const int L4 = (L + 3) >> 2;
-    uint32_t *vt = reinterpret_cast<uint32_t *>(sw + D1S_KC);
-    uint4 *wp = reinterpret_cast<uint4 *>(sw + D1S_QL);
-    for (int i = tid; i < 2 * 16 * L4; i += D1_THREADS) {
-        const int gg = i / (16 * L4), t4 = (i / 16) % L4, d4 = i & 15;
-        uint32_t r[4], o[4];
+        const float f1 = pow2i(sh1), f2 = pow2i(sh - sh1);
+        // W = rint(RN32(P * vscale) * 2^(26-F)), P = bf16(E / Z) <= bf16(1 / Z), so
+        // RN32(P * vscale) < 2^(F+1) and W <= 2^27
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int t = 4 * t4 + j;
-            r[j] = t < L - 1 ? reinterpret_cast<const uint32_t *>(sw + D1S_VC)[(gg * D1_SHORT + t) * 16 + d4]
-                 : t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + gg) * 64)[d4] : 0u;
+        for (int j = 0; j < 4; ++j)
+            if (hl + 16 * j < L)
+                W[hl + 16 * j] = __float2uint_rn(__fmul_rn(__fmul_rn(__fmul_rn(rbf(__fmul_rn(e[j], iv)), vsj[j]), f1), f2));
+        __syncwarp();
+        // context: exact sum over the keys of W times the V codes (|W v| < 2^34,
+        // 64 keys < 2^40)
+        long long c[4] = {0, 0, 0, 0};
+#pragma unroll 4
+        for (int t = 0; t < L; ++t) {
+            const int wt = (int)W[t];
+            const uint32_t v4 = t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + g) * 64)[hl]
+                                           : reinterpret_cast<const uint32_t *>(sw + D1S_VC)[(g * D1_SHORT + t) * 16 + hl];
+            c[0] += (long long)wt * (int)(int8_t)(v4 & 0xffu);
+            c[1] += (long long)wt * (int)(int8_t)((v4 >> 8) & 0xffu);
+            c[2] += (long long)wt * (int)(int8_t)((v4 >> 16) & 0xffu);
+            c[3] += (long long)wt * (int)(int8_t)(v4 >> 24);
         }
-        transpose4(r, o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int d = 4 * d4 + j;
-            vt[(gg * 64 + d) * 16 + (t4 ^ (d & 15))] = o[j];
-        }
-    }
-    for (int i = tid; i < QB_QH * L4; i += D1_THREADS) {
-        const int hh = i / L4, t4 = i % L4;
-        const uint32_t *W = reinterpret_cast<const uint32_t *>(S) + hh * D1S_SS;
-        uint32_t r[4], o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) r[j] = 4 * t4 + j < L ? W[4 * t4 + j] : 0u;
-        transpose4(r, o);
-        wp[hh * 16 + t4] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    d1_sync();
-    for (int i = tid; i < QB_QH * 64; i += D1_THREADS) {
-        const int hh = i >> 6, d = i & 63, gg = hh / 7;
-        int acc[4] = {0, 0, 0, 0};
-        for (int t4 = 0; t4 < L4; ++t4) {
-            const uint32_t v = vt[(gg * 64 + d) * 16 + (t4 ^ (d & 15))];
-            const uint4 w = wp[hh * 16 + t4];
-            acc[0] = dp4a_su(v, w.x, acc[0]);
-            acc[1] = dp4a_su(v, w.y, acc[1]);
-            acc[2] = dp4a_su(v, w.z, acc[2]);
-            acc[3] = dp4a_su(v, w.w, acc[3]);
-        }
-        const long long dot = (long long)acc[0] + (long long)acc[1] * 256ll + (long long)acc[2] * 65536ll +
-                              (long long)acc[3] * 16777216ll;
-        ctx[hh * 64 + d] = f2bf(unalign28(dot, F[hh]));
+        uint2 pk;
+        pk.x = (uint32_t)f2bf(unalign28(c[0], f)) | ((uint32_t)f2bf(unalign28(c[1], f)) << 16);
+        pk.y = (uint32_t)f2bf(unalign28(c[2], f)) | ((uint32_t)f2bf(unalign28(c[3], f)) << 16);
+        reinterpret_cast<uint2 *>(ctx + h * 64)[hl] = pk;
     }
     d1_sync();
 }

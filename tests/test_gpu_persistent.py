@@ -68,6 +68,30 @@ def test_persistent_long_context_equals_per_kernel(engine, golden, length):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize('length', [0, 29, 61])
+def test_persistent_short_context_edges_equal_per_kernel(engine, golden, length):
+    """The fused short-context phase (every CTA attends over at most 64 keys,
+    one warp per head, lane = keys lane and lane + 32): single-row steps from
+    synthetic caches across its edges, 1..4 keys, 30..33 keys (the second key
+    per lane starts at 33) and 62..65 keys (65 leaves the short phase)."""
+    out = {}
+    for persistent in (True, False):
+        engine.set_persistent(persistent)
+        engine.reset(1)
+        if length:
+            engine.fill_kv_synthetic(1, length, 7 + length)
+        toks, logits, tok = [], [], golden['prompt'][0]
+        for i in range(4):
+            tok, lg = engine.forward(1, [tok], length + i, want_logits=True)
+            toks.append(tok)
+            logits.append(from_bits(lg))
+        out[persistent] = (toks, logits)
+    engine.set_persistent(True)
+    assert out[True][0] == out[False][0]
+    for i, (a, b) in enumerate(zip(out[True][1], out[False][1])):
+        assert np.array_equal(a, b), f'step {i}'
+
+
 def test_persistent_device_and_host_decode_steps(engine, golden):
     import torch
     prompt = golden['prompt']
