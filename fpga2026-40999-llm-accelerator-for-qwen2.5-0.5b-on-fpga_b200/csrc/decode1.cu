@@ -65,17 +65,13 @@ constexpr int D1S_VC = d1_al16(D1S_KC + 2 * D1_SHORT * 64);          // int8 [2]
 constexpr int D1S_KS = d1_al16(D1S_VC + 2 * D1_SHORT * 64);          // float [2][64 + 8] K scales (16-byte aligned superset)
 constexpr int D1S_VS = d1_al16(D1S_KS + 2 * (D1_SHORT + 8) * 4);     // float [2][64 + 8] V scales
 constexpr int D1S_QL = d1_al16(D1S_VS + 2 * (D1_SHORT + 8) * 4);     // int8 [14][272] q limb planes
-constexpr int D1S_NEW = d1_al16(D1S_QL + 14 * D1S_QLS);              // int8 [2 k|v][2 heads][64] new codes
-constexpr int D1S_WS = D1_SHORT + 1;                                  // softmax weights per head, padded
-constexpr int D1S_W = d1_al16(D1S_NEW + 4 * 64);                     // u32 [14][65] softmax weights W
+constexpr int D1S_WS = D1_SHORT + 2;                                  // softmax weights per head (+1 zero), 8-byte rows
+constexpr int D1S_W = d1_al16(D1S_QL + 14 * D1S_QLS);                // u32 [14][66] softmax weights W
 constexpr int D1S_CTX = d1_al16(D1S_W + 14 * D1S_WS * 4);            // bf16 [896] context
 constexpr int D1S_MISC = d1_al16(D1S_CTX + QB_HID * 2);              // qe[16], nsc[4]
-constexpr int D1S_QKV = d1_al16(D1S_MISC + 128 * 4);                 // bf16 [1152] this step's q | k | v (pre-RoPE)
-constexpr int D1_SHORT_BYTES = d1_al16(D1S_QKV + QB_QKV * 2);
+constexpr int D1_SHORT_BYTES = d1_al16(D1S_MISC + 32 * 4);
 constexpr int D1_LIMB_BYTES = d1_al16(4 * QB_FFN + 16);
 static_assert(D1S_QLS % 16 == 0 && D1_RING % 16 == 0, "16-byte aligned rows");
-static_assert(14 * 16 * 16 <= D1S_NEW - D1S_QL, "W byte planes fit in the q limb area");
-static_assert(2 * 64 * 64 <= D1S_VC - D1S_KC, "V^T fits in the K history area");
 
 struct D1Smem {
     int ring, work, shortw, bars, segs, layers, red, accs, part, total;
@@ -103,6 +99,19 @@ static_assert(d1_smem().shortw % 16 == 0 && d1_smem().work % 16 == 0 && d1_smem(
 
 // Barrier of the 256 compute threads (the producer warp never joins).
 __device__ __forceinline__ void d1_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Two-way dot products of two unsigned 16-bit halves of a with two signed
+// bytes of b (bytes 0, 1 for lo, bytes 2, 3 for hi), plus c.
+__device__ __forceinline__ int dp2a_lo_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
 // [begin, end) of part c of n items split over g parts
 __device__ __forceinline__ void d1_part(int n, int c, int g, int &b, int &e) {
@@ -727,61 +736,74 @@ __device__ void d1_issue_history(const D1Args &a, int layer, uint32_t slot, uint
 }
 
 // Fused short-context attention (every CTA, all 14 heads): see the file
-// comment; leaves ctx (bf16 [896]) in shared memory.
+// comment; leaves ctx (bf16 [896]) in shared memory. Every step runs on
+// half-warps (16 lanes): the 18 head vectors of this step's q | k | v, then
+// one half-warp per query head for the scores, the softmax and the context,
+// with one CTA barrier between the two and one at the end. The new key and
+// value go into row pos of the history area, next to the bulk-copied rows
+// [0, pos), so the loops over the keys read one layout.
 __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, uint32_t pos, uint8_t *sw,
-                                   uint64_t *kvbar, long long *red, bool &ok) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+                                   uint64_t *kvbar, bool &ok) {
+    const int tid = threadIdx.x, warp = tid >> 5, hl = tid & 15;
     const int L = (int)pos + 1;
     int8_t *ql = reinterpret_cast<int8_t *>(sw + D1S_QL);
-    int8_t *nw = reinterpret_cast<int8_t *>(sw + D1S_NEW);  // [k|v][g][64]
+    int8_t *kc = reinterpret_cast<int8_t *>(sw + D1S_KC), *vc = reinterpret_cast<int8_t *>(sw + D1S_VC);
     uint16_t *ctx = reinterpret_cast<uint16_t *>(sw + D1S_CTX);
     int *qe = reinterpret_cast<int *>(sw + D1S_MISC);
     float *nsc = reinterpret_cast<float *>(qe + 16);  // new scales [k|v][g]
-    uint16_t *qkv = reinterpret_cast<uint16_t *>(sw + D1S_QKV);
-    if (tid < QB_QKV / 8) reinterpret_cast<uint4 *>(qkv)[tid] = __ldcg(reinterpret_cast<const uint4 *>(a.qkv) + tid);
-    const float *cs = a.rope + (size_t)pos * 64;
-    const float c = cs[lane], sn = cs[32 + lane];
-    d1_sync();
-    // 18 head vectors: q heads 0..13, k heads (14, 15), v heads (16, 17)
-    for (int hv = warp; hv < 18; hv += D1_WARPS) {
-        const uint16_t *p = qkv + hv * 64;
-        float lo = bf2f(p[lane]), hi = bf2f(p[lane + 32]);
-        if (hv < 16) {  // RoPE on q and k (model_backend.py:73-78)
-            const float nlo = rbf(__fadd_rn(__fmul_rn(lo, c), __fmul_rn(-hi, sn)));
-            const float nhi = rbf(__fadd_rn(__fmul_rn(hi, c), __fmul_rn(lo, sn)));
-            lo = nlo;
-            hi = nhi;
+    // 18 head vectors: q heads 0..13, k heads (14, 15), v heads (16, 17); lane
+    // hl of a half-warp holds dims 2 hl, 2 hl + 1 and their RoPE partners
+    // 2 hl + 32, 2 hl + 33 (model_backend.py:73-78)
+    const float2 cs = reinterpret_cast<const float2 *>(a.rope + (size_t)pos * 64)[hl];
+    const float2 sn = reinterpret_cast<const float2 *>(a.rope + (size_t)pos * 64 + 32)[hl];
+    for (int hv = tid >> 4; hv < 18; hv += 16) {
+        const uint32_t plo = __ldcg(reinterpret_cast<const uint32_t *>(a.qkv + hv * 64) + hl);
+        const uint32_t phi = __ldcg(reinterpret_cast<const uint32_t *>(a.qkv + hv * 64 + 32) + hl);
+        float v[4] = {bflo(plo), bfhi(plo), bflo(phi), bfhi(phi)};  // dims 2hl, 2hl+1, 2hl+32, 2hl+33
+        if (hv < 16) {
+            const float c2[2] = {cs.x, cs.y}, s2[2] = {sn.x, sn.y};
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float lo = v[i], hi = v[2 + i];
+                v[i] = rbf(__fadd_rn(__fmul_rn(lo, c2[i]), __fmul_rn(-hi, s2[i])));
+                v[2 + i] = rbf(__fadd_rn(__fmul_rn(hi, c2[i]), __fmul_rn(lo, s2[i])));
+            }
         }
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+        for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (hv < QB_QH) {
-            const int e = row_exponent(warp_max(fmaxf(fabsf(lo), fabsf(hi))));
-            int l0[4], l1[4];
-            limbs4(align28_int(lo, e), l0);
-            limbs4(align28_int(hi, e), l1);
+            const int e = row_exponent(amax);
+            int lm[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) limbs4(align28_int(v[i], e), lm[i]);
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
-                ql[hv * D1S_QLS + l * 64 + lane] = (int8_t)l0[l];
-                ql[hv * D1S_QLS + l * 64 + lane + 32] = (int8_t)l1[l];
+                uint16_t *row = reinterpret_cast<uint16_t *>(ql + hv * D1S_QLS + l * 64);
+                row[hl] = (uint16_t)((lm[0][l] & 0xff) | ((lm[1][l] & 0xff) << 8));
+                row[16 + hl] = (uint16_t)((lm[2][l] & 0xff) | ((lm[3][l] & 0xff) << 8));
             }
-            if (lane == 0) qe[hv] = e;
+            if (hl == 0) qe[hv] = e;
         } else {
             const int isv = hv >= 16, g = (hv - 14) & 1;
-            const float amax = warp_max(fmaxf(fabsf(lo), fabsf(hi)));
-            const float s = __fdiv_rn(amax, 127.0f);
-            int clo = 0, chi = 0;
-            if (s > 0.f) {
-                clo = (int)fminf(fmaxf(rintf(__fdiv_rn(lo, s)), -127.f), 127.f);
-                chi = (int)fminf(fmaxf(rintf(__fdiv_rn(hi, s)), -127.f), 127.f);
-            }
-            int8_t *nc = nw + (isv * 2 + g) * 64;
-            nc[lane] = (int8_t)clo;
-            nc[lane + 32] = (int8_t)chi;
-            if (lane == 0) nsc[isv * 2 + g] = s;
+            const float sc = __fdiv_rn(amax, 127.0f);
+            int cd[4] = {0, 0, 0, 0};
+            if (sc > 0.f)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) cd[i] = (int)fminf(fmaxf(rintf(__fdiv_rn(v[i], sc)), -127.f), 127.f);
+            const uint16_t wlo = (uint16_t)((cd[0] & 0xff) | ((cd[1] & 0xff) << 8));
+            const uint16_t whi = (uint16_t)((cd[2] & 0xff) | ((cd[3] & 0xff) << 8));
+            uint16_t *row = reinterpret_cast<uint16_t *>((isv ? vc : kc) + (g * D1_SHORT + pos) * 64);
+            row[hl] = wlo;
+            row[16 + hl] = whi;
+            if (hl == 0) nsc[isv * 2 + g] = sc;
             if (blockIdx.x == 0) {  // the one writer of the cache entry
                 const size_t base = ((size_t)slot * 2 + g) * a.cap + pos;
-                int8_t *gc = (isv ? a.vc : a.kc) + (size_t)a.codes_per_layer * layer + base * 64;
-                gc[lane] = (int8_t)clo;
-                gc[lane + 32] = (int8_t)chi;
-                if (lane == 0) (isv ? a.vs : a.ks)[(size_t)a.scales_per_layer * layer + base] = s;
+                uint16_t *gc =
+                    reinterpret_cast<uint16_t *>((isv ? a.vc : a.kc) + (size_t)a.codes_per_layer * layer + base * 64);
+                gc[hl] = wlo;
+                gc[16 + hl] = whi;
+                if (hl == 0) (isv ? a.vs : a.ks)[(size_t)a.scales_per_layer * layer + base] = sc;
             }
         }
     }
@@ -797,16 +819,14 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         vsh[gg] = reinterpret_cast<const float *>(sw + D1S_VS + gg * (D1_SHORT + 8) * 4 +
                                                   (reinterpret_cast<uintptr_t>(a.vs + o) & 15));
     }
-    auto kscale = [&](int gg, int t) -> float { return t == L - 1 ? nsc[gg] : ksh[gg][t]; };
-    auto vscale = [&](int gg, int t) -> float { return t == L - 1 ? nsc[2 + gg] : vsh[gg][t]; };
-    // one half-warp per query head (warps 0..6), every step inside the half
-    // (shuffles and one warp-synchronous buffer, no CTA barrier): lane hl takes
-    // keys hl, hl + 16, hl + 32, hl + 48 for the scores and the softmax and
-    // dims 4 hl .. 4 hl + 3 for the context
+    // one half-warp per query head (warps 0..6): lane hl takes keys hl, hl + 16,
+    // hl + 32, hl + 48 for the scores and the softmax and dims 4 hl .. 4 hl + 3
+    // for the context
     if (warp < QB_QH / 2) {
-        const int h = tid >> 4, hl = tid & 15, g = h / 7;
+        const int h = tid >> 4, g = h / 7;
         const uint4 *qr = reinterpret_cast<const uint4 *>(ql + h * D1S_QLS);
         uint32_t *W = reinterpret_cast<uint32_t *>(sw + D1S_W) + h * D1S_WS;
+        const float knew = nsc[g], vnew = nsc[2 + g];
         float sc[4], vsj[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -814,8 +834,7 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
             sc[j] = -INFINITY;
             vsj[j] = 0.f;
             if (t < L) {
-                const uint4 *kr = reinterpret_cast<const uint4 *>(
-                    t == L - 1 ? nw + g * 64 : reinterpret_cast<const int8_t *>(sw + D1S_KC) + (g * D1_SHORT + t) * 64);
+                const uint4 *kr = reinterpret_cast<const uint4 *>(kc + (g * D1_SHORT + t) * 64);
                 int d4[4] = {0, 0, 0, 0};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -832,8 +851,8 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
                 }
                 const long long dot = (long long)d4[0] + (long long)d4[1] * 128ll + (long long)d4[2] * 16384ll +
                                       (long long)d4[3] * 2097152ll;
-                sc[j] = rbf(__fmul_rn(unalign28(dot, qe[h]), kscale(g, t)) * 0.125f);
-                vsj[j] = vscale(g, t);
+                sc[j] = rbf(__fmul_rn(unalign28(dot, qe[h]), t == L - 1 ? knew : ksh[g][t]) * 0.125f);
+                vsj[j] = t == L - 1 ? vnew : vsh[g][t];
             }
         }
         float M = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
@@ -863,20 +882,31 @@ __device__ void d1_attention_short(const D1Args &a, int layer, uint32_t slot, ui
         for (int j = 0; j < 4; ++j)
             if (hl + 16 * j < L)
                 W[hl + 16 * j] = __float2uint_rn(__fmul_rn(__fmul_rn(__fmul_rn(rbf(__fmul_rn(e[j], iv)), vsj[j]), f1), f2));
+        if (hl == 0 && (L & 1)) W[L] = 0u;  // the odd key's partner in the pairs below
         __syncwarp();
-        // context: exact sum over the keys of W times the V codes (|W v| < 2^34,
-        // 64 keys < 2^40)
-        long long c[4] = {0, 0, 0, 0};
-#pragma unroll 4
-        for (int t = 0; t < L; ++t) {
-            const int wt = (int)W[t];
-            const uint32_t v4 = t == L - 1 ? reinterpret_cast<const uint32_t *>(nw + (2 + g) * 64)[hl]
-                                           : reinterpret_cast<const uint32_t *>(sw + D1S_VC)[(g * D1_SHORT + t) * 16 + hl];
-            c[0] += (long long)wt * (int)(int8_t)(v4 & 0xffu);
-            c[1] += (long long)wt * (int)(int8_t)((v4 >> 8) & 0xffu);
-            c[2] += (long long)wt * (int)(int8_t)((v4 >> 16) & 0xffu);
-            c[3] += (long long)wt * (int)(int8_t)(v4 >> 24);
+        // context: exact sum over the keys of W times the V codes, two keys per
+        // dp2a (W's 16-bit halves, unsigned, times the two keys' codes of one
+        // dim, signed); every partial sum is exact in int32 (64 x 65535 x 127 < 2^30)
+        int lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+        const uint32_t *vr = reinterpret_cast<const uint32_t *>(vc + g * D1_SHORT * 64) + hl;
+#pragma unroll 2
+        for (int t = 0; t < L; t += 2) {
+            const uint2 w2 = *reinterpret_cast<const uint2 *>(W + t);
+            const uint32_t wl = __byte_perm(w2.x, w2.y, 0x5410u), wh = __byte_perm(w2.x, w2.y, 0x7632u);
+            const uint32_t v0 = vr[t * 16], v1 = vr[(t + 1) * 16];
+            const uint32_t p01 = __byte_perm(v0, v1, 0x5140u), p23 = __byte_perm(v0, v1, 0x7362u);
+            lo[0] = dp2a_lo_us(wl, p01, lo[0]);
+            hi[0] = dp2a_lo_us(wh, p01, hi[0]);
+            lo[1] = dp2a_hi_us(wl, p01, lo[1]);
+            hi[1] = dp2a_hi_us(wh, p01, hi[1]);
+            lo[2] = dp2a_lo_us(wl, p23, lo[2]);
+            hi[2] = dp2a_lo_us(wh, p23, hi[2]);
+            lo[3] = dp2a_hi_us(wl, p23, lo[3]);
+            hi[3] = dp2a_hi_us(wh, p23, hi[3]);
         }
+        long long c[4];
+#pragma unroll
+        for (int d = 0; d < 4; ++d) c[d] = (long long)lo[d] + (long long)hi[d] * 65536ll;
         uint2 pk;
         pk.x = (uint32_t)f2bf(unalign28(c[0], f)) | ((uint32_t)f2bf(unalign28(c[1], f)) << 16);
         pk.y = (uint32_t)f2bf(unalign28(c[2], f)) | ((uint32_t)f2bf(unalign28(c[3], f)) << 16);
@@ -900,7 +930,6 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     uint8_t *work = sm + Ls.work, *sw = sm + Ls.shortw;
     int8_t *xl = reinterpret_cast<int8_t *>(work);
     int *ex = reinterpret_cast<int *>(work + 4 * QB_FFN);
-    long long *red = reinterpret_cast<long long *>(sm + Ls.red);
     uint8_t *rd = sm + Ls.red;
     int *part = reinterpret_cast<int *>(sm + Ls.part);
     const int tid = threadIdx.x, c = blockIdx.x, G = gridDim.x, warp = tid >> 5;
@@ -935,7 +964,12 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     uint32_t g[4];
     for (int l = 0; l < QB_NL; ++l) {
         int b, e;
-        if (shortctx && tid == 0) d1_issue_history(a, l, slot, pos, sw, kvbar);
+        // this layer's K/V history by warp 7, which holds no values in the
+        // RMSNorm below (the previous layer's reads of the area are long done)
+        if (shortctx && tid == QB_HID / 4) {
+            tc::fence_proxy_async_smem();
+            d1_issue_history(a, l, slot, pos, sw, kvbar);
+        }
         // A: RMSNorm + QKV rows + bias (pre-RoPE)
         d1_part(QB_QKV, c, G, b, e);
         {
@@ -952,7 +986,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
         d1_grid_sync(a, ++nbar, ok);
         // B + C: attention, then O + residual
         if (shortctx) {
-            d1_attention_short(a, l, slot, pos, sw, kvbar, red, ok);
+            d1_attention_short(a, l, slot, pos, sw, kvbar, ok);
             d1_row896<false, false>(reinterpret_cast<const uint16_t *>(sw + D1S_CTX), nullptr, 0.f, xl, ex, rd);
         } else {
             if (c < QB_KVH) d1_attention(a, l, c, slot, pos, work, rd);
