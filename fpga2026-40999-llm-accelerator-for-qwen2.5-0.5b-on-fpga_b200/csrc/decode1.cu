@@ -981,9 +981,11 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                                   [&](int r, float acc) {
                                       a.qkv[b + r] = f2bf(rbf(rbf(rbf(acc) * sc[r]) + bf2f(bs[r])));
                                   });
-            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
+        // the slice goes back to the producer after the barrier: bulk copies
+        // issued just before it were measured to delay its release fence
+        d1_done(R, s++);
         // B + C: attention, then O + residual
         if (shortctx) {
             d1_attention_short(a, l, slot, pos, sw, kvbar, ok);
@@ -1003,9 +1005,9 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                                       xo[r] = v;
                                       a.x[b + r] = f2bf(v);
                                   });
-            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
+        d1_done(R, s++);
         // D: RMSNorm + gate/up pairs + SiLU*mul (rows 2j, 2j+1 stay in one warp)
         d1_part(QB_FFN, c, G, b, e);
         {
@@ -1031,9 +1033,9 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                     }
                 }
             }
-            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
+        d1_done(R, s++);
         // E: down + residual
         d1_row4864(a.mid, xl, ex, rd);
         d1_part(QB_HID, c, G, b, e);
@@ -1046,9 +1048,9 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                                       xo[r] = v;
                                       a.x[b + r] = f2bf(v);
                                   });
-            d1_done(R, s++);
         }
         d1_grid_sync(a, ++nbar, ok);
+        d1_done(R, s++);
     }
     // LM head: final RMSNorm (gains come with the first piece), this CTA's
     // rows in 32-row pieces (4 per warp), the warp's best (value, index)
