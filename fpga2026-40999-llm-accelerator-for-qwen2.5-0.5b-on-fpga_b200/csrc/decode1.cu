@@ -14,8 +14,8 @@
 // the current phase computes or waits. Phases are separated by grid barriers
 // (an arrival counter in global memory, bounded spin):
 //   A  every CTA: RMSNorm of x (exact sum of squares) -> limb planes in shared
-//      memory; its QKV rows + bias -> qkv (pre-RoPE, bf16). The same thread
-//      also starts the bulk copies of this layer's KV8 history (short contexts)
+//      memory; its QKV rows + bias -> qkv (pre-RoPE, bf16). Meanwhile warp 7
+//      starts the bulk copies of this layer's KV8 history (short contexts)
 //   B+C short contexts (<= 64 keys): every CTA computes the attention of all
 //      14 heads itself from the prefetched history and the new key/value (RoPE,
 //      KV8 quantise; CTA 0 appends them to the cache), then its O rows +
