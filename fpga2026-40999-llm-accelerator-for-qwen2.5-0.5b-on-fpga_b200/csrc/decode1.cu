@@ -44,6 +44,7 @@ constexpr int D1_SEGS = 16;      // slices in flight at most (one mbarrier each)
 constexpr int D1_LM_ROWS = 32;   // LM-head rows per slice
 constexpr int D1_MAXROWS = 72;   // largest projection slice of one CTA (gate/up pairs)
 constexpr int D1_SHORT = 64;     // contexts up to this many keys use the fused B+C phase
+constexpr unsigned D1_BAR_STRIDE = 128;  // grid barriers per launch at most (97 short, 121 long)
 
 constexpr int D1S_QLS = 4 * 64 + 16;  // q limb planes per head: 16-byte aligned, padded against bank conflicts
 
@@ -250,7 +251,7 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
 // loads, the CTA proceeds together. After `limit` polls the wait gives up
 // with code 20 in the error flag; `extra` raises the target (a host-set test
 // switch makes the last barrier unreachable that way, see D1Args).
-__device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &ok, unsigned extra = 0,
+__device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned base, unsigned k, bool &ok, unsigned extra = 0,
                                              uint32_t limit = 1u << 24) {
     __shared__ int s_ok;
     d1_sync();
@@ -259,9 +260,9 @@ __device__ __forceinline__ void d1_grid_sync(const D1Args &a, unsigned k, bool &
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         bool good = ok;
         if (good) {
-            const unsigned target = k * gridDim.x + extra;
+            const unsigned target = base + k * gridDim.x + extra;
             uint32_t spins = 0;
-            while (ld_acquire_gpu(a.bar) < target) {
+            while ((int)(ld_acquire_gpu(a.bar) - target) < 0) {  // wrap-safe
                 if (++spins > limit) {
                     atomicExch(a.err, 20u);
                     good = false;
@@ -948,7 +949,20 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
         if ((tid & 31) == 0) d1_produce(a, R);  // weights are constant: stream from the start
         return;
     }
-    const uint32_t slot = __ldcg(a.meta + 1), pos = __ldcg(a.meta + 2);
+    uint32_t id, slot, pos;
+    if (a.tok_in) {  // device-resident step: the token of slot 0 at its current position
+        id = __ldcg(a.tok_in);
+        slot = 0;
+        pos = __ldcg(a.slot_pos);
+    } else {
+        id = __ldcg(a.meta);
+        slot = __ldcg(a.meta + 1);
+        pos = __ldcg(a.meta + 2);
+    }
+    const uint16_t *x0 = a.embed + (size_t)id * QB_HID;  // the step's embedding row
+    // barrier targets of this launch: every launch advances the arrival
+    // counter by exactly D1_BAR_STRIDE arrivals per CTA (the last barrier pads it)
+    const unsigned launches = __ldcg(a.bar + 1), base = launches * (D1_BAR_STRIDE * (unsigned)G);
     const bool shortctx = pos + 1 <= (uint32_t)D1_SHORT;
     // this CTA's rows of the residual stream (the O and down rows are the same
     // partition), kept here so the residual additions need no global read
@@ -956,7 +970,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     {
         int b, e;
         d1_part(QB_HID, c, G, b, e);
-        if (tid < e - b) xo[tid] = bf2f(__ldcg(a.x + b + tid));
+        if (tid < e - b) xo[tid] = bf2f(__ldg(x0 + b + tid));
     }
     bool ok = true;
     unsigned nbar = 0;
@@ -974,7 +988,8 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
         d1_part(QB_QKV, c, G, b, e);
         {
             const uint8_t *seg = d1_wait(a, R, s, g, ok);
-            d1_row896<true, true>(a.x, reinterpret_cast<const uint16_t *>(seg + g[3]), a.eps, xl, ex, rd);
+            d1_row896<true, true>(l == 0 ? x0 : a.x, reinterpret_cast<const uint16_t *>(seg + g[3]), a.eps, xl, ex,
+                                  rd);
             const float *sc = reinterpret_cast<const float *>(seg + g[1]);
             const uint16_t *bs = reinterpret_cast<const uint16_t *>(seg + g[2]);
             d1_mma_rows16<QB_HID>(reinterpret_cast<const int8_t *>(seg), e - b, xl, ex[0], part,
@@ -982,7 +997,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                                       a.qkv[b + r] = f2bf(rbf(rbf(rbf(acc) * sc[r]) + bf2f(bs[r])));
                                   });
         }
-        d1_grid_sync(a, ++nbar, ok);
+        d1_grid_sync(a, base, ++nbar, ok);
         // the slice goes back to the producer after the barrier: bulk copies
         // issued just before it were measured to delay its release fence
         d1_done(R, s++);
@@ -992,7 +1007,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
             d1_row896<false, false>(reinterpret_cast<const uint16_t *>(sw + D1S_CTX), nullptr, 0.f, xl, ex, rd);
         } else {
             if (c < QB_KVH) d1_attention(a, l, c, slot, pos, work, rd);
-            d1_grid_sync(a, ++nbar, ok);
+            d1_grid_sync(a, base, ++nbar, ok);
             d1_row896<false, true>(a.ctx, nullptr, 0.f, xl, ex, rd);
         }
         d1_part(QB_HID, c, G, b, e);
@@ -1006,7 +1021,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                                       a.x[b + r] = f2bf(v);
                                   });
         }
-        d1_grid_sync(a, ++nbar, ok);
+        d1_grid_sync(a, base, ++nbar, ok);
         d1_done(R, s++);
         // D: RMSNorm + gate/up pairs + SiLU*mul (rows 2j, 2j+1 stay in one warp)
         d1_part(QB_FFN, c, G, b, e);
@@ -1034,7 +1049,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                 }
             }
         }
-        d1_grid_sync(a, ++nbar, ok);
+        d1_grid_sync(a, base, ++nbar, ok);
         d1_done(R, s++);
         // E: down + residual
         d1_row4864(a.mid, xl, ex, rd);
@@ -1049,7 +1064,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                                       a.x[b + r] = f2bf(v);
                                   });
         }
-        d1_grid_sync(a, ++nbar, ok);
+        d1_grid_sync(a, base, ++nbar, ok);
         d1_done(R, s++);
     }
     // LM head: final RMSNorm (gains come with the first piece), this CTA's
@@ -1125,7 +1140,7 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
     }
     // every slice has been consumed (no bulk copy is in flight) and the
     // projections run on mma.sync: nothing asynchronous is outstanding here
-    d1_grid_sync(a, ++nbar, ok, a.expire_last_barrier ? 1u : 0u, a.expire_last_barrier ? (1u << 14) : (1u << 24));
+    d1_grid_sync(a, base, ++nbar, ok, a.expire_last_barrier ? 1u : 0u, a.expire_last_barrier ? (1u << 14) : (1u << 24));
     if (c == 0 && tid < 32) {
         float v = -INFINITY;
         uint32_t i = 0;
@@ -1146,7 +1161,15 @@ __global__ void __launch_bounds__(D1_BLOCK, 1) decode1_kernel(D1Args a) {
                 i = oi;
             }
         }
-        if (tid == 0) a.tokens[0] = i;
+        if (tid == 0) {
+            a.tokens[0] = i;
+            // every CTA has arrived at every barrier and read the counters:
+            // pad the arrivals to the next launch's base, count the launch,
+            // advance the slot's position (device-resident steps)
+            atomicAdd(a.bar, (D1_BAR_STRIDE - nbar) * (unsigned)G);
+            a.bar[1] = launches + 1;
+            if (a.slot_pos) a.slot_pos[0] = pos + 1;
+        }
     }
 }
 
@@ -1186,7 +1209,6 @@ int launch_decode1(const D1Args &a, cudaStream_t st) {
         d1_grid = sms;
         configured |= 1u << (dev & 31);
     }
-    if (cudaMemsetAsync(a.bar, 0, 4, st) != cudaSuccess) return -3;
     pdl_break();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d1_grid);

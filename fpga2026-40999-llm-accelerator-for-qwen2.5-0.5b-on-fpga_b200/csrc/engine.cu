@@ -294,6 +294,7 @@ int allocate(qwen_b200 *h) {
     if ((rc = dalloc(h, (void **)&h->meta, R * 4 * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->d1_layers, NL * sizeof(D1Layer)))) return rc;
     if ((rc = dalloc(h, (void **)&h->d1_bar, 256))) return rc;
+    CK(cudaMemset(h->d1_bar, 0, 256));  // the persistent launch's arrival and launch counters
     if ((rc = dalloc(h, (void **)&h->d1_cand_v, 1024 * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->d1_cand_i, 1024 * 4))) return rc;
     if ((rc = dalloc(h, (void **)&h->tokens, R * 4))) return rc;
@@ -389,6 +390,9 @@ int check_device_flags(qwen_b200 *h) {
     CK(cudaMemcpy(&flag, h->tc_ws, 4, cudaMemcpyDeviceToHost));
     if (flag) {
         cudaMemset(h->tc_ws, 0, 4);
+        // a persistent launch that gave up waiting may have left its barrier
+        // counters off their launch stride: start them again
+        if (h->d1_bar) cudaMemset(h->d1_bar, 0, 256);
         return fail(h, QWEN_B200_ETIMEOUT, "a pipeline wait on the device timed out (code %u)", flag);
     }
     return 0;
@@ -447,20 +451,27 @@ int prepare_tiles(qwen_b200 *h, int m, const uint32_t *slots, const uint32_t *po
 // stride n (ids n | slots n | positions n | logit rows n). nlog rows get the
 // LM head: rows listed at meta+3n, or all rows when identity. Without
 // lm_head the nlog rows are only gathered into h->xl (identity false).
+// Whether a forward of n rows (max_len keys at most) runs as the persistent
+// single-row launch.
+static bool uses_decode1(const qwen_b200 *h, int n, int max_len, int nlog, bool identity) {
+    const bool dump = h->dump_layer >= 0 && h->d_dump;
+    return n == 1 && nlog == 1 && identity && !dump && h->persistent && !h->rtl &&
+           decode1_supported(max_len, h->persistent == 1 ? QB_D1_AUTO_KEYS : QB_D1_MAX_KEYS);
+}
+
+// tok_in / slot_pos (device-resident single-row steps, uses_decode1 true):
+// the persistent launch reads the token and the position itself and advances
+// the position, in place of the step's prologue and epilogue kernels.
 int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint16_t *logits_dst, uint32_t *tokens_dst,
-                cudaStream_t st, bool lm_head = true) {
+                cudaStream_t st, bool lm_head = true, const uint32_t *tok_in = nullptr, uint32_t *slot_pos = nullptr) {
     const uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n, *lrows = h->meta + 3 * n;
     const int cap = (int)h->cfg.max_context;
     const float eps = h->cfg.rms_eps;
     const bool dump = h->dump_layer >= 0 && h->d_dump;
     PdlChain chain;  // consecutive kernels of the forward overlap one another
-    {
-        LaunchScope ls(h, 0, st, 1);
-        RK(launch_embed(h->embed, ids, n, h->x, st));
-    }
-    if (n == 1 && nlog == 1 && identity && !dump && h->persistent && !h->rtl &&
-        decode1_supported(max_len, h->persistent == 1 ? QB_D1_AUTO_KEYS : QB_D1_MAX_KEYS)) {
-        // one row: every layer, the LM head and the argmax in one persistent launch
+    if (lm_head && uses_decode1(h, n, max_len, nlog, identity)) {
+        // one row: the embedding, every layer, the LM head and the argmax in
+        // one persistent launch
         D1Args a;
         a.layers = h->d1_layers;
         a.lmw = h->lmw;
@@ -475,6 +486,9 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
         a.scales_per_layer = kv_layer_scales(h);
         a.cap = cap;
         a.meta = h->meta;
+        a.embed = h->embed;
+        a.tok_in = tok_in;
+        a.slot_pos = tok_in ? slot_pos : nullptr;
         a.x = h->x;
         a.qkv = h->qkvb;
         a.ctx = h->ctx;
@@ -490,6 +504,11 @@ int run_forward(qwen_b200 *h, int n, int max_len, int nlog, bool identity, uint1
         LaunchScope ls(h, 8, st, 1);
         RK(launch_decode1(a, st));
         return 0;
+    }
+    if (tok_in) return fail(h, QWEN_B200_EINVAL, "device-resident token input needs the persistent single-row launch");
+    {
+        LaunchScope ls(h, 0, st, 1);
+        RK(launch_embed(h->embed, ids, n, h->x, st));
     }
     for (int l = 0; l < NL; ++l) {
         const LayerW &W = h->L[l];
@@ -1062,6 +1081,8 @@ static int enqueue_device_step(qwen_b200 *h, const uint32_t *d_in, int n, int ma
                                cudaStream_t st) {
     uint32_t *ids = h->meta, *slots = h->meta + n, *positions = h->meta + 2 * n;
     h->nlaunch = 0;
+    if (uses_decode1(h, n, max_len, n, true))  // one launch reads the token and advances the position
+        return run_forward(h, n, max_len, n, true, nullptr, d_out, st, true, d_in, h->slot_pos);
     PdlChain chain;  // prologue, the layers and the epilogue overlap one another
     {
         LaunchScope ls(h, 7, st, 1);

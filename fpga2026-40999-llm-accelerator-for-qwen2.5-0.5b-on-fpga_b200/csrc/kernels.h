@@ -62,12 +62,15 @@ struct D1Args {
     size_t codes_per_layer, scales_per_layer;
     int cap;
     const uint32_t *meta;              // ids | slots | positions of the row (n = 1)
+    const uint16_t *embed;             // [151936][896]: layer 0 reads the token's row itself
+    const uint32_t *tok_in;            // nullable: a device-resident step, token tok_in[0] in slot 0 at
+    uint32_t *slot_pos;                // position slot_pos[0], which the launch advances (else meta)
     uint16_t *x, *qkv, *ctx, *mid;     // [896] residual, [1152], [896], [4864]
     uint16_t *logits;                  // nullable [151936]
     uint32_t *tokens;                  // [1]
     float *cand_v;                     // [grid] per-CTA best value
     uint32_t *cand_i;                  // [grid] per-CTA best index
-    unsigned *bar;                     // grid barrier counter (reset by the launch)
+    unsigned *bar;                     // [0] arrivals, [1] launches: monotonic, zeroed once
     unsigned *err;                     // error flag of the bounded waits
     float eps;
     // test switch (host-set): the last grid barrier waits for one arrival
