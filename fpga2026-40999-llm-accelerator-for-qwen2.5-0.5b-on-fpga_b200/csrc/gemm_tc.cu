@@ -51,6 +51,8 @@ constexpr int TC_NL = 4;             // activation limbs
 constexpr int TC_MN = TC_NL * TC_BN; // UMMA N
 constexpr int TC_CONV = 256;         // epilogue threads (warps 2..9)
 constexpr int TC_THREADS = 64 + TC_CONV;
+constexpr int TP_CONV = 512;         // epilogue threads of the persistent projections (warps 2..17)
+constexpr int TP_THREADS = 64 + TP_CONV;
 constexpr int TC_MAX_SPLITS = 8;
 constexpr int TC_SLOTS = 148;        // one CTA per SM
 
@@ -101,6 +103,12 @@ __device__ __forceinline__ void tmem_ld16i_nowait(uint32_t taddr, int (&v)[16]) 
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
+}
+// 8 columns of this warp's TMEM lane quarter; tmem_ld_wait() completes them
+__device__ __forceinline__ void tmem_ld8i_nowait(uint32_t taddr, int (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ float exact_acc(long long dot, int e) { return unalign28(dot, e); }
@@ -696,7 +704,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // consecutive channels; SiLU(gate) * up pairs the channels of neighbouring
 // lanes. Same arithmetic as tc_gemm_kernel (bit-identical outputs).
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TP_THREADS, 1)
     tc_persist_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap lmap, TcArgs a) {
     using L = LhSmem;
     constexpr int AS = L::A_STAGES, BS = L::B_STAGES;
@@ -725,7 +733,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
-            tc::mbar_init(&acc_empty[b], TC_CONV / 32);  // one arrival per epilogue warp
+            tc::mbar_init(&acc_empty[b], TP_CONV / 32);  // one arrival per epilogue warp
         }
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
@@ -831,7 +839,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
     } else {
         // lane quarter q: channels 32q..32q+31 of a tile (this thread: one
-        // channel), rows 32h..32h+31
+        // channel), rows 16h..16h+15 (16 epilogue warps: four per quarter)
         const int q = warp & 3, h = (warp - 2) >> 2;
         pdl_wait();  // row exponents and residual rows come from preceding kernels
         for (int j = 0; j < nt; ++j) {
@@ -843,54 +851,72 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = ok && tc::mbar_wait(&acc_full[buf], (j >> 1) & 1, a.err, 26);
             tc::tc_fence_after();
 #pragma unroll 1
-            for (int hh = 0; hh < 2; ++hh) {
-                const int r0 = m0 + 32 * h + 16 * hh;  // first of this pass's 16 rows
-                int d[TC_NL][16];
+            for (int sp = 0; sp < 2; ++sp) {
+                // rows r0 .. r0 + 7 of this warp's 16 (fewer live registers
+                // than one pass of 16 with 16 epilogue warps)
+                const int r0 = m0 + 16 * h + 8 * sp;
+                int d[TC_NL][8];
 #pragma unroll
                 for (int l = 0; l < TC_NL; ++l) {
                     if (ok) {
-                        tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) +
-                                              (uint32_t)(buf * TC_MN + l * TC_BN + 32 * h + 16 * hh),
-                                          d[l]);
+                        tmem_ld8i_nowait(tmem + ((uint32_t)(q * 32) << 16) +
+                                             (uint32_t)(buf * TC_MN + l * TC_BN + 16 * h + 8 * sp),
+                                         d[l]);
                     } else {
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) d[l][jj] = 0;
+                        for (int jj = 0; jj < 8; ++jj) d[l][jj] = 0;
                     }
                 }
-                // residual rows, requested before the TMEM data is used
-                float res[16];
+                // residual rows and row exponents, requested before the TMEM
+                // data is used
+                float res[8];
                 if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
+                    for (int jj = 0; jj < 8; ++jj)
                         res[jj] = r0 + jj < a.M ? bf2f(a.y[(size_t)(r0 + jj) * a.N + n]) : 0.f;
                 }
+                int exr[8];
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) exr[jj] = r0 + jj < a.M ? __ldg(a.ex + r0 + jj) : 0;
                 if (ok) tmem_ld_wait();
-                if (hh == 1) {
+                if (sp == 1) {
                     // this warp's TMEM reads are complete: the buffer may be refilled
                     tc::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
                 }
+                float o[8];
 #pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
-                    const int m = r0 + jj;
+                for (int jj = 0; jj < 8; ++jj) {
                     // K = 896: limb pairs fold in int32 as in tc_gemm_kernel
                     const long long v = KC <= 14 ? (long long)(d[0][jj] + d[1][jj] * 128) +
                                                        (long long)(d[2][jj] + d[3][jj] * 128) * 16384ll
                                                  : (long long)d[0][jj] + (long long)d[1][jj] * 128ll +
                                                        (long long)d[2][jj] * 16384ll + (long long)d[3][jj] * 2097152ll;
-                    const bool live = m < a.M;  // the same for every lane of the warp
-                    const float o = live ? rbf(rbf(exact_acc(v, __ldg(a.ex + m))) * scn) : 0.f;
-                    if constexpr (EPI == EPI_SWIGLU) {
-                        // channels 2i (gate i) and 2i+1 (up i): model_backend.py:105-106
-                        const float up = __shfl_xor_sync(0xffffffffu, o, 1);
-                        if (live && !(lane & 1))
-                            a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = f2bf(rbf(silu_q(o)) * up);
-                    } else if (live) {
-                        float w = o;
-                        if constexpr (EPI == EPI_BIAS) w = rbf(o + bn);
-                        if constexpr (EPI == EPI_RESIDUAL) w = rbf(res[jj] + o);
-                        a.y[(size_t)m * a.N + n] = f2bf(w);
+                    o[jj] = r0 + jj < a.M ? rbf(rbf(exact_acc(v, exr[jj])) * scn) : 0.f;
+                }
+                if constexpr (EPI == EPI_SWIGLU) {
+                    // channels 2i (gate i) and 2i+1 (up i), model_backend.py:105-106;
+                    // rows in pairs so that both lanes of a channel pair work: the
+                    // gate lane takes the first row, the up lane the second
+#pragma unroll
+                    for (int jj = 0; jj < 8; jj += 2) {
+                        const bool odd = lane & 1;
+                        const float other = __shfl_xor_sync(0xffffffffu, odd ? o[jj] : o[jj + 1], 1);
+                        const float gt = odd ? other : o[jj], up = odd ? o[jj + 1] : other;
+                        const int m = r0 + jj + (odd ? 1 : 0);
+                        if (m < a.M) a.y[(size_t)m * (a.N >> 1) + (n >> 1)] = f2bf(rbf(silu_q(gt)) * up);
+                    }
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int m = r0 + jj;
+                        if (m < a.M) {  // the same for every lane of the warp
+                            float w = o[jj];
+                            if constexpr (EPI == EPI_BIAS) w = rbf(o[jj] + bn);
+                            if constexpr (EPI == EPI_RESIDUAL) w = rbf(res[jj] + o[jj]);
+                            a.y[(size_t)m * a.N + n] = f2bf(w);
+                        }
                     }
                 }
             }
@@ -1042,7 +1068,7 @@ static int run_persist(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs 
         configured |= 1u << (dev & 31);
     }
     const int tiles = (a.N / TC_BM) * ((a.M + TC_BN - 1) / TC_BN);
-    return launch_pdl(tc_persist_kernel<EPI>, dim3(tiles < TC_SLOTS ? tiles : TC_SLOTS), dim3(TC_THREADS),
+    return launch_pdl(tc_persist_kernel<EPI>, dim3(tiles < TC_SLOTS ? tiles : TC_SLOTS), dim3(TP_THREADS),
                       (size_t)L::ALLOC, st, 1u, wmap, lmap, a);
 }
 
