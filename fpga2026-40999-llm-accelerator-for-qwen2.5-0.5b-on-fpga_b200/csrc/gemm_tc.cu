@@ -124,7 +124,7 @@ __device__ __forceinline__ float exact_acc(long long dot, int e) { return unalig
 template <int NR>
 __device__ __forceinline__ void tc_argmax_rows(const TcArgs &a, const float (&v)[NR], int n, int m0, int c0, int q,
                                                int lane, uint8_t *red) {
-    static_assert(NR == 16 || NR == 32, "rows per call");
+    static_assert(NR == 8 || NR == 16 || NR == 32, "rows per call");
     const float sc = a.scale[n];
     float *red_v = reinterpret_cast<float *>(red);
     uint32_t *red_i = reinterpret_cast<uint32_t *>(red + 4 * TC_BN * 4);
@@ -171,8 +171,9 @@ __device__ __forceinline__ void tc_argmax_rows(const TcArgs &a, const float (&v)
             }
         }
     }
-    // NR = 32: lane l holds row l; NR = 16: lanes 2r and 2r + 1 both hold row r
-    if (NR == 32 || (lane & 1) == 0) {
+    // NR = 32: lane l holds row l; NR = 16: lanes 2r and 2r + 1 both hold row
+    // r; NR = 8: lanes 4r .. 4r + 3
+    if ((lane & (32 / NR - 1)) == 0) {
         red_v[q * TC_BN + c0 + row] = bv[0];
         red_i[q * TC_BN + c0 + row] = bi[0];
     }
@@ -491,19 +492,20 @@ struct LhSmem {
     static_assert(ALLOC <= 227 * 1024, "shared memory of one CTA");
 };
 
-// Barrier 1 over the 256 epilogue threads, returning the AND of v over them
+// Barrier 1 over the N epilogue threads, returning the AND of v over them
 // (every epilogue thread leaves a tile loop at the same iteration).
+template <int N>
 __device__ __forceinline__ bool epi_bar_and(bool v) {
     uint32_t r;
     asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
-        : "r"((uint32_t)v)
+        : "r"((uint32_t)v), "n"(N)
         : "memory");
     return r != 0;
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TP_THREADS, 1)
     tc_lmhead_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap lmap, TcArgs a) {
     using L = LhSmem;
     constexpr int AS = L::A_STAGES, BS = L::B_STAGES;
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
-            tc::mbar_init(&acc_empty[b], TC_CONV / 32);  // one arrival per epilogue warp
+            tc::mbar_init(&acc_empty[b], TP_CONV / 32);  // one arrival per epilogue warp
         }
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
@@ -637,7 +639,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         __syncwarp();
     } else {
-        // lane quarter q (channels 32q..32q+31 of a tile), rows 32h..32h+31
+        // lane quarter q (channels 32q..32q+31 of a tile), rows 16h..16h+15
+        // (16 epilogue warps: four per quarter), in two sub-passes of 8 rows
         const int q = warp & 3, h = (warp - 2) >> 2, ct = threadIdx.x - 64;
         pdl_wait();  // row exponents come from the preceding kernel
         for (int j = 0; j < nt; ++j) {
@@ -648,40 +651,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc::tc_fence_after();
             uint8_t *red = smem + L::RED_OFF + buf * L::RED_BYTES;
 #pragma unroll 1
-            for (int hh = 0; hh < 2; ++hh) {
-                float f[16];
-                int d[TC_NL][16];
+            for (int sp = 0; sp < 2; ++sp) {
+                const int c0 = 16 * h + 8 * sp;  // first of this sub-pass's 8 rows in the tile
+                float f[8];
+                int d[TC_NL][8];
 #pragma unroll
                 for (int l = 0; l < TC_NL; ++l) {
                     if (ok) {
-                        tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) +
-                                              (uint32_t)(buf * TC_MN + l * TC_BN + 32 * h + 16 * hh),
-                                          d[l]);
+                        tmem_ld8i_nowait(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TC_MN + l * TC_BN + c0),
+                                         d[l]);
                     } else {
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) d[l][jj] = 0;
+                        for (int jj = 0; jj < 8; ++jj) d[l][jj] = 0;
                     }
                 }
+                int exr[8];
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) exr[jj] = m0 + c0 + jj < a.M ? __ldg(a.ex + m0 + c0 + jj) : 0;
                 if (ok) tmem_ld_wait();
 #pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
+                for (int jj = 0; jj < 8; ++jj) {
                     // K = 896: limb pairs fold in int32 as in tc_gemm_kernel
                     const long long v = KC <= 14 ? (long long)(d[0][jj] + d[1][jj] * 128) +
                                                        (long long)(d[2][jj] + d[3][jj] * 128) * 16384ll
                                                  : (long long)d[0][jj] + (long long)d[1][jj] * 128ll +
                                                        (long long)d[2][jj] * 16384ll + (long long)d[3][jj] * 2097152ll;
-                    const int r = 32 * h + 16 * hh + jj;
-                    f[jj] = m0 + r < a.M ? exact_acc(v, a.ex[m0 + r]) : 0.f;
+                    f[jj] = m0 + c0 + jj < a.M ? exact_acc(v, exr[jj]) : 0.f;
                 }
-                if (hh == 1) {
+                if (sp == 1) {
                     // this warp's TMEM reads are complete: the buffer may be refilled
                     tc::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&acc_empty[buf]);
                 }
-                tc_argmax_rows<16>(a, f, n0 + q * 32 + lane, m0, 32 * h + 16 * hh, q, lane, red);
+                tc_argmax_rows<8>(a, f, n0 + q * 32 + lane, m0, c0, q, lane, red);
             }
-            if (!epi_bar_and(ok)) break;
+            if (!epi_bar_and<TP_CONV>(ok)) break;
             tc_argmax_flush(a, red, m0, n_tile, ct);
         }
     }
@@ -1051,7 +1056,7 @@ static int run_lmhead(const CUtensorMap &wmap, const CUtensorMap &lmap, TcArgs &
         configured |= 1u << (dev & 31);
     }
     const int tiles = (a.N / TC_BM) * ((a.M + TC_BN - 1) / TC_BN);
-    return launch_pdl(tc_lmhead_kernel, dim3(tiles < TC_SLOTS ? tiles : TC_SLOTS), dim3(TC_THREADS), (size_t)L::ALLOC,
+    return launch_pdl(tc_lmhead_kernel, dim3(tiles < TC_SLOTS ? tiles : TC_SLOTS), dim3(TP_THREADS), (size_t)L::ALLOC,
                       st, 1u, wmap, lmap, a);
 }
 
