@@ -49,9 +49,9 @@ constexpr int TC_BN = 64;            // batch rows per tile
 constexpr int TC_BK = 128;           // k per stage (bytes of int8)
 constexpr int TC_NL = 4;             // activation limbs
 constexpr int TC_MN = TC_NL * TC_BN; // UMMA N
-constexpr int TC_CONV = 256;         // epilogue threads (warps 2..9)
+constexpr int TC_CONV = 512;         // epilogue threads (warps 2..17): four warps per TMEM lane quarter
 constexpr int TC_THREADS = 64 + TC_CONV;
-constexpr int TP_CONV = 512;         // epilogue threads of the persistent projections (warps 2..17)
+constexpr int TP_CONV = TC_CONV;     // the persistent kernels' epilogue threads
 constexpr int TP_THREADS = 64 + TP_CONV;
 constexpr int TC_MAX_SPLITS = 8;
 constexpr int TC_SLOTS = 148;        // one CTA per SM
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         __syncwarp();
     } else {
-        // this warp: TMEM lane quarter q (channels 32q..32q+31), rows 32h..32h+31
+        // this warp: TMEM lane quarter q (channels 32q..32q+31), rows 16h..16h+15
         const int q = warp & 3, h = (warp - 2) >> 2, ct = threadIdx.x - 64;
         // per-channel scales and biases are constants: staged before the wait
         float *scs = reinterpret_cast<float *>(smem + L::SC_OFF);
@@ -391,15 +391,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // the limbs of 16 rows at a time fold into int64 (keeps the fold in registers)
         long long *tile = reinterpret_cast<long long *>(smem + L::A_OFF);
         long long *pt = a.part + ((size_t)(m_tile * (a.N / TC_BM) + n_tile) * a.splits + split) * (TC_BN * TC_BM);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        {
             long long v[16];
             int d[TC_NL][16];
             // the four limb column groups in flight together, one wait
 #pragma unroll
             for (int l = 0; l < TC_NL; ++l) {
                 if (ok) {
-                    tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(l * TC_BN + 32 * h + 16 * hh), d[l]);
+                    tmem_ld16i_nowait(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(l * TC_BN + 16 * h), d[l]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) d[l][j] = 0;
@@ -422,7 +421,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const int r = 32 * h + 16 * hh + j;
+                const int r = 16 * h + j;
                 if (a.splits > 1)
                     pt[r * TC_BM + q * 32 + lane] = v[j];  // 256 contiguous bytes per warp and row
                 else
