@@ -391,7 +391,8 @@ def run_ours(args):
 
 def prefill_sharded(args, rank, world, local):
     """Prefill of args.prefill_prompts prompts of args.prefill_len seeded random
-    ids through all 24 layers (tensor-core projections in 4096-row chunks),
+    ids through all 24 layers (tensor-core projections; the rows of all of a
+    GPU's prompts go through the layers together, --prefill-chunk at a time),
     request-sharded (prompts / N per GPU), then the LM head split by
     vocabulary over the GPUs: an NCCL all-gather of every prompt's last hidden
     row, each GPU's (value, index) per row over its vocabulary range, an NCCL
@@ -407,7 +408,8 @@ def prefill_sharded(args, rank, world, local):
     mine = list(D.shard_requests(P, world, rank))
     rng = np.random.default_rng(SEED + 99)
     prompts = [rng.integers(0, VOCAB, T).astype(np.uint32) for _ in range(P)]  # the same on every rank
-    eng = qwen_b200.Engine(device=local, max_seqs=P, max_context=T + 8, max_rows=4096).load_synthetic(SEED)
+    eng = qwen_b200.Engine(device=local, max_seqs=P, max_context=T + 8,
+                           max_rows=args.prefill_chunk).load_synthetic(SEED)
     vb, ve = D.vocab_shard(VOCAB, world, rank)
     # bf16 bit patterns, gathered as bfloat16 (NCCL has no 16-bit integer type)
     hid_local = torch.empty((len(mine), HID), dtype=torch.bfloat16, device='cuda')
@@ -808,6 +810,8 @@ def main():
     ap.add_argument('--prefill-prompts', type=int, default=8)
     ap.add_argument('--prefill-len', type=int, default=4096)
     ap.add_argument('--prefill-reps', type=int, default=2)
+    ap.add_argument('--prefill-chunk', type=int, default=32768,
+                    help='rows that go through the layers together (the engine\'s max_rows)')
     ap.add_argument('--prefill-only', action='store_true',
                     help='run only the prefill record (prints its own JSON object)')
     ap.add_argument('--micro', action='store_true',
