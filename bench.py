@@ -617,11 +617,12 @@ def micro_timer(torch, stream, reps):
 
 
 def micro_gemm(torch, L, stream, sp, timed, hbm):
-    """W8A16 projections through the C ABI: rows <= 8 on the GEMV family
-    (qwen_b200_op_gemm_w8a16 / _residual, op_swiglu, op_lm_head_argmax), more
-    rows on the tcgen05 GEMM (qwen_b200_op_gemm_w8a16_tc, which also builds the
-    activation limb planes; the LM head shape writes its bf16 logits). Weights
-    int8 per-output-channel from N(0, 0.02), activations bf16 N(0, 1)."""
+    """W8A16 projections through the C ABI, on the kernel family the engine
+    runs at that row count: one row on the GEMV family (qwen_b200_op_gemm_w8a16
+    / _residual, op_swiglu, op_lm_head_argmax), two rows and more on the
+    tcgen05 GEMM (qwen_b200_op_gemm_w8a16_tc, which also builds the activation
+    limb planes; the LM head shape writes its bf16 logits). Weights int8
+    per-output-channel from N(0, 0.02), activations bf16 N(0, 1)."""
     g = torch.Generator(device='cuda').manual_seed(SEED)
     out = []
     for name, K, N, epi in GEMM_SHAPES:
@@ -636,7 +637,7 @@ def micro_gemm(torch, L, stream, sp, timed, hbm):
             n_out = N // 2 if epi == 'swiglu' else N
             y = torch.zeros(M, n_out, device='cuda', dtype=torch.bfloat16)
             ws = None
-            if M <= 8:
+            if M == 1:
                 if epi == 'argmax':
                     wsb = L.qwen_b200_lm_head_workspace(M, N)
                     ws = torch.zeros(wsb, dtype=torch.uint8, device='cuda')
@@ -666,15 +667,15 @@ def micro_gemm(torch, L, stream, sp, timed, hbm):
                                                           ws.data_ptr(), wsb, sp)
                 kernel = 'act_quant_kernel + tc_gemm_kernel'
             us = timed(fn)
-            if M > 8:
+            if M > 1:
                 assert int(ws[:4].view(torch.int32)[0].item()) == 0, 'pipeline wait expired'
-            out_bytes = (0 if epi == 'argmax' and M <= 8 else M * n_out * 2) * (2 if epi == 'residual' else 1)
+            out_bytes = (0 if epi == 'argmax' and M == 1 else M * n_out * 2) * (2 if epi == 'residual' else 1)
             nbytes = N * K + 4 * N + (2 * N if epi == 'bias' else 0) + M * K * 2 + out_bytes
             flops = 2.0 * M * N * K
             rec = {'shape': f'{K}x{N}', 'name': name, 'rows': M, 'kernel': kernel, 'us': round(us, 2),
                    'bytes': nbytes, 'gbs': round(nbytes / us / 1e3, 1), 'hbm_frac': round(nbytes / us / 1e3 / hbm, 4),
                    'tops': round(flops / us / 1e6, 2)}
-            if M > 8:
+            if M > 1:
                 # exact mode: four int8 limb planes, i.e. 4 x 2MNK tensor ops executed
                 rec['int8_tensor_frac_nominal'] = round(4 * flops / (us * 1e-6) / INT8_DENSE_NOMINAL, 4)
             out.append(rec)

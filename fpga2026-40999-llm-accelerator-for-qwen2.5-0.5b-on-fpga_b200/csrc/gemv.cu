@@ -11,6 +11,8 @@
 // dp4a multiplies four codes by four limb bytes at a time, the limb sums fold
 // in int64 and the lanes' partial sums are added exactly, so the result does
 // not depend on how the sum is split.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "qkv_epi.cuh"
@@ -270,53 +272,67 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const uint16_t *__restrict
     const int m0 = blockIdx.y * MT;
     const int mrows = min(MT, rows - m0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = (blockIdx.x * NW + warp) * RW;
+    // the CTA walks 32-row blocks blockIdx.x, + gridDim.x, ...: the tile rows'
+    // RMSNorm and limb planes once, the next block's weight rows in flight
+    // while the current one is reduced
+    int blk = blockIdx.x;
     GemvRows<K, RW> g;
-    gemv_load<K, RW>(w, n0, n0 < vocab, g);
+    {
+        const int n0 = (blk * NW + warp) * RW;
+        gemv_load<K, RW>(w, n0, n0 < vocab, g);
+    }
     pdl_wait();
     pdl_trigger();
     load_x_limbs<K, MT, NW * 32>(x, m0, mrows, gamma, eps, xl, ex);
-    float best_v[MT];
-    uint32_t best_i[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        best_v[m] = -INFINITY;
-        best_i[m] = 0;
-    }
-    if (n0 < vocab) {
-        float acc[RW][MT];
-        gemv_dot<K, RW, MT>(g, xl, ex, acc);
-#pragma unroll
-        for (int r = 0; r < RW; ++r)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const float v = rbf(rbf(acc[r][m]) * scale[n0 + r]);
-                if (better(v, (uint32_t)(n_base + n0 + r), best_v[m], best_i[m])) {
-                    best_v[m] = v;
-                    best_i[m] = (uint32_t)(n_base + n0 + r);
-                }
-                if (logits && ((r * MT + m) & 31) == lane && m < mrows)
-                    logits[(size_t)(m0 + m) * vocab + n0 + r] = f2bf(v);
-            }
-    }
-    if (lane == 0)
+    for (; blk < nblk; blk += gridDim.x) {
+        const int n0 = (blk * NW + warp) * RW;
+        GemvRows<K, RW> gn;
+        const int nb = blk + (int)gridDim.x, n1 = (nb * NW + warp) * RW;
+        if (nb < nblk) gemv_load<K, RW>(w, n1, n1 < vocab, gn);
+        float best_v[MT];
+        uint32_t best_i[MT];
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-            bv[warp][m] = best_v[m];
-            bi[warp][m] = best_i[m];
+            best_v[m] = -INFINITY;
+            best_i[m] = 0;
         }
-    __syncthreads();
-    if (threadIdx.x < mrows) {
-        const int m = threadIdx.x;
-        float v = bv[0][m];
-        uint32_t i = bi[0][m];
-        for (int k = 1; k < NW; ++k)
-            if (better(bv[k][m], bi[k][m], v, i)) {
-                v = bv[k][m];
-                i = bi[k][m];
+        if (n0 < vocab) {
+            float acc[RW][MT];
+            gemv_dot<K, RW, MT>(g, xl, ex, acc);
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    const float v = rbf(rbf(acc[r][m]) * scale[n0 + r]);
+                    if (better(v, (uint32_t)(n_base + n0 + r), best_v[m], best_i[m])) {
+                        best_v[m] = v;
+                        best_i[m] = (uint32_t)(n_base + n0 + r);
+                    }
+                    if (logits && ((r * MT + m) & 31) == lane && m < mrows)
+                        logits[(size_t)(m0 + m) * vocab + n0 + r] = f2bf(v);
+                }
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                bv[warp][m] = best_v[m];
+                bi[warp][m] = best_i[m];
             }
-        pv[(size_t)(m0 + m) * nblk + blockIdx.x] = v;
-        pi[(size_t)(m0 + m) * nblk + blockIdx.x] = i;
+        __syncthreads();
+        if (threadIdx.x < mrows) {
+            const int m = threadIdx.x;
+            float v = bv[0][m];
+            uint32_t i = bi[0][m];
+            for (int k = 1; k < NW; ++k)
+                if (better(bv[k][m], bi[k][m], v, i)) {
+                    v = bv[k][m];
+                    i = bi[k][m];
+                }
+            pv[(size_t)(m0 + m) * nblk + blk] = v;
+            pi[(size_t)(m0 + m) * nblk + blk] = i;
+        }
+        __syncthreads();  // bv / bi are written again by the next block
+        if (nb < nblk) g = gn;
     }
 }
 
@@ -367,7 +383,20 @@ template <int MT>
 static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w, const float *scale,
                   int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, int n_base, cudaStream_t st) {
     const size_t smem = (size_t)MT * (4 * QB_HID + 4);
-    dim3 grid(nblk, (rows + MT - 1) / MT);
+    // as many CTAs per row tile as fit on the GPU at once (each then walks
+    // several 32-row blocks): one RMSNorm per CTA instead of one per block
+    static int resident = 0;
+    if (!resident) {
+        int dev = 0, sms = 0, per_sm = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lm_head_kernel<MT>, 256, smem) != cudaSuccess ||
+            per_sm < 1)
+            return -3;
+        resident = sms * per_sm;
+    }
+    const int tiles = (rows + MT - 1) / MT;
+    const int per_tile = std::max(1, std::min(nblk, resident / tiles));
+    dim3 grid(per_tile, tiles);
     return launch_pdl(lm_head_kernel<MT>, grid, dim3(256), smem, st, 1, x, rows, gamma, eps, w, scale, vocab, logits,
                       pv, pi, nblk, n_base);
 }
