@@ -49,7 +49,7 @@ KERNEL_NAMES_GEMV = {'qkv_rope_kv8': 'qkv_kernel', 'attention': 'attn_rs_kernel'
                      'o_proj_residual': 'gemv_kernel<896,EPI_RESIDUAL>',
                      'gate_up_swiglu': 'gemv_kernel<896,EPI_SWIGLU>',
                      'down_residual': 'gemv_kernel<4864,EPI_RESIDUAL>',
-                     'lm_head_argmax': 'lm_head_kernel + argmax_reduce_kernel',
+                     'lm_head_argmax': 'lm_head1_kernel + argmax_reduce_kernel',
                      'embedding': 'embed_kernel', 'bookkeeping': 'decode_prologue/epilogue_kernel',
                      'persistent_decode': 'decode1_kernel'}
 KERNEL_NAMES_TC = dict(KERNEL_NAMES_GEMV,
@@ -645,7 +645,7 @@ def micro_gemm(torch, L, stream, sp, timed, hbm):
                     fn = lambda: L.qwen_b200_op_lm_head_argmax(x.data_ptr(), M, None, 1e-6, w.data_ptr(),
                                                                scale.data_ptr(), N, None, tok.data_ptr(),
                                                                ws.data_ptr(), wsb, sp)
-                    kernel = 'lm_head_kernel + argmax_reduce_kernel'
+                    kernel = 'lm_head1_kernel + argmax_reduce_kernel'
                 elif epi == 'swiglu':
                     fn = lambda: L.qwen_b200_op_swiglu(x.data_ptr(), M, None, 1e-6, w.data_ptr(), scale.data_ptr(),
                                                        y.data_ptr(), sp)

@@ -423,7 +423,8 @@ int lm_head_rows(qwen_b200 *h, const uint16_t *xin, int nlog, int begin, int end
     } else {
         LaunchScope ls(h, 6, st, 2);
         RK(launch_lm_head(xin, nlog, h->g_final, eps, h->lmw + (size_t)begin * HID, h->s_lm + begin, width,
-                          logits_dst, tokens_dst, h->lm_ws, h->lm_ws_bytes, st, begin, values_dst));
+                          logits_dst, tokens_dst, h->lm_ws, h->lm_ws_bytes, st, begin, values_dst,
+                          reinterpret_cast<unsigned *>(h->tc_ws)));
     }
     return 0;
 }

@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "qkv_epi.cuh"
+#include "tc05.cuh"
 #include "xlimbs.cuh"
 
 namespace qb {
@@ -379,6 +380,170 @@ size_t lm_head_workspace(int rows, int vocab) {
     return (size_t)rows * nblk * 8 + 256;
 }
 
+// One activation row: the LM head as one CTA per SM, each streaming its share
+// of the vocabulary rows through a shared-memory ring of 32-row pieces (with
+// their scales) filled by bulk copies from a producer warp, the row's RMSNorm
+// and limb planes formed once per CTA. Warps 2 (p % 4) and 2 (p % 4) + 1 take
+// the two 16-row halves of piece p on m16n8k32 int8 MMAs (weight rows as A,
+// the four limb planes as the N columns; every per-limb sum exact in int32).
+// The CTA's best (value, index) goes to pv / pi[blockIdx.x] for
+// argmax_reduce. Every mbarrier wait is bounded (codes 48, 49 in *err).
+constexpr int L1_ROWS = 32, L1_SLOTS = 6, L1_CW = 8, L1_THREADS = 32 * (L1_CW + 1);
+constexpr int L1_WBYTES = L1_ROWS * QB_HID;     // weight rows of a piece
+constexpr int L1_SLOT = L1_WBYTES + 160;        // + the piece's scales (16-byte aligned superset)
+constexpr int L1_XL = L1_SLOTS * L1_SLOT;       // limb planes [4][896]
+constexpr int L1_EX = L1_XL + 4 * QB_HID;       // row exponent (16 bytes)
+constexpr int L1_BARS = L1_EX + 16;             // full [SLOTS], empty [SLOTS]
+constexpr int L1_RED = L1_BARS + 2 * L1_SLOTS * 8;  // best value [8], index [8]
+constexpr int L1_SMEM = L1_RED + L1_CW * 8;
+static_assert(L1_SLOT % 16 == 0 && L1_XL % 16 == 0 && L1_BARS % 8 == 0, "aligned shared-memory areas");
+
+// m16n8k32 int8 MMA (s8 x s8 -> s32), accumulating into d
+__device__ __forceinline__ void l1_mma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// 16 weight rows [m0, m0 + 16) of a piece (rows >= nr read as 0) against the
+// four limb planes (N columns 0..3), K = 896: thread (gid, tig) loads 16 bytes
+// of rows gid and gid + 8 at k = 64 kb + 16 tig and the limb words at the same
+// k; c = the accumulator fragment (rows gid | gid + 8, limbs 2 tig, 2 tig + 1).
+__device__ __forceinline__ void l1_tile(const int8_t *w, int nr, int m0, const int8_t *xl, int (&c)[4]) {
+    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int ra = m0 + gid, rb = ra + 8;
+    const int8_t *pa = w + ra * QB_HID + 16 * tig, *pb = w + rb * QB_HID + 16 * tig;
+    const int8_t *px = xl + (gid & 3) * QB_HID + 16 * tig;
+    c[0] = c[1] = c[2] = c[3] = 0;
+#pragma unroll 2
+    for (int kb = 0; kb < QB_HID / 64; ++kb) {
+        const uint4 u = ra < nr ? *reinterpret_cast<const uint4 *>(pa + 64 * kb) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 v = rb < nr ? *reinterpret_cast<const uint4 *>(pb + 64 * kb) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 x = gid < 4 ? *reinterpret_cast<const uint4 *>(px + 64 * kb) : make_uint4(0u, 0u, 0u, 0u);
+        l1_mma(c, u.x, v.x, u.y, v.y, x.x, x.y);
+        l1_mma(c, u.z, v.z, u.w, v.w, x.z, x.w);
+    }
+}
+__device__ __forceinline__ void l1_sync() { asm volatile("bar.sync 1, %0;" ::"n"(L1_CW * 32) : "memory"); }
+
+__global__ void __launch_bounds__(L1_THREADS, 1)
+    lm_head1_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ gamma, float eps,
+                    const int8_t *__restrict__ w, const float *__restrict__ scale, int vocab, uint16_t *logits,
+                    float *pv, uint32_t *pi, int n_base, unsigned *err) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    int8_t *xl = reinterpret_cast<int8_t *>(sm + L1_XL);
+    int *ex = reinterpret_cast<int *>(sm + L1_EX);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + L1_BARS), *empty = full + L1_SLOTS;
+    float *bv = reinterpret_cast<float *>(sm + L1_RED);
+    uint32_t *bi = reinterpret_cast<uint32_t *>(sm + L1_RED + L1_CW * 4);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = (int)((long long)vocab * blockIdx.x / gridDim.x);
+    const int e = (int)((long long)vocab * (blockIdx.x + 1) / gridDim.x);
+    const int np = (e - b + L1_ROWS - 1) / L1_ROWS;
+    if (tid == 0) {
+        for (int s = 0; s < L1_SLOTS; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], L1_CW);
+        }
+        tc::mbar_fence_init();
+    }
+    __syncthreads();
+    if (warp == L1_CW) {
+        // producer: the weights are constant, so they stream before the wait
+        // for the kernel that writes x
+        if (lane == 0)
+            for (int p = 0; p < np; ++p) {
+                const int s = p % L1_SLOTS;
+                if (p >= L1_SLOTS && !tc::mbar_wait(&empty[s], (uint32_t)((p / L1_SLOTS) - 1) & 1u, err, 48)) break;
+                const int r0 = b + p * L1_ROWS, nr = min(L1_ROWS, e - r0);
+                const uintptr_t sa = reinterpret_cast<uintptr_t>(scale + r0), sal = sa & ~(uintptr_t)15,
+                                send = (sa + 4 * (uintptr_t)nr + 15) & ~(uintptr_t)15;
+                tc::mbar_arrive_expect_tx(&full[s], (uint32_t)(nr * QB_HID) + (uint32_t)(send - sal));
+                tc::bulk_load(sm + s * L1_SLOT, w + (size_t)r0 * QB_HID, (uint32_t)(nr * QB_HID), &full[s]);
+                tc::bulk_load(sm + s * L1_SLOT + L1_WBYTES, reinterpret_cast<const void *>(sal),
+                              (uint32_t)(send - sal), &full[s]);
+            }
+        return;
+    }
+    pdl_wait();
+    pdl_trigger();
+    // (no CTA-wide barrier: the producer warp never joins one)
+    load_x_limbs<QB_HID, 1, L1_CW * 32, false, false>(x, 0, 1, gamma, eps, xl, ex);
+    l1_sync();
+    const int e0 = ex[0];
+    const int gid = lane >> 2, tig = lane & 3;
+    float best = -INFINITY;
+    uint32_t bidx = 0;
+    bool ok = true;
+    // piece p: warps 2 (p % 4) and 2 (p % 4) + 1 (one 16-row m-tile each);
+    // every warp waits for every piece and releases it
+    for (int p = 0; p < np; ++p) {
+        const int s = p % L1_SLOTS;
+        if (ok) ok = tc::mbar_wait(&full[s], (uint32_t)(p / L1_SLOTS) & 1u, err, 49);
+        if ((p & 3) == (warp >> 1)) {
+            const int r0 = b + p * L1_ROWS, nr = min(L1_ROWS, e - r0), m0 = 16 * (warp & 1);
+            const int8_t *wp = reinterpret_cast<const int8_t *>(sm + s * L1_SLOT);
+            const float *sp = reinterpret_cast<const float *>(sm + s * L1_SLOT + L1_WBYTES +
+                                                              (reinterpret_cast<uintptr_t>(scale + r0) & 15));
+            int cf[4];
+            l1_tile(wp, nr, m0, xl, cf);
+            // exact sums of rows m0 + gid and m0 + gid + 8 on the tig == 0 lanes
+            // (limbs 2 and 3 from the tig == 1 lane)
+            const int c0 = __shfl_down_sync(0xffffffffu, cf[0], 1), c1 = __shfl_down_sync(0xffffffffu, cf[1], 1);
+            const int c2 = __shfl_down_sync(0xffffffffu, cf[2], 1), c3 = __shfl_down_sync(0xffffffffu, cf[3], 1);
+            if (tig == 0) {
+                const long long sum[2] = {
+                    (long long)cf[0] + (long long)cf[1] * 128ll + (long long)c0 * 16384ll + (long long)c1 * 2097152ll,
+                    (long long)cf[2] + (long long)cf[3] * 128ll + (long long)c2 * 16384ll + (long long)c3 * 2097152ll};
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int rr = m0 + gid + 8 * half;
+                    if (rr < nr) {
+                        const int row = r0 + rr;
+                        const float val = rbf(rbf(unalign28(sum[half], e0)) * sp[rr]);
+                        if (logits) logits[row] = f2bf(val);
+                        if (better(val, (uint32_t)(n_base + row), best, bidx)) {
+                            best = val;
+                            bidx = (uint32_t)(n_base + row);
+                        }
+                    }
+                }
+            }
+        }
+        // this warp is done with the piece's shared memory
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[s]);
+    }
+    // best of the warp (the tig == 0 lanes hold candidates)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (better(ov, oi, best, bidx)) {
+            best = ov;
+            bidx = oi;
+        }
+    }
+    if (lane == 0) {
+        bv[warp] = best;
+        bi[warp] = bidx;
+    }
+    l1_sync();
+    if (tid == 0) {
+        float v = bv[0];
+        uint32_t i = bi[0];
+        for (int k = 1; k < L1_CW; ++k)
+            if (better(bv[k], bi[k], v, i)) {
+                v = bv[k];
+                i = bi[k];
+            }
+        pv[blockIdx.x] = v;
+        pi[blockIdx.x] = i;
+    }
+}
+
 template <int MT>
 static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w, const float *scale,
                   int vocab, uint16_t *logits, float *pv, uint32_t *pi, int nblk, int n_base, cudaStream_t st) {
@@ -403,13 +568,32 @@ static int run_lm(const uint16_t *x, int rows, const uint16_t *gamma, float eps,
 
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
                    const float *scale, int vocab, uint16_t *logits, uint32_t *tokens, void *ws, size_t ws_bytes,
-                   cudaStream_t st, int n_base, float *values) {
+                   cudaStream_t st, int n_base, float *values, unsigned *err) {
     if (rows <= 0 || vocab <= 0 || vocab % 4) return -1;
     if (ws_bytes < lm_head_workspace(rows, vocab)) return -1;
     const int nblk = (vocab + 31) / 32;
     float *pv = reinterpret_cast<float *>(ws);
     uint32_t *pi = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(ws) + (size_t)rows * nblk * 4);
     int rc;
+    if (rows == 1 && ((reinterpret_cast<uintptr_t>(w) & 15) == 0)) {
+        static int sms = 0;
+        if (!sms) {
+            int dev = 0;
+            if (cudaGetDevice(&dev) != cudaSuccess ||
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                cudaFuncSetAttribute(lm_head1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L1_SMEM) !=
+                    cudaSuccess)
+                return -3;
+        }
+        // one CTA per SM, at least 32 rows each; bounded-wait codes go to err,
+        // else to the word after pv / pi in the workspace
+        const int grid = std::max(1, std::min(sms, (vocab + L1_ROWS - 1) / L1_ROWS));
+        unsigned *flag = err ? err : reinterpret_cast<unsigned *>(reinterpret_cast<char *>(ws) + (size_t)rows * nblk * 8);
+        rc = launch_pdl(lm_head1_kernel, dim3(grid), dim3(L1_THREADS), (size_t)L1_SMEM, st, 1, x, gamma, eps, w, scale,
+                        vocab, logits, pv, pi, n_base, flag);
+        if (rc) return rc;
+        return launch_pdl(argmax_reduce_kernel, dim3(1), dim3(256), 0, st, 1, pv, pi, grid, tokens, values);
+    }
     if (rows <= 1)
         rc = run_lm<1>(x, rows, gamma, eps, w, scale, vocab, logits, pv, pi, nblk, n_base, st);
     else if (rows <= 2)

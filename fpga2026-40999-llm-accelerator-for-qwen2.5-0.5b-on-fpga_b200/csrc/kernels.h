@@ -90,7 +90,7 @@ size_t lm_head_workspace(int rows, int vocab);
 // receives each row's best logit.
 int launch_lm_head(const uint16_t *x, int rows, const uint16_t *gamma, float eps, const int8_t *w,
                    const float *scale, int vocab, uint16_t *logits, uint32_t *tokens, void *ws, size_t ws_bytes,
-                   cudaStream_t st, int n_base = 0, float *values = nullptr);
+                   cudaStream_t st, int n_base = 0, float *values = nullptr, unsigned *err = nullptr);
 
 // Attention over a KV8 cache (two passes + last-block combine). The
 // workspace is laid out for ws_rows rows (>= rows); its completion counters

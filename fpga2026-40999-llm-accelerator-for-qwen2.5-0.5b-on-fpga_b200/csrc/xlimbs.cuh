@@ -28,7 +28,10 @@ __device__ __forceinline__ uint4 ld_act(const uint4 *p) {
 // every warp forms the same sum and maximum) and converts its share of the
 // words; wider rows are split across the warps, the maximum meeting in
 // shared memory.
-template <int K, int MT, int NT, bool CG = false>
+// SYNC false: no CTA-wide barrier at the end (only for K = 896, whose path has
+// none inside; for CTAs whose other warps never join one), the caller then
+// synchronises the NT threads itself.
+template <int K, int MT, int NT, bool CG = false, bool SYNC = true>
 __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int m0, int mrows,
                                              const uint16_t *__restrict__ gamma, float eps, int8_t *xl, int *ex) {
     constexpr int NWARP = NT / 32;
@@ -143,7 +146,8 @@ __device__ __forceinline__ void load_x_limbs(const uint16_t *__restrict__ x, int
             if (threadIdx.x == 0) ex[m] = e;
         }
     }
-    __syncthreads();
+    static_assert(SYNC || K == QB_HID, "only the 896-wide path has no barrier inside");
+    if constexpr (SYNC) __syncthreads();
 }
 
 }  // namespace qb
