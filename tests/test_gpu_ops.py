@@ -326,3 +326,27 @@ def test_lm_head_argmax_with_planted_ties(rows):
     got_toks = host(toks_d).view(np.uint32).tolist()
     assert got_toks[0] == 8000  # the highest of the tied indices
     assert got_toks == exp_toks
+
+
+@pytest.mark.parametrize('vocab', [4, 100, 1000, 4740, 20004])
+def test_one_row_lm_head_at_ragged_vocabulary_sizes(vocab):
+    """The one-row LM head splits the vocabulary over one CTA per SM (fewer
+    for small vocabularies) in 32-row pieces: sizes whose CTA shares end in
+    partial pieces, and shares of a few rows, still give the oracle's logits
+    and highest-index argmax bit for bit."""
+    keep = Keep()
+    r = rng(70 + vocab)
+    x = rand_bf16(r, (1, 896), 2.0)
+    g = bf16_round(r.uniform(0.5, 1.5, 896).astype(np.float32))
+    w, s = rand_weights(r, vocab, 896)
+    logits_d = dev(np.zeros((1, vocab), np.int16))
+    toks_d = dev(np.zeros(1, np.int32))
+    ws_bytes = L().qwen_b200_lm_head_workspace(1, vocab)
+    ws = dev(np.zeros(ws_bytes, np.uint8))
+    assert L().qwen_b200_op_lm_head_argmax(keep((to_bits(x).view(np.int16))), 1, keep((to_bits(g).view(np.int16))),
+                                           ctypes.c_float(1e-6), keep((w)), keep((s)), vocab, vp(logits_d),
+                                           vp(toks_d), vp(ws), ws_bytes, stream()) == 0
+    sync()
+    exp_logits, exp_toks = lm_oracle(x, g, w, s)
+    assert np.array_equal(from_bits(host(logits_d).view(np.uint16)), exp_logits)
+    assert host(toks_d).view(np.uint32).tolist() == exp_toks
