@@ -6,8 +6,8 @@ are filled by the engine's seeded generator on the GPU and by the oracle's
 restatement of it on the host; the first test checks that both hold the same
 codes and scales. Bar: bit-identical tokens and logits for every sequence
 (the reference's sign-off, compare_rtl_math.py:38, is token equality on
-identical histories; the logit bar of the north star, max|d| <= 2e-2 x range,
-is implied)."""
+identical histories; a logit tolerance of max|d| <= 2e-2 x the logit range is
+implied)."""
 import numpy as np
 import pytest
 

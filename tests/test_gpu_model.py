@@ -80,8 +80,9 @@ def test_teacher_forced_matches_oracle(engine, oracle_kv8, golden):
 
 
 def test_kv8_tokens_against_reference_bf16_kv(engine, golden):
-    """The reference keeps a bf16 KV cache; the engine's KV8 cache is the
-    north-star change. Record agreement with the reference's own tokens."""
+    """The reference keeps a bf16 KV cache; the engine's cache is int8 (KV8),
+    the one change of format this engine makes. Record agreement with the
+    reference's own tokens."""
     g_toks, _ = generate_gpu(engine, golden['prompt'], 6)
     ref_toks = [s['token'] for s in golden['generate']]
     # the oracle in KV8 mode reproduces all six reference tokens on this seed
